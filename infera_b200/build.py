@@ -1,0 +1,122 @@
+"""Build the native parts of infera_b200 in-tree.
+
+* ``infera_b200/lib/libib200_kernels.so`` - every ``csrc/*.cu`` compiled for
+  sm_100a only (``-gencode arch=compute_100a,code=sm_100a``), C ABI, no torch
+  headers (fast to build, loadable with ctypes, travels with the tree).
+* ``infera_b200/lib/libib200_runtime.so`` - host-side C++ runtime
+  (``csrc/runtime/*.cpp``): XXH3 chained block hashing, the paged-KV block
+  allocator with prefix cache, and the scheduler's batch packer.
+* ``infera_b200/lib/ib200_router`` - the native router data plane
+  (``native/router/*.cpp``).
+
+Run ``python -m infera_b200.build`` (or ``__graft_entry__.build()``).
+Objects are rebuilt only when a source or header is newer than its output.
+"""
+
+from __future__ import annotations
+
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG / "csrc"
+RUNTIME_SRC = CSRC / "runtime"
+ROUTER_SRC = PKG / "native" / "router"
+LIB = PKG / "lib"
+OBJ = PKG / "lib" / "obj"
+
+KERNELS_SO = LIB / "libib200_kernels.so"
+RUNTIME_SO = LIB / "libib200_runtime.so"
+ROUTER_BIN = LIB / "ib200_router"
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def _cuda_home() -> Path:
+    return Path(_nvcc()).resolve().parent.parent
+
+
+def _newer(src_files: list[Path], out: Path) -> bool:
+    if not out.exists():
+        return True
+    t = out.stat().st_mtime
+    return any(s.stat().st_mtime > t for s in src_files)
+
+
+def _run(cmd: list[str]) -> None:
+    r = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"build failed: {' '.join(cmd)}\n{r.stdout}")
+
+
+def build_kernels(verbose: bool = False, jobs: int | None = None) -> Path:
+    OBJ.mkdir(parents=True, exist_ok=True)
+    headers = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h"))
+    sources = sorted(CSRC.glob("*.cu"))
+    nvcc = _nvcc()
+    objs: list[Path] = []
+    todo: list[list[str]] = []
+    for src in sources:
+        obj = OBJ / (src.stem + ".o")
+        objs.append(obj)
+        if _newer([src, *headers], obj):
+            cmd = [nvcc, *ARCH_FLAGS, "-O3", "-std=c++17", "-lineinfo", "--use_fast_math",
+                   "-Xcompiler", "-fPIC", "-Xptxas", "-v" if verbose else "-O3",
+                   "-I", str(CSRC), "-c", str(src), "-o", str(obj)]
+            todo.append(cmd)
+    if todo:
+        with cf.ThreadPoolExecutor(max_workers=jobs or min(8, os.cpu_count() or 4)) as ex:
+            list(ex.map(_run, todo))
+    if todo or _newer(objs, KERNELS_SO):
+        _run([nvcc, *ARCH_FLAGS, "-shared", "-o", str(KERNELS_SO), *map(str, objs), "-lcudart"])
+    return KERNELS_SO
+
+
+def build_runtime() -> Path | None:
+    sources = sorted(RUNTIME_SRC.glob("*.cpp")) if RUNTIME_SRC.exists() else []
+    if not sources:
+        return None
+    headers = sorted(RUNTIME_SRC.glob("*.h"))
+    if _newer([*sources, *headers], RUNTIME_SO):
+        LIB.mkdir(parents=True, exist_ok=True)
+        _run(["g++", "-O3", "-std=c++17", "-fPIC", "-shared", "-march=x86-64-v2", "-o", str(RUNTIME_SO),
+              *map(str, sources), "-lpthread"])
+    return RUNTIME_SO
+
+
+def build_router() -> Path | None:
+    sources = sorted(ROUTER_SRC.glob("*.cpp")) if ROUTER_SRC.exists() else []
+    if not sources:
+        return None
+    headers = sorted(ROUTER_SRC.glob("*.h")) + sorted(RUNTIME_SRC.glob("*.h"))
+    if _newer([*sources, *headers], ROUTER_BIN):
+        LIB.mkdir(parents=True, exist_ok=True)
+        _run(["g++", "-O2", "-std=c++17", "-I", str(RUNTIME_SRC), "-o", str(ROUTER_BIN), *map(str, sources),
+              "-lpthread"])
+    return ROUTER_BIN
+
+
+def build_all(verbose: bool = False) -> dict[str, str | None]:
+    out = {"kernels": str(build_kernels(verbose=verbose))}
+    rt = build_runtime()
+    out["runtime"] = str(rt) if rt else None
+    rb = build_router()
+    out["router"] = str(rb) if rb else None
+    return out
+
+
+if __name__ == "__main__":
+    res = build_all(verbose="-v" in sys.argv)
+    for k, v in res.items():
+        print(f"{k}: {v}")

@@ -1,0 +1,384 @@
+// Causal flash attention over a paged KV cache on tcgen05 tensor cores.
+//
+// One CTA computes 128 query rows of one query head:
+//   warp 0      TMA producer: Q tile once, then K/V tiles of 128 keys
+//               (8 pages of 16 tokens, two 64-dim halves each)
+//   warp 1      MMA issuer: S = Q K^T into TMEM (double buffered),
+//               O += P V into TMEM
+//   warps 2..5  softmax: thread <-> query row; reads S from TMEM, writes
+//               bf16 P into shared memory (K-major, 128-byte swizzle),
+//               rescales O in TMEM only when the running max grows by more
+//               than 2^8 (lazy rescale), final O / l epilogue.
+//
+// KV cache layout (per layer): [num_slots, Hkv * 128] bf16 with slot =
+// page * 16 + offset, i.e. a page is 16 tokens x Hkv heads x 128 dims.
+// V tiles are consumed MN-major (dims contiguous) as the B operand.
+//
+// Reference parity: the reference runs prefill attention inside vLLM /
+// SGLang / AITER (not in its tree); this is this framework's own kernel.
+#include "sm100.cuh"
+#include "tma_host.h"
+
+namespace ib200 {
+namespace fa {
+
+constexpr int D = 128;
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int PAGE = 16;
+constexpr int HALF = 64 * 128 * 2;    // not used directly
+constexpr int BLK = 128 * 128;        // bytes of one 128-row x 64-col bf16 block (16 KiB)
+constexpr int KV_STAGES = 2;
+constexpr int NUM_THREADS = 192;
+// smem: Q (2 blocks) + P (2 blocks) + KV_STAGES x (K 2 blocks + V 2 blocks)
+constexpr int SMEM_BYTES = 1024 + (4 + KV_STAGES * 4) * BLK + 512;
+constexpr uint32_t S_COL0 = 0, S_COL1 = 128, O_COL = 256;
+
+struct Params {
+  const int* tiles;        // [num_tiles * 2]: (seq, q_block)
+  const int* q_start;      // [num_seqs] first row of the sequence in Q / O
+  const int* q_len;        // [num_seqs]
+  const int* ctx_len;      // [num_seqs] keys visible after this chunk
+  const int* block_table;  // [rows, max_pages]
+  const int* bt_rows;      // [num_seqs] table row of each sequence (null: row = seq)
+  int max_pages;
+  int num_heads, num_kv_heads;
+  float scale_log2;        // softmax scale * log2(e)
+  __nv_bfloat16* out;      // [T, num_heads * 128]
+  int ldo;
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t sw128_offset(int row, int chunk16) {
+  return static_cast<uint32_t>(row * 128 + ((chunk16 ^ (row & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;              // 2 blocks: dims 0-63, 64-127
+  uint8_t* sP = smem + 2 * BLK;    // 2 blocks: keys 0-63, 64-127
+  uint8_t* sKV = smem + 4 * BLK;   // stage s: K lo, K hi, V lo, V hi
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + KV_STAGES * 4 * BLK);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;                 // [KV_STAGES]
+  uint64_t* v_full = k_full + KV_STAGES;       // [KV_STAGES]
+  uint64_t* kv_empty = v_full + KV_STAGES;     // [KV_STAGES]
+  uint64_t* s_full = kv_empty + KV_STAGES;     // [2]
+  uint64_t* p_full = s_full + 2;               // [1]
+  uint64_t* o_done = p_full + 1;               // [1]
+  uint64_t* drain = o_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.x;
+  const int seq = p.tiles[blockIdx.y * 2 + 0];
+  const int qb = p.tiles[blockIdx.y * 2 + 1];
+  const int kvh = h / (p.num_heads / p.num_kv_heads);
+  const int qlen = p.q_len[seq];
+  const int ctx = p.ctx_len[seq];
+  const int row0 = p.q_start[seq] + qb * BQ;
+  const int valid_rows = min(BQ, qlen - qb * BQ);
+  const int pos0 = ctx - qlen + qb * BQ;           // position of row 0
+  const int last_pos = pos0 + valid_rows - 1;
+  const int n_kv = (last_pos + 1 + BKV - 1) / BKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_last();
+      mbar_expect_tx(q_full, 2 * BLK);
+      tma_load_2d(sQ, &tmQ, q_full, h * D, row0, pol);
+      tma_load_2d(sQ + BLK, &tmQ, q_full, h * D + 64, row0, pol);
+      const int bt_row = p.bt_rows != nullptr ? p.bt_rows[seq] : seq;
+      const int* bt = p.block_table + static_cast<size_t>(bt_row) * p.max_pages;
+      const int n_pages = (ctx + PAGE - 1) / PAGE;
+      long long issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
+        uint8_t* base = sKV + st * 4 * BLK;
+        mbar_expect_tx(&k_full[st], 2 * BLK);
+        for (int pg = 0; pg < BKV / PAGE; ++pg) {
+          int lp = j * (BKV / PAGE) + pg;
+          int page = lp < n_pages ? __ldg(bt + lp) : __ldg(bt);
+          int r = page * PAGE;
+          tma_load_2d(base + pg * PAGE * 128, &tmK, &k_full[st], kvh * D, r, pol);
+          tma_load_2d(base + BLK + pg * PAGE * 128, &tmK, &k_full[st], kvh * D + 64, r, pol);
+        }
+        mbar_expect_tx(&v_full[st], 2 * BLK);
+        for (int pg = 0; pg < BKV / PAGE; ++pg) {
+          int lp = j * (BKV / PAGE) + pg;
+          int page = lp < n_pages ? __ldg(bt + lp) : __ldg(bt);
+          int r = page * PAGE;
+          tma_load_2d(base + 2 * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * D, r, pol);
+          tma_load_2d(base + 3 * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * D + 64, r, pol);
+        }
+        ++issued;
+      }
+      // drain: every issued tile's bytes must have landed before exit
+      mbar_wait(q_full, 0, nullptr, nullptr, 0, kWaitLimitNs / 4);
+      long long first = issued > KV_STAGES ? issued - KV_STAGES : 0;
+      for (long long i = first; i < issued; ++i) {
+        mbar_wait(&k_full[i % KV_STAGES], static_cast<uint32_t>((i / KV_STAGES) & 1), nullptr, nullptr, 0,
+                  kWaitLimitNs / 4);
+        mbar_wait(&v_full[i % KV_STAGES], static_cast<uint32_t>((i / KV_STAGES) & 1), nullptr, nullptr, 0,
+                  kWaitLimitNs / 4);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_qk = make_idesc_bf16(128, 128, false);
+      const uint32_t idesc_pv = make_idesc_bf16(128, 128, true);
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t p_addr = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kStatusTimeoutFull);
+      auto issue_pv = [&](int jj) -> bool {
+        // O += P V_jj once softmax has written P for tile jj
+        if (!mbar_wait(p_full, static_cast<uint32_t>(jj & 1), abort_flag, p.status, kStatusTimeoutTmemEmpty))
+          return false;
+        const int st = jj % KV_STAGES;
+        if (!mbar_wait(&v_full[st], static_cast<uint32_t>((jj / KV_STAGES) & 1), abort_flag, p.status,
+                       kStatusTimeoutFull))
+          return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sKV + st * 4 * BLK + 2 * BLK);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          const uint32_t a = p_addr + (s < 4 ? s * 32 : BLK + (s - 4) * 32);
+          const uint64_t ad = make_sw128_desc(a, 16, 1024);
+          // MN-major V: LBO = distance between the two 64-dim halves, SBO = 8 keys
+          const uint64_t bd = make_sw128_desc(v_addr + s * 2048, BLK, 1024);
+          umma_bf16(tmem + O_COL, ad, bd, idesc_pv, (jj > 0 || s > 0) ? 1u : 0u);
+        }
+        umma_commit(o_done);
+        umma_commit(&kv_empty[st]);
+        return true;
+      };
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j % KV_STAGES;
+        if (!mbar_wait(&k_full[st], static_cast<uint32_t>((j / KV_STAGES) & 1), abort_flag, p.status,
+                       kStatusTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sKV + st * 4 * BLK);
+        const uint32_t s_col = (j & 1) ? S_COL1 : S_COL0;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          const uint32_t off = s < 4 ? s * 32 : BLK + (s - 4) * 32;
+          const uint64_t ad = make_sw128_desc(q_addr + off, 16, 1024);
+          const uint64_t bd = make_sw128_desc(k_addr + off, 16, 1024);
+          umma_bf16(tmem + s_col, ad, bd, idesc_qk, s > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[j & 1]);
+        if (j > 0 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && n_kv > 0) issue_pv(n_kv - 1);
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, p.status, kStatusTimeoutFull);
+    }
+  } else {
+    // softmax warps: thread <-> query row
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const int pos = pos0 + min(r, valid_rows - 1);
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    float m_run = -INFINITY;  // running max in log2 units (scaled)
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status,
+                     kStatusTimeoutTmemFull)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t s_addr = lane_addr + ((j & 1) ? S_COL1 : S_COL0);
+      const int kbase = j * BKV;
+      const int lim = pos - kbase;  // key c visible iff c <= lim
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c0 = 0; c0 < BKV; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(s_addr + c0, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c0 + i <= lim) mx = fmaxf(mx, __uint_as_float(v[i]));
+      }
+      mx *= p.scale_log2;
+      float m_new = fmaxf(m_run, mx);
+      bool rescale = (j == 0) || (m_new > m_run + 8.0f);
+      float m_use = rescale ? m_new : m_run;
+      float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
+      // P of the previous tile must be consumed before P / O are touched
+      if (j > 0) {
+        if (!mbar_wait(o_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status, kStatusTimeoutTmemFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (rescale && j > 0 && alpha != 1.0f) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 16) {
+          uint32_t o[16];
+          tmem_ld16(lane_addr + O_COL + c0, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st16(lane_addr + O_COL + c0, o);
+        }
+        tmem_st_wait();
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c0 = 0; c0 < BKV; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(s_addr + c0, v);
+        tmem_ld_wait();
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float e0 = (c0 + i <= lim) ? exp2f(__uint_as_float(v[i]) * p.scale_log2 - m_use) : 0.f;
+          float e1 = (c0 + i + 1 <= lim) ? exp2f(__uint_as_float(v[i + 1]) * p.scale_log2 - m_use) : 0.f;
+          __nv_bfloat162 b = __floats2bfloat162_rn(e0, e1);
+          sum += __low2float(b) + __high2float(b);
+          packed[i / 2] = *reinterpret_cast<uint32_t*>(&b);
+        }
+        uint8_t* blk = sP + (c0 < 64 ? 0 : BLK);
+        const int chunk0 = (c0 & 63) / 8;  // 16-byte chunk index within the 128-byte row
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          *reinterpret_cast<uint4*>(blk + sw128_offset(r, chunk0 + q)) = w;
+        }
+      }
+      l_run = l_run * alpha + sum;
+      m_run = m_use;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && n_kv > 0) {
+      if (mbar_wait(o_done, static_cast<uint32_t>((n_kv - 1) & 1), abort_flag, p.status, kStatusTimeoutTmemFull)) {
+        tc_fence_after();
+        const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+        const bool write = r < valid_rows;
+        __nv_bfloat16* orow = p.out + static_cast<size_t>(row0 + r) * p.ldo + h * D;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(lane_addr + O_COL + c0, o);
+          tmem_ld_wait();
+          if (write) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 w;
+              w.x = pack_bf16(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
+              w.y = pack_bf16(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+              w.z = pack_bf16(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+              w.w = pack_bf16(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + c0 + i) = w;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fa
+}  // namespace ib200
+
+using namespace ib200;
+
+// q: [T, ldq] bf16 with head h at columns [h*128, h*128+128).
+// k_cache / v_cache: [num_slots, num_kv_heads*128] bf16.
+// tiles: device int32 [num_tiles, 2] (seq, q_block), longest first.
+extern "C" int ib_attn_prefill(const void* q, int T, int ldq, const void* k_cache, const void* v_cache,
+                               long long num_slots, const int* tiles, int num_tiles, const int* q_start,
+                               const int* q_len, const int* ctx_len, const int* block_table, const int* bt_rows,
+                               int max_pages,
+                               int num_heads, int num_kv_heads, float scale, void* out, int ldo, int* status,
+                               cudaStream_t stream) {
+  using namespace ib200::fa;
+  if (num_tiles <= 0 || T <= 0) return 0;
+  if ((ldq % 8) != 0 || (ldo % 8) != 0 || num_heads % num_kv_heads != 0) return -1;
+  CUtensorMap tq, tk, tv;
+  const int kvw = num_kv_heads * D;
+  if (!cached_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, num_heads * D, ldq, 128, 64)) return -2;
+  if (!cached_tmap_2d(&tk, k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, kvw, kvw, 16, 64)) return -2;
+  if (!cached_tmap_2d(&tv, v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, kvw, kvw, 16, 64)) return -2;
+  Params p;
+  p.tiles = tiles;
+  p.q_start = q_start;
+  p.q_len = q_len;
+  p.ctx_len = ctx_len;
+  p.block_table = block_table;
+  p.bt_rows = bt_rows;
+  p.max_pages = max_pages;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.status = status;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_set[dev] = true;
+  }
+  dim3 grid(num_heads, num_tiles);
+  fa_prefill_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}

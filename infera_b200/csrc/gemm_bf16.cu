@@ -1,0 +1,477 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05 / TMEM / TMA).
+//
+//   C[M, N] = A[M, K] . W[N, K]^T        (nn.Linear layout, both K-major)
+//
+// Persistent, warp-specialised kernel, one CTA per SM:
+//   warp 0      TMA producer (one elected lane) -> STAGES-deep smem ring
+//   warp 1      TMEM allocator + MMA issuer (one elected lane)
+//   warps 2..5  epilogue: tcgen05.ld -> registers -> global
+// Two TMEM accumulators (2 x 256 fp32 columns) let the epilogue of tile i
+// overlap the main loop of tile i+1.
+//
+// Two operand orders:
+//   normal  : UMMA M = 128 tokens,       UMMA N = 256 output features
+//   swap-AB : UMMA M = 128 out features, UMMA N = tokens rounded up to 16
+// Swap-AB is the decode shape (few tokens): the weight streams through the
+// 128-row side and every SM keeps HBM busy. Small tile counts are split along
+// K; split partials are reduced with fp32 vector atomics into a zeroed
+// workspace and a finalize kernel converts (and re-zeroes the workspace).
+//
+// Epilogues: plain bf16 store, or SwiGLU on row-interleaved (gate, up)
+// weights (row 2j = gate_j, row 2j+1 = up_j) writing silu(g)*u.
+//
+// Reference parity: the reference delegates all GEMMs to its engines
+// (vLLM/hipBLASLt); there is no GEMM source in it to mirror.
+#include "sm100.cuh"
+#include "tma_host.h"
+
+namespace ib200 {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // one 128-byte swizzle atom of bf16
+constexpr int STAGES = 4;
+constexpr int MAX_BN = 256;
+constexpr int P_STAGE = BM * BK * 2;      // 16 KiB
+constexpr int Q_STAGE = MAX_BN * BK * 2;  // 32 KiB
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = 1024 + STAGES * (P_STAGE + Q_STAGE) + 256;
+
+enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_ATOMIC_F32 = 2 };
+
+struct Params {
+  int M, N, K;      // logical problem: tokens, features (pre-activation), reduction
+  int bn;           // UMMA N
+  int p_tiles, q_tiles, splits, kbps, nkb;
+  int swap;         // 1: P = W (features), Q = A (tokens)
+  int epi;
+  void* out;        // bf16 [M, ldc] or fp32 [M, N] workspace
+  int ldc;
+  int* status;
+};
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& pt, int& qt, int& sp) {
+  sp = t % p.splits;
+  int rest = t / p.splits;
+  pt = rest % p.p_tiles;
+  qt = rest / p.p_tiles;
+}
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// Epilogue for a chunk of `ncols` accumulator columns starting at `c0`.
+// `r` holds this thread's row of the chunk (row = TMEM lane).
+template <int NC>
+__device__ __forceinline__ void store_chunk(const Params& p, int pt, int qt, int row, int c0,
+                                            const uint32_t (&r)[NC]) {
+  if (!p.swap) {
+    const int m = pt * BM + row;
+    const int n0 = qt * p.bn + c0;
+    if (p.epi == EPI_BF16) {
+      if (m >= p.M) return;
+      __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldc + n0;
+      if (n0 + NC <= p.N && (p.ldc & 7) == 0) {
+#pragma unroll
+        for (int j = 0; j < NC; j += 8) {
+          uint4 v;
+          v.x = pack_bf16(__uint_as_float(r[j + 0]), __uint_as_float(r[j + 1]));
+          v.y = pack_bf16(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          v.z = pack_bf16(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5]));
+          v.w = pack_bf16(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7]));
+          *reinterpret_cast<uint4*>(C + j) = v;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < NC; ++j)
+          if (n0 + j < p.N) C[j] = __float2bfloat16(__uint_as_float(r[j]));
+      }
+    } else if (p.epi == EPI_SWIGLU) {
+      if (m >= p.M) return;
+      __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldc + n0 / 2;
+      if (n0 + NC <= p.N && (p.ldc & 7) == 0) {
+#pragma unroll
+        for (int j = 0; j < NC; j += 16) {
+          float o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            o[i] = silu(__uint_as_float(r[j + 2 * i])) * __uint_as_float(r[j + 2 * i + 1]);
+          uint4 v;
+          v.x = pack_bf16(o[0], o[1]);
+          v.y = pack_bf16(o[2], o[3]);
+          v.z = pack_bf16(o[4], o[5]);
+          v.w = pack_bf16(o[6], o[7]);
+          *reinterpret_cast<uint4*>(C + j / 2) = v;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < NC; j += 2)
+          if (n0 + j + 1 < p.N)
+            C[j / 2] = __float2bfloat16(silu(__uint_as_float(r[j])) * __uint_as_float(r[j + 1]));
+      }
+    } else {
+      if (m >= p.M) return;
+      float* W = reinterpret_cast<float*>(p.out) + static_cast<size_t>(m) * p.N + n0;
+      if (n0 + NC <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+        for (int j = 0; j < NC; j += 4)
+          red_add_v4(W + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                     __uint_as_float(r[j + 3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < NC; ++j)
+          if (n0 + j < p.N) atomicAdd(W + j, __uint_as_float(r[j]));
+      }
+    }
+  } else {
+    // swap-AB: row = output feature, columns = tokens
+    const int n = pt * BM + row;
+    const int m0 = qt * p.bn + c0;
+    if (p.epi == EPI_BF16) {
+      if (n >= p.N) return;
+      __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.out) + n;
+#pragma unroll
+      for (int j = 0; j < NC; ++j)
+        if (m0 + j < p.M) C[static_cast<size_t>(m0 + j) * p.ldc] = __float2bfloat16(__uint_as_float(r[j]));
+    } else if (p.epi == EPI_SWIGLU) {
+      // lanes 2j / 2j+1 hold gate_j / up_j for the same tokens
+      const bool even = (threadIdx.x & 1) == 0;
+      __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.out) + n / 2;
+#pragma unroll
+      for (int j = 0; j < NC; ++j) {
+        float mine = __uint_as_float(r[j]);
+        float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+        if (even && n + 1 < p.N && m0 + j < p.M)
+          C[static_cast<size_t>(m0 + j) * p.ldc] = __float2bfloat16(silu(mine) * other);
+      }
+    } else {
+      if (n >= p.N) return;
+      float* W = reinterpret_cast<float*>(p.out) + n;
+#pragma unroll
+      for (int j = 0; j < NC; ++j)
+        if (m0 + j < p.M) atomicAdd(W + static_cast<size_t>(m0 + j) * p.N, __uint_as_float(r[j]));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
+                     const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sP = smem;
+  uint8_t* sQ = smem + STAGES * P_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sQ + STAGES * Q_STAGE);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total = p.p_tiles * p.q_tiles * p.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmP);
+    tma_prefetch_desc(&tmQ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_act = policy_evict_last();
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t polP = p.swap ? pol_w : pol_act;
+      const uint64_t polQ = p.swap ? pol_act : pol_w;
+      const uint32_t tx = static_cast<uint32_t>((BM + p.bn) * BK * 2);
+      uint32_t stage = 0, phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int pt, qt, sp;
+        tile_coords(p, t, pt, qt, sp);
+        const int kb0 = sp * p.kbps;
+        const int kb1 = min(kb0 + p.kbps, p.nkb);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], tx);
+          tma_load_2d(sP + stage * P_STAGE, &tmP, &full[stage], kb * BK, pt * BM, polP);
+          tma_load_2d(sQ + stage * Q_STAGE, &tmQ, &full[stage], kb * BK, qt * p.bn, polQ);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every copy already issued land before the CTA can exit.
+        long long first = issued > STAGES ? issued - STAGES : 0;
+        for (long long i = first; i < issued; ++i)
+          mbar_wait(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1), nullptr, nullptr, 0,
+                    kWaitLimitNs / 4);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_bf16(BM, p.bn);
+      uint32_t stage = 0, phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
+        int pt, qt, sp;
+        tile_coords(p, t, pt, qt, sp);
+        const int kb0 = sp * p.kbps;
+        const int kb1 = min(kb0 + p.kbps, p.nkb);
+        const uint32_t acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status, kStatusTimeoutTmemEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * MAX_BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sP + stage * P_STAGE);
+          const uint32_t b_addr = smem_u32(sQ + stage * Q_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = make_sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = make_sw128_desc(b_addr + kk * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+      // Every MMA this thread issued must be finished before TMEM is freed.
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, p.status, kStatusTimeoutFull);
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = q * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
+      int pt, qt, sp;
+      tile_coords(p, t, pt, qt, sp);
+      const uint32_t acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutTmemFull)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * MAX_BN;
+      int c0 = 0;
+      for (; c0 + 32 <= p.bn; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c0, r);
+        tmem_ld_wait();
+        store_chunk<32>(p, pt, qt, row, c0, r);
+      }
+      if (c0 < p.bn) {
+        uint32_t r[16];
+        tmem_ld16(t_row + c0, r);
+        tmem_ld_wait();
+        store_chunk<16>(p, pt, qt, row, c0, r);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// Reduce the fp32 split-K workspace into the bf16 output (optionally
+// applying SwiGLU) and zero the workspace for its next use.
+__global__ void splitk_finalize_kernel(float* __restrict__ ws, __nv_bfloat16* __restrict__ out, int M, int N,
+                                       int ldc, int swiglu) {
+  const int m = blockIdx.y;
+  if (m >= M) return;
+  float* row = ws + static_cast<size_t>(m) * N;
+  __nv_bfloat16* orow = out + static_cast<size_t>(m) * ldc;
+  if (!swiglu) {
+    for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < N; n += gridDim.x * blockDim.x * 4) {
+      if (n + 4 <= N) {
+        float4 v = *reinterpret_cast<float4*>(row + n);
+        *reinterpret_cast<float4*>(row + n) = make_float4(0.f, 0.f, 0.f, 0.f);
+        uint2 o;
+        o.x = pack_bf16(v.x, v.y);
+        o.y = pack_bf16(v.z, v.w);
+        *reinterpret_cast<uint2*>(orow + n) = o;
+      } else {
+        for (int j = n; j < N; ++j) {
+          orow[j] = __float2bfloat16(row[j]);
+          row[j] = 0.f;
+        }
+      }
+    }
+  } else {
+    for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < N; n += gridDim.x * blockDim.x * 4) {
+      float4 v = *reinterpret_cast<float4*>(row + n);
+      *reinterpret_cast<float4*>(row + n) = make_float4(0.f, 0.f, 0.f, 0.f);
+      uint32_t o = pack_bf16(silu(v.x) * v.y, silu(v.z) * v.w);
+      *reinterpret_cast<uint32_t*>(orow + n / 2) = o;
+    }
+  }
+}
+
+struct Plan {
+  Params p;
+  int grid;
+};
+
+// Choose operand order, tile width and split-K factor for one problem.
+inline Plan make_plan(int M, int N, int K, int num_sms, int force_split) {
+  Plan pl{};
+  Params& p = pl.p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.nkb = (K + BK - 1) / BK;
+  p.swap = M <= 128 ? 1 : 0;
+  if (p.swap) {
+    p.bn = ((M + 15) / 16) * 16;
+    p.p_tiles = (N + BM - 1) / BM;
+    p.q_tiles = 1;
+  } else {
+    p.bn = MAX_BN;
+    p.p_tiles = (M + BM - 1) / BM;
+    p.q_tiles = (N + MAX_BN - 1) / MAX_BN;
+  }
+  const int tiles = p.p_tiles * p.q_tiles;
+  int best = 1;
+  if (force_split > 0) {
+    best = force_split;
+  } else if (tiles < num_sms) {
+    // minimise waves/split (time in units of one full tile), with a 3%
+    // penalty per extra split for the atomics and the finalize pass
+    double best_cost = 1e30;
+    for (int s = 1; s <= 16; ++s) {
+      if (p.nkb / s < 4 && s > 1) break;
+      double waves = static_cast<double>((tiles * s + num_sms - 1) / num_sms);
+      double cost = waves / s * (1.0 + 0.03 * (s - 1));
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = s;
+      }
+    }
+  }
+  if ((N % 4) != 0) best = 1;
+  p.kbps = (p.nkb + best - 1) / best;
+  p.splits = (p.nkb + p.kbps - 1) / p.kbps;
+  const int units = tiles * p.splits;
+  pl.grid = units < num_sms ? units : num_sms;
+  return pl;
+}
+
+}  // namespace gemm
+}  // namespace ib200
+
+using namespace ib200;
+
+// C ABI. Returns 0 on success, a negative code on bad arguments / encode
+// failure, or a CUDA error code from the launch.
+//   epi: 0 = bf16 store, 1 = SwiGLU (out has N/2 columns)
+//   ws : fp32 workspace of >= M*N floats, all zero on entry (left zero), only
+//        touched when the plan splits K; may be null if split_k == 1 forced.
+extern "C" int ib_gemm_bf16(const void* A, const void* W, void* out, int M, int N, int K, int lda, int ldw,
+                            int ldc, int epi, float* ws, int force_split, int* status, cudaStream_t stream) {
+  using namespace ib200::gemm;
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if ((K % 8) != 0 || (lda % 8) != 0 || (ldw % 8) != 0) return -1;
+  if (epi == EPI_SWIGLU && (N % 2) != 0) return -1;
+  const int num_sms = num_sms_for_current_device();
+  Plan pl = make_plan(M, N, K, num_sms, ws == nullptr ? 1 : force_split);
+  Params& p = pl.p;
+  p.status = status;
+  p.ldc = ldc;
+  const bool split = p.splits > 1;
+  p.epi = split ? EPI_ATOMIC_F32 : epi;
+  p.out = split ? static_cast<void*>(ws) : out;
+
+  CUtensorMap tmP, tmQ;
+  const void* Pbase = p.swap ? W : A;
+  const void* Qbase = p.swap ? A : W;
+  const int Prows = p.swap ? N : M;
+  const int Qrows = p.swap ? M : N;
+  const int Pld = p.swap ? ldw : lda;
+  const int Qld = p.swap ? lda : ldw;
+  if (!cached_tmap_2d(&tmP, Pbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Prows, K, Pld, BM, BK)) return -2;
+  if (!cached_tmap_2d(&tmQ, Qbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Qrows, K, Qld, p.bn, BK)) return -2;
+
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_set[dev] = true;
+  }
+  gemm_bf16_kernel<<<pl.grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmP, tmQ, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (split) {
+    dim3 g((N + 1023) / 1024, M);
+    splitk_finalize_kernel<<<g, 256, 0, stream>>>(ws, static_cast<__nv_bfloat16*>(out), M, N, ldc,
+                                                  epi == EPI_SWIGLU ? 1 : 0);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  return 0;
+}
+
+// Plan introspection for tests and benchmarks: writes
+// [swap, bn, p_tiles, q_tiles, splits, kbps, grid].
+extern "C" void ib_gemm_bf16_plan(int M, int N, int K, int num_sms, int force_split, int* out7) {
+  using namespace ib200::gemm;
+  Plan pl = make_plan(M, N, K, num_sms, force_split);
+  out7[0] = pl.p.swap;
+  out7[1] = pl.p.bn;
+  out7[2] = pl.p.p_tiles;
+  out7[3] = pl.p.q_tiles;
+  out7[4] = pl.p.splits;
+  out7[5] = pl.p.kbps;
+  out7[6] = pl.grid;
+}

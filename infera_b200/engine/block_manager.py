@@ -1,0 +1,215 @@
+"""Paged KV-cache block manager with a content-addressed prefix cache.
+
+* A page holds ``page_size`` (16) tokens of K and V for every layer.
+* Full pages are content-addressed by the chained block hash
+  ``h_i = XXH3_64(h_{i-1} as u64 LE || tokens as u32 LE)`` with
+  ``h_{-1} = 0`` - the same chain the router computes from token ids, so an
+  engine hash equals the router's hash for the same prefix.
+* Pages whose refcount drops to zero keep their hash and sit in an LRU of
+  evictable pages; a later request with the same prefix re-references them
+  (prefix hit). Allocation takes never-hashed free pages first, then evicts
+  the least recently used cached page.
+* Every page that becomes cached is reported as ``BlockStored`` and every
+  eviction as ``BlockRemoved`` through the ``event_sink`` callback, in the
+  vLLM KV-event vocabulary the router consumes.
+
+Reference parity: the reference leaves paging to its engines (vLLM's
+KVCacheManager / SGLang's RadixCache); its router-side mirror of this cache
+is ``infera/router/kv_event/client.py`` and the hash chain
+``infera/router/kv_event/hasher.py:20-42``.
+"""
+
+from __future__ import annotations
+
+from collections import OrderedDict
+from dataclasses import dataclass, field
+from typing import Callable
+
+from infera_b200.utils.hashing import chain_hashes
+
+
+@dataclass
+class SeqBlocks:
+    """Per-sequence page list and how many of its tokens are in the cache."""
+
+    pages: list[int] = field(default_factory=list)
+    hashes: list[int] = field(default_factory=list)   # hashes of the full pages registered so far
+    num_cached_tokens: int = 0                          # tokens with K/V present (computed or hit)
+
+
+class BlockManager:
+    def __init__(self, num_pages: int, page_size: int = 16, enable_prefix_cache: bool = True,
+                 event_sink: Callable[[str, dict], None] | None = None, reserved_pages: int = 1):
+        self.num_pages = num_pages
+        self.page_size = page_size
+        self.enable_prefix_cache = enable_prefix_cache
+        self.event_sink = event_sink
+        # page 0.. reserved_pages-1 are never handed out (padding target for graphs)
+        self.reserved = reserved_pages
+        self.refcount = [0] * num_pages
+        self.page_hash: list[int | None] = [None] * num_pages
+        self.free_plain: list[int] = list(range(num_pages - 1, reserved_pages - 1, -1))
+        self.evictable: OrderedDict[int, None] = OrderedDict()   # cached pages with refcount 0 (LRU order)
+        self.hash_to_page: dict[int, int] = {}
+        self.stats = {"hit_tokens": 0, "query_tokens": 0, "evictions": 0}
+
+    # ------------------------------------------------------------------ capacity
+    def num_free(self) -> int:
+        return len(self.free_plain) + len(self.evictable)
+
+    def usage(self) -> float:
+        usable = self.num_pages - self.reserved
+        return 1.0 - self.num_free() / max(1, usable)
+
+    def can_allocate(self, n: int, watermark: int = 0) -> bool:
+        return self.num_free() - watermark >= n
+
+    # ------------------------------------------------------------------ allocation
+    def _take_page(self) -> int:
+        if self.free_plain:
+            return self.free_plain.pop()
+        if not self.evictable:
+            raise MemoryError("KV cache exhausted")
+        page, _ = self.evictable.popitem(last=False)
+        h = self.page_hash[page]
+        if h is not None:
+            if self.hash_to_page.get(h) == page:
+                del self.hash_to_page[h]
+            self.page_hash[page] = None
+            self.stats["evictions"] += 1
+            self._emit("BlockRemoved", {"block_hashes": [h], "medium": "GPU"})
+        return page
+
+    def _release(self, page: int) -> None:
+        self.refcount[page] -= 1
+        if self.refcount[page] == 0:
+            if self.page_hash[page] is not None and self.enable_prefix_cache:
+                self.evictable[page] = None
+            else:
+                self.page_hash[page] = None
+                self.free_plain.append(page)
+
+    def _emit(self, kind: str, payload: dict) -> None:
+        if self.event_sink is not None:
+            self.event_sink(kind, payload)
+
+    # ------------------------------------------------------------------ prefix lookup
+    def match_prefix(self, token_ids: list[int], hashes: list[int] | None = None) -> tuple[list[int], list[int]]:
+        """Longest run of cached full pages at the start of ``token_ids``.
+
+        Returns (pages, hashes) of the hit; at least one token is always left
+        to compute, so a fully cached prompt gives back its last page.
+        """
+        if not self.enable_prefix_cache:
+            return [], []
+        if hashes is None:
+            hashes = chain_hashes(token_ids, self.page_size)
+        pages: list[int] = []
+        for h in hashes:
+            p = self.hash_to_page.get(h)
+            if p is None:
+                break
+            pages.append(p)
+        n = len(pages)
+        if n > 0 and n * self.page_size >= len(token_ids):
+            n -= 1
+        return pages[:n], hashes[:n]
+
+    def allocate_prompt(self, token_ids: list[int], num_tokens: int,
+                        hashes: list[int] | None = None) -> SeqBlocks | None:
+        """Reference the prefix hit and allocate pages for ``num_tokens``
+        tokens in total. Returns None (and changes nothing) if memory is
+        short."""
+        hit_pages, hit_hashes = self.match_prefix(token_ids, hashes)
+        need = (num_tokens + self.page_size - 1) // self.page_size - len(hit_pages)
+        # hit pages that are currently evictable do not count as free for us
+        hit_evictable = sum(1 for p in hit_pages if self.refcount[p] == 0)
+        if self.num_free() - hit_evictable < need:
+            return None
+        for p in hit_pages:
+            if self.refcount[p] == 0:
+                self.evictable.pop(p, None)
+            self.refcount[p] += 1
+        sb = SeqBlocks(pages=list(hit_pages), hashes=list(hit_hashes),
+                       num_cached_tokens=len(hit_pages) * self.page_size)
+        for _ in range(max(0, need)):
+            p = self._take_page()
+            self.refcount[p] = 1
+            sb.pages.append(p)
+        self.stats["hit_tokens"] += sb.num_cached_tokens
+        self.stats["query_tokens"] += len(token_ids)
+        return sb
+
+    def ensure_capacity(self, sb: SeqBlocks, num_tokens: int) -> bool:
+        """Grow ``sb`` to hold ``num_tokens`` tokens; False if memory is short."""
+        need = (num_tokens + self.page_size - 1) // self.page_size - len(sb.pages)
+        if need <= 0:
+            return True
+        if self.num_free() < need:
+            return False
+        for _ in range(need):
+            p = self._take_page()
+            self.refcount[p] = 1
+            sb.pages.append(p)
+        return True
+
+    def commit_full_pages(self, sb: SeqBlocks, token_ids: list[int], num_computed: int) -> None:
+        """Register every page that is now completely computed in the prefix
+        cache (and announce it)."""
+        sb.num_cached_tokens = max(sb.num_cached_tokens, num_computed)
+        if not self.enable_prefix_cache:
+            return
+        n_full = num_computed // self.page_size
+        start = len(sb.hashes)
+        if n_full <= start:
+            return
+        parent = sb.hashes[-1] if sb.hashes else 0
+        new_hashes = chain_hashes(token_ids[start * self.page_size: n_full * self.page_size], self.page_size,
+                                  parent=parent)
+        stored_h: list[int] = []
+        stored_tokens: list[int] = []
+        first_parent = parent
+        for i, h in enumerate(new_hashes):
+            idx = start + i
+            page = sb.pages[idx]
+            sb.hashes.append(h)
+            existing = self.hash_to_page.get(h)
+            if existing is None:
+                self.hash_to_page[h] = page
+                self.page_hash[page] = h
+                stored_h.append(h)
+                stored_tokens.extend(token_ids[idx * self.page_size:(idx + 1) * self.page_size])
+            elif existing != page:
+                # identical content computed twice (two requests raced on the
+                # same prefix); keep the first copy, this page stays private
+                pass
+        if stored_h:
+            self._emit("BlockStored", {
+                "block_hashes": stored_h,
+                "parent_block_hash": first_parent if start > 0 else None,
+                "token_ids": stored_tokens,
+                "block_size": self.page_size,
+                "lora_id": None,
+                "medium": "GPU",
+            })
+
+    def free(self, sb: SeqBlocks) -> None:
+        # release in reverse so the tail of a prefix is evicted before its head
+        for p in reversed(sb.pages):
+            self._release(p)
+        sb.pages = []
+        sb.hashes = []
+
+    def clear_cache(self) -> None:
+        """Drop every evictable cached page (AllBlocksCleared)."""
+        for page in list(self.evictable.keys()):
+            h = self.page_hash[page]
+            if h is not None and self.hash_to_page.get(h) == page:
+                del self.hash_to_page[h]
+            self.page_hash[page] = None
+            self.free_plain.append(page)
+        self.evictable.clear()
+        self._emit("AllBlocksCleared", {})
+
+    def cached_hashes(self) -> list[int]:
+        return list(self.hash_to_page.keys())

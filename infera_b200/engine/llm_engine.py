@@ -1,0 +1,213 @@
+"""The serving engine: scheduler + block manager + model runner.
+
+``LLMEngine.step()`` runs one iteration (schedule -> one forward -> sample
+-> bookkeeping) and returns the new tokens of every request that produced
+one. It is single-threaded by design; :mod:`infera_b200.engine.async_engine`
+runs it on a dedicated thread for the HTTP server.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import Callable
+
+import torch
+
+from infera_b200.engine.block_manager import BlockManager
+from infera_b200.engine.model_runner import ModelRunner
+from infera_b200.engine.request import Request, RequestOutput, SamplingParams, Status
+from infera_b200.engine.scheduler import Scheduler
+from infera_b200.models.config import DenseConfig, get_config
+from infera_b200.models.dense import DenseModel
+
+
+@dataclass
+class EngineConfig:
+    model: str = "llama-3.1-8b"
+    page_size: int = 16
+    max_num_seqs: int = 256
+    max_batched_tokens: int = 2048
+    gpu_memory_utilization: float = 0.90
+    num_pages: int | None = None          # override the memory-derived page count
+    use_cuda_graphs: bool = True
+    enable_prefix_cache: bool = True
+    seed: int = 0
+    long_prefill_threshold: int = 0
+    max_model_len: int | None = None
+    model_overrides: dict = field(default_factory=dict)
+
+
+class LLMEngine:
+    def __init__(self, cfg: EngineConfig, device: str | torch.device = "cuda:0",
+                 event_sink: Callable[[str, dict], None] | None = None, model_cfg: DenseConfig | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        mcfg = model_cfg or get_config(cfg.model)
+        for k, v in cfg.model_overrides.items():
+            setattr(mcfg, k, v)
+        if cfg.max_model_len:
+            mcfg.max_model_len = cfg.max_model_len
+        self.model_cfg = mcfg
+        self.model = DenseModel(mcfg, self.device, seed=cfg.seed)
+        num_pages = cfg.num_pages or self._derive_num_pages()
+        self._event_sink = event_sink
+        self.bm = BlockManager(num_pages, cfg.page_size, cfg.enable_prefix_cache, event_sink=self._on_kv_event)
+        self.scheduler = Scheduler(self.bm, cfg.max_num_seqs, cfg.max_batched_tokens, mcfg.max_model_len,
+                                   watermark_pages=max(1, num_pages // 100),
+                                   long_prefill_threshold=cfg.long_prefill_threshold)
+        self.runner = ModelRunner(self.model, num_pages, cfg.page_size, cfg.max_num_seqs, cfg.max_batched_tokens,
+                                  use_graphs=cfg.use_cuda_graphs)
+        self.requests: dict[str, Request] = {}
+        self.num_steps = 0
+        self.clock: Callable[[], float] = time.monotonic
+        self.counters = {"prompt_tokens": 0, "generation_tokens": 0, "finished": 0, "preemptions": 0}
+
+    # ------------------------------------------------------------------ sizing
+    def _derive_num_pages(self) -> int:
+        mcfg = self.model_cfg
+        per_page = 2 * mcfg.num_layers * self.cfg.page_size * mcfg.kv_size * 2
+        if self.device.type != "cuda":
+            return 512
+        torch.cuda.synchronize()
+        free, total = torch.cuda.mem_get_info(self.device)
+        # leave room for activations, graphs, workspaces
+        max_tok = self.cfg.max_batched_tokens + self.cfg.max_num_seqs
+        act = max_tok * (mcfg.hidden * 3 + mcfg.qkv_size + mcfg.q_size + mcfg.ffn) * 2
+        act += self.cfg.max_num_seqs * mcfg.vocab * 2 * 2
+        reserve = act + 2 * 1024 ** 3 + int(total * (1.0 - self.cfg.gpu_memory_utilization))
+        budget = max(0, free - reserve)
+        return max(64, budget // per_page)
+
+    # ------------------------------------------------------------------ events
+    def _on_kv_event(self, kind: str, payload: dict) -> None:
+        if self._event_sink is not None:
+            self._event_sink(kind, payload)
+
+    def set_event_sink(self, sink: Callable[[str, dict], None] | None) -> None:
+        self._event_sink = sink
+
+    # ------------------------------------------------------------------ API
+    def add_request(self, request_id: str, prompt_token_ids: list[int], sampling: SamplingParams | None = None,
+                    arrival_time: float | None = None) -> Request:
+        if request_id in self.requests:
+            raise ValueError(f"duplicate request id {request_id}")
+        if not prompt_token_ids:
+            raise ValueError("empty prompt")
+        req = Request(request_id=request_id, prompt_token_ids=list(prompt_token_ids),
+                      sampling=sampling or SamplingParams(), eos_token_id=self.model_cfg.eos_token_id)
+        req.arrival_time = self.clock() if arrival_time is None else arrival_time
+        self.requests[request_id] = req
+        self.scheduler.add(req)
+        return req
+
+    def abort_request(self, request_id: str) -> bool:
+        r = self.scheduler.abort(request_id)
+        if r is not None:
+            self.requests.pop(request_id, None)
+            return True
+        return False
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.num_unfinished() > 0
+
+    def num_running(self) -> int:
+        return len(self.scheduler.running)
+
+    def num_waiting(self) -> int:
+        return len(self.scheduler.waiting)
+
+    def _block_table_updates(self, chunks) -> tuple[list[int], list[int]]:
+        idx, val = [], []
+        mp = self.runner.max_pages
+        for c in chunks:
+            r = c.req
+            pages = r.blocks.pages
+            if r.pages_synced < len(pages):
+                base = r.table_row * mp
+                for j in range(r.pages_synced, len(pages)):
+                    idx.append(base + j)
+                    val.append(pages[j])
+                r.pages_synced = len(pages)
+        return idx, val
+
+    def step(self) -> list[RequestOutput]:
+        sched = self.scheduler.schedule()
+        outputs: list[RequestOutput] = []
+        for r in sched.preempted:
+            if r.status == Status.FINISHED_LENGTH:  # prompt longer than the model allows
+                outputs.append(self._finish(r, Status.FINISHED_LENGTH))
+            else:
+                self.counters["preemptions"] += 1
+        if sched.empty:
+            return outputs
+        upd = self._block_table_updates(sched.prefills + sched.decodes)
+        res = self.runner.execute(sched, upd)
+        now = self.clock()
+        self.num_steps += 1
+        for c in sched.prefills:
+            c.req.num_computed = c.start + c.num_tokens
+            self.counters["prompt_tokens"] += c.num_tokens
+        for c in sched.decodes:
+            c.req.num_computed = c.start + 1
+        # register newly completed pages in the prefix cache
+        for c in sched.prefills + sched.decodes:
+            r = c.req
+            if r.blocks is not None and r.num_computed // self.bm.page_size > len(r.blocks.hashes):
+                self.bm.commit_full_pages(r.blocks, r.all_token_ids(), r.num_computed)
+        for c, tok in zip(res.rows, res.token_ids):
+            r = c.req
+            if r.status != Status.RUNNING:
+                continue
+            r.output_token_ids.append(int(tok))
+            self.counters["generation_tokens"] += 1
+            if r.first_token_time is None:
+                r.first_token_time = now
+            r.token_times.append(now)
+            st = r.check_stop()
+            if st is not None:
+                outputs.append(self._finish(r, st, new=[int(tok)]))
+            else:
+                outputs.append(RequestOutput(r.request_id, [int(tok)], False, None, len(r.prompt_token_ids),
+                                             r.num_cached_prompt_tokens, len(r.output_token_ids)))
+        return outputs
+
+    def _finish(self, r: Request, st: Status, new: list[int] | None = None) -> RequestOutput:
+        self.scheduler.finish(r, st)
+        r.finish_time = self.clock()
+        self.requests.pop(r.request_id, None)
+        self.counters["finished"] += 1
+        return RequestOutput(r.request_id, new or [], True, st.value, len(r.prompt_token_ids),
+                             r.num_cached_prompt_tokens, len(r.output_token_ids))
+
+    # ------------------------------------------------------------------ helpers
+    def generate(self, prompts: list[list[int]], sampling: SamplingParams | None = None) -> list[list[int]]:
+        """Offline batch generation: returns the output ids of each prompt."""
+        ids = []
+        for i, p in enumerate(prompts):
+            rid = f"gen-{self.num_steps}-{i}"
+            self.add_request(rid, p, sampling)
+            ids.append(rid)
+        outs: dict[str, list[int]] = {rid: [] for rid in ids}
+        while self.has_unfinished():
+            for o in self.step():
+                if o.request_id in outs:
+                    outs[o.request_id].extend(o.new_token_ids)
+        return [outs[r] for r in ids]
+
+    def stats(self) -> dict:
+        bm = self.bm
+        q = max(1, bm.stats["query_tokens"])
+        return {
+            "running": self.num_running(),
+            "waiting": self.num_waiting(),
+            "kv_usage": bm.usage(),
+            "num_pages": bm.num_pages,
+            "prefix_hit_rate": bm.stats["hit_tokens"] / q,
+            "steps": self.num_steps,
+            "h2d_bytes": self.runner.h2d_bytes,
+            "d2h_bytes": self.runner.d2h_bytes,
+            **self.counters,
+        }

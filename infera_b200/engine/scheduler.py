@@ -1,0 +1,191 @@
+"""Continuous-batching scheduler with chunked prefill.
+
+Each step packs, within ``max_batched_tokens``:
+  1. one token for every running sequence that is decoding;
+  2. the next chunk of every running sequence still in prefill;
+  3. new sequences from the waiting queue (FCFS), each with as large a
+     first chunk as the budget allows, while pages and sequence slots last.
+
+A decoding sequence that cannot get a page preempts the most recently
+admitted running sequence (its pages are freed and it re-enters the waiting
+queue at the front; its prompt plus generated tokens are recomputed, with
+any surviving prefix pages reused through the prefix cache).
+
+Reference parity: the reference relies on vLLM's / SGLang's schedulers; the
+router-visible behaviour it depends on (prefix-cache hits announced through
+KV events, in-flight counts for drain) is reproduced here.
+"""
+
+from __future__ import annotations
+
+from collections import deque
+from dataclasses import dataclass, field
+
+from infera_b200.engine.block_manager import BlockManager
+from infera_b200.engine.request import Request, Status
+
+
+@dataclass
+class ScheduledChunk:
+    req: Request
+    start: int          # first position computed this step
+    num_tokens: int
+    is_decode: bool
+    needs_logits: bool  # the chunk ends at the last known token -> sample
+
+
+@dataclass
+class SchedulerOutput:
+    prefills: list[ScheduledChunk] = field(default_factory=list)
+    decodes: list[ScheduledChunk] = field(default_factory=list)
+    preempted: list[Request] = field(default_factory=list)
+
+    @property
+    def num_tokens(self) -> int:
+        return sum(c.num_tokens for c in self.prefills) + len(self.decodes)
+
+    @property
+    def empty(self) -> bool:
+        return not self.prefills and not self.decodes
+
+
+class Scheduler:
+    def __init__(self, block_manager: BlockManager, max_num_seqs: int = 256, max_batched_tokens: int = 4096,
+                 max_model_len: int = 32768, watermark_pages: int = 0, long_prefill_threshold: int = 0):
+        self.bm = block_manager
+        self.max_num_seqs = max_num_seqs
+        self.max_batched_tokens = max_batched_tokens
+        self.max_model_len = max_model_len
+        self.watermark = watermark_pages
+        # a single sequence's chunk is capped so that one long prompt cannot
+        # occupy the whole budget while decode latency suffers (0: no cap)
+        self.long_prefill_threshold = long_prefill_threshold
+        self.waiting: deque[Request] = deque()
+        self.running: list[Request] = []
+        self.free_rows: list[int] = list(range(max_num_seqs - 1, -1, -1))
+
+    # ------------------------------------------------------------------
+    def add(self, req: Request) -> None:
+        self.waiting.append(req)
+
+    def num_unfinished(self) -> int:
+        return len(self.waiting) + len(self.running)
+
+    def abort(self, request_id: str) -> Request | None:
+        for i, r in enumerate(self.running):
+            if r.request_id == request_id:
+                self.running.pop(i)
+                self._release(r)
+                r.status = Status.FINISHED_ABORTED
+                return r
+        for r in list(self.waiting):
+            if r.request_id == request_id:
+                self.waiting.remove(r)
+                r.status = Status.FINISHED_ABORTED
+                return r
+        return None
+
+    def _release(self, r: Request) -> None:
+        if r.blocks is not None:
+            self.bm.free(r.blocks)
+            r.blocks = None
+        if r.table_row >= 0:
+            self.free_rows.append(r.table_row)
+            r.table_row = -1
+        r.pages_synced = 0
+
+    def finish(self, r: Request, status: Status) -> None:
+        r.status = status
+        if r in self.running:
+            self.running.remove(r)
+        if r.blocks is not None:
+            # make everything computed so far reusable by later turns
+            self.bm.commit_full_pages(r.blocks, r.all_token_ids(), r.num_computed)
+        self._release(r)
+
+    def _preempt(self, victim: Request, out: SchedulerOutput) -> None:
+        self.running.remove(victim)
+        if victim.blocks is not None:
+            self.bm.commit_full_pages(victim.blocks, victim.all_token_ids(), victim.num_computed)
+        self._release(victim)
+        victim.status = Status.WAITING
+        victim.num_computed = 0
+        victim.num_preemptions += 1
+        victim.prompt_hashes = None
+        self.waiting.appendleft(victim)
+        out.preempted.append(victim)
+
+    # ------------------------------------------------------------------
+    def schedule(self) -> SchedulerOutput:
+        out = SchedulerOutput()
+        budget = self.max_batched_tokens
+        ps = self.bm.page_size
+
+        # 1 + 2: running sequences (oldest first)
+        i = 0
+        while i < len(self.running):
+            r = self.running[i]
+            pending = r.num_tokens - r.num_computed
+            if pending <= 0:
+                i += 1
+                continue
+            is_decode = pending == 1 and len(r.output_token_ids) > 0
+            n = 1 if is_decode else min(pending, budget)
+            if self.long_prefill_threshold and not is_decode:
+                n = min(n, self.long_prefill_threshold)
+            if n <= 0:
+                i += 1
+                continue
+            while not self.bm.ensure_capacity(r.blocks, r.num_computed + n):
+                victim = self.running[-1]
+                if victim is r:
+                    # nothing else to take pages from: this one waits
+                    self._preempt(r, out)
+                    r = None
+                    break
+                self._preempt(victim, out)
+            if r is None:
+                continue
+            chunk = ScheduledChunk(r, r.num_computed, n, is_decode, r.num_computed + n == r.num_tokens)
+            (out.decodes if is_decode else out.prefills).append(chunk)
+            budget -= n
+            i += 1
+            if budget <= 0:
+                break
+
+        # 3: admit waiting sequences
+        while self.waiting and budget > 0 and self.free_rows and len(self.running) < self.max_num_seqs:
+            r = self.waiting[0]
+            toks = r.all_token_ids()
+            total = len(toks)
+            if total >= self.max_model_len:
+                self.waiting.popleft()
+                r.status = Status.FINISHED_LENGTH
+                r.finish_time = None
+                out.preempted.append(r)  # reported as finished by the engine
+                continue
+            if r.prompt_hashes is None:
+                from infera_b200.utils.hashing import chain_hashes
+
+                r.prompt_hashes = chain_hashes(toks, ps)
+            sb = self.bm.allocate_prompt(toks, total, r.prompt_hashes)
+            if sb is None or not self.bm.can_allocate(0, self.watermark):
+                if sb is not None:
+                    self.bm.free(sb)
+                break
+            self.waiting.popleft()
+            r.blocks = sb
+            r.num_computed = sb.num_cached_tokens
+            if r.num_preemptions == 0:
+                r.num_cached_prompt_tokens = sb.num_cached_tokens
+            r.status = Status.RUNNING
+            r.table_row = self.free_rows.pop()
+            r.pages_synced = 0
+            self.running.append(r)
+            pending = total - r.num_computed
+            n = min(pending, budget)
+            if self.long_prefill_threshold:
+                n = min(n, self.long_prefill_threshold)
+            out.prefills.append(ScheduledChunk(r, r.num_computed, n, False, r.num_computed + n == total))
+            budget -= n
+        return out

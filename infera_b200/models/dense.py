@@ -1,0 +1,182 @@
+"""Dense GQA decoder (Llama-3 / Qwen3 shapes) on the sm_100a ops.
+
+The forward pass works on a flat batch of tokens (``ForwardBatch``): first
+the prefill chunks of zero or more sequences, then one token for each
+decoding sequence. Per layer:
+
+    qkv  = x @ Wqkv^T                       tcgen05 GEMM
+    rope(q, k); k, v -> paged cache         fused kernel
+    attn = prefill FA (chunks) | decode split-KV (one token per seq)
+    o    = attn @ Wo^T                      tcgen05 GEMM
+    h   += o ; x = rmsnorm(h)               fused kernel
+    act  = silu(x Wg^T) * (x Wu^T)          tcgen05 GEMM, SwiGLU epilogue
+    d    = act @ Wd^T                       tcgen05 GEMM
+    h   += d ; x = rmsnorm(h)               fused kernel (next layer's norm)
+
+The gate/up weight is stored row-interleaved (gate_0, up_0, gate_1, ...)
+so the GEMM epilogue can apply SwiGLU without a second pass.
+Only the rows in ``logits_idx`` reach the LM head.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from infera_b200.models.config import DenseConfig
+from infera_b200.ops import kernels as K
+
+
+@dataclass
+class ForwardBatch:
+    """Device-side metadata of one engine step (all int32 on the model's device)."""
+
+    token_ids: torch.Tensor        # [T]
+    positions: torch.Tensor        # [T]
+    slots: torch.Tensor            # [T] cache slot of each token (page*16+off)
+    logits_idx: torch.Tensor       # [S] rows whose logits are needed
+    num_prefill_tokens: int = 0
+    # prefill (chunks) metadata
+    p_q_start: torch.Tensor | None = None
+    p_q_len: torch.Tensor | None = None
+    p_ctx_len: torch.Tensor | None = None
+    p_block_table: torch.Tensor | None = None
+    p_tiles: torch.Tensor | None = None
+    p_host_meta: tuple[list[int], list[int]] | None = None
+    p_bt_rows: torch.Tensor | None = None
+    # decode metadata (rows [num_prefill_tokens, T))
+    d_block_table: torch.Tensor | None = None
+    d_seq_lens: torch.Tensor | None = None
+    d_bt_rows: torch.Tensor | None = None
+    d_splits: int = 1
+    num_decode: int = 0
+
+
+class DenseWeights:
+    def __init__(self, cfg: DenseConfig, device: torch.device, seed: int = 0, std: float = 0.02):
+        self.cfg = cfg
+        g = torch.Generator(device=device).manual_seed(seed)
+        bf = torch.bfloat16
+
+        def rnd(*shape, scale=std):
+            return (torch.randn(*shape, generator=g, device=device, dtype=torch.float32) * scale).to(bf)
+
+        H = cfg.hidden
+        self.embed = rnd(cfg.vocab, H, scale=1.0)
+        self.layers = []
+        out_scale = std / math.sqrt(2 * cfg.num_layers)
+        for _ in range(cfg.num_layers):
+            lw = {
+                "ln1": torch.ones(H, dtype=bf, device=device),
+                "ln2": torch.ones(H, dtype=bf, device=device),
+                "qkv": rnd(cfg.qkv_size, H),
+                "o": rnd(H, cfg.q_size, scale=out_scale),
+                "gate_up": rnd(2 * cfg.ffn, H),      # interleaved rows (g0, u0, g1, u1, ...)
+                "down": rnd(H, cfg.ffn, scale=out_scale),
+            }
+            if cfg.qk_norm:
+                lw["q_norm"] = torch.ones(cfg.head_dim, dtype=bf, device=device)
+                lw["k_norm"] = torch.ones(cfg.head_dim, dtype=bf, device=device)
+            self.layers.append(lw)
+        self.final_norm = torch.ones(H, dtype=bf, device=device)
+        self.lm_head = rnd(cfg.vocab, H)
+
+    def nbytes(self) -> int:
+        n = self.embed.numel() + self.lm_head.numel() + self.final_norm.numel()
+        for lw in self.layers:
+            n += sum(t.numel() for t in lw.values())
+        return 2 * n
+
+
+class DenseModel:
+    """Stateless forward over a paged KV cache owned by the engine."""
+
+    def __init__(self, cfg: DenseConfig, device: torch.device | str, seed: int = 0):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.w = DenseWeights(cfg, self.device, seed=seed)
+        self.cos_sin = K.rope_cos_sin(cfg.max_model_len, cfg.head_dim, cfg.rope_theta, cfg.rope_scaling,
+                                      device=self.device)
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    # ------------------------------------------------------------------
+    def _qk_norm(self, qkv: torch.Tensor, lw: dict) -> None:
+        cfg = self.cfg
+        T = qkv.shape[0]
+        D = cfg.head_dim
+        nq, nk = cfg.num_heads, cfg.num_kv_heads
+        q = qkv[:, : nq * D].reshape(T * nq, D)
+        k = qkv[:, nq * D:(nq + nk) * D].reshape(T * nk, D)
+        qkv[:, : nq * D] = K.rmsnorm(q.contiguous(), lw["q_norm"], cfg.rms_eps).view(T, nq * D)
+        qkv[:, nq * D:(nq + nk) * D] = K.rmsnorm(k.contiguous(), lw["k_norm"], cfg.rms_eps).view(T, nk * D)
+
+    def forward(self, fb: ForwardBatch, k_caches: torch.Tensor, v_caches: torch.Tensor,
+                bufs: dict | None = None) -> torch.Tensor:
+        """Returns logits [S, vocab] for the rows in ``fb.logits_idx``.
+
+        ``k_caches`` / ``v_caches``: [num_layers, num_slots, kv_size] bf16.
+        ``bufs``: optional preallocated activations (used by CUDA graphs).
+        """
+        cfg = self.cfg
+        T = fb.token_ids.shape[0]
+        Tp = fb.num_prefill_tokens
+        H = cfg.hidden
+        dev = self.device
+        bf = torch.bfloat16
+        if bufs is None:
+            bufs = {}
+        h = bufs.get("h")
+        h = K.embed(fb.token_ids, self.w.embed, out=None if h is None else h[:T])
+        x = bufs["x"][:T] if "x" in bufs else torch.empty(T, H, dtype=bf, device=dev)
+        qkv = bufs["qkv"][:T] if "qkv" in bufs else torch.empty(T, cfg.qkv_size, dtype=bf, device=dev)
+        attn = bufs["attn"][:T] if "attn" in bufs else torch.empty(T, cfg.q_size, dtype=bf, device=dev)
+        o = bufs["o"][:T] if "o" in bufs else torch.empty(T, H, dtype=bf, device=dev)
+        act = bufs["act"][:T] if "act" in bufs else torch.empty(T, cfg.ffn, dtype=bf, device=dev)
+        K.rmsnorm(h, self.w.layers[0]["ln1"], cfg.rms_eps, out=x)
+        for li, lw in enumerate(self.w.layers):
+            K.linear(x, lw["qkv"], out=qkv)
+            if cfg.qk_norm:
+                self._qk_norm(qkv, lw)
+            kc, vc = k_caches[li], v_caches[li]
+            K.rope_kvwrite(qkv, fb.positions, fb.slots, self.cos_sin, cfg.num_heads, cfg.num_kv_heads,
+                           cfg.head_dim, kc, vc)
+            if Tp > 0:
+                K.attn_prefill(qkv[:Tp], kc, vc, fb.p_block_table, fb.p_q_start, fb.p_q_len, fb.p_ctx_len,
+                               fb.p_tiles, cfg.num_heads, cfg.num_kv_heads, self.scale, out=attn[:Tp],
+                               host_meta=fb.p_host_meta, bt_rows=fb.p_bt_rows)
+            if fb.num_decode > 0:
+                K.attn_decode(qkv[Tp:T], kc, vc, fb.d_block_table, fb.d_seq_lens, cfg.num_heads, cfg.num_kv_heads,
+                              self.scale, splits=fb.d_splits, out=attn[Tp:T], bt_rows=fb.d_bt_rows)
+            K.linear(attn, lw["o"], out=o)
+            K.add_rmsnorm(o, h, lw["ln2"], cfg.rms_eps, out=x)
+            K.linear(x, lw["gate_up"], out=act, swiglu=True)
+            K.linear(act, lw["down"], out=o)
+            nxt = self.w.layers[li + 1]["ln1"] if li + 1 < cfg.num_layers else self.w.final_norm
+            K.add_rmsnorm(o, h, nxt, cfg.rms_eps, out=x)
+        S = fb.logits_idx.shape[0]
+        xs = bufs["xs"][:S] if "xs" in bufs else None
+        xs = K.gather_rows(x, fb.logits_idx, out=xs)
+        logits = bufs["logits"][:S] if "logits" in bufs else None
+        return K.linear(xs, self.w.lm_head, out=logits)
+
+    def alloc_buffers(self, max_tokens: int, max_seqs: int) -> dict:
+        cfg = self.cfg
+        bf = torch.bfloat16
+        dev = self.device
+        return {
+            "h": torch.empty(max_tokens, cfg.hidden, dtype=bf, device=dev),
+            "x": torch.empty(max_tokens, cfg.hidden, dtype=bf, device=dev),
+            "qkv": torch.empty(max_tokens, cfg.qkv_size, dtype=bf, device=dev),
+            "attn": torch.empty(max_tokens, cfg.q_size, dtype=bf, device=dev),
+            "o": torch.empty(max_tokens, cfg.hidden, dtype=bf, device=dev),
+            "act": torch.empty(max_tokens, cfg.ffn, dtype=bf, device=dev),
+            "xs": torch.empty(max_seqs, cfg.hidden, dtype=bf, device=dev),
+            "logits": torch.empty(max_seqs, cfg.vocab, dtype=bf, device=dev),
+        }
+
+    def max_gemm_workspace(self, max_tokens: int) -> int:
+        cfg = self.cfg
+        widest = max(cfg.qkv_size, cfg.hidden, 2 * cfg.ffn, cfg.vocab)
+        return max_tokens * widest

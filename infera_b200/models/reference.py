@@ -1,0 +1,72 @@
+"""Plain fp32 PyTorch forward of the dense decoder over a full sequence
+(no paging, no chunking, no cache). The oracle for engine tests."""
+
+from __future__ import annotations
+
+import torch
+
+from infera_b200.models.dense import DenseModel
+
+
+@torch.no_grad()
+def reference_logits(model: DenseModel, token_ids: list[int]) -> torch.Tensor:
+    """Logits [len(token_ids), vocab] in fp32, computed on the CPU."""
+    cfg = model.cfg
+    w = model.w
+    T = len(token_ids)
+    D = cfg.head_dim
+    nq, nk = cfg.num_heads, cfg.num_kv_heads
+    G = nq // nk
+    ids = torch.tensor(token_ids, dtype=torch.long)
+    cs = model.cos_sin.cpu()[:T]
+    cos, sin = cs[..., 0], cs[..., 1]
+
+    def f(t):
+        return t.detach().float().cpu()
+
+    def norm(x, g, eps=cfg.rms_eps):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * f(g)
+
+    def rope(x):  # [T, heads, D]
+        half = D // 2
+        a, b = x[..., :half], x[..., half:]
+        c, s = cos[:, None, :], sin[:, None, :]
+        return torch.cat([a * c - b * s, b * c + a * s], dim=-1)
+
+    h = f(w.embed)[ids]
+    mask = torch.triu(torch.ones(T, T, dtype=torch.bool), 1)
+    for lw in w.layers:
+        x = norm(h, lw["ln1"])
+        qkv = x @ f(lw["qkv"]).t()
+        q = qkv[:, : nq * D].view(T, nq, D)
+        k = qkv[:, nq * D:(nq + nk) * D].view(T, nk, D)
+        v = qkv[:, (nq + nk) * D:].view(T, nk, D)
+        if cfg.qk_norm:
+            q = norm(q, lw["q_norm"])
+            k = norm(k, lw["k_norm"])
+        q, k = rope(q), rope(k)
+        k = k.repeat_interleave(G, dim=1)
+        v = v.repeat_interleave(G, dim=1)
+        s = torch.einsum("thd,shd->hts", q, k) / D ** 0.5
+        s = s.masked_fill(mask[None], float("-inf"))
+        o = torch.einsum("hts,shd->thd", torch.softmax(s, -1), v).reshape(T, nq * D)
+        h = h + o @ f(lw["o"]).t()
+        x = norm(h, lw["ln2"])
+        gu = x @ f(lw["gate_up"]).t()
+        act = torch.nn.functional.silu(gu[:, 0::2]) * gu[:, 1::2]
+        h = h + act @ f(lw["down"]).t()
+    x = norm(h, w.final_norm)
+    return x @ f(w.lm_head).t()
+
+
+def reference_greedy(model: DenseModel, prompt: list[int], n: int) -> tuple[list[int], list[float]]:
+    """Greedy continuation and the top1-top2 logit margin at each step."""
+    toks = list(prompt)
+    out, margins = [], []
+    for _ in range(n):
+        lg = reference_logits(model, toks)[-1]
+        top = torch.topk(lg, 2)
+        out.append(int(top.indices[0]))
+        margins.append(float(top.values[0] - top.values[1]))
+        toks.append(out[-1])
+    return out, margins

@@ -1,0 +1,96 @@
+"""Loader for the in-tree native libraries.
+
+``libib200_kernels.so`` holds every sm_100a CUDA kernel behind a C ABI;
+``libib200_runtime.so`` holds the host-side C++ runtime (hashing, block
+allocator). Both are built in-tree by :mod:`infera_b200.build` and loaded
+with :mod:`ctypes`.
+
+On a machine with a GPU a missing kernel library is an error, never a silent
+fallback: :func:`kernels` raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+_LIB_DIR = Path(__file__).resolve().parent.parent / "lib"
+_lock = threading.Lock()
+_kernels: ctypes.CDLL | None = None
+_runtime: ctypes.CDLL | None = None
+
+c_int = ctypes.c_int
+c_ll = ctypes.c_longlong
+c_float = ctypes.c_float
+c_vp = ctypes.c_void_p
+c_ip = ctypes.c_void_p  # int* passed as raw address
+
+
+def kernel_lib_path() -> Path:
+    return _LIB_DIR / "libib200_kernels.so"
+
+
+def runtime_lib_path() -> Path:
+    return _LIB_DIR / "libib200_runtime.so"
+
+
+def _declare_kernels(lib: ctypes.CDLL) -> None:
+    sig = {
+        "ib_gemm_bf16": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_int, c_vp,
+                         c_vp],
+        "ib_gemm_bf16_plan": [c_int, c_int, c_int, c_int, c_int, c_vp],
+        "ib_rmsnorm": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_vp],
+        "ib_add_rmsnorm": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float, c_vp],
+        "ib_rope_kvwrite": [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp],
+        "ib_embed": [c_vp, c_vp, c_vp, c_int, c_int, c_vp],
+        "ib_sample": [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp],
+        "ib_gather_rows": [c_vp, c_vp, c_vp, c_int, c_int, c_vp],
+        "ib_attn_decode": [c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float,
+                           c_vp, c_vp, c_vp, c_int, c_vp],
+        "ib_attn_prefill": [c_vp, c_int, c_int, c_vp, c_vp, c_ll, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int,
+                            c_int, c_int, c_float, c_vp, c_int, c_vp, c_vp],
+        "ib_scatter_i32": [c_vp, c_vp, c_vp, c_int, c_vp],
+    }
+    for name, args in sig.items():
+        fn = getattr(lib, name, None)
+        if fn is None:
+            continue
+        fn.argtypes = args
+        fn.restype = c_int if name != "ib_gemm_bf16_plan" else None
+
+
+def kernels() -> ctypes.CDLL:
+    """The CUDA kernel library; raises if it was not built."""
+    global _kernels
+    if _kernels is None:
+        with _lock:
+            if _kernels is None:
+                path = kernel_lib_path()
+                if not path.exists():
+                    raise RuntimeError(
+                        f"{path} is missing: build it with `python -m infera_b200.build` "
+                        "(the CUDA path has no fallback)")
+                lib = ctypes.CDLL(str(path), mode=os.RTLD_NOW | os.RTLD_GLOBAL)
+                _declare_kernels(lib)
+                _kernels = lib
+    return _kernels
+
+
+def runtime() -> ctypes.CDLL | None:
+    """The host C++ runtime library, or None when it was not built."""
+    global _runtime
+    if _runtime is None:
+        with _lock:
+            if _runtime is None:
+                path = runtime_lib_path()
+                if not path.exists():
+                    return None
+                _runtime = ctypes.CDLL(str(path))
+    return _runtime
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed with code {rc}")

@@ -1,0 +1,419 @@
+"""Tensor-level entry points for the sm_100a kernels.
+
+Every function takes and returns torch tensors. On CUDA tensors it calls the
+native kernel from ``libib200_kernels.so`` (there is no library fallback on a
+GPU). On CPU tensors it runs the plain fp32 PyTorch restatement of the same
+op, which is also the oracle the GPU tests compare against.
+
+Per-device scratch (the split-K fp32 workspace, the decode split-KV
+partials and the kernel status word) lives in :class:`DeviceScratch`; the
+engine sizes it once at start-up so that CUDA-graph capture never allocates.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from infera_b200.ops import _native
+
+# ---------------------------------------------------------------- scratch
+
+
+@dataclass
+class DeviceScratch:
+    device: torch.device
+    status: torch.Tensor
+    gemm_ws: torch.Tensor = field(default_factory=lambda: torch.empty(0))
+    dec_o: torch.Tensor = field(default_factory=lambda: torch.empty(0))
+    dec_lse: torch.Tensor = field(default_factory=lambda: torch.empty(0))
+    frozen: bool = False
+
+    def ensure_gemm(self, numel: int) -> torch.Tensor:
+        if self.gemm_ws.numel() < numel:
+            if self.frozen:
+                raise RuntimeError(f"GEMM workspace too small ({self.gemm_ws.numel()} < {numel}) after freeze")
+            self.gemm_ws = torch.zeros(numel, dtype=torch.float32, device=self.device)
+        return self.gemm_ws
+
+    def ensure_decode(self, o_numel: int, lse_numel: int) -> tuple[torch.Tensor, torch.Tensor]:
+        if self.dec_o.numel() < o_numel or self.dec_lse.numel() < lse_numel:
+            if self.frozen:
+                raise RuntimeError("decode scratch too small after freeze")
+            self.dec_o = torch.empty(max(o_numel, self.dec_o.numel()), dtype=torch.float32, device=self.device)
+            self.dec_lse = torch.empty(max(lse_numel, self.dec_lse.numel()), dtype=torch.float32,
+                                       device=self.device)
+        return self.dec_o, self.dec_lse
+
+    def read_status(self) -> int:
+        return int(self.status.item())
+
+    def clear_status(self) -> None:
+        self.status.zero_()
+
+
+_scratch: dict[int, DeviceScratch] = {}
+
+
+def scratch(device: torch.device | int | None = None) -> DeviceScratch:
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    elif isinstance(device, int):
+        device = torch.device("cuda", device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    s = _scratch.get(idx)
+    if s is None:
+        dev = torch.device("cuda", idx)
+        s = DeviceScratch(device=dev, status=torch.zeros(1, dtype=torch.int32, device=dev))
+        _scratch[idx] = s
+    return s
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+# ---------------------------------------------------------------- GEMM
+
+
+def gemm_plan(M: int, N: int, K: int, num_sms: int = 148, force_split: int = 0) -> dict:
+    out = (_native.c_int * 7)()
+    _native.kernels().ib_gemm_bf16_plan(M, N, K, num_sms, force_split, out)
+    keys = ["swap", "bn", "p_tiles", "q_tiles", "splits", "kbps", "grid"]
+    return dict(zip(keys, list(out)))
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, swiglu: bool = False,
+           force_split: int = 0) -> torch.Tensor:
+    """y = x @ w.T (bf16 in/out, fp32 accumulate).
+
+    ``swiglu=True`` expects ``w`` rows interleaved as (gate_0, up_0, gate_1,
+    up_1, ...) and returns silu(gate) * up with half the columns.
+    """
+    M, K = x.shape
+    N = w.shape[0]
+    n_out = N // 2 if swiglu else N
+    if not x.is_cuda:
+        y = x.float() @ w.float().t()
+        if swiglu:
+            g, u = y[:, 0::2], y[:, 1::2]
+            y = torch.nn.functional.silu(g) * u
+        y = y.to(torch.bfloat16)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    assert x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+    assert x.stride(1) == 1 and w.stride(1) == 1
+    if out is None:
+        out = torch.empty(M, n_out, dtype=torch.bfloat16, device=x.device)
+    sc = scratch(x.device)
+    ws = sc.ensure_gemm(M * N)
+    rc = _native.kernels().ib_gemm_bf16(x.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, K, x.stride(0),
+                                        w.stride(0), out.stride(0), 1 if swiglu else 0, ws.data_ptr(),
+                                        force_split, sc.status.data_ptr(), _stream())
+    _native.check(rc, "ib_gemm_bf16")
+    return out
+
+
+# ---------------------------------------------------------------- norms / rope / embed
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    if not x.is_cuda:
+        xf = x.float()
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+        y = y.to(x.dtype)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    T, H = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    rc = _native.kernels().ib_rmsnorm(x.data_ptr(), w.data_ptr(), out.data_ptr(), T, H, x.stride(0), out.stride(0),
+                                      eps, _stream())
+    _native.check(rc, "ib_rmsnorm")
+    return out
+
+
+def add_rmsnorm(delta: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """residual += delta (in place, bf16); return rmsnorm(residual) * w."""
+    if not residual.is_cuda:
+        residual.copy_((residual.float() + delta.float()).to(residual.dtype))
+        return rmsnorm(residual, w, eps, out)
+    T, H = residual.shape
+    if out is None:
+        out = torch.empty_like(residual)
+    rc = _native.kernels().ib_add_rmsnorm(delta.data_ptr(), residual.data_ptr(), w.data_ptr(), out.data_ptr(), T, H,
+                                          delta.stride(0), residual.stride(0), out.stride(0), eps, _stream())
+    _native.check(rc, "ib_add_rmsnorm")
+    return out
+
+
+def rope_cos_sin(max_pos: int, head_dim: int, theta: float, scaling: dict | None = None,
+                 device: torch.device | str = "cpu") -> torch.Tensor:
+    """[max_pos, head_dim/2, 2] fp32 (cos, sin) table, with optional
+    Llama-3 frequency scaling (factor, low/high_freq_factor,
+    original_max_position_embeddings)."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    if scaling:
+        factor = scaling.get("factor", 8.0)
+        lo = scaling.get("low_freq_factor", 1.0)
+        hi = scaling.get("high_freq_factor", 4.0)
+        orig = scaling.get("original_max_position_embeddings", 8192)
+        lo_wl, hi_wl = orig / lo, orig / hi
+        wl = 2 * math.pi / inv
+        smooth = (orig / wl - lo) / (hi - lo)
+        scaled = torch.where(wl > lo_wl, inv / factor, inv)
+        mid = (wl <= lo_wl) & (wl >= hi_wl)
+        scaled = torch.where(mid, (1 - smooth) * inv / factor + smooth * inv, scaled)
+        inv = scaled
+    t = torch.arange(max_pos, dtype=torch.float64)
+    f = torch.outer(t, inv)
+    cs = torch.stack([f.cos(), f.sin()], dim=-1).to(torch.float32)
+    return cs.to(device)
+
+
+def rope_kvwrite(qkv: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor, cos_sin: torch.Tensor, hq: int,
+                 hkv: int, head_dim: int, k_cache: torch.Tensor, v_cache: torch.Tensor) -> None:
+    """Rotate q/k of ``qkv`` in place and store k, v at ``slots`` of the
+    caches ([num_slots, hkv*head_dim]); slot -1 skips the store."""
+    T = qkv.shape[0]
+    if not qkv.is_cuda:
+        half = head_dim // 2
+        cs = cos_sin[pos.long()]  # [T, half, 2]
+        c, s = cs[..., 0], cs[..., 1]
+        x = qkv[:, : (hq + hkv) * head_dim].float().view(T, hq + hkv, head_dim)
+        a, b = x[..., :half], x[..., half:]
+        c, s = c[:, None, :], s[:, None, :]
+        ra, rb = a * c - b * s, b * c + a * s
+        rot = torch.cat([ra, rb], dim=-1).to(qkv.dtype).view(T, -1)
+        qkv[:, : (hq + hkv) * head_dim] = rot
+        keep = slots >= 0
+        if keep.any():
+            idx = slots[keep].long()
+            k = qkv[keep, hq * head_dim:(hq + hkv) * head_dim]
+            v = qkv[keep, (hq + hkv) * head_dim:(hq + 2 * hkv) * head_dim]
+            k_cache[idx] = k
+            v_cache[idx] = v
+        return
+    rc = _native.kernels().ib_rope_kvwrite(qkv.data_ptr(), T, qkv.stride(0), pos.data_ptr(), slots.data_ptr(),
+                                           cos_sin.data_ptr(), hq, hkv, head_dim, k_cache.data_ptr(),
+                                           v_cache.data_ptr(), k_cache.stride(0), _stream())
+    _native.check(rc, "ib_rope_kvwrite")
+
+
+def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    if not table.is_cuda:
+        y = table[ids.long()]
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    T = ids.shape[0]
+    H = table.shape[1]
+    if out is None:
+        out = torch.empty(T, H, dtype=table.dtype, device=table.device)
+    rc = _native.kernels().ib_embed(ids.data_ptr(), table.data_ptr(), out.data_ptr(), T, H, _stream())
+    _native.check(rc, "ib_embed")
+    return out
+
+
+def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    if not src.is_cuda:
+        y = src[idx.long()]
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    n = idx.shape[0]
+    if out is None:
+        out = torch.empty(n, src.shape[1], dtype=src.dtype, device=src.device)
+    rc = _native.kernels().ib_gather_rows(src.data_ptr(), idx.data_ptr(), out.data_ptr(), n, src.stride(0),
+                                          _stream())
+    _native.check(rc, "ib_gather_rows")
+    return out
+
+
+def _mix64(z: torch.Tensor) -> torch.Tensor:
+    # same splitmix64 finaliser as the kernel, on uint64 emulated in int64
+    m = (1 << 64) - 1
+    z = [int(v) & m for v in z.tolist()]
+    out = []
+    for v in z:
+        v = (v + 0x9E3779B97F4A7C15) & m
+        v = ((v ^ (v >> 30)) * 0xBF58476D1CE4E5B9) & m
+        v = ((v ^ (v >> 27)) * 0x94D049BB133111EB) & m
+        out.append(v ^ (v >> 31))
+    return out
+
+
+def sample(logits: torch.Tensor, temperature: torch.Tensor | None = None, seeds: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy (temperature 0) or Gumbel-max sampling per row -> int32 ids."""
+    B, V = logits.shape
+    if not logits.is_cuda:
+        x = logits.float()
+        if temperature is not None and bool((temperature > 0).any()):
+            res = []
+            for b in range(B):
+                T = float(temperature[b])
+                if T <= 0:
+                    res.append(int(torch.argmax(x[b])))
+                    continue
+                seed = int(seeds[b]) if seeds is not None else 0
+                m = (1 << 64) - 1
+                keys = [((seed * 0x100000001B3) & m) ^ i for i in range(V)]
+                hs = _mix64(torch.tensor([k if k < (1 << 63) else k - (1 << 64) for k in keys]))
+                u = torch.tensor([((h >> 40) + 0.5) / 16777216.0 for h in hs], dtype=torch.float32)
+                g = x[b] / T - torch.log(-torch.log(u))
+                res.append(int(torch.argmax(g)))
+            y = torch.tensor(res, dtype=torch.int32)
+        else:
+            y = torch.argmax(x, dim=-1).to(torch.int32)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(B, dtype=torch.int32, device=logits.device)
+    rc = _native.kernels().ib_sample(logits.data_ptr(), B, logits.stride(0), V, _ptr(temperature), _ptr(seeds),
+                                     out.data_ptr(), _stream())
+    _native.check(rc, "ib_sample")
+    return out
+
+
+# ---------------------------------------------------------------- attention
+
+
+def _ref_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                   q_pos: list[list[int]], ctx_lens: list[int], hq: int, hkv: int, scale: float,
+                   page: int = 16) -> list[torch.Tensor]:
+    """fp32 oracle: for each sequence, q rows [n_i, hq*D] attend causally to
+    the first ctx_len keys of its pages. Returns a list of [n_i, hq*D]."""
+    D = k_cache.shape[1] // hkv
+    G = hq // hkv
+    outs = []
+    row = 0
+    for i, ctx in enumerate(ctx_lens):
+        n = len(q_pos[i])
+        pages = block_table[i, : (ctx + page - 1) // page].long()
+        slots = (pages[:, None] * page + torch.arange(page)[None, :]).reshape(-1)[:ctx]
+        k = k_cache[slots].float().view(ctx, hkv, D)
+        v = v_cache[slots].float().view(ctx, hkv, D)
+        qi = q[row: row + n].float().view(n, hq, D)
+        k = k.repeat_interleave(G, dim=1)
+        v = v.repeat_interleave(G, dim=1)
+        s = torch.einsum("nhd,khd->hnk", qi, k) * scale
+        pos = torch.tensor(q_pos[i])[:, None]
+        mask = torch.arange(ctx)[None, :] > pos
+        s = s.masked_fill(mask[None], float("-inf"))
+        p = torch.softmax(s, dim=-1)
+        o = torch.einsum("hnk,khd->nhd", p, v).reshape(n, hq * D)
+        outs.append(o)
+        row += n
+    return outs
+
+
+def decode_splits(batch: int, hkv: int, max_len: int, num_sms: int = 148) -> int:
+    """Split-KV factor: enough CTAs for ~2 waves, at least 4 tiles per split."""
+    ctas = max(1, batch * hkv)
+    want = max(1, (2 * num_sms + ctas - 1) // ctas)
+    tiles = max(1, (max_len + 63) // 64)
+    return int(max(1, min(want, (tiles + 3) // 4, 64)))
+
+
+def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                seq_lens: torch.Tensor, hq: int, hkv: int, scale: float, splits: int = 1,
+                out: torch.Tensor | None = None, bt_rows: torch.Tensor | None = None) -> torch.Tensor:
+    """Single-token attention per sequence. q: [B, >=hq*D] (row stride
+    free), seq_lens: int32 [B] (keys including the current token)."""
+    B = seq_lens.shape[0]
+    D = k_cache.shape[1] // hkv
+    if not q.is_cuda:
+        lens = [int(x) for x in seq_lens.tolist()]
+        bt = block_table if bt_rows is None else block_table[bt_rows.long()]
+        outs = _ref_attention(q[:, : hq * D], k_cache, v_cache, bt, [[n - 1] for n in lens], lens, hq, hkv, scale)
+        y = torch.cat(outs, 0).to(q.dtype)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(B, hq * D, dtype=q.dtype, device=q.device)
+    o_ptr = lse_ptr = None
+    if splits > 1:
+        o, lse = scratch(q.device).ensure_decode(B * hq * splits * D, B * hq * splits)
+        o_ptr, lse_ptr = o.data_ptr(), lse.data_ptr()
+    rc = _native.kernels().ib_attn_decode(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                                          block_table.data_ptr(), _ptr(bt_rows), seq_lens.data_ptr(),
+                                          block_table.stride(0), B, hq, hkv, splits, scale, o_ptr, lse_ptr,
+                                          out.data_ptr(), out.stride(0), _stream())
+    _native.check(rc, "ib_attn_decode")
+    return out
+
+
+def prefill_tiles(q_lens: list[int]) -> list[tuple[int, int]]:
+    """(seq, q_block) work items of 128 query rows, longest-work first."""
+    items = []
+    for s, n in enumerate(q_lens):
+        for b in range((n + 127) // 128):
+            items.append((s, b))
+    # later blocks of long sequences see more keys; schedule them first
+    items.sort(key=lambda it: -(it[1]))
+    return items
+
+
+def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                 q_start: torch.Tensor, q_len: torch.Tensor, ctx_len: torch.Tensor, tiles: torch.Tensor, hq: int,
+                 hkv: int, scale: float, out: torch.Tensor | None = None,
+                 host_meta: tuple[list[int], list[int]] | None = None,
+                 bt_rows: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention for chunks of new tokens whose K/V already sit in the
+    paged cache. q: [T, >=hq*D]; q_start/q_len/ctx_len: int32 [num_seqs];
+    tiles: int32 [num_tiles, 2] from :func:`prefill_tiles`."""
+    T = q.shape[0]
+    D = k_cache.shape[1] // hkv
+    if not q.is_cuda:
+        if host_meta is None:
+            host_meta = ([int(x) for x in q_len.tolist()], [int(x) for x in ctx_len.tolist()])
+        qls, ctxs = host_meta
+        q_pos = [list(range(c - n, c)) for n, c in zip(qls, ctxs)]
+        bt = block_table if bt_rows is None else block_table[bt_rows.long()]
+        outs = _ref_attention(q[:, : hq * D], k_cache, v_cache, bt, q_pos, ctxs, hq, hkv, scale)
+        y = torch.cat(outs, 0).to(q.dtype)
+        if out is not None:
+            out[: y.shape[0]].copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(T, hq * D, dtype=q.dtype, device=q.device)
+    sc = scratch(q.device)
+    rc = _native.kernels().ib_attn_prefill(q.data_ptr(), T, q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                                           k_cache.shape[0], tiles.data_ptr(), tiles.shape[0], q_start.data_ptr(),
+                                           q_len.data_ptr(), ctx_len.data_ptr(), block_table.data_ptr(),
+                                           _ptr(bt_rows), block_table.stride(0), hq, hkv, scale, out.data_ptr(),
+                                           out.stride(0),
+                                           sc.status.data_ptr(), _stream())
+    _native.check(rc, "ib_attn_prefill")
+    return out
+
+
+def scatter_i32(dst: torch.Tensor, idx: torch.Tensor, val: torch.Tensor) -> None:
+    """dst.view(-1)[idx] = val (int32)."""
+    n = idx.shape[0]
+    if n == 0:
+        return
+    if not dst.is_cuda:
+        dst.view(-1)[idx.long()] = val
+        return
+    rc = _native.kernels().ib_scatter_i32(dst.data_ptr(), idx.data_ptr(), val.data_ptr(), n, _stream())
+    _native.check(rc, "ib_scatter_i32")

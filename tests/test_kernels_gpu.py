@@ -1,0 +1,173 @@
+"""Numerics of every sm_100a kernel against the fp32 PyTorch oracle of the
+same op (the CPU path of :mod:`infera_b200.ops.kernels`)."""
+
+import math
+
+import pytest
+import torch
+
+from infera_b200.ops import kernels as K
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / (b.norm() + 1e-6))
+
+
+def _check_status():
+    st = K.scratch(torch.device(DEV, 0)).read_status()
+    assert st == 0, f"kernel status {st}"
+
+
+@pytest.mark.parametrize("M,N,K_", [
+    (1, 4096, 4096), (7, 6144, 4096), (16, 1024, 512), (64, 4096, 14336), (128, 28672, 4096),
+    (129, 4096, 4096), (256, 6144, 4096), (1000, 4096, 4096), (2048, 1024, 4096), (300, 520, 192),
+])
+def test_gemm_bf16(M, N, K_):
+    torch.manual_seed(0)
+    x = (torch.randn(M, K_, device=DEV) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K_, device=DEV) / math.sqrt(K_)).to(torch.bfloat16)
+    y = K.linear(x, w)
+    torch.cuda.synchronize()
+    _check_status()
+    ref = K.linear(x.cpu(), w.cpu())
+    assert _rel_err(y.cpu(), ref) < 1e-2
+
+
+@pytest.mark.parametrize("force_split", [1, 3])
+@pytest.mark.parametrize("M", [5, 200])
+def test_gemm_swiglu(M, force_split):
+    torch.manual_seed(1)
+    N, K_ = 2048, 1024
+    x = (torch.randn(M, K_, device=DEV)).to(torch.bfloat16)
+    w = (torch.randn(N, K_, device=DEV) / math.sqrt(K_)).to(torch.bfloat16)
+    y = K.linear(x, w, swiglu=True, force_split=force_split)
+    torch.cuda.synchronize()
+    _check_status()
+    ref = K.linear(x.cpu(), w.cpu(), swiglu=True)
+    assert y.shape == (M, N // 2)
+    assert _rel_err(y.cpu(), ref) < 1e-2
+    # workspace is left zeroed for the next split-K call
+    assert float(K.scratch().gemm_ws.abs().sum()) == 0.0
+
+
+def test_gemm_repeated_split_consistent():
+    torch.manual_seed(2)
+    x = torch.randn(8, 4096, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(4096, 4096, device=DEV) / 64).to(torch.bfloat16)
+    a = K.linear(x, w)
+    b = K.linear(x, w)
+    torch.cuda.synchronize()
+    assert _rel_err(a, b) < 1e-3
+
+
+@pytest.mark.parametrize("H", [4096, 8192, 5120])
+def test_rmsnorm_and_add(H):
+    torch.manual_seed(3)
+    T = 37
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    d = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    w = torch.randn(H, device=DEV).to(torch.bfloat16)
+    y = K.rmsnorm(x, w, 1e-5)
+    ref = K.rmsnorm(x.cpu(), w.cpu(), 1e-5)
+    assert _rel_err(y.cpu(), ref) < 1e-2
+    r_gpu = x.clone()
+    r_cpu = x.cpu().clone()
+    y2 = K.add_rmsnorm(d, r_gpu, w, 1e-5)
+    ref2 = K.add_rmsnorm(d.cpu(), r_cpu, w.cpu(), 1e-5)
+    torch.cuda.synchronize()
+    assert _rel_err(r_gpu.cpu(), r_cpu) < 1e-2
+    assert _rel_err(y2.cpu(), ref2) < 1e-2
+
+
+def test_rope_kvwrite():
+    torch.manual_seed(4)
+    T, hq, hkv, D = 19, 32, 8, 128
+    cs = K.rope_cos_sin(4096, D, 500000.0, {"factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                                              "original_max_position_embeddings": 8192})
+    qkv = torch.randn(T, (hq + 2 * hkv) * D).to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (T,), dtype=torch.int32)
+    slots = torch.randperm(64, dtype=torch.int32)[:T]
+    slots[3] = -1
+    kc = torch.zeros(64, hkv * D, dtype=torch.bfloat16)
+    vc = torch.zeros(64, hkv * D, dtype=torch.bfloat16)
+    qkv_g, kc_g, vc_g = qkv.cuda(), kc.cuda(), vc.cuda()
+    K.rope_kvwrite(qkv_g, pos.cuda(), slots.cuda(), cs.cuda(), hq, hkv, D, kc_g, vc_g)
+    K.rope_kvwrite(qkv, pos, slots, cs, hq, hkv, D, kc, vc)
+    torch.cuda.synchronize()
+    assert _rel_err(qkv_g.cpu(), qkv) < 1e-2
+    assert _rel_err(kc_g.cpu(), kc) < 1e-2
+    assert torch.equal(vc_g.cpu(), vc)
+
+
+def test_embed_and_sample():
+    torch.manual_seed(5)
+    table = torch.randn(1000, 256).to(torch.bfloat16)
+    ids = torch.randint(0, 1000, (9,), dtype=torch.int32)
+    e = K.embed(ids.cuda(), table.cuda())
+    assert torch.equal(e.cpu(), table[ids.long()])
+    logits = torch.randn(6, 128256).to(torch.bfloat16)
+    g = K.sample(logits.cuda())
+    assert torch.equal(g.cpu(), torch.argmax(logits.float(), -1).to(torch.int32))
+    temp = torch.tensor([0.0, 1.0, 0.7, 1.0, 0.0, 2.0])
+    seeds = torch.tensor([1, 2, 3, 4, 5, 6], dtype=torch.int64)
+    small = logits[:, :512].contiguous()
+    s_gpu = K.sample(small.cuda(), temp.cuda(), seeds.cuda())
+    s_cpu = K.sample(small, temp, seeds)
+    torch.cuda.synchronize()
+    assert torch.equal(s_gpu.cpu(), s_cpu)
+
+
+def _paged_setup(lens, hkv=8, D=128, page=16, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    n_pages = sum((n + page - 1) // page for n in lens) + 3
+    perm = torch.randperm(n_pages, generator=g)
+    max_pages = max((n + page - 1) // page for n in lens)
+    bt = torch.zeros(len(lens), max_pages, dtype=torch.int32)
+    k = 0
+    for i, n in enumerate(lens):
+        for j in range((n + page - 1) // page):
+            bt[i, j] = perm[k]
+            k += 1
+    kc = (torch.randn(n_pages * page, hkv * D, generator=g)).to(torch.bfloat16)
+    vc = (torch.randn(n_pages * page, hkv * D, generator=g)).to(torch.bfloat16)
+    return kc, vc, bt
+
+
+@pytest.mark.parametrize("lens,splits", [([1, 17, 64, 300], 1), ([1, 17, 64, 300], 4), ([5000], 16),
+                                         ([33] * 40, 2)])
+def test_attn_decode(lens, splits):
+    hq, hkv, D = 32, 8, 128
+    kc, vc, bt = _paged_setup(lens, hkv, D)
+    q = torch.randn(len(lens), (hq + 2 * hkv) * D).to(torch.bfloat16)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    scale = 1 / math.sqrt(D)
+    ref = K.attn_decode(q, kc, vc, bt, sl, hq, hkv, scale)
+    out = K.attn_decode(q.cuda(), kc.cuda(), vc.cuda(), bt.cuda(), sl.cuda(), hq, hkv, scale, splits=splits)
+    torch.cuda.synchronize()
+    assert _rel_err(out.cpu(), ref) < 2e-2
+
+
+@pytest.mark.parametrize("q_lens,ctx_lens", [
+    ([128], [128]), ([1, 77, 200], [1, 77, 500]), ([300, 5], [1300, 900]), ([1024], [4096 + 1024]),
+])
+def test_attn_prefill(q_lens, ctx_lens):
+    hq, hkv, D = 32, 8, 128
+    kc, vc, bt = _paged_setup(ctx_lens, hkv, D, seed=7)
+    T = sum(q_lens)
+    q = torch.randn(T, (hq + 2 * hkv) * D).to(torch.bfloat16)
+    q_start = torch.tensor([sum(q_lens[:i]) for i in range(len(q_lens))], dtype=torch.int32)
+    ql = torch.tensor(q_lens, dtype=torch.int32)
+    cl = torch.tensor(ctx_lens, dtype=torch.int32)
+    tiles = torch.tensor(K.prefill_tiles(q_lens), dtype=torch.int32).view(-1, 2)
+    scale = 1 / math.sqrt(D)
+    ref = K.attn_prefill(q, kc, vc, bt, q_start, ql, cl, tiles, hq, hkv, scale)
+    out = K.attn_prefill(q.cuda(), kc.cuda(), vc.cuda(), bt.cuda(), q_start.cuda(), ql.cuda(), cl.cuda(),
+                         tiles.cuda(), hq, hkv, scale)
+    torch.cuda.synchronize()
+    _check_status()
+    assert _rel_err(out.cpu(), ref) < 2e-2
