@@ -1,0 +1,164 @@
+"""Open-loop replay of an agentic trace through an in-process engine.
+
+Arrivals are Poisson at ``rate`` requests/s; each arrival becomes the next
+turn of the next idle session (a session never has two turns in flight).
+Time is measured on the device: a CUDA event is recorded at the end of
+every engine step's kernels, and token timestamps are those events'
+offsets from the window's start event. Arrival times are host offsets from
+the same origin (taken right after a synchronize, so both clocks start
+together).
+
+The replay advances in slices of ``slice_s`` seconds; one slice is one
+benchmark step.
+"""
+
+from __future__ import annotations
+
+import random
+import time
+from collections import deque
+
+import torch
+
+from infera_b200.bench.slo import ReqRecord
+from infera_b200.bench.trace import Session, TraceSpec, build_sessions
+from infera_b200.engine.request import SamplingParams
+
+
+class EngineReplay:
+    def __init__(self, engine, spec: TraceSpec, session_ids: list[int], rate: float, seed: int = 0,
+                 device_timing: bool = True):
+        self.eng = engine
+        self.spec = spec
+        self.rate = rate
+        self.rng = random.Random(seed + 17)
+        self.seed = seed
+        self.sessions: list[Session] = build_sessions(spec, seed, session_ids)
+        self.next_sid = max(session_ids) + 1 + 1_000_000 * (seed + 1)
+        self.idle: deque[Session] = deque(self.sessions)
+        self.pending_arrivals: deque[float] = deque()
+        self.records: dict[str, ReqRecord] = {}
+        self.inflight: dict[str, tuple[Session, list[int]]] = {}
+        self.device_timing = device_timing and torch.cuda.is_available() and engine.device.type == "cuda"
+        self.t0_host = None
+        self.ev0 = None
+        self.step_events: list = []         # (event, host_time)
+        self.token_steps: dict[str, list[int]] = {}
+        self.collected: dict[str, list[int]] = {}
+        self.next_arrival = None
+        self.req_counter = 0
+
+    # ------------------------------------------------------------------ clocks
+    def start_clock(self) -> None:
+        if self.device_timing:
+            torch.cuda.synchronize()
+            self.ev0 = torch.cuda.Event(enable_timing=True)
+            self.ev0.record()
+        self.t0_host = time.monotonic()
+        self.next_arrival = self._draw_gap()
+
+    def now(self) -> float:
+        return time.monotonic() - self.t0_host
+
+    def _draw_gap(self) -> float:
+        return self.rng.expovariate(self.rate)
+
+    # ------------------------------------------------------------------ sessions
+    def _recycle(self, s: Session) -> Session:
+        fresh = build_sessions(self.spec, self.seed, [self.next_sid])[0]
+        fresh.group = s.group
+        fresh.prefix = s.prefix
+        self.next_sid += 1
+        return fresh
+
+    def _issue(self, s: Session, arrival: float) -> None:
+        prompt = s.next_prompt()
+        rid = f"s{s.sid}-t{s.turn}-{self.req_counter}"
+        self.req_counter += 1
+        out_len = s.out_lens[s.turn]
+        self.eng.add_request(rid, prompt, SamplingParams(max_tokens=out_len, ignore_eos=True))
+        self.records[rid] = ReqRecord(rid, arrival, prompt_len=len(prompt))
+        self.inflight[rid] = (s, prompt)
+        self.token_steps[rid] = []
+        self.collected[rid] = []
+        s.busy = True
+
+    def _admit_arrivals(self) -> None:
+        now = self.now()
+        while self.next_arrival is not None and self.next_arrival <= now:
+            self.pending_arrivals.append(self.next_arrival)
+            self.next_arrival += self._draw_gap()
+        while self.pending_arrivals and self.idle:
+            arr = self.pending_arrivals.popleft()
+            s = self.idle.popleft()
+            if s.done(self.spec.context_cap):
+                s = self._recycle(s)
+            self._issue(s, max(arr, 0.0))
+
+    # ------------------------------------------------------------------ main loop
+    def prime_prefixes(self) -> None:
+        """Compute every group's system prefix once (a long-running server
+        has them cached); not part of any measured window."""
+        seen = set()
+        prompts = []
+        for s in self.sessions:
+            key = tuple(s.prefix[:8])
+            if s.prefix and key not in seen:
+                seen.add(key)
+                prompts.append(s.prefix)
+        if prompts:
+            self.eng.generate(prompts, SamplingParams(max_tokens=1, ignore_eos=True))
+
+    def run_until(self, t_end: float) -> None:
+        while True:
+            now = self.now()
+            if now >= t_end:
+                return
+            self._admit_arrivals()
+            if self.eng.has_unfinished():
+                outs = self.eng.step()
+                step_idx = len(self.step_events)
+                if self.device_timing:
+                    ev = torch.cuda.Event(enable_timing=True)
+                    ev.record()
+                    self.step_events.append((ev, self.now()))
+                else:
+                    self.step_events.append((None, self.now()))
+                for o in outs:
+                    rid = o.request_id
+                    rec = self.records.get(rid)
+                    if rec is None:
+                        continue
+                    self.token_steps[rid].extend([step_idx] * len(o.new_token_ids))
+                    self.collected[rid].extend(o.new_token_ids)
+                    if o.finished:
+                        s, prompt = self.inflight.pop(rid)
+                        rec.cached_len = o.num_cached_tokens
+                        rec.out_len = o.num_output_tokens
+                        rec.finish = step_idx  # resolved to a time later
+                        s.history = prompt + self.collected.pop(rid)
+                        s.turn += 1
+                        s.busy = False
+                        self.idle.append(s)
+            else:
+                wait = (self.next_arrival or now) - now
+                if wait > 0:
+                    time.sleep(min(wait, t_end - now, 0.002))
+
+    # ------------------------------------------------------------------ results
+    def resolve(self) -> list[ReqRecord]:
+        """Convert step indices into timestamps (device when available)."""
+        if self.device_timing:
+            torch.cuda.synchronize()
+            times = [self.ev0.elapsed_time(ev) / 1000.0 for ev, _ in self.step_events]
+        else:
+            times = [t for _, t in self.step_events]
+        out = []
+        for rid, rec in self.records.items():
+            steps = self.token_steps.get(rid, [])
+            rec.token_times = [times[i] for i in steps]
+            rec.first_token = rec.token_times[0] if rec.token_times else None
+            if isinstance(rec.finish, int):
+                rec.finish = times[rec.finish]
+            out.append(rec)
+        return out

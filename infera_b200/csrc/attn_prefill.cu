@@ -225,8 +225,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status,
-                     kStatusTimeoutTmemFull)) {
+      if (!mbar_wait_warp(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status,
+                          kStatusTimeoutTmemFull)) {
         ok = false;
         break;
       }
@@ -246,18 +246,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       mx *= p.scale_log2;
       float m_new = fmaxf(m_run, mx);
+      // Per-row choice (FA4-style lazy rescale: keep a stale max unless the
+      // new one exceeds it by 2^8). The TMEM rescale below is warp-collective,
+      // so the warp rescales if ANY of its rows needs it; other rows use 1.0.
       bool rescale = (j == 0) || (m_new > m_run + 8.0f);
       float m_use = rescale ? m_new : m_run;
       float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
+      const bool warp_rescale = __any_sync(0xffffffffu, rescale && j > 0);
       // P of the previous tile must be consumed before P / O are touched
       if (j > 0) {
-        if (!mbar_wait(o_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status, kStatusTimeoutTmemFull)) {
+        if (!mbar_wait_warp(o_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status,
+                            kStatusTimeoutTmemFull)) {
           ok = false;
           break;
         }
         tc_fence_after();
       }
-      if (rescale && j > 0 && alpha != 1.0f) {
+      if (warp_rescale) {
 #pragma unroll 1
         for (int c0 = 0; c0 < D; c0 += 16) {
           uint32_t o[16];
@@ -298,8 +303,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(p_full);
     }
+    ok = __all_sync(0xffffffffu, ok);
     if (ok && n_kv > 0) {
-      if (mbar_wait(o_done, static_cast<uint32_t>((n_kv - 1) & 1), abort_flag, p.status, kStatusTimeoutTmemFull)) {
+      if (mbar_wait_warp(o_done, static_cast<uint32_t>((n_kv - 1) & 1), abort_flag, p.status,
+                         kStatusTimeoutTmemFull)) {
         tc_fence_after();
         const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
         const bool write = r < valid_rows;

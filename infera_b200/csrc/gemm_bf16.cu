@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tile_coords(p, t, pt, qt, sp);
       const uint32_t acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutTmemFull)) break;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutTmemFull)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * MAX_BN;
       int c0 = 0;

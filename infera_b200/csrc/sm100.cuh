@@ -91,6 +91,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait whose outcome is identical for every lane of the warp. Warps
+// that go on to issue warp-collective (.sync.aligned) tcgen05 instructions
+// must use this form: a lane that timed out while its neighbours did not
+// would otherwise leave the warp divergent at the next collective.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               int* status, int code, uint64_t limit_ns = kWaitLimitNs) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, status, code, limit_ns);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");

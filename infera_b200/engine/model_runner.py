@@ -61,14 +61,15 @@ class ModelRunner:
         self.h_out = torch.empty(max(max_num_seqs, 1), dtype=torch.int32, pin_memory=pin)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
+        self.last_logits = None
         if self.on_gpu:
             sc = K.scratch(self.dev)
             sc.ensure_gemm(8 * 1024 * 1024)
             sc.ensure_decode(max_num_seqs * cfg.num_heads * 4 * 128 + 64 * cfg.num_heads * 64 * 128,
                              max_num_seqs * cfg.num_heads * 4 + 64 * cfg.num_heads * 64)
-            sc.frozen = True
         self.graph_sizes = [g for g in (graph_sizes or DEFAULT_GRAPH_SIZES) if g <= max_num_seqs]
         self.graphs: dict[int, tuple] = {}
+        self.graph_launches: dict[int, int] = {}
         self.use_graphs = use_graphs and self.on_gpu
         if self.use_graphs:
             self._capture_all()
@@ -200,6 +201,7 @@ class ModelRunner:
             fb.num_decode = B
             fb.d_splits = K.decode_splits(B, self.cfg.num_kv_heads, max(d_lens)) if self.on_gpu else 1
         logits = self.model.forward(fb, self.k_cache, self.v_cache, self.bufs)
+        self.last_logits = logits
         temp = v("temp").view(torch.float32)
         so, sn = views["seed"]
         seed_t = d[so:so + sn].view(torch.int64)
@@ -257,8 +259,10 @@ class ModelRunner:
                 run()  # warm-up outside capture (tensor-map cache, lazy init)
                 torch.cuda.synchronize()
                 g = torch.cuda.CUDAGraph()
+                n0 = K.LAUNCHES[0]
                 with torch.cuda.graph(g, pool=pool, stream=stream):
                     run()
+                self.graph_launches[B] = K.LAUNCHES[0] - n0
                 self.graphs[B] = (g, lay)
         torch.cuda.current_stream().wait_stream(stream)
         torch.cuda.synchronize()
@@ -297,5 +301,6 @@ class ModelRunner:
         if nu:
             K.scatter_i32(self.block_table, self.d_in[end:end + nu], self.d_in[end + nu:end + 2 * nu])
         g.replay()
+        K.LAUNCHES[0] += self.graph_launches[Bg]
         del pad
         return self._d2h(self.g_out, B)

@@ -1,0 +1,147 @@
+"""``python -m infera_b200.engine.worker``: one engine instance as a fleet
+worker.
+
+Lifecycle (``infera/engine/vllm/__main__.py:142-405``, for this framework's
+own engine):
+
+1. build the engine on the GPU, the KV-event publisher (ZMQ PUB) and the
+   worker HTTP app;
+2. serve HTTP, then register (etcd lease + heartbeat, or the in-process
+   registry) with a record carrying the KV metadata (block size, tokenizer
+   digest and canary, events endpoint);
+3. on SIGTERM / SIGINT: stop the heartbeat, DEREGISTER FIRST (the router
+   stops sending), drain in-flight requests (exact count, bounded by
+   ``--drain-timeout``; optionally hand the stragglers back for migration),
+   then stop the engine and the server.
+"""
+
+from __future__ import annotations
+
+import argparse
+import asyncio
+import logging
+import signal
+import socket
+
+logger = logging.getLogger(__name__)
+
+
+def build_payload(args, tokenizer) -> dict:
+    from infera_b200.common.worker_pool import (DisaggMode, EngineType, KvRegistrationMetadata, WorkerInfo)
+    from infera_b200.utils.tokenizer import canary
+
+    host = args.advertise_host or args.host
+    if host in ("0.0.0.0", ""):
+        host = socket.gethostname()
+    wid = f"{host}:{args.port}"
+    meta = {}
+    if args.disagg_mode != "mixed":
+        meta = {"protocol": "b200-nvlink-push", "params": {"kv_endpoint": args.kv_push_endpoint or ""}}
+    kv = KvRegistrationMetadata(engine_block_size=args.page_size, index_block_size=args.page_size,
+                                tokenizer=tokenizer.name, tokenizer_digest=tokenizer.digest(),
+                                tokenizer_canary=canary(tokenizer), events_endpoint=args.kv_events_endpoint,
+                                snapshot_endpoint=f"http://{host}:{args.port}", tiers=["device"])
+    w = WorkerInfo(worker_id=wid, url=f"http://{host}:{args.port}", model_name=args.served_model_name or args.model,
+                   engine=EngineType.INFERA_B200, disagg_mode=DisaggMode(args.disagg_mode), disagg_meta=meta,
+                   kv_events_endpoint=args.kv_events_endpoint, kv_block_size=args.page_size, kv=kv)
+    return w.to_payload()
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(prog="python -m infera_b200.engine.worker")
+    p.add_argument("--model", default="llama-3.1-8b")
+    p.add_argument("--served-model-name", default=None)
+    p.add_argument("--host", default="127.0.0.1")
+    p.add_argument("--advertise-host", default=None)
+    p.add_argument("--port", type=int, default=9000)
+    p.add_argument("--device", default="cuda:0")
+    p.add_argument("--page-size", type=int, default=16)
+    p.add_argument("--max-num-seqs", type=int, default=128)
+    p.add_argument("--max-batched-tokens", type=int, default=2048)
+    p.add_argument("--gpu-memory-utilization", type=float, default=0.90)
+    p.add_argument("--num-pages", type=int, default=None)
+    p.add_argument("--no-cuda-graphs", action="store_true")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--etcd-endpoint", default=None)
+    p.add_argument("--kv-events-endpoint", default=None, help="ZMQ PUB bind address, e.g. tcp://127.0.0.1:5557")
+    p.add_argument("--disagg-mode", choices=("mixed", "prefill", "decode"), default="mixed")
+    p.add_argument("--kv-push-endpoint", default=None)
+    p.add_argument("--drain-timeout", type=float, default=30.0)
+    p.add_argument("--handback-after", type=float, default=None)
+    p.add_argument("--tokenizer", default=None)
+    p.add_argument("--log-level", default="info")
+    return p.parse_args(argv)
+
+
+async def run_worker(args) -> None:
+    import uvicorn
+
+    from infera_b200.engine.async_engine import AsyncEngine
+    from infera_b200.engine.kv_events import KvEventPublisher
+    from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
+    from infera_b200.engine.server import build_worker_app
+    from infera_b200.utils.tokenizer import load_tokenizer
+
+    pub = KvEventPublisher(args.kv_events_endpoint) if args.kv_events_endpoint else None
+    ecfg = EngineConfig(model=args.model, page_size=args.page_size, max_num_seqs=args.max_num_seqs,
+                        max_batched_tokens=args.max_batched_tokens,
+                        gpu_memory_utilization=args.gpu_memory_utilization, num_pages=args.num_pages,
+                        use_cuda_graphs=not args.no_cuda_graphs, seed=args.seed)
+    eng = LLMEngine(ecfg, device=args.device, event_sink=pub)
+    tok = load_tokenizer(args.tokenizer, vocab_size=eng.model_cfg.vocab)
+    aeng = AsyncEngine(eng)
+    aeng.start()
+    app = build_worker_app(aeng, tok, args.served_model_name or args.model)
+    server = uvicorn.Server(uvicorn.Config(app, host=args.host, port=args.port, log_level="warning",
+                                           access_log=False))
+    serve_task = asyncio.create_task(server.serve())
+    while not server.started:
+        await asyncio.sleep(0.05)
+    payload = build_payload(args, tok)
+    reg = None
+    hb = None
+    if args.etcd_endpoint:
+        from infera_b200.common.registration import EtcdRegistration
+
+        reg = EtcdRegistration(args.etcd_endpoint, payload)
+        await reg.register()
+        hb = asyncio.create_task(reg.heartbeat_loop())
+    logger.info("worker %s serving %s", payload["worker_id"], payload["model_name"])
+    stop = asyncio.Event()
+    loop = asyncio.get_running_loop()
+    for sig in (signal.SIGTERM, signal.SIGINT):
+        loop.add_signal_handler(sig, stop.set)
+    flusher = asyncio.create_task(_flush_loop(pub)) if pub else None
+    await stop.wait()
+    # shutdown: heartbeat off -> deregister -> drain -> stop
+    if hb is not None:
+        hb.cancel()
+    if reg is not None:
+        await reg.deregister()
+    clean = await aeng.drain(args.drain_timeout, args.handback_after)
+    logger.info("drain %s (inflight=%d)", "clean" if clean else "timed out", aeng.inflight)
+    aeng.stop()
+    if flusher is not None:
+        flusher.cancel()
+    if pub is not None:
+        pub.close()
+    server.should_exit = True
+    await serve_task
+    if reg is not None:
+        await reg.close()
+
+
+async def _flush_loop(pub) -> None:
+    while True:
+        await asyncio.sleep(0.01)
+        pub.flush()
+
+
+def main(argv=None) -> None:
+    args = parse_args(argv)
+    logging.basicConfig(level=getattr(logging, args.log_level.upper(), logging.INFO))
+    asyncio.run(run_worker(args))
+
+
+if __name__ == "__main__":
+    main()

@@ -29,19 +29,21 @@ class DeviceScratch:
     gemm_ws: torch.Tensor = field(default_factory=lambda: torch.empty(0))
     dec_o: torch.Tensor = field(default_factory=lambda: torch.empty(0))
     dec_lse: torch.Tensor = field(default_factory=lambda: torch.empty(0))
-    frozen: bool = False
 
+    # Growth is refused while a CUDA graph is being captured (a captured
+    # kernel must keep pointing at live memory); engines size the scratch
+    # before they capture.
     def ensure_gemm(self, numel: int) -> torch.Tensor:
         if self.gemm_ws.numel() < numel:
-            if self.frozen:
-                raise RuntimeError(f"GEMM workspace too small ({self.gemm_ws.numel()} < {numel}) after freeze")
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError(f"GEMM workspace too small ({self.gemm_ws.numel()} < {numel}) during capture")
             self.gemm_ws = torch.zeros(numel, dtype=torch.float32, device=self.device)
         return self.gemm_ws
 
     def ensure_decode(self, o_numel: int, lse_numel: int) -> tuple[torch.Tensor, torch.Tensor]:
         if self.dec_o.numel() < o_numel or self.dec_lse.numel() < lse_numel:
-            if self.frozen:
-                raise RuntimeError("decode scratch too small after freeze")
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("decode scratch too small during capture")
             self.dec_o = torch.empty(max(o_numel, self.dec_o.numel()), dtype=torch.float32, device=self.device)
             self.dec_lse = torch.empty(max(lse_numel, self.dec_lse.numel()), dtype=torch.float32,
                                        device=self.device)
@@ -69,6 +71,39 @@ def scratch(device: torch.device | int | None = None) -> DeviceScratch:
         s = DeviceScratch(device=dev, status=torch.zeros(1, dtype=torch.int32, device=dev))
         _scratch[idx] = s
     return s
+
+
+# Number of kernel launches issued through this module (graph replays add
+# the launches captured in the graph); used to report launch counts.
+LAUNCHES = [0]
+_plan_cache: dict[tuple[int, int, int, int], int] = {}
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
+
+def _gemm_splits(M: int, N: int, K: int, force_split: int = 0) -> int:
+    key = (M, N, K, force_split)
+    v = _plan_cache.get(key)
+    if v is None:
+        v = gemm_plan(M, N, K, _num_sms(), force_split)["splits"]
+        _plan_cache[key] = v
+    return v
+
+
+def _gemm_launches(M: int, N: int, K: int, force_split: int = 0) -> int:
+    return 1 + (1 if _gemm_splits(M, N, K, force_split) > 1 else 0)
+
+
+_NUM_SMS: list[int] = []
+
+
+def _num_sms() -> int:
+    if not _NUM_SMS:
+        _NUM_SMS.append(torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+                        if torch.cuda.is_available() else 148)
+    return _NUM_SMS[0]
 
 
 def _stream() -> int:
@@ -114,11 +149,13 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, sw
     if out is None:
         out = torch.empty(M, n_out, dtype=torch.bfloat16, device=x.device)
     sc = scratch(x.device)
-    ws = sc.ensure_gemm(M * N)
+    splits = _gemm_splits(M, N, K, force_split)
+    ws = sc.ensure_gemm(M * N if splits > 1 else 1)
     rc = _native.kernels().ib_gemm_bf16(x.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, K, x.stride(0),
                                         w.stride(0), out.stride(0), 1 if swiglu else 0, ws.data_ptr(),
                                         force_split, sc.status.data_ptr(), _stream())
     _native.check(rc, "ib_gemm_bf16")
+    _count(_gemm_launches(M, N, K, force_split))
     return out
 
 
@@ -140,6 +177,7 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | No
     rc = _native.kernels().ib_rmsnorm(x.data_ptr(), w.data_ptr(), out.data_ptr(), T, H, x.stride(0), out.stride(0),
                                       eps, _stream())
     _native.check(rc, "ib_rmsnorm")
+    _count()
     return out
 
 
@@ -155,6 +193,7 @@ def add_rmsnorm(delta: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, ep
     rc = _native.kernels().ib_add_rmsnorm(delta.data_ptr(), residual.data_ptr(), w.data_ptr(), out.data_ptr(), T, H,
                                           delta.stride(0), residual.stride(0), out.stride(0), eps, _stream())
     _native.check(rc, "ib_add_rmsnorm")
+    _count()
     return out
 
 
@@ -209,6 +248,7 @@ def rope_kvwrite(qkv: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor, cos_
                                            cos_sin.data_ptr(), hq, hkv, head_dim, k_cache.data_ptr(),
                                            v_cache.data_ptr(), k_cache.stride(0), _stream())
     _native.check(rc, "ib_rope_kvwrite")
+    _count()
 
 
 def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -224,6 +264,7 @@ def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = Non
         out = torch.empty(T, H, dtype=table.dtype, device=table.device)
     rc = _native.kernels().ib_embed(ids.data_ptr(), table.data_ptr(), out.data_ptr(), T, H, _stream())
     _native.check(rc, "ib_embed")
+    _count()
     return out
 
 
@@ -240,6 +281,7 @@ def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None =
     rc = _native.kernels().ib_gather_rows(src.data_ptr(), idx.data_ptr(), out.data_ptr(), n, src.stride(0),
                                           _stream())
     _native.check(rc, "ib_gather_rows")
+    _count()
     return out
 
 
@@ -288,6 +330,7 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor | None = None, seeds:
     rc = _native.kernels().ib_sample(logits.data_ptr(), B, logits.stride(0), V, _ptr(temperature), _ptr(seeds),
                                      out.data_ptr(), _stream())
     _native.check(rc, "ib_sample")
+    _count()
     return out
 
 
@@ -358,6 +401,7 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, b
                                           block_table.stride(0), B, hq, hkv, splits, scale, o_ptr, lse_ptr,
                                           out.data_ptr(), out.stride(0), _stream())
     _native.check(rc, "ib_attn_decode")
+    _count(2 if splits > 1 else 1)
     return out
 
 
@@ -404,6 +448,7 @@ def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
                                            out.stride(0),
                                            sc.status.data_ptr(), _stream())
     _native.check(rc, "ib_attn_prefill")
+    _count()
     return out
 
 
@@ -417,3 +462,4 @@ def scatter_i32(dst: torch.Tensor, idx: torch.Tensor, val: torch.Tensor) -> None
         return
     rc = _native.kernels().ib_scatter_i32(dst.data_ptr(), idx.data_ptr(), val.data_ptr(), n, _stream())
     _native.check(rc, "ib_scatter_i32")
+    _count()

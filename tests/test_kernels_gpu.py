@@ -171,3 +171,27 @@ def test_attn_prefill(q_lens, ctx_lens):
     torch.cuda.synchronize()
     _check_status()
     assert _rel_err(out.cpu(), ref) < 2e-2
+
+
+def test_attn_prefill_divergent_rescale():
+    """Rows whose running max grows by different amounts across KV tiles, so
+    the lazy O rescale is needed by some rows of a warp and not others."""
+    hq, hkv, D = 32, 8, 128
+    ctx = 1024
+    kc, vc, bt = _paged_setup([ctx], hkv, D, seed=11)
+    growth = torch.linspace(0.2, 4.0, kc.shape[0])[:, None]
+    kc = (kc.float() * growth).to(torch.bfloat16)
+    q = torch.randn(ctx, (hq + 2 * hkv) * D)
+    q[:, : hq * D] *= (torch.arange(ctx) % 7 + 1).float()[:, None] * 0.5
+    q = q.to(torch.bfloat16)
+    q_start = torch.tensor([0], dtype=torch.int32)
+    ql = torch.tensor([ctx], dtype=torch.int32)
+    cl = torch.tensor([ctx], dtype=torch.int32)
+    tiles = torch.tensor(K.prefill_tiles([ctx]), dtype=torch.int32).view(-1, 2)
+    scale = 1 / math.sqrt(D)
+    ref = K.attn_prefill(q, kc, vc, bt, q_start, ql, cl, tiles, hq, hkv, scale)
+    out = K.attn_prefill(q.cuda(), kc.cuda(), vc.cuda(), bt.cuda(), q_start.cuda(), ql.cuda(), cl.cuda(),
+                         tiles.cuda(), hq, hkv, scale)
+    torch.cuda.synchronize()
+    _check_status()
+    assert _rel_err(out.cpu(), ref) < 2e-2
