@@ -285,3 +285,106 @@ extern "C" int ib_attn_decode(const void* q, int ldq, const void* k_cache, const
   }
   return 0;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point (declared, with its contract, in
+// attn_decode_noalloc.h). Same kernels as ib_attn_decode; the split-KV
+// partials live in file-scope device arrays instead of caller memory.
+#include <mutex>
+
+#include "attn_decode_noalloc.h"
+
+namespace ib200 {
+namespace dec_noalloc {
+
+// Split-KV partial outputs and their log-sum-exp. In host code these names
+// are host-side stand-ins, not device addresses: never hand them to a
+// kernel; use the addresses looked up by device_scratch().
+static __device__ __align__(256) float g_o_part[IB_DECODE_NOALLOC_MAX_ROWS * dec::D];
+static __device__ __align__(256) float g_lse_part[IB_DECODE_NOALLOC_MAX_ROWS];
+
+struct DeviceScratch {
+  float* o = nullptr;
+  float* lse = nullptr;
+  bool ready = false;
+};
+constexpr int kMaxDevices = 64;
+static DeviceScratch g_scratch[kMaxDevices];
+static std::mutex g_mu;
+
+// Device addresses of the arrays for the current device, looked up once per
+// device (with that device current) and cached.
+static int device_scratch(DeviceScratch** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return IB_DECODE_NOALLOC_SETUP_FAILED;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceScratch& s = g_scratch[dev];
+  if (!s.ready) {
+    void* o = nullptr;
+    void* lse = nullptr;
+    if (cudaGetSymbolAddress(&o, g_o_part) != cudaSuccess) return IB_DECODE_NOALLOC_SETUP_FAILED;
+    if (cudaGetSymbolAddress(&lse, g_lse_part) != cudaSuccess) return IB_DECODE_NOALLOC_SETUP_FAILED;
+    s.o = static_cast<float*>(o);
+    s.lse = static_cast<float*>(lse);
+    s.ready = true;
+  }
+  *out = &s;
+  return 0;
+}
+
+}  // namespace dec_noalloc
+}  // namespace ib200
+
+extern "C" int ib_attn_decode_noalloc_max_rows(void) { return IB_DECODE_NOALLOC_MAX_ROWS; }
+
+extern "C" int ib_attn_decode_noalloc(const void* q, int ldq, const void* k_cache, const void* v_cache,
+                                      const int* block_table, const int* bt_rows, const int* seq_lens, int max_pages,
+                                      int B, int hq, int hkv, int splits, float scale, void* out, int ldo,
+                                      cudaStream_t stream) {
+  if (B <= 0) return 0;
+  if (hkv <= 0 || hq % hkv != 0 || splits < 1) return -1;
+  const int G = hq / hkv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return -1;
+  float* o_part = nullptr;
+  float* lse_part = nullptr;
+  if (splits > 1) {
+    if (static_cast<long long>(B) * hq * splits > IB_DECODE_NOALLOC_MAX_ROWS) return IB_DECODE_NOALLOC_TOO_BIG;
+    dec_noalloc::DeviceScratch* s = nullptr;
+    const int rc = dec_noalloc::device_scratch(&s);
+    if (rc != 0) return rc;
+    o_part = s->o;
+    lse_part = s->lse;
+  }
+  dec::Params p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.ldq = ldq;
+  p.k = static_cast<const __nv_bfloat16*>(k_cache);
+  p.v = static_cast<const __nv_bfloat16*>(v_cache);
+  p.block_table = block_table;
+  p.bt_rows = bt_rows;
+  p.seq_lens = seq_lens;
+  p.max_pages = max_pages;
+  p.hq = hq;
+  p.hkv = hkv;
+  p.splits = splits;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o_part = o_part;
+  p.lse_part = lse_part;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  switch (G) {
+    case 1: launch_decode<1>(p, B, stream); break;
+    case 2: launch_decode<2>(p, B, stream); break;
+    case 4: launch_decode<4>(p, B, stream); break;
+    default: launch_decode<8>(p, B, stream); break;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (splits > 1) {
+    dim3 grid(B, hq);
+    dec::combine_kernel<<<grid, dec::D, 0, stream>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  return 0;
+}
