@@ -126,24 +126,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int* bt = p.block_table + static_cast<size_t>(bt_row) * p.max_pages;
       const int n_pages = (ctx + PAGE - 1) / PAGE;
       long long issued = 0;
+      int nxt[8];
+      load_tile_pages(bt, 0, n_pages, nxt);
       for (int j = 0; j < n_kv; ++j) {
         const int st = j % KV_STAGES;
         const uint32_t ph = (j / KV_STAGES) & 1;
+        int cur[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
+        if (j + 1 < n_kv) load_tile_pages(bt, j + 1, n_pages, nxt);  // in flight while we wait
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
         uint8_t* base = sKV + st * 4 * BLK;
         mbar_expect_tx(&k_full[st], 2 * BLK);
+#pragma unroll
         for (int pg = 0; pg < BKV / PAGE; ++pg) {
-          int lp = j * (BKV / PAGE) + pg;
-          int page = lp < n_pages ? __ldg(bt + lp) : __ldg(bt);
-          int r = page * PAGE;
+          const int r = cur[pg] * PAGE;
           tma_load_2d(base + pg * PAGE * 128, &tmK, &k_full[st], kvh * D, r, pol);
           tma_load_2d(base + BLK + pg * PAGE * 128, &tmK, &k_full[st], kvh * D + 64, r, pol);
         }
         mbar_expect_tx(&v_full[st], 2 * BLK);
+#pragma unroll
         for (int pg = 0; pg < BKV / PAGE; ++pg) {
-          int lp = j * (BKV / PAGE) + pg;
-          int page = lp < n_pages ? __ldg(bt + lp) : __ldg(bt);
-          int r = page * PAGE;
+          const int r = cur[pg] * PAGE;
           tma_load_2d(base + 2 * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * D, r, pol);
           tma_load_2d(base + 3 * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * D + 64, r, pol);
         }

@@ -101,6 +101,17 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
   return __all_sync(0xffffffffu, ok);
 }
 
+// Page ids of one 128-token KV tile (8 pages of 16 tokens). The eight loads
+// are independent so their latencies overlap; pages past the sequence's last
+// page map to its first page (always valid, masked by the caller).
+__device__ __forceinline__ void load_tile_pages(const int* bt, int tile, int n_pages, int (&pg)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int lp = tile * 8 + i;
+    pg[i] = __ldg(bt + (lp < n_pages ? lp : 0));
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
@@ -208,9 +219,15 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr, uint32_t
 // Instruction descriptor for kind::f16 with bf16 inputs and fp32 accumulate.
 //  bits 4-5 D format (1 = f32), 7-9 A format (1 = bf16), 10-12 B format,
 //  15 A major (0 = K-major), 16 B major (1 = MN-major), 17-22 N>>3, 24-28 M>>4.
-__host__ __device__ constexpr uint32_t make_idesc_bf16(uint32_t m, uint32_t n, bool b_mn_major = false) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((n >> 3) << 17) |
-         ((m >> 4) << 24);
+__host__ __device__ constexpr uint32_t make_idesc_bf16(uint32_t m, uint32_t n, bool b_mn_major = false,
+                                                       bool a_mn_major = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// Named barrier among `count` threads (ids 1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // Instruction descriptor for kind::f8f6f4 with e4m3 inputs and fp32 accumulate

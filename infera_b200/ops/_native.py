@@ -52,6 +52,8 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_attn_prefill": [c_vp, c_int, c_int, c_vp, c_vp, c_ll, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int,
                             c_int, c_int, c_float, c_vp, c_int, c_vp, c_vp],
         "ib_scatter_i32": [c_vp, c_vp, c_vp, c_int, c_vp],
+        "ib_attn_decode_tc": [c_vp, c_int, c_vp, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
+                              c_float, c_vp, c_vp, c_vp, c_int, c_vp, c_vp],
     }
     for name, args in sig.items():
         fn = getattr(lib, name, None)

@@ -376,9 +376,13 @@ def decode_splits(batch: int, hkv: int, max_len: int, num_sms: int = 148) -> int
 
 def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
                 seq_lens: torch.Tensor, hq: int, hkv: int, scale: float, splits: int = 1,
-                out: torch.Tensor | None = None, bt_rows: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, bt_rows: torch.Tensor | None = None,
+                impl: str = "tc") -> torch.Tensor:
     """Single-token attention per sequence. q: [B, >=hq*D] (row stride
-    free), seq_lens: int32 [B] (keys including the current token)."""
+    free), seq_lens: int32 [B] (keys including the current token).
+
+    ``impl="tc"`` is the tcgen05/TMA kernel the engine uses; ``"simt"`` is
+    the FP32-pipe kernel behind the allocation-free C entry point."""
     B = seq_lens.shape[0]
     D = k_cache.shape[1] // hkv
     if not q.is_cuda:
@@ -393,14 +397,23 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, b
     if out is None:
         out = torch.empty(B, hq * D, dtype=q.dtype, device=q.device)
     o_ptr = lse_ptr = None
+    sc = scratch(q.device)
     if splits > 1:
-        o, lse = scratch(q.device).ensure_decode(B * hq * splits * D, B * hq * splits)
+        o, lse = sc.ensure_decode(B * hq * splits * D, B * hq * splits)
         o_ptr, lse_ptr = o.data_ptr(), lse.data_ptr()
-    rc = _native.kernels().ib_attn_decode(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
-                                          block_table.data_ptr(), _ptr(bt_rows), seq_lens.data_ptr(),
-                                          block_table.stride(0), B, hq, hkv, splits, scale, o_ptr, lse_ptr,
-                                          out.data_ptr(), out.stride(0), _stream())
-    _native.check(rc, "ib_attn_decode")
+    if impl == "tc":
+        rc = _native.kernels().ib_attn_decode_tc(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                                                 k_cache.shape[0], block_table.data_ptr(), _ptr(bt_rows),
+                                                 seq_lens.data_ptr(), block_table.stride(0), B, hq, hkv, splits,
+                                                 scale, o_ptr, lse_ptr, out.data_ptr(), out.stride(0),
+                                                 sc.status.data_ptr(), _stream())
+        _native.check(rc, "ib_attn_decode_tc")
+    else:
+        rc = _native.kernels().ib_attn_decode(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                                              block_table.data_ptr(), _ptr(bt_rows), seq_lens.data_ptr(),
+                                              block_table.stride(0), B, hq, hkv, splits, scale, o_ptr, lse_ptr,
+                                              out.data_ptr(), out.stride(0), _stream())
+        _native.check(rc, "ib_attn_decode")
     _count(2 if splits > 1 else 1)
     return out
 
