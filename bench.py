@@ -52,10 +52,11 @@ def log(*a) -> None:
 def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
-    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=15)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--rate", type=float, default=6.0, help="Poisson arrivals per second per GPU")
+    ap.add_argument("--rate", type=float, default=8.0,
+                    help="Poisson arrivals per second per GPU (8 = 64 req/s over 8 instances, the top of the sweep)")
     ap.add_argument("--slice", type=float, default=1.0, help="seconds of trace per step")
     ap.add_argument("--model", default=MODEL)
     ap.add_argument("--max-num-seqs", type=int, default=128)
@@ -165,7 +166,20 @@ def run_ours(args) -> dict:
         "prefix_hit_rate": st["prefix_hit_rate"], "clocks": clocks,
         "kernel_status": K.scratch(dev).read_status(),
     }
+    e2e_local = None
+    if not args.no_e2e:
+        from infera_b200.bench.e2e import run_e2e_on_engine
+
+        _barrier(world)
+        log("e2e: serving the same engine over HTTP, load generator in a separate process")
+        e2e_local = run_e2e_on_engine(eng, model=args.model, rank=rank,
+                                      sessions=range(rank * SESSIONS_PER_GPU + 100000,
+                                                     (rank + 1) * SESSIONS_PER_GPU + 100000),
+                                      rate=args.rate, warmup_s=args.warmup * args.slice,
+                                      timed_s=(args.e2e_steps or args.steps) * args.slice, seed=args.seed + rank)
+        log(f"e2e done: {e2e_local['completed']} completed, {e2e_local['errors']} errors")
     allr = _gather(local_res, world)
+    e2e_all = _gather(e2e_local, world) if e2e_local is not None else None
     del rp
     eng_cfg = ecfg
     del eng
@@ -194,6 +208,10 @@ def run_ours(args) -> dict:
         "kernel_status": max(r["kernel_status"] for r in allr),
         "engine_cfg": {"max_num_seqs": eng_cfg.max_num_seqs, "max_batched_tokens": eng_cfg.max_batched_tokens},
     }
+    if e2e_all is not None:
+        from infera_b200.bench.e2e import aggregate
+
+        res["e2e"] = aggregate(e2e_all)
     return res
 
 
@@ -208,11 +226,7 @@ def main(argv=None) -> int:
     t0 = time.time()
     res = run_ours(args)
     rank = int(os.environ.get("RANK", "0"))
-    e2e = None
-    if not args.no_e2e:
-        from infera_b200.bench.e2e import run_e2e
-
-        e2e = run_e2e(args)
+    e2e = res.get("e2e")
     if rank != 0:
         return 0
     K_ = args.steps

@@ -91,9 +91,11 @@ class EngineReplay:
         while self.pending_arrivals and self.idle:
             arr = self.pending_arrivals.popleft()
             s = self.idle.popleft()
+            idle_since = s.idle_since
             if s.done(self.spec.context_cap):
                 s = self._recycle(s)
-            self._issue(s, max(arr, 0.0))
+            # a turn cannot exist before its session's previous turn ended
+            self._issue(s, max(arr, idle_since, 0.0))
 
     # ------------------------------------------------------------------ main loop
     def prime_prefixes(self) -> None:
@@ -139,6 +141,7 @@ class EngineReplay:
                         s.history = prompt + self.collected.pop(rid)
                         s.turn += 1
                         s.busy = False
+                        s.idle_since = self.now()
                         self.idle.append(s)
             else:
                 wait = (self.next_arrival or now) - now

@@ -48,6 +48,8 @@ PRESETS = {
     "pd-70b": TraceSpec("pd-70b", 256, 4, 7372, 1, 8, (820, 25395), (256, 256), 128256),
     "ep-dsv3": TraceSpec("ep-dsv3", 256, 1, 0, 1, None, (2048, 16384), (256, 1024), 129280),
     "tiering-32b": TraceSpec("tiering-32b", 256, 5, 65536, 1, None, (512, 512), (128, 128), 151936, 131072, True),
+    # small shape for tests
+    "tiny": TraceSpec("tiny", 8, 3, 32, 4, None, (8, 16), (2, 4), 1000, 512),
 }
 
 
@@ -61,6 +63,7 @@ class Session:
     history: list[int] = field(default_factory=list)   # prompt of the last turn + its output
     turn: int = 0
     busy: bool = False
+    idle_since: float = 0.0
 
     def next_prompt(self) -> list[int]:
         base = self.history if self.history else self.prefix

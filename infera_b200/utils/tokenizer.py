@@ -24,10 +24,14 @@ CANARY_STRING = "The quick brown fox jumps over the lazy dog. 0123456789 ~!@#$%^
 
 
 class ByteTokenizer:
-    BYTE_BASE = 1000
-
-    def __init__(self, vocab_size: int = 128256, bos_id: int = 128000, eos_id: int = 128001):
+    def __init__(self, vocab_size: int = 128256, bos_id: int | None = None, eos_id: int | None = None):
         self.vocab_size = vocab_size
+        # bytes live at [BYTE_BASE, BYTE_BASE + 256); small test vocabularies start them at 0
+        self.BYTE_BASE = 1000 if vocab_size >= 2048 else 0
+        if bos_id is None:
+            bos_id = 128000 if vocab_size > 128010 else vocab_size - 16
+        if eos_id is None:
+            eos_id = bos_id + 1
         self.bos_id = bos_id
         self.eos_id = eos_id
         self.start_id = bos_id + 6   # <|start_header|>
