@@ -1,0 +1,90 @@
+"""Standalone kernel cases for timing and profiling (small device
+footprint, inputs larger than L2 where the case is memory-bound).
+
+    python -m infera_b200.bench.kernel_cases <case> [--iters N]
+
+Cases: gemm_prefill (2048x6144x4096 bf16), gemm_decode (64 tokens x
+28672x4096, SwiGLU epilogue), gemm_lmhead (64x128256x4096), decode_attn
+(32 seqs x 8192 keys, GQA 32/8), prefill_attn (2048 queries over 2048 keys,
+causal), prefill_attn_prefix (1024 queries over 8192 keys). Prints one JSON
+line: mean CUDA-event time per launch after 3 warm-up launches, and the
+achieved TFLOP/s or GB/s.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from infera_b200.ops import kernels as K
+
+
+def _time(fn, iters: int) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def run_case(case: str, iters: int) -> dict:
+    dev = "cuda"
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(0)
+    if case.startswith("gemm"):
+        M, N, Kd, swiglu = {"gemm_prefill": (2048, 6144, 4096, False), "gemm_decode": (64, 28672, 4096, True),
+                            "gemm_lmhead": (64, 128256, 4096, False)}[case]
+        x = torch.randn(M, Kd, device=dev, generator=g).to(bf)
+        w = (torch.randn(N, Kd, device=dev, generator=g) / math.sqrt(Kd)).to(bf)
+        ms = _time(lambda: K.linear(x, w, swiglu=swiglu), iters)
+        fl = 2 * M * N * Kd
+        by = (M * Kd + N * Kd + M * (N // 2 if swiglu else N)) * 2
+        return {"case": case, "ms": ms, "tflops": fl / ms / 1e9, "gbs": by / ms / 1e6, "plan": K.gemm_plan(M, N, Kd)}
+    hq, hkv, D = 32, 8, 128
+    if case == "decode_attn":
+        B, L = 32, 8192
+        pages = B * L // 16
+        kc = torch.randn(pages * 16, hkv * D, device=dev, generator=g).to(bf)
+        vc = torch.randn(pages * 16, hkv * D, device=dev, generator=g).to(bf)
+        bt = torch.randperm(pages, device=dev, dtype=torch.int32).view(B, -1)
+        sl = torch.full((B,), L, dtype=torch.int32, device=dev)
+        q = torch.randn(B, hq * D, device=dev, generator=g).to(bf)
+        sp = K.decode_splits(B, hkv, L)
+        ms = _time(lambda: K.attn_decode(q, kc, vc, bt, sl, hq, hkv, 1 / math.sqrt(D), splits=sp), iters)
+        by = 2 * B * L * hkv * D * 2
+        return {"case": case, "ms": ms, "gbs": by / ms / 1e6, "splits": sp}
+    if case in ("prefill_attn", "prefill_attn_prefix"):
+        ql, ctx = (2048, 2048) if case == "prefill_attn" else (1024, 8192)
+        pages = ctx // 16
+        kc = torch.randn(pages * 16, hkv * D, device=dev, generator=g).to(bf)
+        vc = torch.randn(pages * 16, hkv * D, device=dev, generator=g).to(bf)
+        bt = torch.arange(pages, device=dev, dtype=torch.int32).view(1, -1)
+        q = torch.randn(ql, hq * D, device=dev, generator=g).to(bf)
+        tiles = torch.tensor(K.prefill_tiles([ql]), dtype=torch.int32, device=dev)
+        meta = [torch.tensor([v], dtype=torch.int32, device=dev) for v in (0, ql, ctx)]
+        ms = _time(lambda: K.attn_prefill(q, kc, vc, bt, *meta, tiles, hq, hkv, 1 / math.sqrt(D)), iters)
+        keys = sum(ctx - ql + i + 1 for i in range(ql))
+        return {"case": case, "ms": ms, "tflops": 4 * keys * D * hq / ms / 1e9}
+    raise SystemExit(f"unknown case {case}")
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case")
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args(argv)
+    res = run_case(a.case, a.iters)
+    res["status"] = K.scratch().read_status()
+    print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()
