@@ -1,0 +1,195 @@
+"""CPU fleet benchmark for the router plumbing (serving config 1).
+
+Everything runs in one process on localhost, over the real wire paths:
+an in-memory etcd v3 JSON gateway; N mock engine workers (each registers
+with a 30 s lease and heartbeats, publishes KV events on its own ZMQ PUB
+socket); the router (KV-aware policy, etcd discovery, ZMQ event client)
+behind the FastAPI front door; and the open-loop trace replayed by the HTTP
+load generator against the router. Optionally one worker receives the
+shutdown sequence mid-run (heartbeat stop -> deregister -> drain -> stop)
+and the run reports whether any request failed.
+
+    python -m infera_b200.bench.fleet [--workers 4] [--rate 20] [--duration 60] [--drain-at 30]
+
+Reports the prefix-hit rate seen by the workers, TTFT p50 / p99, request
+errors and the per-worker request split.
+"""
+
+from __future__ import annotations
+
+import argparse
+import asyncio
+import json
+import socket
+import threading
+import time
+
+from infera_b200.bench.slo import percentile
+
+
+def free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+class ServerThread:
+    """A uvicorn server on a background thread."""
+
+    def __init__(self, app, port: int):
+        import uvicorn
+
+        self.port = port
+        self.server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning",
+                                                   access_log=False))
+        self.thread = threading.Thread(target=self.server.run, daemon=True)
+
+    def start(self) -> "ServerThread":
+        self.thread.start()
+        t0 = time.time()
+        while not self.server.started and time.time() - t0 < 30:
+            time.sleep(0.02)
+        return self
+
+    def stop(self) -> None:
+        self.server.should_exit = True
+        self.thread.join(timeout=10)
+
+
+class MockWorker:
+    def __init__(self, idx: int, etcd_url: str, model: str, *, capacity_blocks=4096, prefill_ms=0.05,
+                 decode_ms=10.0, vocab=32000):
+        from infera_b200.bench.mock_engine import MockEngine, build_mock_app
+        from infera_b200.common.worker_pool import EngineType, KvRegistrationMetadata, WorkerInfo
+        from infera_b200.engine.kv_events import KvEventPublisher
+        from infera_b200.utils.tokenizer import ByteTokenizer, canary
+
+        self.port = free_port()
+        ev_port = free_port()
+        self.ev_endpoint = f"tcp://127.0.0.1:{ev_port}"
+        self.pub = KvEventPublisher(self.ev_endpoint, flush_ms=0.0)
+        self.eng = MockEngine(capacity_blocks=capacity_blocks, prefill_ms_per_token=prefill_ms,
+                              decode_ms_per_token=decode_ms, vocab=vocab, publisher=self.pub, seed=idx)
+        self.server = ServerThread(build_mock_app(self.eng, model), self.port)
+        tok = ByteTokenizer(vocab_size=vocab)
+        kv = KvRegistrationMetadata(engine_block_size=16, index_block_size=16, tokenizer=tok.name,
+                                    tokenizer_digest=tok.digest(), tokenizer_canary=canary(tok),
+                                    events_endpoint=self.ev_endpoint)
+        self.info = WorkerInfo(worker_id=f"127.0.0.1:{self.port}", url=f"http://127.0.0.1:{self.port}",
+                               model_name=model, engine=EngineType.INFERA_B200, kv_events_endpoint=self.ev_endpoint,
+                               kv_block_size=16, kv=kv)
+        self.etcd_url = etcd_url
+        self.reg = None
+        self.hb = None
+
+    async def start(self) -> None:
+        from infera_b200.common.registration import EtcdRegistration
+
+        self.server.start()
+        self.reg = EtcdRegistration(self.etcd_url, self.info.to_payload())
+        await self.reg.register()
+        self.hb = asyncio.create_task(self.reg.heartbeat_loop())
+
+    async def shutdown(self, drain_timeout: float = 60.0) -> dict:
+        """Heartbeat off -> deregister -> drain in-flight -> stop."""
+        t0 = time.monotonic()
+        if self.hb is not None:
+            self.hb.cancel()
+        await self.reg.deregister()
+        t_dereg = time.monotonic() - t0
+        while self.eng.inflight > 0 and time.monotonic() - t0 < drain_timeout:
+            await asyncio.sleep(0.01)
+        drained = self.eng.inflight == 0
+        self.eng.draining = True
+        self.server.stop()
+        self.pub.close()
+        await self.reg.close()
+        return {"deregister_s": t_dereg, "drain_s": time.monotonic() - t0, "drained": drained}
+
+
+async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 60.0, drain_at: float | None = 30.0,
+                    sessions: int = 64, policy: str = "kv-aware", seed: int = 0, trace: str = "router-plumbing",
+                    decode_ms: float = 10.0, prefill_ms: float = 0.05) -> dict:
+    from types import SimpleNamespace
+
+    from infera_b200.bench.http_loadgen import run as loadgen
+    from infera_b200.common.etcd_fake import build_app as etcd_app
+    from infera_b200.server.__main__ import build_router_stack
+    from infera_b200.server.app import build_app
+
+    model = "mock-model"
+    etcd = ServerThread(etcd_app(), free_port()).start()
+    etcd_url = f"http://127.0.0.1:{etcd.port}"
+    ws = [MockWorker(i, etcd_url, model, decode_ms=decode_ms, prefill_ms=prefill_ms) for i in range(workers)]
+    for w in ws:
+        await w.start()
+    args = SimpleNamespace(router_policy=policy, router_tokenizer_path=None, kv_overlap_weight=1.0,
+                           kv_prefill_overlap_weight=None, kv_decode_overlap_weight=None,
+                           breaker_failure_threshold=3, breaker_cooldown_s=5.0, breaker_max_cooldown_s=60.0,
+                           discovery_backend="etcd", etcd_endpoint=etcd_url, etcd_prefix="/infera/workers/",
+                           request_max_retries=1, migration_limit=0, router_mode="auto", enable_profiling=True,
+                           enable_scaling_api=False, scaling_deployment=None, kvd_socket_path=None, block_size=16,
+                           k8s_label_selector=None, k8s_namespace=None)
+    state = build_router_stack(args)
+    app = build_app(state)
+    app.router.on_startup.append(state.registry.start)
+    router = ServerThread(app, free_port()).start()
+    router_url = f"http://127.0.0.1:{router.port}"
+    t_wait = time.time()
+    while len(state.registry.pool.list_active()) < workers and time.time() - t_wait < 10:
+        await asyncio.sleep(0.05)
+    drain_info = {}
+
+    async def drainer():
+        await asyncio.sleep(drain_at)
+        t0 = time.monotonic()
+        victim = ws[-1]
+        info = await victim.shutdown()
+        # time until the router no longer lists the victim
+        info["router_removed"] = victim.info.worker_id not in [w.worker_id for w in state.registry.pool.all()]
+        info["t"] = time.monotonic() - t0
+        drain_info.update(info)
+
+    dtask = asyncio.create_task(drainer()) if drain_at is not None and workers > 1 else None
+    res = await loadgen(router_url, model, trace, list(range(sessions)), rate, duration, seed, stop_after_s=30.0)
+    if dtask is not None:
+        await dtask
+    recs = [r for r in res["records"] if r["token_times"]]
+    ttfts = [r["token_times"][0] - r["arrival"] for r in recs]
+    prompt = sum(r["prompt_len"] for r in recs)
+    cached = sum(r["cached_len"] for r in recs)
+    split = {w.info.worker_id: w.eng.stats["requests"] for w in ws}
+    view = {wid: len(state.policy.kv_client.cache_view(wid)) for wid in split} if policy == "kv-aware" else {}
+    out = {
+        "requests": len(res["records"]), "completed": len(recs), "errors": res["errors"],
+        "prefix_hit_rate": cached / max(1, prompt),
+        "ttft_p50_ms": 1000 * percentile(ttfts, 50), "ttft_p99_ms": 1000 * percentile(ttfts, 99),
+        "per_worker_requests": split, "router_view_blocks": view, "drain": drain_info,
+    }
+    router.stop()
+    for w in ws:
+        if w.server.thread.is_alive():
+            await w.shutdown(drain_timeout=5)
+    await state.registry.stop()
+    etcd.stop()
+    return out
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--workers", type=int, default=4)
+    ap.add_argument("--rate", type=float, default=20.0)
+    ap.add_argument("--duration", type=float, default=60.0)
+    ap.add_argument("--drain-at", type=float, default=30.0)
+    ap.add_argument("--sessions", type=int, default=64)
+    ap.add_argument("--policy", default="kv-aware")
+    a = ap.parse_args(argv)
+    res = asyncio.run(run_fleet(workers=a.workers, rate=a.rate, duration=a.duration, drain_at=a.drain_at,
+                                sessions=a.sessions, policy=a.policy))
+    print(json.dumps(res, indent=1))
+
+
+if __name__ == "__main__":
+    main()

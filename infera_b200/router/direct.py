@@ -9,7 +9,7 @@ from fastapi.responses import JSONResponse, Response
 
 from infera_b200.common.worker_pool import DisaggMode
 from infera_b200.router.disagg import DisaggRouter
-from infera_b200.router.mixed import BaseRouter, MixedRouter
+from infera_b200.router.mixed import BaseRouter, MixedRouter, Retry
 from infera_b200.router.policy.target import RouteTarget
 
 WORKER_HEADER = "x-worker-instance-id"
@@ -43,4 +43,10 @@ class DirectRouter(BaseRouter):
             return JSONResponse({"error": f"worker {wid!r} is {w.disagg_mode.value}; name a prefill worker too"},
                                 status_code=400)
         t = RouteTarget(w, w.dp_rank)
-        return await self.mixed._attempt(t, [], body, body.get("_infera_cache_hints"), path, stream)
+        try:
+            resp = await self.mixed._attempt(t, [], body, body.get("_infera_cache_hints"), path, stream)
+        except Retry as r:  # no failover in direct mode: the gateway picked this worker
+            self.breaker.record_failure(wid, r.status)
+            return r.response
+        self.breaker.record_success(wid)
+        return resp
