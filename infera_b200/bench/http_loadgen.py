@@ -28,14 +28,20 @@ from infera_b200.bench.trace import PRESETS, build_sessions
 
 
 async def run(url: str, model: str, spec_name: str, sids: list[int], rate: float, duration: float, seed: int,
-              stop_after_s: float | None = None, extra_body: dict | None = None) -> dict:
+              stop_after_s: float | None = None, extra_body: dict | None = None, text_prompts: bool = False,
+              start_at: float | None = None) -> dict:
+    """``text_prompts``: send prompts as ``t<id>`` words and read generated
+    ids back from the text (for servers whose tokenizer maps words to ids
+    one to one; see :mod:`infera_b200.bench.hf_model_dir`)."""
+    from infera_b200.bench.hf_model_dir import ids_to_text, text_to_ids
+
     spec = PRESETS[spec_name]
     sessions = build_sessions(spec, seed, sids)
     idle = deque(sessions)
     rng = random.Random(seed + 17)
     pending: deque[float] = deque()
     records: list[dict] = []
-    t0 = time.monotonic()
+    t0 = time.monotonic() if start_at is None else start_at
     next_sid = max(sids) + 1 + 1_000_000 * (seed + 1)
     limits = httpx.Limits(max_connections=None, max_keepalive_connections=1024)
     tasks: set[asyncio.Task] = set()
@@ -47,9 +53,11 @@ async def run(url: str, model: str, spec_name: str, sids: list[int], rate: float
 
         async def one(s, arrival):
             prompt = s.next_prompt()
-            body = {"model": model, "prompt": prompt, "max_tokens": s.out_lens[s.turn], "stream": True,
-                    "ignore_eos": True, "return_token_ids": True, "temperature": 0.0,
+            body = {"model": model, "prompt": ids_to_text(prompt) if text_prompts else prompt,
+                    "max_tokens": s.out_lens[s.turn], "stream": True, "ignore_eos": True, "temperature": 0.0,
                     "stream_options": {"include_usage": True}}
+            if not text_prompts:
+                body["return_token_ids"] = True
             if extra_body:
                 body.update(extra_body)
             rec = {"arrival": arrival, "token_times": [], "finish": None, "prompt_len": len(prompt),
@@ -81,7 +89,9 @@ async def run(url: str, model: str, spec_name: str, sids: list[int], rate: float
                                     rec["cached_len"] = int(det.get("cached_tokens") or 0)
                                 for ch in obj.get("choices") or []:
                                     ids = ch.get("token_ids")
-                                    if ids is None and ch.get("text") is not None:
+                                    if ids is None and text_prompts:
+                                        ids = text_to_ids(ch.get("text") or "")
+                                    elif ids is None and ch.get("text") is not None:
                                         ids = [0]
                                     for tok in ids or []:
                                         out_ids.append(int(tok))
@@ -136,9 +146,11 @@ def main(argv=None) -> None:
     ap.add_argument("--duration", type=float, required=True)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--drain-s", type=float, default=0.0)
+    ap.add_argument("--text-prompts", action="store_true")
     a = ap.parse_args(argv)
     lo, hi = (int(x) for x in a.sessions.split(":"))
-    res = asyncio.run(run(a.url, a.model, a.trace, list(range(lo, hi)), a.rate, a.duration, a.seed, a.drain_s))
+    res = asyncio.run(run(a.url, a.model, a.trace, list(range(lo, hi)), a.rate, a.duration, a.seed, a.drain_s,
+                          text_prompts=a.text_prompts))
     json.dump(res, sys.stdout)
     sys.stdout.flush()
 
