@@ -1,0 +1,54 @@
+// KV page gather / scatter between the paged cache and a contiguous chunk.
+//
+// Chunk layout (KV chunk blob v2 payload): [C, L, T, H] with C = 2 (K, V),
+// L layers, T = n_pages * 16 tokens, H = kv elements per token.
+// Cache layout: per channel [L, num_slots, H] (slot = page * 16 + offset), so
+// one page of one layer is 16 * H contiguous elements: each CTA moves one
+// (page, layer, channel) block with 16-byte vector accesses.
+//
+//   dir 0 (gather / save):  chunk[c, l, p*16 + i, :] = cache_c[l, pages[p]*16 + i, :]
+//   dir 1 (scatter / load): cache_c[l, pages[p]*16 + i, :] = chunk[c, l, p*16 + i, :]
+//
+// Reference parity: the reference implements this transfer as a Triton
+// kernel (infera/engine/vllm/triton_kv_gather.py:82-220, with a Python loop
+// oracle at :546-627); this is the CUDA counterpart for this cache layout.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ib200 {
+namespace kvp {
+
+__global__ void page_copy_kernel(uint4* __restrict__ k_cache, uint4* __restrict__ v_cache, uint4* __restrict__ chunk,
+                                 const int* __restrict__ pages, int n_pages, int L, long long slots_per_layer,
+                                 int vec_per_token, int dir) {
+  const int p = blockIdx.x, l = blockIdx.y, c = blockIdx.z;
+  uint4* cache = c == 0 ? k_cache : v_cache;
+  const long long page = pages[p];
+  const long long tokens = static_cast<long long>(n_pages) * 16;
+  const long long n = 16ll * vec_per_token;
+  uint4* cbase = cache + (static_cast<long long>(l) * slots_per_layer + page * 16) * vec_per_token;
+  uint4* xbase = chunk + ((static_cast<long long>(c) * L + l) * tokens + static_cast<long long>(p) * 16) *
+                             vec_per_token;
+  if (dir == 0) {
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) xbase[i] = cbase[i];
+  } else {
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) cbase[i] = xbase[i];
+  }
+}
+
+}  // namespace kvp
+}  // namespace ib200
+
+// k_cache / v_cache: [L, slots, H] of elem_bytes elements; chunk: [2, L, n_pages*16, H].
+// H * elem_bytes must be a multiple of 16.
+extern "C" int ib_kv_page_copy(void* k_cache, void* v_cache, void* chunk, const int* pages, int n_pages, int L,
+                               long long slots_per_layer, int H, int elem_bytes, int dir, cudaStream_t stream) {
+  if (n_pages <= 0) return 0;
+  if ((H * elem_bytes) % 16 != 0 || (dir != 0 && dir != 1)) return -1;
+  dim3 grid(n_pages, L, 2);
+  ib200::kvp::page_copy_kernel<<<grid, 256, 0, stream>>>(
+      static_cast<uint4*>(k_cache), static_cast<uint4*>(v_cache), static_cast<uint4*>(chunk), pages, n_pages, L,
+      slots_per_layer, H * elem_bytes / 16, dir);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}

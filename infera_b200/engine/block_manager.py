@@ -51,7 +51,8 @@ class BlockManager:
         self.free_plain: list[int] = list(range(num_pages - 1, reserved_pages - 1, -1))
         self.evictable: OrderedDict[int, None] = OrderedDict()   # cached pages with refcount 0 (LRU order)
         self.hash_to_page: dict[int, int] = {}
-        self.stats = {"hit_tokens": 0, "query_tokens": 0, "evictions": 0}
+        self.stats = {"hit_tokens": 0, "query_tokens": 0, "evictions": 0, "tier_hit_tokens": 0}
+        self.tier = None   # optional TierManager: saves evicted prefix pages, promotes them back
 
     # ------------------------------------------------------------------ capacity
     def num_free(self) -> int:
@@ -73,6 +74,8 @@ class BlockManager:
         page, _ = self.evictable.popitem(last=False)
         h = self.page_hash[page]
         if h is not None:
+            if self.tier is not None:
+                self.tier.on_evict(page, h)   # copy out before the page is reused
             if self.hash_to_page.get(h) == page:
                 del self.hash_to_page[h]
             self.page_hash[page] = None
@@ -120,7 +123,14 @@ class BlockManager:
         """Reference the prefix hit and allocate pages for ``num_tokens``
         tokens in total. Returns None (and changes nothing) if memory is
         short."""
+        if hashes is None:
+            hashes = chain_hashes(token_ids, self.page_size)
         hit_pages, hit_hashes = self.match_prefix(token_ids, hashes)
+        n_tier = 0
+        if self.tier is not None and self.enable_prefix_cache:
+            n_tier = self.tier.match(hashes[len(hit_pages):])
+            if (len(hit_pages) + n_tier) * self.page_size >= len(token_ids):
+                n_tier = max(0, (len(token_ids) - 1) // self.page_size - len(hit_pages))
         need = (num_tokens + self.page_size - 1) // self.page_size - len(hit_pages)
         # hit pages that are currently evictable do not count as free for us
         hit_evictable = sum(1 for p in hit_pages if self.refcount[p] == 0)
@@ -136,6 +146,13 @@ class BlockManager:
             p = self._take_page()
             self.refcount[p] = 1
             sb.pages.append(p)
+        if n_tier > 0:
+            start = len(hit_pages)
+            got = self.tier.load(sb.pages[start:start + n_tier], hashes[start:start + n_tier])
+            if got > 0:
+                self.commit_full_pages(sb, token_ids, (start + got) * self.page_size)
+                sb.num_cached_tokens = (start + got) * self.page_size
+                self.stats["tier_hit_tokens"] += got * self.page_size
         self.stats["hit_tokens"] += sb.num_cached_tokens
         self.stats["query_tokens"] += len(token_ids)
         return sb

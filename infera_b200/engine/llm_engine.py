@@ -22,6 +22,23 @@ from infera_b200.models.config import DenseConfig, get_config
 from infera_b200.models.dense import DenseModel
 
 
+def _tier_store(spec: str):
+    """Build the store behind a ``kv_tier`` spec (see EngineConfig)."""
+    kind, _, rest = spec.partition(":")
+    if kind == "kvd":
+        from infera_b200.kvd.client import SyncKvdStore
+
+        return SyncKvdStore(rest)
+    if kind == "host":
+        from infera_b200.kvd.store import HostStore
+        from infera_b200.kvd.tablespace import Tablespace
+
+        gib, _, nvme = rest.partition(":")
+        l3 = Tablespace(nvme, fsync=False) if nvme else None
+        return HostStore(int(float(gib or 4) * (1 << 30)), l3=l3)
+    raise ValueError(f"unknown kv_tier spec {spec!r}")
+
+
 @dataclass
 class EngineConfig:
     model: str = "llama-3.1-8b"
@@ -36,6 +53,9 @@ class EngineConfig:
     long_prefill_threshold: int = 0
     max_model_len: int | None = None
     model_overrides: dict = field(default_factory=dict)
+    # KV tiering: None (off), "host:<GiB>[:<nvme dir>]" (in-process host store,
+    # optional NVMe tablespace) or "kvd:<socket path>" (shared daemon)
+    kv_tier: str | None = None
 
 
 class LLMEngine:
@@ -60,6 +80,13 @@ class LLMEngine:
                                    long_prefill_threshold=cfg.long_prefill_threshold)
         self.runner = ModelRunner(self.model, num_pages, cfg.page_size, cfg.max_num_seqs, cfg.max_batched_tokens,
                                   use_graphs=cfg.use_cuda_graphs)
+        self.tier = None
+        if cfg.kv_tier:
+            from infera_b200.engine.tiering import TierManager
+
+            self.tier = TierManager(self.runner.k_cache, self.runner.v_cache, _tier_store(cfg.kv_tier),
+                                    cfg.page_size)
+            self.bm.tier = self.tier
         self.requests: dict[str, Request] = {}
         self.num_steps = 0
         self.clock: Callable[[], float] = time.monotonic

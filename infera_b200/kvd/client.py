@@ -119,6 +119,36 @@ def hash_key(h: int) -> bytes:
     return int(h).to_bytes(8, "little", signed=False)
 
 
+class SyncKvdStore:
+    """Blocking facade over :class:`KvdClient` (its own event-loop thread) with
+    the ``set / get / exists`` surface the engine's tier manager uses."""
+
+    def __init__(self, path: str, shared_arena: bool = True):
+        import threading
+
+        self.loop = asyncio.new_event_loop()
+        self._t = threading.Thread(target=self.loop.run_forever, daemon=True)
+        self._t.start()
+        self.client = KvdClient(path, "infera-b200-engine")
+        self._run(self.client.connect(shared_arena=shared_arena))
+
+    def _run(self, coro):
+        return asyncio.run_coroutine_threadsafe(coro, self.loop).result()
+
+    def set(self, key: bytes, value, retention: str = "long") -> bool:
+        return self._run(self.client.set(key, bytes(value), retention))
+
+    def get(self, key: bytes) -> bytes | None:
+        return self._run(self.client.get(key))
+
+    def exists(self, key: bytes) -> bool:
+        return self._run(self.client.exists([key]))[0]
+
+    def close(self) -> None:
+        self._run(self.client.close())
+        self.loop.call_soon_threadsafe(self.loop.stop)
+
+
 class KvdPrefetchClient:
     """Router side: one short-lived connection per prewarm request."""
 

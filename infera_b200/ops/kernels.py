@@ -476,3 +476,29 @@ def scatter_i32(dst: torch.Tensor, idx: torch.Tensor, val: torch.Tensor) -> None
     rc = _native.kernels().ib_scatter_i32(dst.data_ptr(), idx.data_ptr(), val.data_ptr(), n, _stream())
     _native.check(rc, "ib_scatter_i32")
     _count()
+
+
+def kv_page_copy(k_cache: torch.Tensor, v_cache: torch.Tensor, chunk: torch.Tensor, pages: torch.Tensor,
+                 page_size: int = 16, gather: bool = True) -> None:
+    """Move whole KV pages between the cache ([L, slots, H] per channel) and a
+    contiguous chunk [2, L, n_pages*page_size, H]: ``gather=True`` copies
+    cache -> chunk (save), ``False`` chunk -> cache (load)."""
+    n = pages.shape[0]
+    if n == 0:
+        return
+    L, slots, H = k_cache.shape
+    if not k_cache.is_cuda:
+        idx = (pages.long()[:, None] * page_size + torch.arange(page_size)[None, :]).reshape(-1)
+        view = chunk.view(2, L, n * page_size, H)
+        for c, cache in enumerate((k_cache, v_cache)):
+            if gather:
+                view[c] = cache[:, idx]
+            else:
+                cache[:, idx] = view[c]
+        return
+    assert page_size == 16 and chunk.is_contiguous()
+    rc = _native.kernels().ib_kv_page_copy(k_cache.data_ptr(), v_cache.data_ptr(), chunk.data_ptr(),
+                                           pages.data_ptr(), n, L, slots, H, k_cache.element_size(),
+                                           0 if gather else 1, _stream())
+    _native.check(rc, "ib_kv_page_copy")
+    _count()

@@ -1,0 +1,60 @@
+"""KV chunk format v2, page gather/scatter, and engine tiering: a prefix
+evicted from HBM is saved to the host tier and promoted back on the next
+request, with outputs unchanged."""
+
+import pytest
+import torch
+
+from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
+from infera_b200.engine.packed_format import ChunkHeader, PackedFormatError, pack_chunk, unpack_chunk
+from infera_b200.engine.request import SamplingParams
+from infera_b200.models.reference import reference_greedy
+from infera_b200.ops import kernels as K
+
+
+def test_packed_format_roundtrip_and_alignment():
+    h = ChunkHeader(chunk_tokens=16, block_size=16, num_layers=3, hidden_dim=64, dtype="bf16",
+                    layer_names=("a", "b", "c"))
+    payload = bytes(range(256)) * (h.payload_bytes // 256)
+    blob = pack_chunk(h, payload)
+    h2, p2 = unpack_chunk(blob)
+    assert h2.payload_byte_offset % 4096 == 0 and bytes(p2) == payload and h2.layer_names == ("a", "b", "c")
+    with pytest.raises(PackedFormatError):
+        unpack_chunk(blob[:100])
+    with pytest.raises(PackedFormatError):
+        pack_chunk(h, payload[:-2])
+
+
+def test_kv_page_copy_roundtrip():
+    L, slots, H = 2, 64, 32
+    k = torch.randn(L, slots, H).to(torch.bfloat16)
+    v = torch.randn(L, slots, H).to(torch.bfloat16)
+    pages = torch.tensor([3, 1], dtype=torch.int32)
+    chunk = torch.empty(2 * L * 32 * H, dtype=torch.bfloat16)
+    K.kv_page_copy(k, v, chunk, pages, gather=True)
+    c = chunk.view(2, L, 32, H)
+    assert torch.equal(c[0, 1, :16], k[1, 48:64]) and torch.equal(c[1, 0, 16:], v[0, 16:32])
+    k2, v2 = torch.zeros_like(k), torch.zeros_like(v)
+    K.kv_page_copy(k2, v2, chunk, pages, gather=False)
+    assert torch.equal(k2[:, 48:64], k[:, 48:64]) and torch.equal(v2[:, 16:32], v[:, 16:32])
+
+
+def test_engine_tier_save_and_promote():
+    eng = LLMEngine(EngineConfig(model="tiny-dense", use_cuda_graphs=False, num_pages=12, max_batched_tokens=256,
+                                 kv_tier="host:0.05"), device="cpu")
+    g = torch.Generator().manual_seed(4)
+    a = torch.randint(0, 1000, (64,), generator=g).tolist()
+    sp = SamplingParams(max_tokens=2, ignore_eos=True)
+    eng.generate([a], sp)
+    for _ in range(3):  # other prompts push A's pages out of HBM
+        eng.generate([torch.randint(0, 1000, (64,), generator=g).tolist()], sp)
+    eng.tier.flush()
+    assert eng.tier.stats["saved"] >= 4
+    a2 = a + [5, 6, 7]
+    out = eng.generate([a2], SamplingParams(max_tokens=3, ignore_eos=True))[0]
+    assert eng.bm.stats["tier_hit_tokens"] >= 48
+    ref, margins = reference_greedy(eng.model, a2, 3)
+    for i, (x, y) in enumerate(zip(out, ref)):
+        if x != y:
+            assert margins[i] < 0.05
+            break
