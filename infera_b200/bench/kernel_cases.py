@@ -1,13 +1,13 @@
 """Standalone kernel cases for timing and profiling (small device
 footprint, inputs larger than L2 where the case is memory-bound).
 
-    python -m infera_b200.bench.kernel_cases <case> [--iters N]
+    python -m infera_b200.bench.kernel_cases <case> [<case> ...] [--iters N]
 
 Cases: gemm_prefill (2048x6144x4096 bf16), gemm_decode (64 tokens x
 28672x4096, SwiGLU epilogue), gemm_lmhead (64x128256x4096), decode_attn
 (32 seqs x 8192 keys, GQA 32/8), prefill_attn (2048 queries over 2048 keys,
 causal), prefill_attn_prefix (1024 queries over 8192 keys). Prints one JSON
-line: mean CUDA-event time per launch after 3 warm-up launches, and the
+line per case: mean CUDA-event time per launch after 3 warm-up launches, and the
 achieved TFLOP/s or GB/s.
 """
 
@@ -78,12 +78,13 @@ def run_case(case: str, iters: int) -> dict:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case")
+    ap.add_argument("cases", nargs="+")
     ap.add_argument("--iters", type=int, default=20)
     a = ap.parse_args(argv)
-    res = run_case(a.case, a.iters)
-    res["status"] = K.scratch().read_status()
-    print(json.dumps(res), flush=True)
+    for case in a.cases:
+        res = run_case(case, a.iters)
+        res["status"] = K.scratch().read_status()
+        print(json.dumps(res), flush=True)
 
 
 if __name__ == "__main__":

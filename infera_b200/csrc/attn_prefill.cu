@@ -5,10 +5,14 @@
 //               (8 pages of 16 tokens, two 64-dim halves each)
 //   warp 1      MMA issuer: S = Q K^T into TMEM (double buffered),
 //               O += P V into TMEM
-//   warps 2..5  softmax: thread <-> query row; reads S from TMEM, writes
-//               bf16 P into shared memory (K-major, 128-byte swizzle),
-//               rescales O in TMEM only when the running max grows by more
-//               than 2^8 (lazy rescale), final O / l epilogue.
+//   warps 2..9  softmax, two warpgroups per query tile: warps w and w+4
+//               share a TMEM lane quadrant (the same 32 rows) and each
+//               handles half of the 128 keys of S / P and half of the 128
+//               dims of O, exchanging only per-row maxima (bounded mbarrier
+//               pair barrier); P goes to shared memory (K-major, 128-byte
+//               swizzle); O is rescaled in TMEM only when the running max
+//               grows by more than 2^8 (lazy rescale); final O / l epilogue.
+//               Half of the exponentials run on the FMA pipe (polynomial).
 //
 // KV cache layout (per layer): [num_slots, Hkv * 128] bf16 with slot =
 // page * 16 + offset, i.e. a page is 16 tokens x Hkv heads x 128 dims.
@@ -29,9 +33,9 @@ constexpr int PAGE = 16;
 constexpr int HALF = 64 * 128 * 2;    // not used directly
 constexpr int BLK = 128 * 128;        // bytes of one 128-row x 64-col bf16 block (16 KiB)
 constexpr int KV_STAGES = 2;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 320;  // producer, MMA, 8 softmax warps
 // smem: Q (2 blocks) + P (2 blocks) + KV_STAGES x (K 2 blocks + V 2 blocks)
-constexpr int SMEM_BYTES = 1024 + (4 + KV_STAGES * 4) * BLK + 512;
+constexpr int SMEM_BYTES = 1024 + (4 + KV_STAGES * 4) * BLK + 4096;
 constexpr uint32_t S_COL0 = 0, S_COL1 = 128, O_COL = 256;
 
 struct Params {
@@ -48,6 +52,18 @@ struct Params {
   int ldo;
   int* status;
 };
+
+// 2^x on the FMA pipe: split x = n + f (n integer, f in [0,1)), evaluate a
+// cubic fitted to 2^f on [0,1) (max relative error 8.6e-5, far below bf16's
+// 3.9e-3), and add n to the exponent. x = -inf (masked) gives 0.
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float xc = fmaxf(x, -127.0f);
+  const float n = floorf(xc);
+  const float f = xc - n;
+  const float pf = fmaf(fmaf(fmaf(0.07705903f, f, 0.22765373f), f, 0.69511485f), f, 1.0f);
+  const float r = __int_as_float(__float_as_int(pf) + (static_cast<int>(n) << 23));
+  return x == -INFINITY ? 0.0f : r;
+}
 
 __device__ __forceinline__ uint32_t sw128_offset(int row, int chunk16) {
   return static_cast<uint32_t>(row * 128 + ((chunk16 ^ (row & 7)) << 4));
@@ -70,8 +86,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* p_full = s_full + 2;               // [1]
   uint64_t* o_done = p_full + 1;               // [1]
   uint64_t* drain = o_done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* pair = drain + 1;                  // [4] per TMEM quadrant: the two softmax warps on it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(tmem_slot + 4);   // [2 tiles][2 halves][BQ] row maxima
+  float* lsum = red + 4 * BQ;                               // [2 halves][BQ] row sums
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -96,7 +115,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
+    for (int i = 0; i < 4; ++i) mbar_init(&pair[i], 64);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -220,42 +240,65 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_wait(drain, 0, nullptr, p.status, kStatusTimeoutFull);
     }
   } else {
-    // softmax warps: thread <-> query row
+    // softmax warps 2..9: two warpgroups per query tile. Warps w and w+4
+    // share a TMEM lane quadrant (the same 32 rows); warpgroup `half` owns
+    // keys [64*half, 64*half+64) of S and P and dims [64*half, +64) of O.
     const int q4 = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = q4 * 32 + lane;
+    const int cb = half * 64;
     const int pos = pos0 + min(r, valid_rows - 1);
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
     float m_run = -INFINITY;  // running max in log2 units (scaled)
-    float l_run = 0.f;
+    float l_run = 0.f;        // this half's share of the row sum
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
+    uint32_t pph = 0;         // phase of this quadrant's pair barrier
+    auto pair_sync = [&]() {
+      mbar_arrive(&pair[q4]);
+      ok = mbar_wait_warp(&pair[q4], pph & 1u, abort_flag, p.status, kStatusTimeoutTmemFull) && ok;
+      ++pph;
+    };
+    for (int j = 0; j < n_kv && ok; ++j) {
       if (!mbar_wait_warp(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status,
                           kStatusTimeoutTmemFull)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t s_addr = lane_addr + ((j & 1) ? S_COL1 : S_COL0);
+      const uint32_t s_addr = lane_addr + ((j & 1) ? S_COL1 : S_COL0) + cb;
       const int kbase = j * BKV;
-      const int lim = pos - kbase;  // key c visible iff c <= lim
+      const int lim = pos - kbase - cb;  // local key c visible iff c <= lim
+      // every row of the CTA sees the whole tile when it ends at or before the
+      // position of row 0 (CTA-uniform): no per-element mask needed
+      const bool full_tile = kbase + BKV - 1 <= pos0;
+      uint32_t v[64];
+      tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      tmem_ld_wait();
       float mx = -INFINITY;
+      if (full_tile) {
 #pragma unroll
-      for (int c0 = 0; c0 < BKV; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(s_addr + c0, v);
-        tmem_ld_wait();
+        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
+      } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c0 + i <= lim) mx = fmaxf(mx, __uint_as_float(v[i]));
+        for (int i = 0; i < 64; ++i) {
+          if (i > lim) v[i] = __float_as_uint(-INFINITY);
+          mx = fmaxf(mx, __uint_as_float(v[i]));
+        }
       }
-      mx *= p.scale_log2;
-      float m_new = fmaxf(m_run, mx);
-      // Per-row choice (FA4-style lazy rescale: keep a stale max unless the
-      // new one exceeds it by 2^8). The TMEM rescale below is warp-collective,
-      // so the warp rescales if ANY of its rows needs it; other rows use 1.0.
-      bool rescale = (j == 0) || (m_new > m_run + 8.0f);
-      float m_use = rescale ? m_new : m_run;
-      float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
+      // combine the two halves' maxima of each row (double-buffered by tile)
+      red[((j & 1) * 2 + half) * BQ + r] = mx;
+      pair_sync();
+      if (!ok) break;
+      mx = fmaxf(red[((j & 1) * 2) * BQ + r], red[((j & 1) * 2 + 1) * BQ + r]) * p.scale_log2;
+      const float m_new = fmaxf(m_run, mx);
+      // Per-row choice (lazy rescale: keep a stale max unless the new one
+      // exceeds it by 2^8). Both halves make the same choice for a row; the
+      // TMEM rescale is warp-collective, so the warp rescales if ANY of its
+      // rows needs it, with factor 1.0 for the others.
+      const bool rescale = (j == 0) || (m_new > m_run + 8.0f);
+      const float m_use = rescale ? m_new : m_run;
+      const float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
       const bool warp_rescale = __any_sync(0xffffffffu, rescale && j > 0);
       // P of the previous tile must be consumed before P / O are touched
       if (j > 0) {
@@ -268,38 +311,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (warp_rescale) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += 16) {
+        for (int c0 = 0; c0 < 64; c0 += 16) {
           uint32_t o[16];
-          tmem_ld16(lane_addr + O_COL + c0, o);
+          tmem_ld16(lane_addr + O_COL + cb + c0, o);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st16(lane_addr + O_COL + c0, o);
+          tmem_st16(lane_addr + O_COL + cb + c0, o);
         }
         tmem_st_wait();
       }
+      // P = 2^(s*scale - m): even columns on the MUFU unit, odd columns with
+      // the FMA-pipe polynomial. Masked entries hold -inf and give exactly 0.
       float sum = 0.f;
+      const float sl = p.scale_log2;
 #pragma unroll
-      for (int c0 = 0; c0 < BKV; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(s_addr + c0, v);
-        tmem_ld_wait();
-        uint32_t packed[16];
+      for (int i = 0; i < 64; i += 2) {
+        const float e0 = exp2f(fmaf(__uint_as_float(v[i]), sl, -m_use));
+        const float e1 = exp2_fma(fmaf(__uint_as_float(v[i + 1]), sl, -m_use));
+        __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
+        sum += __low2float(bb) + __high2float(bb);
+        v[i / 2] = *reinterpret_cast<uint32_t*>(&bb);   // packed pairs reuse the low half of v
+      }
+      uint8_t* blk = sP + half * BLK;
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float e0 = (c0 + i <= lim) ? exp2f(__uint_as_float(v[i]) * p.scale_log2 - m_use) : 0.f;
-          float e1 = (c0 + i + 1 <= lim) ? exp2f(__uint_as_float(v[i + 1]) * p.scale_log2 - m_use) : 0.f;
-          __nv_bfloat162 b = __floats2bfloat162_rn(e0, e1);
-          sum += __low2float(b) + __high2float(b);
-          packed[i / 2] = *reinterpret_cast<uint32_t*>(&b);
-        }
-        uint8_t* blk = sP + (c0 < 64 ? 0 : BLK);
-        const int chunk0 = (c0 & 63) / 8;  // 16-byte chunk index within the 128-byte row
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 w = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-          *reinterpret_cast<uint4*>(blk + sw128_offset(r, chunk0 + q)) = w;
-        }
+      for (int q = 0; q < 8; ++q) {
+        const uint4 w = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        *reinterpret_cast<uint4*>(blk + sw128_offset(r, q)) = w;
       }
       l_run = l_run * alpha + sum;
       m_run = m_use;
@@ -308,17 +346,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_arrive(p_full);
     }
     ok = __all_sync(0xffffffffu, ok);
+    // row sums: add the two halves' shares
+    lsum[half * BQ + r] = l_run;
+    pair_sync();
     if (ok && n_kv > 0) {
       if (mbar_wait_warp(o_done, static_cast<uint32_t>((n_kv - 1) & 1), abort_flag, p.status,
                          kStatusTimeoutTmemFull)) {
         tc_fence_after();
-        const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+        const float l = lsum[r] + lsum[BQ + r];
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
         const bool write = r < valid_rows;
-        __nv_bfloat16* orow = p.out + static_cast<size_t>(row0 + r) * p.ldo + h * D;
+        __nv_bfloat16* orow = p.out + static_cast<size_t>(row0 + r) * p.ldo + h * D + cb;
 #pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += 32) {
+        for (int c0 = 0; c0 < 64; c0 += 32) {
           uint32_t o[32];
-          tmem_ld32(lane_addr + O_COL + c0, o);
+          tmem_ld32(lane_addr + O_COL + cb + c0, o);
           tmem_ld_wait();
           if (write) {
 #pragma unroll
