@@ -16,10 +16,14 @@ events recorded at the end of each engine iteration, relative to the
 window's origin; the value is the sum over ranks of SLO-meeting requests
 completed in the window divided by the longest rank's window.
 
-The end-to-end figure ("e2e") replays the same trace through the worker's
-OpenAI-compatible HTTP API (/v1/completions, streamed), timed by wall clock
-on the client, which includes every step's pinned host->device copy of the
-inputs and device->host copy of the sampled tokens.
+The end-to-end figure ("e2e") is the reference arm's setup with this
+framework's parts: every rank's engine (prefix cache cleared) serves the
+OpenAI-compatible HTTP API from a separate worker process, all workers sit
+behind one KV-aware router (etcd discovery, ZMQ KV events), and each rank's
+load generator replays the same sessions and seed as the reference arm
+against the router's /v1/completions (streamed), timed by the client's wall
+clock. That includes every step's pinned host->device copy of the inputs
+and device->host copy of the sampled tokens.
 """
 
 from __future__ import annotations
@@ -62,6 +66,7 @@ def parse_args(argv=None):
     ap.add_argument("--max-num-seqs", type=int, default=128)
     ap.add_argument("--max-batched-tokens", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--router-backend", choices=("python", "native"), default="python")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
@@ -80,7 +85,12 @@ def _dist_init():
 
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        global _GLOO
+        _GLOO = dist.new_group(backend="gloo", timeout=timedelta(seconds=900))
     return rank, world, local
+
+
+_GLOO = None
 
 
 def _barrier(world):
@@ -90,13 +100,22 @@ def _barrier(world):
         dist.barrier()
 
 
+def _host_barrier(world):
+    """Barrier over a gloo group: no GPU work, safe while another thread of
+    this process drives the engine."""
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(group=_GLOO)
+
+
 def _gather(obj, world):
     if world == 1:
         return [obj]
     import torch.distributed as dist
 
     out = [None] * world
-    dist.all_gather_object(out, obj)
+    dist.all_gather_object(out, obj, group=_GLOO)
     return out
 
 
@@ -168,15 +187,14 @@ def run_ours(args) -> dict:
     }
     e2e_local = None
     if not args.no_e2e:
-        from infera_b200.bench.e2e import run_e2e_on_engine
+        from infera_b200.bench.e2e import run_e2e_fleet
 
-        _barrier(world)
-        log("e2e: serving the same engine over HTTP, load generator in a separate process")
-        e2e_local = run_e2e_on_engine(eng, model=args.model, rank=rank,
-                                      sessions=range(rank * SESSIONS_PER_GPU + 100000,
-                                                     (rank + 1) * SESSIONS_PER_GPU + 100000),
-                                      rate=args.rate, warmup_s=args.warmup * args.slice,
-                                      timed_s=(args.e2e_steps or args.steps) * args.slice, seed=args.seed + rank)
+        log(f"e2e: {world} worker(s) behind the {args.router_backend} router, load generator per rank")
+        e2e_local = run_e2e_fleet(eng, model=args.model, rank=rank, world=world, barrier=lambda: _host_barrier(world),
+                                  sessions=range(rank * SESSIONS_PER_GPU, (rank + 1) * SESSIONS_PER_GPU),
+                                  rate=args.rate, warmup_s=args.warmup * args.slice,
+                                  timed_s=(args.e2e_steps or args.steps) * args.slice, seed=args.seed + rank,
+                                  router_backend=args.router_backend)
         log(f"e2e done: {e2e_local['completed']} completed, {e2e_local['errors']} errors")
     allr = _gather(local_res, world)
     e2e_all = _gather(e2e_local, world) if e2e_local is not None else None
@@ -211,7 +229,8 @@ def run_ours(args) -> dict:
     if e2e_all is not None:
         from infera_b200.bench.e2e import aggregate
 
-        res["e2e"] = aggregate(e2e_all)
+        res["e2e"] = aggregate(e2e_all, f"OpenAI /v1/completions over HTTP (streamed) through the "
+                                        f"{args.router_backend} KV-aware router, client wall clock")
     return res
 
 
@@ -246,7 +265,8 @@ def main(argv=None) -> int:
         "config": {
             "model": MODEL, "architecture": "32L, hidden 4096, 32q/8kv heads, head_dim 128, SwiGLU 14336, "
                                             "vocab 128256, RoPE theta 500000",
-            "deployment": f"{args.gpus} instance(s) at TP=1, sessions pinned to instances by prefix group",
+            "deployment": f"{args.gpus} instance(s) at TP=1; device-timed: sessions pinned to instances by "
+                          f"prefix group; e2e: behind one KV-aware router",
             "parallelism": f"dp{args.gpus}",
             "global_batch": f"continuous batching, <= {res['engine_cfg']['max_num_seqs']} seqs / instance",
             "seq_len": "context <= 32768 (prefix 4096 shared by 32 sessions, +U[256,1024]/turn, out U[128,512])",

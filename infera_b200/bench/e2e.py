@@ -1,18 +1,32 @@
-"""End-to-end measurement through the public HTTP API.
+"""End-to-end measurement through the public HTTP API, behind the router.
 
-The engine that served the device-timed window is wrapped in the worker's
-OpenAI-compatible server (the same app ``python -m infera_b200.engine.worker``
-serves) on ``127.0.0.1:<port>``, and a separate load-generator process
-replays the trace against ``/v1/completions`` (streamed). Latencies are the
-client's wall clock; every engine iteration copies its packed inputs from
-pinned host memory and reads the sampled ids back, and those bytes are
-counted from the engine's copy counters over the timed slices.
+The same fleet shape as the reference arm: one worker per GPU, all behind
+one KV-aware router that discovers them through etcd (an in-memory etcd v3
+JSON-gateway server; no etcd binary exists here) and follows their KV
+events over ZMQ. Per rank:
+
+* the engine that served the device-timed window is wrapped in an
+  :class:`~infera_b200.engine.core_ipc.EngineCoreServer` whose step loop
+  runs on a thread of the benchmark process (the GPU owner), with its
+  prefix cache cleared first so the run starts cold like the reference's;
+* ``python -m infera_b200.engine.worker --attach-core`` serves the
+  OpenAI-compatible HTTP API for it in a separate process and registers it;
+* rank 0 also runs the router (``python -m infera_b200.server``) and the
+  etcd stand-in;
+* a separate load-generator process replays the trace - the same sessions
+  and seed as the reference arm - against the router's ``/v1/completions``
+  (streamed). Latencies are the client's wall clock.
+
+Every engine iteration copies its packed inputs from pinned host memory and
+reads the sampled ids back; those bytes are counted from the engine's copy
+counters over the run.
 """
 
 from __future__ import annotations
 
 import json
 import os
+import signal
 import subprocess
 import sys
 import threading
@@ -20,47 +34,124 @@ import time
 
 from infera_b200.bench.slo import SLO, ReqRecord, percentile, summarize
 
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+ETCD_PORT = 23890
+ROUTER_PORT = 28100
+WORKER_PORT0 = 29200
+EVENTS_PORT0 = 29300
 
-def _serve_in_thread(app, port: int):
-    import uvicorn
 
-    server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning",
-                                           access_log=False))
-    th = threading.Thread(target=server.run, name="e2e-http", daemon=True)
-    th.start()
+def _spawn(cmd, log_path, env=None):
+    f = open(log_path, "w")
+    e = dict(env or os.environ)
+    e["PYTHONPATH"] = os.pathsep.join([ROOT] + [p for p in e.get("PYTHONPATH", "").split(os.pathsep) if p])
+    return subprocess.Popen(cmd, stdout=f, stderr=subprocess.STDOUT, env=e, start_new_session=True)
+
+
+def _stop(p, sig=signal.SIGTERM, timeout=60.0):
+    if p is None or p.poll() is not None:
+        return
+    try:
+        os.killpg(p.pid, sig)
+        p.wait(timeout=timeout)
+    except Exception:
+        try:
+            os.killpg(p.pid, signal.SIGKILL)
+        except Exception:
+            pass
+
+
+def _wait_http(url: str, pred, timeout: float) -> bool:
+    import httpx
+
     t0 = time.time()
-    while not server.started and time.time() - t0 < 30:
-        time.sleep(0.05)
-    return server, th
+    while time.time() - t0 < timeout:
+        try:
+            r = httpx.get(url, timeout=5)
+            if r.status_code == 200 and pred(r):
+                return True
+        except Exception:
+            pass
+        time.sleep(0.5)
+    return False
 
 
-def run_e2e_on_engine(engine, *, model: str, rank: int, sessions: range, rate: float, warmup_s: float,
-                      timed_s: float, seed: int) -> dict:
-    from infera_b200.engine.async_engine import AsyncEngine
-    from infera_b200.engine.server import build_worker_app
-    from infera_b200.utils.tokenizer import load_tokenizer
+def router_cmd(backend: str) -> list[str]:
+    return [sys.executable, "-m", "infera_b200.server", "--discovery-backend", "etcd",
+            "--etcd-endpoint", f"127.0.0.1:{ETCD_PORT}", "--router-policy", "kv-aware",
+            "--router-backend", backend, "--host", "127.0.0.1", "--port", str(ROUTER_PORT),
+            "--log-level", "warning"]
 
-    port = 18100 + rank
-    aeng = AsyncEngine(engine)
-    aeng.start()
-    app = build_worker_app(aeng, load_tokenizer(None, vocab_size=engine.model_cfg.vocab), model)
-    server, th = _serve_in_thread(app, port)
-    h2d0, d2h0 = engine.runner.h2d_bytes, engine.runner.d2h_bytes
-    it0 = engine.num_steps
-    cmd = [sys.executable, "-m", "infera_b200.bench.http_loadgen", "--url", f"http://127.0.0.1:{port}",
-           "--model", model, "--sessions", f"{sessions.start}:{sessions.stop}", "--rate", str(rate),
-           "--duration", str(warmup_s + timed_s), "--seed", str(seed + 1000), "--drain-s", "0"]
-    env = dict(os.environ)
-    env["PYTHONPATH"] = os.pathsep.join([os.getcwd(), env.get("PYTHONPATH", "")])
-    out = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, env=env, timeout=warmup_s + timed_s + 300)
-    h2d, d2h = engine.runner.h2d_bytes - h2d0, engine.runner.d2h_bytes - d2h0
-    iters = engine.num_steps - it0
-    server.should_exit = True
-    th.join(timeout=10)
-    aeng.stop()
-    if out.returncode != 0:
-        raise RuntimeError(f"load generator failed: {out.stderr.decode()[-2000:]}")
-    res = json.loads(out.stdout)
+
+def run_e2e_fleet(engine, *, model: str, rank: int, world: int, barrier, sessions: range, rate: float,
+                  warmup_s: float, timed_s: float, seed: int, router_backend: str = "python",
+                  logdir: str | None = None, trace: str = "agentic-8b", drain_s: float = 0.0) -> dict:
+    """``barrier()`` synchronises the ranks (host-side)."""
+    from infera_b200.engine.core_ipc import EngineCoreServer, ipc_pair
+    from infera_b200.engine.kv_events import KvEventPublisher
+
+    logdir = logdir or (os.path.join(ROOT, "gpurun_out") if os.path.isdir(os.path.join(ROOT, "gpurun_out"))
+                        else "/tmp")
+    procs = []
+    th = None
+    stop = threading.Event()
+    worker = None
+    pub = None
+    try:
+        if rank == 0:
+            procs.append(_spawn([sys.executable, "-m", "infera_b200.common.etcd_fake", "--port", str(ETCD_PORT)],
+                                os.path.join(logdir, "e2e_etcd.log")))
+            _wait_http(f"http://127.0.0.1:{ETCD_PORT}/health", lambda r: True, 60)
+            procs.append(_spawn(router_cmd(router_backend), os.path.join(logdir, "e2e_router.log")))
+        barrier()
+        # cold start: nothing cached from the device-timed window
+        ev_ep = f"tcp://127.0.0.1:{EVENTS_PORT0 + rank}"
+        pub = KvEventPublisher(ev_ep)
+        engine.set_event_sink(pub)
+        engine.bm.clear_cache()
+        in_addr, out_addr = ipc_pair(f"r{rank}")
+        srv = EngineCoreServer(engine, in_addr, out_addr, publisher=pub)
+        th = threading.Thread(target=srv.run, kwargs={"should_stop": stop.is_set}, name="engine-core",
+                              daemon=True)
+        th.start()
+        port = WORKER_PORT0 + rank
+        worker = _spawn([sys.executable, "-m", "infera_b200.engine.worker", "--attach-core", f"{in_addr},{out_addr}",
+                         "--model", model, "--served-model-name", model, "--host", "127.0.0.1", "--port", str(port),
+                         "--etcd-endpoint", f"127.0.0.1:{ETCD_PORT}", "--kv-events-endpoint", ev_ep,
+                         "--page-size", str(engine.bm.page_size), "--log-level", "warning"],
+                        os.path.join(logdir, f"e2e_worker{rank}.log"))
+        if rank == 0:
+            ok = _wait_http(f"http://127.0.0.1:{ROUTER_PORT}/v1/workers",
+                            lambda r: len(r.json().get("workers", [])) >= world, 300)
+            if not ok:
+                raise RuntimeError("e2e: workers did not appear at the router")
+        barrier()
+        h2d0, d2h0 = engine.runner.h2d_bytes, engine.runner.d2h_bytes
+        it0 = engine.num_steps
+        cmd = [sys.executable, "-m", "infera_b200.bench.http_loadgen", "--url", f"http://127.0.0.1:{ROUTER_PORT}",
+               "--model", model, "--sessions", f"{sessions.start}:{sessions.stop}", "--rate", str(rate),
+               "--duration", str(warmup_s + timed_s), "--seed", str(seed), "--drain-s", str(drain_s),
+               "--trace", trace]
+        env = dict(os.environ)
+        env["PYTHONPATH"] = os.pathsep.join([ROOT, env.get("PYTHONPATH", "")])
+        out = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, env=env,
+                             timeout=warmup_s + timed_s + 300)
+        h2d, d2h = engine.runner.h2d_bytes - h2d0, engine.runner.d2h_bytes - d2h0
+        iters = engine.num_steps - it0
+        if out.returncode != 0:
+            raise RuntimeError(f"load generator failed: {out.stderr.decode()[-2000:]}")
+        res = json.loads(out.stdout)
+        barrier()
+    finally:
+        _stop(worker)
+        stop.set()
+        if th is not None:
+            th.join(timeout=120)
+        for p in reversed(procs):
+            _stop(p)
+        engine.set_event_sink(None)
+        if pub is not None:
+            pub.close()
     recs = []
     for r in res["records"]:
         rec = ReqRecord("", r["arrival"], prompt_len=r["prompt_len"], cached_len=r["cached_len"],
@@ -76,26 +167,28 @@ def run_e2e_on_engine(engine, *, model: str, rank: int, sessions: range, rate: f
     return {
         "window_s": timed_s, "slo_met": st["slo_met"], "completed": st["completed"],
         "ttfts": [r.ttft for r in done if r.ttft is not None], "itls": [x for r in done for x in r.itls()],
-        "errors": res["errors"],
+        "errors": res["errors"], "prefix_hit_rate": st["prefix_hit_rate"],
         # copies happen every engine iteration; report them per benchmark step (1 s slice)
         "h2d_per_step": h2d / total, "d2h_per_step": d2h / total, "iterations": iters,
     }
 
 
-def aggregate(allr: list[dict]) -> dict:
+def aggregate(allr: list[dict], path: str) -> dict:
     win = max(r["window_s"] for r in allr)
     ttfts = [x for r in allr for x in r["ttfts"]]
     itls = [x for r in allr for x in r["itls"]]
     return {
         "value": round(sum(r["slo_met"] for r in allr) / win, 4),
         "unit": "req/s",
-        "path": "OpenAI /v1/completions over HTTP (streamed), client wall clock",
+        "path": path,
         "completed": sum(r["completed"] for r in allr),
         "slo_met": sum(r["slo_met"] for r in allr),
         "ttft_p50_s": round(percentile(ttfts, 50), 4),
         "ttft_p99_s": round(percentile(ttfts, 99), 4),
+        "itl_p50_ms": round(1000 * percentile(itls, 50), 3),
         "itl_p99_ms": round(1000 * percentile(itls, 99), 3),
         "errors": sum(r["errors"] for r in allr),
+        "prefix_hit_rate": round(sum(r.get("prefix_hit_rate", 0.0) for r in allr) / len(allr), 4),
         "h2d_bytes_per_step": int(sum(r["h2d_per_step"] for r in allr)),
         "d2h_bytes_per_step": int(sum(r["d2h_per_step"] for r in allr)),
     }

@@ -175,7 +175,7 @@ def run_reference(args) -> dict:
             dist.all_gather_object(allr, local_res)
         if rank != 0:
             return {}
-        agg = aggregate(allr)
+        agg = aggregate(allr, "reference router /v1/completions over HTTP (streamed), client wall clock")
         return {
             "metric": "goodput req/s within p99 TTFT/ITL SLO on synthetic agentic trace; p50 TTFT",
             "value": agg["value"], "unit": "req/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,

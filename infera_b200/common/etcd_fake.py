@@ -147,6 +147,10 @@ def build_app(state: EtcdState | None = None) -> FastAPI:
     app = FastAPI()
     app.state.etcd = st
 
+    @app.get("/health")
+    async def health():
+        return {"health": "true"}
+
     @app.post("/v3/kv/range")
     async def kv_range(req: Request):
         body = await req.json()

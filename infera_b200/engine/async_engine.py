@@ -157,3 +157,34 @@ class AsyncEngine:
         s["draining"] = self.draining
         s["errors"] = self.errors
         return s
+
+    async def stats_async(self) -> dict:
+        return self.stats()
+
+    async def kv_snapshot(self) -> dict:
+        bm = self.engine.bm
+        return {"block_size": bm.page_size, "block_hashes": [str(h) for h in bm.cached_hashes()], "ts": time.time()}
+
+    async def start_profile(self) -> dict:
+        import torch
+
+        if self.profiler is not None:
+            return {"error": "already profiling"}
+        acts = [torch.profiler.ProfilerActivity.CPU]
+        if torch.cuda.is_available():
+            acts.append(torch.profiler.ProfilerActivity.CUDA)
+        self.profiler = torch.profiler.profile(activities=acts, record_shapes=False)
+        self.profiler.__enter__()
+        return {"status": "started"}
+
+    async def stop_profile(self) -> dict:
+        if self.profiler is None:
+            return {"error": "not profiling"}
+        p, self.profiler = self.profiler, None
+        p.__exit__(None, None, None)
+        path = f"/tmp/infera_b200_profile_{int(time.time())}.json"
+        try:
+            p.export_chrome_trace(path)
+        except Exception as e:
+            return {"status": "stopped", "error": str(e)}
+        return {"status": "stopped", "trace": path}

@@ -23,7 +23,7 @@ import uuid
 from fastapi import FastAPI, Request
 from fastapi.responses import JSONResponse, Response, StreamingResponse
 
-from infera_b200.engine.async_engine import HANDBACK, AsyncEngine
+from infera_b200.engine.async_engine import HANDBACK
 from infera_b200.engine.request import SamplingParams
 from infera_b200.router.transport import DRAINING_NOTICE
 from infera_b200.utils.tokenizer import request_token_ids
@@ -43,7 +43,7 @@ def _sse(obj: dict) -> bytes:
     return b"data: " + json.dumps(obj, separators=(",", ":")).encode() + b"\n\n"
 
 
-def build_worker_app(aeng: AsyncEngine, tokenizer, model_name: str, extra_metrics=None) -> FastAPI:
+def build_worker_app(aeng, tokenizer, model_name: str, extra_metrics=None) -> FastAPI:
     app = FastAPI(title="infera-b200 worker")
     app.state.aeng = aeng
 
@@ -157,7 +157,7 @@ def build_worker_app(aeng: AsyncEngine, tokenizer, model_name: str, extra_metric
 
     @app.get("/metrics")
     async def metrics():
-        s = aeng.stats()
+        s = await aeng.stats_async()
         lines = []
 
         def g(name, v, help_):
@@ -180,34 +180,16 @@ def build_worker_app(aeng: AsyncEngine, tokenizer, model_name: str, extra_metric
 
     @app.get("/v1/kv-snapshot")
     async def kv_snapshot():
-        eng = aeng.engine
-        return {"block_size": eng.bm.page_size, "block_hashes": [str(h) for h in eng.bm.cached_hashes()],
-                "ts": time.time()}
+        return await aeng.kv_snapshot()
 
     @app.post("/start_profile")
     async def start_profile(request: Request):
-        import torch
-
-        if aeng.profiler is not None:
-            return JSONResponse({"error": "already profiling"}, status_code=409)
-        acts = [torch.profiler.ProfilerActivity.CPU]
-        if torch.cuda.is_available():
-            acts.append(torch.profiler.ProfilerActivity.CUDA)
-        aeng.profiler = torch.profiler.profile(activities=acts, record_shapes=False)
-        aeng.profiler.__enter__()
-        return {"status": "started"}
+        res = await aeng.start_profile()
+        return JSONResponse(res, status_code=409 if "error" in res else 200)
 
     @app.post("/stop_profile")
     async def stop_profile(request: Request):
-        if aeng.profiler is None:
-            return JSONResponse({"error": "not profiling"}, status_code=409)
-        p, aeng.profiler = aeng.profiler, None
-        p.__exit__(None, None, None)
-        path = f"/tmp/infera_b200_profile_{int(time.time())}.json"
-        try:
-            p.export_chrome_trace(path)
-        except Exception as e:
-            return {"status": "stopped", "error": str(e)}
-        return {"status": "stopped", "trace": path}
+        res = await aeng.stop_profile()
+        return JSONResponse(res, status_code=409 if res.get("error") == "not profiling" else 200)
 
     return app

@@ -4,8 +4,10 @@ worker.
 Lifecycle (``infera/engine/vllm/__main__.py:142-405``, for this framework's
 own engine):
 
-1. build the engine on the GPU, the KV-event publisher (ZMQ PUB) and the
-   worker HTTP app;
+1. start the engine core (by default a child process that owns the GPU, the
+   KV-event publisher and the step loop, reached over ZMQ IPC; or an
+   already-running core given by ``--attach-core``; or, with
+   ``--in-process``, a thread of this process) and the worker HTTP app;
 2. serve HTTP, then register (etcd lease + heartbeat, or the in-process
    registry) with a record carrying the KV metadata (block size, tokenizer
    digest and canary, events endpoint);
@@ -69,28 +71,108 @@ def parse_args(argv=None):
     p.add_argument("--drain-timeout", type=float, default=30.0)
     p.add_argument("--handback-after", type=float, default=None)
     p.add_argument("--tokenizer", default=None)
+    p.add_argument("--kv-tier", default=None, help="host:<GiB>[:<nvme dir>] or kvd:<socket>")
+    p.add_argument("--in-process", action="store_true", help="run the engine on a thread of this process")
+    p.add_argument("--attach-core", default=None, help="IN,OUT ipc addresses of a running engine core")
     p.add_argument("--log-level", default="info")
     return p.parse_args(argv)
+
+
+def _core_cmd(args, in_addr: str, out_addr: str) -> list[str]:
+    import sys
+
+    cmd = [sys.executable, "-m", "infera_b200.engine.core_ipc", "--in", in_addr, "--out", out_addr,
+           "--model", args.model, "--device", args.device, "--page-size", str(args.page_size),
+           "--max-num-seqs", str(args.max_num_seqs), "--max-batched-tokens", str(args.max_batched_tokens),
+           "--gpu-memory-utilization", str(args.gpu_memory_utilization), "--seed", str(args.seed)]
+    if args.num_pages:
+        cmd += ["--num-pages", str(args.num_pages)]
+    if args.no_cuda_graphs:
+        cmd.append("--no-cuda-graphs")
+    if args.kv_events_endpoint:
+        cmd += ["--kv-events-endpoint", args.kv_events_endpoint]
+    if args.kv_tier:
+        cmd += ["--kv-tier", args.kv_tier]
+    return cmd
+
+
+async def start_engine(args):
+    """Returns (serving engine, vocab size, shutdown coroutine factory)."""
+    if args.in_process:
+        from infera_b200.engine.async_engine import AsyncEngine
+        from infera_b200.engine.kv_events import KvEventPublisher
+        from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
+
+        pub = KvEventPublisher(args.kv_events_endpoint) if args.kv_events_endpoint else None
+        ecfg = EngineConfig(model=args.model, page_size=args.page_size, max_num_seqs=args.max_num_seqs,
+                            max_batched_tokens=args.max_batched_tokens,
+                            gpu_memory_utilization=args.gpu_memory_utilization, num_pages=args.num_pages,
+                            use_cuda_graphs=not args.no_cuda_graphs, seed=args.seed, kv_tier=args.kv_tier)
+        eng = LLMEngine(ecfg, device=args.device, event_sink=pub)
+        aeng = AsyncEngine(eng)
+        aeng.start()
+        flusher = asyncio.create_task(_flush_loop(pub)) if pub else None
+
+        async def shutdown():
+            aeng.stop()
+            if flusher is not None:
+                flusher.cancel()
+            if pub is not None:
+                pub.close()
+
+        return aeng, eng.model_cfg.vocab, shutdown
+    import subprocess
+
+    from infera_b200.engine.core_ipc import EngineCoreClient, ipc_pair
+
+    proc = None
+    if args.attach_core:
+        in_addr, out_addr = args.attach_core.split(",")
+        client = EngineCoreClient(in_addr, out_addr)
+        await client.call("ping", timeout=60.0)
+        st = await client.call("stats")
+        info = {"vocab": None, "num_pages": st.get("num_pages")}
+        client.mark_ready(info)
+    else:
+        in_addr, out_addr = ipc_pair()
+        client = EngineCoreClient(in_addr, out_addr)
+        client._ensure_started()
+        proc = subprocess.Popen(_core_cmd(args, in_addr, out_addr))
+        while True:
+            try:
+                info = await client.wait_ready(timeout=5.0)
+                break
+            except asyncio.TimeoutError:
+                if proc.poll() is not None:
+                    raise RuntimeError(f"engine core exited with code {proc.returncode}")
+
+    async def shutdown():
+        if proc is not None:
+            await client.shutdown()
+            for _ in range(300):
+                if proc.poll() is not None:
+                    break
+                await asyncio.sleep(0.1)
+            if proc.poll() is None:
+                proc.terminate()
+        client.stop()
+
+    vocab = info.get("vocab")
+    if vocab is None:
+        from infera_b200.models.config import get_config
+
+        vocab = get_config(args.model).vocab
+    return client, vocab, shutdown
 
 
 async def run_worker(args) -> None:
     import uvicorn
 
-    from infera_b200.engine.async_engine import AsyncEngine
-    from infera_b200.engine.kv_events import KvEventPublisher
-    from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
     from infera_b200.engine.server import build_worker_app
     from infera_b200.utils.tokenizer import load_tokenizer
 
-    pub = KvEventPublisher(args.kv_events_endpoint) if args.kv_events_endpoint else None
-    ecfg = EngineConfig(model=args.model, page_size=args.page_size, max_num_seqs=args.max_num_seqs,
-                        max_batched_tokens=args.max_batched_tokens,
-                        gpu_memory_utilization=args.gpu_memory_utilization, num_pages=args.num_pages,
-                        use_cuda_graphs=not args.no_cuda_graphs, seed=args.seed)
-    eng = LLMEngine(ecfg, device=args.device, event_sink=pub)
-    tok = load_tokenizer(args.tokenizer, vocab_size=eng.model_cfg.vocab)
-    aeng = AsyncEngine(eng)
-    aeng.start()
+    aeng, vocab, shutdown_engine = await start_engine(args)
+    tok = load_tokenizer(args.tokenizer, vocab_size=vocab)
     app = build_worker_app(aeng, tok, args.served_model_name or args.model)
     server = uvicorn.Server(uvicorn.Config(app, host=args.host, port=args.port, log_level="warning",
                                            access_log=False))
@@ -111,7 +193,6 @@ async def run_worker(args) -> None:
     loop = asyncio.get_running_loop()
     for sig in (signal.SIGTERM, signal.SIGINT):
         loop.add_signal_handler(sig, stop.set)
-    flusher = asyncio.create_task(_flush_loop(pub)) if pub else None
     await stop.wait()
     # shutdown: heartbeat off -> deregister -> drain -> stop
     if hb is not None:
@@ -120,11 +201,7 @@ async def run_worker(args) -> None:
         await reg.deregister()
     clean = await aeng.drain(args.drain_timeout, args.handback_after)
     logger.info("drain %s (inflight=%d)", "clean" if clean else "timed out", aeng.inflight)
-    aeng.stop()
-    if flusher is not None:
-        flusher.cancel()
-    if pub is not None:
-        pub.close()
+    await shutdown_engine()
     server.should_exit = True
     await serve_task
     if reg is not None:
