@@ -111,10 +111,11 @@ class MockWorker:
 
 async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 60.0, drain_at: float | None = 30.0,
                     sessions: int = 64, policy: str = "kv-aware", seed: int = 0, trace: str = "router-plumbing",
-                    decode_ms: float = 10.0, prefill_ms: float = 0.05) -> dict:
+                    decode_ms: float = 10.0, prefill_ms: float = 0.05, router_backend: str = "python") -> dict:
+    """``router_backend``: "python" (the router stack in this process) or
+    "native" (the C++ router binary as a child process)."""
     from types import SimpleNamespace
 
-    from infera_b200.bench.http_loadgen import run as loadgen
     from infera_b200.common.etcd_fake import build_app as etcd_app
     from infera_b200.server.__main__ import build_router_stack
     from infera_b200.server.app import build_app
@@ -125,20 +126,78 @@ async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 6
     ws = [MockWorker(i, etcd_url, model, decode_ms=decode_ms, prefill_ms=prefill_ms) for i in range(workers)]
     for w in ws:
         await w.start()
-    args = SimpleNamespace(router_policy=policy, router_tokenizer_path=None, kv_overlap_weight=1.0,
-                           kv_prefill_overlap_weight=None, kv_decode_overlap_weight=None,
-                           breaker_failure_threshold=3, breaker_cooldown_s=5.0, breaker_max_cooldown_s=60.0,
-                           discovery_backend="etcd", etcd_endpoint=etcd_url, etcd_prefix="/infera/workers/",
-                           request_max_retries=1, migration_limit=0, router_mode="auto", enable_profiling=True,
-                           enable_scaling_api=False, scaling_deployment=None, kvd_socket_path=None, block_size=16,
-                           k8s_label_selector=None, k8s_namespace=None)
-    state = build_router_stack(args)
-    app = build_app(state)
-    app.router.on_startup.append(state.registry.start)
-    router = ServerThread(app, free_port()).start()
-    router_url = f"http://127.0.0.1:{router.port}"
+    native = None
+    state = None
+    if router_backend == "native":
+        import subprocess
+
+        from infera_b200.server.launch_native import router_binary
+
+        rport = free_port()
+        native = subprocess.Popen([router_binary(), "--port", str(rport), "--host", "127.0.0.1",
+                                   "--discovery-backend", "etcd", "--etcd-endpoint", etcd_url,
+                                   "--router-policy", policy, "--log-level", "warning"],
+                                  stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL, start_new_session=True)
+        router_url = f"http://127.0.0.1:{rport}"
+    else:
+        args = SimpleNamespace(router_policy=policy, router_tokenizer_path=None, kv_overlap_weight=1.0,
+                               kv_prefill_overlap_weight=None, kv_decode_overlap_weight=None,
+                               breaker_failure_threshold=3, breaker_cooldown_s=5.0, breaker_max_cooldown_s=60.0,
+                               discovery_backend="etcd", etcd_endpoint=etcd_url, etcd_prefix="/infera/workers/",
+                               request_max_retries=1, migration_limit=0, router_mode="auto", enable_profiling=True,
+                               enable_scaling_api=False, scaling_deployment=None, kvd_socket_path=None, block_size=16,
+                               k8s_label_selector=None, k8s_namespace=None)
+        state = build_router_stack(args)
+        app = build_app(state)
+        app.router.on_startup.append(state.registry.start)
+        router = ServerThread(app, free_port()).start()
+        router_url = f"http://127.0.0.1:{router.port}"
+
+    import httpx
+
+    async def listed() -> list[str]:
+        if state is not None:
+            return [w.worker_id for w in state.registry.pool.list_active()]
+        try:
+            async with httpx.AsyncClient() as c:
+                r = await c.get(router_url + "/v1/workers", timeout=2)
+            return [w["worker_id"] for w in r.json()["workers"] if w.get("status", "active") == "active"]
+        except Exception:
+            return []
+
+    async def view_size(wid: str) -> int:
+        if state is not None:
+            return len(state.policy.kv_client.cache_view(wid))
+        async with httpx.AsyncClient() as c:
+            r = await c.get(router_url + f"/v1/admin/cache-view/{wid}", timeout=5)
+        return int(r.json().get("num_blocks", 0)) if r.status_code == 200 else 0
+
+    try:
+        return await _drive(ws, listed, view_size, router_url, workers, drain_at, trace, sessions, rate, duration, seed,
+                            model, policy)
+    finally:
+        if native is not None:
+            native.terminate()
+            try:
+                native.wait(timeout=10)
+            except Exception:
+                native.kill()
+        else:
+            router.stop()
+        for w in ws:
+            if w.server.thread.is_alive():
+                await w.shutdown(drain_timeout=5)
+        if state is not None:
+            await state.registry.stop()
+        etcd.stop()
+
+
+async def _drive(ws, listed, view_size, router_url, workers, drain_at, trace, sessions, rate, duration, seed, model,
+                 policy) -> dict:
+    from infera_b200.bench.http_loadgen import run as loadgen
+
     t_wait = time.time()
-    while len(state.registry.pool.list_active()) < workers and time.time() - t_wait < 10:
+    while len(await listed()) < workers and time.time() - t_wait < 15:
         await asyncio.sleep(0.05)
     drain_info = {}
 
@@ -147,8 +206,12 @@ async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 6
         t0 = time.monotonic()
         victim = ws[-1]
         info = await victim.shutdown()
-        # time until the router no longer lists the victim
-        info["router_removed"] = victim.info.worker_id not in [w.worker_id for w in state.registry.pool.all()]
+        # the router no longer lists the victim
+        t1 = time.monotonic()
+        while victim.info.worker_id in await listed() and time.monotonic() - t1 < 2.0:
+            await asyncio.sleep(0.005)
+        info["router_removed"] = victim.info.worker_id not in await listed()
+        info["router_reaction_s"] = time.monotonic() - t1
         info["t"] = time.monotonic() - t0
         drain_info.update(info)
 
@@ -161,19 +224,13 @@ async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 6
     prompt = sum(r["prompt_len"] for r in recs)
     cached = sum(r["cached_len"] for r in recs)
     split = {w.info.worker_id: w.eng.stats["requests"] for w in ws}
-    view = {wid: len(state.policy.kv_client.cache_view(wid)) for wid in split} if policy == "kv-aware" else {}
+    view = {wid: await view_size(wid) for wid in split} if policy == "kv-aware" else {}
     out = {
         "requests": len(res["records"]), "completed": len(recs), "errors": res["errors"],
         "prefix_hit_rate": cached / max(1, prompt),
         "ttft_p50_ms": 1000 * percentile(ttfts, 50), "ttft_p99_ms": 1000 * percentile(ttfts, 99),
         "per_worker_requests": split, "router_view_blocks": view, "drain": drain_info,
     }
-    router.stop()
-    for w in ws:
-        if w.server.thread.is_alive():
-            await w.shutdown(drain_timeout=5)
-    await state.registry.stop()
-    etcd.stop()
     return out
 
 
@@ -185,9 +242,10 @@ def main(argv=None) -> None:
     ap.add_argument("--drain-at", type=float, default=30.0)
     ap.add_argument("--sessions", type=int, default=64)
     ap.add_argument("--policy", default="kv-aware")
+    ap.add_argument("--router-backend", choices=("python", "native"), default="python")
     a = ap.parse_args(argv)
     res = asyncio.run(run_fleet(workers=a.workers, rate=a.rate, duration=a.duration, drain_at=a.drain_at,
-                                sessions=a.sessions, policy=a.policy))
+                                sessions=a.sessions, policy=a.policy, router_backend=a.router_backend))
     print(json.dumps(res, indent=1))
 
 

@@ -95,6 +95,24 @@ def build_runtime() -> Path | None:
     return RUNTIME_SO
 
 
+def xxhash_include() -> Path:
+    """Directory holding the reference xxHash header (BSD-2-Clause), which
+    the native code includes for XXH3-64: bit-exact with the Python
+    ``xxhash`` package by construction. pyarrow vendors a copy."""
+    cands = [os.environ.get("XXHASH_INCLUDE")]
+    try:
+        import pyarrow
+
+        cands.append(os.path.join(pyarrow.get_include(), "arrow", "vendored", "xxhash"))
+    except Exception:
+        pass
+    cands += ["/usr/include", "/usr/local/include"]
+    for c in cands:
+        if c and (Path(c) / "xxhash.h").exists():
+            return Path(c)
+    raise RuntimeError("xxhash.h not found (set XXHASH_INCLUDE)")
+
+
 def build_router() -> Path | None:
     sources = sorted(ROUTER_SRC.glob("*.cpp")) if ROUTER_SRC.exists() else []
     if not sources:
@@ -102,8 +120,19 @@ def build_router() -> Path | None:
     headers = sorted(ROUTER_SRC.glob("*.h")) + sorted(RUNTIME_SRC.glob("*.h"))
     if _newer([*sources, *headers], ROUTER_BIN):
         LIB.mkdir(parents=True, exist_ok=True)
-        _run(["g++", "-O2", "-std=c++17", "-I", str(RUNTIME_SRC), "-o", str(ROUTER_BIN), *map(str, sources),
-              "-lpthread"])
+        objs = []
+        todo = []
+        for src in sources:
+            obj = OBJ / ("router_" + src.stem + ".o")
+            objs.append(obj)
+            if _newer([src, *headers], obj):
+                todo.append(["g++", "-O2", "-std=c++17", "-Wall", "-I", str(ROUTER_SRC), "-I", str(xxhash_include()),
+                             "-c", str(src), "-o", str(obj)])
+        OBJ.mkdir(parents=True, exist_ok=True)
+        if todo:
+            with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
+                list(ex.map(_run, todo))
+        _run(["g++", "-o", str(ROUTER_BIN), *map(str, objs), "-lpthread"])
     return ROUTER_BIN
 
 

@@ -1,0 +1,170 @@
+"""The C++ router (``infera_b200/lib/ib200_router``) against mock workers:
+bit-exact block hashing, KV-aware routing from ZMQ events and drain over
+etcd, failover, PD body shaping, and the HTTP routes. Mirrors the
+reference's Rust router tests (mock upstream workers plus the real app,
+``rust/router/tests/functional.rs:35-50``; ZMQ event replay,
+``rust/router/tests/kv_event_zmq.rs``)."""
+
+import asyncio
+import json
+import os
+import subprocess
+import time
+
+import httpx
+import pytest
+from fastapi import FastAPI, Request
+from fastapi.responses import JSONResponse, StreamingResponse
+
+from infera_b200.bench.fleet import MockWorker, ServerThread, free_port, run_fleet
+from infera_b200.common.etcd_fake import build_app as etcd_app
+from infera_b200.server.launch_native import native_argv, router_binary
+from infera_b200.utils.hashing import chain_hashes
+
+
+@pytest.fixture(scope="module")
+def binary():
+    return router_binary()
+
+
+def _start_router(binary, *args):
+    port = free_port()
+    p = subprocess.Popen([binary, "--port", str(port), "--host", "127.0.0.1", *args], stdout=subprocess.DEVNULL,
+                         stderr=subprocess.DEVNULL, start_new_session=True)
+    url = f"http://127.0.0.1:{port}"
+    t0 = time.time()
+    while time.time() - t0 < 10:
+        try:
+            if httpx.get(url + "/health", timeout=1).status_code == 200:
+                return p, url
+        except httpx.HTTPError:
+            time.sleep(0.05)
+    p.kill()
+    raise RuntimeError("native router did not start")
+
+
+def _stop(p):
+    p.terminate()
+    try:
+        p.wait(timeout=10)
+    except subprocess.TimeoutExpired:
+        p.kill()
+
+
+@pytest.mark.parametrize("bs", [4, 16, 32, 64])
+def test_chain_hashes_bit_exact(binary, bs):
+    ids = [(i * 7919 + 13) % 128256 for i in range(bs * 9 + 3)]
+    out = subprocess.run([binary, "--print-chain-hashes", str(bs)], input=" ".join(map(str, ids)).encode(),
+                         stdout=subprocess.PIPE, timeout=30, check=True).stdout.decode().split()
+    assert [int(x) for x in out] == chain_hashes(ids, bs)
+
+
+def test_native_fleet_kv_routing_and_drain():
+    res = asyncio.run(run_fleet(workers=3, rate=12.0, duration=8.0, drain_at=4.0, sessions=12, decode_ms=2.0,
+                                router_backend="native"))
+    assert res["errors"] == 0
+    assert res["completed"] >= 40
+    assert res["drain"]["drained"] and res["drain"]["router_removed"]
+    assert res["prefix_hit_rate"] > 0.5
+    assert sum(v > 0 for v in res["router_view_blocks"].values()) >= 2
+
+
+def _records_file(tmp_path, workers):
+    f = tmp_path / "workers.json"
+    f.write_text(json.dumps(workers))
+    return str(f)
+
+
+def test_failover_and_routes(binary, tmp_path):
+    async def go():
+        etcd = ServerThread(etcd_app(), free_port()).start()
+        etcd_url = f"http://127.0.0.1:{etcd.port}"
+        ws = [MockWorker(i, etcd_url, "m", decode_ms=1.0) for i in range(2)]
+        for w in ws:
+            await w.start()
+        p, url = _start_router(binary, "--etcd-endpoint", etcd_url, "--request-max-retries", "1")
+        try:
+            t0 = time.time()
+            while len(httpx.get(url + "/v1/workers").json()["workers"]) < 2 and time.time() - t0 < 10:
+                await asyncio.sleep(0.05)
+            ws[0].eng.fail_next = 100
+            ws[1].eng.fail_next = 0
+            body = {"model": "m", "prompt": list(range(64)), "max_tokens": 4, "ignore_eos": True}
+            async with httpx.AsyncClient(timeout=20) as c:
+                outs = [await c.post(url + "/v1/completions", json=dict(body, stream=(i % 2 == 0))) for i in range(6)]
+                models = (await c.get(url + "/v1/models")).json()
+                metrics = (await c.get(url + "/metrics")).text
+                missing = await c.get(url + "/v1/nope")
+                bad = await c.post(url + "/v1/completions", content=b"{not json")
+            return outs, models, metrics, missing, bad
+        finally:
+            _stop(p)
+            for w in ws:
+                await w.shutdown(drain_timeout=2)
+            etcd.stop()
+
+    outs, models, metrics, missing, bad = asyncio.run(go())
+    assert all(r.status_code == 200 for r in outs)
+    assert all(r.headers.get("x-infera-request-id") for r in outs)
+    assert any(b"[DONE]" in r.content for r in outs)
+    assert models["data"][0]["id"] == "m"
+    assert 'infera_requests_total{router="native",outcome="ok"} 6' in metrics
+    assert "infera_router_failovers_total" in metrics
+    assert missing.status_code == 404 and bad.status_code == 400
+
+
+def _pd_app(role: str, seen: list):
+    app = FastAPI()
+
+    @app.post("/v1/completions")
+    async def completions(request: Request):
+        body = await request.json()
+        seen.append(body)
+        if role == "prefill":
+            return JSONResponse({"choices": [{"text": "x", "finish_reason": "length"}]})
+
+        async def gen():
+            for _ in range(3):
+                yield b'data: {"choices":[{"text":"y","finish_reason":null}]}\n\n'
+            yield b"data: [DONE]\n\n"
+
+        return StreamingResponse(gen(), media_type="text/event-stream")
+
+    return app
+
+
+def test_pd_nvlink_push_shaping(binary, tmp_path):
+    pseen, dseen = [], []
+    ps = ServerThread(_pd_app("prefill", pseen), free_port()).start()
+    ds = ServerThread(_pd_app("decode", dseen), free_port()).start()
+    meta = {"protocol": "b200-nvlink-push", "params": {"kv_endpoint": "ipc://decode-pool"}}
+    recs = [{"worker_id": "p0", "url": f"http://127.0.0.1:{ps.port}", "model_name": "m", "disagg_mode": "prefill",
+             "disagg_meta": meta, "kv_block_size": 16},
+            {"worker_id": "d0", "url": f"http://127.0.0.1:{ds.port}", "model_name": "m", "disagg_mode": "decode",
+             "disagg_meta": meta, "kv_block_size": 16}]
+    p, url = _start_router(binary, "--discovery-backend", "static", "--static-workers", _records_file(tmp_path, recs))
+    try:
+        r = httpx.post(url + "/v1/completions", json={"model": "m", "prompt": [1, 2, 3], "max_tokens": 10,
+                                                      "stream": True}, timeout=20)
+        direct = httpx.post(url + "/v1/completions", json={"model": "m", "prompt": [1], "max_tokens": 2},
+                            headers={"x-worker-instance-id": "d0"}, timeout=20)
+    finally:
+        _stop(p)
+        ps.stop()
+        ds.stop()
+    assert r.status_code == 200 and r.content.count(b'"y"') == 3 and b"[DONE]" in r.content
+    pb, db = pseen[0], dseen[0]
+    assert pb["max_tokens"] == 1 and pb["stream"] is False
+    assert pb["kv_transfer_params"]["do_remote_decode"] is True
+    assert pb["kv_transfer_params"]["decode_kv_endpoint"] == "ipc://decode-pool"
+    assert db["max_tokens"] == 9 and db["stream"] is True
+    assert db["kv_transfer_params"]["room"] == pb["kv_transfer_params"]["room"]
+    assert db["kv_transfer_params"]["infera_retention"] == "long"
+    # auto mode ignores gateway headers: that request was routed as a PD pair too
+    assert direct.status_code == 200 and len(pseen) == 2
+
+
+def test_launcher_strips_python_only_flags():
+    argv = ["--router-backend", "native", "--enable-profiling", "--kvd-socket-path", "/tmp/x", "--port", "9"]
+    assert native_argv(argv) == ["--router-backend", "native", "--port", "9"]
+    assert os.path.exists(router_binary())
