@@ -66,7 +66,8 @@ def parse_args(argv=None):
     ap.add_argument("--max-num-seqs", type=int, default=128)
     ap.add_argument("--max-batched-tokens", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--router-backend", choices=("python", "native"), default="python")
+    ap.add_argument("--router-backend", choices=("python", "native"), default="native",
+                    help="router in front of the e2e fleet: the C++ data plane (default) or the Python one")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
