@@ -1,0 +1,137 @@
+"""Row-parallel GEMM + all-reduce + residual add + RMSNorm across a
+tensor-parallel group: the fused NVLink path against the NCCL baseline.
+
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
+        -m infera_b200.bench.tp_comm_bench [--rows 64] [--hidden 8192] [--k-total 8192]
+
+Each rank holds a K-slice of the weight (``k_total / N`` columns) and of the
+activations; the full product is the sum over ranks. Checks both paths
+against a single-GPU fp32 computation of the whole problem, then times
+each (CUDA events on the launching stream, warm-up first, max over ranks)
+and prints one JSON line per row count on rank 0. The roofline for the
+fused path is the slower of the GEMM's FLOPs at the measured bf16 peak and
+the bytes each rank must push over NVLink at 770 GB/s and the weight
+bytes at the measured HBM copy bandwidth (small row counts are
+weight-bandwidth bound). Timed loops are captured in CUDA graphs.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+from infera_b200.ops import kernels as K
+from infera_b200.parallel.comm import TPComm
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--rows", default="1,16,64,128,256")
+    ap.add_argument("--hidden", type=int, default=8192)
+    ap.add_argument("--k-total", type=int, default=8192)
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--check-only", action="store_true")
+    a = ap.parse_args(argv)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    nccl = gloo = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        nccl = dist.group.WORLD
+        gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=120))
+    H, KT = a.hidden, a.k_total
+    Ks = KT // world
+    rows = [int(r) for r in a.rows.split(",")]
+    comm = TPComm(rank, world, dev, H, max_rows=max(rows), nccl_group=nccl, gloo_group=gloo)
+    g = torch.Generator(device=dev).manual_seed(1234)  # same full tensors on every rank
+    worst = 0.0
+    results = []
+    for M in rows:
+        x_full = (torch.randn(M, KT, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        w_full = (torch.randn(H, KT, device=dev, generator=g) / KT ** 0.5).to(torch.bfloat16)
+        h0 = torch.randn(M, H, device=dev, generator=g).to(torch.bfloat16)
+        nw = (1.0 + 0.1 * torch.randn(H, device=dev, generator=g)).to(torch.bfloat16)
+        xs = x_full[:, rank * Ks:(rank + 1) * Ks].contiguous()
+        ws = w_full[:, rank * Ks:(rank + 1) * Ks].contiguous()
+        ref_h = (h0.float() + x_full.float() @ w_full.float().t()).to(torch.bfloat16)
+        ref_x = (ref_h.float() * torch.rsqrt(ref_h.float().pow(2).mean(-1, keepdim=True) + 1e-5) * nw.float())
+        out = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+        for parity in (0, 1, 0, 1):  # alternate like the layers do
+            h = h0.clone()
+            comm.gemm_allreduce_add_rmsnorm(xs, ws, h, nw, 1e-5, out, parity)
+        torch.cuda.synchronize()
+        err = float((out.float() - ref_x).norm() / ref_x.norm())
+        herr = float((h.float() - ref_h.float()).norm() / ref_h.float().norm())
+        # NCCL baseline on the same problem
+        base = TPComm(rank, world, dev, H, max_rows=max(rows), nccl_group=nccl, gloo_group=gloo, fused=False)
+        hb = h0.clone()
+        outb = torch.empty_like(out)
+        base.gemm_allreduce_add_rmsnorm(xs, ws, hb, nw, 1e-5, outb, 0)
+        torch.cuda.synchronize()
+        errb = float((outb.float() - ref_x).norm() / ref_x.norm())
+        status = K.scratch(dev).read_status()
+        worst = max(worst, err, errb)
+        res = {"rows": M, "hidden": H, "k_per_rank": Ks, "world": world, "rel_err_fused": err,
+               "rel_err_residual": herr, "rel_err_nccl": errb, "status": status}
+        if not a.check_only:
+            # rotate weight copies totalling > 256 MB so every launch reads HBM, not L2
+            nrep = max(1, -(-(256 << 20) // (H * Ks * 2)))
+            wl = [ws] + [ws.clone() for _ in range(nrep - 1)]
+            for name, c in (("fused", comm), ("nccl", base)):
+                hh = h0.clone()
+                for i in range(4):
+                    c.gemm_allreduce_add_rmsnorm(xs, ws, hh, nw, 1e-5, out, i & 1)
+                torch.cuda.synchronize()
+                # capture the loop in a CUDA graph: device time, not the
+                # host's launch rate
+                gr = torch.cuda.CUDAGraph()
+                st = torch.cuda.Stream()
+                st.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(st):
+                    with torch.cuda.graph(gr, stream=st):
+                        for i in range(a.iters):
+                            c.gemm_allreduce_add_rmsnorm(xs, wl[i % nrep], hh, nw, 1e-5, out, i & 1)
+                torch.cuda.current_stream().wait_stream(st)
+                torch.cuda.synchronize()
+                gr.replay()  # warm
+                torch.cuda.synchronize()
+                if world > 1:
+                    dist.barrier(group=gloo)
+                s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+                s.record()
+                gr.replay()
+                e.record()
+                torch.cuda.synchronize()
+                us = s.elapsed_time(e) * 1000 / a.iters
+                del gr
+                t = torch.tensor([us], device=dev)
+                if world > 1:
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=nccl)
+                res[f"us_{name}"] = round(float(t.item()), 2)
+            flops = 2.0 * M * H * Ks
+            w_bytes = H * Ks * 2
+            push_bytes = (world - 1) * M * H * 2
+            res["roofline_us"] = round(max(flops / 1672.1e12, w_bytes / 6534.5e9, push_bytes / 770e9) * 1e6, 2)
+            res["roofline_note"] = "max(FLOPs / 1672.1 TF, weight bytes / 6534.5 GB/s, pushed bytes / 770 GB/s)"
+            res["frac_fused"] = round(res["roofline_us"] / res["us_fused"], 3)
+        results.append(res)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    comm.close()
+    if world > 1:
+        dist.barrier(group=gloo)
+        dist.destroy_process_group()
+    if worst > 2e-2:
+        raise SystemExit(f"tensor-parallel all-reduce mismatch: worst relative error {worst}")
+
+
+if __name__ == "__main__":
+    main()

@@ -39,6 +39,7 @@ constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES = 1024 + STAGES * (P_STAGE + Q_STAGE) + 256;
 
 enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_ATOMIC_F32 = 2 };
+constexpr int kMaxPeers = 8;
 
 struct Params {
   int M, N, K;      // logical problem: tokens, features (pre-activation), reduction
@@ -49,6 +50,14 @@ struct Params {
   void* out;        // bf16 [M, ldc] or fp32 [M, N] workspace
   int ldc;
   int* status;
+  // push mode (world >= 2, EPI_BF16 only): every output tile is stored to
+  // world destinations (this rank's receive slot on every rank, peers over
+  // NVLink), then the last CTA bumps one arrival counter on every rank
+  int push;
+  int world;
+  void* peer_out[kMaxPeers];
+  unsigned int* peer_flag[kMaxPeers];
+  unsigned int* done_ctr;   // local, zero between launches
 };
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
@@ -75,21 +84,25 @@ __device__ __forceinline__ void store_chunk(const Params& p, int pt, int qt, int
     const int n0 = qt * p.bn + c0;
     if (p.epi == EPI_BF16) {
       if (m >= p.M) return;
-      __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldc + n0;
-      if (n0 + NC <= p.N && (p.ldc & 7) == 0) {
+      const int nout = p.push ? p.world : 1;
+      for (int d = 0; d < nout; ++d) {
+        void* base = p.push ? p.peer_out[d] : p.out;
+        __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(base) + static_cast<size_t>(m) * p.ldc + n0;
+        if (n0 + NC <= p.N && (p.ldc & 7) == 0) {
 #pragma unroll
-        for (int j = 0; j < NC; j += 8) {
-          uint4 v;
-          v.x = pack_bf16(__uint_as_float(r[j + 0]), __uint_as_float(r[j + 1]));
-          v.y = pack_bf16(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-          v.z = pack_bf16(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5]));
-          v.w = pack_bf16(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7]));
-          *reinterpret_cast<uint4*>(C + j) = v;
+          for (int j = 0; j < NC; j += 8) {
+            uint4 v;
+            v.x = pack_bf16(__uint_as_float(r[j + 0]), __uint_as_float(r[j + 1]));
+            v.y = pack_bf16(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+            v.z = pack_bf16(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5]));
+            v.w = pack_bf16(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7]));
+            *reinterpret_cast<uint4*>(C + j) = v;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < NC; ++j)
+            if (n0 + j < p.N) C[j] = __float2bfloat16(__uint_as_float(r[j]));
         }
-      } else {
-#pragma unroll
-        for (int j = 0; j < NC; ++j)
-          if (n0 + j < p.N) C[j] = __float2bfloat16(__uint_as_float(r[j]));
       }
     } else if (p.epi == EPI_SWIGLU) {
       if (m >= p.M) return;
@@ -134,10 +147,13 @@ __device__ __forceinline__ void store_chunk(const Params& p, int pt, int qt, int
     const int m0 = qt * p.bn + c0;
     if (p.epi == EPI_BF16) {
       if (n >= p.N) return;
-      __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.out) + n;
+      const int nout = p.push ? p.world : 1;
+      for (int d = 0; d < nout; ++d) {
+        __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.push ? p.peer_out[d] : p.out) + n;
 #pragma unroll
-      for (int j = 0; j < NC; ++j)
-        if (m0 + j < p.M) C[static_cast<size_t>(m0 + j) * p.ldc] = __float2bfloat16(__uint_as_float(r[j]));
+        for (int j = 0; j < NC; ++j)
+          if (m0 + j < p.M) C[static_cast<size_t>(m0 + j) * p.ldc] = __float2bfloat16(__uint_as_float(r[j]));
+      }
     } else if (p.epi == EPI_SWIGLU) {
       // lanes 2j / 2j+1 hold gate_j / up_j for the same tokens
       const bool even = (threadIdx.x & 1) == 0;
@@ -315,12 +331,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   }
 
+  // push mode: make this thread's peer stores visible system-wide before
+  // the CTA reports completion
+  if (p.push && warp >= 2) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 1) {
     __syncwarp();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+  if (p.push && threadIdx.x == 0) {
+    // the last CTA to finish signals every rank once for the whole GEMM
+    if (atomicAdd(p.done_ctr, 1u) == gridDim.x - 1) {
+      *p.done_ctr = 0;
+      __threadfence_system();
+      for (int d = 0; d < p.world; ++d) atomicAdd_system(p.peer_flag[d], 1u);
+    }
   }
 }
 
@@ -428,6 +455,9 @@ extern "C" int ib_gemm_bf16(const void* A, const void* W, void* out, int M, int 
   Params& p = pl.p;
   p.status = status;
   p.ldc = ldc;
+  p.push = 0;
+  p.world = 1;
+  p.done_ctr = nullptr;
   const bool split = p.splits > 1;
   p.epi = split ? EPI_ATOMIC_F32 : epi;
   p.out = split ? static_cast<void*>(ws) : out;
@@ -460,6 +490,53 @@ extern "C" int ib_gemm_bf16(const void* A, const void* W, void* out, int M, int 
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   return 0;
+}
+
+// Fused GEMM + one-shot all-reduce push (row-parallel tensor-parallel
+// layers): out = A @ W^T computed locally, each tile stored to
+// peer_out[d] (this rank's receive slot on rank d, bf16 [M, ldc]) for every
+// rank d, then peer_flag[d] (rank d's arrival counter for this rank) is
+// incremented once. done_ctr: a local zero-initialised counter. No split-K.
+extern "C" int ib_gemm_bf16_push(const void* A, const void* W, int M, int N, int K, int lda, int ldw, int ldc,
+                                 int world, void* const* peer_out, unsigned int* const* peer_flag,
+                                 unsigned int* done_ctr, int* status, cudaStream_t stream) {
+  using namespace ib200::gemm;
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if ((K % 8) != 0 || (lda % 8) != 0 || (ldw % 8) != 0) return -1;
+  if (world < 1 || world > kMaxPeers) return -1;
+  const int num_sms = num_sms_for_current_device();
+  Plan pl = make_plan(M, N, K, num_sms, 1);
+  Params& p = pl.p;
+  p.status = status;
+  p.ldc = ldc;
+  p.epi = EPI_BF16;
+  p.out = peer_out[0];
+  p.push = 1;
+  p.world = world;
+  for (int d = 0; d < kMaxPeers; ++d) {
+    p.peer_out[d] = d < world ? peer_out[d] : nullptr;
+    p.peer_flag[d] = d < world ? peer_flag[d] : nullptr;
+  }
+  p.done_ctr = done_ctr;
+  CUtensorMap tmP, tmQ;
+  const void* Pbase = p.swap ? W : A;
+  const void* Qbase = p.swap ? A : W;
+  const int Prows = p.swap ? N : M;
+  const int Qrows = p.swap ? M : N;
+  const int Pld = p.swap ? ldw : lda;
+  const int Qld = p.swap ? lda : ldw;
+  if (!cached_tmap_2d(&tmP, Pbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Prows, K, Pld, BM, BK)) return -2;
+  if (!cached_tmap_2d(&tmQ, Qbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Qrows, K, Qld, p.bn, BK)) return -2;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_set[dev] = true;
+  }
+  gemm_bf16_kernel<<<pl.grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmP, tmQ, p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
 
 // Plan introspection for tests and benchmarks: writes

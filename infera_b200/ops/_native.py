@@ -55,6 +55,16 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_kv_page_copy": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_ll, c_int, c_int, c_int, c_vp],
         "ib_attn_decode_tc": [c_vp, c_int, c_vp, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
                               c_float, c_vp, c_vp, c_vp, c_int, c_vp, c_vp],
+        "ib_gemm_bf16_push": [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp,
+                              c_vp],
+        "ib_ar_add_rmsnorm": [c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_float, c_vp,
+                              c_vp, c_vp],
+        "ib_sym_alloc": [ctypes.c_size_t, c_vp],
+        "ib_sym_free": [c_vp],
+        "ib_ipc_handle": [c_vp, c_vp],
+        "ib_ipc_open": [c_vp, c_vp],
+        "ib_ipc_close": [c_vp],
+        "ib_can_access_peer": [c_int, c_int],
     }
     for name, args in sig.items():
         fn = getattr(lib, name, None)

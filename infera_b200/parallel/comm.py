@@ -1,0 +1,155 @@
+"""Tensor-parallel group of one node: NCCL for the baseline collectives and a
+symmetric NVLink region for the fused ones.
+
+``TPComm`` owns, per rank, one cudaMalloc'd region exported with CUDA IPC
+and mapped by every peer:
+
+    [parity 0 | parity 1] x [source rank 0 .. world-1] x [max_rows, hidden] bf16
+    arrival counters [parity][source rank] (u32)
+
+The row-parallel GEMMs of a layer (attention output, MLP down) alternate
+parities. ``gemm_allreduce_add_rmsnorm`` runs
+
+    ib_gemm_bf16_push   (tcgen05 GEMM whose epilogue stores every tile into
+                         this rank's slot on every rank, then signals)
+    ib_ar_add_rmsnorm   (waits for every rank's arrival, sums the partials
+                         in fp32, adds the residual, RMSNorm)
+
+for up to ``max_rows`` tokens (decode and small prefill steps); larger
+batches take the baseline: GEMM, ``torch.distributed.all_reduce`` (NCCL),
+add + RMSNorm. Reference counterpart: the engines' TP all-reduce
+(vLLM / SGLang over RCCL on the reference's hardware); the fused form is
+this framework's.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+import torch.distributed as dist
+
+from infera_b200.ops import _native
+from infera_b200.ops import kernels as K
+
+MAX_PEERS = 8
+FLAG_BYTES = 256  # 2 parities x 8 sources x 4 B, padded
+
+
+class TPComm:
+    def __init__(self, rank: int, world: int, device: torch.device, hidden: int, max_rows: int = 256,
+                 nccl_group=None, gloo_group=None, fused: bool = True):
+        if world > MAX_PEERS:
+            raise ValueError(f"tensor parallel size {world} > {MAX_PEERS}")
+        self.rank, self.world = rank, world
+        self.device = torch.device(device)
+        self.hidden = hidden
+        self.max_rows = max_rows
+        self.nccl = nccl_group
+        self.gloo = gloo_group
+        self.fused = fused and self.device.type == "cuda" and os.environ.get("INFERA_TP_FUSED", "1") != "0"
+        self.base = None
+        self.peers: list[int] = []
+        if self.fused:
+            self._setup_symmetric()
+
+    # ------------------------------------------------------------------ setup
+    def _setup_symmetric(self) -> None:
+        lib = _native.kernels()
+        self.slot_elems = self.max_rows * self.hidden
+        self.data_bytes = 2 * self.world * self.slot_elems * 2
+        total = self.data_bytes + FLAG_BYTES
+        ptr = ctypes.c_void_p()
+        _native.check(lib.ib_sym_alloc(total, ctypes.byref(ptr)), "ib_sym_alloc")
+        self.base = ptr.value
+        handle = (ctypes.c_char * 64)()
+        _native.check(lib.ib_ipc_handle(ctypes.c_void_p(self.base), handle), "ib_ipc_handle")
+        mine = bytes(handle)
+        if self.world > 1:
+            allh = [None] * self.world
+            dist.all_gather_object(allh, mine, group=self.gloo)
+        else:
+            allh = [mine]
+        self._opened = []
+        for r, h in enumerate(allh):
+            if r == self.rank:
+                self.peers.append(self.base)
+                continue
+            p = ctypes.c_void_p()
+            buf = (ctypes.c_char * 64).from_buffer_copy(h)
+            _native.check(lib.ib_ipc_open(buf, ctypes.byref(p)), f"ib_ipc_open(rank {r})")
+            self.peers.append(p.value)
+            self._opened.append(p.value)
+        # local counters: done_ctr[2], consumed[2], fin_ctr[2]
+        self.ctr = torch.zeros(8, dtype=torch.int32, device=self.device)
+        if self.world > 1:
+            dist.barrier(group=self.gloo)
+
+    def close(self) -> None:
+        if self.base is None:
+            return
+        lib = _native.kernels()
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.gloo)
+        for p in self._opened:
+            lib.ib_ipc_close(ctypes.c_void_p(p))
+        lib.ib_sym_free(ctypes.c_void_p(self.base))
+        self.base = None
+
+    # ------------------------------------------------------------------ ops
+    def _slot(self, rank_base: int, parity: int, src: int) -> int:
+        return rank_base + ((parity * self.world + src) * self.slot_elems) * 2
+
+    def _flag(self, rank_base: int, parity: int, src: int) -> int:
+        return rank_base + self.data_bytes + (parity * MAX_PEERS + src) * 4
+
+    def uses_fused(self, rows: int) -> bool:
+        return self.fused and rows <= self.max_rows
+
+    def gemm_allreduce_add_rmsnorm(self, x: torch.Tensor, w: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor,
+                                   eps: float, out: torch.Tensor, parity: int, tmp: torch.Tensor | None = None
+                                   ) -> torch.Tensor:
+        """h += all_reduce(x @ w.T); out = rmsnorm(h) * norm_w (h updated in place)."""
+        M, Kd = x.shape
+        N = w.shape[0]
+        if not self.uses_fused(M):
+            o = K.linear(x, w, out=None if tmp is None else tmp[:M])
+            if self.world > 1:
+                dist.all_reduce(o, group=self.nccl)
+            return K.add_rmsnorm(o, h, norm_w, eps, out=out)
+        assert N == self.hidden and h.is_contiguous() and out.is_contiguous()
+        lib = _native.kernels()
+        sc = K.scratch(x.device)
+        peer_out = (ctypes.c_void_p * MAX_PEERS)(*[self._slot(self.peers[d], parity, self.rank)
+                                                   for d in range(self.world)])
+        peer_flag = (ctypes.c_void_p * MAX_PEERS)(*[self._flag(self.peers[d], parity, self.rank)
+                                                    for d in range(self.world)])
+        ctr = self.ctr.data_ptr()
+        stream = K._stream()
+        rc = lib.ib_gemm_bf16_push(x.data_ptr(), w.data_ptr(), M, N, Kd, x.stride(0), w.stride(0), self.hidden,
+                                   self.world, peer_out, peer_flag, ctypes.c_void_p(ctr + 4 * parity),
+                                   sc.status.data_ptr(), stream)
+        _native.check(rc, "ib_gemm_bf16_push")
+        rc = lib.ib_ar_add_rmsnorm(ctypes.c_void_p(self._slot(self.base, parity, 0)), self.slot_elems, self.hidden,
+                                   ctypes.c_void_p(self._flag(self.base, parity, 0)),
+                                   ctypes.c_void_p(ctr + 4 * (2 + parity)), ctypes.c_void_p(ctr + 4 * (4 + parity)),
+                                   self.world, M, N, h.data_ptr(), norm_w.data_ptr(), eps, out.data_ptr(),
+                                   sc.status.data_ptr(), stream)
+        _native.check(rc, "ib_ar_add_rmsnorm")
+        K._count(2)
+        return out
+
+    def all_gather_rows(self, x: torch.Tensor) -> torch.Tensor:
+        """[M, n] per rank -> [M, world * n] (columns in rank order), NCCL."""
+        if self.world == 1:
+            return x
+        parts = [torch.empty_like(x) for _ in range(self.world)]
+        dist.all_gather(parts, x.contiguous(), group=self.nccl)
+        return torch.cat(parts, dim=1)
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            dist.all_reduce(x, group=self.nccl)
+        return x

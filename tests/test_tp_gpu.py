@@ -1,0 +1,31 @@
+"""Tensor-parallel fused GEMM + all-reduce + add + RMSNorm (NVLink peer
+stores) against a single-GPU fp32 computation of the whole problem, and
+against the NCCL baseline path."""
+
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_fused_allreduce_single_rank():
+    from infera_b200.bench.tp_comm_bench import main
+
+    # world 1 exercises the push / arrival / consume bookkeeping on one GPU
+    main(["--rows", "1,64,200", "--hidden", "4096", "--k-total", "2048", "--check-only"])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_allreduce_two_ranks():
+    env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29611", "-m",
+           "infera_b200.bench.tp_comm_bench", "--rows", "1,64,256", "--check-only"]
+    r = subprocess.run(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, timeout=300)
+    assert r.returncode == 0, r.stdout.decode()[-3000:]
