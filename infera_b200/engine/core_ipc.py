@@ -188,6 +188,8 @@ class EngineCoreServer:
         if not eng.has_unfinished():
             if self._pull.poll(idle_wait_ms):
                 self._drain_inbox()
+            elif hasattr(eng, "idle"):
+                eng.idle()
         else:
             self._drain_inbox()
         if eng.has_unfinished():
@@ -409,22 +411,44 @@ def main(argv=None) -> None:
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-events-endpoint", default=None)
     p.add_argument("--kv-tier", default=None)
+    p.add_argument("--tp-size", type=int, default=1, help="tensor-parallel ranks (RANK / LOCAL_RANK / MASTER_* from env)")
     a = p.parse_args(argv)
     from infera_b200.engine.kv_events import KvEventPublisher
     from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
 
-    pub = KvEventPublisher(a.kv_events_endpoint) if a.kv_events_endpoint else None
+    tp = None
+    rank = 0
+    device = a.device
+    if a.tp_size > 1:
+        from infera_b200.parallel.launch import init_tp
+
+        tp, rank, device = init_tp(a.tp_size, model=a.model)
+    pub = KvEventPublisher(a.kv_events_endpoint) if a.kv_events_endpoint and rank == 0 else None
     cfg = EngineConfig(model=a.model, page_size=a.page_size, max_num_seqs=a.max_num_seqs,
                        max_batched_tokens=a.max_batched_tokens, gpu_memory_utilization=a.gpu_memory_utilization,
                        num_pages=a.num_pages, use_cuda_graphs=not a.no_cuda_graphs, seed=a.seed, kv_tier=a.kv_tier)
-    eng = LLMEngine(cfg, device=a.device, event_sink=pub)
-    srv = EngineCoreServer(eng, a.in_addr, a.out_addr, publisher=pub,
+    eng = LLMEngine(cfg, device=device, event_sink=pub, tp=tp)
+    if rank > 0:
+        from infera_b200.engine.tp_engine import follower_loop
+
+        follower_loop(eng, tp.gloo)
+        tp.close()
+        return
+    served = eng
+    if tp is not None:
+        from infera_b200.engine.tp_engine import TPLeader
+
+        served = TPLeader(eng, tp.gloo)
+    srv = EngineCoreServer(served, a.in_addr, a.out_addr, publisher=pub,
                            info={"vocab": eng.model_cfg.vocab, "page_size": cfg.page_size,
-                                 "num_pages": eng.bm.num_pages, "pid": os.getpid()})
+                                 "num_pages": eng.bm.num_pages, "pid": os.getpid(), "tp_size": a.tp_size})
     stop = [False]
     signal.signal(signal.SIGTERM, lambda *_: stop.__setitem__(0, True))
     srv.announce_ready()
     srv.run(should_stop=lambda: stop[0])
+    if tp is not None:
+        served.shutdown()
+        tp.close()
     if pub is not None:
         pub.close()
     srv.close()

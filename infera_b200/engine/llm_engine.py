@@ -60,7 +60,8 @@ class EngineConfig:
 
 class LLMEngine:
     def __init__(self, cfg: EngineConfig, device: str | torch.device = "cuda:0",
-                 event_sink: Callable[[str, dict], None] | None = None, model_cfg: DenseConfig | None = None):
+                 event_sink: Callable[[str, dict], None] | None = None, model_cfg: DenseConfig | None = None,
+                 tp=None):
         self.cfg = cfg
         self.device = torch.device(device)
         if self.device.type == "cuda":
@@ -71,8 +72,16 @@ class LLMEngine:
         if cfg.max_model_len:
             mcfg.max_model_len = cfg.max_model_len
         self.model_cfg = mcfg
-        self.model = DenseModel(mcfg, self.device, seed=cfg.seed)
+        self.tp = tp
+        self.model = DenseModel(mcfg, self.device, seed=cfg.seed, tp=tp)
         num_pages = cfg.num_pages or self._derive_num_pages()
+        if tp is not None and tp.world > 1:
+            # every rank runs the same scheduler: agree on the page count
+            import torch.distributed as dist
+
+            t = torch.tensor([num_pages], dtype=torch.int64)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=tp.gloo)
+            num_pages = int(t.item())
         self._event_sink = event_sink
         self.bm = BlockManager(num_pages, cfg.page_size, cfg.enable_prefix_cache, event_sink=self._on_kv_event)
         self.scheduler = Scheduler(self.bm, cfg.max_num_seqs, cfg.max_batched_tokens, mcfg.max_model_len,
@@ -88,13 +97,16 @@ class LLMEngine:
                                     cfg.page_size)
             self.bm.tier = self.tier
         self.requests: dict[str, Request] = {}
+        # commands applied since the last step, when a tensor-parallel leader
+        # replays them on its followers (None: not recorded)
+        self.cmd_log: list | None = None
         self.num_steps = 0
         self.clock: Callable[[], float] = time.monotonic
         self.counters = {"prompt_tokens": 0, "generation_tokens": 0, "finished": 0, "preemptions": 0}
 
     # ------------------------------------------------------------------ sizing
     def _derive_num_pages(self) -> int:
-        mcfg = self.model_cfg
+        mcfg = self.model.cfg  # this rank's shard of the model
         per_page = 2 * mcfg.num_layers * self.cfg.page_size * mcfg.kv_size * 2
         if self.device.type != "cuda":
             return 512
@@ -128,9 +140,13 @@ class LLMEngine:
         req.arrival_time = self.clock() if arrival_time is None else arrival_time
         self.requests[request_id] = req
         self.scheduler.add(req)
+        if self.cmd_log is not None:
+            self.cmd_log.append(("add", request_id, list(prompt_token_ids), req.sampling))
         return req
 
     def abort_request(self, request_id: str) -> bool:
+        if self.cmd_log is not None:
+            self.cmd_log.append(("abort", request_id))
         r = self.scheduler.abort(request_id)
         if r is not None:
             self.requests.pop(request_id, None)

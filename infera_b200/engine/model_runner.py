@@ -14,6 +14,7 @@ bucket; steps with prefill chunks run eagerly.
 from __future__ import annotations
 
 import bisect
+import zlib
 from dataclasses import dataclass
 
 import numpy as np
@@ -120,7 +121,8 @@ class ModelRunner:
         for i, c in enumerate(sampled):
             sp = c.req.sampling
             temps[i] = sp.temperature
-            base = sp.seed if sp.seed is not None else hash(c.req.request_id) & 0x7FFFFFFF
+            # deterministic across processes (tensor-parallel ranks sample alike)
+            base = sp.seed if sp.seed is not None else zlib.crc32(c.req.request_id.encode()) & 0x7FFFFFFF
             seeds[i] = base * 1000003 + len(c.req.output_token_ids)
         return temps, seeds
 

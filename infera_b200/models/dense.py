@@ -16,12 +16,22 @@ decoding sequence. Per layer:
 The gate/up weight is stored row-interleaved (gate_0, up_0, gate_1, ...)
 so the GEMM epilogue can apply SwiGLU without a second pass.
 Only the rows in ``logits_idx`` reach the LM head.
+
+Tensor parallelism (``tp``: a :class:`infera_b200.parallel.comm.TPComm`):
+QKV and gate/up are column-parallel (each rank owns 1/world of the heads
+and of the MLP width), the attention output and MLP down projections are
+row-parallel and each is followed by an all-reduce fused with the residual
+add and the next RMSNorm (NVLink one-shot push for small batches, NCCL
+otherwise); the LM head is vocab-parallel and its logits are all-gathered.
+``model.cfg`` is this rank's local shape; ``model.full_cfg`` the model's.
+Weights are generated full-size from the seed and sliced, so any TP size
+computes the same model.
 """
 
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 
 import torch
 
@@ -55,7 +65,8 @@ class ForwardBatch:
 
 
 class DenseWeights:
-    def __init__(self, cfg: DenseConfig, device: torch.device, seed: int = 0, std: float = 0.02):
+    def __init__(self, cfg: DenseConfig, device: torch.device, seed: int = 0, std: float = 0.02,
+                 rank: int = 0, world: int = 1):
         self.cfg = cfg
         g = torch.Generator(device=device).manual_seed(seed)
         bf = torch.bfloat16
@@ -63,25 +74,45 @@ class DenseWeights:
         def rnd(*shape, scale=std):
             return (torch.randn(*shape, generator=g, device=device, dtype=torch.float32) * scale).to(bf)
 
-        H = cfg.hidden
+        H, D, W, r = cfg.hidden, cfg.head_dim, world, rank
+        hq, hk = cfg.num_heads // W, cfg.num_kv_heads // W
+        f = cfg.ffn // W
+        q_rows = slice(r * hq * D, (r + 1) * hq * D)
+        k_rows = slice(cfg.q_size + r * hk * D, cfg.q_size + (r + 1) * hk * D)
+        v_rows = slice(cfg.q_size + cfg.kv_size + r * hk * D, cfg.q_size + cfg.kv_size + (r + 1) * hk * D)
+
+        def shard_rows(t, *sl):
+            return t if W == 1 else torch.cat([t[x] for x in sl], 0).contiguous()
+
+        def shard_cols(t, a, b):
+            return t if W == 1 else t[:, a:b].contiguous()
+
         self.embed = rnd(cfg.vocab, H, scale=1.0)
         self.layers = []
         out_scale = std / math.sqrt(2 * cfg.num_layers)
         for _ in range(cfg.num_layers):
+            qkv = rnd(cfg.qkv_size, H)
+            o = rnd(H, cfg.q_size, scale=out_scale)
+            gu = rnd(2 * cfg.ffn, H)      # interleaved rows (g0, u0, g1, u1, ...)
+            dn = rnd(H, cfg.ffn, scale=out_scale)
             lw = {
                 "ln1": torch.ones(H, dtype=bf, device=device),
                 "ln2": torch.ones(H, dtype=bf, device=device),
-                "qkv": rnd(cfg.qkv_size, H),
-                "o": rnd(H, cfg.q_size, scale=out_scale),
-                "gate_up": rnd(2 * cfg.ffn, H),      # interleaved rows (g0, u0, g1, u1, ...)
-                "down": rnd(H, cfg.ffn, scale=out_scale),
+                "qkv": shard_rows(qkv, q_rows, k_rows, v_rows),
+                "o": shard_cols(o, r * hq * D, (r + 1) * hq * D),
+                "gate_up": shard_rows(gu, slice(2 * r * f, 2 * (r + 1) * f)),
+                "down": shard_cols(dn, r * f, (r + 1) * f),
             }
+            del qkv, o, gu, dn
             if cfg.qk_norm:
                 lw["q_norm"] = torch.ones(cfg.head_dim, dtype=bf, device=device)
                 lw["k_norm"] = torch.ones(cfg.head_dim, dtype=bf, device=device)
             self.layers.append(lw)
         self.final_norm = torch.ones(H, dtype=bf, device=device)
-        self.lm_head = rnd(cfg.vocab, H)
+        lm = rnd(cfg.vocab, H)
+        vl = cfg.vocab // W
+        self.lm_head = lm if W == 1 else lm[r * vl:(r + 1) * vl].contiguous()
+        del lm
 
     def nbytes(self) -> int:
         n = self.embed.numel() + self.lm_head.numel() + self.final_norm.numel()
@@ -93,10 +124,17 @@ class DenseWeights:
 class DenseModel:
     """Stateless forward over a paged KV cache owned by the engine."""
 
-    def __init__(self, cfg: DenseConfig, device: torch.device | str, seed: int = 0):
-        self.cfg = cfg
+    def __init__(self, cfg: DenseConfig, device: torch.device | str, seed: int = 0, tp=None):
+        self.full_cfg = cfg
+        self.tp = tp
+        W = tp.world if tp is not None else 1
+        r = tp.rank if tp is not None else 0
+        if cfg.num_heads % W or cfg.num_kv_heads % W or cfg.ffn % W or cfg.vocab % W:
+            raise ValueError(f"{cfg.name} does not split over {W} tensor-parallel ranks")
+        self.cfg = replace(cfg, num_heads=cfg.num_heads // W, num_kv_heads=cfg.num_kv_heads // W,
+                           ffn=cfg.ffn // W) if W > 1 else cfg
         self.device = torch.device(device)
-        self.w = DenseWeights(cfg, self.device, seed=seed)
+        self.w = DenseWeights(cfg, self.device, seed=seed, rank=r, world=W)
         self.cos_sin = K.rope_cos_sin(cfg.max_model_len, cfg.head_dim, cfg.rope_theta, cfg.rope_scaling,
                                       device=self.device)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
@@ -149,17 +187,25 @@ class DenseModel:
             if fb.num_decode > 0:
                 K.attn_decode(qkv[Tp:T], kc, vc, fb.d_block_table, fb.d_seq_lens, cfg.num_heads, cfg.num_kv_heads,
                               self.scale, splits=fb.d_splits, out=attn[Tp:T], bt_rows=fb.d_bt_rows)
-            K.linear(attn, lw["o"], out=o)
-            K.add_rmsnorm(o, h, lw["ln2"], cfg.rms_eps, out=x)
-            K.linear(x, lw["gate_up"], out=act, swiglu=True)
-            K.linear(act, lw["down"], out=o)
             nxt = self.w.layers[li + 1]["ln1"] if li + 1 < cfg.num_layers else self.w.final_norm
-            K.add_rmsnorm(o, h, nxt, cfg.rms_eps, out=x)
+            if self.tp is None:
+                K.linear(attn, lw["o"], out=o)
+                K.add_rmsnorm(o, h, lw["ln2"], cfg.rms_eps, out=x)
+                K.linear(x, lw["gate_up"], out=act, swiglu=True)
+                K.linear(act, lw["down"], out=o)
+                K.add_rmsnorm(o, h, nxt, cfg.rms_eps, out=x)
+            else:
+                self.tp.gemm_allreduce_add_rmsnorm(attn, lw["o"], h, lw["ln2"], cfg.rms_eps, x, 0, tmp=o)
+                K.linear(x, lw["gate_up"], out=act, swiglu=True)
+                self.tp.gemm_allreduce_add_rmsnorm(act, lw["down"], h, nxt, cfg.rms_eps, x, 1, tmp=o)
         S = fb.logits_idx.shape[0]
         xs = bufs["xs"][:S] if "xs" in bufs else None
         xs = K.gather_rows(x, fb.logits_idx, out=xs)
         logits = bufs["logits"][:S] if "logits" in bufs else None
-        return K.linear(xs, self.w.lm_head, out=logits)
+        if self.tp is None or self.tp.world == 1:
+            return K.linear(xs, self.w.lm_head, out=logits)
+        local = K.linear(xs, self.w.lm_head, out=bufs["logits_local"][:S] if "logits_local" in bufs else None)
+        return self.tp.all_gather_cols(local, out=logits)
 
     def alloc_buffers(self, max_tokens: int, max_seqs: int) -> dict:
         cfg = self.cfg
@@ -174,6 +220,8 @@ class DenseModel:
             "act": torch.empty(max_tokens, cfg.ffn, dtype=bf, device=dev),
             "xs": torch.empty(max_seqs, cfg.hidden, dtype=bf, device=dev),
             "logits": torch.empty(max_seqs, cfg.vocab, dtype=bf, device=dev),
+            **({"logits_local": torch.empty(max_seqs, self.w.lm_head.shape[0], dtype=bf, device=dev)}
+               if self.tp is not None and self.tp.world > 1 else {}),
         }
 
     def max_gemm_workspace(self, max_tokens: int) -> int:

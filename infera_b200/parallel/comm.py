@@ -141,13 +141,18 @@ class TPComm:
         K._count(2)
         return out
 
-    def all_gather_rows(self, x: torch.Tensor) -> torch.Tensor:
-        """[M, n] per rank -> [M, world * n] (columns in rank order), NCCL."""
+    def all_gather_cols(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """[M, n] per rank -> [M, world * n] (rank r's columns at r*n), NCCL."""
         if self.world == 1:
             return x
-        parts = [torch.empty_like(x) for _ in range(self.world)]
-        dist.all_gather(parts, x.contiguous(), group=self.nccl)
-        return torch.cat(parts, dim=1)
+        M, n = x.shape
+        stacked = torch.empty(self.world * M, n, dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(stacked, x.contiguous(), group=self.nccl)
+        full = stacked.view(self.world, M, n).permute(1, 0, 2).reshape(M, self.world * n)
+        if out is not None:
+            out.copy_(full)
+            return out
+        return full
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
