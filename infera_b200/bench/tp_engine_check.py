@@ -43,6 +43,7 @@ def main(argv=None) -> None:
     if rank > 0:
         follower_loop(eng, tp.gloo)
         follower_loop(eng, tp.gloo)
+        eng.close()
         tp.close()
         dist.destroy_process_group()
         return
@@ -57,6 +58,7 @@ def main(argv=None) -> None:
         ref = ref_eng.generate(prompts[:4], SamplingParams(max_tokens=8, ignore_eos=True))
         agree = sum(x == y for o, r in zip(outs, ref) for x, y in zip(o, r)) / sum(len(r) for r in ref)
         res["greedy_agreement"] = round(agree, 4)
+        ref_eng.close()
         del ref_eng
         torch.cuda.empty_cache()
     # decode step time: prefill the batch, then time decode-only steps
@@ -80,6 +82,7 @@ def main(argv=None) -> None:
     res.update({"batch": a.batch, "context": a.prompt_len, "decode_ms_per_step": round(sum(t) / len(t), 3),
                 "status": int(__import__("infera_b200.ops.kernels", fromlist=["x"]).scratch(dev).read_status())})
     print(json.dumps(res), flush=True)
+    eng.close()
     tp.close()
     dist.destroy_process_group()
 

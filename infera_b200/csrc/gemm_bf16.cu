@@ -353,6 +353,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // Reduce the fp32 split-K workspace into the bf16 output (optionally
 // applying SwiGLU) and zero the workspace for its next use.
+struct PushDst {
+  void* out[kMaxPeers];
+  unsigned int* flag[kMaxPeers];
+};
+
+// Split-K finalize for push mode: fp32 workspace -> bf16 rows stored to
+// every rank's receive slot (zeroing the workspace), then the last CTA
+// signals every rank once.
+__global__ void splitk_finalize_push_kernel(float* __restrict__ ws, int M, int N, int ldc, int world,
+                                            const PushDst dst, unsigned int* done_ctr) {
+  const int m = blockIdx.y;
+  if (m < M) {
+    float* row = ws + static_cast<size_t>(m) * N;
+    for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < N; n += gridDim.x * blockDim.x * 4) {
+      if (n + 4 <= N) {
+        float4 v = *reinterpret_cast<float4*>(row + n);
+        *reinterpret_cast<float4*>(row + n) = make_float4(0.f, 0.f, 0.f, 0.f);
+        uint2 o;
+        o.x = pack_bf16(v.x, v.y);
+        o.y = pack_bf16(v.z, v.w);
+        for (int d = 0; d < world; ++d)
+          *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(dst.out[d]) + static_cast<size_t>(m) * ldc + n) = o;
+      } else {
+        for (int j = n; j < N; ++j) {
+          const __nv_bfloat16 b = __float2bfloat16(row[j]);
+          row[j] = 0.f;
+          for (int d = 0; d < world; ++d) static_cast<__nv_bfloat16*>(dst.out[d])[static_cast<size_t>(m) * ldc + j] = b;
+        }
+      }
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(done_ctr, 1u) == gridDim.x * gridDim.y - 1) {
+      *done_ctr = 0;
+      __threadfence_system();
+      for (int d = 0; d < world; ++d) atomicAdd_system(dst.flag[d], 1u);
+    }
+  }
+}
+
 __global__ void splitk_finalize_kernel(float* __restrict__ ws, __nv_bfloat16* __restrict__ out, int M, int N,
                                        int ldc, int swiglu) {
   const int m = blockIdx.y;
@@ -499,19 +541,22 @@ extern "C" int ib_gemm_bf16(const void* A, const void* W, void* out, int M, int 
 // incremented once. done_ctr: a local zero-initialised counter. No split-K.
 extern "C" int ib_gemm_bf16_push(const void* A, const void* W, int M, int N, int K, int lda, int ldw, int ldc,
                                  int world, void* const* peer_out, unsigned int* const* peer_flag,
-                                 unsigned int* done_ctr, int* status, cudaStream_t stream) {
+                                 unsigned int* done_ctr, float* ws, int* status, cudaStream_t stream) {
   using namespace ib200::gemm;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if ((K % 8) != 0 || (lda % 8) != 0 || (ldw % 8) != 0) return -1;
   if (world < 1 || world > kMaxPeers) return -1;
   const int num_sms = num_sms_for_current_device();
-  Plan pl = make_plan(M, N, K, num_sms, 1);
+  // split K like the plain GEMM does (small M leaves most SMs idle
+  // otherwise); the split path pushes from its finalize kernel
+  Plan pl = make_plan(M, N, K, num_sms, ws == nullptr ? 1 : 0);
   Params& p = pl.p;
+  const bool split = p.splits > 1;
   p.status = status;
-  p.ldc = ldc;
-  p.epi = EPI_BF16;
-  p.out = peer_out[0];
-  p.push = 1;
+  p.ldc = split ? N : ldc;
+  p.epi = split ? EPI_ATOMIC_F32 : EPI_BF16;
+  p.out = split ? static_cast<void*>(ws) : peer_out[0];
+  p.push = split ? 0 : 1;
   p.world = world;
   for (int d = 0; d < kMaxPeers; ++d) {
     p.peer_out[d] = d < world ? peer_out[d] : nullptr;
@@ -536,7 +581,19 @@ extern "C" int ib_gemm_bf16_push(const void* A, const void* W, int M, int N, int
   }
   gemm_bf16_kernel<<<pl.grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmP, tmQ, p);
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 0 : static_cast<int>(e);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (split) {
+    PushDst dst;
+    for (int d = 0; d < kMaxPeers; ++d) {
+      dst.out[d] = p.peer_out[d];
+      dst.flag[d] = p.peer_flag[d];
+    }
+    dim3 g((N + 1023) / 1024, M);
+    splitk_finalize_push_kernel<<<g, 256, 0, stream>>>(ws, M, N, ldc, world, dst, done_ctr);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  return 0;
 }
 
 // Plan introspection for tests and benchmarks: writes

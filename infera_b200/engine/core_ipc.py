@@ -432,6 +432,7 @@ def main(argv=None) -> None:
         from infera_b200.engine.tp_engine import follower_loop
 
         follower_loop(eng, tp.gloo)
+        eng.close()
         tp.close()
         return
     served = eng
@@ -448,6 +449,7 @@ def main(argv=None) -> None:
     srv.run(should_stop=lambda: stop[0])
     if tp is not None:
         served.shutdown()
+        eng.close()
         tp.close()
     if pub is not None:
         pub.close()

@@ -225,6 +225,10 @@ class LLMEngine:
         return RequestOutput(r.request_id, new or [], True, st.value, len(r.prompt_token_ids),
                              r.num_cached_prompt_tokens, len(r.output_token_ids))
 
+    def close(self) -> None:
+        """Release device resources that outlive a process group (graphs)."""
+        self.runner.release_graphs()
+
     # ------------------------------------------------------------------ helpers
     def generate(self, prompts: list[list[int]], sampling: SamplingParams | None = None) -> list[list[int]]:
         """Offline batch generation: returns the output ids of each prompt."""

@@ -269,6 +269,13 @@ class ModelRunner:
         torch.cuda.current_stream().wait_stream(stream)
         torch.cuda.synchronize()
 
+    def release_graphs(self) -> None:
+        """Drop the captured graphs (a graph holding NCCL calls must be
+        released before its process group is destroyed)."""
+        if self.graphs:
+            torch.cuda.synchronize(self.dev)
+            self.graphs.clear()
+
     def _run_graph(self, ids, pos, slots, dmeta, temps, seeds, bt_updates) -> list[int]:
         B = len(ids)
         Bg = self.graph_sizes[bisect.bisect_left(self.graph_sizes, B)]

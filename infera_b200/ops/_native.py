@@ -56,7 +56,7 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_attn_decode_tc": [c_vp, c_int, c_vp, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
                               c_float, c_vp, c_vp, c_vp, c_int, c_vp, c_vp],
         "ib_gemm_bf16_push": [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp,
-                              c_vp],
+                              c_vp, c_vp],
         "ib_ar_add_rmsnorm": [c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_float, c_vp,
                               c_vp, c_vp],
         "ib_sym_alloc": [ctypes.c_size_t, c_vp],

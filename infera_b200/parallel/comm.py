@@ -128,9 +128,11 @@ class TPComm:
                                                     for d in range(self.world)])
         ctr = self.ctr.data_ptr()
         stream = K._stream()
+        splits = K._gemm_splits(M, N, Kd, 0)
+        ws = sc.ensure_gemm(M * N if splits > 1 else 1)
         rc = lib.ib_gemm_bf16_push(x.data_ptr(), w.data_ptr(), M, N, Kd, x.stride(0), w.stride(0), self.hidden,
                                    self.world, peer_out, peer_flag, ctypes.c_void_p(ctr + 4 * parity),
-                                   sc.status.data_ptr(), stream)
+                                   ws.data_ptr(), sc.status.data_ptr(), stream)
         _native.check(rc, "ib_gemm_bf16_push")
         rc = lib.ib_ar_add_rmsnorm(ctypes.c_void_p(self._slot(self.base, parity, 0)), self.slot_elems, self.hidden,
                                    ctypes.c_void_p(self._flag(self.base, parity, 0)),
@@ -138,7 +140,7 @@ class TPComm:
                                    self.world, M, N, h.data_ptr(), norm_w.data_ptr(), eps, out.data_ptr(),
                                    sc.status.data_ptr(), stream)
         _native.check(rc, "ib_ar_add_rmsnorm")
-        K._count(2)
+        K._count(3 if splits > 1 else 2)
         return out
 
     def all_gather_cols(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -34,10 +34,10 @@ def test_fused_allreduce_two_ranks():
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_tp_engine_matches_single_gpu():
     env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
-    cmd = ["timeout", "-k", "10", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+    cmd = ["timeout", "-k", "10", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29612", "-m",
            "infera_b200.bench.tp_engine_check", "--model", "llama-3.1-8b", "--batch", "8", "--decode-steps", "24"]
-    r = subprocess.run(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, timeout=700)
+    r = subprocess.run(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, timeout=330)
     out = r.stdout.decode()
     assert r.returncode == 0, out[-3000:]
     line = [x for x in out.splitlines() if x.startswith("{")][-1]
