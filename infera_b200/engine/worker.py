@@ -65,6 +65,8 @@ def parse_args(argv=None):
     p.add_argument("--no-cuda-graphs", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--etcd-endpoint", default=None)
+    p.add_argument("--k8s-register", action="store_true",
+                   help="register through this Pod's worker-info annotation (in-cluster service account)")
     p.add_argument("--kv-events-endpoint", default=None, help="ZMQ PUB bind address, e.g. tcp://127.0.0.1:5557")
     p.add_argument("--disagg-mode", choices=("mixed", "prefill", "decode"), default="mixed")
     p.add_argument("--kv-push-endpoint", default=None)
@@ -171,6 +173,12 @@ async def run_worker(args) -> None:
     from infera_b200.engine.server import build_worker_app
     from infera_b200.utils.tokenizer import load_tokenizer
 
+    if args.disagg_mode != "mixed":
+        from infera_b200.common.disagg_preflight import preflight
+
+        preflight(mode=args.disagg_mode, advertise_host=args.advertise_host or args.host,
+                  kv_endpoint=args.kv_push_endpoint, single_node=(args.advertise_host or args.host) in
+                  ("127.0.0.1", "localhost", "0.0.0.0"))
     aeng, vocab, shutdown_engine = await start_engine(args)
     tok = load_tokenizer(args.tokenizer, vocab_size=vocab)
     app = build_worker_app(aeng, tok, args.served_model_name or args.model)
@@ -186,6 +194,13 @@ async def run_worker(args) -> None:
         from infera_b200.common.registration import EtcdRegistration
 
         reg = EtcdRegistration(args.etcd_endpoint, payload)
+        await reg.register()
+        hb = asyncio.create_task(reg.heartbeat_loop())
+    elif args.k8s_register:
+        from infera_b200.common.k8s_client import InClusterClient
+        from infera_b200.common.registration_k8s import K8sRegistration
+
+        reg = K8sRegistration(InClusterClient(), payload)
         await reg.register()
         hb = asyncio.create_task(reg.heartbeat_loop())
     logger.info("worker %s serving %s", payload["worker_id"], payload["model_name"])

@@ -97,3 +97,37 @@ class InProcessTransport:
 
     async def aclose(self) -> None:
         return None
+
+
+class RoutingTransport:
+    """Picks a transport per worker from its record's ``request_transport``
+    (``http`` by default; ``bus`` for workers behind a message bus)."""
+
+    def __init__(self, http: HttpTransport | None = None, bus_client=None):
+        self.http = http or HttpTransport()
+        self.bus = bus_client
+
+    def _for(self, worker):
+        if getattr(worker, "request_transport", "http") == "bus":
+            if self.bus is None:
+                raise LookupError(f"worker {worker.worker_id} wants the bus transport but none is configured")
+            return self.bus
+        return self.http
+
+    async def stream(self, worker, path, body, headers=None):
+        try:
+            t = self._for(worker)
+        except LookupError as e:
+            yield ERROR, 0, str(e).encode()
+            return
+        async for item in t.stream(worker, path, body, headers):
+            yield item
+
+    async def get(self, worker, path):
+        return await self.http.get(worker, path)
+
+    async def post(self, worker, path, body=None):
+        return await self.http.post(worker, path, body)
+
+    async def aclose(self) -> None:
+        await self.http.aclose()
