@@ -76,17 +76,21 @@ def _wait_http(url: str, pred, timeout: float) -> bool:
     return False
 
 
-def router_cmd(backend: str) -> list[str]:
+def router_cmd(backend: str, etcd_port: int = ETCD_PORT, router_port: int = ROUTER_PORT) -> list[str]:
     return [sys.executable, "-m", "infera_b200.server", "--discovery-backend", "etcd",
-            "--etcd-endpoint", f"127.0.0.1:{ETCD_PORT}", "--router-policy", "kv-aware",
-            "--router-backend", backend, "--host", "127.0.0.1", "--port", str(ROUTER_PORT),
+            "--etcd-endpoint", f"127.0.0.1:{etcd_port}", "--router-policy", "kv-aware",
+            "--router-backend", backend, "--host", "127.0.0.1", "--port", str(router_port),
             "--log-level", "warning"]
 
 
 def run_e2e_fleet(engine, *, model: str, rank: int, world: int, barrier, sessions: range, rate: float,
                   warmup_s: float, timed_s: float, seed: int, router_backend: str = "python",
-                  logdir: str | None = None, trace: str = "agentic-8b", drain_s: float = 0.0) -> dict:
-    """``barrier()`` synchronises the ranks (host-side)."""
+                  logdir: str | None = None, trace: str = "agentic-8b", drain_s: float = 0.0,
+                  ports: dict | None = None, appear_timeout: float = 300.0) -> dict:
+    """``barrier()`` synchronises the ranks (host-side). ``ports`` overrides
+    the fixed ports (keys etcd, router, worker0, events0)."""
+    P = {"etcd": ETCD_PORT, "router": ROUTER_PORT, "worker0": WORKER_PORT0, "events0": EVENTS_PORT0}
+    P.update(ports or {})
     from infera_b200.engine.core_ipc import EngineCoreServer, ipc_pair
     from infera_b200.engine.kv_events import KvEventPublisher
 
@@ -99,13 +103,14 @@ def run_e2e_fleet(engine, *, model: str, rank: int, world: int, barrier, session
     pub = None
     try:
         if rank == 0:
-            procs.append(_spawn([sys.executable, "-m", "infera_b200.common.etcd_fake", "--port", str(ETCD_PORT)],
+            procs.append(_spawn([sys.executable, "-m", "infera_b200.common.etcd_fake", "--port", str(P["etcd"])],
                                 os.path.join(logdir, "e2e_etcd.log")))
-            _wait_http(f"http://127.0.0.1:{ETCD_PORT}/health", lambda r: True, 60)
-            procs.append(_spawn(router_cmd(router_backend), os.path.join(logdir, "e2e_router.log")))
+            _wait_http(f"http://127.0.0.1:{P['etcd']}/health", lambda r: True, 60)
+            procs.append(_spawn(router_cmd(router_backend, P["etcd"], P["router"]),
+                                os.path.join(logdir, "e2e_router.log")))
         barrier()
         # cold start: nothing cached from the device-timed window
-        ev_ep = f"tcp://127.0.0.1:{EVENTS_PORT0 + rank}"
+        ev_ep = f"tcp://127.0.0.1:{P['events0'] + rank}"
         pub = KvEventPublisher(ev_ep)
         engine.set_event_sink(pub)
         engine.bm.clear_cache()
@@ -114,21 +119,21 @@ def run_e2e_fleet(engine, *, model: str, rank: int, world: int, barrier, session
         th = threading.Thread(target=srv.run, kwargs={"should_stop": stop.is_set}, name="engine-core",
                               daemon=True)
         th.start()
-        port = WORKER_PORT0 + rank
+        port = P["worker0"] + rank
         worker = _spawn([sys.executable, "-m", "infera_b200.engine.worker", "--attach-core", f"{in_addr},{out_addr}",
                          "--model", model, "--served-model-name", model, "--host", "127.0.0.1", "--port", str(port),
-                         "--etcd-endpoint", f"127.0.0.1:{ETCD_PORT}", "--kv-events-endpoint", ev_ep,
+                         "--etcd-endpoint", f"127.0.0.1:{P['etcd']}", "--kv-events-endpoint", ev_ep,
                          "--page-size", str(engine.bm.page_size), "--log-level", "warning"],
                         os.path.join(logdir, f"e2e_worker{rank}.log"))
         if rank == 0:
-            ok = _wait_http(f"http://127.0.0.1:{ROUTER_PORT}/v1/workers",
-                            lambda r: len(r.json().get("workers", [])) >= world, 300)
+            ok = _wait_http(f"http://127.0.0.1:{P['router']}/v1/workers",
+                            lambda r: len(r.json().get("workers", [])) >= world, appear_timeout)
             if not ok:
                 raise RuntimeError("e2e: workers did not appear at the router")
         barrier()
         h2d0, d2h0 = engine.runner.h2d_bytes, engine.runner.d2h_bytes
         it0 = engine.num_steps
-        cmd = [sys.executable, "-m", "infera_b200.bench.http_loadgen", "--url", f"http://127.0.0.1:{ROUTER_PORT}",
+        cmd = [sys.executable, "-m", "infera_b200.bench.http_loadgen", "--url", f"http://127.0.0.1:{P['router']}",
                "--model", model, "--sessions", f"{sessions.start}:{sessions.stop}", "--rate", str(rate),
                "--duration", str(warmup_s + timed_s), "--seed", str(seed), "--drain-s", str(drain_s),
                "--trace", trace]
