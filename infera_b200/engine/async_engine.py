@@ -84,6 +84,11 @@ class AsyncEngine:
                 self.inflight -= 1
 
     def _loop(self) -> None:
+        dev = getattr(self.engine, "device", None)
+        if dev is not None and dev.type == "cuda":
+            import torch
+
+            torch.cuda.set_device(dev)  # the CUDA current device is per thread
         while self._running:
             try:
                 block = not self.engine.has_unfinished()

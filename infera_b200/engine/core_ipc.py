@@ -209,6 +209,11 @@ class EngineCoreServer:
         return not self._stop
 
     def run(self, should_stop=None) -> None:
+        dev = getattr(getattr(self.engine, "engine", self.engine), "device", None)
+        if dev is not None and dev.type == "cuda":
+            import torch
+
+            torch.cuda.set_device(dev)  # per-thread state: this loop may run on a fresh thread
         while self.run_once():
             if should_stop is not None and should_stop():
                 break

@@ -177,6 +177,11 @@ class LLMEngine:
         return idx, val
 
     def step(self) -> list[RequestOutput]:
+        # the CUDA current device is per host thread: a step driven from a
+        # thread that never selected this engine's GPU would launch the
+        # kernels on the wrong device with this device's pointers
+        if self.device.type == "cuda" and torch.cuda.current_device() != self.device.index:
+            torch.cuda.set_device(self.device)
         sched = self.scheduler.schedule()
         outputs: list[RequestOutput] = []
         for r in sched.preempted:

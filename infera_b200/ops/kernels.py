@@ -65,6 +65,11 @@ def scratch(device: torch.device | int | None = None) -> DeviceScratch:
     elif isinstance(device, int):
         device = torch.device("cuda", device)
     idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx != torch.cuda.current_device():
+        # launches go to the current device's stream: refuse instead of
+        # faulting on another device's pointers
+        raise RuntimeError(f"tensors on cuda:{idx} but this thread's current device is "
+                           f"cuda:{torch.cuda.current_device()} (call torch.cuda.set_device first)")
     s = _scratch.get(idx)
     if s is None:
         dev = torch.device("cuda", idx)
