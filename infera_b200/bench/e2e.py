@@ -80,7 +80,7 @@ def router_cmd(backend: str, etcd_port: int = ETCD_PORT, router_port: int = ROUT
     return [sys.executable, "-m", "infera_b200.server", "--discovery-backend", "etcd",
             "--etcd-endpoint", f"127.0.0.1:{etcd_port}", "--router-policy", "kv-aware",
             "--router-backend", backend, "--host", "127.0.0.1", "--port", str(router_port),
-            "--log-level", "warning"]
+            "--log-level", os.environ.get("INFERA_E2E_LOG_LEVEL", "warning")]
 
 
 def run_e2e_fleet(engine, *, model: str, rank: int, world: int, barrier, sessions: range, rate: float,
@@ -123,7 +123,7 @@ def run_e2e_fleet(engine, *, model: str, rank: int, world: int, barrier, session
         worker = _spawn([sys.executable, "-m", "infera_b200.engine.worker", "--attach-core", f"{in_addr},{out_addr}",
                          "--model", model, "--served-model-name", model, "--host", "127.0.0.1", "--port", str(port),
                          "--etcd-endpoint", f"127.0.0.1:{P['etcd']}", "--kv-events-endpoint", ev_ep,
-                         "--page-size", str(engine.bm.page_size), "--log-level", "warning"],
+                         "--page-size", str(engine.bm.page_size), "--log-level", os.environ.get("INFERA_E2E_LOG_LEVEL", "warning")],
                         os.path.join(logdir, f"e2e_worker{rank}.log"))
         if rank == 0:
             ok = _wait_http(f"http://127.0.0.1:{P['router']}/v1/workers",

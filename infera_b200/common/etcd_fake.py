@@ -54,6 +54,9 @@ class EtcdState:
         self.next_lease = 7587000000000000000
         self.watchers: list[tuple[bytes, bytes, asyncio.Queue, asyncio.AbstractEventLoop]] = []
         self.lock = threading.RLock()
+        # (revision, event) history, so a watch can start from a past revision
+        self.history: list[tuple[int, dict]] = []
+        self.history_cap = 100000
 
     # --------------------------------------------------------------- helpers
     @staticmethod
@@ -65,6 +68,10 @@ class EtcdState:
         return key <= k < end
 
     def _notify(self, events: list[dict]) -> None:
+        for e in events:
+            self.history.append((self.rev, e))
+        if len(self.history) > self.history_cap:
+            del self.history[: len(self.history) - self.history_cap]
         for key, end, q, loop in list(self.watchers):
             evs = [e for e in events if self._in_range(_b64d(e["kv"]["key"]), key, end)]
             if evs:
@@ -202,7 +209,14 @@ def build_app(state: EtcdState | None = None) -> FastAPI:
         key, end = _b64d(cr.get("key")), _b64d(cr.get("range_end"))
         q: asyncio.Queue = asyncio.Queue()
         entry = (key, end, q, asyncio.get_running_loop())
-        st.watchers.append(entry)
+        start = int(cr.get("start_revision", 0) or 0)
+        with st.lock:
+            # replay what happened since start_revision (as etcd does), then go live
+            if start > 0:
+                past = [e for rev, e in st.history if rev >= start and st._in_range(_b64d(e["kv"]["key"]), key, end)]
+                if past:
+                    q.put_nowait({"result": {"header": st.header(), "events": past}})
+            st.watchers.append(entry)
 
         async def gen():
             try:

@@ -52,3 +52,62 @@ extern "C" int ib_kv_page_copy(void* k_cache, void* v_cache, void* chunk, const 
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
+
+// ---------------------------------------------------------------------------
+// Prefill -> decode KV push (PD disaggregation over NVLink).
+//
+// Copies whole pages of layers [l0, l1) from this instance's caches into
+// another instance's caches (dst_* are CUDA-IPC mappings of the decode
+// instance's [L, slots, H] tensors on a peer GPU, or local pointers when both
+// instances share a GPU): dst_c[l, dst_pages[p]*16 + i, :] =
+// src_c[l, src_pages[p]*16 + i, :]. One CTA per (page, layer, channel);
+// 16-byte loads from local HBM, 16-byte stores over NVLink (plain peer
+// stores, no multicast). Called per layer as the prefill finishes it, or once
+// for the whole range.
+namespace ib200 {
+namespace kvp {
+
+__global__ void __launch_bounds__(256) kv_push_kernel(const uint4* __restrict__ src_k, const uint4* __restrict__ src_v,
+                                                      uint4* __restrict__ dst_k, uint4* __restrict__ dst_v,
+                                                      const int* __restrict__ src_pages,
+                                                      const int* __restrict__ dst_pages, int l0,
+                                                      long long src_slots, long long dst_slots, int vec_per_token) {
+  const int p = blockIdx.x, l = l0 + blockIdx.y, c = blockIdx.z;
+  const uint4* src = c == 0 ? src_k : src_v;
+  uint4* dst = c == 0 ? dst_k : dst_v;
+  const long long n = 16ll * vec_per_token;
+  const uint4* s = src + (static_cast<long long>(l) * src_slots + static_cast<long long>(src_pages[p]) * 16) *
+                             vec_per_token;
+  uint4* d = dst + (static_cast<long long>(l) * dst_slots + static_cast<long long>(dst_pages[p]) * 16) *
+                       vec_per_token;
+  // four independent 16-byte transfers in flight per thread
+  long long i = threadIdx.x;
+  for (; i + 3 * blockDim.x < n; i += 4 * blockDim.x) {
+    const uint4 a = __ldg(s + i), b = __ldg(s + i + blockDim.x), e = __ldg(s + i + 2 * blockDim.x),
+                f = __ldg(s + i + 3 * blockDim.x);
+    d[i] = a;
+    d[i + blockDim.x] = b;
+    d[i + 2 * blockDim.x] = e;
+    d[i + 3 * blockDim.x] = f;
+  }
+  for (; i < n; i += blockDim.x) d[i] = __ldg(s + i);
+}
+
+}  // namespace kvp
+}  // namespace ib200
+
+// src_*: this instance's caches [L, src_slots, H]; dst_*: the receiver's
+// caches [L, dst_slots, H] (peer or local pointers); pages: int32 device
+// arrays of n_pages each. Layers [l0, l1). H * elem_bytes % 16 == 0.
+extern "C" int ib_kv_push_pages(const void* src_k, const void* src_v, void* dst_k, void* dst_v, const int* src_pages,
+                                const int* dst_pages, int n_pages, int l0, int l1, long long src_slots,
+                                long long dst_slots, int H, int elem_bytes, cudaStream_t stream) {
+  if (n_pages <= 0 || l1 <= l0) return 0;
+  if ((H * elem_bytes) % 16 != 0) return -1;
+  dim3 grid(n_pages, l1 - l0, 2);
+  ib200::kvp::kv_push_kernel<<<grid, 256, 0, stream>>>(
+      static_cast<const uint4*>(src_k), static_cast<const uint4*>(src_v), static_cast<uint4*>(dst_k),
+      static_cast<uint4*>(dst_v), src_pages, dst_pages, l0, src_slots, dst_slots, H * elem_bytes / 16);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}

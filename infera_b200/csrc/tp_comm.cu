@@ -239,3 +239,14 @@ extern "C" int ib_can_access_peer(int dev, int peer) {
   cudaDeviceCanAccessPeer(&ok, dev, peer);
   return ok;
 }
+
+// Let kernels on the current device access `peer`'s memory directly (one
+// process driving two GPUs). Already-enabled counts as success.
+extern "C" int ib_enable_peer_access(int peer) {
+  cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    return 0;
+  }
+  return static_cast<int>(e);
+}

@@ -417,6 +417,8 @@ def main(argv=None) -> None:
     p.add_argument("--kv-events-endpoint", default=None)
     p.add_argument("--kv-tier", default=None)
     p.add_argument("--tp-size", type=int, default=1, help="tensor-parallel ranks (RANK / LOCAL_RANK / MASTER_* from env)")
+    p.add_argument("--disagg-mode", choices=("mixed", "prefill", "decode"), default="mixed")
+    p.add_argument("--kv-push-endpoint", default=None)
     a = p.parse_args(argv)
     from infera_b200.engine.kv_events import KvEventPublisher
     from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
@@ -431,7 +433,8 @@ def main(argv=None) -> None:
     pub = KvEventPublisher(a.kv_events_endpoint) if a.kv_events_endpoint and rank == 0 else None
     cfg = EngineConfig(model=a.model, page_size=a.page_size, max_num_seqs=a.max_num_seqs,
                        max_batched_tokens=a.max_batched_tokens, gpu_memory_utilization=a.gpu_memory_utilization,
-                       num_pages=a.num_pages, use_cuda_graphs=not a.no_cuda_graphs, seed=a.seed, kv_tier=a.kv_tier)
+                       num_pages=a.num_pages, use_cuda_graphs=not a.no_cuda_graphs, seed=a.seed, kv_tier=a.kv_tier,
+                       disagg_mode=a.disagg_mode, kv_push_endpoint=a.kv_push_endpoint)
     eng = LLMEngine(cfg, device=device, event_sink=pub, tp=tp)
     if rank > 0:
         from infera_b200.engine.tp_engine import follower_loop

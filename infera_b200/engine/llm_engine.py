@@ -56,6 +56,10 @@ class EngineConfig:
     # KV tiering: None (off), "host:<GiB>[:<nvme dir>]" (in-process host store,
     # optional NVMe tablespace) or "kvd:<socket path>" (shared daemon)
     kv_tier: str | None = None
+    # prefill/decode disaggregation: "mixed", "prefill" or "decode"; a decode
+    # instance serves its KV rendezvous on kv_push_endpoint
+    disagg_mode: str = "mixed"
+    kv_push_endpoint: str | None = None
 
 
 class LLMEngine:
@@ -96,6 +100,15 @@ class LLMEngine:
             self.tier = TierManager(self.runner.k_cache, self.runner.v_cache, _tier_store(cfg.kv_tier),
                                     cfg.page_size)
             self.bm.tier = self.tier
+        self.pd_rendezvous = None
+        self.pd_agent = None
+        if cfg.disagg_mode == "decode":
+            from infera_b200.engine.pd import PDRendezvous
+
+            ep = cfg.kv_push_endpoint or f"local://{id(self)}"
+            self.pd_rendezvous = PDRendezvous(self, ep)
+            self.scheduler.on_park = lambda r, pages, skip, n: self.pd_rendezvous.publish(
+                r.remote_room, r.request_id, [int(x) for x in pages], skip, n)
         self.requests: dict[str, Request] = {}
         # commands applied since the last step, when a tensor-parallel leader
         # replays them on its followers (None: not recorded)
@@ -138,6 +151,11 @@ class LLMEngine:
         req = Request(request_id=request_id, prompt_token_ids=list(prompt_token_ids),
                       sampling=sampling or SamplingParams(), eos_token_id=self.model_cfg.eos_token_id)
         req.arrival_time = self.clock() if arrival_time is None else arrival_time
+        ktp = req.sampling.kv_transfer or {}
+        if ktp.get("do_remote_prefill") and self.pd_rendezvous is not None and "room" in ktp:
+            req.remote_room = int(ktp["room"])
+        if ktp.get("do_remote_decode") and ktp.get("decode_kv_endpoint") and "room" in ktp:
+            req.remote_decode = (int(ktp["room"]), str(ktp["decode_kv_endpoint"]))
         self.requests[request_id] = req
         self.scheduler.add(req)
         if self.cmd_log is not None:
@@ -154,7 +172,22 @@ class LLMEngine:
         return False
 
     def has_unfinished(self) -> bool:
-        return self.scheduler.num_unfinished() > 0
+        return self.scheduler.num_unfinished() > 0 or (self.pd_agent is not None and self.pd_agent.pending() > 0)
+
+    # ------------------------------------------------------------------ PD
+    def _pd_progress(self) -> None:
+        if self.pd_agent is not None and self.pd_agent.pending():
+            self.pd_agent.progress()
+        if self.pd_rendezvous is not None and self.scheduler.parked:
+            for r in list(self.scheduler.parked.values()):
+                st = self.pd_rendezvous.poll(r.remote_room)
+                if st != "pending":
+                    self.scheduler.resume_parked(r, st == "ok")
+
+    def _release_pushed(self, job) -> None:
+        if job.blocks is not None:
+            self.bm.free(job.blocks)
+            job.blocks = None
 
     def num_running(self) -> int:
         return len(self.scheduler.running)
@@ -182,6 +215,8 @@ class LLMEngine:
         # kernels on the wrong device with this device's pointers
         if self.device.type == "cuda" and torch.cuda.current_device() != self.device.index:
             torch.cuda.set_device(self.device)
+        if self.pd_agent is not None or self.pd_rendezvous is not None:
+            self._pd_progress()
         sched = self.scheduler.schedule()
         outputs: list[RequestOutput] = []
         for r in sched.preempted:
@@ -190,6 +225,8 @@ class LLMEngine:
             else:
                 self.counters["preemptions"] += 1
         if sched.empty:
+            if self.scheduler.parked or (self.pd_agent is not None and self.pd_agent.pending()):
+                time.sleep(0.0005)  # only waiting on a KV push
             return outputs
         upd = self._block_table_updates(sched.prefills + sched.decodes)
         res = self.runner.execute(sched, upd)
@@ -223,7 +260,17 @@ class LLMEngine:
         return outputs
 
     def _finish(self, r: Request, st: Status, new: list[int] | None = None) -> RequestOutput:
-        self.scheduler.finish(r, st)
+        if r.remote_decode is not None and r.num_computed >= len(r.prompt_token_ids) - 1:
+            # PD prefill: hold the prompt's pages until they are pushed
+            from infera_b200.engine.pd import PDPushAgent, PushJob
+
+            held = self.scheduler.finish(r, st, hold_blocks=True)
+            if self.pd_agent is None:
+                self.pd_agent = PDPushAgent(self)
+            room, ep = r.remote_decode
+            self.pd_agent.submit(PushJob(r.request_id, room, ep, held))
+        else:
+            self.scheduler.finish(r, st)
         r.finish_time = self.clock()
         self.requests.pop(r.request_id, None)
         self.counters["finished"] += 1
@@ -261,5 +308,10 @@ class LLMEngine:
             "steps": self.num_steps,
             "h2d_bytes": self.runner.h2d_bytes,
             "d2h_bytes": self.runner.d2h_bytes,
+            "pd_push_queue": self.pd_agent.pending() if self.pd_agent is not None else 0,
+            "pd_pushes": self.pd_agent.stats["pushes"] if self.pd_agent is not None else 0,
+            "pd_push_bytes": self.pd_agent.stats["bytes"] if self.pd_agent is not None else 0,
+            "pd_push_seconds": self.pd_agent.stats["push_s"] if self.pd_agent is not None else 0.0,
+            "pd_parked": len(self.scheduler.parked),
             **self.counters,
         }

@@ -1,0 +1,328 @@
+"""Prefill/decode disaggregation between two engine instances: the
+``b200-nvlink-push`` protocol, engine side.
+
+The router sends the same request to a prefill instance (one output token,
+``kv_transfer_params = {do_remote_decode, room, decode_kv_endpoint}``) and
+to a decode instance (the remaining tokens, ``{do_remote_prefill, room}``).
+
+Decode instance (:class:`PDRendezvous`): on admission of a remote-prefill
+request it allocates KV pages for the prompt minus its last token (reusing
+any prefix it already caches), parks the request, and publishes
+``room -> (page ids beyond the cached prefix, number of cached tokens)``.
+It serves, on its KV endpoint (ZMQ REP, msgpack):
+
+    {"op": "describe"} -> CUDA-IPC handles (+ offsets) of its K / V caches,
+                          slots per layer, layers, pid, device
+    {"op": "pages", "room"} -> {"ready", "pages", "skip_tokens", "n_tokens"}
+    {"op": "done", "room", "ok"} -> ack; the parked request resumes with the
+                          pushed tokens counted as computed (or, if not ok,
+                          computes its prompt itself)
+
+Prefill instance (:class:`PDPushAgent`): when a remote-decode request has
+computed its prompt, its pages are held (not freed) until the push ends;
+between engine steps the agent gets the room's page list, maps the decode
+caches once per endpoint (CUDA IPC; plain pointers when both instances
+live in one process), and the engine launches ``ib_kv_push_pages`` on its
+stream (peer stores over NVLink); when the copy's event completes it sends
+``done`` and releases the pages. A room that never becomes ready within
+``timeout_s`` is dropped (the decode side times out too and recomputes).
+
+Protocol role of ``infera/router/disagg_protocols`` + the engines' KV
+connectors (Mooncake / MoRI / NIXL in the reference); the transport here is
+this framework's own NVLink page push.
+"""
+
+from __future__ import annotations
+
+import logging
+import os
+import threading
+import time
+from dataclasses import dataclass, field
+
+import msgpack
+import torch
+
+logger = logging.getLogger(__name__)
+
+# endpoint -> decode engine, for instances sharing one process (tests, 1-GPU demos)
+_LOCAL: dict[str, object] = {}
+
+
+def _pack(o) -> bytes:
+    return msgpack.packb(o, use_bin_type=True)
+
+
+def _unpack(b: bytes):
+    return msgpack.unpackb(b, raw=False)
+
+
+def _ipc_handle(t: torch.Tensor) -> tuple[bytes, int]:
+    """(cudaIpcMemHandle of the allocation holding ``t``, byte offset of ``t`` in it)."""
+    st = t.untyped_storage()
+    info = st._share_cuda_()
+    handle, offset = info[1], info[3]
+    return bytes(handle), int(offset) + t.storage_offset() * t.element_size()
+
+
+# --------------------------------------------------------------------------- decode side
+
+
+@dataclass
+class Room:
+    room: int
+    rid: str
+    pages: list[int]
+    skip_tokens: int
+    n_tokens: int
+    created: float = field(default_factory=time.monotonic)
+    done: bool = False
+    ok: bool = False
+
+
+class PDRendezvous:
+    def __init__(self, engine, endpoint: str, timeout_s: float = 30.0):
+        self.engine = engine
+        self.endpoint = endpoint
+        self.timeout_s = timeout_s
+        self.rooms: dict[int, Room] = {}
+        self.lock = threading.Lock()
+        self._stop = False
+        self.stats = {"rooms": 0, "done": 0, "failed": 0, "timeouts": 0}
+        _LOCAL[endpoint] = engine
+        self._th = threading.Thread(target=self._serve, name="pd-rendezvous", daemon=True)
+        self._th.start()
+
+    # called by the engine thread
+    def publish(self, room: int, rid: str, pages: list[int], skip_tokens: int, n_tokens: int) -> None:
+        with self.lock:
+            self.rooms[room] = Room(room, rid, pages, skip_tokens, n_tokens)
+            self.stats["rooms"] += 1
+
+    def poll(self, room: int) -> str:
+        """pending / ok / failed / timeout"""
+        with self.lock:
+            r = self.rooms.get(room)
+            if r is None:
+                return "failed"
+            if r.done:
+                self.rooms.pop(room, None)
+                return "ok" if r.ok else "failed"
+            if time.monotonic() - r.created > self.timeout_s:
+                self.rooms.pop(room, None)
+                self.stats["timeouts"] += 1
+                return "timeout"
+            return "pending"
+
+    def forget(self, room: int) -> None:
+        with self.lock:
+            self.rooms.pop(room, None)
+
+    def describe(self) -> dict:
+        run = self.engine.runner
+        d = {"pid": os.getpid(), "layers": int(run.k_cache.shape[0]), "slots": int(run.k_cache.shape[1]),
+             "H": int(run.k_cache.shape[2]), "device": run.k_cache.device.index if run.k_cache.is_cuda else -1}
+        if run.k_cache.is_cuda:
+            d["k"], d["k_off"] = _ipc_handle(run.k_cache)
+            d["v"], d["v_off"] = _ipc_handle(run.v_cache)
+        return d
+
+    def handle(self, msg: dict) -> dict:
+        op = msg.get("op")
+        if op == "describe":
+            return self.describe()
+        if op == "pages":
+            with self.lock:
+                r = self.rooms.get(int(msg["room"]))
+                if r is None:
+                    return {"ready": False}
+                return {"ready": True, "pages": r.pages, "skip_tokens": r.skip_tokens, "n_tokens": r.n_tokens}
+        if op == "done":
+            with self.lock:
+                r = self.rooms.get(int(msg["room"]))
+                if r is not None:
+                    r.done, r.ok = True, bool(msg.get("ok"))
+                    self.stats["done" if r.ok else "failed"] += 1
+            return {"ack": True}
+        return {"error": f"unknown op {op!r}"}
+
+    def _serve(self) -> None:
+        if not self.endpoint.startswith(("ipc://", "tcp://")):
+            return  # in-process only
+        import zmq
+
+        sock = zmq.Context.instance().socket(zmq.REP)
+        sock.bind(self.endpoint)
+        poller = zmq.Poller()
+        poller.register(sock, zmq.POLLIN)
+        while not self._stop:
+            if not poller.poll(200):
+                continue
+            try:
+                req = _unpack(sock.recv())
+                sock.send(_pack(self.handle(req)))
+            except Exception as e:  # keep serving
+                logger.warning("pd rendezvous: %s", e)
+                try:
+                    sock.send(_pack({"error": str(e)}))
+                except Exception:
+                    pass
+        sock.close(linger=0)
+
+    def close(self) -> None:
+        self._stop = True
+        _LOCAL.pop(self.endpoint, None)
+
+
+# --------------------------------------------------------------------------- prefill side
+
+
+@dataclass
+class PushJob:
+    rid: str
+    room: int
+    endpoint: str
+    blocks: object              # SeqBlocks held until the push ends
+    created: float = field(default_factory=time.monotonic)
+    plan: dict | None = None    # page list from the decode side
+    event: object = None        # CUDA event of the launched copy
+    launched_at: float = 0.0
+
+
+class _Peer:
+    """Where a decode instance's caches are, seen from this process."""
+
+    def __init__(self, endpoint: str, engine_device: torch.device):
+        self.endpoint = endpoint
+        self.local = _LOCAL.get(endpoint)
+        self.sock = None
+        self.k = self.v = None
+        self.slots = 0
+        if self.local is not None:
+            self.k, self.v = self.local.runner.k_cache, self.local.runner.v_cache
+            self.slots = self.k.shape[1]
+            if self.k.is_cuda and self.k.device != engine_device:
+                # one process driving both GPUs: map the peer directly
+                from infera_b200.ops import _native
+
+                _native.check(_native.kernels().ib_enable_peer_access(self.k.device.index),
+                              f"enable peer access to {self.k.device}")
+                self.k, self.v = self.k.data_ptr(), self.v.data_ptr()
+
+    def call(self, msg: dict, timeout_ms: int = 2000) -> dict:
+        if self.local is not None:
+            return self.local.pd_rendezvous.handle(msg)
+        import zmq
+
+        if self.sock is None:
+            self.sock = zmq.Context.instance().socket(zmq.REQ)
+            self.sock.setsockopt(zmq.RCVTIMEO, timeout_ms)
+            self.sock.setsockopt(zmq.SNDTIMEO, timeout_ms)
+            self.sock.setsockopt(zmq.LINGER, 0)
+            self.sock.connect(self.endpoint)
+        try:
+            self.sock.send(_pack(msg))
+            return _unpack(self.sock.recv())
+        except zmq.Again:
+            self.sock.close(linger=0)  # a REQ socket is stuck after a timeout
+            self.sock = None
+            raise TimeoutError(f"pd endpoint {self.endpoint} did not answer")
+
+    def map(self) -> None:
+        if self.k is not None:
+            return
+        d = self.call({"op": "describe"})
+        self.slots = d["slots"]
+        if d["pid"] == os.getpid():
+            raise RuntimeError("same-process decode engine not registered locally")
+        from infera_b200.ops import _native
+        import ctypes
+
+        lib = _native.kernels()
+        ptrs = []
+        for key in ("k", "v"):
+            p = ctypes.c_void_p()
+            buf = (ctypes.c_char * 64).from_buffer_copy(d[key])
+            _native.check(lib.ib_ipc_open(buf, ctypes.byref(p)), "ib_ipc_open(decode KV cache)")
+            ptrs.append(p.value + d[key + "_off"])
+        self.k, self.v = ptrs
+
+
+class PDPushAgent:
+    def __init__(self, engine, timeout_s: float = 30.0):
+        self.engine = engine
+        self.timeout_s = timeout_s
+        self.jobs: list[PushJob] = []
+        self.peers: dict[str, _Peer] = {}
+        self.stats = {"pushes": 0, "pages": 0, "bytes": 0, "timeouts": 0, "push_s": 0.0}
+
+    def submit(self, job: PushJob) -> None:
+        self.jobs.append(job)
+
+    def pending(self) -> int:
+        return len(self.jobs)
+
+    def _peer(self, ep: str) -> _Peer:
+        p = self.peers.get(ep)
+        if p is None:
+            p = self.peers[ep] = _Peer(ep, self.engine.device)
+        return p
+
+    def progress(self) -> None:
+        """Called by the engine thread between steps; never blocks for long."""
+        from infera_b200.ops import kernels as K
+
+        eng = self.engine
+        keep = []
+        for j in self.jobs:
+            peer = self._peer(j.endpoint)
+            try:
+                if j.event is None:
+                    if j.plan is None:
+                        r = peer.call({"op": "pages", "room": j.room}, timeout_ms=200)
+                        if r.get("ready"):
+                            j.plan = r
+                    if j.plan is not None:
+                        peer.map()
+                        skip = j.plan["skip_tokens"] // eng.bm.page_size
+                        n_tok = j.plan["n_tokens"]
+                        n_pages = (n_tok + eng.bm.page_size - 1) // eng.bm.page_size - skip
+                        dst = j.plan["pages"][:n_pages]
+                        src = j.blocks.pages[skip:skip + len(dst)]
+                        dev = eng.runner.k_cache.device
+                        sp = torch.tensor(src, dtype=torch.int32, device=dev)
+                        dp = torch.tensor(dst, dtype=torch.int32, device=dev)
+                        K.kv_push_pages(eng.runner.k_cache, eng.runner.v_cache, peer.k, peer.v, sp, dp,
+                                        dst_slots=peer.slots)
+                        j.launched_at = time.monotonic()
+                        if eng.runner.k_cache.is_cuda:
+                            j.event = torch.cuda.Event()
+                            j.event.record()
+                        else:
+                            j.event = True
+                        j._tensors = (sp, dp)
+                        self.stats["pages"] += len(dst)
+                        L, _, H = eng.runner.k_cache.shape
+                        self.stats["bytes"] += 2 * len(dst) * eng.bm.page_size * L * H * eng.runner.k_cache.element_size()
+                if j.event is not None and (j.event is True or j.event.query()):
+                    peer.call({"op": "done", "room": j.room, "ok": True})
+                    self.stats["pushes"] += 1
+                    self.stats["push_s"] += time.monotonic() - j.launched_at
+                    eng._release_pushed(j)
+                    continue
+            except TimeoutError:
+                pass
+            except Exception as e:
+                logger.warning("kv push for room %s failed: %s", j.room, e)
+                try:
+                    peer.call({"op": "done", "room": j.room, "ok": False})
+                except Exception:
+                    pass
+                eng._release_pushed(j)
+                continue
+            if j.event is None and time.monotonic() - j.created > self.timeout_s:
+                self.stats["timeouts"] += 1
+                eng._release_pushed(j)
+                continue
+            keep.append(j)
+        self.jobs = keep

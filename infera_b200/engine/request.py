@@ -20,6 +20,9 @@ class SamplingParams:
     # retention hint from the router (none / ephemeral / short / long); the
     # engine uses it to order prefix-cache eviction and tier spills
     retention: str | None = None
+    # prefill/decode disaggregation parameters from the router
+    # (kv_transfer_params of the b200-nvlink-push protocol)
+    kv_transfer: dict | None = None
 
 
 class Status(enum.Enum):
@@ -54,6 +57,10 @@ class Request:
     token_times: list[float] = field(default_factory=list)
     finish_time: float | None = None
     num_cached_prompt_tokens: int = 0
+    # PD: decode side waits for room ``remote_room``'s pushed KV; prefill side
+    # pushes to (room, decode endpoint) once its prompt is computed
+    remote_room: int | None = None
+    remote_decode: tuple | None = None
 
     @property
     def num_tokens(self) -> int:

@@ -62,6 +62,9 @@ class Scheduler:
         self.long_prefill_threshold = long_prefill_threshold
         self.waiting: deque[Request] = deque()
         self.running: list[Request] = []
+        # PD decode side: admitted requests waiting for their pushed KV
+        self.parked: dict[str, Request] = {}
+        self.on_park = None  # fn(request, pages to receive, skip_tokens, n_tokens)
         self.free_rows: list[int] = list(range(max_num_seqs - 1, -1, -1))
 
     # ------------------------------------------------------------------
@@ -69,9 +72,24 @@ class Scheduler:
         self.waiting.append(req)
 
     def num_unfinished(self) -> int:
-        return len(self.waiting) + len(self.running)
+        return len(self.waiting) + len(self.running) + len(self.parked)
+
+    def resume_parked(self, r: Request, pushed_ok: bool) -> None:
+        """The pushed KV arrived (prompt minus its last token now cached) or
+        the push failed (the request computes its prompt itself)."""
+        if self.parked.pop(r.request_id, None) is None:
+            return
+        if pushed_ok:
+            r.num_computed = max(r.num_computed, len(r.prompt_token_ids) - 1)
+        r.status = Status.RUNNING
+        self.running.append(r)
 
     def abort(self, request_id: str) -> Request | None:
+        r = self.parked.pop(request_id, None)
+        if r is not None:
+            self._release(r)
+            r.status = Status.FINISHED_ABORTED
+            return r
         for i, r in enumerate(self.running):
             if r.request_id == request_id:
                 self.running.pop(i)
@@ -94,14 +112,19 @@ class Scheduler:
             r.table_row = -1
         r.pages_synced = 0
 
-    def finish(self, r: Request, status: Status) -> None:
+    def finish(self, r: Request, status: Status, hold_blocks: bool = False):
+        """``hold_blocks``: keep the pages referenced (returned) for a KV push."""
         r.status = status
         if r in self.running:
             self.running.remove(r)
         if r.blocks is not None:
             # make everything computed so far reusable by later turns
             self.bm.commit_full_pages(r.blocks, r.all_token_ids(), r.num_computed)
+        held = None
+        if hold_blocks:
+            held, r.blocks = r.blocks, None
         self._release(r)
+        return held
 
     def _preempt(self, victim: Request, out: SchedulerOutput) -> None:
         self.running.remove(victim)
@@ -178,9 +201,20 @@ class Scheduler:
             r.num_computed = sb.num_cached_tokens
             if r.num_preemptions == 0:
                 r.num_cached_prompt_tokens = sb.num_cached_tokens
-            r.status = Status.RUNNING
             r.table_row = self.free_rows.pop()
             r.pages_synced = 0
+            if r.remote_room is not None and self.on_park is not None and r.num_preemptions == 0:
+                # PD decode: the prefill instance pushes the prompt's KV
+                # (all but the last token) into the pages beyond the prefix
+                # this instance already caches; wait for it
+                n_tok = len(r.prompt_token_ids) - 1
+                skip = min(sb.num_cached_tokens, n_tok) // ps
+                n_pages = (n_tok + ps - 1) // ps
+                r.status = Status.WAITING
+                self.parked[r.request_id] = r
+                self.on_park(r, sb.pages[skip:n_pages], skip * ps, n_tok)
+                continue
+            r.status = Status.RUNNING
             self.running.append(r)
             pending = total - r.num_computed
             n = min(pending, budget)

@@ -36,7 +36,8 @@ def _sampling(body: dict, default_max: int) -> SamplingParams:
     return SamplingParams(max_tokens=int(mt), temperature=float(body.get("temperature") or 0.0),
                           seed=body.get("seed"), stop_token_ids=[int(x) for x in stop_ids],
                           ignore_eos=bool(body.get("ignore_eos", False)), min_tokens=int(body.get("min_tokens", 0)),
-                          retention=ktp.get("infera_retention") or body.get("infera_retention"))
+                          retention=ktp.get("infera_retention") or body.get("infera_retention"),
+                          kv_transfer={k: v for k, v in ktp.items() if k != "infera_retention"} or None)
 
 
 def _sse(obj: dict) -> bytes:
@@ -169,6 +170,10 @@ def build_worker_app(aeng, tokenizer, model_name: str, extra_metrics=None) -> Fa
         g("infera_engine:kv_cache_usage_perc", round(s["kv_usage"], 6), "Fraction of KV pages in use")
         g("infera_engine:prefix_cache_hit_rate", round(s["prefix_hit_rate"], 6), "Prompt tokens served from cache")
         g("infera_engine:pd_push_queue", s.get("pd_push_queue", 0), "KV pushes not yet acknowledged")
+        g("infera_engine:pd_pushes_total", s.get("pd_pushes", 0), "KV pushes completed")
+        g("infera_engine:pd_push_bytes_total", s.get("pd_push_bytes", 0), "KV bytes pushed to decode instances")
+        g("infera_engine:pd_push_seconds_total", round(s.get("pd_push_seconds", 0.0), 6), "Launch-to-done push time")
+        g("infera_engine:pd_parked", s.get("pd_parked", 0), "Requests waiting for pushed KV")
         g("infera_engine:generation_tokens_total", s["generation_tokens"], "Generated tokens")
         g("infera_engine:prompt_tokens_total", s["prompt_tokens"], "Computed prompt tokens")
         # names the reference's drain reader understands

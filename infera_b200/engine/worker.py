@@ -95,6 +95,9 @@ def _core_cmd(args, in_addr: str, out_addr: str) -> list[str]:
         cmd += ["--kv-events-endpoint", args.kv_events_endpoint]
     if args.kv_tier:
         cmd += ["--kv-tier", args.kv_tier]
+    cmd += ["--disagg-mode", args.disagg_mode]
+    if args.kv_push_endpoint:
+        cmd += ["--kv-push-endpoint", args.kv_push_endpoint]
     return cmd
 
 
@@ -109,7 +112,8 @@ async def start_engine(args):
         ecfg = EngineConfig(model=args.model, page_size=args.page_size, max_num_seqs=args.max_num_seqs,
                             max_batched_tokens=args.max_batched_tokens,
                             gpu_memory_utilization=args.gpu_memory_utilization, num_pages=args.num_pages,
-                            use_cuda_graphs=not args.no_cuda_graphs, seed=args.seed, kv_tier=args.kv_tier)
+                            use_cuda_graphs=not args.no_cuda_graphs, seed=args.seed, kv_tier=args.kv_tier,
+                            disagg_mode=args.disagg_mode, kv_push_endpoint=args.kv_push_endpoint)
         eng = LLMEngine(ecfg, device=args.device, event_sink=pub)
         aeng = AsyncEngine(eng)
         aeng.start()
@@ -131,7 +135,16 @@ async def start_engine(args):
     if args.attach_core:
         in_addr, out_addr = args.attach_core.split(",")
         client = EngineCoreClient(in_addr, out_addr)
-        await client.call("ping", timeout=60.0)
+        # the core drops a reply sent before this client's receive socket is
+        # connected: ask again until one arrives
+        t0 = asyncio.get_running_loop().time()
+        while True:
+            try:
+                await client.call("ping", timeout=1.0)
+                break
+            except asyncio.TimeoutError:
+                if asyncio.get_running_loop().time() - t0 > 120:
+                    raise RuntimeError(f"engine core at {in_addr} does not answer")
         st = await client.call("stats")
         info = {"vocab": None, "num_pages": st.get("num_pages")}
         client.mark_ready(info)

@@ -437,7 +437,7 @@ class App {
       const Value* ep = meta_param(d, "kv_endpoint");
       kp.set("decode_kv_endpoint", ep ? *ep : Value());
       pb->set("kv_transfer_params", kp);
-      remaining(*db);
+      // the decode instance recomputes the last prompt token and keeps the full token budget
       Value kd = Value::object();
       kd.set("do_remote_prefill", Value::boolean(true));
       kd.set("room", Value::uinteger(room));

@@ -65,6 +65,8 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_ipc_open": [c_vp, c_vp],
         "ib_ipc_close": [c_vp],
         "ib_can_access_peer": [c_int, c_int],
+        "ib_enable_peer_access": [c_int],
+        "ib_kv_push_pages": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_int, c_int, c_vp],
     }
     for name, args in sig.items():
         fn = getattr(lib, name, None)

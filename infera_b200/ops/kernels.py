@@ -507,3 +507,35 @@ def kv_page_copy(k_cache: torch.Tensor, v_cache: torch.Tensor, chunk: torch.Tens
                                            0 if gather else 1, _stream())
     _native.check(rc, "ib_kv_page_copy")
     _count()
+
+
+def kv_push_pages(src_k: torch.Tensor, src_v: torch.Tensor, dst_k, dst_v, src_pages: torch.Tensor,
+                  dst_pages: torch.Tensor, layers: tuple[int, int] | None = None, dst_slots: int | None = None,
+                  page_size: int = 16) -> None:
+    """Copy whole KV pages of layers [l0, l1) from ``src_*`` ([L, slots, H]
+    tensors) into ``dst_*``: tensors on this device, or raw device pointers
+    (ints, CUDA-IPC mappings of another instance's caches; then
+    ``dst_slots`` is required)."""
+    n = src_pages.shape[0]
+    if n == 0:
+        return
+    L, slots, H = src_k.shape
+    l0, l1 = layers if layers is not None else (0, L)
+    if not src_k.is_cuda:
+        idx_s = (src_pages.long()[:, None] * page_size + torch.arange(page_size)[None, :]).reshape(-1)
+        idx_d = (dst_pages.long()[:, None] * page_size + torch.arange(page_size)[None, :]).reshape(-1)
+        for s, d in ((src_k, dst_k), (src_v, dst_v)):
+            d[l0:l1, idx_d] = s[l0:l1, idx_s]
+        return
+    assert page_size == 16
+    if isinstance(dst_k, torch.Tensor):
+        dst_slots = dst_k.shape[1]
+        dk, dv = dst_k.data_ptr(), dst_v.data_ptr()
+    else:
+        assert dst_slots is not None
+        dk, dv = int(dst_k), int(dst_v)
+    rc = _native.kernels().ib_kv_push_pages(src_k.data_ptr(), src_v.data_ptr(), dk, dv, src_pages.data_ptr(),
+                                            dst_pages.data_ptr(), n, l0, l1, slots, dst_slots, H,
+                                            src_k.element_size(), _stream())
+    _native.check(rc, "ib_kv_push_pages")
+    _count()

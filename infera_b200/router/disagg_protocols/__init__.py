@@ -4,9 +4,10 @@ A protocol is stateless and shared; the router owns connections, retries
 and metrics (interface of ``infera/router/disagg_protocols/base.py:20-91``).
 
 * ``b200-nvlink-push`` (this framework's engines; concurrent): the prefill
-  leg runs for one token and pushes each finished layer's KV pages straight
-  into the decode instance's paged cache over NVLink; the decode leg waits
-  for the per-layer ready flags of its room and decodes the rest.
+  leg computes the prompt (one token) and pushes its KV pages straight into
+  the decode instance's paged cache over NVLink; the decode leg parks until
+  its room's pages arrived, recomputes only the last prompt token and
+  generates the full token budget.
 * body-shaping twins of the reference's protocols, kept so fleets that mix
   engines route identically: ``sglang-bootstrap`` (concurrent),
   ``vllm-mooncake`` (concurrent), ``vllm-mori-write`` (concurrent),
@@ -61,7 +62,9 @@ class NvlinkPushProtocol:
         return out
 
     def annotate_decode(self, body, p, d, room_id, handoff):
-        out = decode_remaining(body)
+        # the decode instance recomputes the last prompt token and samples
+        # every output token itself: the full token budget stays with it
+        out = dict(body)
         out["kv_transfer_params"] = {"do_remote_prefill": True, "room": room_id, "prefill_worker": p.worker_id}
         return out
 

@@ -181,7 +181,7 @@ def test_auto_router_pd_and_empty_pool():
     assert code == 200 and b"[DONE]" in body
     legs = {h: (mt, k) for h, mt, k in seen}
     assert legs["p0"][0] == 1 and legs["p0"][1]["do_remote_decode"]
-    assert legs["d0"][0] == 3 and legs["d0"][1]["do_remote_prefill"]
+    assert legs["d0"][0] == 4 and legs["d0"][1]["do_remote_prefill"]  # decode keeps the full budget
     assert legs["p0"][1]["room"] == legs["d0"][1]["room"]
 
 

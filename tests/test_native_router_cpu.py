@@ -157,7 +157,7 @@ def test_pd_nvlink_push_shaping(binary, tmp_path):
     assert pb["max_tokens"] == 1 and pb["stream"] is False
     assert pb["kv_transfer_params"]["do_remote_decode"] is True
     assert pb["kv_transfer_params"]["decode_kv_endpoint"] == "ipc://decode-pool"
-    assert db["max_tokens"] == 9 and db["stream"] is True
+    assert db["max_tokens"] == 10 and db["stream"] is True
     assert db["kv_transfer_params"]["room"] == pb["kv_transfer_params"]["room"]
     assert db["kv_transfer_params"]["infera_retention"] == "long"
     # auto mode ignores gateway headers: that request was routed as a PD pair too

