@@ -34,6 +34,10 @@ import os
 import sys
 import time
 
+# stdout carries exactly one JSON line: NCCL's own messages (the version
+# banner when NCCL_DEBUG is set) go to stderr
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
