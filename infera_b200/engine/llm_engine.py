@@ -92,7 +92,7 @@ class LLMEngine:
                                    watermark_pages=max(1, num_pages // 100),
                                    long_prefill_threshold=cfg.long_prefill_threshold)
         self.runner = ModelRunner(self.model, num_pages, cfg.page_size, cfg.max_num_seqs, cfg.max_batched_tokens,
-                                  use_graphs=cfg.use_cuda_graphs)
+                                  use_graphs=cfg.use_cuda_graphs, exportable=cfg.disagg_mode == "decode")
         self.tier = None
         if cfg.kv_tier:
             from infera_b200.engine.tiering import TierManager

@@ -35,7 +35,8 @@ class StepResult:
 
 class ModelRunner:
     def __init__(self, model: DenseModel, num_pages: int, page_size: int, max_num_seqs: int,
-                 max_batched_tokens: int, use_graphs: bool = True, graph_sizes: list[int] | None = None):
+                 max_batched_tokens: int, use_graphs: bool = True, graph_sizes: list[int] | None = None,
+                 exportable: bool = False):
         self.model = model
         cfg = model.cfg
         self.cfg = cfg
@@ -49,8 +50,17 @@ class ModelRunner:
         # KV cache: [layers, slots, kv_size] for K and for V, zero-initialised so
         # that padding pages always hold finite values
         slots = num_pages * page_size
-        self.k_cache = torch.zeros(cfg.num_layers, slots, cfg.kv_size, dtype=torch.bfloat16, device=self.dev)
-        self.v_cache = torch.zeros(cfg.num_layers, slots, cfg.kv_size, dtype=torch.bfloat16, device=self.dev)
+        shape = (cfg.num_layers, slots, cfg.kv_size)
+        if exportable and self.on_gpu:
+            # own cudaMalloc allocations: exportable whole with CUDA IPC
+            # (the decode side of a PD pair maps them into prefill processes)
+            from infera_b200.parallel.symmem import device_tensor
+
+            self.k_cache, self._k_buf = device_tensor(shape, torch.bfloat16, self.dev)
+            self.v_cache, self._v_buf = device_tensor(shape, torch.bfloat16, self.dev)
+        else:
+            self.k_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.dev)
+            self.v_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.dev)
         self.block_table = torch.zeros(max_num_seqs + 1, self.max_pages, dtype=torch.int32, device=self.dev)
         self.dummy_row = max_num_seqs
         self.bufs = model.alloc_buffers(self.max_tokens, max(max_num_seqs, 1))

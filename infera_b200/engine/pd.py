@@ -89,6 +89,7 @@ class PDRendezvous:
         self.lock = threading.Lock()
         self._stop = False
         self.stats = {"rooms": 0, "done": 0, "failed": 0, "timeouts": 0}
+        self._describe = self._make_describe()
         _LOCAL[endpoint] = engine
         self._th = threading.Thread(target=self._serve, name="pd-rendezvous", daemon=True)
         self._th.start()
@@ -118,14 +119,22 @@ class PDRendezvous:
         with self.lock:
             self.rooms.pop(room, None)
 
-    def describe(self) -> dict:
+    def _make_describe(self) -> dict:
         run = self.engine.runner
         d = {"pid": os.getpid(), "layers": int(run.k_cache.shape[0]), "slots": int(run.k_cache.shape[1]),
              "H": int(run.k_cache.shape[2]), "device": run.k_cache.device.index if run.k_cache.is_cuda else -1}
+        kb = getattr(run, "_k_buf", None)
         if run.k_cache.is_cuda:
-            d["k"], d["k_off"] = _ipc_handle(run.k_cache)
-            d["v"], d["v_off"] = _ipc_handle(run.v_cache)
+            if kb is not None:  # own allocations: whole-buffer handles at offset 0
+                d["k"], d["k_off"] = kb.ipc_handle(), 0
+                d["v"], d["v_off"] = run._v_buf.ipc_handle(), 0
+            else:
+                d["k"], d["k_off"] = _ipc_handle(run.k_cache)
+                d["v"], d["v_off"] = _ipc_handle(run.v_cache)
         return d
+
+    def describe(self) -> dict:
+        return self._describe
 
     def handle(self, msg: dict) -> dict:
         op = msg.get("op")
@@ -249,15 +258,27 @@ class _Peer:
 
 
 class PDPushAgent:
+    """Network I/O (page lists, cache mapping, done notices) runs on the
+    agent's thread; the engine thread only launches copies and polls their
+    events, so a slow decode instance never stalls prefill steps."""
+
     def __init__(self, engine, timeout_s: float = 30.0):
         self.engine = engine
         self.timeout_s = timeout_s
         self.jobs: list[PushJob] = []
         self.peers: dict[str, _Peer] = {}
-        self.stats = {"pushes": 0, "pages": 0, "bytes": 0, "timeouts": 0, "push_s": 0.0}
+        self.lock = threading.Lock()
+        self._notices: list[tuple[str, int, bool]] = []
+        self._wake = threading.Event()
+        self._stop = False
+        self.stats = {"pushes": 0, "pages": 0, "bytes": 0, "timeouts": 0, "failures": 0, "push_s": 0.0}
+        self._th = threading.Thread(target=self._run, name="pd-push-agent", daemon=True)
+        self._th.start()
 
     def submit(self, job: PushJob) -> None:
-        self.jobs.append(job)
+        with self.lock:
+            self.jobs.append(job)
+        self._wake.set()
 
     def pending(self) -> int:
         return len(self.jobs)
@@ -268,56 +289,77 @@ class PDPushAgent:
             p = self.peers[ep] = _Peer(ep, self.engine.device)
         return p
 
+    # ------------------------------------------------------------------ agent thread
+    def _run(self) -> None:
+        dev = self.engine.device
+        if dev.type == "cuda":
+            torch.cuda.set_device(dev)  # IPC mappings are made in this thread
+        while not self._stop:
+            self._wake.wait(0.002)
+            self._wake.clear()
+            with self.lock:
+                todo = [j for j in self.jobs if j.plan is None and not getattr(j, "failed", False)]
+                notices, self._notices = self._notices, []
+            for ep, room, ok in notices:
+                try:
+                    self._peer(ep).call({"op": "done", "room": room, "ok": ok})
+                except Exception as e:
+                    logger.warning("kv push: done notice for room %s failed: %s", room, e)
+            for j in todo:
+                peer = self._peer(j.endpoint)
+                try:
+                    r = peer.call({"op": "pages", "room": j.room}, timeout_ms=500)
+                    if r.get("ready"):
+                        peer.map()
+                        j.plan = r
+                except TimeoutError:
+                    pass
+                except Exception as e:
+                    logger.warning("kv push for room %s failed: %s", j.room, e)
+                    j.failed = True
+                    with self.lock:
+                        self._notices.append((j.endpoint, j.room, False))
+
+    # ------------------------------------------------------------------ engine thread
     def progress(self) -> None:
-        """Called by the engine thread between steps; never blocks for long."""
         from infera_b200.ops import kernels as K
 
         eng = self.engine
         keep = []
-        for j in self.jobs:
-            peer = self._peer(j.endpoint)
-            try:
-                if j.event is None:
-                    if j.plan is None:
-                        r = peer.call({"op": "pages", "room": j.room}, timeout_ms=200)
-                        if r.get("ready"):
-                            j.plan = r
-                    if j.plan is not None:
-                        peer.map()
-                        skip = j.plan["skip_tokens"] // eng.bm.page_size
-                        n_tok = j.plan["n_tokens"]
-                        n_pages = (n_tok + eng.bm.page_size - 1) // eng.bm.page_size - skip
-                        dst = j.plan["pages"][:n_pages]
-                        src = j.blocks.pages[skip:skip + len(dst)]
-                        dev = eng.runner.k_cache.device
-                        sp = torch.tensor(src, dtype=torch.int32, device=dev)
-                        dp = torch.tensor(dst, dtype=torch.int32, device=dev)
-                        K.kv_push_pages(eng.runner.k_cache, eng.runner.v_cache, peer.k, peer.v, sp, dp,
-                                        dst_slots=peer.slots)
-                        j.launched_at = time.monotonic()
-                        if eng.runner.k_cache.is_cuda:
-                            j.event = torch.cuda.Event()
-                            j.event.record()
-                        else:
-                            j.event = True
-                        j._tensors = (sp, dp)
-                        self.stats["pages"] += len(dst)
-                        L, _, H = eng.runner.k_cache.shape
-                        self.stats["bytes"] += 2 * len(dst) * eng.bm.page_size * L * H * eng.runner.k_cache.element_size()
-                if j.event is not None and (j.event is True or j.event.query()):
-                    peer.call({"op": "done", "room": j.room, "ok": True})
-                    self.stats["pushes"] += 1
-                    self.stats["push_s"] += time.monotonic() - j.launched_at
-                    eng._release_pushed(j)
-                    continue
-            except TimeoutError:
-                pass
-            except Exception as e:
-                logger.warning("kv push for room %s failed: %s", j.room, e)
-                try:
-                    peer.call({"op": "done", "room": j.room, "ok": False})
-                except Exception:
-                    pass
+        with self.lock:
+            jobs = list(self.jobs)
+        for j in jobs:
+            if getattr(j, "failed", False):
+                self.stats["failures"] += 1
+                eng._release_pushed(j)
+                continue
+            if j.event is None and j.plan is not None:
+                peer = self.peers[j.endpoint]
+                ps = eng.bm.page_size
+                skip = j.plan["skip_tokens"] // ps
+                n_pages = (j.plan["n_tokens"] + ps - 1) // ps - skip
+                dst = j.plan["pages"][:n_pages]
+                src = j.blocks.pages[skip:skip + len(dst)]
+                dev = eng.runner.k_cache.device
+                sp = torch.tensor(src, dtype=torch.int32, device=dev)
+                dp = torch.tensor(dst, dtype=torch.int32, device=dev)
+                K.kv_push_pages(eng.runner.k_cache, eng.runner.v_cache, peer.k, peer.v, sp, dp, dst_slots=peer.slots)
+                j.launched_at = time.monotonic()
+                if eng.runner.k_cache.is_cuda:
+                    j.event = torch.cuda.Event()
+                    j.event.record()
+                else:
+                    j.event = True
+                j._tensors = (sp, dp)
+                L, _, H = eng.runner.k_cache.shape
+                self.stats["pages"] += len(dst)
+                self.stats["bytes"] += 2 * len(dst) * ps * L * H * eng.runner.k_cache.element_size()
+            if j.event is not None and (j.event is True or j.event.query()):
+                self.stats["pushes"] += 1
+                self.stats["push_s"] += time.monotonic() - j.launched_at
+                with self.lock:
+                    self._notices.append((j.endpoint, j.room, True))
+                self._wake.set()
                 eng._release_pushed(j)
                 continue
             if j.event is None and time.monotonic() - j.created > self.timeout_s:
@@ -325,4 +367,9 @@ class PDPushAgent:
                 eng._release_pushed(j)
                 continue
             keep.append(j)
-        self.jobs = keep
+        with self.lock:
+            done_ids = {id(j) for j in jobs} - {id(j) for j in keep}
+            self.jobs = [j for j in self.jobs if id(j) not in done_ids]
+
+    def close(self) -> None:
+        self._stop = True
