@@ -73,6 +73,32 @@ def run_case(case: str, iters: int) -> dict:
         ms = _time(lambda: K.attn_prefill(q, kc, vc, bt, *meta, tiles, hq, hkv, 1 / math.sqrt(D)), iters)
         keys = sum(ctx - ql + i + 1 for i in range(ql))
         return {"case": case, "ms": ms, "tflops": 4 * keys * D * hq / ms / 1e9}
+    if case in ("kv_push", "kv_push_local"):
+        # 512 pages x 32 layers x (K, V) of an 8-KV-head x 128 cache: 1 GiB per push
+        L, H, n = 32, hkv * D, 512
+        src_dev = torch.device("cuda", 0)
+        dst_dev = torch.device("cuda", 1 if case == "kv_push" else 0)
+        slots = 2 * n * 16
+        sk = torch.randn(L, slots, H, device=src_dev, generator=g).to(bf)
+        sv = torch.randn(L, slots, H, device=src_dev, generator=g).to(bf)
+        with torch.cuda.device(dst_dev):
+            dk = torch.zeros(L, slots, H, dtype=bf, device=dst_dev)
+            dv = torch.zeros(L, slots, H, dtype=bf, device=dst_dev)
+        if dst_dev != src_dev:
+            from infera_b200.ops import _native
+
+            _native.check(_native.kernels().ib_enable_peer_access(dst_dev.index), "enable peer access")
+        sp = torch.randperm(2 * n, device=src_dev)[:n].to(torch.int32)
+        dp = torch.randperm(2 * n, device=src_dev)[:n].to(torch.int32)
+        fn = lambda: K.kv_push_pages(sk, sv, dk.data_ptr(), dv.data_ptr(), sp, dp, dst_slots=slots)  # noqa: E731
+        ms = _time(fn, iters)
+        torch.cuda.synchronize(dst_dev)
+        idx = (dp.long()[:, None] * 16 + torch.arange(16, device=src_dev)).reshape(-1).to(dst_dev)
+        sidx = (sp.long()[:, None] * 16 + torch.arange(16, device=src_dev)).reshape(-1)
+        ok = torch.equal(dk[:, idx].cpu(), sk[:, sidx].cpu())
+        by = 2 * n * 16 * L * H * 2
+        return {"case": case, "ms": ms, "gbs": by / ms / 1e6, "bytes": by, "exact": ok,
+                "frac_of_nvlink_770": round(by / ms / 1e6 / 770, 3) if case == "kv_push" else None}
     raise SystemExit(f"unknown case {case}")
 
 

@@ -9,7 +9,8 @@ concurrent streamed requests through the router, and prints one JSON line:
 completions, errors, TTFT percentiles, the decode instance's prompt tokens
 computed (only the last token of each prompt when the push worked), and
 the push bandwidth from the prefill instance's counters (bytes pushed over
-launch-to-done time) against the 770 GB/s NVLink reference.
+the push kernels' device time, CUDA events around each launch) against
+the 770 GB/s NVLink reference.
 """
 
 from __future__ import annotations
@@ -104,13 +105,13 @@ def main(argv=None) -> None:
         ok = [r for r in res if r is not None and r[1] == a.max_tokens]
         ttft = sorted(r[0] for r in ok if r[0] is not None)
         pb = pm.get("infera_engine:pd_push_bytes_total", 0.0)
-        ps = pm.get("infera_engine:pd_push_seconds_total", 0.0)
+        ps = pm.get("infera_engine:pd_push_device_seconds_total", 0.0)
         out = {"model": a.model, "requests": a.requests, "prompt_len": a.prompt_len, "completed": len(ok),
                "errors": a.requests - len(ok), "wall_s": round(wall, 3),
                "ttft_p50_s": round(ttft[len(ttft) // 2], 4) if ttft else None,
                "ttft_max_s": round(ttft[-1], 4) if ttft else None,
                "pushes": pm.get("infera_engine:pd_pushes_total"), "push_gbytes": round(pb / 1e9, 3),
-               "push_gbs_launch_to_done": round(pb / ps / 1e9, 1) if ps else None,
+               "push_gbs_device": round(pb / ps / 1e9, 1) if ps else None,
                "push_frac_of_nvlink_770": round(pb / ps / 770e9, 3) if ps else None,
                "decode_prompt_tokens_computed": dm.get("infera_engine:prompt_tokens_total"),
                "prefill_prompt_tokens_computed": pm.get("infera_engine:prompt_tokens_total")}

@@ -312,6 +312,7 @@ class LLMEngine:
             "pd_pushes": self.pd_agent.stats["pushes"] if self.pd_agent is not None else 0,
             "pd_push_bytes": self.pd_agent.stats["bytes"] if self.pd_agent is not None else 0,
             "pd_push_seconds": self.pd_agent.stats["push_s"] if self.pd_agent is not None else 0.0,
+            "pd_push_device_seconds": self.pd_agent.stats["push_device_s"] if self.pd_agent is not None else 0.0,
             "pd_parked": len(self.scheduler.parked),
             **self.counters,
         }

@@ -271,7 +271,8 @@ class PDPushAgent:
         self._notices: list[tuple[str, int, bool]] = []
         self._wake = threading.Event()
         self._stop = False
-        self.stats = {"pushes": 0, "pages": 0, "bytes": 0, "timeouts": 0, "failures": 0, "push_s": 0.0}
+        self.stats = {"pushes": 0, "pages": 0, "bytes": 0, "timeouts": 0, "failures": 0, "push_s": 0.0,
+                      "push_device_s": 0.0}
         self._th = threading.Thread(target=self._run, name="pd-push-agent", daemon=True)
         self._th.start()
 
@@ -343,10 +344,13 @@ class PDPushAgent:
                 dev = eng.runner.k_cache.device
                 sp = torch.tensor(src, dtype=torch.int32, device=dev)
                 dp = torch.tensor(dst, dtype=torch.int32, device=dev)
+                if eng.runner.k_cache.is_cuda:
+                    j.start_event = torch.cuda.Event(enable_timing=True)
+                    j.start_event.record()
                 K.kv_push_pages(eng.runner.k_cache, eng.runner.v_cache, peer.k, peer.v, sp, dp, dst_slots=peer.slots)
                 j.launched_at = time.monotonic()
                 if eng.runner.k_cache.is_cuda:
-                    j.event = torch.cuda.Event()
+                    j.event = torch.cuda.Event(enable_timing=True)
                     j.event.record()
                 else:
                     j.event = True
@@ -357,6 +361,9 @@ class PDPushAgent:
             if j.event is not None and (j.event is True or j.event.query()):
                 self.stats["pushes"] += 1
                 self.stats["push_s"] += time.monotonic() - j.launched_at
+                if j.event is not True:
+                    # the copy kernel's own device time (CUDA events around it)
+                    self.stats["push_device_s"] += j.start_event.elapsed_time(j.event) / 1000.0
                 with self.lock:
                     self._notices.append((j.endpoint, j.room, True))
                 self._wake.set()

@@ -173,6 +173,8 @@ def build_worker_app(aeng, tokenizer, model_name: str, extra_metrics=None) -> Fa
         g("infera_engine:pd_pushes_total", s.get("pd_pushes", 0), "KV pushes completed")
         g("infera_engine:pd_push_bytes_total", s.get("pd_push_bytes", 0), "KV bytes pushed to decode instances")
         g("infera_engine:pd_push_seconds_total", round(s.get("pd_push_seconds", 0.0), 6), "Launch-to-done push time")
+        g("infera_engine:pd_push_device_seconds_total", round(s.get("pd_push_device_seconds", 0.0), 6),
+          "Device time of the push kernels")
         g("infera_engine:pd_parked", s.get("pd_parked", 0), "Requests waiting for pushed KV")
         g("infera_engine:generation_tokens_total", s["generation_tokens"], "Generated tokens")
         g("infera_engine:prompt_tokens_total", s["prompt_tokens"], "Computed prompt tokens")
