@@ -73,6 +73,23 @@ def run_case(case: str, iters: int) -> dict:
         ms = _time(lambda: K.attn_prefill(q, kc, vc, bt, *meta, tiles, hq, hkv, 1 / math.sqrt(D)), iters)
         keys = sum(ctx - ql + i + 1 for i in range(ql))
         return {"case": case, "ms": ms, "tflops": 4 * keys * D * hq / ms / 1e9}
+    if case in ("moe_decode", "moe_prefill"):
+        # one expert-parallel shard of a DeepSeek-V3 layer: 32 local experts,
+        # hidden 7168, expert width 2048; tokens x 8 slots spread over them
+        from infera_b200.models.moe import MoELayer
+
+        T = 64 if case == "moe_decode" else 2048
+        E, H, F, k = 32, 7168, 2048, 8
+        layer = MoELayer(H, F, E, k, device=dev, seed=0)
+        x = torch.randn(T, H, device=dev, generator=g).to(bf)
+        ids = torch.randint(0, E, (T, k), device=dev, dtype=torch.int32, generator=g)
+        wts = torch.full((T, k), 1.0 / k, device=dev)
+        ms = _time(lambda: layer.forward(x, ids, wts), iters)
+        active = int(torch.unique(ids).numel())
+        by = active * 3 * F * H * 2
+        fl = 2 * T * k * 3 * F * H
+        return {"case": case, "ms": ms, "gbs": by / ms / 1e6, "tflops": fl / ms / 1e9, "active_experts": active,
+                "weight_bytes": by}
     if case in ("kv_push", "kv_push_local"):
         # 512 pages x 32 layers x (K, V) of an 8-KV-head x 128 cache: 1 GiB per push
         L, H, n = 32, hkv * D, 512

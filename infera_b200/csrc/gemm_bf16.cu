@@ -58,11 +58,23 @@ struct Params {
   void* peer_out[kMaxPeers];
   unsigned int* peer_flag[kMaxPeers];
   unsigned int* done_ctr;   // local, zero between launches
+  // grouped mode (MoE experts, swap-AB only): tile t = gtab[t] = {expert,
+  // feature tile, first token row, end token row of the expert}; *gnum tiles
+  int grouped;
+  const int4* gtab;
+  const int* gnum;
+  int n_per_expert;         // weight rows per expert (the grouped GEMM's N)
 };
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& pt, int& qt, int& sp) {
+  if (p.grouped) {
+    pt = t;
+    qt = 0;
+    sp = 0;
+    return;
+  }
   sp = t % p.splits;
   int rest = t / p.splits;
   pt = rest % p.p_tiles;
@@ -175,6 +187,44 @@ __device__ __forceinline__ void store_chunk(const Params& p, int pt, int qt, int
   }
 }
 
+// Grouped-mode epilogue (swap-AB): TMEM lane = feature of the expert,
+// columns = that expert's token rows [m0, mend).
+template <int NC>
+__device__ __forceinline__ void store_chunk_grouped(const Params& p, int t, int row, int c0, const uint32_t (&r)[NC]) {
+  const int4 g = p.gtab[t];
+  const int n = g.y * BM + row;
+  const int m0 = g.z + c0;
+  if (p.epi == EPI_SWIGLU) {
+    const bool even = (threadIdx.x & 1) == 0;
+    __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.out) + n / 2;
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+      const float mine = __uint_as_float(r[j]);
+      const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+      if (even && n + 1 < p.n_per_expert && m0 + j < g.w)
+        C[static_cast<size_t>(m0 + j) * p.ldc] = __float2bfloat16(silu(mine) * other);
+    }
+  } else {
+    if (n >= p.n_per_expert) return;
+    __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.out) + n;
+#pragma unroll
+    for (int j = 0; j < NC; ++j)
+      if (m0 + j < g.w) C[static_cast<size_t>(m0 + j) * p.ldc] = __float2bfloat16(__uint_as_float(r[j]));
+  }
+}
+
+__device__ __forceinline__ int tile_prow(const Params& p, int t, int pt) {
+  if (p.grouped) {
+    const int4 g = p.gtab[t];
+    return g.x * p.n_per_expert + g.y * BM;
+  }
+  return pt * BM;
+}
+
+__device__ __forceinline__ int tile_qrow(const Params& p, int t, int qt) {
+  return p.grouped ? p.gtab[t].z : qt * p.bn;
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                      const Params p) {
@@ -193,7 +243,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int total = p.p_tiles * p.q_tiles * p.splits;
+  const int total = p.grouped ? *p.gnum : p.p_tiles * p.q_tiles * p.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -242,8 +292,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           mbar_expect_tx(&full[stage], tx);
-          tma_load_2d(sP + stage * P_STAGE, &tmP, &full[stage], kb * BK, pt * BM, polP);
-          tma_load_2d(sQ + stage * Q_STAGE, &tmQ, &full[stage], kb * BK, qt * p.bn, polQ);
+          tma_load_2d(sP + stage * P_STAGE, &tmP, &full[stage], kb * BK, tile_prow(p, t, pt), polP);
+          tma_load_2d(sQ + stage * Q_STAGE, &tmQ, &full[stage], kb * BK, tile_qrow(p, t, qt), polQ);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -318,13 +368,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t r[32];
         tmem_ld32(t_row + c0, r);
         tmem_ld_wait();
-        store_chunk<32>(p, pt, qt, row, c0, r);
+        if (p.grouped) store_chunk_grouped<32>(p, t, row, c0, r);
+        else store_chunk<32>(p, pt, qt, row, c0, r);
       }
       if (c0 < p.bn) {
         uint32_t r[16];
         tmem_ld16(t_row + c0, r);
         tmem_ld_wait();
-        store_chunk<16>(p, pt, qt, row, c0, r);
+        if (p.grouped) store_chunk_grouped<16>(p, t, row, c0, r);
+        else store_chunk<16>(p, pt, qt, row, c0, r);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -500,6 +552,7 @@ extern "C" int ib_gemm_bf16(const void* A, const void* W, void* out, int M, int 
   p.push = 0;
   p.world = 1;
   p.done_ctr = nullptr;
+  p.grouped = 0;
   const bool split = p.splits > 1;
   p.epi = split ? EPI_ATOMIC_F32 : epi;
   p.out = split ? static_cast<void*>(ws) : out;
@@ -563,6 +616,7 @@ extern "C" int ib_gemm_bf16_push(const void* A, const void* W, int M, int N, int
     p.peer_flag[d] = d < world ? peer_flag[d] : nullptr;
   }
   p.done_ctr = done_ctr;
+  p.grouped = 0;
   CUtensorMap tmP, tmQ;
   const void* Pbase = p.swap ? W : A;
   const void* Qbase = p.swap ? A : W;
@@ -594,6 +648,57 @@ extern "C" int ib_gemm_bf16_push(const void* A, const void* W, int M, int N, int
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   return 0;
+}
+
+// Grouped GEMM over experts (swap-AB): for every tile {e, n_tile, m0, mend}
+// of gtab[0 .. *gnum), out[m, :] (rows m0 .. mend-1) = A[m, :] @ W[e]^T
+// restricted to features [n_tile*128, +128). A: [R, K] tokens sorted by
+// expert; W: [E, N, K] stacked; out: [R, ldc] (N/2 columns with SwiGLU).
+// bn: token columns per tile (16 / 32 / 64 / 128 / 256); grid_tiles: the
+// most tiles gtab can hold (sizes the persistent grid).
+extern "C" int ib_gemm_grouped(const void* A, const void* W, void* out, int R, int N, int K, int E, int lda, int ldw,
+                               int ldc, int epi, const int* gtab, const int* gnum, int bn, int grid_tiles, int* status,
+                               cudaStream_t stream) {
+  using namespace ib200::gemm;
+  if (R <= 0 || N <= 0 || K <= 0 || E <= 0) return 0;
+  if ((K % 8) != 0 || (lda % 8) != 0 || (ldw % 8) != 0 || (N % BM) != 0) return -1;
+  if (bn < 16 || bn > MAX_BN || (bn % 16) != 0) return -1;
+  if (epi == EPI_SWIGLU && (N % 2) != 0) return -1;
+  Params p{};
+  p.M = R;
+  p.N = N;
+  p.K = K;
+  p.bn = bn;
+  p.swap = 1;
+  p.splits = 1;
+  p.nkb = (K + BK - 1) / BK;
+  p.kbps = p.nkb;
+  p.p_tiles = 1;
+  p.q_tiles = 1;
+  p.epi = epi;
+  p.out = out;
+  p.ldc = ldc;
+  p.status = status;
+  p.grouped = 1;
+  p.gtab = reinterpret_cast<const int4*>(gtab);
+  p.gnum = gnum;
+  p.n_per_expert = N;
+  CUtensorMap tmP, tmQ;
+  if (!cached_tmap_2d(&tmP, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<long long>(E) * N, K, ldw, BM, BK))
+    return -2;
+  if (!cached_tmap_2d(&tmQ, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, K, lda, bn, BK)) return -2;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_set[dev] = true;
+  }
+  const int num_sms = num_sms_for_current_device();
+  const int grid = grid_tiles < num_sms ? (grid_tiles > 0 ? grid_tiles : 1) : num_sms;
+  gemm_bf16_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmP, tmQ, p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
 
 // Plan introspection for tests and benchmarks: writes

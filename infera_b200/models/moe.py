@@ -1,0 +1,68 @@
+"""Mixture-of-experts FFN on the sm_100a kernels (DeepSeek-V3 shape).
+
+    logits  = x @ Wg^T                         tcgen05 GEMM (bf16)
+    ids, w  = grouped top-k(sigmoid(logits) + bias)   ib_moe_topk
+    rows    = sort (token, slot) pairs by expert        ib_moe_permute
+    xp      = x[token_of_row]                            gather
+    act     = silu(xp We_gate^T) * (xp We_up^T)          grouped GEMM, SwiGLU epilogue
+    out_r   = act @ We_down^T                            grouped GEMM
+    y       = sum_j w[t, j] * out_r[row(t, j)]           ib_moe_combine
+    y      += shared expert (dense SwiGLU MLP) when configured
+
+Weights are random-initialised from a seed like the dense model's. The
+routing can be passed in (``ids`` / ``wts``) so a test can hold it fixed.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from infera_b200.ops import kernels as K
+
+
+class MoELayer:
+    def __init__(self, hidden: int, moe_ffn: int, num_experts: int, top_k: int, n_groups: int = 1,
+                 topk_groups: int = 1, routed_scaling: float = 1.0, num_shared: int = 0,
+                 device: str | torch.device = "cuda", seed: int = 0, std: float = 0.02):
+        self.H, self.F, self.E, self.k = hidden, moe_ffn, num_experts, top_k
+        self.n_groups, self.topk_groups, self.scaling = n_groups, topk_groups, routed_scaling
+        dev = torch.device(device)
+        g = torch.Generator(device=dev).manual_seed(seed)
+        bf = torch.bfloat16
+
+        def rnd(*shape, scale=std):
+            return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * scale).to(bf)
+
+        self.gate = rnd(num_experts, hidden, scale=1.0 / math.sqrt(hidden))
+        self.bias = torch.zeros(num_experts, dtype=torch.float32, device=dev)
+        self.w13 = rnd(num_experts, 2 * moe_ffn, hidden)          # interleaved gate / up rows
+        self.w2 = rnd(num_experts, hidden, moe_ffn, scale=std / math.sqrt(2))
+        self.shared = None
+        if num_shared:
+            self.shared = (rnd(2 * moe_ffn * num_shared, hidden), rnd(hidden, moe_ffn * num_shared))
+
+    def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        logits = K.linear(x, self.gate)
+        return K.moe_topk(logits, self.k, self.n_groups, self.topk_groups, self.bias, self.scaling)
+
+    def forward(self, x: torch.Tensor, ids: torch.Tensor | None = None, wts: torch.Tensor | None = None
+                ) -> torch.Tensor:
+        if ids is None:
+            ids, wts = self.route(x)
+        offsets, row_of_slot, token_of_row = K.moe_permute(ids, self.E)
+        xp = K.gather_rows(x, token_of_row)
+        act = K.gemm_grouped(xp, self.w13, offsets, swiglu=True)
+        rows = K.gemm_grouped(act, self.w2, offsets)
+        y = K.moe_combine(rows, row_of_slot, wts)
+        if self.shared is not None:
+            y = y + K.linear(K.linear(x, self.shared[0], swiglu=True), self.shared[1])
+        return y
+
+    def to(self, device) -> "MoELayer":
+        for name in ("gate", "bias", "w13", "w2"):
+            setattr(self, name, getattr(self, name).to(device))
+        if self.shared is not None:
+            self.shared = tuple(t.to(device) for t in self.shared)
+        return self

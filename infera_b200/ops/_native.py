@@ -66,6 +66,13 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_ipc_close": [c_vp],
         "ib_can_access_peer": [c_int, c_int],
         "ib_enable_peer_access": [c_int],
+        "ib_moe_topk": [c_vp, c_int, c_int, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_vp, c_vp,
+                        c_vp],
+        "ib_moe_permute": [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+        "ib_moe_tiles": [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp],
+        "ib_moe_combine": [c_vp, c_int, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_int, c_vp],
+        "ib_gemm_grouped": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp,
+                            c_int, c_int, c_vp, c_vp],
         "ib_kv_push_pages": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_int, c_int, c_vp],
     }
     for name, args in sig.items():

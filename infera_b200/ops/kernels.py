@@ -539,3 +539,135 @@ def kv_push_pages(src_k: torch.Tensor, src_v: torch.Tensor, dst_k, dst_v, src_pa
                                             src_k.element_size(), _stream())
     _native.check(rc, "ib_kv_push_pages")
     _count()
+
+
+# ---------------------------------------------------------------- mixture of experts
+
+
+def moe_topk(logits: torch.Tensor, top_k: int, n_groups: int = 1, topk_groups: int = 1,
+             bias: torch.Tensor | None = None, scaling: float = 1.0, renorm: bool = True,
+             softmax: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """Router logits [T, E] -> (expert ids int32 [T, k], weights fp32 [T, k]):
+    sigmoid (or softmax) scores, grouped selection on score + bias (groups
+    ranked by their two best), weights = chosen scores, renormalised, x scaling."""
+    T, E = logits.shape
+    if not logits.is_cuda:
+        x = logits.float()
+        s = torch.softmax(x, -1) if softmax else torch.sigmoid(x)
+        c = s + (bias.float() if bias is not None else 0.0)
+        gs = E // n_groups
+        if n_groups > 1:
+            grp = c.view(T, n_groups, gs).topk(min(2, gs), dim=-1).values.sum(-1)
+            keep = torch.zeros(T, n_groups, dtype=torch.bool)
+            keep.scatter_(1, grp.topk(topk_groups, dim=-1).indices, True)
+            c = c.masked_fill(~keep.repeat_interleave(gs, dim=1), float("-inf"))
+        ids = c.topk(top_k, dim=-1).indices
+        w = s.gather(1, ids)
+        if renorm:
+            w = w / w.sum(-1, keepdim=True).clamp_min(1e-20)
+        return ids.to(torch.int32), (w * scaling).float()
+    ids = torch.empty(T, top_k, dtype=torch.int32, device=logits.device)
+    wts = torch.empty(T, top_k, dtype=torch.float32, device=logits.device)
+    rc = _native.kernels().ib_moe_topk(logits.data_ptr(), logits.stride(0), 1 if logits.dtype == torch.bfloat16 else 0,
+                                       _ptr(bias), T, E, n_groups, topk_groups, top_k, 1 if softmax else 0,
+                                       1 if renorm else 0, scaling, ids.data_ptr(), wts.data_ptr(), _stream())
+    _native.check(rc, "ib_moe_topk")
+    _count()
+    return ids, wts
+
+
+def moe_permute(ids: torch.Tensor, E: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(offsets [E+1], row_of_slot [T*k], token_of_row [T*k]) int32: the
+    expert-sorted row of every (token, slot) and each row's token."""
+    T, k = ids.shape
+    n = T * k
+    dev = ids.device
+    if not ids.is_cuda:
+        flat = ids.reshape(-1).long()
+        order = torch.argsort(flat, stable=True)
+        counts = torch.bincount(flat, minlength=E)
+        offsets = torch.zeros(E + 1, dtype=torch.int32)
+        offsets[1:] = torch.cumsum(counts, 0).to(torch.int32)
+        row_of_slot = torch.empty(n, dtype=torch.int32)
+        row_of_slot[order] = torch.arange(n, dtype=torch.int32)
+        token_of_row = (order // k).to(torch.int32)
+        return offsets, row_of_slot, token_of_row
+    ws = torch.empty(2 * E + (E + 1) + 2 * n, dtype=torch.int32, device=dev)
+    counts, cursor = ws[:E], ws[E:2 * E]
+    offsets = ws[2 * E:3 * E + 1]
+    row_of_slot = ws[3 * E + 1:3 * E + 1 + n]
+    token_of_row = ws[3 * E + 1 + n:]
+    rc = _native.kernels().ib_moe_permute(ids.data_ptr(), T, k, E, counts.data_ptr(), cursor.data_ptr(),
+                                          offsets.data_ptr(), row_of_slot.data_ptr(), token_of_row.data_ptr(),
+                                          _stream())
+    _native.check(rc, "ib_moe_permute")
+    _count(3)
+    return offsets, row_of_slot, token_of_row
+
+
+def grouped_bn(rows: int, E: int) -> int:
+    avg = max(1, rows // max(1, E))
+    for b in (16, 32, 64, 128):
+        if avg <= b:
+            return b
+    return 256
+
+
+def gemm_grouped(xp: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor, swiglu: bool = False,
+                 out: torch.Tensor | None = None, bn: int | None = None) -> torch.Tensor:
+    """Rows of ``xp`` [R, K] sorted by expert (``offsets`` [E+1]) times their
+    expert's weight ``w`` [E, N, K]: out [R, N] (N/2 with ``swiglu``; gate
+    and up rows interleaved per expert as in the dense layers)."""
+    R, Kd = xp.shape
+    E, N, _ = w.shape
+    n_out = N // 2 if swiglu else N
+    if not xp.is_cuda:
+        y = torch.empty(R, N, dtype=torch.float32)
+        off = offsets.tolist()
+        for e in range(E):
+            a, b = off[e], off[e + 1]
+            if b > a:
+                y[a:b] = xp[a:b].float() @ w[e].float().t()
+        if swiglu:
+            y = torch.nn.functional.silu(y[:, 0::2]) * y[:, 1::2]
+        y = y.to(torch.bfloat16)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(R, n_out, dtype=torch.bfloat16, device=xp.device)
+    bn = bn or grouped_bn(R, E)
+    cap = (-(-R // bn) + E) * (N // 128)
+    tab = torch.empty(cap * 4 + 1, dtype=torch.int32, device=xp.device)
+    num = tab[cap * 4:]
+    lib = _native.kernels()
+    _native.check(lib.ib_moe_tiles(offsets.data_ptr(), E, N, bn, tab.data_ptr(), num.data_ptr(), _stream()),
+                  "ib_moe_tiles")
+    sc = scratch(xp.device)
+    rc = lib.ib_gemm_grouped(xp.data_ptr(), w.data_ptr(), out.data_ptr(), R, N, Kd, E, xp.stride(0), w.stride(1),
+                             out.stride(0), 1 if swiglu else 0, tab.data_ptr(), num.data_ptr(), bn, cap,
+                             sc.status.data_ptr(), _stream())
+    _native.check(rc, "ib_gemm_grouped")
+    _count(2)
+    return out
+
+
+def moe_combine(rows: torch.Tensor, row_of_slot: torch.Tensor, wts: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    T, k = wts.shape
+    H = rows.shape[1]
+    if not rows.is_cuda:
+        g = rows.float()[row_of_slot.long()].view(T, k, H)
+        y = (g * wts.float()[:, :, None]).sum(1).to(torch.bfloat16)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=rows.device)
+    rc = _native.kernels().ib_moe_combine(rows.data_ptr(), rows.stride(0), row_of_slot.data_ptr(), wts.data_ptr(), T,
+                                          k, H, out.data_ptr(), out.stride(0), _stream())
+    _native.check(rc, "ib_moe_combine")
+    _count()
+    return out
