@@ -31,6 +31,20 @@ class DenseConfig:
     max_model_len: int = 32768 + 1024
     weight_dtype: str = "bf16"      # "bf16" or "fp8" (e4m3, 128x128 block scales)
     eos_token_id: int = 128001
+    # mixture-of-experts FFN (0 experts: dense). Layers >= moe_first_layer
+    # use routed experts (+ shared experts) instead of the dense MLP.
+    num_experts: int = 0
+    moe_top_k: int = 0
+    moe_ffn: int = 0
+    moe_first_layer: int = 0
+    moe_n_groups: int = 1
+    moe_topk_groups: int = 1
+    moe_routed_scaling: float = 1.0
+    moe_num_shared: int = 0
+    moe_softmax: bool = False
+
+    def is_moe_layer(self, i: int) -> bool:
+        return self.num_experts > 0 and i >= self.moe_first_layer
 
     @property
     def q_size(self) -> int:
@@ -104,11 +118,24 @@ PRESETS: dict[str, DenseConfig | MoEConfig] = {
                              vocab=151936, rope_theta=1000000.0, rope_scaling=None, rms_eps=1e-6, qk_norm=True,
                              max_model_len=65536 + 2048, eos_token_id=151645),
     "deepseek-v3": MoEConfig(),
+    # GQA attention + routed experts (Qwen3-30B-A3B shape)
+    "qwen3-30b-a3b": DenseConfig(name="qwen3-30b-a3b", num_layers=48, hidden=2048, num_heads=32, num_kv_heads=4,
+                                 ffn=6144, vocab=151936, rope_theta=1000000.0, rope_scaling=None, rms_eps=1e-6,
+                                 qk_norm=True, eos_token_id=151645, num_experts=128, moe_top_k=8, moe_ffn=768,
+                                 moe_softmax=True),
     # small shapes for tests (same structure, tiny sizes)
     "tiny-dense": DenseConfig(name="tiny-dense", num_layers=2, hidden=256, num_heads=4, num_kv_heads=2, ffn=512,
                               vocab=1024, max_model_len=2048, eos_token_id=1),
     "tiny-dense-gpu": DenseConfig(name="tiny-dense-gpu", num_layers=2, hidden=1024, num_heads=8, num_kv_heads=2,
                                   ffn=2048, vocab=4096, max_model_len=4096, eos_token_id=1),
+    "tiny-moe-gqa": DenseConfig(name="tiny-moe-gqa", num_layers=3, hidden=256, num_heads=4, num_kv_heads=2,
+                                ffn=512, vocab=1024, max_model_len=2048, eos_token_id=1, num_experts=8, moe_top_k=2,
+                                moe_ffn=128, moe_first_layer=1, moe_n_groups=2, moe_topk_groups=1,
+                                moe_routed_scaling=1.5, moe_num_shared=1),
+    "tiny-moe-gqa-gpu": DenseConfig(name="tiny-moe-gqa-gpu", num_layers=3, hidden=1024, num_heads=8, num_kv_heads=2,
+                                    ffn=2048, vocab=4096, max_model_len=4096, eos_token_id=1, num_experts=16,
+                                    moe_top_k=4, moe_ffn=512, moe_first_layer=1, moe_n_groups=4,
+                                    moe_topk_groups=2, moe_routed_scaling=2.0, moe_num_shared=1),
     "tiny-moe": MoEConfig(name="tiny-moe", num_layers=3, num_dense_layers=1, hidden=256, dense_ffn=512,
                           num_heads=4, q_lora_rank=128, kv_lora_rank=64, qk_rope_dim=32, qk_nope_dim=32,
                           v_head_dim=32, num_experts=8, moe_ffn=128, top_k=2, n_groups=2, topk_groups=1,

@@ -90,7 +90,7 @@ class DenseWeights:
         self.embed = rnd(cfg.vocab, H, scale=1.0)
         self.layers = []
         out_scale = std / math.sqrt(2 * cfg.num_layers)
-        for _ in range(cfg.num_layers):
+        for li in range(cfg.num_layers):
             qkv = rnd(cfg.qkv_size, H)
             o = rnd(H, cfg.q_size, scale=out_scale)
             gu = rnd(2 * cfg.ffn, H)      # interleaved rows (g0, u0, g1, u1, ...)
@@ -104,6 +104,15 @@ class DenseWeights:
                 "down": shard_cols(dn, r * f, (r + 1) * f),
             }
             del qkv, o, gu, dn
+            if cfg.is_moe_layer(li):
+                if W > 1:
+                    raise NotImplementedError("tensor parallelism of expert layers (use expert parallelism)")
+                from infera_b200.models.moe import MoELayer
+
+                del lw["gate_up"], lw["down"]
+                lw["moe"] = MoELayer(H, cfg.moe_ffn, cfg.num_experts, cfg.moe_top_k, cfg.moe_n_groups,
+                                     cfg.moe_topk_groups, cfg.moe_routed_scaling, cfg.moe_num_shared, device,
+                                     seed=seed * 1000 + li, std=std)
             if cfg.qk_norm:
                 lw["q_norm"] = torch.ones(cfg.head_dim, dtype=bf, device=device)
                 lw["k_norm"] = torch.ones(cfg.head_dim, dtype=bf, device=device)
@@ -117,7 +126,11 @@ class DenseWeights:
     def nbytes(self) -> int:
         n = self.embed.numel() + self.lm_head.numel() + self.final_norm.numel()
         for lw in self.layers:
-            n += sum(t.numel() for t in lw.values())
+            for k, t in lw.items():
+                if k == "moe":
+                    n += t.w13.numel() + t.w2.numel() + t.gate.numel()
+                else:
+                    n += t.numel()
         return 2 * n
 
 
@@ -188,7 +201,12 @@ class DenseModel:
                 K.attn_decode(qkv[Tp:T], kc, vc, fb.d_block_table, fb.d_seq_lens, cfg.num_heads, cfg.num_kv_heads,
                               self.scale, splits=fb.d_splits, out=attn[Tp:T], bt_rows=fb.d_bt_rows)
             nxt = self.w.layers[li + 1]["ln1"] if li + 1 < cfg.num_layers else self.w.final_norm
-            if self.tp is None:
+            if "moe" in lw:
+                K.linear(attn, lw["o"], out=o)
+                K.add_rmsnorm(o, h, lw["ln2"], cfg.rms_eps, out=x)
+                y = lw["moe"].forward(x)
+                K.add_rmsnorm(y, h, nxt, cfg.rms_eps, out=x)
+            elif self.tp is None:
                 K.linear(attn, lw["o"], out=o)
                 K.add_rmsnorm(o, h, lw["ln2"], cfg.rms_eps, out=x)
                 K.linear(x, lw["gate_up"], out=act, swiglu=True)

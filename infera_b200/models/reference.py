@@ -52,11 +52,32 @@ def reference_logits(model: DenseModel, token_ids: list[int]) -> torch.Tensor:
         o = torch.einsum("hts,shd->thd", torch.softmax(s, -1), v).reshape(T, nq * D)
         h = h + o @ f(lw["o"]).t()
         x = norm(h, lw["ln2"])
+        if "moe" in lw:
+            h = h + _moe_ref(lw["moe"], x, f)
+            continue
         gu = x @ f(lw["gate_up"]).t()
         act = torch.nn.functional.silu(gu[:, 0::2]) * gu[:, 1::2]
         h = h + act @ f(lw["down"]).t()
     x = norm(h, w.final_norm)
     return x @ f(w.lm_head).t()
+
+
+def _moe_ref(m, x: torch.Tensor, f) -> torch.Tensor:
+    """fp32 routed experts (+ shared): the same grouped routing as the kernels."""
+    from infera_b200.ops import kernels as K
+
+    logits = x @ f(m.gate).t()
+    ids, wts = K.moe_topk(logits, m.k, m.n_groups, m.topk_groups, f(m.bias), m.scaling)
+    y = torch.zeros_like(x)
+    for t in range(x.shape[0]):
+        for j in range(m.k):
+            e = int(ids[t, j])
+            gu = x[t] @ f(m.w13[e]).t()
+            y[t] += float(wts[t, j]) * ((torch.nn.functional.silu(gu[0::2]) * gu[1::2]) @ f(m.w2[e]).t())
+    if m.shared is not None:
+        gu = x @ f(m.shared[0]).t()
+        y += (torch.nn.functional.silu(gu[:, 0::2]) * gu[:, 1::2]) @ f(m.shared[1]).t()
+    return y
 
 
 def reference_greedy(model: DenseModel, prompt: list[int], n: int) -> tuple[list[int], list[float]]:

@@ -41,3 +41,21 @@ def test_permute_and_layer_match_dense_computation():
     hs = x.float() @ layer.shared[0].float().t()
     ref += (torch.nn.functional.silu(hs[:, 0::2]) * hs[:, 1::2]).to(torch.bfloat16).float() @ layer.shared[1].float().t()
     assert float((y.float() - ref).norm() / ref.norm()) < 2e-2
+
+
+def test_engine_serves_moe_model():
+    from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
+    from infera_b200.engine.request import SamplingParams
+    from infera_b200.models.reference import reference_greedy
+
+    eng = LLMEngine(EngineConfig(model="tiny-moe-gqa", use_cuda_graphs=False, num_pages=64, max_batched_tokens=24),
+                    device="cpu")
+    g = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (9, 30)]
+    outs = eng.generate(prompts, SamplingParams(max_tokens=5, ignore_eos=True))
+    for p, o in zip(prompts, outs):
+        ref, margins = reference_greedy(eng.model, p, 5)
+        for i, (a, b) in enumerate(zip(o, ref)):
+            if a != b:
+                assert margins[i] < 0.05, (i, a, b, margins[i])
+                break

@@ -82,3 +82,22 @@ def test_moe_layer(T):
     torch.cuda.synchronize()
     _status()
     assert _rel(out.cpu(), ref) < 2e-2
+
+
+def test_engine_moe_model_with_graphs():
+    from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
+    from infera_b200.engine.request import SamplingParams
+    from infera_b200.models.reference import reference_logits
+
+    eng = LLMEngine(EngineConfig(model="tiny-moe-gqa-gpu", num_pages=256, max_num_seqs=16), device="cuda:0")
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 4000, (n,), generator=g).tolist() for n in (7, 65, 200)]
+    outs = eng.generate(prompts, SamplingParams(max_tokens=6, ignore_eos=True))
+    _status()
+    assert [len(o) for o in outs] == [6, 6, 6]
+    # the first sampled token is the argmax of the oracle's last-position logits
+    # unless the top two are within rounding
+    for p, o in zip(prompts, outs):
+        lg = reference_logits(eng.model, p)[-1]
+        top = torch.topk(lg, 2)
+        assert o[0] == int(top.indices[0]) or float(top.values[0] - top.values[1]) < 0.05
