@@ -32,6 +32,7 @@ def main(argv=None) -> None:
     ap.add_argument("--experts", type=int, default=32)
     ap.add_argument("--top-k", type=int, default=4)
     ap.add_argument("--iters", type=int, default=0)
+    ap.add_argument("--fused", action="store_true", help="NVLink peer-store dispatch / return (GPUs)")
     a = ap.parse_args(argv)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -43,6 +44,7 @@ def main(argv=None) -> None:
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=120)) if not a.cpu else None
     full = MoELayer(a.hidden, a.ffn, a.experts, a.top_k, n_groups=4, topk_groups=2, routed_scaling=2.0,
                     num_shared=1, device="cpu", seed=7)
     g = torch.Generator().manual_seed(11)
@@ -50,13 +52,17 @@ def main(argv=None) -> None:
     x = x_all[rank * a.tokens:(rank + 1) * a.tokens].contiguous()
     ids, wts = full.route(x)  # same routing on both paths
     ref = full.forward(x, ids, wts)
-    ep = EPMoE(full, rank, world, device=dev)
+    ep = EPMoE(full, rank, world, device=dev, fused=a.fused, max_tokens=a.tokens, gloo_group=gloo)
     y = ep.forward(x.to(dev), ids.to(dev), wts.to(dev))
     if dev.type == "cuda":
         torch.cuda.synchronize()
     err = float((y.float().cpu() - ref.float()).norm() / ref.float().norm())
-    res = {"rank": rank, "world": world, "rel_err": round(err, 5), "sent_rows": ep.stats["sent_rows"],
-           "recv_rows": ep.stats["recv_rows"]}
+    res = {"rank": rank, "world": world, "fused": ep.fused, "rel_err": round(err, 5),
+           "sent_rows": ep.stats["sent_rows"], "recv_rows": ep.stats["recv_rows"]}
+    if dev.type == "cuda":
+        from infera_b200.ops import kernels as K
+
+        res["status"] = K.scratch(dev).read_status()
     if a.iters and dev.type == "cuda":
         xd, idd, wd = x.to(dev), ids.to(dev), wts.to(dev)
         for _ in range(3):
@@ -76,6 +82,8 @@ def main(argv=None) -> None:
     if rank == 0:
         print(json.dumps({"ranks": out, "max_rel_err": max(r["rel_err"] for r in out)}), flush=True)
     dist.barrier()
+    if hasattr(ep, "close"):
+        ep.close()
     dist.destroy_process_group()
     if err > 2e-2:
         raise SystemExit(f"expert-parallel mismatch on rank {rank}: {err}")

@@ -1,0 +1,208 @@
+// Expert-parallel dispatch and return over NVLink peer memory (no
+// all-to-all library call on the data path).
+//
+// Every rank holds, in a CUDA-IPC region mapped by all ranks, a receive
+// buffer laid out [local expert][source rank][rows] and a return buffer
+// laid out like its own expert-sorted rows. With the all-gathered counts
+// C[src][expert] (int32 [W, E], every rank has the same copy):
+//
+//   ib_ep_offsets   per rank: where each of its sorted rows lands on its
+//                   destination (dst_off[E]), its local experts' row ranges
+//                   (loc_off[El+1]) and every source's sorted offsets
+//                   (src_off[W, E]);
+//   ib_ep_dispatch  copies each sorted row x[r] (expert e) to
+//                   recv[dest(e)][dst_off[e] + r - offsets[e]] with 16-byte
+//                   peer stores, then the last CTA adds 1 to an arrival
+//                   counter on every rank;
+//   ib_ep_wait      waits (bounded, 2 s) until all W arrivals of a round are in;
+//   ib_ep_return    copies each expert-output row p < loc_off[El] (local
+//                   expert e, source s) back to ret[s][src_off[s][e] + (p -
+//                   start of (e, s))], then signals like the dispatch.
+//
+// Waits are bounded by %globaltimer; on timeout a status word is set and
+// the kernel returns, so a dead rank turns into an error, not a hang.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ib200 {
+namespace ep {
+
+constexpr int kMaxRanks = 8;
+constexpr int kStatusTimeoutEp = 0x4201;
+constexpr unsigned long long kWaitNs = 2000000000ull;
+
+struct Peers {
+  void* buf[kMaxRanks];            // recv (dispatch) or ret (return) base on each rank
+  unsigned int* flag[kMaxRanks];   // arrival counter on each rank for this phase
+};
+
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// single block; W * E <= blockDim-friendly sizes (E <= 1024, W <= 8)
+__global__ void offsets_kernel(const int* __restrict__ C, int W, int E, int rank, int* __restrict__ dst_off,
+                               int* __restrict__ loc_off, int* __restrict__ src_off) {
+  const int El = E / W;
+  // src_off[s, e] = sum_{e' < e} C[s][e']
+  for (int s = threadIdx.x; s < W; s += blockDim.x) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      src_off[s * E + e] = acc;
+      acc += C[s * E + e];
+    }
+  }
+  // dst_off[e] for this rank as the source: the block of expert e on its
+  // destination starts after the destination's earlier local experts (all
+  // sources) and after the lower-ranked sources of expert e
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int d = e / El;
+    int acc = 0;
+    for (int e2 = d * El; e2 < e; ++e2)
+      for (int s = 0; s < W; ++s) acc += C[s * E + e2];
+    for (int s = 0; s < rank; ++s) acc += C[s * E + e];
+    dst_off[e] = acc;
+  }
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int el = 0; el < El; ++el) {
+      loc_off[el] = acc;
+      for (int s = 0; s < W; ++s) acc += C[s * E + rank * El + el];
+    }
+    loc_off[El] = acc;
+  }
+}
+
+__device__ __forceinline__ int find_bin(const int* __restrict__ off, int n, int r) {
+  // largest e with off[e] <= r (off[0] = 0, non-decreasing, n + 1 entries)
+  int lo = 0, hi = n;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (off[mid] <= r) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void signal_all(unsigned int* done_ctr, const Peers& pr, int world) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(done_ctr, 1u) == gridDim.x - 1) {
+      *done_ctr = 0;
+      __threadfence_system();
+      for (int d = 0; d < world; ++d) atomicAdd_system(pr.flag[d], 1u);
+    }
+  }
+}
+
+// one CTA per group of rows; rows are H bf16 (H * 2 % 16 == 0)
+__global__ void __launch_bounds__(256) dispatch_kernel(const uint4* __restrict__ x, int rows, int vec_per_row,
+                                                       const int* __restrict__ offsets, int E, int El,
+                                                       const int* __restrict__ dst_off, Peers pr, int world,
+                                                       unsigned int* done_ctr) {
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int e = find_bin(offsets, E, r);
+    const int d = e / El;
+    const long long pos = static_cast<long long>(dst_off[e]) + (r - offsets[e]);
+    uint4* dst = static_cast<uint4*>(pr.buf[d]) + pos * vec_per_row;
+    const uint4* src = x + static_cast<long long>(r) * vec_per_row;
+    for (int i = threadIdx.x; i < vec_per_row; i += blockDim.x) dst[i] = __ldg(src + i);
+  }
+  signal_all(done_ctr, pr, world);
+}
+
+__global__ void __launch_bounds__(256) return_kernel(const uint4* __restrict__ y, int rows, int vec_per_row,
+                                                     const int* __restrict__ C, int W, int E, int El, int rank,
+                                                     const int* __restrict__ loc_off,
+                                                     const int* __restrict__ src_off, Peers pr,
+                                                     unsigned int* done_ctr) {
+  const int nrows = min(rows, loc_off[El]);  // rows actually received this round
+  for (int p = blockIdx.x; p < nrows; p += gridDim.x) {
+    const int el = find_bin(loc_off, El, p);
+    const int e = rank * El + el;
+    int rel = p - loc_off[el];
+    int s = 0;
+    while (s < W - 1 && rel >= C[s * E + e]) {
+      rel -= C[s * E + e];
+      ++s;
+    }
+    const long long src_row = static_cast<long long>(src_off[s * E + e]) + rel;
+    uint4* dst = static_cast<uint4*>(pr.buf[s]) + src_row * vec_per_row;
+    const uint4* src = y + static_cast<long long>(p) * vec_per_row;
+    for (int i = threadIdx.x; i < vec_per_row; i += blockDim.x) dst[i] = __ldg(src + i);
+  }
+  signal_all(done_ctr, pr, W);
+}
+
+__global__ void wait_kernel(const unsigned int* flag, unsigned int target, int* status) {
+  if (threadIdx.x != 0) return;
+  const unsigned long long t0 = gtimer();
+  while (ld_acquire_sys(flag) < target) {
+    if (gtimer() - t0 > kWaitNs) {
+      atomicCAS(status, 0, kStatusTimeoutEp);
+      return;
+    }
+  }
+}
+
+}  // namespace ep
+}  // namespace ib200
+
+using namespace ib200::ep;
+
+extern "C" int ib_ep_offsets(const int* C, int W, int E, int rank, int* dst_off, int* loc_off, int* src_off,
+                             cudaStream_t stream) {
+  if (W < 1 || W > kMaxRanks || E % W) return -1;
+  offsets_kernel<<<1, 256, 0, stream>>>(C, W, E, rank, dst_off, loc_off, src_off);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+// peer_buf / peer_flag: host arrays of `world` device pointers
+extern "C" int ib_ep_dispatch(const void* x, int rows, int H, const int* offsets, int E, int world,
+                              const int* dst_off, void* const* peer_buf, unsigned int* const* peer_flag,
+                              unsigned int* done_ctr, cudaStream_t stream) {
+  if (world < 1 || world > kMaxRanks || (H * 2) % 16) return -1;
+  Peers pr{};
+  for (int d = 0; d < world; ++d) {
+    pr.buf[d] = peer_buf[d];
+    pr.flag[d] = peer_flag[d];
+  }
+  const int grid = rows < 1 ? 1 : (rows < 2048 ? rows : 2048);
+  dispatch_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(x), rows, H * 2 / 16, offsets, E, E / world,
+                                            dst_off, pr, world, done_ctr);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+extern "C" int ib_ep_return(const void* y, int rows, int H, const int* C, int world, int E, int rank,
+                            const int* loc_off, const int* src_off, void* const* peer_buf,
+                            unsigned int* const* peer_flag, unsigned int* done_ctr, cudaStream_t stream) {
+  if (world < 1 || world > kMaxRanks || (H * 2) % 16) return -1;
+  Peers pr{};
+  for (int d = 0; d < world; ++d) {
+    pr.buf[d] = peer_buf[d];
+    pr.flag[d] = peer_flag[d];
+  }
+  const int grid = rows < 1 ? 1 : (rows < 2048 ? rows : 2048);
+  return_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(y), rows, H * 2 / 16, C, world, E, E / world,
+                                          rank, loc_off, src_off, pr, done_ctr);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+extern "C" int ib_ep_wait(const unsigned int* flag, unsigned int target, int* status, cudaStream_t stream) {
+  wait_kernel<<<1, 32, 0, stream>>>(flag, target, status);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}

@@ -71,6 +71,10 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_moe_permute": [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
         "ib_moe_tiles": [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp],
         "ib_moe_combine": [c_vp, c_int, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_int, c_vp],
+        "ib_ep_offsets": [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp],
+        "ib_ep_dispatch": [c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp],
+        "ib_ep_return": [c_vp, c_int, c_int, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+        "ib_ep_wait": [c_vp, ctypes.c_uint, c_vp, c_vp],
         "ib_gemm_grouped": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp,
                             c_int, c_int, c_vp, c_vp],
         "ib_kv_push_pages": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_int, c_int, c_vp],

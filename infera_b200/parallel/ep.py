@@ -13,9 +13,20 @@ stays data-parallel); one layer's MoE step is
     return   = the inverse regroup and all-to-all
     combine  = weighted sum per token (ib_moe_combine) + shared expert
 
-The collectives are NCCL's all-to-all over NVLink (gloo on CPU for the
-tests). The split sizes need one small host read per layer. Reference
-counterpart: the engines' EP MoE (vLLM / SGLang over their a2a backends).
+Two data paths:
+
+* baseline: NCCL all-to-all over NVLink (gloo on CPU for the tests); the
+  split sizes need one small host read per layer;
+* fused (``fused=True``, GPUs): the counts are all-gathered (NCCL, a few
+  KB) and the rows move with this framework's kernels over NVLink peer
+  memory - ``ib_ep_dispatch`` stores each sorted row straight into its
+  destination's receive buffer at its [local expert][source] place (no
+  regroup on the receiver), ``ib_ep_return`` stores each expert output
+  back at its source's sorted row; arrival counters with bounded waits
+  separate the phases, and nothing is read back to the host.
+
+Reference counterpart: the engines' EP MoE (vLLM / SGLang over their a2a
+backends).
 """
 
 from __future__ import annotations
@@ -23,12 +34,18 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
+import ctypes
+
 from infera_b200.models.moe import MoELayer
+from infera_b200.ops import _native
 from infera_b200.ops import kernels as K
+
+FLAGS = 256  # two u32 arrival counters, padded
 
 
 class EPMoE:
-    def __init__(self, full: MoELayer, rank: int, world: int, group=None, device: str | torch.device = "cuda"):
+    def __init__(self, full: MoELayer, rank: int, world: int, group=None, device: str | torch.device = "cuda",
+                 fused: bool = False, max_tokens: int = 256, gloo_group=None):
         if full.E % world:
             raise ValueError(f"{full.E} experts do not split over {world} ranks")
         self.rank, self.world, self.group = rank, world, group
@@ -42,6 +59,110 @@ class EPMoE:
         self.w2 = full.w2[lo:hi].to(dev).contiguous()
         self.shared = None if full.shared is None else tuple(t.to(dev) for t in full.shared)
         self.stats = {"sent_rows": 0, "recv_rows": 0}
+        self.device = dev
+        self.fused = fused and dev.type == "cuda"
+        if self.fused:
+            self._setup_symmetric(max_tokens * full.k * world, full.H, gloo_group)
+
+    # ------------------------------------------------------------------ fused path
+    def _setup_symmetric(self, max_rows: int, H: int, gloo_group) -> None:
+        lib = _native.kernels()
+        self.max_rows, self.H = max_rows, H
+        self.buf_bytes = max_rows * H * 2
+        total = FLAGS + 2 * self.buf_bytes
+        p = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _native.check(lib.ib_sym_alloc(total, ctypes.byref(p)), "ib_sym_alloc")
+            self.base = p.value
+            h = (ctypes.c_char * 64)()
+            _native.check(lib.ib_ipc_handle(ctypes.c_void_p(self.base), h), "ib_ipc_handle")
+        allh = [None] * self.world
+        dist.all_gather_object(allh, bytes(h), group=gloo_group)
+        self.peers = []
+        for r, hb in enumerate(allh):
+            if r == self.rank:
+                self.peers.append(self.base)
+                continue
+            q = ctypes.c_void_p()
+            buf = (ctypes.c_char * 64).from_buffer_copy(hb)
+            with torch.cuda.device(self.device):
+                _native.check(lib.ib_ipc_open(buf, ctypes.byref(q)), f"ib_ipc_open(rank {r})")
+            self.peers.append(q.value)
+        self.round = 0
+        self.ctr = torch.zeros(4, dtype=torch.int32, device=self.device)  # done counters of the two phases
+        W, E = self.world, self.E
+        self.counts_all = torch.zeros(W * E, dtype=torch.int32, device=self.device)
+        self.offs = torch.zeros(E + self.El + 1 + W * E, dtype=torch.int32, device=self.device)
+        dist.barrier(group=gloo_group)
+
+    def _recv_view(self, base: int) -> int:
+        return base + FLAGS
+
+    def _ret_view(self, base: int) -> int:
+        return base + FLAGS + self.buf_bytes
+
+    def _tensor_at(self, ptr: int, rows: int) -> torch.Tensor:
+        from infera_b200.parallel.symmem import _View
+
+        class _Buf:
+            pass
+
+        b = _Buf()
+        b.ptr = ptr
+        t = torch.as_tensor(_View(b, (rows, self.H), "<i2"), device=self.device).view(torch.bfloat16)
+        return t
+
+    def _forward_fused(self, x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor) -> torch.Tensor:
+        lib = _native.kernels()
+        W, E, El, H = self.world, self.E, self.El, x.shape[1]
+        sc = K.scratch(x.device)
+        stream = K._stream()
+        offsets, row_of_slot, token_of_row = K.moe_permute(ids, E)
+        xs = K.gather_rows(x, token_of_row)
+        R = xs.shape[0]
+        counts = (offsets[1:] - offsets[:-1]).contiguous()
+        dist.all_gather_into_tensor(self.counts_all, counts, group=self.group)
+        dst_off = self.offs[:E]
+        loc_off = self.offs[E:E + El + 1]
+        src_off = self.offs[E + El + 1:]
+        _native.check(lib.ib_ep_offsets(self.counts_all.data_ptr(), W, E, self.rank, dst_off.data_ptr(),
+                                        loc_off.data_ptr(), src_off.data_ptr(), stream), "ib_ep_offsets")
+        self.round += 1
+        target = self.round * W
+        recv_peers = (ctypes.c_void_p * 8)(*[self._recv_view(b) for b in self.peers])
+        flagA = (ctypes.c_void_p * 8)(*[b for b in self.peers])
+        ctr = self.ctr.data_ptr()
+        _native.check(lib.ib_ep_dispatch(xs.data_ptr(), R, H, offsets.data_ptr(), E, W, dst_off.data_ptr(),
+                                         recv_peers, flagA, ctypes.c_void_p(ctr), stream), "ib_ep_dispatch")
+        _native.check(lib.ib_ep_wait(ctypes.c_void_p(self.base), target, sc.status.data_ptr(), stream), "ib_ep_wait")
+        recv = self._tensor_at(self._recv_view(self.base), self.max_rows)
+        bn = K.grouped_bn(R, El)
+        act = K.gemm_grouped(recv, self.w13, loc_off, swiglu=True, bn=bn)
+        out_r = K.gemm_grouped(act, self.w2, loc_off, bn=bn)
+        ret_peers = (ctypes.c_void_p * 8)(*[self._ret_view(b) for b in self.peers])
+        flagB = (ctypes.c_void_p * 8)(*[b + 4 for b in self.peers])
+        _native.check(lib.ib_ep_return(out_r.data_ptr(), self.max_rows, H, self.counts_all.data_ptr(), W, E,
+                                       self.rank, loc_off.data_ptr(), src_off.data_ptr(), ret_peers, flagB,
+                                       ctypes.c_void_p(ctr + 4), stream), "ib_ep_return")
+        _native.check(lib.ib_ep_wait(ctypes.c_void_p(self.base + 4), target, sc.status.data_ptr(), stream),
+                      "ib_ep_wait")
+        ret = self._tensor_at(self._ret_view(self.base), self.max_rows)
+        K._count(5)
+        self.stats["sent_rows"] += R
+        y = K.moe_combine(ret, row_of_slot, wts)
+        if self.shared is not None:
+            y = y + K.linear(K.linear(x, self.shared[0], swiglu=True), self.shared[1])
+        return y
+
+    def close(self) -> None:
+        if getattr(self, "base", None):
+            lib = _native.kernels()
+            torch.cuda.synchronize(self.device)
+            for r, p in enumerate(self.peers):
+                if r != self.rank:
+                    lib.ib_ipc_close(ctypes.c_void_p(p))
+            lib.ib_sym_free(ctypes.c_void_p(self.base))
+            self.base = None
 
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits=None, in_splits=None) -> None:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
@@ -56,6 +177,10 @@ class EPMoE:
         W, El, H = self.world, self.El, x.shape[1]
         if ids is None:
             ids, wts = self.route(x)
+        if self.fused:
+            if x.shape[0] * self.k * W > self.max_rows:
+                raise ValueError("more tokens than the symmetric buffers hold (raise max_tokens)")
+            return self._forward_fused(x, ids, wts)
         offsets, row_of_slot, token_of_row = K.moe_permute(ids, self.E)
         xs = K.gather_rows(x, token_of_row)
         send_counts = (offsets[1:] - offsets[:-1]).to(torch.int64).view(W, El).contiguous()
