@@ -5,7 +5,8 @@ footprint, inputs larger than L2 where the case is memory-bound).
 
 Cases: gemm_prefill (2048x6144x4096 bf16), gemm_decode (64 tokens x
 28672x4096, SwiGLU epilogue), gemm_lmhead (64x128256x4096), decode_attn
-(32 seqs x 8192 keys, GQA 32/8), prefill_attn (2048 queries over 2048 keys,
+(32 seqs x 8192 keys, GQA 32/8), fp8_decode (64 x 28672 x 8192 e4m3,
+block scales, SwiGLU), fp8_prefill (4096 x 8192 x 8192 e4m3), prefill_attn (2048 queries over 2048 keys,
 causal), prefill_attn_prefix (1024 queries over 8192 keys). Prints one JSON
 line per case: mean CUDA-event time per launch after 3 warm-up launches, and the
 achieved TFLOP/s or GB/s.
@@ -48,6 +49,19 @@ def run_case(case: str, iters: int) -> dict:
         fl = 2 * M * N * Kd
         by = (M * Kd + N * Kd + M * (N // 2 if swiglu else N)) * 2
         return {"case": case, "ms": ms, "tflops": fl / ms / 1e9, "gbs": by / ms / 1e6, "plan": K.gemm_plan(M, N, Kd)}
+    if case.startswith("fp8_"):
+        from infera_b200.ops import fp8
+
+        M, N, Kd, swiglu = {"fp8_decode": (64, 28672, 8192, True), "fp8_prefill": (4096, 8192, 8192, False),
+                            "fp8_decode_small": (8, 10240, 8192, False)}[case]
+        x = torch.randn(M, Kd, device=dev, generator=g).to(bf)
+        wq = fp8.quantize_weight(torch.randn(N, Kd, device=dev, generator=g) / math.sqrt(Kd))
+        q, sf = fp8.quant_act(x)
+        ms = _time(lambda: fp8.gemm_fp8(q, sf, wq, swiglu=swiglu), iters)
+        ms_q = _time(lambda: fp8.linear(x, wq, swiglu=swiglu), iters)
+        fl = 2 * M * N * Kd
+        by = M * Kd + N * Kd + N * Kd // 16384 + M * (N // 2 if swiglu else N) * 2
+        return {"case": case, "ms": ms, "ms_with_act_quant": ms_q, "tflops": fl / ms / 1e9, "gbs": by / ms / 1e6}
     hq, hkv, D = 32, 8, 128
     if case == "decode_attn":
         B, L = 32, 8192

@@ -20,6 +20,18 @@
 // Epilogues: plain bf16 store, or SwiGLU on row-interleaved (gate, up)
 // weights (row 2j = gate_j, row 2j+1 = up_j) writing silu(g)*u.
 //
+// fp8 (W8A8, e4m3) instantiation: the same pipeline with one 128-byte
+// stage = 128 K elements, issued as kind::mxf8f6f4.block_scale MMAs. Weights
+// carry one UE8M0 scale per 128x128 block and activations one per token and
+// 128-wide K group; the tensor core applies them per 32-wide K chunk, so no
+// promotion pass is needed. Four extra warps (6..9, one per TMEM lane
+// quadrant) stage each pipeline stage's scale factors into TMEM with
+// tcgen05.st: the weight block's byte in 4 columns, the tile's token scales
+// in 8 columns (token r at lane r % 32, column r / 32, replicated in every
+// lane quadrant). fp8 always runs swap-AB (UMMA M = 128 output features,
+// UMMA N = up to 192 tokens, a multiple of 32); TMEM holds two 192-column
+// accumulators and four 16-column scale slots.
+//
 // Reference parity: the reference delegates all GEMMs to its engines
 // (vLLM/hipBLASLt); there is no GEMM source in it to mirror.
 #include "sm100.cuh"
@@ -37,6 +49,11 @@ constexpr int Q_STAGE = MAX_BN * BK * 2;  // 32 KiB
 constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES = 1024 + STAGES * (P_STAGE + Q_STAGE) + 256;
+constexpr int NUM_THREADS_FP8 = 320;
+constexpr int MAX_BN_FP8 = 192;
+constexpr int BK_FP8 = 128;           // one 128-byte swizzle atom of e4m3
+constexpr int SF_COL0 = 2 * MAX_BN_FP8;  // scale slots after the accumulators
+constexpr int SF_SLOT = 16;              // per stage: A scales at +0 (4), B at +8 (8)
 
 enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_ATOMIC_F32 = 2 };
 constexpr int kMaxPeers = 8;
@@ -64,6 +81,12 @@ struct Params {
   const int4* gtab;
   const int* gnum;
   int n_per_expert;         // weight rows per expert (the grouped GEMM's N)
+  // fp8: UE8M0 scale bytes. sf_w [ceil(rows of W / 128), sf_w_ld] (one per
+  // 128x128 weight block); sf_a [K / 128, sf_a_ld] (K-group-major, one per
+  // token and 128-wide K group)
+  const uint8_t* sf_w;
+  const uint8_t* sf_a;
+  int sf_w_ld, sf_a_ld;
 };
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
@@ -225,9 +248,12 @@ __device__ __forceinline__ int tile_qrow(const Params& p, int t, int qt) {
   return p.grouped ? p.gtab[t].z : qt * p.bn;
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
-                     const Params p) {
+template <bool FP8>
+__global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
+                const Params p) {
+  constexpr int kBK = FP8 ? BK_FP8 : BK;          // K elements per stage (128 bytes per row)
+  constexpr int kAccCols = FP8 ? MAX_BN_FP8 : MAX_BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sP = smem;
@@ -238,7 +264,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* tfull = bars + 2 * STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* sf_full = drain + 1;  // fp8: scale factors of a stage are in TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_full + STAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -255,6 +282,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&tempty[a], 128);
     }
     mbar_init(drain, 1);
+    if (FP8)
+      for (int s = 0; s < STAGES; ++s) mbar_init(&sf_full[s], 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -277,7 +306,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint64_t pol_w = policy_evict_first();
       const uint64_t polP = p.swap ? pol_w : pol_act;
       const uint64_t polQ = p.swap ? pol_act : pol_w;
-      const uint32_t tx = static_cast<uint32_t>((BM + p.bn) * BK * 2);
+      const uint32_t tx = static_cast<uint32_t>((BM + p.bn) * 128);
       uint32_t stage = 0, phase = 0;
       long long issued = 0;
       bool ok = true;
@@ -292,8 +321,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           mbar_expect_tx(&full[stage], tx);
-          tma_load_2d(sP + stage * P_STAGE, &tmP, &full[stage], kb * BK, tile_prow(p, t, pt), polP);
-          tma_load_2d(sQ + stage * Q_STAGE, &tmQ, &full[stage], kb * BK, tile_qrow(p, t, qt), polQ);
+          tma_load_2d(sP + stage * P_STAGE, &tmP, &full[stage], kb * kBK, tile_prow(p, t, pt), polP);
+          tma_load_2d(sQ + stage * Q_STAGE, &tmQ, &full[stage], kb * kBK, tile_qrow(p, t, qt), polQ);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -311,7 +340,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = make_idesc_bf16(BM, p.bn);
+      const uint32_t idesc = FP8 ? make_idesc_mxf8(BM, p.bn) : make_idesc_bf16(BM, p.bn);
       uint32_t stage = 0, phase = 0;
       int local = 0;
       bool ok = true;
@@ -324,20 +353,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status, kStatusTimeoutTmemEmpty)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * MAX_BN;
+        const uint32_t d_tmem = tmem_base + acc * kAccCols;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          if (FP8 && !mbar_wait(&sf_full[stage], phase, abort_flag, p.status, kStatusTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sP + stage * P_STAGE);
           const uint32_t b_addr = smem_u32(sQ + stage * Q_STAGE);
+          // four UMMAs per 128-byte stage: K = 16 (bf16) or 32 (e4m3) each,
+          // 32 bytes further into the swizzle atom
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
+          for (int kk = 0; kk < 4; ++kk) {
             const uint64_t ad = make_sw128_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = make_sw128_desc(b_addr + kk * 32, 16, 1024);
-            umma_bf16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            if (FP8) {
+              const uint32_t sfa = tmem_base + SF_COL0 + stage * SF_SLOT;
+              umma_mxf8(d_tmem, ad, bd, idesc, sfa, sfa + 8, (kb > kb0 || kk > 0) ? 1u : 0u);
+            } else {
+              umma_bf16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            }
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -351,6 +391,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       umma_commit(drain);
       mbar_wait(drain, 0, nullptr, p.status, kStatusTimeoutFull);
     }
+  } else if (FP8 && warp >= 6) {
+    // scale-factor stagers: one warp per TMEM lane quadrant writes the same
+    // values into its own quadrant
+    const int q = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      int pt, qt, sp;
+      tile_coords(p, t, pt, qt, sp);
+      const int kb0 = sp * p.kbps;
+      const int kb1 = min(kb0 + p.kbps, p.nkb);
+      const int wrow = tile_prow(p, t, pt) / BM;
+      const int tok0 = tile_qrow(p, t, qt);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_warp(&empty[stage], phase ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();  // the MMAs that read this slot before have completed
+        const uint32_t wb = __ldg(p.sf_w + static_cast<size_t>(wrow) * p.sf_w_ld + kb) * 0x01010101u;
+        uint32_t r[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int tok = tok0 + c * 32 + lane;
+          const uint32_t b = (c * 32 < p.bn && tok < p.M)
+                                 ? __ldg(p.sf_a + static_cast<size_t>(kb) * p.sf_a_ld + tok)
+                                 : 127u;
+          r[c] = b * 0x01010101u;
+        }
+        const uint32_t slot = tmem_base + lane_base + SF_COL0 + stage * SF_SLOT;
+        tmem_st4(slot, wb, wb, wb, wb);
+        tmem_st8(slot + 8, r);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sf_full[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
   } else {
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = q * 32 + lane;
@@ -362,7 +445,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutTmemFull)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * MAX_BN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kAccCols;
       int c0 = 0;
       for (; c0 + 32 <= p.bn; c0 += 32) {
         uint32_t r[32];
@@ -385,7 +468,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   // push mode: make this thread's peer stores visible system-wide before
   // the CTA reports completion
-  if (p.push && warp >= 2) __threadfence_system();
+  if (p.push && warp >= 2 && warp < 6) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -484,6 +567,68 @@ struct Plan {
   int grid;
 };
 
+template <bool FP8>
+inline int launch_gemm(const CUtensorMap& tmP, const CUtensorMap& tmQ, const Params& p, int grid,
+                       cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaFuncSetAttribute(gemm_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_set[dev] = true;
+  }
+  gemm_kernel<FP8><<<grid, FP8 ? NUM_THREADS_FP8 : NUM_THREADS, SMEM_BYTES, stream>>>(tmP, tmQ, p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+// Split-K factor for a plan whose tiles are set: minimise waves/split (time
+// in units of one full tile), with a 3% penalty per extra split for the
+// atomics and the finalize pass.
+inline void choose_splits(Plan& pl, int num_sms, int force_split) {
+  Params& p = pl.p;
+  const int tiles = p.p_tiles * p.q_tiles;
+  int best = 1;
+  if (force_split > 0) {
+    best = force_split;
+  } else if (tiles < num_sms) {
+    double best_cost = 1e30;
+    for (int s = 1; s <= 16; ++s) {
+      if (p.nkb / s < 4 && s > 1) break;
+      double waves = static_cast<double>((tiles * s + num_sms - 1) / num_sms);
+      double cost = waves / s * (1.0 + 0.03 * (s - 1));
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = s;
+      }
+    }
+  }
+  if ((p.N % 4) != 0) best = 1;
+  p.kbps = (p.nkb + best - 1) / best;
+  p.splits = (p.nkb + p.kbps - 1) / p.kbps;
+  const int units = tiles * p.splits;
+  pl.grid = units < num_sms ? units : num_sms;
+}
+
+// fp8 plan: always swap-AB; token tiles of up to 192 (multiples of 32)
+// balanced over the token count.
+inline Plan make_plan_fp8(int M, int N, int K, int num_sms, int force_split) {
+  Plan pl{};
+  Params& p = pl.p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.nkb = K / BK_FP8;
+  p.swap = 1;
+  const int qt = (M + MAX_BN_FP8 - 1) / MAX_BN_FP8;
+  const int per = (M + qt - 1) / qt;
+  p.bn = ((per + 31) / 32) * 32;
+  p.p_tiles = (N + BM - 1) / BM;
+  p.q_tiles = qt;
+  choose_splits(pl, num_sms, force_split);
+  return pl;
+}
+
 // Choose operand order, tile width and split-K factor for one problem.
 inline Plan make_plan(int M, int N, int K, int num_sms, int force_split) {
   Plan pl{};
@@ -502,29 +647,7 @@ inline Plan make_plan(int M, int N, int K, int num_sms, int force_split) {
     p.p_tiles = (M + BM - 1) / BM;
     p.q_tiles = (N + MAX_BN - 1) / MAX_BN;
   }
-  const int tiles = p.p_tiles * p.q_tiles;
-  int best = 1;
-  if (force_split > 0) {
-    best = force_split;
-  } else if (tiles < num_sms) {
-    // minimise waves/split (time in units of one full tile), with a 3%
-    // penalty per extra split for the atomics and the finalize pass
-    double best_cost = 1e30;
-    for (int s = 1; s <= 16; ++s) {
-      if (p.nkb / s < 4 && s > 1) break;
-      double waves = static_cast<double>((tiles * s + num_sms - 1) / num_sms);
-      double cost = waves / s * (1.0 + 0.03 * (s - 1));
-      if (cost < best_cost - 1e-9) {
-        best_cost = cost;
-        best = s;
-      }
-    }
-  }
-  if ((N % 4) != 0) best = 1;
-  p.kbps = (p.nkb + best - 1) / best;
-  p.splits = (p.nkb + p.kbps - 1) / p.kbps;
-  const int units = tiles * p.splits;
-  pl.grid = units < num_sms ? units : num_sms;
+  choose_splits(pl, num_sms, force_split);
   return pl;
 }
 
@@ -533,19 +656,57 @@ inline Plan make_plan(int M, int N, int K, int num_sms, int force_split) {
 
 using namespace ib200;
 
-// C ABI. Returns 0 on success, a negative code on bad arguments / encode
-// failure, or a CUDA error code from the launch.
-//   epi: 0 = bf16 store, 1 = SwiGLU (out has N/2 columns)
-//   ws : fp32 workspace of >= M*N floats, all zero on entry (left zero), only
-//        touched when the plan splits K; may be null if split_k == 1 forced.
-extern "C" int ib_gemm_bf16(const void* A, const void* W, void* out, int M, int N, int K, int lda, int ldw,
-                            int ldc, int epi, float* ws, int force_split, int* status, cudaStream_t stream) {
-  using namespace ib200::gemm;
+namespace ib200 {
+namespace gemm {
+
+// Operand element type of one launch: bf16, or e4m3 with UE8M0 block scales.
+struct Operands {
+  bool fp8;
+  const uint8_t* sf_a;  // [K/128, sf_a_ld]
+  int sf_a_ld;
+  const uint8_t* sf_w;  // [weight rows / 128, K/128]
+};
+
+inline bool operands_ok(const Operands& o, int K, int lda, int ldw) {
+  if (!o.fp8) return (K % 8) == 0 && (lda % 8) == 0 && (ldw % 8) == 0;
+  return (K % BK_FP8) == 0 && (lda % 16) == 0 && (ldw % 16) == 0 && o.sf_a != nullptr && o.sf_w != nullptr;
+}
+
+inline void set_scales(Params& p, const Operands& o) {
+  p.sf_a = o.sf_a;
+  p.sf_a_ld = o.sf_a_ld;
+  p.sf_w = o.sf_w;
+  p.sf_w_ld = p.K / BK_FP8;
+}
+
+inline bool encode_pq(const Operands& o, const Params& p, const void* A, const void* W, long long w_rows, int lda,
+                      int ldw, CUtensorMap* tmP, CUtensorMap* tmQ) {
+  const void* Pbase = p.swap ? W : A;
+  const void* Qbase = p.swap ? A : W;
+  const long long Prows = p.swap ? w_rows : p.M;
+  const long long Qrows = p.swap ? p.M : w_rows;
+  const int Pld = p.swap ? ldw : lda;
+  const int Qld = p.swap ? lda : ldw;
+  if (o.fp8)
+    return cached_tmap_2d(tmP, Pbase, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Prows, p.K, Pld, BM, BK_FP8) &&
+           cached_tmap_2d(tmQ, Qbase, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Qrows, p.K, Qld, p.bn, BK_FP8);
+  return cached_tmap_2d(tmP, Pbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Prows, p.K, Pld, BM, BK) &&
+         cached_tmap_2d(tmQ, Qbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Qrows, p.K, Qld, p.bn, BK);
+}
+
+inline int launch(const Operands& o, const CUtensorMap& tmP, const CUtensorMap& tmQ, const Params& p, int grid,
+                  cudaStream_t stream) {
+  return o.fp8 ? launch_gemm<true>(tmP, tmQ, p, grid, stream) : launch_gemm<false>(tmP, tmQ, p, grid, stream);
+}
+
+inline int run_dense(const Operands& o, const void* A, const void* W, void* out, int M, int N, int K, int lda,
+                     int ldw, int ldc, int epi, float* ws, int force_split, int* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  if ((K % 8) != 0 || (lda % 8) != 0 || (ldw % 8) != 0) return -1;
+  if (!operands_ok(o, K, lda, ldw)) return -1;
   if (epi == EPI_SWIGLU && (N % 2) != 0) return -1;
   const int num_sms = num_sms_for_current_device();
-  Plan pl = make_plan(M, N, K, num_sms, ws == nullptr ? 1 : force_split);
+  const int fs = ws == nullptr ? 1 : force_split;
+  Plan pl = o.fp8 ? make_plan_fp8(M, N, K, num_sms, fs) : make_plan(M, N, K, num_sms, fs);
   Params& p = pl.p;
   p.status = status;
   p.ldc = ldc;
@@ -553,56 +714,35 @@ extern "C" int ib_gemm_bf16(const void* A, const void* W, void* out, int M, int 
   p.world = 1;
   p.done_ctr = nullptr;
   p.grouped = 0;
+  set_scales(p, o);
   const bool split = p.splits > 1;
   p.epi = split ? EPI_ATOMIC_F32 : epi;
   p.out = split ? static_cast<void*>(ws) : out;
-
   CUtensorMap tmP, tmQ;
-  const void* Pbase = p.swap ? W : A;
-  const void* Qbase = p.swap ? A : W;
-  const int Prows = p.swap ? N : M;
-  const int Qrows = p.swap ? M : N;
-  const int Pld = p.swap ? ldw : lda;
-  const int Qld = p.swap ? lda : ldw;
-  if (!cached_tmap_2d(&tmP, Pbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Prows, K, Pld, BM, BK)) return -2;
-  if (!cached_tmap_2d(&tmQ, Qbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Qrows, K, Qld, p.bn, BK)) return -2;
-
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    attr_set[dev] = true;
-  }
-  gemm_bf16_kernel<<<pl.grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmP, tmQ, p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return static_cast<int>(e);
+  if (!encode_pq(o, p, A, W, N, lda, ldw, &tmP, &tmQ)) return -2;
+  int rc = launch(o, tmP, tmQ, p, pl.grid, stream);
+  if (rc != 0) return rc;
   if (split) {
     dim3 g((N + 1023) / 1024, M);
     splitk_finalize_kernel<<<g, 256, 0, stream>>>(ws, static_cast<__nv_bfloat16*>(out), M, N, ldc,
                                                   epi == EPI_SWIGLU ? 1 : 0);
-    e = cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   return 0;
 }
 
-// Fused GEMM + one-shot all-reduce push (row-parallel tensor-parallel
-// layers): out = A @ W^T computed locally, each tile stored to
-// peer_out[d] (this rank's receive slot on rank d, bf16 [M, ldc]) for every
-// rank d, then peer_flag[d] (rank d's arrival counter for this rank) is
-// incremented once. done_ctr: a local zero-initialised counter. No split-K.
-extern "C" int ib_gemm_bf16_push(const void* A, const void* W, int M, int N, int K, int lda, int ldw, int ldc,
-                                 int world, void* const* peer_out, unsigned int* const* peer_flag,
-                                 unsigned int* done_ctr, float* ws, int* status, cudaStream_t stream) {
-  using namespace ib200::gemm;
+inline int run_push(const Operands& o, const void* A, const void* W, int M, int N, int K, int lda, int ldw, int ldc,
+                    int world, void* const* peer_out, unsigned int* const* peer_flag, unsigned int* done_ctr,
+                    float* ws, int* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  if ((K % 8) != 0 || (lda % 8) != 0 || (ldw % 8) != 0) return -1;
+  if (!operands_ok(o, K, lda, ldw)) return -1;
   if (world < 1 || world > kMaxPeers) return -1;
   const int num_sms = num_sms_for_current_device();
   // split K like the plain GEMM does (small M leaves most SMs idle
   // otherwise); the split path pushes from its finalize kernel
-  Plan pl = make_plan(M, N, K, num_sms, ws == nullptr ? 1 : 0);
+  const int fs = ws == nullptr ? 1 : 0;
+  Plan pl = o.fp8 ? make_plan_fp8(M, N, K, num_sms, fs) : make_plan(M, N, K, num_sms, fs);
   Params& p = pl.p;
   const bool split = p.splits > 1;
   p.status = status;
@@ -617,25 +757,11 @@ extern "C" int ib_gemm_bf16_push(const void* A, const void* W, int M, int N, int
   }
   p.done_ctr = done_ctr;
   p.grouped = 0;
+  set_scales(p, o);
   CUtensorMap tmP, tmQ;
-  const void* Pbase = p.swap ? W : A;
-  const void* Qbase = p.swap ? A : W;
-  const int Prows = p.swap ? N : M;
-  const int Qrows = p.swap ? M : N;
-  const int Pld = p.swap ? ldw : lda;
-  const int Qld = p.swap ? lda : ldw;
-  if (!cached_tmap_2d(&tmP, Pbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Prows, K, Pld, BM, BK)) return -2;
-  if (!cached_tmap_2d(&tmQ, Qbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Qrows, K, Qld, p.bn, BK)) return -2;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    attr_set[dev] = true;
-  }
-  gemm_bf16_kernel<<<pl.grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmP, tmQ, p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return static_cast<int>(e);
+  if (!encode_pq(o, p, A, W, N, lda, ldw, &tmP, &tmQ)) return -2;
+  int rc = launch(o, tmP, tmQ, p, pl.grid, stream);
+  if (rc != 0) return rc;
   if (split) {
     PushDst dst;
     for (int d = 0; d < kMaxPeers; ++d) {
@@ -644,25 +770,19 @@ extern "C" int ib_gemm_bf16_push(const void* A, const void* W, int M, int N, int
     }
     dim3 g((N + 1023) / 1024, M);
     splitk_finalize_push_kernel<<<g, 256, 0, stream>>>(ws, M, N, ldc, world, dst, done_ctr);
-    e = cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   return 0;
 }
 
-// Grouped GEMM over experts (swap-AB): for every tile {e, n_tile, m0, mend}
-// of gtab[0 .. *gnum), out[m, :] (rows m0 .. mend-1) = A[m, :] @ W[e]^T
-// restricted to features [n_tile*128, +128). A: [R, K] tokens sorted by
-// expert; W: [E, N, K] stacked; out: [R, ldc] (N/2 columns with SwiGLU).
-// bn: token columns per tile (16 / 32 / 64 / 128 / 256); grid_tiles: the
-// most tiles gtab can hold (sizes the persistent grid).
-extern "C" int ib_gemm_grouped(const void* A, const void* W, void* out, int R, int N, int K, int E, int lda, int ldw,
-                               int ldc, int epi, const int* gtab, const int* gnum, int bn, int grid_tiles, int* status,
-                               cudaStream_t stream) {
-  using namespace ib200::gemm;
+inline int run_grouped(const Operands& o, const void* A, const void* W, void* out, int R, int N, int K, int E,
+                       int lda, int ldw, int ldc, int epi, const int* gtab, const int* gnum, int bn, int grid_tiles,
+                       int* status, cudaStream_t stream) {
   if (R <= 0 || N <= 0 || K <= 0 || E <= 0) return 0;
-  if ((K % 8) != 0 || (lda % 8) != 0 || (ldw % 8) != 0 || (N % BM) != 0) return -1;
-  if (bn < 16 || bn > MAX_BN || (bn % 16) != 0) return -1;
+  if (!operands_ok(o, K, lda, ldw) || (N % BM) != 0) return -1;
+  if (o.fp8 ? (bn < 32 || bn > MAX_BN_FP8 || (bn % 32) != 0) : (bn < 16 || bn > MAX_BN || (bn % 16) != 0))
+    return -1;
   if (epi == EPI_SWIGLU && (N % 2) != 0) return -1;
   Params p{};
   p.M = R;
@@ -671,7 +791,7 @@ extern "C" int ib_gemm_grouped(const void* A, const void* W, void* out, int R, i
   p.bn = bn;
   p.swap = 1;
   p.splits = 1;
-  p.nkb = (K + BK - 1) / BK;
+  p.nkb = o.fp8 ? K / BK_FP8 : (K + BK - 1) / BK;
   p.kbps = p.nkb;
   p.p_tiles = 1;
   p.q_tiles = 1;
@@ -683,22 +803,79 @@ extern "C" int ib_gemm_grouped(const void* A, const void* W, void* out, int R, i
   p.gtab = reinterpret_cast<const int4*>(gtab);
   p.gnum = gnum;
   p.n_per_expert = N;
+  set_scales(p, o);
   CUtensorMap tmP, tmQ;
-  if (!cached_tmap_2d(&tmP, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<long long>(E) * N, K, ldw, BM, BK))
-    return -2;
-  if (!cached_tmap_2d(&tmQ, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, K, lda, bn, BK)) return -2;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    attr_set[dev] = true;
-  }
+  if (!encode_pq(o, p, A, W, static_cast<long long>(E) * N, lda, ldw, &tmP, &tmQ)) return -2;
   const int num_sms = num_sms_for_current_device();
   const int grid = grid_tiles < num_sms ? (grid_tiles > 0 ? grid_tiles : 1) : num_sms;
-  gemm_bf16_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmP, tmQ, p);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 0 : static_cast<int>(e);
+  return launch(o, tmP, tmQ, p, grid, stream);
+}
+
+}  // namespace gemm
+}  // namespace ib200
+
+// C ABI. Returns 0 on success, a negative code on bad arguments / encode
+// failure, or a CUDA error code from the launch.
+//   epi: 0 = bf16 store, 1 = SwiGLU (out has N/2 columns)
+//   ws : fp32 workspace of >= M*N floats, all zero on entry (left zero), only
+//        touched when the plan splits K; may be null if split_k == 1 forced.
+extern "C" int ib_gemm_bf16(const void* A, const void* W, void* out, int M, int N, int K, int lda, int ldw,
+                            int ldc, int epi, float* ws, int force_split, int* status, cudaStream_t stream) {
+  const gemm::Operands o{false, nullptr, 0, nullptr};
+  return gemm::run_dense(o, A, W, out, M, N, K, lda, ldw, ldc, epi, ws, force_split, status, stream);
+}
+
+// W8A8 e4m3 GEMM with UE8M0 block scales: A [M, K] e4m3 (row pitch lda
+// bytes), sf_a [K/128, sf_a_ld] (token-group scales, K-group-major), W
+// [N, K] e4m3, sf_w [ceil(N/128), K/128] (128x128 block scales); out bf16.
+extern "C" int ib_gemm_fp8(const void* A, const uint8_t* sf_a, int sf_a_ld, const void* W, const uint8_t* sf_w,
+                           void* out, int M, int N, int K, int lda, int ldw, int ldc, int epi, float* ws,
+                           int force_split, int* status, cudaStream_t stream) {
+  const gemm::Operands o{true, sf_a, sf_a_ld, sf_w};
+  return gemm::run_dense(o, A, W, out, M, N, K, lda, ldw, ldc, epi, ws, force_split, status, stream);
+}
+
+// Fused GEMM + one-shot all-reduce push (row-parallel tensor-parallel
+// layers): out = A @ W^T computed locally, each tile stored to
+// peer_out[d] (this rank's receive slot on rank d, bf16 [M, ldc]) for every
+// rank d, then peer_flag[d] (rank d's arrival counter for this rank) is
+// incremented once. done_ctr: a local zero-initialised counter.
+extern "C" int ib_gemm_bf16_push(const void* A, const void* W, int M, int N, int K, int lda, int ldw, int ldc,
+                                 int world, void* const* peer_out, unsigned int* const* peer_flag,
+                                 unsigned int* done_ctr, float* ws, int* status, cudaStream_t stream) {
+  const gemm::Operands o{false, nullptr, 0, nullptr};
+  return gemm::run_push(o, A, W, M, N, K, lda, ldw, ldc, world, peer_out, peer_flag, done_ctr, ws, status, stream);
+}
+
+extern "C" int ib_gemm_fp8_push(const void* A, const uint8_t* sf_a, int sf_a_ld, const void* W, const uint8_t* sf_w,
+                                int M, int N, int K, int lda, int ldw, int ldc, int world, void* const* peer_out,
+                                unsigned int* const* peer_flag, unsigned int* done_ctr, float* ws, int* status,
+                                cudaStream_t stream) {
+  const gemm::Operands o{true, sf_a, sf_a_ld, sf_w};
+  return gemm::run_push(o, A, W, M, N, K, lda, ldw, ldc, world, peer_out, peer_flag, done_ctr, ws, status, stream);
+}
+
+// Grouped GEMM over experts (swap-AB): for every tile {e, n_tile, m0, mend}
+// of gtab[0 .. *gnum), out[m, :] (rows m0 .. mend-1) = A[m, :] @ W[e]^T
+// restricted to features [n_tile*128, +128). A: [R, K] tokens sorted by
+// expert; W: [E, N, K] stacked; out: [R, ldc] (N/2 columns with SwiGLU).
+// bn: token columns per tile (16 / 32 / 64 / 128 / 256); grid_tiles: the
+// most tiles gtab can hold (sizes the persistent grid).
+extern "C" int ib_gemm_grouped(const void* A, const void* W, void* out, int R, int N, int K, int E, int lda, int ldw,
+                               int ldc, int epi, const int* gtab, const int* gnum, int bn, int grid_tiles, int* status,
+                               cudaStream_t stream) {
+  const gemm::Operands o{false, nullptr, 0, nullptr};
+  return gemm::run_grouped(o, A, W, out, R, N, K, E, lda, ldw, ldc, epi, gtab, gnum, bn, grid_tiles, status, stream);
+}
+
+// fp8 grouped GEMM: as above with e4m3 operands; sf_a [K/128, sf_a_ld] over
+// the sorted rows, sf_w [E*N/128, K/128]; bn a multiple of 32 up to 192.
+extern "C" int ib_gemm_fp8_grouped(const void* A, const uint8_t* sf_a, int sf_a_ld, const void* W,
+                                   const uint8_t* sf_w, void* out, int R, int N, int K, int E, int lda, int ldw,
+                                   int ldc, int epi, const int* gtab, const int* gnum, int bn, int grid_tiles,
+                                   int* status, cudaStream_t stream) {
+  const gemm::Operands o{true, sf_a, sf_a_ld, sf_w};
+  return gemm::run_grouped(o, A, W, out, R, N, K, E, lda, ldw, ldc, epi, gtab, gnum, bn, grid_tiles, status, stream);
 }
 
 // Plan introspection for tests and benchmarks: writes
@@ -706,6 +883,18 @@ extern "C" int ib_gemm_grouped(const void* A, const void* W, void* out, int R, i
 extern "C" void ib_gemm_bf16_plan(int M, int N, int K, int num_sms, int force_split, int* out7) {
   using namespace ib200::gemm;
   Plan pl = make_plan(M, N, K, num_sms, force_split);
+  out7[0] = pl.p.swap;
+  out7[1] = pl.p.bn;
+  out7[2] = pl.p.p_tiles;
+  out7[3] = pl.p.q_tiles;
+  out7[4] = pl.p.splits;
+  out7[5] = pl.p.kbps;
+  out7[6] = pl.grid;
+}
+
+extern "C" void ib_gemm_fp8_plan(int M, int N, int K, int num_sms, int force_split, int* out7) {
+  using namespace ib200::gemm;
+  Plan pl = make_plan_fp8(M, N, K, num_sms, force_split);
   out7[0] = pl.p.swap;
   out7[1] = pl.p.bn;
   out7[2] = pl.p.p_tiles;

@@ -128,6 +128,11 @@ PRESETS: dict[str, DenseConfig | MoEConfig] = {
                               vocab=1024, max_model_len=2048, eos_token_id=1),
     "tiny-dense-gpu": DenseConfig(name="tiny-dense-gpu", num_layers=2, hidden=1024, num_heads=8, num_kv_heads=2,
                                   ffn=2048, vocab=4096, max_model_len=4096, eos_token_id=1),
+    "tiny-dense-fp8": DenseConfig(name="tiny-dense-fp8", num_layers=2, hidden=256, num_heads=4, num_kv_heads=2,
+                                  ffn=512, vocab=1024, max_model_len=2048, eos_token_id=1, weight_dtype="fp8"),
+    "tiny-dense-fp8-gpu": DenseConfig(name="tiny-dense-fp8-gpu", num_layers=2, hidden=1024, num_heads=8,
+                                      num_kv_heads=2, ffn=2048, vocab=4096, max_model_len=4096, eos_token_id=1,
+                                      weight_dtype="fp8"),
     "tiny-moe-gqa": DenseConfig(name="tiny-moe-gqa", num_layers=3, hidden=256, num_heads=4, num_kv_heads=2,
                                 ffn=512, vocab=1024, max_model_len=2048, eos_token_id=1, num_experts=8, moe_top_k=2,
                                 moe_ffn=128, moe_first_layer=1, moe_n_groups=2, moe_topk_groups=1,

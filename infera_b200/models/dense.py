@@ -104,6 +104,11 @@ class DenseWeights:
                 "down": shard_cols(dn, r * f, (r + 1) * f),
             }
             del qkv, o, gu, dn
+            if cfg.weight_dtype == "fp8":
+                from infera_b200.ops import fp8
+
+                for key in ("qkv", "o", "gate_up", "down"):
+                    lw[key] = fp8.quantize_weight(lw[key])
             if cfg.is_moe_layer(li):
                 if W > 1:
                     raise NotImplementedError("tensor parallelism of expert layers (use expert parallelism)")
@@ -124,14 +129,16 @@ class DenseWeights:
         del lm
 
     def nbytes(self) -> int:
-        n = self.embed.numel() + self.lm_head.numel() + self.final_norm.numel()
+        n = 2 * (self.embed.numel() + self.lm_head.numel() + self.final_norm.numel())
         for lw in self.layers:
             for k, t in lw.items():
                 if k == "moe":
-                    n += t.w13.numel() + t.w2.numel() + t.gate.numel()
-                else:
-                    n += t.numel()
-        return 2 * n
+                    n += 2 * (t.w13.numel() + t.w2.numel() + t.gate.numel())
+                elif isinstance(t, torch.Tensor):
+                    n += 2 * t.numel()
+                else:  # fp8 weight: 1 byte per element + one scale byte per block
+                    n += t.q.numel() + t.sf.numel()
+        return n
 
 
 class DenseModel:

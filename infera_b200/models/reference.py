@@ -24,6 +24,16 @@ def reference_logits(model: DenseModel, token_ids: list[int]) -> torch.Tensor:
     def f(t):
         return t.detach().float().cpu()
 
+    def mm(x, wt):
+        """x @ W^T; an fp8 weight also quantises x the way the engine does
+        (e4m3 with a power-of-two scale per token and 128-wide group)."""
+        if isinstance(wt, torch.Tensor):
+            return x @ f(wt).t()
+        from infera_b200.ops import fp8
+
+        q, sf = fp8.quant_act(x.to(torch.bfloat16))
+        return fp8.dequant_act(q, sf) @ wt.to("cpu").dequant().t()
+
     def norm(x, g, eps=cfg.rms_eps):
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * f(g)
 
@@ -37,7 +47,7 @@ def reference_logits(model: DenseModel, token_ids: list[int]) -> torch.Tensor:
     mask = torch.triu(torch.ones(T, T, dtype=torch.bool), 1)
     for lw in w.layers:
         x = norm(h, lw["ln1"])
-        qkv = x @ f(lw["qkv"]).t()
+        qkv = mm(x, lw["qkv"])
         q = qkv[:, : nq * D].view(T, nq, D)
         k = qkv[:, nq * D:(nq + nk) * D].view(T, nk, D)
         v = qkv[:, (nq + nk) * D:].view(T, nk, D)
@@ -50,14 +60,14 @@ def reference_logits(model: DenseModel, token_ids: list[int]) -> torch.Tensor:
         s = torch.einsum("thd,shd->hts", q, k) / D ** 0.5
         s = s.masked_fill(mask[None], float("-inf"))
         o = torch.einsum("hts,shd->thd", torch.softmax(s, -1), v).reshape(T, nq * D)
-        h = h + o @ f(lw["o"]).t()
+        h = h + mm(o, lw["o"])
         x = norm(h, lw["ln2"])
         if "moe" in lw:
             h = h + _moe_ref(lw["moe"], x, f)
             continue
-        gu = x @ f(lw["gate_up"]).t()
+        gu = mm(x, lw["gate_up"])
         act = torch.nn.functional.silu(gu[:, 0::2]) * gu[:, 1::2]
-        h = h + act @ f(lw["down"]).t()
+        h = h + mm(act, lw["down"])
     x = norm(h, w.final_norm)
     return x @ f(w.lm_head).t()
 

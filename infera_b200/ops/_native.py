@@ -78,13 +78,21 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_gemm_grouped": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp,
                             c_int, c_int, c_vp, c_vp],
         "ib_kv_push_pages": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_int, c_int, c_vp],
+        "ib_gemm_fp8": [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp,
+                        c_int, c_vp, c_vp],
+        "ib_gemm_fp8_push": [c_vp, c_vp, c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp,
+                             c_vp, c_vp, c_vp, c_vp, c_vp],
+        "ib_gemm_fp8_grouped": [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int,
+                                c_int, c_int, c_vp, c_vp, c_int, c_int, c_vp, c_vp],
+        "ib_gemm_fp8_plan": [c_int, c_int, c_int, c_int, c_int, c_vp],
+        "ib_quant_fp8_act": [c_vp, c_int, c_int, c_int, c_vp, c_int, c_vp, c_int, c_vp],
     }
     for name, args in sig.items():
         fn = getattr(lib, name, None)
         if fn is None:
             continue
         fn.argtypes = args
-        fn.restype = c_int if name != "ib_gemm_bf16_plan" else None
+        fn.restype = None if name in ("ib_gemm_bf16_plan", "ib_gemm_fp8_plan") else c_int
 
 
 def kernels() -> ctypes.CDLL:

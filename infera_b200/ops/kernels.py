@@ -136,6 +136,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, sw
     ``swiglu=True`` expects ``w`` rows interleaved as (gate_0, up_0, gate_1,
     up_1, ...) and returns silu(gate) * up with half the columns.
     """
+    if not isinstance(w, torch.Tensor):  # fp8 block-scaled weight
+        from infera_b200.ops import fp8
+
+        return fp8.linear(x, w, out=out, swiglu=swiglu)
     M, K = x.shape
     N = w.shape[0]
     n_out = N // 2 if swiglu else N

@@ -128,12 +128,23 @@ class TPComm:
                                                     for d in range(self.world)])
         ctr = self.ctr.data_ptr()
         stream = K._stream()
-        splits = K._gemm_splits(M, N, Kd, 0)
-        ws = sc.ensure_gemm(M * N if splits > 1 else 1)
-        rc = lib.ib_gemm_bf16_push(x.data_ptr(), w.data_ptr(), M, N, Kd, x.stride(0), w.stride(0), self.hidden,
-                                   self.world, peer_out, peer_flag, ctypes.c_void_p(ctr + 4 * parity),
-                                   ws.data_ptr(), sc.status.data_ptr(), stream)
-        _native.check(rc, "ib_gemm_bf16_push")
+        if isinstance(w, torch.Tensor):
+            splits = K._gemm_splits(M, N, Kd, 0)
+            ws = sc.ensure_gemm(M * N if splits > 1 else 1)
+            rc = lib.ib_gemm_bf16_push(x.data_ptr(), w.data_ptr(), M, N, Kd, x.stride(0), w.stride(0), self.hidden,
+                                       self.world, peer_out, peer_flag, ctypes.c_void_p(ctr + 4 * parity),
+                                       ws.data_ptr(), sc.status.data_ptr(), stream)
+            _native.check(rc, "ib_gemm_bf16_push")
+        else:  # fp8 block-scaled weight: quantise the activation, same push epilogue
+            from infera_b200.ops import fp8
+
+            q, sf = fp8.quant_act(x)
+            splits = fp8._splits(M, N, Kd)
+            ws = sc.ensure_gemm(M * N if splits > 1 else 1)
+            rc = lib.ib_gemm_fp8_push(q.data_ptr(), sf.data_ptr(), sf.stride(0), w.q.data_ptr(), w.sf.data_ptr(), M,
+                                      N, Kd, q.stride(0), w.q.stride(0), self.hidden, self.world, peer_out, peer_flag,
+                                      ctypes.c_void_p(ctr + 4 * parity), ws.data_ptr(), sc.status.data_ptr(), stream)
+            _native.check(rc, "ib_gemm_fp8_push")
         rc = lib.ib_ar_add_rmsnorm(ctypes.c_void_p(self._slot(self.base, parity, 0)), self.slot_elems, self.hidden,
                                    ctypes.c_void_p(self._flag(self.base, parity, 0)),
                                    ctypes.c_void_p(ctr + 4 * (2 + parity)), ctypes.c_void_p(ctr + 4 * (4 + parity)),
