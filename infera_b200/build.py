@@ -3,9 +3,6 @@
 * ``infera_b200/lib/libib200_kernels.so`` - every ``csrc/*.cu`` compiled for
   sm_100a only (``-gencode arch=compute_100a,code=sm_100a``), C ABI, no torch
   headers (fast to build, loadable with ctypes, travels with the tree).
-* ``infera_b200/lib/libib200_runtime.so`` - host-side C++ runtime
-  (``csrc/runtime/*.cpp``): XXH3 chained block hashing, the paged-KV block
-  allocator with prefix cache, and the scheduler's batch packer.
 * ``infera_b200/lib/ib200_router`` - the native router data plane
   (``native/router/*.cpp``).
 
@@ -24,13 +21,11 @@ from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
-RUNTIME_SRC = CSRC / "runtime"
 ROUTER_SRC = PKG / "native" / "router"
 LIB = PKG / "lib"
 OBJ = PKG / "lib" / "obj"
 
 KERNELS_SO = LIB / "libib200_kernels.so"
-RUNTIME_SO = LIB / "libib200_runtime.so"
 ROUTER_BIN = LIB / "ib200_router"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -83,18 +78,6 @@ def build_kernels(verbose: bool = False, jobs: int | None = None) -> Path:
     return KERNELS_SO
 
 
-def build_runtime() -> Path | None:
-    sources = sorted(RUNTIME_SRC.glob("*.cpp")) if RUNTIME_SRC.exists() else []
-    if not sources:
-        return None
-    headers = sorted(RUNTIME_SRC.glob("*.h"))
-    if _newer([*sources, *headers], RUNTIME_SO):
-        LIB.mkdir(parents=True, exist_ok=True)
-        _run(["g++", "-O3", "-std=c++17", "-fPIC", "-shared", "-march=x86-64-v2", "-o", str(RUNTIME_SO),
-              *map(str, sources), "-lpthread"])
-    return RUNTIME_SO
-
-
 def xxhash_include() -> Path:
     """Directory holding the reference xxHash header (BSD-2-Clause), which
     the native code includes for XXH3-64: bit-exact with the Python
@@ -117,7 +100,7 @@ def build_router() -> Path | None:
     sources = sorted(ROUTER_SRC.glob("*.cpp")) if ROUTER_SRC.exists() else []
     if not sources:
         return None
-    headers = sorted(ROUTER_SRC.glob("*.h")) + sorted(RUNTIME_SRC.glob("*.h"))
+    headers = sorted(ROUTER_SRC.glob("*.h"))
     if _newer([*sources, *headers], ROUTER_BIN):
         LIB.mkdir(parents=True, exist_ok=True)
         objs = []
@@ -138,8 +121,6 @@ def build_router() -> Path | None:
 
 def build_all(verbose: bool = False) -> dict[str, str | None]:
     out = {"kernels": str(build_kernels(verbose=verbose))}
-    rt = build_runtime()
-    out["runtime"] = str(rt) if rt else None
     rb = build_router()
     out["router"] = str(rb) if rb else None
     return out

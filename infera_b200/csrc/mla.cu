@@ -1,0 +1,507 @@
+// Multi-head latent attention (DeepSeek-V3 MLA), absorbed form, on tcgen05.
+//
+// The cache holds one 576-wide latent row per token: the RMS-normalised
+// compressed KV c (512) followed by the rotated shared rope key (64). With
+// the up-projections absorbed into the query and output sides, attention is
+// multi-query attention with one 576-dim key / 512-dim value head:
+//
+//   S[h, t] = q[h] . cache[t]              (q = [W_UK^T q_nope | rope(q_pe)])
+//   O[h]    = softmax_t(S[h, :] * scale) . cache[:, 0:512]
+//
+// One CTA handles one query (128 head rows; fewer heads leave the rest of
+// the tile unused), one 256-dim half of the value dims and one split of the
+// keys:
+//   warp 0      TMA producer: the query's 9 x [128 x 64] blocks once, then
+//               key tiles of 32 tokens (2 pages x 9 blocks of 64 dims) into a
+//               2-stage ring
+//   warp 1      MMA issuer: S = Q K^T (M 128, N 32, K 576) into TMEM (double
+//               buffered); O += P V (M 128, N 256, K 32) with V = the tile's
+//               latent dims of this CTA's half, read MN-major from the same
+//               ring stage
+//   warps 2..5  softmax, thread = head row: running max with lazy O rescale
+//               (only when the max grows by more than 2^8), P to shared
+//               memory (K-major, 64-byte swizzle), final O / l epilogue or
+//               split partials with their log-sum-exp
+// TMEM: S 2 x 32 columns, O 256 columns. The 128 x 512 fp32 output of all
+// heads would fill TMEM on its own, hence the value split over two CTAs (the
+// two recompute S; they read the same key tiles, which L2 serves once).
+// Prefill reuses the kernel with one "query" per prompt token (its own
+// causal key count).
+//
+// Reference parity: the reference serves DeepSeek-V3 MLA through its
+// engines (AITER MLA in vLLM / SGLang); none of that code is in its tree.
+#include "sm100.cuh"
+#include "tma_host.h"
+
+namespace ib200 {
+namespace mla {
+
+constexpr int DL = 512;
+constexpr int DR = 64;
+constexpr int DQK = DL + DR;
+constexpr int NCH = DQK / 64;              // 9 blocks of 64 dims
+constexpr int BT = 32;                     // keys per tile
+constexpr int PAGE = 16;
+constexpr int STAGES = 2;
+constexpr int QCH = 128 * 128;             // one [128 rows x 64 dims] bf16 block
+constexpr int KCH = BT * 128;              // one [32 keys x 64 dims] block
+constexpr int KV_STAGE = NCH * KCH;        // 36 KiB
+constexpr int P_BYTES = 128 * BT * 2;      // 8 KiB
+constexpr int DV = 256;                    // value dims per CTA
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t S_COL0 = 0, S_COL1 = 32, O_COL = 64;
+constexpr int SMEM_BYTES = 1024 + NCH * QCH + STAGES * KV_STAGE + P_BYTES + 256;
+
+struct Params {
+  const int* q_row;        // [nq] block-table row of each query
+  const int* q_kvlen;      // [nq] keys visible to each query
+  const int* block_table;  // [rows, max_pages]
+  int max_pages;
+  int hq;                  // head rows per query (<= 128)
+  int splits;              // key splits per query (each covers ceil(tiles / splits) tiles)
+  float scale_log2;
+  __nv_bfloat16* out;      // [nq, hq, 512]
+  float* o_part;           // [nq, splits, hq, 512]
+  float* lse_part;         // [nq, splits, hq] (log2 units)
+  int* status;
+};
+
+// K-major operand with 64-byte swizzle (layout type 4): 8-row atoms of
+// 64-byte rows, atoms SBO bytes apart.
+__device__ __forceinline__ uint64_t make_sw64_desc(uint32_t smem_addr, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
+  d |= 4ull << 61;
+  return d;
+}
+
+// byte offset of 16-byte chunk c (0..3) of row r in a 64-byte-swizzled tile
+__device__ __forceinline__ uint32_t sw64_offset(int r, int c) {
+  return static_cast<uint32_t>((r >> 3) * 512 + (r & 7) * 64 + ((c ^ ((r & 7) >> 1)) << 4));
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    mla_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+                      const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + NCH * QCH;
+  uint8_t* sP = sKV + STAGES * KV_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;          // [STAGES]
+  uint64_t* kv_empty = kv_full + STAGES; // [STAGES]
+  uint64_t* s_full = kv_empty + STAGES;  // [2]
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 1;
+  uint64_t* drain = o_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qi = blockIdx.x;
+  const int half = blockIdx.y;
+  const int sp = blockIdx.z;
+  const int kvlen = p.q_kvlen[qi];
+  const int n_tiles_all = (kvlen + BT - 1) / BT;
+  const int tps = (n_tiles_all + p.splits - 1) / p.splits;
+  const int tile0 = sp * tps;
+  const int n_tiles = max(0, min(n_tiles_all - tile0, tps));
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmKV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && n_tiles > 0) {
+      const uint64_t pol_q = policy_evict_first();
+      const uint64_t pol_kv = policy_evict_last();  // the other value half reads the same tiles
+      mbar_expect_tx(q_full, NCH * QCH);
+      for (int c = 0; c < NCH; ++c) tma_load_2d(sQ + c * QCH, &tmQ, q_full, c * 64, qi * p.hq, pol_q);
+      const int* bt = p.block_table + static_cast<size_t>(p.q_row[qi]) * p.max_pages;
+      const int n_pages = (kvlen + PAGE - 1) / PAGE;
+      long long issued = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j % STAGES;
+        const uint32_t ph = (j / STAGES) & 1;
+        const int lp0 = (tile0 + j) * 2;
+        const int pg0 = __ldg(bt + lp0);
+        const int pg1 = __ldg(bt + (lp0 + 1 < n_pages ? lp0 + 1 : lp0));
+        if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
+        uint8_t* base = sKV + st * KV_STAGE;
+        mbar_expect_tx(&kv_full[st], KV_STAGE);
+        for (int c = 0; c < NCH; ++c) {
+          tma_load_2d(base + c * KCH, &tmKV, &kv_full[st], c * 64, pg0 * PAGE, pol_kv);
+          tma_load_2d(base + c * KCH + PAGE * 128, &tmKV, &kv_full[st], c * 64, pg1 * PAGE, pol_kv);
+        }
+        ++issued;
+      }
+      // drain: every issued copy must land before the CTA exits
+      mbar_wait(q_full, 0, nullptr, nullptr, 0, kWaitLimitNs / 4);
+      const long long first = issued > STAGES ? issued - STAGES : 0;
+      for (long long i = first; i < issued; ++i)
+        mbar_wait(&kv_full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1), nullptr, nullptr, 0,
+                  kWaitLimitNs / 4);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t idesc_qk = make_idesc_bf16(128, BT);
+      const uint32_t idesc_pv = make_idesc_bf16(128, DV, true);
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t p_addr = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kStatusTimeoutFull);
+      auto issue_pv = [&](int jj) -> bool {
+        if (!mbar_wait(p_full, static_cast<uint32_t>(jj & 1), abort_flag, p.status, kStatusTimeoutTmemEmpty))
+          return false;
+        tc_fence_after();
+        const int st = jj % STAGES;
+        // V = latent dims [256*half, +256) of the tile: blocks 4*half .. 4*half+3
+        const uint32_t v_addr = smem_u32(sKV + st * KV_STAGE + half * 4 * KCH);
+#pragma unroll
+        for (int kk = 0; kk < BT / 16; ++kk) {
+          const uint64_t ad = make_sw64_desc(p_addr + kk * 32, 512);
+          // MN-major V: LBO = distance between 64-dim blocks, SBO = 8 keys
+          const uint64_t bd = make_sw128_desc(v_addr + kk * 2048, KCH, 1024);
+          umma_bf16(tmem + O_COL, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(o_done);
+        umma_commit(&kv_empty[st]);
+        return true;
+      };
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j % STAGES;
+        if (!mbar_wait(&kv_full[st], static_cast<uint32_t>((j / STAGES) & 1), abort_flag, p.status,
+                       kStatusTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sKV + st * KV_STAGE);
+        const uint32_t s_col = (j & 1) ? S_COL1 : S_COL0;
+        for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = make_sw128_desc(q_addr + c * QCH + kk * 32, 16, 1024);
+            const uint64_t bd = make_sw128_desc(k_addr + c * KCH + kk * 32, 16, 1024);
+            umma_bf16(tmem + s_col, ad, bd, idesc_qk, (c > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        umma_commit(&s_full[j & 1]);
+        if (j > 0 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok) issue_pv(n_tiles - 1);
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, p.status, kStatusTimeoutFull);
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;  // head row
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      if (!mbar_wait_warp(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status,
+                          kStatusTimeoutTmemFull)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld32(lane_addr + ((j & 1) ? S_COL1 : S_COL0), v);
+      tmem_ld_wait();
+      const int lim = kvlen - (tile0 + j) * BT;  // keys c < lim are valid
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (i >= lim) v[i] = __float_as_uint(-INFINITY);
+        mx = fmaxf(mx, __uint_as_float(v[i]));
+      }
+      mx *= p.scale_log2;
+      const float m_new = fmaxf(m_run, mx);
+      const bool rescale = (j == 0) || (m_new > m_run + 8.0f);
+      const float m_use = rescale ? m_new : m_run;
+      const float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
+      const bool warp_rescale = __any_sync(0xffffffffu, rescale && j > 0);
+      if (j > 0) {
+        // P of the previous tile must be consumed (and O complete) first
+        if (!mbar_wait_warp(o_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status,
+                            kStatusTimeoutTmemFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (warp_rescale) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < DV; c0 += 16) {
+          uint32_t o[16];
+          tmem_ld16(lane_addr + O_COL + c0, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st16(lane_addr + O_COL + c0, o);
+        }
+        tmem_st_wait();
+      }
+      float sum = 0.f;
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const float e0 = exp2f(fmaf(__uint_as_float(v[i]), p.scale_log2, -m_use));
+        const float e1 = exp2f(fmaf(__uint_as_float(v[i + 1]), p.scale_log2, -m_use));
+        __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
+        sum += __low2float(bb) + __high2float(bb);
+        pk[i / 2] = *reinterpret_cast<uint32_t*>(&bb);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(sP + sw64_offset(r, c)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      l_run = l_run * alpha + sum;
+      m_run = m_use;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    const bool write = r < p.hq;
+    const size_t row = static_cast<size_t>(qi) * p.hq + r;
+    const int dv0 = half * DV;
+    if (n_tiles == 0) {
+      // no keys in this split: an empty partial (or zeros)
+      if (write) {
+        if (p.splits == 1) {
+          for (int c = 0; c < DV; ++c) p.out[row * DL + dv0 + c] = __float2bfloat16(0.f);
+        } else {
+          const size_t prow = (static_cast<size_t>(qi) * p.splits + sp) * p.hq + r;
+          for (int c = 0; c < DV; ++c) p.o_part[prow * DL + dv0 + c] = 0.f;
+          if (half == 0) p.lse_part[prow] = -INFINITY;
+        }
+      }
+    } else if (ok && mbar_wait_warp(o_done, static_cast<uint32_t>((n_tiles - 1) & 1), abort_flag, p.status,
+                                    kStatusTimeoutTmemFull)) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+      const size_t prow = (static_cast<size_t>(qi) * p.splits + sp) * p.hq + r;
+#pragma unroll 1
+      for (int c0 = 0; c0 < DV; c0 += 32) {
+        uint32_t o[32];
+        tmem_ld32(lane_addr + O_COL + c0, o);
+        tmem_ld_wait();
+        if (!write) continue;
+        if (p.splits == 1) {
+          __nv_bfloat16* dst = p.out + row * DL + dv0 + c0;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
+            w.y = pack_bf16(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+            w.z = pack_bf16(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+            w.w = pack_bf16(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + i) = w;
+          }
+        } else {
+          float* dst = p.o_part + prow * DL + dv0 + c0;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(dst + i) =
+                make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                            __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+        }
+      }
+      if (write && p.splits > 1 && half == 0) p.lse_part[prow] = m_run + log2f(l_run);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// out[row] = sum_s 2^(lse_s - m) o_s / sum_s 2^(lse_s - m); one CTA per
+// (query, head) row, 128 threads x 4 dims.
+__global__ void __launch_bounds__(128) mla_combine_kernel(const float* __restrict__ o_part,
+                                                          const float* __restrict__ lse_part, int hq, int splits,
+                                                          __nv_bfloat16* __restrict__ out) {
+  const int row = blockIdx.x;  // qi * hq + h
+  const int qi = row / hq;
+  const int h = row - qi * hq;
+  float m = -INFINITY;
+  for (int s = 0; s < splits; ++s) m = fmaxf(m, lse_part[(static_cast<size_t>(qi) * splits + s) * hq + h]);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float wsum = 0.f;
+  if (m > -INFINITY) {
+    for (int s = 0; s < splits; ++s) {
+      const size_t prow = (static_cast<size_t>(qi) * splits + s) * hq + h;
+      const float w = exp2f(lse_part[prow] - m);
+      if (w == 0.f) continue;
+      const float4 o = *reinterpret_cast<const float4*>(o_part + prow * DL + threadIdx.x * 4);
+      acc[0] += w * o.x;
+      acc[1] += w * o.y;
+      acc[2] += w * o.z;
+      acc[3] += w * o.w;
+      wsum += w;
+    }
+  }
+  const float inv = wsum > 0.f ? 1.0f / wsum : 0.f;
+  uint2 v;
+  v.x = pack_bf16(acc[0] * inv, acc[1] * inv);
+  v.y = pack_bf16(acc[2] * inv, acc[3] * inv);
+  *reinterpret_cast<uint2*>(out + static_cast<size_t>(row) * DL + threadIdx.x * 4) = v;
+}
+
+// One CTA per token: c = rmsnorm(kva[0:512]) * w, k_pe = rope(kva[512:576]),
+// cache[slot] = [c | k_pe] (slot < 0: no write), and every head's rope part
+// of q (columns 512..575 of each 576-wide head row) rotated in place.
+// Rotation pairs (i, i + 32) ("rotate half"); cos_sin [max_pos, 32, 2].
+__global__ void __launch_bounds__(256) mla_rope_kvwrite_kernel(__nv_bfloat16* __restrict__ q, int hq,
+                                                               const __nv_bfloat16* __restrict__ kva, int ldkva,
+                                                               const int* __restrict__ pos,
+                                                               const int* __restrict__ slots,
+                                                               const float2* __restrict__ cos_sin,
+                                                               const __nv_bfloat16* __restrict__ w, float eps,
+                                                               __nv_bfloat16* __restrict__ cache) {
+  __shared__ float red[8];
+  const int t = blockIdx.x;
+  const __nv_bfloat16* kr = kva + static_cast<size_t>(t) * ldkva;
+  const int slot = slots[t];
+  const int ps = pos[t];
+  // RMSNorm of the 512 latent dims: 2 per thread
+  const __nv_bfloat162 c2 = reinterpret_cast<const __nv_bfloat162*>(kr)[threadIdx.x];
+  const float c0 = __low2float(c2), c1 = __high2float(c2);
+  float ss = c0 * c0 + c1 * c1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float inv = rsqrtf(tot / DL + eps);
+  const __nv_bfloat162 w2 = reinterpret_cast<const __nv_bfloat162*>(w)[threadIdx.x];
+  __nv_bfloat16* crow = slot >= 0 ? cache + static_cast<size_t>(slot) * DQK : nullptr;
+  if (crow != nullptr)
+    reinterpret_cast<__nv_bfloat162*>(crow)[threadIdx.x] =
+        __floats2bfloat162_rn(c0 * inv * __low2float(w2), c1 * inv * __high2float(w2));
+  const float2* cs = cos_sin + static_cast<size_t>(ps) * (DR / 2);
+  // shared rope key
+  if (threadIdx.x < DR / 2 && crow != nullptr) {
+    const int i = threadIdx.x;
+    const float a = __bfloat162float(kr[DL + i]), b = __bfloat162float(kr[DL + i + DR / 2]);
+    const float2 c = cs[i];
+    crow[DL + i] = __float2bfloat16(a * c.x - b * c.y);
+    crow[DL + i + DR / 2] = __float2bfloat16(b * c.x + a * c.y);
+  }
+  // every head's rope query
+  for (int k = threadIdx.x; k < hq * (DR / 2); k += blockDim.x) {
+    const int h = k / (DR / 2);
+    const int i = k - h * (DR / 2);
+    __nv_bfloat16* qr = q + (static_cast<size_t>(t) * hq + h) * DQK + DL;
+    const float a = __bfloat162float(qr[i]), b = __bfloat162float(qr[i + DR / 2]);
+    const float2 c = cs[i];
+    qr[i] = __float2bfloat16(a * c.x - b * c.y);
+    qr[i + DR / 2] = __float2bfloat16(b * c.x + a * c.y);
+  }
+}
+
+}  // namespace mla
+}  // namespace ib200
+
+using namespace ib200;
+
+// q: [nq * hq, 576] bf16 (absorbed queries, rope part already rotated);
+// cache: [num_slots, 576] bf16; q_row / q_kvlen: [nq] device int32; out:
+// [nq, hq, 512] bf16. splits > 1 needs o_part [nq, splits, hq, 512] and
+// lse_part [nq, splits, hq] fp32 scratch.
+extern "C" int ib_mla_decode(const void* q, int nq, int hq, const void* cache, long long num_slots,
+                             const int* q_row, const int* q_kvlen, const int* block_table, int max_pages,
+                             int splits, float scale, void* out, float* o_part, float* lse_part,
+                             int* status, cudaStream_t stream) {
+  using namespace ib200::mla;
+  if (nq <= 0) return 0;
+  if (hq < 1 || hq > 128 || splits < 1 || (splits > 1 && (o_part == nullptr || lse_part == nullptr))) return -1;
+  CUtensorMap tq, tkv;
+  if (!cached_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<long long>(nq) * hq, DQK, DQK, 128,
+                      64))
+    return -2;
+  if (!cached_tmap_2d(&tkv, cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, DQK, DQK, PAGE, 64)) return -2;
+  Params p;
+  p.q_row = q_row;
+  p.q_kvlen = q_kvlen;
+  p.block_table = block_table;
+  p.max_pages = max_pages;
+  p.hq = hq;
+  p.splits = splits;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.o_part = o_part;
+  p.lse_part = lse_part;
+  p.status = status;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_set[dev] = true;
+  }
+  dim3 grid(nq, 2, splits);
+  mla_decode_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tq, tkv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (splits > 1) {
+    mla_combine_kernel<<<nq * hq, 128, 0, stream>>>(o_part, lse_part, hq, splits, static_cast<__nv_bfloat16*>(out));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  return 0;
+}
+
+extern "C" int ib_mla_rope_kvwrite(void* q, int T, int hq, const void* kva, int ldkva, const int* pos,
+                                   const int* slots, const void* cos_sin, const void* norm_w, float eps, void* cache,
+                                   cudaStream_t stream) {
+  using namespace ib200::mla;
+  if (T <= 0) return 0;
+  if ((ldkva % 2) != 0) return -1;
+  mla_rope_kvwrite_kernel<<<T, 256, 0, stream>>>(
+      static_cast<__nv_bfloat16*>(q), hq, static_cast<const __nv_bfloat16*>(kva), ldkva, pos, slots,
+      static_cast<const float2*>(cos_sin), static_cast<const __nv_bfloat16*>(norm_w), eps,
+      static_cast<__nv_bfloat16*>(cache));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}

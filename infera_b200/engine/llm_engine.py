@@ -77,7 +77,14 @@ class LLMEngine:
             mcfg.max_model_len = cfg.max_model_len
         self.model_cfg = mcfg
         self.tp = tp
-        self.model = DenseModel(mcfg, self.device, seed=cfg.seed, tp=tp)
+        if getattr(mcfg, "kv_channels", 2) == 1:  # MLA: one latent cache row per token
+            from infera_b200.models.mla import MLAModel
+
+            if cfg.kv_tier or cfg.disagg_mode != "mixed":
+                raise NotImplementedError("KV tiering / PD disaggregation of a latent (MLA) cache")
+            self.model = MLAModel(mcfg, self.device, seed=cfg.seed, tp=tp)
+        else:
+            self.model = DenseModel(mcfg, self.device, seed=cfg.seed, tp=tp)
         num_pages = cfg.num_pages or self._derive_num_pages()
         if tp is not None and tp.world > 1:
             # every rank runs the same scheduler: agree on the page count
@@ -120,7 +127,7 @@ class LLMEngine:
     # ------------------------------------------------------------------ sizing
     def _derive_num_pages(self) -> int:
         mcfg = self.model.cfg  # this rank's shard of the model
-        per_page = 2 * mcfg.num_layers * self.cfg.page_size * mcfg.kv_size * 2
+        per_page = getattr(mcfg, "kv_channels", 2) * mcfg.num_layers * self.cfg.page_size * mcfg.kv_size * 2
         if self.device.type != "cuda":
             return 512
         torch.cuda.synchronize()

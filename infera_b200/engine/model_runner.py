@@ -51,16 +51,18 @@ class ModelRunner:
         # that padding pages always hold finite values
         slots = num_pages * page_size
         shape = (cfg.num_layers, slots, cfg.kv_size)
+        # latent (MLA) caches have one channel: v_cache is a placeholder
+        v_shape = shape if getattr(cfg, "kv_channels", 2) == 2 else (cfg.num_layers, 1, 1)
         if exportable and self.on_gpu:
             # own cudaMalloc allocations: exportable whole with CUDA IPC
             # (the decode side of a PD pair maps them into prefill processes)
             from infera_b200.parallel.symmem import device_tensor
 
             self.k_cache, self._k_buf = device_tensor(shape, torch.bfloat16, self.dev)
-            self.v_cache, self._v_buf = device_tensor(shape, torch.bfloat16, self.dev)
+            self.v_cache, self._v_buf = device_tensor(v_shape, torch.bfloat16, self.dev)
         else:
             self.k_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.dev)
-            self.v_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.dev)
+            self.v_cache = torch.zeros(v_shape, dtype=torch.bfloat16, device=self.dev)
         self.block_table = torch.zeros(max_num_seqs + 1, self.max_pages, dtype=torch.int32, device=self.dev)
         self.dummy_row = max_num_seqs
         self.bufs = model.alloc_buffers(self.max_tokens, max(max_num_seqs, 1))

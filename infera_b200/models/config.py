@@ -43,6 +43,8 @@ class DenseConfig:
     moe_num_shared: int = 0
     moe_softmax: bool = False
 
+    kv_channels: int = 2  # K and V caches
+
     def is_moe_layer(self, i: int) -> bool:
         return self.num_experts > 0 and i >= self.moe_first_layer
 
@@ -103,6 +105,37 @@ class MoEConfig:
     def latent_dim(self) -> int:
         return self.kv_lora_rank + self.qk_rope_dim  # 576 per token per layer
 
+    # the paged cache holds one latent row per token (no separate V)
+    kv_channels: int = 1
+
+    @property
+    def kv_size(self) -> int:
+        return self.latent_dim
+
+    @property
+    def num_kv_heads(self) -> int:
+        return 1
+
+    @property
+    def head_dim(self) -> int:
+        return self.qk_nope_dim + self.qk_rope_dim
+
+    # activation widths for memory sizing
+    @property
+    def q_size(self) -> int:
+        return self.num_heads * self.latent_dim
+
+    @property
+    def qkv_size(self) -> int:
+        return self.q_lora_rank + self.num_heads * self.head_dim + self.latent_dim
+
+    @property
+    def ffn(self) -> int:
+        return max(self.dense_ffn, self.moe_ffn * max(1, self.num_shared_experts))
+
+    def is_moe_layer(self, i: int) -> bool:
+        return self.num_experts > 0 and i >= self.num_dense_layers
+
     def kv_bytes_per_token(self, dtype_bytes: int = 2) -> int:
         return self.num_layers * self.latent_dim * dtype_bytes
 
@@ -141,6 +174,10 @@ PRESETS: dict[str, DenseConfig | MoEConfig] = {
                                     ffn=2048, vocab=4096, max_model_len=4096, eos_token_id=1, num_experts=16,
                                     moe_top_k=4, moe_ffn=512, moe_first_layer=1, moe_n_groups=4,
                                     moe_topk_groups=2, moe_routed_scaling=2.0, moe_num_shared=1),
+    "tiny-mla-gpu": MoEConfig(name="tiny-mla-gpu", num_layers=3, num_dense_layers=1, hidden=1024, dense_ffn=2048,
+                              num_heads=16, q_lora_rank=512, kv_lora_rank=512, qk_rope_dim=64, qk_nope_dim=128,
+                              v_head_dim=128, num_experts=16, moe_ffn=512, top_k=4, n_groups=4, topk_groups=2,
+                              vocab=4096, max_model_len=4096, weight_dtype="fp8"),
     "tiny-moe": MoEConfig(name="tiny-moe", num_layers=3, num_dense_layers=1, hidden=256, dense_ffn=512,
                           num_heads=4, q_lora_rank=128, kv_lora_rank=64, qk_rope_dim=32, qk_nope_dim=32,
                           v_head_dim=32, num_experts=8, moe_ffn=128, top_k=2, n_groups=2, topk_groups=1,

@@ -25,7 +25,7 @@ from infera_b200.ops import kernels as K
 class MoELayer:
     def __init__(self, hidden: int, moe_ffn: int, num_experts: int, top_k: int, n_groups: int = 1,
                  topk_groups: int = 1, routed_scaling: float = 1.0, num_shared: int = 0,
-                 device: str | torch.device = "cuda", seed: int = 0, std: float = 0.02):
+                 device: str | torch.device = "cuda", seed: int = 0, std: float = 0.02, weight_dtype: str = "bf16"):
         self.H, self.F, self.E, self.k = hidden, moe_ffn, num_experts, top_k
         self.n_groups, self.topk_groups, self.scaling = n_groups, topk_groups, routed_scaling
         dev = torch.device(device)
@@ -42,6 +42,15 @@ class MoELayer:
         self.shared = None
         if num_shared:
             self.shared = (rnd(2 * moe_ffn * num_shared, hidden), rnd(hidden, moe_ffn * num_shared))
+        # fp8: experts stacked to [E*2F, H] / [E*H, F] e4m3 with 128x128 block scales
+        self.fp8 = weight_dtype == "fp8"
+        if self.fp8:
+            from infera_b200.ops import fp8
+
+            self.w13 = fp8.quantize_weight(self.w13.reshape(num_experts * 2 * moe_ffn, hidden))
+            self.w2 = fp8.quantize_weight(self.w2.reshape(num_experts * hidden, moe_ffn))
+            if self.shared is not None:
+                self.shared = tuple(fp8.quantize_weight(t) for t in self.shared)
 
     def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         logits = K.linear(x, self.gate)
@@ -53,12 +62,25 @@ class MoELayer:
             ids, wts = self.route(x)
         offsets, row_of_slot, token_of_row = K.moe_permute(ids, self.E)
         xp = K.gather_rows(x, token_of_row)
-        act = K.gemm_grouped(xp, self.w13, offsets, swiglu=True)
-        rows = K.gemm_grouped(act, self.w2, offsets)
+        if self.fp8:
+            from infera_b200.ops import fp8
+
+            act = fp8.gemm_fp8_grouped(xp, self.w13, self.E, offsets, swiglu=True)
+            rows = fp8.gemm_fp8_grouped(act, self.w2, self.E, offsets)
+        else:
+            act = K.gemm_grouped(xp, self.w13, offsets, swiglu=True)
+            rows = K.gemm_grouped(act, self.w2, offsets)
         y = K.moe_combine(rows, row_of_slot, wts)
         if self.shared is not None:
             y = y + K.linear(K.linear(x, self.shared[0], swiglu=True), self.shared[1])
         return y
+
+    def expert(self, e: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Expert e's (w13 [2F, H], w2 [H, F]) as fp32 (dequantised if fp8)."""
+        if self.fp8:
+            return (self.w13.rows(e * 2 * self.F, (e + 1) * 2 * self.F).dequant(),
+                    self.w2.rows(e * self.H, (e + 1) * self.H).dequant())
+        return self.w13[e].float(), self.w2[e].float()
 
     def to(self, device) -> "MoELayer":
         for name in ("gate", "bias", "w13", "w2"):

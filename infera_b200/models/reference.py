@@ -78,15 +78,28 @@ def _moe_ref(m, x: torch.Tensor, f) -> torch.Tensor:
 
     logits = x @ f(m.gate).t()
     ids, wts = K.moe_topk(logits, m.k, m.n_groups, m.topk_groups, f(m.bias), m.scaling)
+
+    def qa(v):  # activations as the fp8 kernels see them
+        if not m.fp8:
+            return v
+        from infera_b200.ops import fp8
+
+        q, sf = fp8.quant_act(v.reshape(-1, v.shape[-1]).to(torch.bfloat16))
+        return fp8.dequant_act(q, sf).reshape(v.shape)
+
+    def wt(t):
+        return t.to("cpu").dequant() if not isinstance(t, torch.Tensor) else f(t)
+
     y = torch.zeros_like(x)
     for t in range(x.shape[0]):
         for j in range(m.k):
-            e = int(ids[t, j])
-            gu = x[t] @ f(m.w13[e]).t()
-            y[t] += float(wts[t, j]) * ((torch.nn.functional.silu(gu[0::2]) * gu[1::2]) @ f(m.w2[e]).t())
+            w13, w2 = (w.cpu() for w in m.expert(int(ids[t, j])))
+            gu = qa(x[t:t + 1]) @ w13.t()
+            a = torch.nn.functional.silu(gu[:, 0::2]) * gu[:, 1::2]
+            y[t] += float(wts[t, j]) * (qa(a) @ w2.t())[0]
     if m.shared is not None:
-        gu = x @ f(m.shared[0]).t()
-        y += (torch.nn.functional.silu(gu[:, 0::2]) * gu[:, 1::2]) @ f(m.shared[1]).t()
+        gu = qa(x) @ wt(m.shared[0]).t()
+        y += qa(torch.nn.functional.silu(gu[:, 0::2]) * gu[:, 1::2]) @ wt(m.shared[1]).t()
     return y
 
 

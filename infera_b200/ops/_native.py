@@ -1,9 +1,8 @@
 """Loader for the in-tree native libraries.
 
-``libib200_kernels.so`` holds every sm_100a CUDA kernel behind a C ABI;
-``libib200_runtime.so`` holds the host-side C++ runtime (hashing, block
-allocator). Both are built in-tree by :mod:`infera_b200.build` and loaded
-with :mod:`ctypes`.
+``libib200_kernels.so`` holds every sm_100a CUDA kernel behind a C ABI,
+built in-tree by :mod:`infera_b200.build` and loaded with :mod:`ctypes`
+(the native router is a separate executable).
 
 On a machine with a GPU a missing kernel library is an error, never a silent
 fallback: :func:`kernels` raises.
@@ -19,7 +18,6 @@ from pathlib import Path
 _LIB_DIR = Path(__file__).resolve().parent.parent / "lib"
 _lock = threading.Lock()
 _kernels: ctypes.CDLL | None = None
-_runtime: ctypes.CDLL | None = None
 
 c_int = ctypes.c_int
 c_ll = ctypes.c_longlong
@@ -30,10 +28,6 @@ c_ip = ctypes.c_void_p  # int* passed as raw address
 
 def kernel_lib_path() -> Path:
     return _LIB_DIR / "libib200_kernels.so"
-
-
-def runtime_lib_path() -> Path:
-    return _LIB_DIR / "libib200_runtime.so"
 
 
 def _declare_kernels(lib: ctypes.CDLL) -> None:
@@ -86,6 +80,9 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
                                 c_int, c_int, c_vp, c_vp, c_int, c_int, c_vp, c_vp],
         "ib_gemm_fp8_plan": [c_int, c_int, c_int, c_int, c_int, c_vp],
         "ib_quant_fp8_act": [c_vp, c_int, c_int, c_int, c_vp, c_int, c_vp, c_int, c_vp],
+        "ib_mla_decode": [c_vp, c_int, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_float, c_vp, c_vp, c_vp,
+                          c_vp, c_vp],
+        "ib_mla_rope_kvwrite": [c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_float, c_vp, c_vp],
     }
     for name, args in sig.items():
         fn = getattr(lib, name, None)
@@ -110,19 +107,6 @@ def kernels() -> ctypes.CDLL:
                 _declare_kernels(lib)
                 _kernels = lib
     return _kernels
-
-
-def runtime() -> ctypes.CDLL | None:
-    """The host C++ runtime library, or None when it was not built."""
-    global _runtime
-    if _runtime is None:
-        with _lock:
-            if _runtime is None:
-                path = runtime_lib_path()
-                if not path.exists():
-                    return None
-                _runtime = ctypes.CDLL(str(path))
-    return _runtime
 
 
 def check(rc: int, what: str) -> None:

@@ -48,6 +48,8 @@ class EPMoE:
                  fused: bool = False, max_tokens: int = 256, gloo_group=None):
         if full.E % world:
             raise ValueError(f"{full.E} experts do not split over {world} ranks")
+        if getattr(full, "fp8", False):
+            raise NotImplementedError("expert parallelism over fp8 experts")
         self.rank, self.world, self.group = rank, world, group
         self.E, self.El, self.k = full.E, full.E // world, full.k
         self.full = full
