@@ -6,7 +6,8 @@ footprint, inputs larger than L2 where the case is memory-bound).
 Cases: gemm_prefill (2048x6144x4096 bf16), gemm_decode (64 tokens x
 28672x4096, SwiGLU epilogue), gemm_lmhead (64x128256x4096), decode_attn
 (32 seqs x 8192 keys, GQA 32/8), fp8_decode (64 x 28672 x 8192 e4m3,
-block scales, SwiGLU), fp8_prefill (4096 x 8192 x 8192 e4m3), prefill_attn (2048 queries over 2048 keys,
+block scales, SwiGLU), fp8_prefill (4096 x 8192 x 8192 e4m3), mla_decode (64
+queries x 128 heads over 4096 latent keys each), prefill_attn (2048 queries over 2048 keys,
 causal), prefill_attn_prefix (1024 queries over 8192 keys). Prints one JSON
 line per case: mean CUDA-event time per launch after 3 warm-up launches, and the
 achieved TFLOP/s or GB/s.
@@ -62,6 +63,21 @@ def run_case(case: str, iters: int) -> dict:
         fl = 2 * M * N * Kd
         by = M * Kd + N * Kd + N * Kd // 16384 + M * (N // 2 if swiglu else N) * 2
         return {"case": case, "ms": ms, "ms_with_act_quant": ms_q, "tflops": fl / ms / 1e9, "gbs": by / ms / 1e6}
+    if case == "mla_decode":
+        from infera_b200.ops import mla as M
+
+        B, L, hq = 64, 4096, 128
+        pages = B * L // 16
+        cache = torch.randn(pages * 16, 576, device=dev, generator=g).to(bf)
+        bt = torch.randperm(pages, device=dev, dtype=torch.int32).view(B, -1)
+        q = (torch.randn(B, hq, 576, device=dev, generator=g) * 0.05).to(bf)
+        rows = torch.arange(B, dtype=torch.int32, device=dev)
+        kvl = torch.full((B,), L, dtype=torch.int32, device=dev)
+        ms = _time(lambda: M.mla_attention(q, cache, bt, rows, kvl, 0.07, max_kvlen=L), iters)
+        fl = 2 * B * hq * L * (576 + 512)            # useful FLOPs (S and PV once)
+        by = B * L * 576 * 2 + B * hq * (576 + 512) * 2
+        return {"case": case, "ms": ms, "tflops": fl / ms / 1e9, "gbs": by / ms / 1e6,
+                "splits": M.mla_splits(B, L, K._num_sms())}
     hq, hkv, D = 32, 8, 128
     if case == "decode_attn":
         B, L = 32, 8192
