@@ -393,46 +393,69 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     }
   } else if (FP8 && warp >= 6) {
     // scale-factor stagers: one warp per TMEM lane quadrant writes the same
-    // values into its own quadrant
+    // values into its own quadrant. The scale bytes of stage i+2 are loaded
+    // while stage i is stored (two register sets used alternately), so a
+    // global-load latency is not paid once per stage.
     const int q = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    uint32_t stage = 0, phase = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      int pt, qt, sp;
-      tile_coords(p, t, pt, qt, sp);
-      const int kb0 = sp * p.kbps;
-      const int kb1 = min(kb0 + p.kbps, p.nkb);
-      const int wrow = tile_prow(p, t, pt) / BM;
-      const int tok0 = tile_qrow(p, t, qt);
-      for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait_warp(&empty[stage], phase ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) {
-          ok = false;
-          break;
+    // fetch cursor over the (tile, k-block) sequence this CTA walks
+    int ft = blockIdx.x, fkb = 0, fkb1 = 0, fwrow = 0, ftok0 = 0;
+    bool fresh = true;
+    auto fetch = [&](uint32_t& wb, uint32_t (&r)[8]) -> bool {
+      while (true) {
+        if (ft >= total) return false;
+        if (fresh) {
+          int pt, qt, sp;
+          tile_coords(p, ft, pt, qt, sp);
+          fkb = sp * p.kbps;
+          fkb1 = min(fkb + p.kbps, p.nkb);
+          fwrow = tile_prow(p, ft, pt) / BM;
+          ftok0 = tile_qrow(p, ft, qt);
+          fresh = false;
         }
-        tc_fence_after();  // the MMAs that read this slot before have completed
-        const uint32_t wb = __ldg(p.sf_w + static_cast<size_t>(wrow) * p.sf_w_ld + kb) * 0x01010101u;
-        uint32_t r[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const int tok = tok0 + c * 32 + lane;
-          const uint32_t b = (c * 32 < p.bn && tok < p.M)
-                                 ? __ldg(p.sf_a + static_cast<size_t>(kb) * p.sf_a_ld + tok)
-                                 : 127u;
-          r[c] = b * 0x01010101u;
-        }
-        const uint32_t slot = tmem_base + lane_base + SF_COL0 + stage * SF_SLOT;
-        tmem_st4(slot, wb, wb, wb, wb);
-        tmem_st8(slot + 8, r);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sf_full[stage]);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (fkb < fkb1) break;
+        ft += gridDim.x;
+        fresh = true;
       }
+      wb = __ldg(p.sf_w + static_cast<size_t>(fwrow) * p.sf_w_ld + fkb);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int tok = ftok0 + c * 32 + lane;
+        r[c] = (c * 32 < p.bn && tok < p.M) ? __ldg(p.sf_a + static_cast<size_t>(fkb) * p.sf_a_ld + tok) : 127u;
+      }
+      ++fkb;
+      return true;
+    };
+    uint32_t stage = 0, phase = 0;
+    auto store = [&](uint32_t wb, const uint32_t (&r)[8]) -> bool {
+      if (!mbar_wait_warp(&empty[stage], phase ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) return false;
+      tc_fence_after();  // the MMAs that read this slot before have completed
+      uint32_t rr[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) rr[c] = r[c] * 0x01010101u;
+      const uint32_t w4 = wb * 0x01010101u;
+      const uint32_t slot = tmem_base + lane_base + SF_COL0 + stage * SF_SLOT;
+      tmem_st4(slot, w4, w4, w4, w4);
+      tmem_st8(slot + 8, rr);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sf_full[stage]);
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+      return true;
+    };
+    uint32_t wa = 0, ra[8], wbb = 0, rb[8];
+    bool has_a = fetch(wa, ra);
+    bool has_b = fetch(wbb, rb);
+    while (has_a) {
+      if (!store(wa, ra)) break;
+      has_a = fetch(wa, ra);
+      if (!has_b) break;
+      if (!store(wbb, rb)) break;
+      has_b = fetch(wbb, rb);
     }
   } else {
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
@@ -591,7 +614,8 @@ inline void choose_splits(Plan& pl, int num_sms, int force_split) {
   int best = 1;
   if (force_split > 0) {
     best = force_split;
-  } else if (tiles < num_sms) {
+  } else if (tiles < num_sms || (p.M <= 256 && tiles % num_sms != 0 && tiles < 4 * num_sms)) {
+    // few tiles, or a decode-sized GEMM whose last wave is partly empty
     double best_cost = 1e30;
     for (int s = 1; s <= 16; ++s) {
       if (p.nkb / s < 4 && s > 1) break;

@@ -65,7 +65,7 @@ class EngineConfig:
 class LLMEngine:
     def __init__(self, cfg: EngineConfig, device: str | torch.device = "cuda:0",
                  event_sink: Callable[[str, dict], None] | None = None, model_cfg: DenseConfig | None = None,
-                 tp=None):
+                 tp=None, ep=None):
         self.cfg = cfg
         self.device = torch.device(device)
         if self.device.type == "cuda":
@@ -82,7 +82,7 @@ class LLMEngine:
 
             if cfg.kv_tier or cfg.disagg_mode != "mixed":
                 raise NotImplementedError("KV tiering / PD disaggregation of a latent (MLA) cache")
-            self.model = MLAModel(mcfg, self.device, seed=cfg.seed, tp=tp)
+            self.model = MLAModel(mcfg, self.device, seed=cfg.seed, tp=tp, ep=ep)
         else:
             self.model = DenseModel(mcfg, self.device, seed=cfg.seed, tp=tp)
         num_pages = cfg.num_pages or self._derive_num_pages()

@@ -74,6 +74,7 @@ class ModelRunner:
         self.h_out = torch.empty(max(max_num_seqs, 1), dtype=torch.int32, pin_memory=pin)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
+        self.forwards = 0
         self.last_logits = None
         if self.on_gpu:
             sc = K.scratch(self.dev)
@@ -139,7 +140,22 @@ class ModelRunner:
         return temps, seeds
 
     # ------------------------------------------------------------------ execution
+    def idle_forward(self) -> None:
+        """One forward over a single padding token (no cache write, reads
+        the dummy table row) whose result is dropped: keeps a rank whose
+        scheduler has nothing to run in step with the collectives inside the
+        model (expert-parallel MoE layers under data-parallel attention)."""
+        dev = self.dev
+        one = torch.ones(1, dtype=torch.int32, device=dev)
+        zero = torch.zeros(1, dtype=torch.int32, device=dev)
+        fb = ForwardBatch(token_ids=zero, positions=zero, slots=-one, logits_idx=zero, num_prefill_tokens=0,
+                          d_block_table=self.block_table, d_seq_lens=one, d_splits=1, num_decode=1)
+        fb.d_bt_rows = torch.full((1,), self.dummy_row, dtype=torch.int32, device=dev)
+        self.model.forward(fb, self.k_cache, self.v_cache, None)
+        self.forwards += 1
+
     def execute(self, sched: SchedulerOutput, bt_updates: tuple[list[int], list[int]]) -> StepResult:
+        self.forwards += 1
         ids, pos, slots, logits_rows, sampled, Tp, pmeta, dmeta = self._pack(sched, bt_updates)
         T = len(ids)
         S = len(logits_rows)

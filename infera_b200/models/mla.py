@@ -107,7 +107,11 @@ class MLAModel:
     """Stateless forward over the paged latent cache owned by the engine
     (``k_caches`` [num_layers, slots, 576]; ``v_caches`` is unused)."""
 
-    def __init__(self, cfg: MoEConfig, device: torch.device | str, seed: int = 0, tp=None):
+    def __init__(self, cfg: MoEConfig, device: torch.device | str, seed: int = 0, tp=None, ep=None):
+        """``ep``: expert parallelism under data-parallel attention - an
+        object with ``rank``, ``world``, ``group`` (the all-to-all group),
+        ``gloo`` and ``fused``; every MoE layer keeps only this rank's
+        E / world experts and exchanges tokens with the other ranks."""
         if tp is not None and tp.world > 1:
             raise NotImplementedError("tensor parallelism of MLA layers (use data-parallel attention + EP)")
         self.full_cfg = cfg
@@ -115,6 +119,14 @@ class MLAModel:
         self.tp = None
         self.device = torch.device(device)
         self.w = MLAWeights(cfg, self.device, seed=seed)
+        self.ep = ep
+        if ep is not None and ep.world > 1:
+            from infera_b200.parallel.ep import EPMoE
+
+            for lw in self.w.layers:
+                if "moe" in lw:
+                    lw["moe"] = EPMoE(lw["moe"], ep.rank, ep.world, group=ep.group, device=self.device,
+                                      fused=ep.fused, max_tokens=ep.max_tokens, gloo_group=ep.gloo)
         self.cos_sin = K.rope_cos_sin(cfg.max_model_len, cfg.qk_rope_dim, cfg.rope_theta, None, device=self.device)
         self.scale = M.default_scale(cfg.qk_nope_dim, cfg.qk_rope_dim)
 

@@ -195,8 +195,8 @@ def gemm_fp8_grouped(xp: torch.Tensor, w: FP8Weight, n_experts: int, offsets: to
         return y.to(torch.bfloat16)
     q, sf = quant_act(xp)
     out = torch.empty(R, n_out, dtype=torch.bfloat16, device=xp.device)
-    bn = bn or max(32, min(192, K.grouped_bn(R, n_experts)))
-    bn = ((bn + 31) // 32) * 32
+    bn = bn or K.grouped_bn(R, n_experts)
+    bn = min(192, max(32, ((bn + 31) // 32) * 32))  # the fp8 kernel's token tiles: multiples of 32, <= 192
     cap = (-(-R // bn) + n_experts) * (N // 128)
     tab = torch.empty(cap * 4 + 1, dtype=torch.int32, device=xp.device)
     num = tab[cap * 4:]

@@ -48,17 +48,22 @@ class EPMoE:
                  fused: bool = False, max_tokens: int = 256, gloo_group=None):
         if full.E % world:
             raise ValueError(f"{full.E} experts do not split over {world} ranks")
-        if getattr(full, "fp8", False):
-            raise NotImplementedError("expert parallelism over fp8 experts")
         self.rank, self.world, self.group = rank, world, group
         self.E, self.El, self.k = full.E, full.E // world, full.k
-        self.full = full
+        # routing parameters only: the other ranks' experts are not kept
+        self.n_groups, self.topk_groups, self.scaling = full.n_groups, full.topk_groups, full.scaling
         dev = torch.device(device)
         lo, hi = rank * self.El, (rank + 1) * self.El
         self.gate = full.gate.to(dev)
         self.bias = full.bias.to(dev)
-        self.w13 = full.w13[lo:hi].to(dev).contiguous()
-        self.w2 = full.w2[lo:hi].to(dev).contiguous()
+        self.fp8 = getattr(full, "fp8", False)
+        if self.fp8:  # stacked e4m3 experts: rows of experts lo..hi-1
+            self.F = full.F
+            self.w13 = full.w13.rows(lo * 2 * full.F, hi * 2 * full.F).to(dev)
+            self.w2 = full.w2.rows(lo * full.H, hi * full.H).to(dev)
+        else:
+            self.w13 = full.w13[lo:hi].to(dev).contiguous()
+            self.w2 = full.w2[lo:hi].to(dev).contiguous()
         self.shared = None if full.shared is None else tuple(t.to(dev) for t in full.shared)
         self.stats = {"sent_rows": 0, "recv_rows": 0}
         self.device = dev
@@ -138,9 +143,7 @@ class EPMoE:
                                          recv_peers, flagA, ctypes.c_void_p(ctr), stream), "ib_ep_dispatch")
         _native.check(lib.ib_ep_wait(ctypes.c_void_p(self.base), target, sc.status.data_ptr(), stream), "ib_ep_wait")
         recv = self._tensor_at(self._recv_view(self.base), self.max_rows)
-        bn = K.grouped_bn(R, El)
-        act = K.gemm_grouped(recv, self.w13, loc_off, swiglu=True, bn=bn)
-        out_r = K.gemm_grouped(act, self.w2, loc_off, bn=bn)
+        out_r = self._experts(recv, loc_off, K.grouped_bn(R, El))
         ret_peers = (ctypes.c_void_p * 8)(*[self._ret_view(b) for b in self.peers])
         flagB = (ctypes.c_void_p * 8)(*[b + 4 for b in self.peers])
         _native.check(lib.ib_ep_return(out_r.data_ptr(), self.max_rows, H, self.counts_all.data_ptr(), W, E,
@@ -156,6 +159,16 @@ class EPMoE:
             y = y + K.linear(K.linear(x, self.shared[0], swiglu=True), self.shared[1])
         return y
 
+    def _experts(self, xr: torch.Tensor, loc_off: torch.Tensor, bn: int | None = None) -> torch.Tensor:
+        """This rank's experts over rows grouped by local expert."""
+        if self.fp8:
+            from infera_b200.ops import fp8
+
+            act = fp8.gemm_fp8_grouped(xr, self.w13, self.El, loc_off, swiglu=True, bn=bn)
+            return fp8.gemm_fp8_grouped(act, self.w2, self.El, loc_off, bn=bn)
+        act = K.gemm_grouped(xr, self.w13, loc_off, swiglu=True, bn=bn)
+        return K.gemm_grouped(act, self.w2, loc_off, bn=bn)
+
     def close(self) -> None:
         if getattr(self, "base", None):
             lib = _native.kernels()
@@ -170,9 +183,8 @@ class EPMoE:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
     def route(self, x: torch.Tensor):
-        f = self.full
         logits = K.linear(x, self.gate)
-        return K.moe_topk(logits, f.k, f.n_groups, f.topk_groups, self.bias, f.scaling)
+        return K.moe_topk(logits, self.k, self.n_groups, self.topk_groups, self.bias, self.scaling)
 
     def forward(self, x: torch.Tensor, ids: torch.Tensor | None = None, wts: torch.Tensor | None = None
                 ) -> torch.Tensor:
@@ -215,8 +227,7 @@ class EPMoE:
         loc_off[1:] = torch.cumsum(exp_order.sum(1), 0).to(torch.int32)
         loc_off = loc_off.to(x.device)
         if xr.shape[0]:
-            act = K.gemm_grouped(xr, self.w13, loc_off, swiglu=True)
-            out_r = K.gemm_grouped(act, self.w2, loc_off)
+            out_r = self._experts(xr, loc_off)
             back = out_r[perm_d]
         else:
             back = torch.empty(0, H, dtype=x.dtype, device=x.device)

@@ -45,3 +45,17 @@ def test_ep_nccl_two_ranks():
 def test_ep_fused_two_ranks():
     res = _run(2, 29773, "--fused")
     assert all(rk["fused"] for rk in res["ranks"])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("fused", [False, True])
+def test_dp_attention_ep_two_gpus(fused):
+    env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "10", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(29775 + int(fused)), "-m",
+           "infera_b200.bench.dp_check", "--model", "tiny-mla-gpu", "--prompts", "5"] + (["--fused"] if fused else [])
+    r = subprocess.run(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, timeout=330)
+    out = r.stdout.decode()
+    assert r.returncode == 0, out[-3000:]
+    res = json.loads([x for x in out.splitlines() if x.startswith("{")][-1])
+    assert res["agreement"] >= 0.9, res
