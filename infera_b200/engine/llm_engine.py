@@ -60,6 +60,8 @@ class EngineConfig:
     # instance serves its KV rendezvous on kv_push_endpoint
     disagg_mode: str = "mixed"
     kv_push_endpoint: str | None = None
+    # PD prefill: push each layer's KV pages inside the prompt's last forward
+    pd_layerwise: bool = True
 
 
 class LLMEngine:
@@ -163,6 +165,12 @@ class LLMEngine:
             req.remote_room = int(ktp["room"])
         if ktp.get("do_remote_decode") and ktp.get("decode_kv_endpoint") and "room" in ktp:
             req.remote_decode = (int(ktp["room"]), str(ktp["decode_kv_endpoint"]))
+            if self.cfg.pd_layerwise:
+                from infera_b200.engine.pd import PDPushAgent
+
+                if self.pd_agent is None:
+                    self.pd_agent = PDPushAgent(self)
+                self.pd_agent.prefetch(request_id, *req.remote_decode)
         self.requests[request_id] = req
         self.scheduler.add(req)
         if self.cmd_log is not None:
@@ -236,7 +244,22 @@ class LLMEngine:
                 time.sleep(0.0005)  # only waiting on a KV push
             return outputs
         upd = self._block_table_updates(sched.prefills + sched.decodes)
-        res = self.runner.execute(sched, upd)
+        layer_push = None
+        if self.pd_agent is not None and self.pd_agent.early:
+            items = []
+            for c in sched.prefills:
+                r = c.req
+                if r.remote_decode is not None and c.start + c.num_tokens >= len(r.prompt_token_ids):
+                    it = self.pd_agent.layer_item(r)
+                    if it is not None:
+                        items.append(it)
+            if items:
+                from infera_b200.engine.pd import LayerPush
+
+                layer_push = LayerPush(self, items)
+        res = self.runner.execute(sched, upd, layer_hook=layer_push)
+        if layer_push is not None:
+            layer_push.finish()
         now = self.clock()
         self.num_steps += 1
         for c in sched.prefills:
@@ -275,7 +298,12 @@ class LLMEngine:
             if self.pd_agent is None:
                 self.pd_agent = PDPushAgent(self)
             room, ep = r.remote_decode
-            self.pd_agent.submit(PushJob(r.request_id, room, ep, held))
+            job = self.pd_agent.take_early(r.request_id)
+            if job is None:
+                job = PushJob(r.request_id, room, ep, held)
+            else:
+                job.blocks = held  # pushed layer by layer already, or still waiting for its plan
+            self.pd_agent.submit(job)
         else:
             self.scheduler.finish(r, st)
         r.finish_time = self.clock()

@@ -154,13 +154,17 @@ class ModelRunner:
         self.model.forward(fb, self.k_cache, self.v_cache, None)
         self.forwards += 1
 
-    def execute(self, sched: SchedulerOutput, bt_updates: tuple[list[int], list[int]]) -> StepResult:
+    def execute(self, sched: SchedulerOutput, bt_updates: tuple[list[int], list[int]],
+                layer_hook=None) -> StepResult:
+        """``layer_hook(layer)``: called by the model right after each
+        layer's KV write (forces the eager path)."""
         self.forwards += 1
+        self._layer_hook = layer_hook
         ids, pos, slots, logits_rows, sampled, Tp, pmeta, dmeta = self._pack(sched, bt_updates)
         T = len(ids)
         S = len(logits_rows)
         temps, seeds = self._sampling_arrays(sampled)
-        if Tp == 0 and self.use_graphs and T > 0 and T <= self.graph_sizes[-1]:
+        if Tp == 0 and self.use_graphs and T > 0 and T <= self.graph_sizes[-1] and layer_hook is None:
             toks = self._run_graph(ids, pos, slots, dmeta, temps, seeds, bt_updates)
         else:
             toks = self._run_eager(ids, pos, slots, logits_rows, Tp, pmeta, dmeta, temps, seeds, bt_updates)
@@ -217,6 +221,7 @@ class ModelRunner:
             K.scatter_i32(self.block_table, v("ui"), v("uv"))
         fb = ForwardBatch(token_ids=v("ids"), positions=v("pos"), slots=v("slots"), logits_idx=v("lidx"),
                           num_prefill_tokens=Tp)
+        fb.layer_hook = getattr(self, "_layer_hook", None)
         if Tp > 0:
             fb.p_q_start, fb.p_q_len, fb.p_ctx_len = v("qs"), v("ql"), v("cl")
             fb.p_block_table = self.block_table

@@ -27,6 +27,14 @@ stream (peer stores over NVLink); when the copy's event completes it sends
 ``done`` and releases the pages. A room that never becomes ready within
 ``timeout_s`` is dropped (the decode side times out too and recomputes).
 
+Layer by layer: the agent starts resolving a room's page list when the
+request is admitted (``prefetch``). If the list is known when the step that
+completes the prompt is scheduled, that step's forward pushes each layer's
+pages right after the layer's KV write, on a side stream that waits only
+for that layer (:class:`LayerPush`): the transfer overlaps the remaining
+layers' compute instead of following the whole prefill. Otherwise the push
+runs after the prompt as above.
+
 Protocol role of ``infera/router/disagg_protocols`` + the engines' KV
 connectors (Mooncake / MoRI / NIXL in the reference); the transport here is
 this framework's own NVLink page push.
@@ -196,6 +204,63 @@ class PushJob:
     plan: dict | None = None    # page list from the decode side
     event: object = None        # CUDA event of the launched copy
     launched_at: float = 0.0
+    layerwise: bool = False     # pushed layer by layer inside the prompt's last forward
+
+
+class LayerPush:
+    """Per-layer page pushes of one forward (see the module docstring).
+    ``items``: (job, source pages, destination pages, peer) per request."""
+
+    def __init__(self, engine, items: list):
+        self.eng = engine
+        self.items = items
+        self.on_gpu = engine.runner.k_cache.is_cuda
+        if self.on_gpu:
+            agent = engine.pd_agent
+            if agent.side is None:
+                agent.side = torch.cuda.Stream(engine.device)
+            self.side = agent.side
+            self.start = torch.cuda.Event(enable_timing=True)
+            self.start.record()
+
+    def __call__(self, layer: int) -> None:
+        from infera_b200.ops import kernels as K
+
+        r = self.eng.runner
+        if not self.on_gpu:
+            for _, sp, dp, peer in self.items:
+                K.kv_push_pages(r.k_cache, r.v_cache, peer.k, peer.v, sp, dp, layers=(layer, layer + 1),
+                                dst_slots=peer.slots)
+            return
+        ev = torch.cuda.Event()
+        ev.record()  # this layer's KV pages are written
+        self.side.wait_event(ev)
+        with torch.cuda.stream(self.side):
+            for _, sp, dp, peer in self.items:
+                K.kv_push_pages(r.k_cache, r.v_cache, peer.k, peer.v, sp, dp, layers=(layer, layer + 1),
+                                dst_slots=peer.slots)
+
+    def finish(self) -> None:
+        """After the forward: every job's completion event (the side stream's
+        last push); the main stream also waits for it before the pages can be
+        reused."""
+        end = True
+        if self.on_gpu:
+            end = torch.cuda.Event(enable_timing=True)
+            end.record(self.side)
+            torch.cuda.current_stream().wait_event(end)
+        L, _, H = self.eng.runner.k_cache.shape
+        ps = self.eng.bm.page_size
+        for job, sp, dp, _ in self.items:
+            job.event = end
+            job.start_event = self.start if self.on_gpu else None
+            job.launched_at = time.monotonic()
+            job._tensors = (sp, dp)
+            job.layerwise = True
+            st = self.eng.pd_agent.stats
+            st["pages"] += int(dp.shape[0])
+            st["bytes"] += 2 * int(dp.shape[0]) * ps * L * H * self.eng.runner.k_cache.element_size()
+            st["layerwise"] += 1
 
 
 class _Peer:
@@ -272,14 +337,48 @@ class PDPushAgent:
         self._wake = threading.Event()
         self._stop = False
         self.stats = {"pushes": 0, "pages": 0, "bytes": 0, "timeouts": 0, "failures": 0, "push_s": 0.0,
-                      "push_device_s": 0.0}
+                      "push_device_s": 0.0, "layerwise": 0}
+        self.early: dict[str, PushJob] = {}   # admitted, plan being resolved, prompt not done yet
+        self.side = None                       # stream of the layer-by-layer pushes
         self._th = threading.Thread(target=self._run, name="pd-push-agent", daemon=True)
         self._th.start()
 
     def submit(self, job: PushJob) -> None:
         with self.lock:
+            self.early.pop(job.rid, None)
             self.jobs.append(job)
         self._wake.set()
+
+    def prefetch(self, rid: str, room: int, endpoint: str) -> None:
+        """Start resolving the room's page list at admission."""
+        with self.lock:
+            self.early[rid] = PushJob(rid, room, endpoint, None)
+        self._wake.set()
+
+    def take_early(self, rid: str) -> PushJob | None:
+        with self.lock:
+            return self.early.pop(rid, None)
+
+    def layer_item(self, req):
+        """(job, source pages, destination pages, peer) for a request whose
+        prompt completes in the next forward, if its page list is known."""
+        with self.lock:
+            j = self.early.get(req.request_id)
+        if j is None or j.plan is None or req.blocks is None:
+            return None
+        peer = self.peers.get(j.endpoint)
+        if peer is None or peer.k is None:
+            return None
+        ps = self.engine.bm.page_size
+        skip = j.plan["skip_tokens"] // ps
+        n_pages = (j.plan["n_tokens"] + ps - 1) // ps - skip
+        dst = j.plan["pages"][:n_pages]
+        src = req.blocks.pages[skip:skip + len(dst)]
+        if len(src) != len(dst):
+            return None
+        dev = self.engine.runner.k_cache.device
+        return (j, torch.tensor(src, dtype=torch.int32, device=dev), torch.tensor(dst, dtype=torch.int32, device=dev),
+                peer)
 
     def pending(self) -> int:
         return len(self.jobs)
@@ -300,6 +399,7 @@ class PDPushAgent:
             self._wake.clear()
             with self.lock:
                 todo = [j for j in self.jobs if j.plan is None and not getattr(j, "failed", False)]
+                todo += [j for j in self.early.values() if j.plan is None and not getattr(j, "failed", False)]
                 notices, self._notices = self._notices, []
             for ep, room, ok in notices:
                 try:
@@ -318,8 +418,9 @@ class PDPushAgent:
                 except Exception as e:
                     logger.warning("kv push for room %s failed: %s", j.room, e)
                     j.failed = True
-                    with self.lock:
-                        self._notices.append((j.endpoint, j.room, False))
+                    if j.blocks is not None or j in self.jobs:
+                        with self.lock:
+                            self._notices.append((j.endpoint, j.room, False))
 
     # ------------------------------------------------------------------ engine thread
     def progress(self) -> None:
@@ -361,8 +462,9 @@ class PDPushAgent:
             if j.event is not None and (j.event is True or j.event.query()):
                 self.stats["pushes"] += 1
                 self.stats["push_s"] += time.monotonic() - j.launched_at
-                if j.event is not True:
-                    # the copy kernel's own device time (CUDA events around it)
+                if j.event is not True and getattr(j, "start_event", None) is not None:
+                    # the copy kernels' own device time (CUDA events around them;
+                    # layer by layer: from the forward's start to the last push)
                     self.stats["push_device_s"] += j.start_event.elapsed_time(j.event) / 1000.0
                 with self.lock:
                     self._notices.append((j.endpoint, j.room, True))

@@ -62,6 +62,7 @@ class ForwardBatch:
     d_bt_rows: torch.Tensor | None = None
     d_splits: int = 1
     num_decode: int = 0
+    layer_hook: object = None  # called with the layer index after its KV write
 
 
 class DenseWeights:
@@ -200,6 +201,8 @@ class DenseModel:
             kc, vc = k_caches[li], v_caches[li]
             K.rope_kvwrite(qkv, fb.positions, fb.slots, self.cos_sin, cfg.num_heads, cfg.num_kv_heads,
                            cfg.head_dim, kc, vc)
+            if fb.layer_hook is not None:
+                fb.layer_hook(li)
             if Tp > 0:
                 K.attn_prefill(qkv[:Tp], kc, vc, fb.p_block_table, fb.p_q_start, fb.p_q_len, fb.p_ctx_len,
                                fb.p_tiles, cfg.num_heads, cfg.num_kv_heads, self.scale, out=attn[:Tp],

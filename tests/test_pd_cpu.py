@@ -66,3 +66,32 @@ def test_pd_push_timeout_falls_back_to_local_prefill():
         for o in dec.step():
             out.extend(o.new_token_ids)
     assert out == ref and dec.pd_rendezvous.stats["timeouts"] == 1
+
+
+def test_pd_layerwise_push_inside_the_last_prefill_forward():
+    import time
+
+    g = torch.Generator().manual_seed(8)
+    prompt = torch.randint(0, 1024, (70,), generator=g).tolist()
+    ref = _eng().generate([prompt], SamplingParams(max_tokens=5, ignore_eos=True))[0]
+    dec = _eng(disagg_mode="decode", kv_push_endpoint="local://pd-test-layerwise")
+    pre = _eng(disagg_mode="prefill", max_batched_tokens=24)  # the prompt takes several chunks
+    dec.add_request("d", prompt, SamplingParams(max_tokens=5, ignore_eos=True,
+                                                kv_transfer={"do_remote_prefill": True, "room": 31}))
+    dec.step()  # parks the request and publishes its pages
+    pre.add_request("p", prompt, SamplingParams(max_tokens=1, ignore_eos=True,
+                                                kv_transfer={"do_remote_decode": True, "room": 31,
+                                                             "decode_kv_endpoint": dec.pd_rendezvous.endpoint}))
+    out = []
+    for _ in range(500):
+        if pre.has_unfinished():
+            pre.step()
+            time.sleep(0.01)  # lets the agent thread resolve the page list between chunks
+        if dec.has_unfinished():
+            for o in dec.step():
+                out.extend(o.new_token_ids)
+        if not dec.has_unfinished() and not pre.has_unfinished():
+            break
+    assert out == ref
+    assert pre.pd_agent.stats["layerwise"] == 1 and pre.pd_agent.stats["pushes"] == 1
+    assert dec.counters["prompt_tokens"] == 1
