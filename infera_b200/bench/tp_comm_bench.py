@@ -36,6 +36,9 @@ def main(argv=None) -> None:
     ap.add_argument("--k-total", type=int, default=8192)
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--check-only", action="store_true")
+    ap.add_argument("--one-shot-rows", type=int, default=0,
+                    help="largest row count for the one-shot path; larger rows take the two-shot "
+                         "(reduce-scatter + all-gather) path (0: one-shot for every row count)")
     a = ap.parse_args(argv)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -50,7 +53,12 @@ def main(argv=None) -> None:
     H, KT = a.hidden, a.k_total
     Ks = KT // world
     rows = [int(r) for r in a.rows.split(",")]
-    comm = TPComm(rank, world, dev, H, max_rows=max(rows), nccl_group=nccl, gloo_group=gloo)
+    if a.one_shot_rows:
+        os.environ["INFERA_TP_TWO_SHOT"] = "1"
+        comm = TPComm(rank, world, dev, H, max_rows=a.one_shot_rows, nccl_group=nccl, gloo_group=gloo,
+                      max_rows_rs=max(rows))
+    else:
+        comm = TPComm(rank, world, dev, H, max_rows=max(rows), nccl_group=nccl, gloo_group=gloo)
     g = torch.Generator(device=dev).manual_seed(1234)  # same full tensors on every rank
     worst = 0.0
     results = []
@@ -69,7 +77,12 @@ def main(argv=None) -> None:
             comm.gemm_allreduce_add_rmsnorm(xs, ws, h, nw, 1e-5, out, parity)
         torch.cuda.synchronize()
         err = float((out.float() - ref_x).norm() / ref_x.norm())
-        herr = float((h.float() - ref_h.float()).norm() / ref_h.float().norm())
+        two = comm.uses_two_shot(M)
+        if two:  # the residual is kept by each row block's owner only
+            own = (torch.arange(M, device=dev) // 128) % world == rank
+            herr = float((h[own].float() - ref_h[own].float()).norm() / ref_h[own].float().norm()) if own.any() else 0.0
+        else:
+            herr = float((h.float() - ref_h.float()).norm() / ref_h.float().norm())
         # NCCL baseline on the same problem
         base = TPComm(rank, world, dev, H, max_rows=max(rows), nccl_group=nccl, gloo_group=gloo, fused=False)
         hb = h0.clone()
@@ -79,8 +92,8 @@ def main(argv=None) -> None:
         errb = float((outb.float() - ref_x).norm() / ref_x.norm())
         status = K.scratch(dev).read_status()
         worst = max(worst, err, errb)
-        res = {"rows": M, "hidden": H, "k_per_rank": Ks, "world": world, "rel_err_fused": err,
-               "rel_err_residual": herr, "rel_err_nccl": errb, "status": status}
+        res = {"rows": M, "hidden": H, "k_per_rank": Ks, "world": world, "path": "two-shot" if two else "one-shot",
+               "rel_err_fused": err, "rel_err_residual": herr, "rel_err_nccl": errb, "status": status}
         if not a.check_only:
             # rotate weight copies totalling > 256 MB so every launch reads HBM, not L2
             nrep = max(1, -(-(256 << 20) // (H * Ks * 2)))
@@ -90,6 +103,21 @@ def main(argv=None) -> None:
                 for i in range(4):
                     c.gemm_allreduce_add_rmsnorm(xs, ws, hh, nw, 1e-5, out, i & 1)
                 torch.cuda.synchronize()
+                if name == "fused" and two:
+                    # host-counted rounds: timed eagerly (large row counts, launch cost negligible)
+                    if world > 1:
+                        dist.barrier(group=gloo)
+                    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+                    s.record()
+                    for i in range(a.iters):
+                        c.gemm_allreduce_add_rmsnorm(xs, wl[i % nrep], hh, nw, 1e-5, out, i & 1)
+                    e.record()
+                    torch.cuda.synchronize()
+                    t = torch.tensor([s.elapsed_time(e) * 1000 / a.iters], device=dev)
+                    if world > 1:
+                        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=nccl)
+                    res[f"us_{name}"] = round(float(t.item()), 2)
+                    continue
                 # capture the loop in a CUDA graph: device time, not the
                 # host's launch rate
                 gr = torch.cuda.CUDAGraph()
@@ -118,7 +146,7 @@ def main(argv=None) -> None:
                 res[f"us_{name}"] = round(float(t.item()), 2)
             flops = 2.0 * M * H * Ks
             w_bytes = H * Ks * 2
-            push_bytes = (world - 1) * M * H * 2
+            push_bytes = (2 * (world - 1) / world if two else (world - 1)) * M * H * 2
             res["roofline_us"] = round(max(flops / 1672.1e12, w_bytes / 6534.5e9, push_bytes / 770e9) * 1e6, 2)
             res["roofline_note"] = "max(FLOPs / 1672.1 TF, weight bytes / 6534.5 GB/s, pushed bytes / 770 GB/s)"
             res["frac_fused"] = round(res["roofline_us"] / res["us_fused"], 3)

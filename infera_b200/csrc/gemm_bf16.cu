@@ -75,6 +75,7 @@ struct Params {
   void* peer_out[kMaxPeers];
   unsigned int* peer_flag[kMaxPeers];
   unsigned int* done_ctr;   // local, zero between launches
+  int push_owner;           // 1: a tile of token rows goes only to rank (row block % world) (reduce-scatter)
   // grouped mode (MoE experts, swap-AB only): tile t = gtab[t] = {expert,
   // feature tile, first token row, end token row of the expert}; *gnum tiles
   int grouped;
@@ -121,6 +122,7 @@ __device__ __forceinline__ void store_chunk(const Params& p, int pt, int qt, int
       if (m >= p.M) return;
       const int nout = p.push ? p.world : 1;
       for (int d = 0; d < nout; ++d) {
+        if (p.push && p.push_owner && d != pt % p.world) continue;
         void* base = p.push ? p.peer_out[d] : p.out;
         __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(base) + static_cast<size_t>(m) * p.ldc + n0;
         if (n0 + NC <= p.N && (p.ldc & 7) == 0) {
@@ -187,7 +189,8 @@ __device__ __forceinline__ void store_chunk(const Params& p, int pt, int qt, int
         __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.push ? p.peer_out[d] : p.out) + n;
 #pragma unroll
         for (int j = 0; j < NC; ++j)
-          if (m0 + j < p.M) C[static_cast<size_t>(m0 + j) * p.ldc] = __float2bfloat16(__uint_as_float(r[j]));
+          if (m0 + j < p.M && !(p.push && p.push_owner && d != ((m0 + j) >> 7) % p.world))
+            C[static_cast<size_t>(m0 + j) * p.ldc] = __float2bfloat16(__uint_as_float(r[j]));
       }
     } else if (p.epi == EPI_SWIGLU) {
       // lanes 2j / 2j+1 hold gate_j / up_j for the same tokens
@@ -520,8 +523,11 @@ struct PushDst {
 // every rank's receive slot (zeroing the workspace), then the last CTA
 // signals every rank once.
 __global__ void splitk_finalize_push_kernel(float* __restrict__ ws, int M, int N, int ldc, int world,
-                                            const PushDst dst, unsigned int* done_ctr) {
+                                            const PushDst dst, unsigned int* done_ctr, int owner) {
   const int m = blockIdx.y;
+  // owner mode (reduce-scatter): row m goes only to rank (m / 128) % world
+  const int d0 = owner ? (m / BM) % world : 0;
+  const int d1 = owner ? d0 + 1 : world;
   if (m < M) {
     float* row = ws + static_cast<size_t>(m) * N;
     for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < N; n += gridDim.x * blockDim.x * 4) {
@@ -531,13 +537,13 @@ __global__ void splitk_finalize_push_kernel(float* __restrict__ ws, int M, int N
         uint2 o;
         o.x = pack_bf16(v.x, v.y);
         o.y = pack_bf16(v.z, v.w);
-        for (int d = 0; d < world; ++d)
+        for (int d = d0; d < d1; ++d)
           *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(dst.out[d]) + static_cast<size_t>(m) * ldc + n) = o;
       } else {
         for (int j = n; j < N; ++j) {
           const __nv_bfloat16 b = __float2bfloat16(row[j]);
           row[j] = 0.f;
-          for (int d = 0; d < world; ++d) static_cast<__nv_bfloat16*>(dst.out[d])[static_cast<size_t>(m) * ldc + j] = b;
+          for (int d = d0; d < d1; ++d) static_cast<__nv_bfloat16*>(dst.out[d])[static_cast<size_t>(m) * ldc + j] = b;
         }
       }
     }
@@ -758,7 +764,7 @@ inline int run_dense(const Operands& o, const void* A, const void* W, void* out,
 
 inline int run_push(const Operands& o, const void* A, const void* W, int M, int N, int K, int lda, int ldw, int ldc,
                     int world, void* const* peer_out, unsigned int* const* peer_flag, unsigned int* done_ctr,
-                    float* ws, int* status, cudaStream_t stream) {
+                    float* ws, int* status, cudaStream_t stream, int owner = 0) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if (!operands_ok(o, K, lda, ldw)) return -1;
   if (world < 1 || world > kMaxPeers) return -1;
@@ -781,6 +787,7 @@ inline int run_push(const Operands& o, const void* A, const void* W, int M, int 
   }
   p.done_ctr = done_ctr;
   p.grouped = 0;
+  p.push_owner = owner;  // reduce-scatter: token row m goes to rank (m / 128) % world
   set_scales(p, o);
   CUtensorMap tmP, tmQ;
   if (!encode_pq(o, p, A, W, N, lda, ldw, &tmP, &tmQ)) return -2;
@@ -793,7 +800,7 @@ inline int run_push(const Operands& o, const void* A, const void* W, int M, int 
       dst.flag[d] = p.peer_flag[d];
     }
     dim3 g((N + 1023) / 1024, M);
-    splitk_finalize_push_kernel<<<g, 256, 0, stream>>>(ws, M, N, ldc, world, dst, done_ctr);
+    splitk_finalize_push_kernel<<<g, 256, 0, stream>>>(ws, M, N, ldc, world, dst, done_ctr, owner);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return static_cast<int>(e);
   }
@@ -869,6 +876,25 @@ extern "C" int ib_gemm_bf16_push(const void* A, const void* W, int M, int N, int
                                  unsigned int* done_ctr, float* ws, int* status, cudaStream_t stream) {
   const gemm::Operands o{false, nullptr, 0, nullptr};
   return gemm::run_push(o, A, W, M, N, K, lda, ldw, ldc, world, peer_out, peer_flag, done_ctr, ws, status, stream);
+}
+
+// Reduce-scatter variant (two-shot all-reduce, first half): each 128-row
+// block of the output goes only to rank (block % world).
+extern "C" int ib_gemm_bf16_push_rs(const void* A, const void* W, int M, int N, int K, int lda, int ldw, int ldc,
+                                    int world, void* const* peer_out, unsigned int* const* peer_flag,
+                                    unsigned int* done_ctr, float* ws, int* status, cudaStream_t stream) {
+  const gemm::Operands o{false, nullptr, 0, nullptr};
+  return gemm::run_push(o, A, W, M, N, K, lda, ldw, ldc, world, peer_out, peer_flag, done_ctr, ws, status, stream,
+                        1);
+}
+
+extern "C" int ib_gemm_fp8_push_rs(const void* A, const uint8_t* sf_a, int sf_a_ld, const void* W,
+                                   const uint8_t* sf_w, int M, int N, int K, int lda, int ldw, int ldc, int world,
+                                   void* const* peer_out, unsigned int* const* peer_flag, unsigned int* done_ctr,
+                                   float* ws, int* status, cudaStream_t stream) {
+  const gemm::Operands o{true, sf_a, sf_a_ld, sf_w};
+  return gemm::run_push(o, A, W, M, N, K, lda, ldw, ldc, world, peer_out, peer_flag, done_ctr, ws, status, stream,
+                        1);
 }
 
 extern "C" int ib_gemm_fp8_push(const void* A, const uint8_t* sf_a, int sf_a_ld, const void* W, const uint8_t* sf_w,

@@ -53,6 +53,8 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+constexpr int kMaxRanks = 8;
+
 struct ArParams {
   const __nv_bfloat16* recv;  // this parity's receive region: [world][rows][ld]
   long long src_stride;       // elements between source slots
@@ -66,6 +68,13 @@ struct ArParams {
   float eps;
   __nv_bfloat16* x;           // normalized output [M, H]
   int* status;
+  // two-shot (reduce-scatter) mode: this rank handles only its row blocks
+  // ((row / 128) % world == rank), stores each normalised row into every
+  // rank's x buffer and, once all its rows are out, bumps every rank's x
+  // arrival counter
+  int owner, rank;
+  __nv_bfloat16* x_peer[kMaxRanks];
+  unsigned int* x_flag[kMaxRanks];
 };
 
 template <int VPT>
@@ -92,7 +101,8 @@ __global__ void __launch_bounds__(256) ar_add_rmsnorm_kernel(const ArParams p) {
   }
   __syncthreads();
   const int row = blockIdx.x;
-  if (s_ok && row < p.M) {
+  const bool mine = !p.owner || ((row >> 7) % p.world) == p.rank;
+  if (s_ok && row < p.M && mine) {
     const int nvec = p.H / 8;
     float acc[VPT][8];
     float ss = 0.f;
@@ -150,10 +160,16 @@ __global__ void __launch_bounds__(256) ar_add_rmsnorm_kernel(const ArParams p) {
 #pragma unroll
         for (int i = 0; i < 8; i += 2)
           o32[i / 2] = pack2(acc[k][i] * rstd * bf2f(wb[i]), acc[k][i + 1] * rstd * bf2f(wb[i + 1]));
-        *reinterpret_cast<uint4*>(xrow + v * 8) = out;
+        if (p.owner) {
+          for (int d = 0; d < p.world; ++d)
+            *reinterpret_cast<uint4*>(p.x_peer[d] + static_cast<size_t>(row) * p.H + v * 8) = out;
+        } else {
+          *reinterpret_cast<uint4*>(xrow + v * 8) = out;
+        }
       }
     }
   }
+  if (p.owner) __threadfence_system();  // the broadcast rows before the arrival signal
   // bookkeeping: the last CTA marks this round consumed
   __syncthreads();
   if (tid == 0) {
@@ -161,7 +177,21 @@ __global__ void __launch_bounds__(256) ar_add_rmsnorm_kernel(const ArParams p) {
     if (atomicAdd(p.fin_ctr, 1u) == gridDim.x - 1) {
       *p.fin_ctr = 0;
       *reinterpret_cast<volatile unsigned int*>(p.consumed) = s_target;
-      __threadfence();
+      __threadfence_system();
+      if (p.owner)
+        for (int d = 0; d < p.world; ++d) atomicAdd_system(p.x_flag[d], 1u);
+    }
+  }
+}
+
+// Bounded wait until *flag >= target (the x rows of every owner arrived).
+__global__ void tp_wait_kernel(const unsigned int* flag, unsigned int target, int* status) {
+  if (threadIdx.x != 0) return;
+  const unsigned long long t0 = globaltimer();
+  while (ld_acquire_sys(flag) < target) {
+    if (globaltimer() - t0 > kWaitNs) {
+      atomicCAS(status, 0, kStatusTimeoutArrive);
+      return;
     }
   }
 }
@@ -191,6 +221,8 @@ extern "C" int ib_ar_add_rmsnorm(const void* recv, long long src_stride, int ld,
   p.eps = eps;
   p.x = static_cast<__nv_bfloat16*>(x);
   p.status = status;
+  p.owner = 0;
+  p.rank = 0;
   const int vpt = (H / 8 + 255) / 256;
   if (vpt <= 2) ar_add_rmsnorm_kernel<2><<<M, 256, 0, stream>>>(p);
   else if (vpt <= 4) ar_add_rmsnorm_kernel<4><<<M, 256, 0, stream>>>(p);
@@ -249,4 +281,48 @@ extern "C" int ib_enable_peer_access(int peer) {
     return 0;
   }
   return static_cast<int>(e);
+}
+
+// Two-shot consumer: like ib_ar_add_rmsnorm for this rank's row blocks only
+// (h holds valid rows only there); the normalised rows go to x_peer[d] on
+// every rank d, then every rank's x_flag[d] is incremented once.
+extern "C" int ib_ar_add_rmsnorm_rs(const void* recv, long long src_stride, int ld, const unsigned int* flags,
+                                    unsigned int* consumed, unsigned int* fin_ctr, int world, int rank, int M, int H,
+                                    void* h, const void* w, float eps, void* const* x_peer,
+                                    unsigned int* const* x_flag, int* status, cudaStream_t stream) {
+  if (M <= 0) return 0;
+  if ((H % 8) != 0 || (ld % 8) != 0 || H > 8 * 256 * 8 || world < 1 || world > kMaxRanks) return -1;
+  ArParams p;
+  p.recv = static_cast<const __nv_bfloat16*>(recv);
+  p.src_stride = src_stride;
+  p.ld = ld;
+  p.flags = flags;
+  p.consumed = consumed;
+  p.fin_ctr = fin_ctr;
+  p.world = world;
+  p.M = M;
+  p.H = H;
+  p.h = static_cast<__nv_bfloat16*>(h);
+  p.w = static_cast<const __nv_bfloat16*>(w);
+  p.eps = eps;
+  p.x = nullptr;
+  p.status = status;
+  p.owner = 1;
+  p.rank = rank;
+  for (int d = 0; d < kMaxRanks; ++d) {
+    p.x_peer[d] = d < world ? static_cast<__nv_bfloat16*>(x_peer[d]) : nullptr;
+    p.x_flag[d] = d < world ? x_flag[d] : nullptr;
+  }
+  const int vpt = (H / 8 + 255) / 256;
+  if (vpt <= 2) ar_add_rmsnorm_kernel<2><<<M, 256, 0, stream>>>(p);
+  else if (vpt <= 4) ar_add_rmsnorm_kernel<4><<<M, 256, 0, stream>>>(p);
+  else ar_add_rmsnorm_kernel<8><<<M, 256, 0, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+extern "C" int ib_tp_wait(const unsigned int* flag, unsigned int target, int* status, cudaStream_t stream) {
+  tp_wait_kernel<<<1, 32, 0, stream>>>(flag, target, status);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
 }

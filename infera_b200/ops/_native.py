@@ -80,6 +80,13 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
                                 c_int, c_int, c_vp, c_vp, c_int, c_int, c_vp, c_vp],
         "ib_gemm_fp8_plan": [c_int, c_int, c_int, c_int, c_int, c_vp],
         "ib_quant_fp8_act": [c_vp, c_int, c_int, c_int, c_vp, c_int, c_vp, c_int, c_vp],
+        "ib_gemm_bf16_push_rs": [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp,
+                                 c_vp, c_vp, c_vp],
+        "ib_gemm_fp8_push_rs": [c_vp, c_vp, c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+        "ib_ar_add_rmsnorm_rs": [c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_float,
+                                 c_vp, c_vp, c_vp, c_vp],
+        "ib_tp_wait": [c_vp, ctypes.c_uint, c_vp, c_vp],
         "ib_mla_decode": [c_vp, c_int, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_float, c_vp, c_vp, c_vp,
                           c_vp, c_vp],
         "ib_mla_rope_kvwrite": [c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_float, c_vp, c_vp],

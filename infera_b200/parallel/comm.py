@@ -15,9 +15,23 @@ parities. ``gemm_allreduce_add_rmsnorm`` runs
     ib_ar_add_rmsnorm   (waits for every rank's arrival, sums the partials
                          in fp32, adds the residual, RMSNorm)
 
-for up to ``max_rows`` tokens (decode and small prefill steps); larger
-batches take the baseline: GEMM, ``torch.distributed.all_reduce`` (NCCL),
-add + RMSNorm. Reference counterpart: the engines' TP all-reduce
+for up to ``max_rows`` tokens (decode and small prefill steps). Larger
+batches, up to ``max_rows_rs``, take the two-shot form when it moves fewer
+bytes (world >= 4, or ``INFERA_TP_TWO_SHOT=1``):
+
+    ib_gemm_*_push_rs     (the epilogue stores each 128-row block of the
+                           output only into its owner's slot, owner =
+                           block % world: a reduce-scatter fused into the GEMM)
+    ib_ar_add_rmsnorm_rs  (the owner sums its blocks' partials, adds the
+                           residual, RMSNorm, and stores the normalised rows
+                           into every rank's x buffer: the all-gather)
+    ib_tp_wait            (bounded wait for every owner's rows)
+
+Per rank that sends 2 (W-1)/W of the activation over NVLink instead of the
+one-shot's (W-1) times it. The residual stays valid only on each row
+block's owner, which is the only rank that reads it again. Anything larger
+takes the baseline: GEMM, ``torch.distributed.all_reduce`` (NCCL), add +
+RMSNorm. Reference counterpart: the engines' TP all-reduce
 (vLLM / SGLang over RCCL on the reference's hardware); the fused form is
 this framework's.
 """
@@ -39,13 +53,16 @@ FLAG_BYTES = 256  # 2 parities x 8 sources x 4 B, padded
 
 class TPComm:
     def __init__(self, rank: int, world: int, device: torch.device, hidden: int, max_rows: int = 256,
-                 nccl_group=None, gloo_group=None, fused: bool = True):
+                 nccl_group=None, gloo_group=None, fused: bool = True, max_rows_rs: int = 0):
         if world > MAX_PEERS:
             raise ValueError(f"tensor parallel size {world} > {MAX_PEERS}")
         self.rank, self.world = rank, world
         self.device = torch.device(device)
         self.hidden = hidden
         self.max_rows = max_rows
+        self.cap = max(max_rows, max_rows_rs)
+        self.two_shot = (world >= 4 or os.environ.get("INFERA_TP_TWO_SHOT") == "1") and max_rows_rs > max_rows
+        self.x_round = [0, 0]
         self.nccl = nccl_group
         self.gloo = gloo_group
         self.fused = fused and self.device.type == "cuda" and os.environ.get("INFERA_TP_FUSED", "1") != "0"
@@ -57,9 +74,10 @@ class TPComm:
     # ------------------------------------------------------------------ setup
     def _setup_symmetric(self) -> None:
         lib = _native.kernels()
-        self.slot_elems = self.max_rows * self.hidden
+        self.slot_elems = self.cap * self.hidden
         self.data_bytes = 2 * self.world * self.slot_elems * 2
-        total = self.data_bytes + FLAG_BYTES
+        self.x_bytes = self.slot_elems * 2 if self.two_shot else 0   # per parity
+        total = self.data_bytes + FLAG_BYTES + 2 * self.x_bytes
         ptr = ctypes.c_void_p()
         _native.check(lib.ib_sym_alloc(total, ctypes.byref(ptr)), "ib_sym_alloc")
         self.base = ptr.value
@@ -105,8 +123,17 @@ class TPComm:
     def _flag(self, rank_base: int, parity: int, src: int) -> int:
         return rank_base + self.data_bytes + (parity * MAX_PEERS + src) * 4
 
+    def _xflag(self, rank_base: int, parity: int) -> int:
+        return rank_base + self.data_bytes + 128 + parity * 4
+
+    def _xbuf(self, rank_base: int, parity: int) -> int:
+        return rank_base + self.data_bytes + FLAG_BYTES + parity * self.x_bytes
+
     def uses_fused(self, rows: int) -> bool:
         return self.fused and rows <= self.max_rows
+
+    def uses_two_shot(self, rows: int) -> bool:
+        return self.fused and self.two_shot and self.max_rows < rows <= self.cap
 
     def gemm_allreduce_add_rmsnorm(self, x: torch.Tensor, w: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor,
                                    eps: float, out: torch.Tensor, parity: int, tmp: torch.Tensor | None = None
@@ -114,6 +141,8 @@ class TPComm:
         """h += all_reduce(x @ w.T); out = rmsnorm(h) * norm_w (h updated in place)."""
         M, Kd = x.shape
         N = w.shape[0]
+        if self.uses_two_shot(M):
+            return self._two_shot(x, w, h, norm_w, eps, out, parity)
         if not self.uses_fused(M):
             o = K.linear(x, w, out=None if tmp is None else tmp[:M])
             if self.world > 1:
@@ -153,6 +182,64 @@ class TPComm:
         _native.check(rc, "ib_ar_add_rmsnorm")
         K._count(3 if splits > 1 else 2)
         return out
+
+    def _two_shot(self, x, w, h, norm_w, eps, out, parity: int) -> torch.Tensor:
+        M, Kd = x.shape
+        N = w.shape[0]
+        assert N == self.hidden and h.is_contiguous() and out.is_contiguous()
+        lib = _native.kernels()
+        sc = K.scratch(x.device)
+        peer_out = (ctypes.c_void_p * MAX_PEERS)(*[self._slot(self.peers[d], parity, self.rank)
+                                                   for d in range(self.world)])
+        peer_flag = (ctypes.c_void_p * MAX_PEERS)(*[self._flag(self.peers[d], parity, self.rank)
+                                                    for d in range(self.world)])
+        ctr = self.ctr.data_ptr()
+        stream = K._stream()
+        if isinstance(w, torch.Tensor):
+            splits = K._gemm_splits(M, N, Kd, 0)
+            ws = sc.ensure_gemm(M * N if splits > 1 else 1)
+            rc = lib.ib_gemm_bf16_push_rs(x.data_ptr(), w.data_ptr(), M, N, Kd, x.stride(0), w.stride(0),
+                                          self.hidden, self.world, peer_out, peer_flag,
+                                          ctypes.c_void_p(ctr + 4 * parity), ws.data_ptr(), sc.status.data_ptr(),
+                                          stream)
+            _native.check(rc, "ib_gemm_bf16_push_rs")
+        else:
+            from infera_b200.ops import fp8
+
+            q, sf = fp8.quant_act(x)
+            splits = fp8._splits(M, N, Kd)
+            ws = sc.ensure_gemm(M * N if splits > 1 else 1)
+            rc = lib.ib_gemm_fp8_push_rs(q.data_ptr(), sf.data_ptr(), sf.stride(0), w.q.data_ptr(), w.sf.data_ptr(),
+                                         M, N, Kd, q.stride(0), w.q.stride(0), self.hidden, self.world, peer_out,
+                                         peer_flag, ctypes.c_void_p(ctr + 4 * parity), ws.data_ptr(),
+                                         sc.status.data_ptr(), stream)
+            _native.check(rc, "ib_gemm_fp8_push_rs")
+        x_peer = (ctypes.c_void_p * MAX_PEERS)(*[self._xbuf(self.peers[d], parity) for d in range(self.world)])
+        x_flag = (ctypes.c_void_p * MAX_PEERS)(*[self._xflag(self.peers[d], parity) for d in range(self.world)])
+        rc = lib.ib_ar_add_rmsnorm_rs(ctypes.c_void_p(self._slot(self.base, parity, 0)), self.slot_elems, self.hidden,
+                                      ctypes.c_void_p(self._flag(self.base, parity, 0)),
+                                      ctypes.c_void_p(ctr + 4 * (2 + parity)), ctypes.c_void_p(ctr + 4 * (4 + parity)),
+                                      self.world, self.rank, M, N, h.data_ptr(), norm_w.data_ptr(), eps, x_peer,
+                                      x_flag, sc.status.data_ptr(), stream)
+        _native.check(rc, "ib_ar_add_rmsnorm_rs")
+        self.x_round[parity] += 1
+        target = (self.x_round[parity] * self.world) & 0xFFFFFFFF
+        rc = lib.ib_tp_wait(ctypes.c_void_p(self._xflag(self.base, parity)), target, sc.status.data_ptr(), stream)
+        _native.check(rc, "ib_tp_wait")
+        out.copy_(self._x_view(parity, M))
+        K._count(4 if splits > 1 else 3)
+        return out
+
+    def _x_view(self, parity: int, rows: int) -> torch.Tensor:
+        from infera_b200.parallel.symmem import _View
+
+        class _B:
+            pass
+
+        b = _B()
+        b.ptr = self._xbuf(self.base, parity)
+        t = torch.as_tensor(_View(b, (rows, self.hidden), "<i2"), device=self.device).view(torch.bfloat16)
+        return t
 
     def all_gather_cols(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """[M, n] per rank -> [M, world * n] (rank r's columns at r*n), NCCL."""

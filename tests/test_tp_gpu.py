@@ -21,6 +21,24 @@ def test_fused_allreduce_single_rank():
     main(["--rows", "1,64,200", "--hidden", "4096", "--k-total", "2048", "--check-only"])
 
 
+def test_two_shot_single_rank():
+    from infera_b200.bench.tp_comm_bench import main
+
+    # reduce-scatter epilogue + owner reduce / broadcast + wait, on one GPU
+    main(["--rows", "64,300,1024", "--hidden", "4096", "--k-total", "2048", "--check-only",
+          "--one-shot-rows", "128"])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_shot_two_ranks():
+    env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29613", "-m",
+           "infera_b200.bench.tp_comm_bench", "--rows", "256,700,2048", "--one-shot-rows", "256", "--check-only"]
+    r = subprocess.run(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, timeout=300)
+    assert r.returncode == 0, r.stdout.decode()[-3000:]
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_fused_allreduce_two_ranks():
     env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
