@@ -19,8 +19,10 @@ from infera_b200.parallel.comm import TPComm
 
 
 def init_tp(tp_size: int, hidden: int | None = None, model: str | None = None, max_rows: int = 256,
-            timeout_s: float = 600.0):
-    """Returns (TPComm, rank, device). ``hidden`` defaults from ``model``."""
+            timeout_s: float = 600.0, max_rows_rs: int = 2048 + 256):
+    """Returns (TPComm, rank, device). ``hidden`` defaults from ``model``;
+    steps of up to ``max_rows`` tokens use the one-shot fused all-reduce, up
+    to ``max_rows_rs`` the two-shot one (at 4 or more ranks)."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(tp_size)))
     local = int(os.environ.get("LOCAL_RANK", str(rank)))
@@ -37,5 +39,6 @@ def init_tp(tp_size: int, hidden: int | None = None, model: str | None = None, m
         from infera_b200.models.config import get_config
 
         hidden = get_config(model or "llama-3.1-8b").hidden
-    tp = TPComm(rank, world, dev, hidden, max_rows=max_rows, nccl_group=dist.group.WORLD, gloo_group=gloo)
+    tp = TPComm(rank, world, dev, hidden, max_rows=max_rows, nccl_group=dist.group.WORLD, gloo_group=gloo,
+                max_rows_rs=max_rows_rs)
     return tp, rank, dev
