@@ -620,8 +620,7 @@ inline void choose_splits(Plan& pl, int num_sms, int force_split) {
   int best = 1;
   if (force_split > 0) {
     best = force_split;
-  } else if (tiles < num_sms || (p.M <= 256 && tiles % num_sms != 0 && tiles < 4 * num_sms)) {
-    // few tiles, or a decode-sized GEMM whose last wave is partly empty
+  } else if (tiles < num_sms) {
     double best_cost = 1e30;
     for (int s = 1; s <= 16; ++s) {
       if (p.nkb / s < 4 && s > 1) break;
