@@ -3,7 +3,7 @@
 //   C[M, N] = A[M, K] . W[N, K]^T        (nn.Linear layout, both K-major)
 //
 // Persistent, warp-specialised kernel, one CTA per SM:
-//   warp 0      TMA producer (one elected lane) -> STAGES-deep smem ring
+//   warp 0      TMA producer (one elected lane) -> 4-deep (fp8: 5-deep) smem ring
 //   warp 1      TMEM allocator + MMA issuer (one elected lane)
 //   warps 2..5  epilogue: tcgen05.ld -> registers -> global
 // Two TMEM accumulators (2 x 256 fp32 columns) let the epilogue of tile i
@@ -48,7 +48,11 @@ constexpr int P_STAGE = BM * BK * 2;      // 16 KiB
 constexpr int Q_STAGE = MAX_BN * BK * 2;  // 32 KiB
 constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 512;
-constexpr int SMEM_BYTES = 1024 + STAGES * (P_STAGE + Q_STAGE) + 256;
+constexpr int STAGES_FP8 = 5;                  // shorter MMA time per byte: a deeper ring
+constexpr int Q_STAGE_FP8 = 192 * 128;         // 192 token rows x 128 e4m3
+constexpr int SMEM_BF16 = STAGES * (P_STAGE + Q_STAGE);
+constexpr int SMEM_FP8 = STAGES_FP8 * (P_STAGE + Q_STAGE_FP8);
+constexpr int SMEM_BYTES = 1024 + (SMEM_BF16 > SMEM_FP8 ? SMEM_BF16 : SMEM_FP8) + 256;
 constexpr int NUM_THREADS_FP8 = 320;
 constexpr int MAX_BN_FP8 = 192;
 constexpr int BK_FP8 = 128;           // one 128-byte swizzle atom of e4m3
@@ -257,18 +261,20 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
                 const Params p) {
   constexpr int kBK = FP8 ? BK_FP8 : BK;          // K elements per stage (128 bytes per row)
   constexpr int kAccCols = FP8 ? MAX_BN_FP8 : MAX_BN;
+  constexpr int kStages = FP8 ? STAGES_FP8 : STAGES;
+  constexpr int kQStage = FP8 ? Q_STAGE_FP8 : Q_STAGE;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sP = smem;
-  uint8_t* sQ = smem + STAGES * P_STAGE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sQ + STAGES * Q_STAGE);
+  uint8_t* sQ = smem + kStages * P_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sQ + kStages * kQStage);
   uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* empty = bars + kStages;
+  uint64_t* tfull = bars + 2 * kStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* sf_full = drain + 1;  // fp8: scale factors of a stage are in TMEM
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_full + STAGES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_full + kStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -276,7 +282,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
   const int total = p.grouped ? *p.gnum : p.p_tiles * p.q_tiles * p.splits;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -286,7 +292,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     }
     mbar_init(drain, 1);
     if (FP8)
-      for (int s = 0; s < STAGES; ++s) mbar_init(&sf_full[s], 4);
+      for (int s = 0; s < kStages; ++s) mbar_init(&sf_full[s], 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -325,9 +331,9 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
           }
           mbar_expect_tx(&full[stage], tx);
           tma_load_2d(sP + stage * P_STAGE, &tmP, &full[stage], kb * kBK, tile_prow(p, t, pt), polP);
-          tma_load_2d(sQ + stage * Q_STAGE, &tmQ, &full[stage], kb * kBK, tile_qrow(p, t, qt), polQ);
+          tma_load_2d(sQ + stage * kQStage, &tmQ, &full[stage], kb * kBK, tile_qrow(p, t, qt), polQ);
           ++issued;
-          if (++stage == STAGES) {
+          if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -335,9 +341,9 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       }
       if (!ok) {
         // Let every copy already issued land before the CTA can exit.
-        long long first = issued > STAGES ? issued - STAGES : 0;
+        long long first = issued > kStages ? issued - kStages : 0;
         for (long long i = first; i < issued; ++i)
-          mbar_wait(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1), nullptr, nullptr, 0,
+          mbar_wait(&full[i % kStages], static_cast<uint32_t>((i / kStages) & 1), nullptr, nullptr, 0,
                     kWaitLimitNs / 4);
       }
     }
@@ -368,7 +374,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sP + stage * P_STAGE);
-          const uint32_t b_addr = smem_u32(sQ + stage * Q_STAGE);
+          const uint32_t b_addr = smem_u32(sQ + stage * kQStage);
           // four UMMAs per 128-byte stage: K = 16 (bf16) or 32 (e4m3) each,
           // 32 bytes further into the swizzle atom
 #pragma unroll
@@ -383,7 +389,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
             }
           }
           umma_commit(&empty[stage]);
-          if (++stage == STAGES) {
+          if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -444,7 +450,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sf_full[stage]);
-      if (++stage == STAGES) {
+      if (++stage == kStages) {
         stage = 0;
         phase ^= 1u;
       }
