@@ -54,7 +54,8 @@ def run_case(case: str, iters: int) -> dict:
         from infera_b200.ops import fp8
 
         M, N, Kd, swiglu = {"fp8_decode": (64, 28672, 8192, True), "fp8_prefill": (4096, 8192, 8192, False),
-                            "fp8_decode_small": (8, 10240, 8192, False)}[case]
+                            "fp8_decode_small": (8, 10240, 8192, False),
+                            "fp8_prefill_small": (2048, 4096, 4096, False)}[case]
         x = torch.randn(M, Kd, device=dev, generator=g).to(bf)
         wq = fp8.quantize_weight(torch.randn(N, Kd, device=dev, generator=g) / math.sqrt(Kd))
         q, sf = fp8.quant_act(x)
@@ -63,10 +64,10 @@ def run_case(case: str, iters: int) -> dict:
         fl = 2 * M * N * Kd
         by = M * Kd + N * Kd + N * Kd // 16384 + M * (N // 2 if swiglu else N) * 2
         return {"case": case, "ms": ms, "ms_with_act_quant": ms_q, "tflops": fl / ms / 1e9, "gbs": by / ms / 1e6}
-    if case == "mla_decode":
+    if case in ("mla_decode", "mla_decode_small"):
         from infera_b200.ops import mla as M
 
-        B, L, hq = 64, 4096, 128
+        B, L, hq = (64, 4096, 128) if case == "mla_decode" else (16, 4096, 128)
         pages = B * L // 16
         cache = torch.randn(pages * 16, 576, device=dev, generator=g).to(bf)
         bt = torch.randperm(pages, device=dev, dtype=torch.int32).view(B, -1)
