@@ -12,17 +12,21 @@
 // the tile unused), one 256-dim half of the value dims and one split of the
 // keys:
 //   warp 0      TMA producer: the query's 9 x [128 x 64] blocks once, then
-//               key tiles of 32 tokens (2 pages x 9 blocks of 64 dims) into a
-//               2-stage ring
-//   warp 1      MMA issuer: S = Q K^T (M 128, N 32, K 576) into TMEM (double
-//               buffered); O += P V (M 128, N 256, K 32) with V = the tile's
+//               key tiles of one page (16 tokens x 9 blocks of 64 dims) into
+//               a 4-stage ring
+//   warp 1      MMA issuer: S = Q K^T (M 128, N 16, K 576) into TMEM (double
+//               buffered); O += P V (M 128, N 256, K 16) with V = the tile's
 //               latent dims of this CTA's half, read MN-major from the same
 //               ring stage
 //   warps 2..5  softmax, thread = head row: running max with lazy O rescale
 //               (only when the max grows by more than 2^8), P to shared
-//               memory (K-major, 64-byte swizzle), final O / l epilogue or
-//               split partials with their log-sum-exp
-// TMEM: S 2 x 32 columns, O 256 columns. The 128 x 512 fp32 output of all
+//               memory (K-major, 64-byte swizzle; even tiles in the first 16
+//               columns, odd tiles in the last 16, so P of tile j is written
+//               while tile j-1's P is still being read), final O / l
+//               epilogue or split partials with their log-sum-exp
+// Small page-sized tiles in a 4-deep ring keep more key bytes in flight
+// than a 2-deep ring of larger tiles in the same 72 KiB.
+// TMEM: S 2 x 16 columns, O 256 columns. The 128 x 512 fp32 output of all
 // heads would fill TMEM on its own, hence the value split over two CTAs (the
 // two recompute S; they read the same key tiles, which L2 serves once).
 // Prefill reuses the kernel with one "query" per prompt token (its own
@@ -40,16 +44,16 @@ constexpr int DL = 512;
 constexpr int DR = 64;
 constexpr int DQK = DL + DR;
 constexpr int NCH = DQK / 64;              // 9 blocks of 64 dims
-constexpr int BT = 32;                     // keys per tile
+constexpr int BT = 16;                     // keys per tile (one page)
 constexpr int PAGE = 16;
-constexpr int STAGES = 2;
+constexpr int STAGES = 4;
 constexpr int QCH = 128 * 128;             // one [128 rows x 64 dims] bf16 block
-constexpr int KCH = BT * 128;              // one [32 keys x 64 dims] block
-constexpr int KV_STAGE = NCH * KCH;        // 36 KiB
-constexpr int P_BYTES = 128 * BT * 2;      // 8 KiB
+constexpr int KCH = BT * 128;              // one [16 keys x 64 dims] block
+constexpr int KV_STAGE = NCH * KCH;        // 18 KiB
+constexpr int P_BYTES = 128 * 32 * 2;      // 8 KiB: two 16-key halves
 constexpr int DV = 256;                    // value dims per CTA
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t S_COL0 = 0, S_COL1 = 32, O_COL = 64;
+constexpr uint32_t S_COL0 = 0, S_COL1 = 16, O_COL = 64;
 constexpr int SMEM_BYTES = 1024 + NCH * QCH + STAGES * KV_STAGE + P_BYTES + 256;
 
 struct Params {
@@ -97,8 +101,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* kv_empty = kv_full + STAGES; // [STAGES]
   uint64_t* s_full = kv_empty + STAGES;  // [2]
   uint64_t* p_full = s_full + 2;
-  uint64_t* o_done = p_full + 1;
-  uint64_t* drain = o_done + 1;
+  uint64_t* o_done = p_full + 1;         // [2]: PV of even / odd tiles
+  uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -122,7 +126,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
     mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    mbar_init(&o_done[0], 1);
+    mbar_init(&o_done[1], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -147,21 +152,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_expect_tx(q_full, NCH * QCH);
       for (int c = 0; c < NCH; ++c) tma_load_2d(sQ + c * QCH, &tmQ, q_full, c * 64, qi * p.hq, pol_q);
       const int* bt = p.block_table + static_cast<size_t>(p.q_row[qi]) * p.max_pages;
-      const int n_pages = (kvlen + PAGE - 1) / PAGE;
       long long issued = 0;
+      int pg_next = __ldg(bt + tile0);
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % STAGES;
         const uint32_t ph = (j / STAGES) & 1;
-        const int lp0 = (tile0 + j) * 2;
-        const int pg0 = __ldg(bt + lp0);
-        const int pg1 = __ldg(bt + (lp0 + 1 < n_pages ? lp0 + 1 : lp0));
+        const int pg = pg_next;
+        if (j + 1 < n_tiles) pg_next = __ldg(bt + tile0 + j + 1);  // in flight while we wait
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
         uint8_t* base = sKV + st * KV_STAGE;
         mbar_expect_tx(&kv_full[st], KV_STAGE);
-        for (int c = 0; c < NCH; ++c) {
-          tma_load_2d(base + c * KCH, &tmKV, &kv_full[st], c * 64, pg0 * PAGE, pol_kv);
-          tma_load_2d(base + c * KCH + PAGE * 128, &tmKV, &kv_full[st], c * 64, pg1 * PAGE, pol_kv);
-        }
+        for (int c = 0; c < NCH; ++c) tma_load_2d(base + c * KCH, &tmKV, &kv_full[st], c * 64, pg * PAGE, pol_kv);
         ++issued;
       }
       // drain: every issued copy must land before the CTA exits
@@ -183,16 +184,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           return false;
         tc_fence_after();
         const int st = jj % STAGES;
-        // V = latent dims [256*half, +256) of the tile: blocks 4*half .. 4*half+3
+        // V = latent dims [256*half, +256) of the tile: blocks 4*half .. 4*half+3;
+        // P of this tile = columns [16*(jj&1), +16) of the P buffer
         const uint32_t v_addr = smem_u32(sKV + st * KV_STAGE + half * 4 * KCH);
-#pragma unroll
-        for (int kk = 0; kk < BT / 16; ++kk) {
-          const uint64_t ad = make_sw64_desc(p_addr + kk * 32, 512);
-          // MN-major V: LBO = distance between 64-dim blocks, SBO = 8 keys
-          const uint64_t bd = make_sw128_desc(v_addr + kk * 2048, KCH, 1024);
-          umma_bf16(tmem + O_COL, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(o_done);
+        const uint64_t ad = make_sw64_desc(p_addr + (jj & 1) * 32, 512);
+        // MN-major V: LBO = distance between 64-dim blocks, SBO = 8 keys
+        const uint64_t bd = make_sw128_desc(v_addr, KCH, 1024);
+        umma_bf16(tmem + O_COL, ad, bd, idesc_pv, jj > 0 ? 1u : 0u);
+        umma_commit(&o_done[jj & 1]);
         umma_commit(&kv_empty[st]);
         return true;
       };
@@ -238,13 +237,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      uint32_t v[32];
-      tmem_ld32(lane_addr + ((j & 1) ? S_COL1 : S_COL0), v);
+      uint32_t v[16];
+      tmem_ld16(lane_addr + ((j & 1) ? S_COL1 : S_COL0), v);
       tmem_ld_wait();
       const int lim = kvlen - (tile0 + j) * BT;  // keys c < lim are valid
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         if (i >= lim) v[i] = __float_as_uint(-INFINITY);
         mx = fmaxf(mx, __uint_as_float(v[i]));
       }
@@ -254,10 +253,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float m_use = rescale ? m_new : m_run;
       const float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
       const bool warp_rescale = __any_sync(0xffffffffu, rescale && j > 0);
-      if (j > 0) {
-        // P of the previous tile must be consumed (and O complete) first
-        if (!mbar_wait_warp(o_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status,
-                            kStatusTimeoutTmemFull)) {
+      // this P half was last read by tile j-2's PV; a rescale of O needs
+      // every PV so far (tile j-1's, which completes after j-2's) done
+      const int wait_tile = warp_rescale ? j - 1 : j - 2;
+      if (wait_tile >= 0) {
+        if (!mbar_wait_warp(&o_done[wait_tile & 1], static_cast<uint32_t>((wait_tile >> 1) & 1), abort_flag,
+                            p.status, kStatusTimeoutTmemFull)) {
           ok = false;
           break;
         }
@@ -276,9 +277,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_st_wait();
       }
       float sum = 0.f;
-      uint32_t pk[16];
+      uint32_t pk[8];
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
+      for (int i = 0; i < 16; i += 2) {
         const float e0 = exp2f(fmaf(__uint_as_float(v[i]), p.scale_log2, -m_use));
         const float e1 = exp2f(fmaf(__uint_as_float(v[i + 1]), p.scale_log2, -m_use));
         __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
@@ -286,8 +287,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         pk[i / 2] = *reinterpret_cast<uint32_t*>(&bb);
       }
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<uint4*>(sP + sw64_offset(r, c)) =
+      for (int c = 0; c < 2; ++c)
+        *reinterpret_cast<uint4*>(sP + sw64_offset(r, 2 * (j & 1) + c)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       l_run = l_run * alpha + sum;
       m_run = m_use;
@@ -310,8 +311,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (half == 0) p.lse_part[prow] = -INFINITY;
         }
       }
-    } else if (ok && mbar_wait_warp(o_done, static_cast<uint32_t>((n_tiles - 1) & 1), abort_flag, p.status,
-                                    kStatusTimeoutTmemFull)) {
+    } else if (ok && mbar_wait_warp(&o_done[(n_tiles - 1) & 1], static_cast<uint32_t>(((n_tiles - 1) >> 1) & 1),
+                                    abort_flag, p.status, kStatusTimeoutTmemFull)) {
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
       const size_t prow = (static_cast<size_t>(qi) * p.splits + sp) * p.hq + r;
