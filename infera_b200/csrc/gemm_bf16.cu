@@ -402,9 +402,9 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     }
   } else if (FP8 && warp >= 6) {
     // scale-factor stagers: one warp per TMEM lane quadrant writes the same
-    // values into its own quadrant. The scale bytes of stage i+2 are loaded
-    // while stage i is stored (two register sets used alternately), so a
-    // global-load latency is not paid once per stage.
+    // values into its own quadrant. The scale bytes of stage i+4 are loaded
+    // while stage i is stored, so a global-load latency is not paid once
+    // per stage.
     const int q = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     // fetch cursor over the (tile, k-block) sequence this CTA walks
@@ -456,15 +456,27 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       }
       return true;
     };
-    uint32_t wa = 0, ra[8], wbb = 0, rb[8];
-    bool has_a = fetch(wa, ra);
-    bool has_b = fetch(wbb, rb);
-    while (has_a) {
-      if (!store(wa, ra)) break;
-      has_a = fetch(wa, ra);
-      if (!has_b) break;
-      if (!store(wbb, rb)) break;
-      has_b = fetch(wbb, rb);
+    // four register sets in flight: the loads of stage i+4 are issued when
+    // stage i is stored (compile-time indices keep them in registers)
+    constexpr int kAhead = 4;
+    uint32_t wv[kAhead], rv[kAhead][8];
+    bool has[kAhead];
+#pragma unroll
+    for (int k = 0; k < kAhead; ++k) has[k] = fetch(wv[k], rv[k]);
+    bool go = true;
+    while (go) {
+#pragma unroll
+      for (int k = 0; k < kAhead; ++k) {
+        if (go && has[k]) {
+          if (!store(wv[k], rv[k])) {
+            go = false;
+          } else {
+            has[k] = fetch(wv[k], rv[k]);
+          }
+        } else {
+          go = false;
+        }
+      }
     }
   } else {
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
