@@ -96,27 +96,42 @@ def xxhash_include() -> Path:
     raise RuntimeError("xxhash.h not found (set XXHASH_INCLUDE)")
 
 
-def build_router() -> Path | None:
+SANITIZERS = {
+    # name: compile / link flags (race and memory checking of the host code;
+    # the GPU-side sanitizer is not available on the GPU machines)
+    "asan": ["-O1", "-g", "-fno-omit-frame-pointer", "-fsanitize=address,undefined", "-fno-sanitize-recover=undefined"],
+    "tsan": ["-O1", "-g", "-fno-omit-frame-pointer", "-fsanitize=thread"],
+}
+
+
+def build_router(sanitize: str | None = None) -> Path | None:
+    """The native router; ``sanitize`` ("asan" = AddressSanitizer +
+    UndefinedBehaviorSanitizer, "tsan" = ThreadSanitizer) builds
+    ``ib200_router_<name>`` next to the release binary."""
     sources = sorted(ROUTER_SRC.glob("*.cpp")) if ROUTER_SRC.exists() else []
     if not sources:
         return None
     headers = sorted(ROUTER_SRC.glob("*.h"))
-    if _newer([*sources, *headers], ROUTER_BIN):
+    flags = ["-O2"] if sanitize is None else SANITIZERS[sanitize]
+    out_bin = ROUTER_BIN if sanitize is None else LIB / f"ib200_router_{sanitize}"
+    tag = "router_" if sanitize is None else f"router_{sanitize}_"
+    if _newer([*sources, *headers], out_bin):
         LIB.mkdir(parents=True, exist_ok=True)
         objs = []
         todo = []
         for src in sources:
-            obj = OBJ / ("router_" + src.stem + ".o")
+            obj = OBJ / (tag + src.stem + ".o")
             objs.append(obj)
             if _newer([src, *headers], obj):
-                todo.append(["g++", "-O2", "-std=c++17", "-Wall", "-I", str(ROUTER_SRC), "-I", str(xxhash_include()),
+                todo.append(["g++", *flags, "-std=c++17", "-Wall", "-I", str(ROUTER_SRC), "-I", str(xxhash_include()),
                              "-c", str(src), "-o", str(obj)])
         OBJ.mkdir(parents=True, exist_ok=True)
         if todo:
             with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
                 list(ex.map(_run, todo))
-        _run(["g++", "-o", str(ROUTER_BIN), *map(str, objs), "-lpthread"])
-    return ROUTER_BIN
+        link = [] if sanitize is None else [f for f in flags if f.startswith("-fsanitize")]
+        _run(["g++", *link, "-o", str(out_bin), *map(str, objs), "-lpthread"])
+    return out_bin
 
 
 def build_all(verbose: bool = False) -> dict[str, str | None]:

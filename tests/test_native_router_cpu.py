@@ -22,15 +22,31 @@ from infera_b200.server.launch_native import native_argv, router_binary
 from infera_b200.utils.hashing import chain_hashes
 
 
-@pytest.fixture(scope="module")
-def binary():
-    return router_binary()
+# release build, plus AddressSanitizer + UndefinedBehaviorSanitizer and
+# ThreadSanitizer builds of the same sources: every router started by a test
+# logs stderr to a file that must hold no sanitizer report
+_SAN_ENV = {"ASAN_OPTIONS": "detect_leaks=0:abort_on_error=0", "UBSAN_OPTIONS": "print_stacktrace=1",
+            "TSAN_OPTIONS": "halt_on_error=0:second_deadlock_stack=1"}
+_SAN_MARKS = ("ERROR: AddressSanitizer", "runtime error:", "WARNING: ThreadSanitizer", "ERROR: ThreadSanitizer")
+
+
+@pytest.fixture(scope="module", params=["release", "asan", "tsan"])
+def binary(request):
+    if request.param == "release":
+        return router_binary()
+    from infera_b200.build import build_router
+
+    return str(build_router(request.param))
 
 
 def _start_router(binary, *args):
+    import tempfile
+
     port = free_port()
+    log = tempfile.NamedTemporaryFile(prefix="ib200_router_", suffix=".log", delete=False)
     p = subprocess.Popen([binary, "--port", str(port), "--host", "127.0.0.1", *args], stdout=subprocess.DEVNULL,
-                         stderr=subprocess.DEVNULL, start_new_session=True)
+                         stderr=log, start_new_session=True, env=dict(os.environ, **_SAN_ENV))
+    p._log_path = log.name
     url = f"http://127.0.0.1:{port}"
     t0 = time.time()
     while time.time() - t0 < 10:
@@ -46,16 +62,26 @@ def _start_router(binary, *args):
 def _stop(p):
     p.terminate()
     try:
-        p.wait(timeout=10)
+        p.wait(timeout=20)
     except subprocess.TimeoutExpired:
         p.kill()
+    path = getattr(p, "_log_path", None)
+    if path:
+        with open(path, errors="replace") as f:
+            text = f.read()
+        os.unlink(path)
+        hits = [m for m in _SAN_MARKS if m in text]
+        assert not hits, text[-6000:]
 
 
 @pytest.mark.parametrize("bs", [4, 16, 32, 64])
 def test_chain_hashes_bit_exact(binary, bs):
     ids = [(i * 7919 + 13) % 128256 for i in range(bs * 9 + 3)]
-    out = subprocess.run([binary, "--print-chain-hashes", str(bs)], input=" ".join(map(str, ids)).encode(),
-                         stdout=subprocess.PIPE, timeout=30, check=True).stdout.decode().split()
+    r = subprocess.run([binary, "--print-chain-hashes", str(bs)], input=" ".join(map(str, ids)).encode(),
+                       stdout=subprocess.PIPE, stderr=subprocess.PIPE, timeout=60, check=True,
+                       env=dict(os.environ, **_SAN_ENV))
+    assert not [m for m in _SAN_MARKS if m in r.stderr.decode(errors="replace")], r.stderr.decode()[-4000:]
+    out = r.stdout.decode().split()
     assert [int(x) for x in out] == chain_hashes(ids, bs)
 
 
