@@ -100,8 +100,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* kv_full = bars + 1;          // [STAGES]
   uint64_t* kv_empty = kv_full + STAGES; // [STAGES]
   uint64_t* s_full = kv_empty + STAGES;  // [2]
+  // [2] each: P half written (128 arrivals) / PV done, for even and odd
+  // tiles. One barrier per half: a warp may run a tile ahead of the others
+  // (writing the other half), and its arrival must not count toward the
+  // tile the slower warps are still writing.
   uint64_t* p_full = s_full + 2;
-  uint64_t* o_done = p_full + 1;         // [2]: PV of even / odd tiles
+  uint64_t* o_done = p_full + 2;
   uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -125,7 +129,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 128);
+    mbar_init(&p_full[0], 128);
+    mbar_init(&p_full[1], 128);
     mbar_init(&o_done[0], 1);
     mbar_init(&o_done[1], 1);
     mbar_init(drain, 1);
@@ -180,7 +185,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t p_addr = smem_u32(sP);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kStatusTimeoutFull);
       auto issue_pv = [&](int jj) -> bool {
-        if (!mbar_wait(p_full, static_cast<uint32_t>(jj & 1), abort_flag, p.status, kStatusTimeoutTmemEmpty))
+        if (!mbar_wait(&p_full[jj & 1], static_cast<uint32_t>((jj >> 1) & 1), abort_flag, p.status,
+                       kStatusTimeoutTmemEmpty))
           return false;
         tc_fence_after();
         const int st = jj % STAGES;
@@ -294,7 +300,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       m_run = m_use;
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1]);
     }
     ok = __all_sync(0xffffffffu, ok);
     const bool write = r < p.hq;
