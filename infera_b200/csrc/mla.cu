@@ -68,7 +68,16 @@ struct Params {
   float* o_part;           // [nq, splits, hq, 512]
   float* lse_part;         // [nq, splits, hq] (log2 units)
   int* status;
+  long long* trace;        // optional: clock64 stamps of CTA (0,0,0)'s pipeline events (see TR_*)
 };
+
+// pipeline event stamps (trace[event * kTraceTiles + tile]) for diagnosis
+enum : int { TR_TMA = 0, TR_KVFULL, TR_SISSUE, TR_PFULL, TR_SFULL, TR_ODONE, TR_PARRIVE, kTraceEvents };
+constexpr int kTraceTiles = 64;
+
+__device__ __forceinline__ void stamp(const Params& p, bool cta0, int ev, int j) {
+  if (p.trace != nullptr && cta0 && j < kTraceTiles) p.trace[ev * kTraceTiles + j] = clock64();
+}
 
 // K-major operand with 64-byte swizzle (layout type 4): 8-row atoms of
 // 64-byte rows, atoms SBO bytes apart.
@@ -120,6 +129,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int tps = (n_tiles_all + p.splits - 1) / p.splits;
   const int tile0 = sp * tps;
   const int n_tiles = max(0, min(n_tiles_all - tile0, tps));
+  const bool cta0 = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -168,6 +178,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint8_t* base = sKV + st * KV_STAGE;
         mbar_expect_tx(&kv_full[st], KV_STAGE);
         for (int c = 0; c < NCH; ++c) tma_load_2d(base + c * KCH, &tmKV, &kv_full[st], c * 64, pg * PAGE, pol_kv);
+        stamp(p, cta0, TR_TMA, j);
         ++issued;
       }
       // drain: every issued copy must land before the CTA exits
@@ -188,6 +199,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!mbar_wait(&p_full[jj & 1], static_cast<uint32_t>((jj >> 1) & 1), abort_flag, p.status,
                        kStatusTimeoutTmemEmpty))
           return false;
+        stamp(p, cta0, TR_PFULL, jj);
         tc_fence_after();
         const int st = jj % STAGES;
         // V = latent dims [256*half, +256) of the tile: blocks 4*half .. 4*half+3;
@@ -208,6 +220,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ok = false;
           break;
         }
+        stamp(p, cta0, TR_KVFULL, j);
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sKV + st * KV_STAGE);
         const uint32_t s_col = (j & 1) ? S_COL1 : S_COL0;
@@ -220,6 +233,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
         umma_commit(&s_full[j & 1]);
+        stamp(p, cta0, TR_SISSUE, j);
         if (j > 0 && !issue_pv(j - 1)) {
           ok = false;
           break;
@@ -242,6 +256,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ok = false;
         break;
       }
+      if (r == 0) stamp(p, cta0, TR_SFULL, j);
       tc_fence_after();
       uint32_t v[16];
       tmem_ld16(lane_addr + ((j & 1) ? S_COL1 : S_COL0), v);
@@ -270,6 +285,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_fence_after();
       }
+      if (r == 0) stamp(p, cta0, TR_ODONE, j);
       if (warp_rescale) {
 #pragma unroll 1
         for (int c0 = 0; c0 < DV; c0 += 16) {
@@ -301,6 +317,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
+      if (r == 0) stamp(p, cta0, TR_PARRIVE, j);
     }
     ok = __all_sync(0xffffffffu, ok);
     const bool write = r < p.hq;
@@ -456,6 +473,12 @@ using namespace ib200;
 // cache: [num_slots, 576] bf16; q_row / q_kvlen: [nq] device int32; out:
 // [nq, hq, 512] bf16. splits > 1 needs o_part [nq, splits, hq, 512] and
 // lse_part [nq, splits, hq] fp32 scratch.
+static long long* g_mla_trace = nullptr;
+
+// Diagnostics: the next launches stamp CTA (0,0,0)'s pipeline events into
+// trace[7 * 64] (clock64), or stop when trace is null.
+extern "C" void ib_mla_set_trace(long long* trace) { g_mla_trace = trace; }
+
 extern "C" int ib_mla_decode(const void* q, int nq, int hq, const void* cache, long long num_slots,
                              const int* q_row, const int* q_kvlen, const int* block_table, int max_pages,
                              int splits, float scale, void* out, float* o_part, float* lse_part,
@@ -480,6 +503,7 @@ extern "C" int ib_mla_decode(const void* q, int nq, int hq, const void* cache, l
   p.o_part = o_part;
   p.lse_part = lse_part;
   p.status = status;
+  p.trace = g_mla_trace;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
