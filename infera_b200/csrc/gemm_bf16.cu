@@ -80,6 +80,7 @@ struct Params {
   unsigned int* peer_flag[kMaxPeers];
   unsigned int* done_ctr;   // local, zero between launches
   int push_owner;           // 1: a tile of token rows goes only to rank (row block % world) (reduce-scatter)
+  long long* trace;         // optional: clock64 stamps of CTA 0's pipeline events (TRG_*)
   // grouped mode (MoE experts, swap-AB only): tile t = gtab[t] = {expert,
   // feature tile, first token row, end token row of the expert}; *gnum tiles
   int grouped;
@@ -93,6 +94,14 @@ struct Params {
   const uint8_t* sf_a;
   int sf_w_ld, sf_a_ld;
 };
+
+// pipeline event stamps of CTA 0 (trace[event * kTraceSteps + k-step]) for diagnosis
+enum : int { TRG_TMA = 0, TRG_FULL, TRG_SFFULL, TRG_ISSUED, TRG_SFARRIVE, kTraceEventsG };
+constexpr int kTraceSteps = 128;
+
+__device__ __forceinline__ void gstamp(const Params& p, int ev, long long i) {
+  if (p.trace != nullptr && blockIdx.x == 0 && i < kTraceSteps) p.trace[ev * kTraceSteps + i] = clock64();
+}
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
@@ -332,6 +341,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
           mbar_expect_tx(&full[stage], tx);
           tma_load_2d(sP + stage * P_STAGE, &tmP, &full[stage], kb * kBK, tile_prow(p, t, pt), polP);
           tma_load_2d(sQ + stage * kQStage, &tmQ, &full[stage], kb * kBK, tile_qrow(p, t, qt), polQ);
+          gstamp(p, TRG_TMA, issued);
           ++issued;
           if (++stage == kStages) {
             stage = 0;
@@ -353,6 +363,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       uint32_t stage = 0, phase = 0;
       int local = 0;
       bool ok = true;
+      long long steps = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
         int pt, qt, sp;
         tile_coords(p, t, pt, qt, sp);
@@ -368,10 +379,12 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
             ok = false;
             break;
           }
+          gstamp(p, TRG_FULL, steps);
           if (FP8 && !mbar_wait(&sf_full[stage], phase, abort_flag, p.status, kStatusTimeoutFull)) {
             ok = false;
             break;
           }
+          gstamp(p, TRG_SFFULL, steps);
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sP + stage * P_STAGE);
           const uint32_t b_addr = smem_u32(sQ + stage * kQStage);
@@ -389,6 +402,8 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
             }
           }
           umma_commit(&empty[stage]);
+          gstamp(p, TRG_ISSUED, steps);
+          ++steps;
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -436,6 +451,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       return true;
     };
     uint32_t stage = 0, phase = 0;
+    long long sf_steps = 0;
     auto store = [&](uint32_t wb, const uint32_t (&r)[8]) -> bool {
       if (!mbar_wait_warp(&empty[stage], phase ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) return false;
       tc_fence_after();  // the MMAs that read this slot before have completed
@@ -450,6 +466,8 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sf_full[stage]);
+      if (lane == 0 && warp == 6) gstamp(p, TRG_SFARRIVE, sf_steps);
+      ++sf_steps;
       if (++stage == kStages) {
         stage = 0;
         phase ^= 1u;
@@ -614,9 +632,13 @@ struct Plan {
   int grid;
 };
 
+static long long* g_gemm_trace = nullptr;
+
 template <bool FP8>
-inline int launch_gemm(const CUtensorMap& tmP, const CUtensorMap& tmQ, const Params& p, int grid,
+inline int launch_gemm(const CUtensorMap& tmP, const CUtensorMap& tmQ, const Params& p_in, int grid,
                        cudaStream_t stream) {
+  Params p = p_in;
+  p.trace = g_gemm_trace;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -970,3 +992,7 @@ extern "C" void ib_gemm_fp8_plan(int M, int N, int K, int num_sms, int force_spl
   out7[5] = pl.p.kbps;
   out7[6] = pl.grid;
 }
+
+// Diagnostics: the next GEMM launches stamp CTA 0's pipeline events into
+// trace[5 * 128] (clock64), or stop when trace is null.
+extern "C" void ib_gemm_set_trace(long long* trace) { ib200::gemm::g_gemm_trace = trace; }

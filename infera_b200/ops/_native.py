@@ -90,6 +90,7 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_mla_decode": [c_vp, c_int, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_float, c_vp, c_vp, c_vp,
                           c_vp, c_vp],
         "ib_mla_set_trace": [c_vp],
+        "ib_gemm_set_trace": [c_vp],
         "ib_mla_rope_kvwrite": [c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_float, c_vp, c_vp],
     }
     for name, args in sig.items():
@@ -97,7 +98,8 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         if fn is None:
             continue
         fn.argtypes = args
-        fn.restype = None if name in ("ib_gemm_bf16_plan", "ib_gemm_fp8_plan", "ib_mla_set_trace") else c_int
+        fn.restype = None if name in ("ib_gemm_bf16_plan", "ib_gemm_fp8_plan", "ib_mla_set_trace",
+                                        "ib_gemm_set_trace") else c_int
 
 
 def kernels() -> ctypes.CDLL:
