@@ -54,9 +54,8 @@ def main(argv=None) -> None:
     Ks = KT // world
     rows = [int(r) for r in a.rows.split(",")]
     if a.one_shot_rows:
-        os.environ["INFERA_TP_TWO_SHOT"] = "1"
         comm = TPComm(rank, world, dev, H, max_rows=a.one_shot_rows, nccl_group=nccl, gloo_group=gloo,
-                      max_rows_rs=max(rows))
+                      max_rows_rs=max(rows), two_shot=True)
     else:
         comm = TPComm(rank, world, dev, H, max_rows=max(rows), nccl_group=nccl, gloo_group=gloo)
     g = torch.Generator(device=dev).manual_seed(1234)  # same full tensors on every rank

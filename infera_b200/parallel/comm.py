@@ -53,7 +53,8 @@ FLAG_BYTES = 256  # 2 parities x 8 sources x 4 B, padded
 
 class TPComm:
     def __init__(self, rank: int, world: int, device: torch.device, hidden: int, max_rows: int = 256,
-                 nccl_group=None, gloo_group=None, fused: bool = True, max_rows_rs: int = 0):
+                 nccl_group=None, gloo_group=None, fused: bool = True, max_rows_rs: int = 0,
+                 two_shot: bool | None = None):
         if world > MAX_PEERS:
             raise ValueError(f"tensor parallel size {world} > {MAX_PEERS}")
         self.rank, self.world = rank, world
@@ -61,7 +62,9 @@ class TPComm:
         self.hidden = hidden
         self.max_rows = max_rows
         self.cap = max(max_rows, max_rows_rs)
-        self.two_shot = (world >= 4 or os.environ.get("INFERA_TP_TWO_SHOT") == "1") and max_rows_rs > max_rows
+        if two_shot is None:
+            two_shot = world >= 4 or os.environ.get("INFERA_TP_TWO_SHOT") == "1"
+        self.two_shot = two_shot and max_rows_rs > max_rows
         self.x_round = [0, 0]
         self.nccl = nccl_group
         self.gloo = gloo_group
