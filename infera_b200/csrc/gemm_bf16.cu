@@ -268,6 +268,7 @@ template <bool FP8>
 __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                 const Params p) {
+  constexpr int kBK = FP8 ? BK_FP8 : BK;          // K elements per stage (128 bytes per row)
   constexpr int kAccCols = FP8 ? MAX_BN_FP8 : MAX_BN;
   constexpr int kStages = FP8 ? STAGES_FP8 : STAGES;
   constexpr int kQStage = FP8 ? Q_STAGE_FP8 : Q_STAGE;
@@ -338,9 +339,8 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
             break;
           }
           mbar_expect_tx(&full[stage], tx);
-          // 32 TMA words (128 bytes) per row and stage
-          tma_load_2d(sP + stage * P_STAGE, &tmP, &full[stage], kb * 32, tile_prow(p, t, pt), polP);
-          tma_load_2d(sQ + stage * kQStage, &tmQ, &full[stage], kb * 32, tile_qrow(p, t, qt), polQ);
+          tma_load_2d(sP + stage * P_STAGE, &tmP, &full[stage], kb * kBK, tile_prow(p, t, pt), polP);
+          tma_load_2d(sQ + stage * kQStage, &tmQ, &full[stage], kb * kBK, tile_qrow(p, t, qt), polQ);
           gstamp(p, TRG_TMA, issued);
           ++issued;
           if (++stage == kStages) {
@@ -756,13 +756,11 @@ inline bool encode_pq(const Operands& o, const Params& p, const void* A, const v
   const long long Qrows = p.swap ? p.M : w_rows;
   const int Pld = p.swap ? ldw : lda;
   const int Qld = p.swap ? lda : ldw;
-  // TMA sees both operand types as 32-bit words (2 bf16 / 4 e4m3 each): the
-  // same bytes and 128-byte swizzle, fewer elements per box (measured: an
-  // 8-bit description of the e4m3 tiles took about twice as long per stage
-  // as the 16-bit bf16 one)
-  const int per = o.fp8 ? 4 : 2;  // operand elements per 32-bit word
-  return cached_tmap_2d(tmP, Pbase, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, Prows, p.K / per, Pld / per, BM, 32) &&
-         cached_tmap_2d(tmQ, Qbase, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, Qrows, p.K / per, Qld / per, p.bn, 32);
+  if (o.fp8)
+    return cached_tmap_2d(tmP, Pbase, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Prows, p.K, Pld, BM, BK_FP8) &&
+           cached_tmap_2d(tmQ, Qbase, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Qrows, p.K, Qld, p.bn, BK_FP8);
+  return cached_tmap_2d(tmP, Pbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Prows, p.K, Pld, BM, BK) &&
+         cached_tmap_2d(tmQ, Qbase, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Qrows, p.K, Qld, p.bn, BK);
 }
 
 inline int launch(const Operands& o, const CUtensorMap& tmP, const CUtensorMap& tmQ, const Params& p, int grid,
