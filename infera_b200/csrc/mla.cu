@@ -26,12 +26,12 @@
 //               memory (K-major, 64-byte swizzle, double buffered so P of
 //               tile j is written while tile j-1's is read), final O / l
 //               epilogue or split partials with their log-sum-exp
-// TMEM (512 columns): Q 288, S 2 x 32, O 128. The quarter split is what
-// lets Q live in TMEM; all four quarters recompute S, but with Q in TMEM an
-// S MMA moves only its 32 key rows from shared memory. With Q in shared
-// memory instead, every MMA re-read a 128-row slice of Q and the S MMAs
-// were bound by that traffic (about 65 cycles per 128 x 16 x 16 MMA,
-// measured with the kernel's event stamps).
+// TMEM (512 columns): Q 288, S 3 x 32, O 128. The quarter split is what
+// lets Q live in TMEM (all four quarters recompute S). The 36 k-steps of S
+// are spread round-robin over three independent accumulators that the
+// softmax adds: a chain of small MMAs into ONE accumulator waits on each
+// previous result, about 63 cycles per 128 x 32 x 16 step whether A came
+// from shared memory or TMEM (measured with the kernel's event stamps).
 // Prefill reuses the kernel with one "query" per prompt token (its own
 // causal key count).
 //
@@ -56,7 +56,8 @@ constexpr int P_BYTES = 128 * BT * 2;      // 8 KiB per P buffer (two buffers)
 constexpr int DV = 128;                    // value dims per CTA
 constexpr int NQUART = DL / DV;            // 4 CTAs per (query, split)
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t Q_COL = 0, S_COL0 = 288, S_COL1 = 320, O_COL = 384;
+constexpr uint32_t Q_COL = 0, S_COL = 288, O_COL = 384;  // S: 3 partial accumulators of 32 columns
+constexpr int S_PARTS = 3;
 constexpr int SMEM_BYTES = 1024 + STAGES * KV_STAGE + 2 * P_BYTES + 256;
 
 struct Params {
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* q_ready = bars;              // Q in TMEM (128 arrivals)
   uint64_t* kv_full = bars + 1;          // [STAGES]
   uint64_t* kv_empty = kv_full + STAGES; // [STAGES]
-  uint64_t* s_full = kv_empty + STAGES;  // [2]
+  uint64_t* s_full = kv_empty + STAGES;  // [2]: S of the tile computed / read by the softmax (s_full[1] = s_free)
   // [2] each: P buffer written (128 arrivals) / PV done, for even and odd
   // tiles. One barrier per buffer: a warp may run a tile ahead of the
   // others (writing the other buffer), and its arrival must not count
@@ -152,7 +153,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&kv_empty[s], 1);
     }
     mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 1);
+    mbar_init(&s_full[1], 128);
     mbar_init(&p_full[0], 128);
     mbar_init(&p_full[1], 128);
     mbar_init(&o_done[0], 1);
@@ -240,18 +241,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         stamp(p, cta0, TR_KVFULL, j);
+        // the single S area: the softmax must have read tile j-1's S
+        if (j > 0 && !mbar_wait(&s_full[1], static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status,
+                                kStatusTimeoutTmemEmpty)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sKV + st * KV_STAGE);
-        const uint32_t s_col = (j & 1) ? S_COL1 : S_COL0;
-        for (int c = 0; c < NCH; ++c) {
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            // Q block c, k-step kk: 16 dims = 8 TMEM columns
-            const uint64_t bd = make_sw128_desc(k_addr + c * KCH + kk * 32, 16, 1024);
-            umma_bf16_ts(tmem + s_col, tmem + Q_COL + c * 32 + kk * 8, bd, idesc_qk, (c > 0 || kk > 0) ? 1u : 0u);
-          }
+#pragma unroll 4
+        for (int i = 0; i < NCH * 4; ++i) {
+          const int c = i >> 2, kk = i & 3;
+          // Q block c, k-step kk: 16 dims = 8 TMEM columns; partial i % 3
+          const uint64_t bd = make_sw128_desc(k_addr + c * KCH + kk * 32, 16, 1024);
+          umma_bf16_ts(tmem + S_COL + (i % S_PARTS) * 32, tmem + Q_COL + c * 32 + kk * 8, bd, idesc_qk,
+                       i >= S_PARTS ? 1u : 0u);
         }
-        umma_commit(&s_full[j & 1]);
+        umma_commit(&s_full[0]);
         stamp(p, cta0, TR_SISSUE, j);
         if (j > 0 && !issue_pv(j - 1)) {
           ok = false;
@@ -292,7 +298,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles && ok; ++j) {
-      if (!mbar_wait_warp(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status,
+      if (!mbar_wait_warp(&s_full[0], static_cast<uint32_t>(j & 1), abort_flag, p.status,
                           kStatusTimeoutTmemFull)) {
         ok = false;
         break;
@@ -300,8 +306,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (r == 0) stamp(p, cta0, TR_SFULL, j);
       tc_fence_after();
       uint32_t v[32];
-      tmem_ld32(lane_addr + ((j & 1) ? S_COL1 : S_COL0), v);
-      tmem_ld_wait();
+      {
+        uint32_t v1[32], v2[32];
+        tmem_ld32(lane_addr + S_COL, v);
+        tmem_ld32(lane_addr + S_COL + 32, v1);
+        tmem_ld32(lane_addr + S_COL + 64, v2);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          v[i] = __float_as_uint(__uint_as_float(v[i]) + __uint_as_float(v1[i]) + __uint_as_float(v2[i]));
+      }
+      tc_fence_before();
+      mbar_arrive(&s_full[1]);  // S area free for the next tile
       const int lim = kvlen - (tile0 + j) * BT;  // keys c < lim are valid
       float mx = -INFINITY;
 #pragma unroll
