@@ -9,29 +9,26 @@
 //   O[h]    = softmax_t(S[h, :] * scale) . cache[:, 0:512]
 //
 // One CTA handles one query (128 head rows; fewer heads leave the rest of
-// the tile unused), one 128-dim quarter of the value dims and one split of
-// the keys:
-//   warps 2..5  first load the query's 128 x 576 rows into TMEM (thread =
-//               head row = TMEM lane, two bf16 per column: 288 columns), so
-//               S = Q K^T reads Q from TMEM (tcgen05.mma with A in TMEM) and
-//               shared memory only feeds the key tiles
-//   warp 0      TMA producer: key tiles of 32 tokens (2 pages x 9 blocks of
-//               64 dims) into a 4-stage ring
-//   warp 1      MMA issuer: S = Q K^T (M 128, N 32, K 576) into TMEM (double
-//               buffered); O += P V (M 128, N 128, K 32) with V = the tile's
-//               latent dims of this CTA's quarter, read MN-major from the
-//               same ring stage
+// the tile unused), one 256-dim half of the value dims and one split of the
+// keys:
+//   warp 0      TMA producer: the query's 9 x [128 x 64] blocks once, then
+//               key tiles of one page (16 tokens x 9 blocks of 64 dims) into
+//               a 4-stage ring
+//   warp 1      MMA issuer: S = Q K^T (M 128, N 16, K 576) into TMEM (double
+//               buffered); O += P V (M 128, N 256, K 16) with V = the tile's
+//               latent dims of this CTA's half, read MN-major from the same
+//               ring stage
 //   warps 2..5  softmax, thread = head row: running max with lazy O rescale
 //               (only when the max grows by more than 2^8), P to shared
-//               memory (K-major, 64-byte swizzle, double buffered so P of
-//               tile j is written while tile j-1's is read), final O / l
+//               memory (K-major, 64-byte swizzle; even tiles in the first 16
+//               columns, odd tiles in the last 16, so P of tile j is written
+//               while tile j-1's P is still being read), final O / l
 //               epilogue or split partials with their log-sum-exp
-// TMEM (512 columns): Q 288, S 3 x 32, O 128. The quarter split is what
-// lets Q live in TMEM (all four quarters recompute S). The 36 k-steps of S
-// are spread round-robin over three independent accumulators that the
-// softmax adds: a chain of small MMAs into ONE accumulator waits on each
-// previous result, about 63 cycles per 128 x 32 x 16 step whether A came
-// from shared memory or TMEM (measured with the kernel's event stamps).
+// Small page-sized tiles in a 4-deep ring keep more key bytes in flight
+// than a 2-deep ring of larger tiles in the same 72 KiB.
+// TMEM: S 2 x 16 columns, O 256 columns. The 128 x 512 fp32 output of all
+// heads would fill TMEM on its own, hence the value split over two CTAs (the
+// two recompute S; they read the same key tiles, which L2 serves once).
 // Prefill reuses the kernel with one "query" per prompt token (its own
 // causal key count).
 //
@@ -47,18 +44,17 @@ constexpr int DL = 512;
 constexpr int DR = 64;
 constexpr int DQK = DL + DR;
 constexpr int NCH = DQK / 64;              // 9 blocks of 64 dims
-constexpr int BT = 32;                     // keys per tile (two pages)
+constexpr int BT = 16;                     // keys per tile (one page)
 constexpr int PAGE = 16;
 constexpr int STAGES = 4;
-constexpr int KCH = BT * 128;              // one [32 keys x 64 dims] block
-constexpr int KV_STAGE = NCH * KCH;        // 36 KiB
-constexpr int P_BYTES = 128 * BT * 2;      // 8 KiB per P buffer (two buffers)
-constexpr int DV = 128;                    // value dims per CTA
-constexpr int NQUART = DL / DV;            // 4 CTAs per (query, split)
+constexpr int QCH = 128 * 128;             // one [128 rows x 64 dims] bf16 block
+constexpr int KCH = BT * 128;              // one [16 keys x 64 dims] block
+constexpr int KV_STAGE = NCH * KCH;        // 18 KiB
+constexpr int P_BYTES = 128 * 32 * 2;      // 8 KiB: two 16-key halves
+constexpr int DV = 256;                    // value dims per CTA
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t Q_COL = 0, S_COL = 288, O_COL = 384;  // S: 3 partial accumulators of 32 columns
-constexpr int S_PARTS = 3;
-constexpr int SMEM_BYTES = 1024 + STAGES * KV_STAGE + 2 * P_BYTES + 256;
+constexpr uint32_t S_COL0 = 0, S_COL1 = 16, O_COL = 64;
+constexpr int SMEM_BYTES = 1024 + NCH * QCH + STAGES * KV_STAGE + P_BYTES + 256;
 
 struct Params {
   const int* q_row;        // [nq] block-table row of each query
@@ -100,34 +96,23 @@ __device__ __forceinline__ uint32_t sw64_offset(int r, int c) {
   return static_cast<uint32_t>((r >> 3) * 512 + (r & 7) * 64 + ((c ^ ((r & 7) >> 1)) << 4));
 }
 
-// D (+)= A . B^T with A (M x 16, bf16, K-major) read from TMEM at a_tmem
-// (lane = row, two consecutive K elements per 32-bit column) and B from
-// shared memory.
-__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                             uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    mla_decode_kernel(const __nv_bfloat16* __restrict__ q, const __grid_constant__ CUtensorMap tmKV, const Params p) {
+    mla_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+                      const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sKV = smem;
-  uint8_t* sP = sKV + STAGES * KV_STAGE;  // [2] buffers of [128 x 32] bf16
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * P_BYTES);
-  uint64_t* q_ready = bars;              // Q in TMEM (128 arrivals)
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + NCH * QCH;
+  uint8_t* sP = sKV + STAGES * KV_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
+  uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;          // [STAGES]
   uint64_t* kv_empty = kv_full + STAGES; // [STAGES]
-  uint64_t* s_full = kv_empty + STAGES;  // [2]: S of the tile computed / read by the softmax (s_full[1] = s_free)
-  // [2] each: P buffer written (128 arrivals) / PV done, for even and odd
-  // tiles. One barrier per buffer: a warp may run a tile ahead of the
-  // others (writing the other buffer), and its arrival must not count
-  // toward the tile the slower warps are still writing.
+  uint64_t* s_full = kv_empty + STAGES;  // [2]
+  // [2] each: P half written (128 arrivals) / PV done, for even and odd
+  // tiles. One barrier per half: a warp may run a tile ahead of the others
+  // (writing the other half), and its arrival must not count toward the
+  // tile the slower warps are still writing.
   uint64_t* p_full = s_full + 2;
   uint64_t* o_done = p_full + 2;
   uint64_t* drain = o_done + 2;
@@ -137,7 +122,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int qi = blockIdx.x;
-  const int quarter = blockIdx.y;
+  const int half = blockIdx.y;
   const int sp = blockIdx.z;
   const int kvlen = p.q_kvlen[qi];
   const int n_tiles_all = (kvlen + BT - 1) / BT;
@@ -147,13 +132,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const bool cta0 = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_ready, 128);
+    mbar_init(q_full, 1);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
     mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 128);
+    mbar_init(&s_full[1], 1);
     mbar_init(&p_full[0], 128);
     mbar_init(&p_full[1], 128);
     mbar_init(&o_done[0], 1);
@@ -162,7 +147,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) tma_prefetch_desc(&tmKV);
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmKV);
+  }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -174,32 +162,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0 && n_tiles > 0) {
-      const uint64_t pol_kv = policy_evict_last();  // the other value quarters read the same tiles
+      const uint64_t pol_q = policy_evict_first();
+      const uint64_t pol_kv = policy_evict_last();  // the other value half reads the same tiles
+      mbar_expect_tx(q_full, NCH * QCH);
+      for (int c = 0; c < NCH; ++c) tma_load_2d(sQ + c * QCH, &tmQ, q_full, c * 64, qi * p.hq, pol_q);
       const int* bt = p.block_table + static_cast<size_t>(p.q_row[qi]) * p.max_pages;
-      const int n_pages = (kvlen + PAGE - 1) / PAGE;
       long long issued = 0;
-      int lp = tile0 * 2;
-      int nx0 = __ldg(bt + lp), nx1 = __ldg(bt + (lp + 1 < n_pages ? lp + 1 : lp));
+      int pg_next = __ldg(bt + tile0);
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % STAGES;
         const uint32_t ph = (j / STAGES) & 1;
-        const int pg0 = nx0, pg1 = nx1;
-        if (j + 1 < n_tiles) {  // next tile's pages, in flight while we wait
-          lp = (tile0 + j + 1) * 2;
-          nx0 = __ldg(bt + lp);
-          nx1 = __ldg(bt + (lp + 1 < n_pages ? lp + 1 : lp));
-        }
+        const int pg = pg_next;
+        if (j + 1 < n_tiles) pg_next = __ldg(bt + tile0 + j + 1);  // in flight while we wait
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
         uint8_t* base = sKV + st * KV_STAGE;
         mbar_expect_tx(&kv_full[st], KV_STAGE);
-        for (int c = 0; c < NCH; ++c) {
-          tma_load_2d(base + c * KCH, &tmKV, &kv_full[st], c * 64, pg0 * PAGE, pol_kv);
-          tma_load_2d(base + c * KCH + PAGE * 128, &tmKV, &kv_full[st], c * 64, pg1 * PAGE, pol_kv);
-        }
+        for (int c = 0; c < NCH; ++c) tma_load_2d(base + c * KCH, &tmKV, &kv_full[st], c * 64, pg * PAGE, pol_kv);
         stamp(p, cta0, TR_TMA, j);
         ++issued;
       }
       // drain: every issued copy must land before the CTA exits
+      mbar_wait(q_full, 0, nullptr, nullptr, 0, kWaitLimitNs / 4);
       const long long first = issued > STAGES ? issued - STAGES : 0;
       for (long long i = first; i < issued; ++i)
         mbar_wait(&kv_full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1), nullptr, nullptr, 0,
@@ -209,9 +192,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0 && n_tiles > 0) {
       const uint32_t idesc_qk = make_idesc_bf16(128, BT);
       const uint32_t idesc_pv = make_idesc_bf16(128, DV, true);
+      const uint32_t q_addr = smem_u32(sQ);
       const uint32_t p_addr = smem_u32(sP);
-      bool ok = mbar_wait(q_ready, 0, abort_flag, p.status, kStatusTimeoutFull);
-      tc_fence_after();
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kStatusTimeoutFull);
       auto issue_pv = [&](int jj) -> bool {
         if (!mbar_wait(&p_full[jj & 1], static_cast<uint32_t>((jj >> 1) & 1), abort_flag, p.status,
                        kStatusTimeoutTmemEmpty))
@@ -219,16 +202,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         stamp(p, cta0, TR_PFULL, jj);
         tc_fence_after();
         const int st = jj % STAGES;
-        // V = latent dims [128*quarter, +128) of the tile: blocks 2*quarter, 2*quarter+1
-        const uint32_t v_addr = smem_u32(sKV + st * KV_STAGE + quarter * 2 * KCH);
-        const uint32_t pb = p_addr + (jj & 1) * P_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BT / 16; ++kk) {
-          const uint64_t ad = make_sw64_desc(pb + kk * 32, 512);
-          // MN-major V: LBO = distance between 64-dim blocks, SBO = 8 keys
-          const uint64_t bd = make_sw128_desc(v_addr + kk * 2048, KCH, 1024);
-          umma_bf16(tmem + O_COL, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-        }
+        // V = latent dims [256*half, +256) of the tile: blocks 4*half .. 4*half+3;
+        // P of this tile = columns [16*(jj&1), +16) of the P buffer
+        const uint32_t v_addr = smem_u32(sKV + st * KV_STAGE + half * 4 * KCH);
+        const uint64_t ad = make_sw64_desc(p_addr + (jj & 1) * 32, 512);
+        // MN-major V: LBO = distance between 64-dim blocks, SBO = 8 keys
+        const uint64_t bd = make_sw128_desc(v_addr, KCH, 1024);
+        umma_bf16(tmem + O_COL, ad, bd, idesc_pv, jj > 0 ? 1u : 0u);
         umma_commit(&o_done[jj & 1]);
         umma_commit(&kv_empty[st]);
         return true;
@@ -241,23 +221,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         stamp(p, cta0, TR_KVFULL, j);
-        // the single S area: the softmax must have read tile j-1's S
-        if (j > 0 && !mbar_wait(&s_full[1], static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status,
-                                kStatusTimeoutTmemEmpty)) {
-          ok = false;
-          break;
-        }
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sKV + st * KV_STAGE);
-#pragma unroll 4
-        for (int i = 0; i < NCH * 4; ++i) {
-          const int c = i >> 2, kk = i & 3;
-          // Q block c, k-step kk: 16 dims = 8 TMEM columns; partial i % 3
-          const uint64_t bd = make_sw128_desc(k_addr + c * KCH + kk * 32, 16, 1024);
-          umma_bf16_ts(tmem + S_COL + (i % S_PARTS) * 32, tmem + Q_COL + c * 32 + kk * 8, bd, idesc_qk,
-                       i >= S_PARTS ? 1u : 0u);
+        const uint32_t s_col = (j & 1) ? S_COL1 : S_COL0;
+        for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = make_sw128_desc(q_addr + c * QCH + kk * 32, 16, 1024);
+            const uint64_t bd = make_sw128_desc(k_addr + c * KCH + kk * 32, 16, 1024);
+            umma_bf16(tmem + s_col, ad, bd, idesc_qk, (c > 0 || kk > 0) ? 1u : 0u);
+          }
         }
-        umma_commit(&s_full[0]);
+        umma_commit(&s_full[j & 1]);
         stamp(p, cta0, TR_SISSUE, j);
         if (j > 0 && !issue_pv(j - 1)) {
           ok = false;
@@ -272,56 +247,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;  // head row
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
-    const bool write = r < p.hq;
-    // Q rows into TMEM: 9 blocks of 64 dims = 32 columns each (rows beyond
-    // the query's heads are zero)
-    if (n_tiles > 0) {
-      const uint4* qrow = reinterpret_cast<const uint4*>(q + (static_cast<size_t>(qi) * p.hq + r) * DQK);
-#pragma unroll 1
-      for (int c = 0; c < NCH; ++c) {
-        uint32_t v[32];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint4 w = write ? __ldg(qrow + c * 8 + i) : make_uint4(0u, 0u, 0u, 0u);
-          v[4 * i] = w.x;
-          v[4 * i + 1] = w.y;
-          v[4 * i + 2] = w.z;
-          v[4 * i + 3] = w.w;
-        }
-        tmem_st32(lane_addr + Q_COL + c * 32, v);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(q_ready);
-    }
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles && ok; ++j) {
-      if (!mbar_wait_warp(&s_full[0], static_cast<uint32_t>(j & 1), abort_flag, p.status,
+      if (!mbar_wait_warp(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status,
                           kStatusTimeoutTmemFull)) {
         ok = false;
         break;
       }
       if (r == 0) stamp(p, cta0, TR_SFULL, j);
       tc_fence_after();
-      uint32_t v[32];
-      {
-        uint32_t v1[32], v2[32];
-        tmem_ld32(lane_addr + S_COL, v);
-        tmem_ld32(lane_addr + S_COL + 32, v1);
-        tmem_ld32(lane_addr + S_COL + 64, v2);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          v[i] = __float_as_uint(__uint_as_float(v[i]) + __uint_as_float(v1[i]) + __uint_as_float(v2[i]));
-      }
-      tc_fence_before();
-      mbar_arrive(&s_full[1]);  // S area free for the next tile
+      uint32_t v[16];
+      tmem_ld16(lane_addr + ((j & 1) ? S_COL1 : S_COL0), v);
+      tmem_ld_wait();
       const int lim = kvlen - (tile0 + j) * BT;  // keys c < lim are valid
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         if (i >= lim) v[i] = __float_as_uint(-INFINITY);
         mx = fmaxf(mx, __uint_as_float(v[i]));
       }
@@ -331,7 +274,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float m_use = rescale ? m_new : m_run;
       const float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
       const bool warp_rescale = __any_sync(0xffffffffu, rescale && j > 0);
-      // this P buffer was last read by tile j-2's PV; a rescale of O needs
+      // this P half was last read by tile j-2's PV; a rescale of O needs
       // every PV so far (tile j-1's, which completes after j-2's) done
       const int wait_tile = warp_rescale ? j - 1 : j - 2;
       if (wait_tile >= 0) {
@@ -356,19 +299,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_st_wait();
       }
       float sum = 0.f;
-      uint32_t pk[16];
+      uint32_t pk[8];
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
+      for (int i = 0; i < 16; i += 2) {
         const float e0 = exp2f(fmaf(__uint_as_float(v[i]), p.scale_log2, -m_use));
         const float e1 = exp2f(fmaf(__uint_as_float(v[i + 1]), p.scale_log2, -m_use));
         __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
         sum += __low2float(bb) + __high2float(bb);
         pk[i / 2] = *reinterpret_cast<uint32_t*>(&bb);
       }
-      uint8_t* pbuf = sP + (j & 1) * P_BYTES;
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<uint4*>(pbuf + sw64_offset(r, c)) =
+      for (int c = 0; c < 2; ++c)
+        *reinterpret_cast<uint4*>(sP + sw64_offset(r, 2 * (j & 1) + c)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       l_run = l_run * alpha + sum;
       m_run = m_use;
@@ -378,8 +320,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (r == 0) stamp(p, cta0, TR_PARRIVE, j);
     }
     ok = __all_sync(0xffffffffu, ok);
+    const bool write = r < p.hq;
     const size_t row = static_cast<size_t>(qi) * p.hq + r;
-    const int dv0 = quarter * DV;
+    const int dv0 = half * DV;
     if (n_tiles == 0) {
       // no keys in this split: an empty partial (or zeros)
       if (write) {
@@ -388,7 +331,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         } else {
           const size_t prow = (static_cast<size_t>(qi) * p.splits + sp) * p.hq + r;
           for (int c = 0; c < DV; ++c) p.o_part[prow * DL + dv0 + c] = 0.f;
-          if (quarter == 0) p.lse_part[prow] = -INFINITY;
+          if (half == 0) p.lse_part[prow] = -INFINITY;
         }
       }
     } else if (ok && mbar_wait_warp(&o_done[(n_tiles - 1) & 1], static_cast<uint32_t>(((n_tiles - 1) >> 1) & 1),
@@ -422,7 +365,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                             __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
         }
       }
-      if (write && p.splits > 1 && quarter == 0) p.lse_part[prow] = m_run + log2f(l_run);
+      if (write && p.splits > 1 && half == 0) p.lse_part[prow] = m_run + log2f(l_run);
     }
   }
 
@@ -543,7 +486,10 @@ extern "C" int ib_mla_decode(const void* q, int nq, int hq, const void* cache, l
   using namespace ib200::mla;
   if (nq <= 0) return 0;
   if (hq < 1 || hq > 128 || splits < 1 || (splits > 1 && (o_part == nullptr || lse_part == nullptr))) return -1;
-  CUtensorMap tkv;
+  CUtensorMap tq, tkv;
+  if (!cached_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<long long>(nq) * hq, DQK, DQK, 128,
+                      64))
+    return -2;
   if (!cached_tmap_2d(&tkv, cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, DQK, DQK, PAGE, 64)) return -2;
   Params p;
   p.q_row = q_row;
@@ -565,8 +511,8 @@ extern "C" int ib_mla_decode(const void* q, int nq, int hq, const void* cache, l
     cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     attr_set[dev] = true;
   }
-  dim3 grid(nq, NQUART, splits);
-  mla_decode_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(static_cast<const __nv_bfloat16*>(q), tkv, p);
+  dim3 grid(nq, 2, splits);
+  mla_decode_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tq, tkv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return static_cast<int>(e);
   if (splits > 1) {

@@ -26,10 +26,10 @@ PAGE = 16
 
 
 def mla_splits(nq: int, max_kvlen: int, num_sms: int = 148) -> int:
-    """Key splits per query: enough CTAs (nq x 4 value quarters x splits) to
+    """Key splits per query: enough CTAs (nq x 2 value halves x splits) to
     cover the SMs, each split keeping at least 4 tiles of 32 keys."""
     tiles = max(1, -(-max_kvlen // 32))
-    want = max(1, -(-num_sms // (4 * max(nq, 1))))
+    want = max(1, -(-num_sms // (2 * max(nq, 1))))
     return max(1, min(want, tiles // 4 if tiles >= 8 else 1, 64))
 
 
