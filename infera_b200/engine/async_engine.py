@@ -180,12 +180,14 @@ class AsyncEngine:
             acts.append(torch.profiler.ProfilerActivity.CUDA)
         self.profiler = torch.profiler.profile(activities=acts, record_shapes=False)
         self.profiler.__enter__()
+        self.engine.trace_phases = True
         return {"status": "started"}
 
     async def stop_profile(self) -> dict:
         if self.profiler is None:
             return {"error": "not profiling"}
         p, self.profiler = self.profiler, None
+        self.engine.trace_phases = False
         p.__exit__(None, None, None)
         path = f"/tmp/infera_b200_profile_{int(time.time())}.json"
         try:

@@ -150,11 +150,13 @@ class EngineCoreServer:
                 acts.append(torch.profiler.ProfilerActivity.CUDA)
             self._profiler = torch.profiler.profile(activities=acts, record_shapes=False)
             self._profiler.__enter__()
+            eng.trace_phases = True
             return {"status": "started"}
         if name == "profile_stop":
             if self._profiler is None:
                 return {"error": "not profiling"}
             p, self._profiler = self._profiler, None
+            eng.trace_phases = False
             p.__exit__(None, None, None)
             path = (args or {}).get("path") or f"/tmp/infera_b200_profile_{int(time.time())}.json"
             p.export_chrome_trace(path)

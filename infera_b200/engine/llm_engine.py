@@ -8,6 +8,8 @@ runs it on a dedicated thread for the HTTP server.
 
 from __future__ import annotations
 
+import contextlib
+
 import time
 from dataclasses import dataclass, field
 from typing import Callable
@@ -62,6 +64,27 @@ class EngineConfig:
     kv_push_endpoint: str | None = None
     # PD prefill: push each layer's KV pages inside the prompt's last forward
     pd_layerwise: bool = True
+
+
+class _PhaseRange:
+    """One named range in the torch profiler's trace and in NVTX."""
+
+    def __init__(self, name: str, cuda: bool):
+        self.name, self.cuda = name, cuda
+        self.rf = None
+
+    def __enter__(self):
+        self.rf = torch.profiler.record_function(self.name)
+        self.rf.__enter__()
+        if self.cuda:
+            torch.cuda.nvtx.range_push(self.name)
+        return self
+
+    def __exit__(self, *exc):
+        if self.cuda:
+            torch.cuda.nvtx.range_pop()
+        self.rf.__exit__(*exc)
+        return False
 
 
 class LLMEngine:
@@ -125,6 +148,9 @@ class LLMEngine:
         self.num_steps = 0
         self.clock: Callable[[], float] = time.monotonic
         self.counters = {"prompt_tokens": 0, "generation_tokens": 0, "finished": 0, "preemptions": 0}
+        # named phase ranges (torch.profiler record_function + NVTX) while a
+        # profile is being taken: schedule / forward (prefill+decode counts) / kv push
+        self.trace_phases = False
 
     # ------------------------------------------------------------------ sizing
     def _derive_num_pages(self) -> int:
@@ -224,6 +250,11 @@ class LLMEngine:
                 r.pages_synced = len(pages)
         return idx, val
 
+    def _phase(self, name: str):
+        if not self.trace_phases:
+            return contextlib.nullcontext()
+        return _PhaseRange(name, self.device.type == "cuda")
+
     def step(self) -> list[RequestOutput]:
         # the CUDA current device is per host thread: a step driven from a
         # thread that never selected this engine's GPU would launch the
@@ -231,8 +262,10 @@ class LLMEngine:
         if self.device.type == "cuda" and torch.cuda.current_device() != self.device.index:
             torch.cuda.set_device(self.device)
         if self.pd_agent is not None or self.pd_rendezvous is not None:
-            self._pd_progress()
-        sched = self.scheduler.schedule()
+            with self._phase("kv_push"):
+                self._pd_progress()
+        with self._phase("schedule"):
+            sched = self.scheduler.schedule()
         outputs: list[RequestOutput] = []
         for r in sched.preempted:
             if r.status == Status.FINISHED_LENGTH:  # prompt longer than the model allows
@@ -257,7 +290,8 @@ class LLMEngine:
                 from infera_b200.engine.pd import LayerPush
 
                 layer_push = LayerPush(self, items)
-        res = self.runner.execute(sched, upd, layer_hook=layer_push)
+        with self._phase(f"forward prefill={len(sched.prefills)} decode={len(sched.decodes)}"):
+            res = self.runner.execute(sched, upd, layer_hook=layer_push)
         if layer_push is not None:
             layer_push.finish()
         now = self.clock()
