@@ -144,6 +144,26 @@ __global__ void __launch_bounds__(256) return_kernel(const uint4* __restrict__ y
   signal_all(done_ctr, pr, W);
 }
 
+// row_map[p] = (source rank << 27) | (row in the source's sorted rows) for
+// every received row p < loc_off[El] (the return_kernel's mapping, for a
+// GEMM epilogue that stores its outputs straight to the sources)
+__global__ void row_map_kernel(int rows, const int* __restrict__ C, int W, int E, int El, int rank,
+                               const int* __restrict__ loc_off, const int* __restrict__ src_off,
+                               int* __restrict__ row_map) {
+  const int nrows = min(rows, loc_off[El]);
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < nrows; p += gridDim.x * blockDim.x) {
+    const int el = find_bin(loc_off, El, p);
+    const int e = rank * El + el;
+    int rel = p - loc_off[el];
+    int s = 0;
+    while (s < W - 1 && rel >= C[s * E + e]) {
+      rel -= C[s * E + e];
+      ++s;
+    }
+    row_map[p] = (s << 27) | (src_off[s * E + e] + rel);
+  }
+}
+
 __global__ void wait_kernel(const unsigned int* flag, unsigned int target, int* status) {
   if (threadIdx.x != 0) return;
   const unsigned long long t0 = gtimer();
@@ -203,6 +223,15 @@ extern "C" int ib_ep_return(const void* y, int rows, int H, const int* C, int wo
 
 extern "C" int ib_ep_wait(const unsigned int* flag, unsigned int target, int* status, cudaStream_t stream) {
   wait_kernel<<<1, 32, 0, stream>>>(flag, target, status);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+extern "C" int ib_ep_row_map(const int* C, int W, int E, int rank, const int* loc_off, const int* src_off,
+                             int rows, int* row_map, cudaStream_t stream) {
+  if (W < 1 || W > kMaxRanks || E % W || rows <= 0) return rows <= 0 ? 0 : -1;
+  const int grid = (rows + 255) / 256 < 1024 ? (rows + 255) / 256 : 1024;
+  row_map_kernel<<<grid, 256, 0, stream>>>(rows, C, W, E, E / W, rank, loc_off, src_off, row_map);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }

@@ -87,6 +87,10 @@ struct Params {
   const int4* gtab;
   const int* gnum;
   int n_per_expert;         // weight rows per expert (the grouped GEMM's N)
+  // grouped push (expert-parallel return fused into the epilogue): output
+  // row m goes to rank row_map[m] >> 27, row row_map[m] & (2^27 - 1) of
+  // peer_out[rank]; then every rank's peer_flag is bumped once (push = 1)
+  const int* row_map;
   // fp8: UE8M0 scale bytes. sf_w [ceil(rows of W / 128), sf_w_ld] (one per
   // 128x128 weight block); sf_a [K / 128, sf_a_ld] (K-group-major, one per
   // token and 128-wide K group)
@@ -242,6 +246,16 @@ __device__ __forceinline__ void store_chunk_grouped(const Params& p, int t, int 
       const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
       if (even && n + 1 < p.n_per_expert && m0 + j < g.w)
         C[static_cast<size_t>(m0 + j) * p.ldc] = __float2bfloat16(silu(mine) * other);
+    }
+  } else if (p.row_map != nullptr) {
+    if (n >= p.n_per_expert) return;
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+      if (m0 + j < g.w) {
+        const int code = __ldg(p.row_map + m0 + j);
+        __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.peer_out[code >> 27]);
+        C[static_cast<size_t>(code & 0x7FFFFFF) * p.ldc + n] = __float2bfloat16(__uint_as_float(r[j]));
+      }
     }
   } else {
     if (n >= p.n_per_expert) return;
@@ -848,7 +862,9 @@ inline int run_push(const Operands& o, const void* A, const void* W, int M, int 
 
 inline int run_grouped(const Operands& o, const void* A, const void* W, void* out, int R, int N, int K, int E,
                        int lda, int ldw, int ldc, int epi, const int* gtab, const int* gnum, int bn, int grid_tiles,
-                       int* status, cudaStream_t stream) {
+                       int* status, cudaStream_t stream, const int* row_map = nullptr, int world = 1,
+                       void* const* peer_out = nullptr, unsigned int* const* peer_flag = nullptr,
+                       unsigned int* done_ctr = nullptr) {
   if (R <= 0 || N <= 0 || K <= 0 || E <= 0) return 0;
   if (!operands_ok(o, K, lda, ldw) || (N % BM) != 0) return -1;
   if (o.fp8 ? (bn < 32 || bn > MAX_BN_FP8 || (bn % 32) != 0) : (bn < 16 || bn > MAX_BN || (bn % 16) != 0))
@@ -873,6 +889,17 @@ inline int run_grouped(const Operands& o, const void* A, const void* W, void* ou
   p.gtab = reinterpret_cast<const int4*>(gtab);
   p.gnum = gnum;
   p.n_per_expert = N;
+  p.row_map = row_map;
+  if (row_map != nullptr) {
+    if (epi != EPI_BF16 || world < 1 || world > kMaxPeers || done_ctr == nullptr) return -1;
+    p.push = 1;
+    p.world = world;
+    for (int d = 0; d < kMaxPeers; ++d) {
+      p.peer_out[d] = d < world ? peer_out[d] : nullptr;
+      p.peer_flag[d] = d < world ? peer_flag[d] : nullptr;
+    }
+    p.done_ctr = done_ctr;
+  }
   set_scales(p, o);
   CUtensorMap tmP, tmQ;
   if (!encode_pq(o, p, A, W, static_cast<long long>(E) * N, lda, ldw, &tmP, &tmQ)) return -2;
@@ -965,6 +992,22 @@ extern "C" int ib_gemm_fp8_grouped(const void* A, const uint8_t* sf_a, int sf_a_
                                    int* status, cudaStream_t stream) {
   const gemm::Operands o{true, sf_a, sf_a_ld, sf_w};
   return gemm::run_grouped(o, A, W, out, R, N, K, E, lda, ldw, ldc, epi, gtab, gnum, bn, grid_tiles, status, stream);
+}
+
+// Grouped GEMM whose epilogue stores every output row m straight into a
+// peer's buffer: row_map[m] = (rank << 27) | row, peer_out[rank] bf16 with
+// row pitch ldc; after the whole GEMM, peer_flag[d] += 1 on every rank d
+// (done_ctr: a local zero-initialised counter). The expert-parallel return
+// of the MoE layer, fused into its down projection. fp8: sf_a / sf_w as in
+// ib_gemm_fp8_grouped (null for bf16).
+extern "C" int ib_gemm_grouped_push(const void* A, const uint8_t* sf_a, int sf_a_ld, const void* W,
+                                    const uint8_t* sf_w, int R, int N, int K, int E, int lda, int ldw, int ldc,
+                                    const int* gtab, const int* gnum, int bn, int grid_tiles, const int* row_map,
+                                    int world, void* const* peer_out, unsigned int* const* peer_flag,
+                                    unsigned int* done_ctr, int* status, cudaStream_t stream) {
+  const gemm::Operands o{sf_w != nullptr, sf_a, sf_a_ld, sf_w};
+  return gemm::run_grouped(o, A, W, nullptr, R, N, K, E, lda, ldw, ldc, gemm::EPI_BF16, gtab, gnum, bn, grid_tiles,
+                           status, stream, row_map, world, peer_out, peer_flag, done_ctr);
 }
 
 // Plan introspection for tests and benchmarks: writes

@@ -617,6 +617,17 @@ def grouped_bn(rows: int, E: int) -> int:
     return 256
 
 
+def grouped_tiles(offsets: torch.Tensor, E: int, N: int, bn: int, R: int) -> tuple[torch.Tensor, torch.Tensor, int]:
+    """Device tile table of a grouped GEMM (``ib_moe_tiles``): (table, count, capacity)."""
+    cap = (-(-R // bn) + E) * (N // 128)
+    tab = torch.empty(cap * 4 + 1, dtype=torch.int32, device=offsets.device)
+    num = tab[cap * 4:]
+    _native.check(_native.kernels().ib_moe_tiles(offsets.data_ptr(), E, N, bn, tab.data_ptr(), num.data_ptr(),
+                                                 _stream()), "ib_moe_tiles")
+    _count(1)
+    return tab, num, cap
+
+
 def gemm_grouped(xp: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor, swiglu: bool = False,
                  out: torch.Tensor | None = None, bn: int | None = None) -> torch.Tensor:
     """Rows of ``xp`` [R, K] sorted by expert (``offsets`` [E+1]) times their
@@ -642,18 +653,14 @@ def gemm_grouped(xp: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor, swigl
     if out is None:
         out = torch.empty(R, n_out, dtype=torch.bfloat16, device=xp.device)
     bn = bn or grouped_bn(R, E)
-    cap = (-(-R // bn) + E) * (N // 128)
-    tab = torch.empty(cap * 4 + 1, dtype=torch.int32, device=xp.device)
-    num = tab[cap * 4:]
+    tab, num, cap = grouped_tiles(offsets, E, N, bn, R)
     lib = _native.kernels()
-    _native.check(lib.ib_moe_tiles(offsets.data_ptr(), E, N, bn, tab.data_ptr(), num.data_ptr(), _stream()),
-                  "ib_moe_tiles")
     sc = scratch(xp.device)
     rc = lib.ib_gemm_grouped(xp.data_ptr(), w.data_ptr(), out.data_ptr(), R, N, Kd, E, xp.stride(0), w.stride(1),
                              out.stride(0), 1 if swiglu else 0, tab.data_ptr(), num.data_ptr(), bn, cap,
                              sc.status.data_ptr(), _stream())
     _native.check(rc, "ib_gemm_grouped")
-    _count(2)
+    _count(1)
     return out
 
 

@@ -21,8 +21,9 @@ Two data paths:
   KB) and the rows move with this framework's kernels over NVLink peer
   memory - ``ib_ep_dispatch`` stores each sorted row straight into its
   destination's receive buffer at its [local expert][source] place (no
-  regroup on the receiver), ``ib_ep_return`` stores each expert output
-  back at its source's sorted row; arrival counters with bounded waits
+  regroup on the receiver), and the down projection's epilogue
+  (``ib_gemm_grouped_push``) stores each expert-output row straight back
+  at its source's sorted row; arrival counters with bounded waits
   separate the phases, and nothing is read back to the host.
 
 Reference counterpart: the engines' EP MoE (vLLM / SGLang over their a2a
@@ -100,6 +101,7 @@ class EPMoE:
         W, E = self.world, self.E
         self.counts_all = torch.zeros(W * E, dtype=torch.int32, device=self.device)
         self.offs = torch.zeros(E + self.El + 1 + W * E, dtype=torch.int32, device=self.device)
+        self.row_map = torch.zeros(max_rows, dtype=torch.int32, device=self.device)
         dist.barrier(group=gloo_group)
 
     def _recv_view(self, base: int) -> int:
@@ -143,16 +145,36 @@ class EPMoE:
                                          recv_peers, flagA, ctypes.c_void_p(ctr), stream), "ib_ep_dispatch")
         _native.check(lib.ib_ep_wait(ctypes.c_void_p(self.base), target, sc.status.data_ptr(), stream), "ib_ep_wait")
         recv = self._tensor_at(self._recv_view(self.base), self.max_rows)
-        out_r = self._experts(recv, loc_off, K.grouped_bn(R, El))
+        # down projection whose epilogue stores each expert-output row straight
+        # into its source's return buffer (the return all-to-all fused in)
+        _native.check(lib.ib_ep_row_map(self.counts_all.data_ptr(), W, E, self.rank, loc_off.data_ptr(),
+                                        src_off.data_ptr(), self.max_rows, self.row_map.data_ptr(), stream),
+                      "ib_ep_row_map")
         ret_peers = (ctypes.c_void_p * 8)(*[self._ret_view(b) for b in self.peers])
         flagB = (ctypes.c_void_p * 8)(*[b + 4 for b in self.peers])
-        _native.check(lib.ib_ep_return(out_r.data_ptr(), self.max_rows, H, self.counts_all.data_ptr(), W, E,
-                                       self.rank, loc_off.data_ptr(), src_off.data_ptr(), ret_peers, flagB,
-                                       ctypes.c_void_p(ctr + 4), stream), "ib_ep_return")
+        bn = K.grouped_bn(R, El)
+        if self.fp8:
+            from infera_b200.ops import fp8
+
+            bn = min(192, max(32, ((bn + 31) // 32) * 32))
+            act = fp8.gemm_fp8_grouped(recv, self.w13, El, loc_off, swiglu=True, bn=bn)
+            a_q, a_sf = fp8.quant_act(act)
+            w2q, w2sf, sf_ld = self.w2.q, self.w2.sf.data_ptr(), a_sf.stride(0)
+            a_ptr, sfa_ptr, lda = a_q.data_ptr(), a_sf.data_ptr(), a_q.stride(0)
+        else:
+            act = K.gemm_grouped(recv, self.w13, loc_off, swiglu=True, bn=bn)
+            w2q, w2sf, sf_ld = self.w2, None, 0
+            a_ptr, sfa_ptr, lda = act.data_ptr(), None, act.stride(0)
+        tab, num, cap = K.grouped_tiles(loc_off, El, H, bn, self.max_rows)
+        _native.check(lib.ib_gemm_grouped_push(a_ptr, sfa_ptr, sf_ld, w2q.data_ptr(), w2sf, self.max_rows, H,
+                                               act.shape[1], El, lda, w2q.stride(-2), H, tab.data_ptr(),
+                                               num.data_ptr(), bn, cap, self.row_map.data_ptr(), W, ret_peers, flagB,
+                                               ctypes.c_void_p(ctr + 4), sc.status.data_ptr(), stream),
+                      "ib_gemm_grouped_push")
         _native.check(lib.ib_ep_wait(ctypes.c_void_p(self.base + 4), target, sc.status.data_ptr(), stream),
                       "ib_ep_wait")
         ret = self._tensor_at(self._ret_view(self.base), self.max_rows)
-        K._count(5)
+        K._count(6)
         self.stats["sent_rows"] += R
         y = K.moe_combine(ret, row_of_slot, wts)
         if self.shared is not None:
