@@ -421,7 +421,13 @@ def main(argv=None) -> None:
     p.add_argument("--tp-size", type=int, default=1, help="tensor-parallel ranks (RANK / LOCAL_RANK / MASTER_* from env)")
     p.add_argument("--disagg-mode", choices=("mixed", "prefill", "decode"), default="mixed")
     p.add_argument("--kv-push-endpoint", default=None)
+    p.add_argument("--dp-attention-size", type=int, default=1,
+                   help="data-parallel attention ranks sharing expert-parallel MoE layers (one core per rank; "
+                        "'{rank}' in --in / --out is replaced by the rank)")
+    p.add_argument("--ep-fused", action="store_true", help="NVLink peer-store expert all-to-all (GPUs)")
     a = p.parse_args(argv)
+    if a.dp_attention_size > 1:
+        return _main_dp(a)
     from infera_b200.engine.kv_events import KvEventPublisher
     from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
 
@@ -464,6 +470,70 @@ def main(argv=None) -> None:
     if pub is not None:
         pub.close()
     srv.close()
+
+
+def _main_dp(a) -> None:
+    """One data-parallel-attention rank (launched by torch.distributed.run)."""
+    import signal
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from infera_b200.engine.dp_attention import DPAttentionEngine, DPServed, EPSpec
+    from infera_b200.engine.kv_events import KvEventPublisher
+    from infera_b200.engine.llm_engine import EngineConfig
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(a.dp_attention_size)))
+    if world != a.dp_attention_size:
+        raise SystemExit(f"WORLD_SIZE={world} but --dp-attention-size {a.dp_attention_size}")
+    on_gpu = a.device.startswith("cuda")
+    if on_gpu:
+        device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", str(rank))))
+        torch.cuda.set_device(device)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+    else:
+        device = torch.device("cpu")
+        dist.init_process_group("gloo", timeout=timedelta(seconds=600))
+    gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=600))
+    events = a.kv_events_endpoint.format(rank=rank) if a.kv_events_endpoint else None
+    pub = KvEventPublisher(events) if events else None
+    cfg = EngineConfig(model=a.model, page_size=a.page_size, max_num_seqs=a.max_num_seqs,
+                       max_batched_tokens=a.max_batched_tokens, gpu_memory_utilization=a.gpu_memory_utilization,
+                       num_pages=a.num_pages, use_cuda_graphs=False, seed=a.seed)
+    dp = DPAttentionEngine(cfg, EPSpec(rank, world, group=None, gloo=gloo, fused=a.ep_fused and on_gpu),
+                           device=device)
+    if pub is not None:
+        dp.engine.set_event_sink(pub)
+    served = DPServed(dp)
+    srv = EngineCoreServer(served, a.in_addr.format(rank=rank), a.out_addr.format(rank=rank), publisher=pub,
+                           info={"vocab": dp.engine.model_cfg.vocab, "page_size": cfg.page_size,
+                                 "num_pages": dp.engine.bm.num_pages, "pid": os.getpid(), "dp_rank": rank,
+                                 "dp_size": world})
+    # SIGTERM ends the loop on the next vote of every rank: a rank that
+    # stopped alone would leave the others waiting in the collective
+    stop = [False]
+    signal.signal(signal.SIGTERM, lambda *_: stop.__setitem__(0, True))
+    srv.announce_ready()
+
+    def should_stop():
+        t = torch.tensor([1 if (stop[0] or srv._stop) else 0], dtype=torch.int32)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=gloo)
+        return bool(t.item())
+
+    # every pass: one lockstep step vote (inside run_once) and one stop vote
+    while True:
+        srv.run_once()
+        if should_stop():
+            break
+    for lw in dp.engine.model.w.layers:
+        if "moe" in lw and hasattr(lw["moe"], "close"):
+            lw["moe"].close()
+    if pub is not None:
+        pub.close()
+    srv.close()
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -83,3 +83,34 @@ class DPAttentionEngine:
                 self.engine.runner.idle_forward()
                 self.idle_forwards += 1
         return got
+
+
+class DPServed:
+    """A data-parallel-attention rank as the engine-core server sees it: the
+    server calls ``step`` every loop pass (``has_unfinished`` is always
+    true), and every call is one lockstep vote of all ranks, so ranks with
+    and without work stay in step. Everything else is this rank's engine."""
+
+    def __init__(self, dp: DPAttentionEngine, idle_sleep_s: float = 0.0005):
+        self.dp = dp
+        self.engine = dp.engine
+        self.idle_sleep_s = idle_sleep_s
+
+    def __getattr__(self, name):
+        return getattr(self.engine, name)
+
+    def has_unfinished(self) -> bool:
+        return True
+
+    def step(self):
+        import time
+
+        if not self.dp._any_rank(self.engine.has_unfinished()):
+            time.sleep(self.idle_sleep_s)
+            return []
+        n0 = self.engine.runner.forwards
+        outs = self.engine.step()
+        if self.engine.runner.forwards == n0:
+            self.engine.runner.idle_forward()
+            self.dp.idle_forwards += 1
+        return outs

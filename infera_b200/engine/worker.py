@@ -45,7 +45,8 @@ def build_payload(args, tokenizer) -> dict:
                                 snapshot_endpoint=f"http://{host}:{args.port}", tiers=["device"])
     w = WorkerInfo(worker_id=wid, url=f"http://{host}:{args.port}", model_name=args.served_model_name or args.model,
                    engine=EngineType.INFERA_B200, disagg_mode=DisaggMode(args.disagg_mode), disagg_meta=meta,
-                   kv_events_endpoint=args.kv_events_endpoint, kv_block_size=args.page_size, kv=kv)
+                   kv_events_endpoint=args.kv_events_endpoint, kv_block_size=args.page_size, kv=kv,
+                   dp_rank=args.dp_rank, dp_size=args.dp_size)
     return w.to_payload()
 
 
@@ -76,6 +77,9 @@ def parse_args(argv=None):
     p.add_argument("--kv-tier", default=None, help="host:<GiB>[:<nvme dir>] or kvd:<socket>")
     p.add_argument("--in-process", action="store_true", help="run the engine on a thread of this process")
     p.add_argument("--attach-core", default=None, help="IN,OUT ipc addresses of a running engine core")
+    p.add_argument("--dp-rank", type=int, default=None,
+                   help="data-parallel attention rank this worker serves (registered for DP-rank routing)")
+    p.add_argument("--dp-size", type=int, default=1)
     p.add_argument("--log-level", default="info")
     return p.parse_args(argv)
 
