@@ -264,6 +264,22 @@ class ModelRunner:
         return lay, v
 
     def _capture_all(self) -> None:
+        # Garbage from earlier engines in this process (graphs, exported
+        # caches) frees device memory when it is collected; a collection in
+        # the middle of a capture would put cudaFree into it and invalidate
+        # the capture. Collect now and keep the collector off until done.
+        import gc
+
+        gc.collect()
+        gc_on = gc.isenabled()
+        gc.disable()
+        try:
+            self._capture_all_sizes()
+        finally:
+            if gc_on:
+                gc.enable()
+
+    def _capture_all_sizes(self) -> None:
         maxB = self.graph_sizes[-1]
         self.g_in = torch.zeros(self._graph_layout(maxB)["_end"] + 16, dtype=torch.int32, device=self.dev)
         self.g_out = torch.zeros(maxB, dtype=torch.int32, device=self.dev)
