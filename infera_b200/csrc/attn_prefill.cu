@@ -51,7 +51,18 @@ struct Params {
   __nv_bfloat16* out;      // [T, num_heads * 128]
   int ldo;
   int* status;
+  long long* trace;        // optional: clock64 stamps of CTA (0,0)'s pipeline events (FTR_*)
 };
+
+// pipeline event stamps (trace[event * kFTraceTiles + tile]) for diagnosis
+enum : int { FTR_TMA = 0, FTR_KFULL, FTR_SISSUE, FTR_PVISSUE, FTR_SFULL, FTR_PAIR, FTR_SOFTMAX, FTR_PARRIVE,
+             kFTraceEvents };
+constexpr int kFTraceTiles = 64;
+
+__device__ __forceinline__ void fstamp(const Params& p, int ev, int j) {
+  if (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && j < kFTraceTiles)
+    p.trace[ev * kFTraceTiles + j] = clock64();
+}
 
 // 2^x on the FMA pipe: split x = n + f (n integer, f in [0,1)), evaluate a
 // cubic fitted to 2^f on [0,1) (max relative error 8.6e-5, far below bf16's
@@ -157,6 +168,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (j + 1 < n_kv) load_tile_pages(bt, j + 1, n_pages, nxt);  // in flight while we wait
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
         uint8_t* base = sKV + st * 4 * BLK;
+        fstamp(p, FTR_TMA, j);
         mbar_expect_tx(&k_full[st], 2 * BLK);
 #pragma unroll
         for (int pg = 0; pg < BKV / PAGE; ++pg) {
@@ -209,6 +221,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           umma_bf16(tmem + O_COL, ad, bd, idesc_pv, (jj > 0 || s > 0) ? 1u : 0u);
         }
         umma_commit(o_done);
+        fstamp(p, FTR_PVISSUE, jj);
         umma_commit(&kv_empty[st]);
         return true;
       };
@@ -219,6 +232,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ok = false;
           break;
         }
+        fstamp(p, FTR_KFULL, j);
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sKV + st * 4 * BLK);
         const uint32_t s_col = (j & 1) ? S_COL1 : S_COL0;
@@ -230,6 +244,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           umma_bf16(tmem + s_col, ad, bd, idesc_qk, s > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[j & 1]);
+        fstamp(p, FTR_SISSUE, j);
         if (j > 0 && !issue_pv(j - 1)) {
           ok = false;
           break;
@@ -258,12 +273,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ok = mbar_wait_warp(&pair[q4], pph & 1u, abort_flag, p.status, kStatusTimeoutTmemFull) && ok;
       ++pph;
     };
+    const bool tr0 = half == 0 && r == 0;  // one softmax thread stamps
     for (int j = 0; j < n_kv && ok; ++j) {
       if (!mbar_wait_warp(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status,
                           kStatusTimeoutTmemFull)) {
         ok = false;
         break;
       }
+      if (tr0) fstamp(p, FTR_SFULL, j);
       tc_fence_after();
       const uint32_t s_addr = lane_addr + ((j & 1) ? S_COL1 : S_COL0) + cb;
       const int kbase = j * BKV;
@@ -289,6 +306,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // combine the two halves' maxima of each row (double-buffered by tile)
       red[((j & 1) * 2 + half) * BQ + r] = mx;
       pair_sync();
+      if (tr0) fstamp(p, FTR_PAIR, j);
       if (!ok) break;
       mx = fmaxf(red[((j & 1) * 2) * BQ + r], red[((j & 1) * 2 + 1) * BQ + r]) * p.scale_log2;
       const float m_new = fmaxf(m_run, mx);
@@ -339,11 +357,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint4 w = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         *reinterpret_cast<uint4*>(blk + sw128_offset(r, q)) = w;
       }
+      if (tr0) fstamp(p, FTR_SOFTMAX, j);
       l_run = l_run * alpha + sum;
       m_run = m_use;
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
+      if (tr0) fstamp(p, FTR_PARRIVE, j);
     }
     ok = __all_sync(0xffffffffu, ok);
     // row sums: add the two halves' shares
@@ -392,6 +412,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 using namespace ib200;
 
+static long long* g_fa_trace = nullptr;
+
+// Diagnostics: the next launches stamp CTA (0,0)'s pipeline events into
+// trace[8 * 64] (clock64), or stop when trace is null.
+extern "C" void ib_attn_prefill_set_trace(long long* trace) { g_fa_trace = trace; }
+
 // q: [T, ldq] bf16 with head h at columns [h*128, h*128+128).
 // k_cache / v_cache: [num_slots, num_kv_heads*128] bf16.
 // tiles: device int32 [num_tiles, 2] (seq, q_block), longest first.
@@ -423,6 +449,7 @@ extern "C" int ib_attn_prefill(const void* q, int T, int ldq, const void* k_cach
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = ldo;
   p.status = status;
+  p.trace = g_fa_trace;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);

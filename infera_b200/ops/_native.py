@@ -94,6 +94,7 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_gemm_grouped_push": [c_vp, c_vp, c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                  c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp],
         "ib_gemm_set_trace": [c_vp],
+        "ib_attn_prefill_set_trace": [c_vp],
         "ib_mla_rope_kvwrite": [c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_float, c_vp, c_vp],
     }
     for name, args in sig.items():
@@ -102,7 +103,7 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
             continue
         fn.argtypes = args
         fn.restype = None if name in ("ib_gemm_bf16_plan", "ib_gemm_fp8_plan", "ib_mla_set_trace",
-                                        "ib_gemm_set_trace") else c_int
+                                        "ib_gemm_set_trace", "ib_attn_prefill_set_trace") else c_int
 
 
 def kernels() -> ctypes.CDLL:
