@@ -1,7 +1,9 @@
 // KV page gather / scatter between the paged cache and a contiguous chunk.
 //
 // Chunk layout (KV chunk blob v2 payload): [C, L, T, H] with C = 2 (K, V),
-// L layers, T = n_pages * 16 tokens, H = kv elements per token.
+// or C = 1 for a latent (MLA) cache, whose one row per token holds the
+// compressed KV and the rope key; L layers, T = n_pages * 16 tokens, H = kv
+// elements per token.
 // Cache layout: per channel [L, num_slots, H] (slot = page * 16 + offset), so
 // one page of one layer is 16 * H contiguous elements: each CTA moves one
 // (page, layer, channel) block with 16-byte vector accesses.
@@ -39,13 +41,15 @@ __global__ void page_copy_kernel(uint4* __restrict__ k_cache, uint4* __restrict_
 }  // namespace kvp
 }  // namespace ib200
 
-// k_cache / v_cache: [L, slots, H] of elem_bytes elements; chunk: [2, L, n_pages*16, H].
+// k_cache / v_cache: [L, slots, H] of elem_bytes elements (v_cache unused when
+// channels == 1); chunk: [channels, L, n_pages*16, H].
 // H * elem_bytes must be a multiple of 16.
 extern "C" int ib_kv_page_copy(void* k_cache, void* v_cache, void* chunk, const int* pages, int n_pages, int L,
-                               long long slots_per_layer, int H, int elem_bytes, int dir, cudaStream_t stream) {
+                               long long slots_per_layer, int H, int elem_bytes, int channels, int dir,
+                               cudaStream_t stream) {
   if (n_pages <= 0) return 0;
-  if ((H * elem_bytes) % 16 != 0 || (dir != 0 && dir != 1)) return -1;
-  dim3 grid(n_pages, L, 2);
+  if ((H * elem_bytes) % 16 != 0 || (dir != 0 && dir != 1) || (channels != 1 && channels != 2)) return -1;
+  dim3 grid(n_pages, L, channels);
   ib200::kvp::page_copy_kernel<<<grid, 256, 0, stream>>>(
       static_cast<uint4*>(k_cache), static_cast<uint4*>(v_cache), static_cast<uint4*>(chunk), pages, n_pages, L,
       slots_per_layer, H * elem_bytes / 16, dir);
@@ -63,7 +67,7 @@ extern "C" int ib_kv_page_copy(void* k_cache, void* v_cache, void* chunk, const 
 // src_c[l, src_pages[p]*16 + i, :]. One CTA per (page, layer, channel);
 // 16-byte loads from local HBM, 16-byte stores over NVLink (plain peer
 // stores, no multicast). Called per layer as the prefill finishes it, or once
-// for the whole range.
+// for the whole range; channels = 1 pushes a latent cache (src_k / dst_k only).
 namespace ib200 {
 namespace kvp {
 
@@ -101,10 +105,10 @@ __global__ void __launch_bounds__(256) kv_push_kernel(const uint4* __restrict__ 
 // arrays of n_pages each. Layers [l0, l1). H * elem_bytes % 16 == 0.
 extern "C" int ib_kv_push_pages(const void* src_k, const void* src_v, void* dst_k, void* dst_v, const int* src_pages,
                                 const int* dst_pages, int n_pages, int l0, int l1, long long src_slots,
-                                long long dst_slots, int H, int elem_bytes, cudaStream_t stream) {
+                                long long dst_slots, int H, int elem_bytes, int channels, cudaStream_t stream) {
   if (n_pages <= 0 || l1 <= l0) return 0;
-  if ((H * elem_bytes) % 16 != 0) return -1;
-  dim3 grid(n_pages, l1 - l0, 2);
+  if ((H * elem_bytes) % 16 != 0 || (channels != 1 && channels != 2)) return -1;
+  dim3 grid(n_pages, l1 - l0, channels);
   ib200::kvp::kv_push_kernel<<<grid, 256, 0, stream>>>(
       static_cast<const uint4*>(src_k), static_cast<const uint4*>(src_v), static_cast<uint4*>(dst_k),
       static_cast<uint4*>(dst_v), src_pages, dst_pages, l0, src_slots, dst_slots, H * elem_bytes / 16);

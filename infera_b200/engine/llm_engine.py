@@ -105,8 +105,6 @@ class LLMEngine:
         if getattr(mcfg, "kv_channels", 2) == 1:  # MLA: one latent cache row per token
             from infera_b200.models.mla import MLAModel
 
-            if cfg.kv_tier or cfg.disagg_mode != "mixed":
-                raise NotImplementedError("KV tiering / PD disaggregation of a latent (MLA) cache")
             self.model = MLAModel(mcfg, self.device, seed=cfg.seed, tp=tp, ep=ep)
         else:
             self.model = DenseModel(mcfg, self.device, seed=cfg.seed, tp=tp)

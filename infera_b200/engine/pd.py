@@ -129,8 +129,11 @@ class PDRendezvous:
 
     def _make_describe(self) -> dict:
         run = self.engine.runner
+        from infera_b200.ops import kernels as K
+
         d = {"pid": os.getpid(), "layers": int(run.k_cache.shape[0]), "slots": int(run.k_cache.shape[1]),
-             "H": int(run.k_cache.shape[2]), "device": run.k_cache.device.index if run.k_cache.is_cuda else -1}
+             "H": int(run.k_cache.shape[2]), "channels": K.kv_channels(run.k_cache, run.v_cache),
+             "device": run.k_cache.device.index if run.k_cache.is_cuda else -1}
         kb = getattr(run, "_k_buf", None)
         if run.k_cache.is_cuda:
             if kb is not None:  # own allocations: whole-buffer handles at offset 0
@@ -244,6 +247,8 @@ class LayerPush:
         """After the forward: every job's completion event (the side stream's
         last push); the main stream also waits for it before the pages can be
         reused."""
+        from infera_b200.ops import kernels as K
+
         end = True
         if self.on_gpu:
             end = torch.cuda.Event(enable_timing=True)
@@ -259,15 +264,17 @@ class LayerPush:
             job.layerwise = True
             st = self.eng.pd_agent.stats
             st["pages"] += int(dp.shape[0])
-            st["bytes"] += 2 * int(dp.shape[0]) * ps * L * H * self.eng.runner.k_cache.element_size()
+            st["bytes"] += (K.kv_channels(self.eng.runner.k_cache, self.eng.runner.v_cache) * int(dp.shape[0]) * ps
+                            * L * H * self.eng.runner.k_cache.element_size())
             st["layerwise"] += 1
 
 
 class _Peer:
     """Where a decode instance's caches are, seen from this process."""
 
-    def __init__(self, endpoint: str, engine_device: torch.device):
+    def __init__(self, endpoint: str, engine_device: torch.device, want: tuple | None = None):
         self.endpoint = endpoint
+        self.want = want              # this side's (layers, H, channels): the peer's cache must match
         self.local = _LOCAL.get(endpoint)
         self.sock = None
         self.k = self.v = None
@@ -275,6 +282,13 @@ class _Peer:
         if self.local is not None:
             self.k, self.v = self.local.runner.k_cache, self.local.runner.v_cache
             self.slots = self.k.shape[1]
+            if want is not None:
+                from infera_b200.ops import kernels as K
+
+                got = (int(self.k.shape[0]), int(self.k.shape[2]), K.kv_channels(self.k, self.v))
+                if got != want:
+                    raise RuntimeError(f"decode instance at {endpoint} has a (layers, H, channels) = {got} "
+                                       f"cache, this instance {want}")
             if self.k.is_cuda and self.k.device != engine_device:
                 # one process driving both GPUs: map the peer directly
                 from infera_b200.ops import _native
@@ -307,6 +321,11 @@ class _Peer:
             return
         d = self.call({"op": "describe"})
         self.slots = d["slots"]
+        if self.want is not None:
+            got = (d["layers"], d["H"], d.get("channels", 2))
+            if got != self.want:
+                raise RuntimeError(f"decode instance at {self.endpoint} has a (layers, H, channels) = {got} "
+                                   f"cache, this instance {self.want}")
         if d["pid"] == os.getpid():
             raise RuntimeError("same-process decode engine not registered locally")
         from infera_b200.ops import _native
@@ -386,7 +405,11 @@ class PDPushAgent:
     def _peer(self, ep: str) -> _Peer:
         p = self.peers.get(ep)
         if p is None:
-            p = self.peers[ep] = _Peer(ep, self.engine.device)
+            r = self.engine.runner
+            from infera_b200.ops import kernels as K
+
+            want = (int(r.k_cache.shape[0]), int(r.k_cache.shape[2]), K.kv_channels(r.k_cache, r.v_cache))
+            p = self.peers[ep] = _Peer(ep, self.engine.device, want)
         return p
 
     # ------------------------------------------------------------------ agent thread
@@ -458,7 +481,8 @@ class PDPushAgent:
                 j._tensors = (sp, dp)
                 L, _, H = eng.runner.k_cache.shape
                 self.stats["pages"] += len(dst)
-                self.stats["bytes"] += 2 * len(dst) * ps * L * H * eng.runner.k_cache.element_size()
+                C = K.kv_channels(eng.runner.k_cache, eng.runner.v_cache)
+                self.stats["bytes"] += C * len(dst) * ps * L * H * eng.runner.k_cache.element_size()
             if j.event is not None and (j.event is True or j.event.query()):
                 self.stats["pushes"] += 1
                 self.stats["push_s"] += time.monotonic() - j.launched_at

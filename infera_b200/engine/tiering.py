@@ -1,7 +1,8 @@
 """KV-cache tiering for the engine: HBM pages <-> host DRAM <-> NVMe.
 
 * Save on eviction: when the block manager is about to reuse a cached page
-  (it held a full, hashed prefix block), the page's K/V for every layer is
+  (it held a full, hashed prefix block), the page's K/V (or, for a latent
+  MLA cache, its one latent row per token) for every layer is
   gathered on the compute stream into a device staging slot (so the page can
   be overwritten right after), copied to pinned host memory on a side
   stream, and handed to a writer thread that packs it as a v2 KV chunk and
@@ -41,15 +42,16 @@ class TierManager:
         self.store = store
         self.ps = page_size
         self.L, _, self.H = k_cache.shape
+        self.C = K.kv_channels(k_cache, v_cache)   # 1 for a latent (MLA) cache
         self.retention = retention
         self.dev = k_cache.device
         self.on_gpu = self.dev.type == "cuda"
-        self.page_bytes = 2 * self.L * page_size * self.H * k_cache.element_size()
+        self.page_bytes = self.C * self.L * page_size * self.H * k_cache.element_size()
         self.header = ChunkHeader(chunk_tokens=page_size, block_size=page_size, num_layers=self.L,
-                                  hidden_dim=self.H, dtype="bf16")
+                                  hidden_dim=self.H, dtype="bf16", num_kv_channels=self.C)
         n = staging_pages
-        self.dev_stage = torch.empty(n, 2 * self.L * page_size * self.H, dtype=k_cache.dtype, device=self.dev)
-        self.host_stage = torch.empty(n, 2 * self.L * page_size * self.H, dtype=k_cache.dtype,
+        self.dev_stage = torch.empty(n, self.C * self.L * page_size * self.H, dtype=k_cache.dtype, device=self.dev)
+        self.host_stage = torch.empty(n, self.C * self.L * page_size * self.H, dtype=k_cache.dtype,
                                       pin_memory=self.on_gpu)
         self.free_slots = queue.Queue()
         for i in range(n):
@@ -131,7 +133,8 @@ class TierManager:
                 hdr, payload = unpack_chunk(blob)
             except PackedFormatError:
                 break
-            if hdr.num_layers != self.L or hdr.hidden_dim != self.H or hdr.chunk_tokens != self.ps:
+            if (hdr.num_layers != self.L or hdr.hidden_dim != self.H or hdr.chunk_tokens != self.ps
+                    or hdr.num_kv_channels != self.C):
                 break
             slot = self.free_slots.get()
             self.host_stage[slot].view(torch.uint8).copy_(torch.frombuffer(bytearray(payload), dtype=torch.uint8))

@@ -182,6 +182,8 @@ class MLAModel:
             cache = k_caches[li]
             M.mla_rope_kvwrite(q_full, kva, fb.positions, fb.slots, self.cos_sin, lw["kv_a_norm"], cfg.rms_eps,
                                cache)
+            if fb.layer_hook is not None:
+                fb.layer_hook(li)   # this layer's latent rows are written (layer-by-layer KV push)
             o_lat = M.mla_attention(q_full, cache, bt, q_row, q_kvlen, self.scale, max_kvlen=max_len,
                                     rope_dim=dr)
             o_hm = o_lat.transpose(0, 1).contiguous().view(Hq * T, L)

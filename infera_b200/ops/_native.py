@@ -46,7 +46,7 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_attn_prefill": [c_vp, c_int, c_int, c_vp, c_vp, c_ll, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int,
                             c_int, c_int, c_float, c_vp, c_int, c_vp, c_vp],
         "ib_scatter_i32": [c_vp, c_vp, c_vp, c_int, c_vp],
-        "ib_kv_page_copy": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_ll, c_int, c_int, c_int, c_vp],
+        "ib_kv_page_copy": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_ll, c_int, c_int, c_int, c_int, c_vp],
         "ib_attn_decode_tc": [c_vp, c_int, c_vp, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
                               c_float, c_vp, c_vp, c_vp, c_int, c_vp, c_vp],
         "ib_gemm_bf16_push": [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp,
@@ -71,7 +71,8 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_ep_wait": [c_vp, ctypes.c_uint, c_vp, c_vp],
         "ib_gemm_grouped": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp,
                             c_int, c_int, c_vp, c_vp],
-        "ib_kv_push_pages": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_int, c_int, c_vp],
+        "ib_kv_push_pages": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_int, c_int, c_int,
+                             c_vp],
         "ib_gemm_fp8": [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp,
                         c_int, c_vp, c_vp],
         "ib_gemm_fp8_push": [c_vp, c_vp, c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp,

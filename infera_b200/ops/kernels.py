@@ -487,19 +487,26 @@ def scatter_i32(dst: torch.Tensor, idx: torch.Tensor, val: torch.Tensor) -> None
     _count()
 
 
+def kv_channels(k_cache: torch.Tensor, v_cache: torch.Tensor) -> int:
+    """2 for a K/V cache pair, 1 for a latent (MLA) cache, whose V tensor is
+    a placeholder (one row per token holds the compressed KV and rope key)."""
+    return 2 if v_cache.shape == k_cache.shape else 1
+
+
 def kv_page_copy(k_cache: torch.Tensor, v_cache: torch.Tensor, chunk: torch.Tensor, pages: torch.Tensor,
                  page_size: int = 16, gather: bool = True) -> None:
     """Move whole KV pages between the cache ([L, slots, H] per channel) and a
-    contiguous chunk [2, L, n_pages*page_size, H]: ``gather=True`` copies
-    cache -> chunk (save), ``False`` chunk -> cache (load)."""
+    contiguous chunk [C, L, n_pages*page_size, H] (C = :func:`kv_channels`):
+    ``gather=True`` copies cache -> chunk (save), ``False`` chunk -> cache (load)."""
     n = pages.shape[0]
     if n == 0:
         return
     L, slots, H = k_cache.shape
+    C = kv_channels(k_cache, v_cache)
     if not k_cache.is_cuda:
         idx = (pages.long()[:, None] * page_size + torch.arange(page_size)[None, :]).reshape(-1)
-        view = chunk.view(2, L, n * page_size, H)
-        for c, cache in enumerate((k_cache, v_cache)):
+        view = chunk.view(C, L, n * page_size, H)
+        for c, cache in enumerate((k_cache, v_cache)[:C]):
             if gather:
                 view[c] = cache[:, idx]
             else:
@@ -507,7 +514,7 @@ def kv_page_copy(k_cache: torch.Tensor, v_cache: torch.Tensor, chunk: torch.Tens
         return
     assert page_size == 16 and chunk.is_contiguous()
     rc = _native.kernels().ib_kv_page_copy(k_cache.data_ptr(), v_cache.data_ptr(), chunk.data_ptr(),
-                                           pages.data_ptr(), n, L, slots, H, k_cache.element_size(),
+                                           pages.data_ptr(), n, L, slots, H, k_cache.element_size(), C,
                                            0 if gather else 1, _stream())
     _native.check(rc, "ib_kv_page_copy")
     _count()
@@ -519,16 +526,18 @@ def kv_push_pages(src_k: torch.Tensor, src_v: torch.Tensor, dst_k, dst_v, src_pa
     """Copy whole KV pages of layers [l0, l1) from ``src_*`` ([L, slots, H]
     tensors) into ``dst_*``: tensors on this device, or raw device pointers
     (ints, CUDA-IPC mappings of another instance's caches; then
-    ``dst_slots`` is required)."""
+    ``dst_slots`` is required). A latent cache (one channel) pushes
+    ``src_k`` only; ``dst_v`` may then be anything."""
     n = src_pages.shape[0]
     if n == 0:
         return
     L, slots, H = src_k.shape
+    C = kv_channels(src_k, src_v)
     l0, l1 = layers if layers is not None else (0, L)
     if not src_k.is_cuda:
         idx_s = (src_pages.long()[:, None] * page_size + torch.arange(page_size)[None, :]).reshape(-1)
         idx_d = (dst_pages.long()[:, None] * page_size + torch.arange(page_size)[None, :]).reshape(-1)
-        for s, d in ((src_k, dst_k), (src_v, dst_v)):
+        for s, d in ((src_k, dst_k), (src_v, dst_v))[:C]:
             d[l0:l1, idx_d] = s[l0:l1, idx_s]
         return
     assert page_size == 16
@@ -537,10 +546,10 @@ def kv_push_pages(src_k: torch.Tensor, src_v: torch.Tensor, dst_k, dst_v, src_pa
         dk, dv = dst_k.data_ptr(), dst_v.data_ptr()
     else:
         assert dst_slots is not None
-        dk, dv = int(dst_k), int(dst_v)
+        dk, dv = int(dst_k), int(dst_v or 0)
     rc = _native.kernels().ib_kv_push_pages(src_k.data_ptr(), src_v.data_ptr(), dk, dv, src_pages.data_ptr(),
                                             dst_pages.data_ptr(), n, l0, l1, slots, dst_slots, H,
-                                            src_k.element_size(), _stream())
+                                            src_k.element_size(), C, _stream())
     _native.check(rc, "ib_kv_push_pages")
     _count()
 

@@ -50,3 +50,78 @@ def test_mla_engine_matches_reference():
             if a != b:
                 assert margins[i] < 0.05, (i, a, b, margins[i])
                 break
+
+
+def _mla(**kw):
+    return LLMEngine(EngineConfig(model="tiny-moe", use_cuda_graphs=False, max_num_seqs=4, **kw), device="cpu")
+
+
+def test_mla_latent_cache_tier_save_and_promote():
+    """A latent cache (one channel) saves to and promotes from the host tier;
+    the chunk header records one KV channel."""
+    eng = _mla(num_pages=12, max_batched_tokens=256, kv_tier="host:0.05")
+    assert eng.tier.C == 1
+    g = torch.Generator().manual_seed(4)
+    a = torch.randint(0, 1000, (64,), generator=g).tolist()
+    sp = SamplingParams(max_tokens=2, ignore_eos=True)
+    eng.generate([a], sp)
+    for _ in range(3):
+        eng.generate([torch.randint(0, 1000, (64,), generator=g).tolist()], sp)
+    eng.tier.flush()
+    assert eng.tier.stats["saved"] >= 4
+    a2 = a + [5, 6, 7]
+    out = eng.generate([a2], SamplingParams(max_tokens=3, ignore_eos=True))[0]
+    assert eng.bm.stats["tier_hit_tokens"] >= 48
+    ref, margins = _greedy_ref(eng.model, a2, 3)
+    for i, (x, y) in enumerate(zip(out, ref)):
+        if x != y:
+            assert margins[i] < 0.05
+            break
+
+
+def test_mla_latent_cache_pd_push():
+    """Prefill -> decode push of a latent cache, whole and layer by layer:
+    the decode output equals a single engine's."""
+    import time
+
+    g = torch.Generator().manual_seed(5)
+    prompt = torch.randint(0, 1024, (70,), generator=g).tolist()
+    ref = _mla(num_pages=64, max_batched_tokens=128).generate([prompt], SamplingParams(max_tokens=4,
+                                                                                       ignore_eos=True))[0]
+    for room, chunk in ((41, 128), (42, 24)):   # one forward (whole push) / several chunks (layer-wise)
+        dec = _mla(num_pages=64, max_batched_tokens=128, disagg_mode="decode",
+                   kv_push_endpoint=f"local://pd-mla-{room}")
+        pre = _mla(num_pages=64, max_batched_tokens=chunk, disagg_mode="prefill")
+        dec.add_request("d", prompt, SamplingParams(max_tokens=4, ignore_eos=True,
+                                                    kv_transfer={"do_remote_prefill": True, "room": room}))
+        dec.step()
+        pre.add_request("p", prompt, SamplingParams(max_tokens=1, ignore_eos=True,
+                                                    kv_transfer={"do_remote_decode": True, "room": room,
+                                                                 "decode_kv_endpoint": dec.pd_rendezvous.endpoint}))
+        out = []
+        for _ in range(500):
+            if pre.has_unfinished():
+                pre.step()
+                time.sleep(0.01)
+            if dec.has_unfinished():
+                for o in dec.step():
+                    out.extend(o.new_token_ids)
+            if not dec.has_unfinished() and not pre.has_unfinished():
+                break
+        assert out == ref, room
+        assert pre.pd_agent.stats["pushes"] == 1 and dec.counters["prompt_tokens"] == 1
+        L, _, H = pre.runner.k_cache.shape
+        assert pre.pd_agent.stats["bytes"] == pre.pd_agent.stats["pages"] * 16 * L * H * 2   # one channel
+
+
+def test_pd_refuses_a_mismatched_decode_cache():
+    import pytest
+
+    dec = LLMEngine(EngineConfig(model="tiny-dense", use_cuda_graphs=False, num_pages=32, disagg_mode="decode",
+                                 kv_push_endpoint="local://pd-mla-mismatch"), device="cpu")
+    pre = _mla(num_pages=32, max_batched_tokens=128, disagg_mode="prefill")
+    from infera_b200.engine.pd import PDPushAgent
+
+    agent = PDPushAgent(pre)
+    with pytest.raises(RuntimeError, match="channels"):
+        agent._peer(dec.pd_rendezvous.endpoint)

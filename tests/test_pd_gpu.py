@@ -54,3 +54,35 @@ def test_pd_push(devs):
     assert K.scratch(dec.device).read_status() == 0
     agree = sum(a == b for a, b in zip(out, ref)) / len(ref)
     assert len(out) == 8 and agree >= 0.75, (out, ref)
+
+
+@pytest.mark.parametrize("channels", [1, 2])
+def test_page_copy_and_push_kernels(channels):
+    """ib_kv_page_copy (gather / scatter) and ib_kv_push_pages on a K/V pair
+    and on a latent (one-channel, 576-wide) cache: bit-exact page moves."""
+    L, slots, H = 3, 64 * 16, 576 if channels == 1 else 256
+    g = torch.Generator().manual_seed(2)
+    k = torch.randn(L, slots, H, generator=g).to(torch.bfloat16).cuda()
+    v = torch.randn(L, slots, H, generator=g).to(torch.bfloat16).cuda() if channels == 2 else \
+        torch.zeros(L, 1, 1, dtype=torch.bfloat16, device="cuda")
+    pages = torch.tensor([5, 0, 63, 17], dtype=torch.int32, device="cuda")
+    chunk = torch.empty(channels * L * 4 * 16 * H, dtype=torch.bfloat16, device="cuda")
+    K.kv_page_copy(k, v, chunk, pages, gather=True)
+    idx = (pages.long()[:, None] * 16 + torch.arange(16, device="cuda")).reshape(-1)
+    view = chunk.view(channels, L, 64, H)
+    assert torch.equal(view[0], k[:, idx])
+    if channels == 2:
+        assert torch.equal(view[1], v[:, idx])
+    k2, v2 = torch.zeros_like(k), torch.zeros_like(v)
+    K.kv_page_copy(k2, v2, chunk, pages, gather=False)
+    assert torch.equal(k2[:, idx], k[:, idx])
+    dk, dv = torch.zeros_like(k), torch.zeros_like(v)
+    dst = torch.tensor([1, 2, 3, 60], dtype=torch.int32, device="cuda")
+    K.kv_push_pages(k, v, dk, dv, pages, dst, layers=(1, 3))
+    torch.cuda.synchronize()
+    idx_d = (dst.long()[:, None] * 16 + torch.arange(16, device="cuda")).reshape(-1)
+    assert torch.equal(dk[1:3, idx_d], k[1:3, idx]) and int(dk[0].abs().sum()) == 0
+    if channels == 2:
+        assert torch.equal(dv[1:3, idx_d], v[1:3, idx])
+    else:
+        assert int(dv.abs().sum()) == 0
