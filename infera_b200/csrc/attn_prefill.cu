@@ -9,7 +9,8 @@
 //               share a TMEM lane quadrant (the same 32 rows) and each
 //               handles half of the 128 keys of S / P and half of the 128
 //               dims of O, exchanging only per-row maxima (bounded mbarrier
-//               pair barrier); P goes to shared memory (K-major, 128-byte
+//               pair barrier); the exponentials run while the previous
+//               tile's PV is on the tensor core; P goes to shared memory (K-major, 128-byte
 //               swizzle); O is rescaled in TMEM only when the running max
 //               grows by more than 2^8 (lazy rescale); final O / l epilogue.
 //               Half of the exponentials run on the FMA pipe (polynomial).
@@ -318,8 +319,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float m_use = rescale ? m_new : m_run;
       const float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
       const bool warp_rescale = __any_sync(0xffffffffu, rescale && j > 0);
-      // P of the previous tile must be consumed before P / O are touched
-      if (j > 0) {
+      // P / O of the previous tile must be consumed before they are touched:
+      // a rescale of O waits here; otherwise the exponentials below run
+      // while the previous tile's PV is still on the tensor core, and the
+      // wait comes just before P is stored
+      if (j > 0 && warp_rescale) {
         if (!mbar_wait_warp(o_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status,
                             kStatusTimeoutTmemFull)) {
           ok = false;
@@ -350,6 +354,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
         sum += __low2float(bb) + __high2float(bb);
         v[i / 2] = *reinterpret_cast<uint32_t*>(&bb);   // packed pairs reuse the low half of v
+      }
+      if (j > 0 && !warp_rescale) {
+        if (!mbar_wait_warp(o_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status,
+                            kStatusTimeoutTmemFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
       }
       uint8_t* blk = sP + half * BLK;
 #pragma unroll
