@@ -136,7 +136,7 @@ class LLMEngine:
             from infera_b200.engine.pd import PDRendezvous
 
             ep = cfg.kv_push_endpoint or f"local://{id(self)}"
-            self.pd_rendezvous = PDRendezvous(self, ep)
+            self.pd_rendezvous = PDRendezvous(self, ep, tp=self._pd_tp())
             self.scheduler.on_park = lambda r, pages, skip, n: self.pd_rendezvous.publish(
                 r.remote_room, r.request_id, [int(x) for x in pages], skip, n)
         self.requests: dict[str, Request] = {}
@@ -189,11 +189,11 @@ class LLMEngine:
             req.remote_room = int(ktp["room"])
         if ktp.get("do_remote_decode") and ktp.get("decode_kv_endpoint") and "room" in ktp:
             req.remote_decode = (int(ktp["room"]), str(ktp["decode_kv_endpoint"]))
-            if self.cfg.pd_layerwise:
+            if self.cfg.pd_layerwise and ktp.get("layerwise", True):   # per request: {"layerwise": false}
                 from infera_b200.engine.pd import PDPushAgent
 
                 if self.pd_agent is None:
-                    self.pd_agent = PDPushAgent(self)
+                    self.pd_agent = PDPushAgent(self, tp=self._pd_tp())
                 self.pd_agent.prefetch(request_id, *req.remote_decode)
         self.requests[request_id] = req
         self.scheduler.add(req)
@@ -214,10 +214,46 @@ class LLMEngine:
         return self.scheduler.num_unfinished() > 0 or (self.pd_agent is not None and self.pd_agent.pending() > 0)
 
     # ------------------------------------------------------------------ PD
+    def _pd_tp(self):
+        """The tensor-parallel group when PD runs over one (world > 1)."""
+        return self.tp if self.tp is not None and self.tp.world > 1 else None
+
+    def pd_tp_decisions(self) -> list:
+        """Tensor-parallel leader, before broadcasting a step: PD events that
+        change scheduling state (plans adopted, pushes completed or failed,
+        parked requests resumed), applied here and returned for the
+        followers to apply at the same point."""
+        cmds = []
+        if self.pd_agent is not None:
+            cmds += self.pd_agent.tp_decisions()
+        if self.pd_rendezvous is not None:
+            cmds += self.pd_rendezvous.tp_decisions()
+        for c in cmds:
+            self.pd_apply(c)
+        return cmds
+
+    def pd_apply(self, c: tuple) -> None:
+        if c[0] == "pd_resume":
+            r = self.scheduler.parked.get(c[1])
+            if r is not None:
+                self.pd_rendezvous.forget(r.remote_room)
+                self.scheduler.resume_parked(r, bool(c[2]))
+        elif self.pd_agent is not None:
+            self.pd_agent.apply(c)
+
+    def pd_fence(self) -> None:
+        """A collective over the tensor-parallel group, queued after this
+        rank's KV pushes (see ``PDPushAgent.progress``)."""
+        import torch.distributed as dist
+
+        if getattr(self, "_fence_buf", None) is None:
+            self._fence_buf = torch.zeros(1, dtype=torch.int32, device=self.device)
+        dist.all_reduce(self._fence_buf, group=self.tp.nccl)
+
     def _pd_progress(self) -> None:
         if self.pd_agent is not None and self.pd_agent.pending():
             self.pd_agent.progress()
-        if self.pd_rendezvous is not None and self.scheduler.parked:
+        if self.pd_rendezvous is not None and self.scheduler.parked and self._pd_tp() is None:
             for r in list(self.scheduler.parked.values()):
                 st = self.pd_rendezvous.poll(r.remote_room)
                 if st != "pending":
@@ -328,7 +364,7 @@ class LLMEngine:
 
             held = self.scheduler.finish(r, st, hold_blocks=True)
             if self.pd_agent is None:
-                self.pd_agent = PDPushAgent(self)
+                self.pd_agent = PDPushAgent(self, tp=self._pd_tp())
             room, ep = r.remote_decode
             job = self.pd_agent.take_early(r.request_id)
             if job is None:

@@ -89,7 +89,13 @@ class Room:
 
 
 class PDRendezvous:
-    def __init__(self, engine, endpoint: str, timeout_s: float = 30.0):
+    """Decode side. With a tensor-parallel group (``tp``), every rank parks
+    the same requests on the same pages (lockstep scheduling); only the
+    leader serves the endpoint, its ``describe`` lists every rank's cache
+    handles (``ranks``), and it decides when a parked request resumes
+    (:meth:`tp_decisions`, replayed on the followers as commands)."""
+
+    def __init__(self, engine, endpoint: str, timeout_s: float = 30.0, tp=None):
         self.engine = engine
         self.endpoint = endpoint
         self.timeout_s = timeout_s
@@ -97,10 +103,35 @@ class PDRendezvous:
         self.lock = threading.Lock()
         self._stop = False
         self.stats = {"rooms": 0, "done": 0, "failed": 0, "timeouts": 0}
-        self._describe = self._make_describe()
-        _LOCAL[endpoint] = engine
-        self._th = threading.Thread(target=self._serve, name="pd-rendezvous", daemon=True)
-        self._th.start()
+        self.tp = tp
+        rank = tp.rank if tp is not None else 0
+        self.leader = rank == 0
+        d = self._make_describe()
+        self._local_key = None
+        if tp is not None:
+            import torch.distributed as dist
+
+            d["local"] = self._local_key = f"{endpoint}#{rank}"
+            _LOCAL[d["local"]] = engine
+            alld = [None] * tp.world
+            dist.all_gather_object(alld, d, group=tp.gloo)
+            d = dict(alld[0], ranks=alld)
+        self._describe = d
+        self._th = None
+        if self.leader:
+            _LOCAL[endpoint] = engine
+            self._th = threading.Thread(target=self._serve, name="pd-rendezvous", daemon=True)
+            self._th.start()
+
+    def tp_decisions(self) -> list:
+        """Leader, before a tensor-parallel step: parked requests whose room
+        ended (pushed, failed or timed out), as ``("pd_resume", rid, ok)``."""
+        out = []
+        for r in list(self.engine.scheduler.parked.values()):
+            st = self.poll(r.remote_room)
+            if st != "pending":
+                out.append(("pd_resume", r.request_id, st == "ok"))
+        return out
 
     # called by the engine thread
     def publish(self, room: int, rid: str, pages: list[int], skip_tokens: int, n_tokens: int) -> None:
@@ -191,10 +222,23 @@ class PDRendezvous:
 
     def close(self) -> None:
         self._stop = True
-        _LOCAL.pop(self.endpoint, None)
+        if self.leader:
+            _LOCAL.pop(self.endpoint, None)
+        if self._local_key is not None:
+            _LOCAL.pop(self._local_key, None)
 
 
 # --------------------------------------------------------------------------- prefill side
+
+
+def _record_done(eng):
+    """Completion marker of the work queued so far on the engine's stream
+    (True on CPU, where everything ran synchronously)."""
+    if not eng.runner.k_cache.is_cuda:
+        return True
+    ev = torch.cuda.Event(enable_timing=True)
+    ev.record()
+    return ev
 
 
 @dataclass
@@ -208,6 +252,8 @@ class PushJob:
     event: object = None        # CUDA event of the launched copy
     launched_at: float = 0.0
     layerwise: bool = False     # pushed layer by layer inside the prompt's last forward
+    resolved: tuple | None = None   # tensor-parallel leader: (plan, describe) to adopt at the next step
+    fail_seen: bool = False         # tensor-parallel leader: failure to announce at the next step
 
 
 class LayerPush:
@@ -254,6 +300,9 @@ class LayerPush:
             end = torch.cuda.Event(enable_timing=True)
             end.record(self.side)
             torch.cuda.current_stream().wait_event(end)
+        if self.eng.pd_agent.tp is not None:
+            self.eng.pd_fence()   # see PDPushAgent.progress
+            end = _record_done(self.eng)
         L, _, H = self.eng.runner.k_cache.shape
         ps = self.eng.bm.page_size
         for job, sp, dp, _ in self.items:
@@ -272,14 +321,18 @@ class LayerPush:
 class _Peer:
     """Where a decode instance's caches are, seen from this process."""
 
-    def __init__(self, endpoint: str, engine_device: torch.device, want: tuple | None = None):
+    def __init__(self, endpoint: str, engine_device: torch.device, want: tuple | None = None,
+                 tp_rank: int | None = None, tp_world: int = 1):
         self.endpoint = endpoint
         self.want = want              # this side's (layers, H, channels): the peer's cache must match
+        self.device = engine_device
+        self.tp_rank, self.tp_world = tp_rank, tp_world   # set: map that rank of a TP decode group
         self.local = _LOCAL.get(endpoint)
         self.sock = None
         self.k = self.v = None
         self.slots = 0
-        if self.local is not None:
+        self.described = None
+        if self.local is not None and tp_rank is None:
             self.k, self.v = self.local.runner.k_cache, self.local.runner.v_cache
             self.slots = self.k.shape[1]
             if want is not None:
@@ -316,16 +369,44 @@ class _Peer:
             self.sock = None
             raise TimeoutError(f"pd endpoint {self.endpoint} did not answer")
 
+    def describe(self) -> dict:
+        if self.described is None:
+            self.described = self.call({"op": "describe"})
+        return self.described
+
     def map(self) -> None:
         if self.k is not None:
             return
-        d = self.call({"op": "describe"})
-        self.slots = d["slots"]
+        self.map_from(self.describe())
+
+    def map_from(self, d: dict) -> None:
+        """Map the decode caches that ``d`` (the decode leader's describe)
+        names for this rank."""
+        if self.k is not None:
+            return
+        if self.tp_rank is not None:
+            ranks = d.get("ranks", [d])
+            if len(ranks) != self.tp_world:
+                raise RuntimeError(f"decode instance at {self.endpoint} has {len(ranks)} tensor-parallel ranks, "
+                                   f"this instance {self.tp_world}")
+            d = ranks[self.tp_rank]
         if self.want is not None:
             got = (d["layers"], d["H"], d.get("channels", 2))
             if got != self.want:
                 raise RuntimeError(f"decode instance at {self.endpoint} has a (layers, H, channels) = {got} "
                                    f"cache, this instance {self.want}")
+        self.slots = d["slots"]
+        loc = _LOCAL.get(d.get("local", ""))
+        if loc is not None:   # the decode rank lives in this process
+            k, v = loc.runner.k_cache, loc.runner.v_cache
+            if k.is_cuda and k.device != self.device:
+                from infera_b200.ops import _native
+
+                _native.check(_native.kernels().ib_enable_peer_access(k.device.index),
+                              f"enable peer access to {k.device}")
+                k, v = k.data_ptr(), v.data_ptr()
+            self.k, self.v = k, v
+            return
         if d["pid"] == os.getpid():
             raise RuntimeError("same-process decode engine not registered locally")
         from infera_b200.ops import _native
@@ -346,12 +427,20 @@ class PDPushAgent:
     agent's thread; the engine thread only launches copies and polls their
     events, so a slow decode instance never stalls prefill steps."""
 
-    def __init__(self, engine, timeout_s: float = 30.0):
+    def __init__(self, engine, timeout_s: float = 30.0, tp=None):
         self.engine = engine
         self.timeout_s = timeout_s
+        # tensor-parallel prefill group: only the leader talks to the decode
+        # side; plans, failures and completions reach every rank as commands
+        # (:meth:`tp_decisions` / :meth:`apply`) so the ranks' block managers
+        # stay identical, and each rank pushes its own KV-head shard into the
+        # same rank of the decode group
+        self.tp = tp
+        self.leader = tp is None or tp.rank == 0
         self.jobs: list[PushJob] = []
         self.peers: dict[str, _Peer] = {}
         self.lock = threading.Lock()
+        self._peer_lock = threading.Lock()
         self._notices: list[tuple[str, int, bool]] = []
         self._wake = threading.Event()
         self._stop = False
@@ -359,8 +448,10 @@ class PDPushAgent:
                       "push_device_s": 0.0, "layerwise": 0}
         self.early: dict[str, PushJob] = {}   # admitted, plan being resolved, prompt not done yet
         self.side = None                       # stream of the layer-by-layer pushes
-        self._th = threading.Thread(target=self._run, name="pd-push-agent", daemon=True)
-        self._th.start()
+        self._th = None
+        if self.leader:
+            self._th = threading.Thread(target=self._run, name="pd-push-agent", daemon=True)
+            self._th.start()
 
     def submit(self, job: PushJob) -> None:
         with self.lock:
@@ -403,14 +494,96 @@ class PDPushAgent:
         return len(self.jobs)
 
     def _peer(self, ep: str) -> _Peer:
+        with self._peer_lock:   # the agent thread and the engine thread both look peers up
+            return self._peer_locked(ep)
+
+    def _peer_locked(self, ep: str) -> _Peer:
         p = self.peers.get(ep)
         if p is None:
             r = self.engine.runner
             from infera_b200.ops import kernels as K
 
             want = (int(r.k_cache.shape[0]), int(r.k_cache.shape[2]), K.kv_channels(r.k_cache, r.v_cache))
-            p = self.peers[ep] = _Peer(ep, self.engine.device, want)
+            if self.tp is not None:
+                p = _Peer(ep, self.engine.device, want, tp_rank=self.tp.rank, tp_world=self.tp.world)
+            else:
+                p = _Peer(ep, self.engine.device, want)
+            self.peers[ep] = p
         return p
+
+    # ------------------------------------------------------------------ tensor-parallel commands
+    def _find(self, rid: str):
+        with self.lock:
+            j = self.early.get(rid)
+            if j is None:
+                j = next((x for x in self.jobs if x.rid == rid), None)
+        return j
+
+    def tp_decisions(self) -> list:
+        """Leader, before a tensor-parallel step: what the agent thread and
+        the leader's copy events decided since the last step, as commands
+        that every rank (this one included) then applies in the same order."""
+        out = []
+        with self.lock:
+            cands = list(self.early.values()) + list(self.jobs)
+            queued = {id(j) for j in self.jobs}
+        now = time.monotonic()
+        for j in cands:
+            if getattr(j, "failed", False):
+                continue
+            if j.fail_seen:
+                out.append(("pd_fail", j.rid))
+            elif j.plan is None and j.resolved is not None:
+                out.append(("pd_plan", j.rid, j.resolved[0], j.endpoint, j.resolved[1]))
+            elif id(j) in queued and j.event is not None and (j.event is True or j.event.query()):
+                out.append(("pd_done", j.rid))
+            elif id(j) in queued and j.event is None and now - j.created > self.timeout_s:
+                out.append(("pd_timeout", j.rid))
+        return out
+
+    def apply(self, cmd: tuple) -> None:
+        """Apply one ``pd_*`` command (every rank of a tensor-parallel group)."""
+        j = self._find(cmd[1])
+        if j is None:
+            return
+        kind = cmd[0]
+        if kind == "pd_plan":
+            _, _, plan, ep, desc = cmd
+            try:
+                self._peer(ep).map_from(desc)
+                j.plan = plan
+            except Exception as e:   # every rank sees the same describe: the same outcome
+                logger.warning("kv push for room %s failed: %s", j.room, e)
+                j.failed = True
+                if self.leader:
+                    with self.lock:
+                        self._notices.append((j.endpoint, j.room, False))
+                    self._wake.set()
+        elif kind == "pd_fail":
+            j.failed = True
+        elif kind == "pd_timeout":
+            self.stats["timeouts"] += 1
+            self._drop(j)
+        elif kind == "pd_done":
+            self._complete(j)
+
+    def _drop(self, j) -> None:
+        self.engine._release_pushed(j)
+        with self.lock:
+            self.jobs = [x for x in self.jobs if x is not j]
+
+    def _complete(self, j) -> None:
+        self.stats["pushes"] += 1
+        self.stats["push_s"] += time.monotonic() - j.launched_at
+        if j.event is not True and getattr(j, "start_event", None) is not None:
+            # the copy kernels' own device time (CUDA events around them;
+            # layer by layer: from the forward's start to the last push)
+            self.stats["push_device_s"] += j.start_event.elapsed_time(j.event) / 1000.0
+        if self.leader:
+            with self.lock:
+                self._notices.append((j.endpoint, j.room, True))
+            self._wake.set()
+        self._drop(j)
 
     # ------------------------------------------------------------------ agent thread
     def _run(self) -> None:
@@ -430,17 +603,25 @@ class PDPushAgent:
                 except Exception as e:
                     logger.warning("kv push: done notice for room %s failed: %s", room, e)
             for j in todo:
+                if j.resolved is not None or j.fail_seen:
+                    continue   # waiting for the next tensor-parallel step to adopt it
                 peer = self._peer(j.endpoint)
                 try:
                     r = peer.call({"op": "pages", "room": j.room}, timeout_ms=500)
                     if r.get("ready"):
-                        peer.map()
-                        j.plan = r
+                        if self.tp is not None:
+                            j.resolved = (r, peer.describe())
+                        else:
+                            peer.map()
+                            j.plan = r
                 except TimeoutError:
                     pass
                 except Exception as e:
                     logger.warning("kv push for room %s failed: %s", j.room, e)
-                    j.failed = True
+                    if self.tp is not None:
+                        j.fail_seen = True
+                    else:
+                        j.failed = True
                     if j.blocks is not None or j in self.jobs:
                         with self.lock:
                             self._notices.append((j.endpoint, j.room, False))
@@ -451,6 +632,7 @@ class PDPushAgent:
 
         eng = self.engine
         keep = []
+        launched = []
         with self.lock:
             jobs = list(self.jobs)
         for j in jobs:
@@ -459,6 +641,7 @@ class PDPushAgent:
                 eng._release_pushed(j)
                 continue
             if j.event is None and j.plan is not None:
+                launched.append(j)
                 peer = self.peers[j.endpoint]
                 ps = eng.bm.page_size
                 skip = j.plan["skip_tokens"] // ps
@@ -473,16 +656,16 @@ class PDPushAgent:
                     j.start_event.record()
                 K.kv_push_pages(eng.runner.k_cache, eng.runner.v_cache, peer.k, peer.v, sp, dp, dst_slots=peer.slots)
                 j.launched_at = time.monotonic()
-                if eng.runner.k_cache.is_cuda:
-                    j.event = torch.cuda.Event(enable_timing=True)
-                    j.event.record()
-                else:
-                    j.event = True
+                if self.tp is None:
+                    j.event = _record_done(eng)
                 j._tensors = (sp, dp)
                 L, _, H = eng.runner.k_cache.shape
                 self.stats["pages"] += len(dst)
                 C = K.kv_channels(eng.runner.k_cache, eng.runner.v_cache)
                 self.stats["bytes"] += C * len(dst) * ps * L * H * eng.runner.k_cache.element_size()
+            if self.tp is not None:
+                keep.append(j)   # completion and timeouts arrive as commands
+                continue
             if j.event is not None and (j.event is True or j.event.query()):
                 self.stats["pushes"] += 1
                 self.stats["push_s"] += time.monotonic() - j.launched_at
@@ -503,6 +686,15 @@ class PDPushAgent:
         with self.lock:
             done_ids = {id(j) for j in jobs} - {id(j) for j in keep}
             self.jobs = [j for j in self.jobs if id(j) not in done_ids]
+        if self.tp is not None and launched:
+            # every rank launched the same pushes: a collective after them
+            # means, once the leader sees it complete, that every rank's
+            # copies have completed (each rank's collective waits for its
+            # own stream's pushes)
+            eng.pd_fence()
+            ev = _record_done(eng)
+            for j in launched:
+                j.event = ev
 
     def close(self) -> None:
         self._stop = True

@@ -46,6 +46,7 @@ class TPLeader:
 
     def step(self):
         cmds, self.engine.cmd_log = self.engine.cmd_log, []
+        cmds += self.engine.pd_tp_decisions()   # applied on this rank already
         self._broadcast(("step", cmds))
         return self.engine.step()
 
@@ -72,21 +73,31 @@ class TPLeader:
         return [outs[r] for r in ids]
 
 
+def follower_step(engine, group) -> bool:
+    """Receive and mirror one leader message (commands, then the step);
+    False once the leader said stop."""
+    obj = [None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    msg = obj[0]
+    if msg == STOP:
+        return False
+    kind, cmds = msg
+    for c in cmds:
+        if c[0] == "add":
+            engine.add_request(c[1], c[2], c[3])
+        elif c[0] == "abort":
+            engine.abort_request(c[1])
+        elif c[0].startswith("pd_"):
+            engine.pd_apply(c)
+    if kind == "step":  # mirror the leader's step exactly
+        engine.step()
+        engine.tp_steps = getattr(engine, "tp_steps", 0) + 1
+    return True
+
+
 def follower_loop(engine, group) -> int:
     """Run on ranks > 0 until the leader says stop; returns the step count."""
-    steps = 0
-    while True:
-        obj = [None]
-        dist.broadcast_object_list(obj, src=0, group=group)
-        msg = obj[0]
-        if msg == STOP:
-            return steps
-        kind, cmds = msg
-        for c in cmds:
-            if c[0] == "add":
-                engine.add_request(c[1], c[2], c[3])
-            elif c[0] == "abort":
-                engine.abort_request(c[1])
-        if kind == "step":  # mirror the leader's step exactly
-            engine.step()
-            steps += 1
+    n0 = getattr(engine, "tp_steps", 0)
+    while follower_step(engine, group):
+        pass
+    return engine.tp_steps - n0 if hasattr(engine, "tp_steps") else 0

@@ -86,3 +86,28 @@ def test_page_copy_and_push_kernels(channels):
         assert torch.equal(dv[1:3, idx_d], v[1:3, idx])
     else:
         assert int(dv.abs().sum()) == 0
+
+
+def test_pd_pair_of_tp2_instances():
+    """The tensor-parallel PD protocol on 2 GPUs (fused TP all-reduce, NCCL
+    fence after the pushes): decode outputs equal a mixed TP instance's."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cmd = ["timeout", "-k", "10", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29796", "-m",
+           "infera_b200.bench.pd_tp_check", "--model", "tiny-dense-gpu"]
+    r = subprocess.run(cmd, env=dict(os.environ, PYTHONPATH=root, NCCL_NVLS_ENABLE="0"), cwd=root,
+                       stdout=subprocess.PIPE, stderr=subprocess.STDOUT, timeout=360)
+    out = r.stdout.decode()
+    assert r.returncode == 0, out[-3000:]
+    res = json.loads([x for x in out.splitlines() if x.startswith("{")][-1])
+    agree = sum(x == y for o, f in zip(res["outputs"], res["reference"]) for x, y in zip(o, f))
+    assert agree >= 0.8 * sum(len(f) for f in res["reference"]), res
+    for rk in res["ranks"]:
+        assert rk["pushes"] == 2 and rk["decode_prompt_tokens"] == 2 and not rk["unfinished"], res
