@@ -33,6 +33,7 @@ def main(argv=None) -> None:
     ap.add_argument("--top-k", type=int, default=4)
     ap.add_argument("--iters", type=int, default=0)
     ap.add_argument("--fused", action="store_true", help="NVLink peer-store dispatch / return (GPUs)")
+    ap.add_argument("--fp8", action="store_true", help="e4m3 experts with 128x128 block scales")
     a = ap.parse_args(argv)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -46,7 +47,7 @@ def main(argv=None) -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=120)) if not a.cpu else None
     full = MoELayer(a.hidden, a.ffn, a.experts, a.top_k, n_groups=4, topk_groups=2, routed_scaling=2.0,
-                    num_shared=1, device="cpu", seed=7)
+                    num_shared=1, device="cpu", seed=7, weight_dtype="fp8" if a.fp8 else "bf16")
     g = torch.Generator().manual_seed(11)
     x_all = torch.randn(world * a.tokens, a.hidden, generator=g).to(torch.bfloat16)
     x = x_all[rank * a.tokens:(rank + 1) * a.tokens].contiguous()

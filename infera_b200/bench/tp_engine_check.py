@@ -58,6 +58,21 @@ def main(argv=None) -> None:
         ref = ref_eng.generate(prompts[:4], SamplingParams(max_tokens=8, ignore_eos=True))
         agree = sum(x == y for o, r in zip(outs, ref) for x, y in zip(o, r)) / sum(len(r) for r in ref)
         res["greedy_agreement"] = round(agree, 4)
+        # random-init weights put many next tokens within rounding distance of
+        # each other: at each sequence's first divergence, how far below the
+        # single-GPU model's best logit the tensor-parallel choice is,
+        # relative to the largest logit magnitude (near 0: a rounding tie)
+        worst, div = 0.0, 0
+        for p, o, r in zip(prompts[:4], outs, ref):
+            i = next((j for j, (x, y) in enumerate(zip(o, r)) if x != y), None)
+            if i is None:
+                continue
+            div += 1
+            ref_eng.generate([p + o[:i]], SamplingParams(max_tokens=1, ignore_eos=True))
+            lg = ref_eng.runner.last_logits[-1].float()
+            worst = max(worst, float(lg.max() - lg[o[i]]) / float(lg.abs().max()))
+        res["divergences"] = div
+        res["max_rel_gap_at_divergence"] = round(worst, 5)
         ref_eng.close()
         del ref_eng
         torch.cuda.empty_cache()

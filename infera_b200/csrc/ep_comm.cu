@@ -14,7 +14,11 @@
 //                   recv[dest(e)][dst_off[e] + r - offsets[e]] with 16-byte
 //                   peer stores, then the last CTA adds 1 to an arrival
 //                   counter on every rank;
-//   ib_ep_wait      waits (bounded, 2 s) until all W arrivals of a round are in;
+//   ib_ep_dispatch_q the same for e4m3 rows plus their UE8M0 scale columns
+//                   (the sender quantised them; half the bytes of bf16);
+//   ib_ep_wait      waits (bounded, 2 s) until all W arrivals of a round are in
+//                   (the up projection can instead wait inside its own
+//                   producer: ib_gemm_grouped_wait);
 //   ib_ep_return    copies each expert-output row p < loc_off[El] (local
 //                   expert e, source s) back to ret[s][src_off[s][e] + (p -
 //                   start of (e, s))], then signals like the dispatch.
@@ -121,6 +125,30 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const uint4* __restrict__
   signal_all(done_ctr, pr, world);
 }
 
+// fp8 dispatch: the sender quantised its sorted rows (e4m3 rows of
+// vec_per_row 16-byte vectors, UE8M0 scales sf [n_groups, sf_ld], one
+// column per row); each row and its n_groups scale bytes go to the same
+// place on the destination (recv rows, recv_sf [n_groups, recv_sf_ld]), so
+// the receiver's fp8 grouped GEMM reads them without a quantisation pass.
+__global__ void __launch_bounds__(256) dispatch_q_kernel(const uint4* __restrict__ x, int rows, int vec_per_row,
+                                                         const uint8_t* __restrict__ sf, int sf_ld, int n_groups,
+                                                         const int* __restrict__ offsets, int E, int El,
+                                                         const int* __restrict__ dst_off, Peers pr, Peers psf,
+                                                         int recv_sf_ld, int world, unsigned int* done_ctr) {
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int e = find_bin(offsets, E, r);
+    const int d = e / El;
+    const long long pos = static_cast<long long>(dst_off[e]) + (r - offsets[e]);
+    uint4* dst = static_cast<uint4*>(pr.buf[d]) + pos * vec_per_row;
+    const uint4* src = x + static_cast<long long>(r) * vec_per_row;
+    for (int i = threadIdx.x; i < vec_per_row; i += blockDim.x) dst[i] = __ldg(src + i);
+    uint8_t* dsf = static_cast<uint8_t*>(psf.buf[d]);
+    for (int g = threadIdx.x; g < n_groups; g += blockDim.x)
+      dsf[static_cast<long long>(g) * recv_sf_ld + pos] = __ldg(sf + static_cast<long long>(g) * sf_ld + r);
+  }
+  signal_all(done_ctr, pr, world);
+}
+
 __global__ void __launch_bounds__(256) return_kernel(const uint4* __restrict__ y, int rows, int vec_per_row,
                                                      const int* __restrict__ C, int W, int E, int El, int rank,
                                                      const int* __restrict__ loc_off,
@@ -201,6 +229,26 @@ extern "C" int ib_ep_dispatch(const void* x, int rows, int H, const int* offsets
   const int grid = rows < 1 ? 1 : (rows < 2048 ? rows : 2048);
   dispatch_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(x), rows, H * 2 / 16, offsets, E, E / world,
                                             dst_off, pr, world, done_ctr);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+// fp8 rows (row_bytes % 16 == 0) with their scale columns; peer_sf: each
+// rank's recv_sf base ([n_groups, recv_sf_ld] bytes)
+extern "C" int ib_ep_dispatch_q(const void* x, int rows, int row_bytes, const uint8_t* sf, int sf_ld, int n_groups,
+                                const int* offsets, int E, int world, const int* dst_off, void* const* peer_buf,
+                                void* const* peer_sf, int recv_sf_ld, unsigned int* const* peer_flag,
+                                unsigned int* done_ctr, cudaStream_t stream) {
+  if (world < 1 || world > kMaxRanks || row_bytes % 16 || n_groups < 0) return -1;
+  Peers pr{}, psf{};
+  for (int d = 0; d < world; ++d) {
+    pr.buf[d] = peer_buf[d];
+    pr.flag[d] = peer_flag[d];
+    psf.buf[d] = peer_sf[d];
+  }
+  const int grid = rows < 1 ? 1 : (rows < 2048 ? rows : 2048);
+  dispatch_q_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(x), rows, row_bytes / 16, sf, sf_ld, n_groups,
+                                              offsets, E, E / world, dst_off, pr, psf, recv_sf_ld, world, done_ctr);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }

@@ -97,7 +97,38 @@ struct Params {
   const uint8_t* sf_w;
   const uint8_t* sf_a;
   int sf_w_ld, sf_a_ld;
+  // optional: the A rows (and fp8 scales) are being stored into this rank's
+  // memory by other GPUs (expert-parallel dispatch); their readers wait,
+  // bounded, until *wait_flag >= wait_target before the first read
+  const unsigned int* wait_flag;
+  unsigned int wait_target;
 };
+
+// Bounded wait for the dispatch's arrival counter (release-incremented by
+// each sender after its stores). On success the generic-proxy view is
+// ordered before this thread's later TMA (async-proxy) reads; on timeout the
+// status is recorded and the CTA's other roles are released through
+// abort_flag.
+__device__ __forceinline__ bool wait_arrivals(const Params& p, volatile int* abort_flag) {
+  if (p.wait_flag == nullptr) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.wait_flag) : "memory");
+    if (v >= p.wait_target) break;
+    if (((++spins) & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        record_status(p.status, kStatusTimeoutPeer);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
 
 // pipeline event stamps of CTA 0 (trace[event * kTraceSteps + k-step]) for diagnosis
 enum : int { TRG_TMA = 0, TRG_FULL, TRG_SFFULL, TRG_ISSUED, TRG_SFARRIVE, kTraceEventsG };
@@ -341,7 +372,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       const uint32_t tx = static_cast<uint32_t>((BM + p.bn) * 128);
       uint32_t stage = 0, phase = 0;
       long long issued = 0;
-      bool ok = true;
+      bool ok = wait_arrivals(p, abort_flag);
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         int pt, qt, sp;
         tile_coords(p, t, pt, qt, sp);
@@ -493,9 +524,14 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     constexpr int kAhead = 4;
     uint32_t wv[kAhead], rv[kAhead][8];
     bool has[kAhead];
+    bool arrived = true;
+    if (p.wait_flag != nullptr) {   // the activation scales arrive with the dispatched rows
+      if (lane == 0) arrived = wait_arrivals(p, abort_flag);
+      arrived = __shfl_sync(0xffffffffu, arrived ? 1 : 0, 0) != 0;
+    }
 #pragma unroll
-    for (int k = 0; k < kAhead; ++k) has[k] = fetch(wv[k], rv[k]);
-    bool go = true;
+    for (int k = 0; k < kAhead; ++k) has[k] = arrived && fetch(wv[k], rv[k]);
+    bool go = arrived;
     while (go) {
 #pragma unroll
       for (int k = 0; k < kAhead; ++k) {
@@ -864,7 +900,8 @@ inline int run_grouped(const Operands& o, const void* A, const void* W, void* ou
                        int lda, int ldw, int ldc, int epi, const int* gtab, const int* gnum, int bn, int grid_tiles,
                        int* status, cudaStream_t stream, const int* row_map = nullptr, int world = 1,
                        void* const* peer_out = nullptr, unsigned int* const* peer_flag = nullptr,
-                       unsigned int* done_ctr = nullptr) {
+                       unsigned int* done_ctr = nullptr, const unsigned int* wait_flag = nullptr,
+                       unsigned int wait_target = 0) {
   if (R <= 0 || N <= 0 || K <= 0 || E <= 0) return 0;
   if (!operands_ok(o, K, lda, ldw) || (N % BM) != 0) return -1;
   if (o.fp8 ? (bn < 32 || bn > MAX_BN_FP8 || (bn % 32) != 0) : (bn < 16 || bn > MAX_BN || (bn % 16) != 0))
@@ -890,6 +927,8 @@ inline int run_grouped(const Operands& o, const void* A, const void* W, void* ou
   p.gnum = gnum;
   p.n_per_expert = N;
   p.row_map = row_map;
+  p.wait_flag = wait_flag;
+  p.wait_target = wait_target;
   if (row_map != nullptr) {
     if (epi != EPI_BF16 || world < 1 || world > kMaxPeers || done_ctr == nullptr) return -1;
     p.push = 1;
@@ -982,6 +1021,21 @@ extern "C" int ib_gemm_grouped(const void* A, const void* W, void* out, int R, i
                                cudaStream_t stream) {
   const gemm::Operands o{false, nullptr, 0, nullptr};
   return gemm::run_grouped(o, A, W, out, R, N, K, E, lda, ldw, ldc, epi, gtab, gnum, bn, grid_tiles, status, stream);
+}
+
+// Grouped GEMM (bf16, or fp8 when sf_w is not null) over rows that other
+// GPUs are still storing into A (and sf_a): the TMA producer and the scale
+// stagers first wait, bounded, until *wait_flag >= wait_target (the
+// expert-parallel dispatch's arrival counter), so the dispatch's wait is
+// fused into the up projection instead of being its own launch.
+extern "C" int ib_gemm_grouped_wait(const void* A, const uint8_t* sf_a, int sf_a_ld, const void* W,
+                                    const uint8_t* sf_w, void* out, int R, int N, int K, int E, int lda, int ldw,
+                                    int ldc, int epi, const int* gtab, const int* gnum, int bn, int grid_tiles,
+                                    const unsigned int* wait_flag, unsigned int wait_target, int* status,
+                                    cudaStream_t stream) {
+  const gemm::Operands o{sf_w != nullptr, sf_a, sf_a_ld, sf_w};
+  return gemm::run_grouped(o, A, W, out, R, N, K, E, lda, ldw, ldc, epi, gtab, gnum, bn, grid_tiles, status, stream,
+                           nullptr, 1, nullptr, nullptr, nullptr, wait_flag, wait_target);
 }
 
 // fp8 grouped GEMM: as above with e4m3 operands; sf_a [K/128, sf_a_ld] over

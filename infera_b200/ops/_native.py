@@ -22,6 +22,7 @@ _kernels: ctypes.CDLL | None = None
 c_int = ctypes.c_int
 c_ll = ctypes.c_longlong
 c_float = ctypes.c_float
+c_uint = ctypes.c_uint
 c_vp = ctypes.c_void_p
 c_ip = ctypes.c_void_p  # int* passed as raw address
 
@@ -94,6 +95,10 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_ep_row_map": [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp, c_vp],
         "ib_gemm_grouped_push": [c_vp, c_vp, c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                  c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp],
+        "ib_gemm_grouped_wait": [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int,
+                                 c_int, c_int, c_vp, c_vp, c_int, c_int, c_vp, c_uint, c_vp, c_vp],
+        "ib_ep_dispatch_q": [c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int,
+                             c_vp, c_vp, c_vp],
         "ib_gemm_set_trace": [c_vp],
         "ib_attn_prefill_set_trace": [c_vp],
         "ib_mla_rope_kvwrite": [c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_float, c_vp, c_vp],

@@ -21,7 +21,10 @@ Two data paths:
   KB) and the rows move with this framework's kernels over NVLink peer
   memory - ``ib_ep_dispatch`` stores each sorted row straight into its
   destination's receive buffer at its [local expert][source] place (no
-  regroup on the receiver), and the down projection's epilogue
+  regroup on the receiver; fp8 experts: the sender quantises and
+  ``ib_ep_dispatch_q`` moves e4m3 rows with their scale columns), the up
+  projection (``ib_gemm_grouped_wait``) waits for the arrivals inside its
+  own TMA producer, and the down projection's epilogue
   (``ib_gemm_grouped_push``) stores each expert-output row straight back
   at its source's sorted row; arrival counters with bounded waits
   separate the phases, and nothing is read back to the host.
@@ -77,7 +80,10 @@ class EPMoE:
         lib = _native.kernels()
         self.max_rows, self.H = max_rows, H
         self.buf_bytes = max_rows * H * 2
-        total = FLAGS + 2 * self.buf_bytes
+        # fp8 experts: the dispatched rows are e4m3 (first half of the
+        # receive buffer) with their scale columns [H/128, max_rows] here
+        self.sf_bytes = ((H // 128) * max_rows + 15) // 16 * 16 if self.fp8 else 0
+        total = FLAGS + 2 * self.buf_bytes + self.sf_bytes
         p = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             _native.check(lib.ib_sym_alloc(total, ctypes.byref(p)), "ib_sym_alloc")
@@ -110,6 +116,9 @@ class EPMoE:
     def _ret_view(self, base: int) -> int:
         return base + FLAGS + self.buf_bytes
 
+    def _sf_view(self, base: int) -> int:
+        return base + FLAGS + 2 * self.buf_bytes
+
     def _tensor_at(self, ptr: int, rows: int) -> torch.Tensor:
         from infera_b200.parallel.symmem import _View
 
@@ -141,10 +150,36 @@ class EPMoE:
         recv_peers = (ctypes.c_void_p * 8)(*[self._recv_view(b) for b in self.peers])
         flagA = (ctypes.c_void_p * 8)(*[b for b in self.peers])
         ctr = self.ctr.data_ptr()
-        _native.check(lib.ib_ep_dispatch(xs.data_ptr(), R, H, offsets.data_ptr(), E, W, dst_off.data_ptr(),
-                                         recv_peers, flagA, ctypes.c_void_p(ctr), stream), "ib_ep_dispatch")
-        _native.check(lib.ib_ep_wait(ctypes.c_void_p(self.base), target, sc.status.data_ptr(), stream), "ib_ep_wait")
-        recv = self._tensor_at(self._recv_view(self.base), self.max_rows)
+        bn = K.grouped_bn(R, El)
+        if self.fp8:
+            from infera_b200.ops import fp8
+
+            bn = min(192, max(32, ((bn + 31) // 32) * 32))
+            # the sender quantises (half the bytes cross NVLink) and the
+            # rows land with their scales where the up projection reads them
+            q, qsf = fp8.quant_act(xs)
+            sf_peers = (ctypes.c_void_p * 8)(*[self._sf_view(b) for b in self.peers])
+            _native.check(lib.ib_ep_dispatch_q(q.data_ptr(), R, H, qsf.data_ptr(), qsf.stride(0), H // 128,
+                                               offsets.data_ptr(), E, W, dst_off.data_ptr(), recv_peers, sf_peers,
+                                               self.max_rows, flagA, ctypes.c_void_p(ctr), stream),
+                          "ib_ep_dispatch_q")
+            w13, w13sf, ldw13 = self.w13.q.data_ptr(), self.w13.sf.data_ptr(), self.w13.q.stride(0)
+            a13, sf13 = self._recv_view(self.base), self._sf_view(self.base)
+            n13 = self.w13.q.shape[0] // El
+        else:
+            _native.check(lib.ib_ep_dispatch(xs.data_ptr(), R, H, offsets.data_ptr(), E, W, dst_off.data_ptr(),
+                                             recv_peers, flagA, ctypes.c_void_p(ctr), stream), "ib_ep_dispatch")
+            w13, w13sf, ldw13 = self.w13.data_ptr(), None, self.w13.stride(1)
+            a13, sf13 = self._recv_view(self.base), None
+            n13 = self.w13.shape[1]
+        # up projection (SwiGLU) over the received rows; its TMA producer and
+        # scale stagers wait for the dispatch's arrivals themselves
+        tab, num, cap = K.grouped_tiles(loc_off, El, n13, bn, self.max_rows)
+        act = torch.empty(self.max_rows, n13 // 2, dtype=torch.bfloat16, device=x.device)
+        _native.check(lib.ib_gemm_grouped_wait(a13, sf13, self.max_rows, w13, w13sf, act.data_ptr(), self.max_rows,
+                                               n13, H, El, H, ldw13, act.stride(0), 1,
+                                               tab.data_ptr(), num.data_ptr(), bn, cap, ctypes.c_void_p(self.base),
+                                               target, sc.status.data_ptr(), stream), "ib_gemm_grouped_wait")
         # down projection whose epilogue stores each expert-output row straight
         # into its source's return buffer (the return all-to-all fused in)
         _native.check(lib.ib_ep_row_map(self.counts_all.data_ptr(), W, E, self.rank, loc_off.data_ptr(),
@@ -152,17 +187,11 @@ class EPMoE:
                       "ib_ep_row_map")
         ret_peers = (ctypes.c_void_p * 8)(*[self._ret_view(b) for b in self.peers])
         flagB = (ctypes.c_void_p * 8)(*[b + 4 for b in self.peers])
-        bn = K.grouped_bn(R, El)
         if self.fp8:
-            from infera_b200.ops import fp8
-
-            bn = min(192, max(32, ((bn + 31) // 32) * 32))
-            act = fp8.gemm_fp8_grouped(recv, self.w13, El, loc_off, swiglu=True, bn=bn)
             a_q, a_sf = fp8.quant_act(act)
             w2q, w2sf, sf_ld = self.w2.q, self.w2.sf.data_ptr(), a_sf.stride(0)
             a_ptr, sfa_ptr, lda = a_q.data_ptr(), a_sf.data_ptr(), a_q.stride(0)
         else:
-            act = K.gemm_grouped(recv, self.w13, loc_off, swiglu=True, bn=bn)
             w2q, w2sf, sf_ld = self.w2, None, 0
             a_ptr, sfa_ptr, lda = act.data_ptr(), None, act.stride(0)
         tab, num, cap = K.grouped_tiles(loc_off, El, H, bn, self.max_rows)

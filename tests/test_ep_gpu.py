@@ -36,6 +36,14 @@ def test_ep_fused_single_rank():
     assert res["ranks"][0]["fused"]
 
 
+def test_ep_fused_single_rank_fp8():
+    """fp8 experts: the sender quantises, ib_ep_dispatch_q moves e4m3 rows
+    with their scale columns, and the up projection waits for them inside
+    its own producer (ib_gemm_grouped_wait)."""
+    res = _run(1, 29774, "--fused", "--fp8")
+    assert res["ranks"][0]["fused"]
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_ep_nccl_two_ranks():
     _run(2, 29772)
