@@ -255,3 +255,21 @@ class BusRequestServer:
                 return False
             await asyncio.sleep(0.01)
         return True
+
+
+def local_http_handler(base_url: str, client=None) -> Handler:
+    """Worker side of the bus transport: forward each request to this
+    worker's own OpenAI HTTP server and relay its frames (the same SSE
+    framing and error mapping as the router's HTTP transport)."""
+    from infera_b200.router.transport import HttpTransport
+
+    http = HttpTransport(client)
+
+    class _Local:
+        url = base_url.rstrip("/")
+
+    async def handler(path: str, body: dict, headers: dict):
+        async for item in http.stream(_Local, path, body, headers):
+            yield item
+
+    return handler

@@ -46,7 +46,8 @@ def build_payload(args, tokenizer) -> dict:
     w = WorkerInfo(worker_id=wid, url=f"http://{host}:{args.port}", model_name=args.served_model_name or args.model,
                    engine=EngineType.INFERA_B200, disagg_mode=DisaggMode(args.disagg_mode), disagg_meta=meta,
                    kv_events_endpoint=args.kv_events_endpoint, kv_block_size=args.page_size, kv=kv,
-                   dp_rank=args.dp_rank, dp_size=args.dp_size)
+                   dp_rank=args.dp_rank, dp_size=args.dp_size,
+                   request_transport="bus" if getattr(args, "nats_url", None) else "http")
     return w.to_payload()
 
 
@@ -80,6 +81,8 @@ def parse_args(argv=None):
     p.add_argument("--dp-rank", type=int, default=None,
                    help="data-parallel attention rank this worker serves (registered for DP-rank routing)")
     p.add_argument("--dp-size", type=int, default=1)
+    p.add_argument("--nats-url", default=None,
+                   help="also serve requests over NATS (infera.req.<worker token>); registers request_transport=bus")
     p.add_argument("--log-level", default="info")
     return p.parse_args(argv)
 
@@ -205,6 +208,18 @@ async def run_worker(args) -> None:
     while not server.started:
         await asyncio.sleep(0.05)
     payload = build_payload(args, tok)
+    bus_srv = bus = None
+    if args.nats_url:
+        from infera_b200.common.nats_wire import NatsBus
+        from infera_b200.common.request_transport import BusRequestClient, BusRequestServer, local_http_handler
+
+        bus = await NatsBus(args.nats_url, name=payload["worker_id"]).connect()
+
+        class _W:
+            worker_id = payload["worker_id"]
+
+        bus_srv = BusRequestServer(bus, BusRequestClient.token(_W), local_http_handler(f"http://127.0.0.1:{args.port}"))
+        await bus_srv.start()
     reg = None
     hb = None
     if args.etcd_endpoint:
@@ -231,6 +246,9 @@ async def run_worker(args) -> None:
         hb.cancel()
     if reg is not None:
         await reg.deregister()
+    if bus_srv is not None:   # NATS streams drain (and hand back) like the HTTP ones
+        await bus_srv.drain(args.drain_timeout, args.handback_after)
+        await bus_srv.stop()
     clean = await aeng.drain(args.drain_timeout, args.handback_after)
     logger.info("drain %s (inflight=%d)", "clean" if clean else "timed out", aeng.inflight)
     await shutdown_engine()
@@ -238,6 +256,8 @@ async def run_worker(args) -> None:
     await serve_task
     if reg is not None:
         await reg.close()
+    if bus is not None:
+        await bus.close()
 
 
 async def _flush_loop(pub) -> None:

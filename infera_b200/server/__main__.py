@@ -55,6 +55,15 @@ def build_router_stack(args, registry=None, transport=None):
     registry.on_worker_removed(lambda w: (policy.on_worker_removed(w.worker_id), breaker.forget(w.worker_id)))
     kw = dict(breaker=breaker, request_max_retries=args.request_max_retries, migration_limit=args.migration_limit,
               metrics=metrics)
+    if transport is None and getattr(args, "request_transport", "http") == "nats":
+        from infera_b200.common.nats_wire import NatsBus
+        from infera_b200.common.request_transport import BusRequestClient
+        from infera_b200.router.transport import RoutingTransport
+
+        # connected by ``serve`` inside the event loop
+        transport = RoutingTransport(bus_client=BusRequestClient(NatsBus(args.nats_url),
+                                                                 idle_timeout=args.nats_idle_timeout,
+                                                                 max_duration=args.nats_max_duration))
     if transport is not None:
         kw["transport"] = transport
     router_cls = DirectRouter if args.router_mode == "direct" else AutoRouter
@@ -81,6 +90,9 @@ async def serve(args) -> None:
     from infera_b200.server.app import build_app
 
     state = build_router_stack(args)
+    bus = getattr(getattr(state.router.transport, "bus", None), "bus", None)
+    if bus is not None:
+        await bus.connect()
     await state.registry.start()
     app = build_app(state)
     cfg = uvicorn.Config(app, host=args.host, port=args.port, log_level=args.log_level, access_log=False)

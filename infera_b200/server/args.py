@@ -28,7 +28,11 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--etcd-prefix", default="/infera/workers/")
     p.add_argument("--k8s-label-selector", default=_env("INFERA_K8S_LABEL_SELECTOR"))
     p.add_argument("--k8s-namespace", default=None)
-    p.add_argument("--request-transport", choices=("http",), default="http")
+    p.add_argument("--request-transport", choices=("http", "nats"), default=_env("INFERA_REQUEST_TRANSPORT", "http"),
+                   help="nats: workers registered with request_transport=bus are reached over NATS, others over HTTP")
+    p.add_argument("--nats-url", default=_env("INFERA_NATS_URL", "nats://127.0.0.1:4222"))
+    p.add_argument("--nats-idle-timeout", type=float, default=900.0)
+    p.add_argument("--nats-max-duration", type=float, default=None)
     p.add_argument("--router-backend", choices=("python", "native"), default=_env("INFERA_ROUTER_BACKEND", "python"))
     p.add_argument("--router-mode", choices=("auto", "direct"), default=_env("INFERA_ROUTER_MODE", "auto"))
     p.add_argument("--router-policy", choices=POLICY_NAMES, default="kv-aware")

@@ -203,3 +203,109 @@ def test_bus_drain_hands_back_streams():
     assert ok and stats["handed_back"] == 1
     assert frames[-1][0] == ERROR and frames[-1][2] == DRAINING_NOTICE.encode()
     assert refused[0][1] == 429
+
+
+def test_nats_wire_client_against_a_protocol_broker():
+    """The NATS protocol client: pub/sub with headers and reply subjects,
+    wildcard subscriptions, request/reply, no-responders, and the bus
+    request transport (streamed frames, admission, cancel) over it."""
+    from infera_b200.common.nats_wire import NatsBus, parse_headers
+    from tests.nats_stub import Broker, matches
+
+    assert matches("a.*.c", "a.b.c") and matches("a.>", "a.b.c") and not matches("a.*", "a.b.c")
+    assert parse_headers(b"NATS/1.0 503\r\n\r\n") == {"status": "503"}
+
+    async def go():
+        br = await Broker().start()
+        url = f"nats://127.0.0.1:{br.port}"
+        a, b = await NatsBus(url).connect(), await NatsBus(url).connect()
+        got = []
+
+        async def on(m):
+            got.append(m)
+
+        unsub = await b.subscribe("infera.kv.events.*", on)
+        await asyncio.sleep(0.02)
+        await a.publish("infera.kv.events.w1", b"\x00\x01payload", headers={"rs-type": "data", "rs-status": "200"},
+                        reply="r.1")
+        await a.publish("infera.kv.events.w2", b"plain")
+        await a.publish("other.subject", b"x")
+        for _ in range(100):
+            if len(got) >= 2:
+                break
+            await asyncio.sleep(0.01)
+        assert [m.data for m in got] == [b"\x00\x01payload", b"plain"]
+        assert got[0].headers == {"rs-type": "data", "rs-status": "200"} and got[0].reply == "r.1"
+        unsub()
+
+        async def echo(m):
+            await b.publish(m.reply, m.data[::-1])
+
+        await b.subscribe("svc.echo", echo)
+        await asyncio.sleep(0.02)
+        rs = await asyncio.gather(*[a.request("svc.echo", f"req{i}".encode(), timeout=2.0) for i in range(5)])
+        assert [m.data for m in rs] == [f"req{i}".encode()[::-1] for i in range(5)]
+        nr = await a.request("svc.nobody", b"", timeout=2.0)   # answered by the broker: no responders
+        assert nr.headers.get("status") == "503" and nr.data == b""
+
+        # the bus request transport over NATS
+        async def handler(path, body, headers):
+            for i in range(3):
+                yield DATA, 200, f"data: {i}\n\n".encode()
+            yield DONE, 200, b""
+
+        srv = BusRequestServer(b, BusRequestClient.token(_worker(0)), handler)
+        await srv.start()
+        await asyncio.sleep(0.02)
+        cl = BusRequestClient(a, idle_timeout=2.0)
+        frames = [x async for x in cl.stream(_worker(0), "/v1/completions", {"stream": True})]
+        assert [k for k, _, _ in frames] == [DATA, DATA, DATA, DONE]
+        assert frames[0][2] == b"data: 0\n\n"
+        cl.admit_timeout = 0.5
+        frames = [x async for x in cl.stream(_worker(7), "/v1/completions", {})]   # nobody serves worker 7
+        assert frames[0][1] == 429
+        await srv.stop()
+        await a.close()
+        await b.close()
+        await br.stop()
+
+    asyncio.run(go())
+
+
+def test_router_reaches_a_bus_worker_over_nats():
+    """Router side: RoutingTransport sends a worker registered with
+    request_transport=bus over NATS; worker side: BusRequestServer relays to
+    the worker's own HTTP server (here an httpx mock of it)."""
+    import httpx
+
+    from infera_b200.common.nats_wire import NatsBus
+    from infera_b200.common.request_transport import local_http_handler
+    from infera_b200.router.transport import RoutingTransport
+    from tests.nats_stub import Broker
+
+    sse = b'data: {"choices":[{"text":"a"}]}\n\ndata: {"choices":[{"text":"b"}]}\n\ndata: [DONE]\n\n'
+
+    def app(req: httpx.Request) -> httpx.Response:
+        assert req.url.path == "/v1/completions"
+        return httpx.Response(200, content=sse, headers={"content-type": "text/event-stream"})
+
+    async def go():
+        br = await Broker().start()
+        url = f"nats://127.0.0.1:{br.port}"
+        wbus, rbus = await NatsBus(url).connect(), await NatsBus(url).connect()
+        w = _worker(3)
+        w.request_transport = "bus"
+        handler = local_http_handler("http://worker.local", client=httpx.AsyncClient(transport=httpx.MockTransport(app)))
+        srv = BusRequestServer(wbus, BusRequestClient.token(w), handler)
+        await srv.start()
+        await asyncio.sleep(0.02)
+        rt = RoutingTransport(bus_client=BusRequestClient(rbus, idle_timeout=2.0))
+        frames = [x async for x in rt.stream(w, "/v1/completions", {"stream": True, "prompt": "x"})]
+        assert [k for k, _, _ in frames] == [DATA, DATA, DATA, DONE]
+        assert frames[-2][2] == b"data: [DONE]\n\n" and srv.stats["served"] == 1
+        await srv.stop()
+        await wbus.close()
+        await rbus.close()
+        await br.stop()
+
+    asyncio.run(go())
