@@ -56,6 +56,12 @@ def test_ep_fused_two_ranks():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_fused_two_ranks_fp8():
+    res = _run(2, 29778, "--fused", "--fp8")
+    assert all(rk["fused"] for rk in res["ranks"])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("fused", [False, True])
 def test_dp_attention_ep_two_gpus(fused):
     env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
