@@ -94,8 +94,7 @@ def run_e2e_fleet(engine, *, model: str, rank: int, world: int, barrier, session
     from infera_b200.engine.core_ipc import EngineCoreServer, ipc_pair
     from infera_b200.engine.kv_events import KvEventPublisher
 
-    logdir = logdir or (os.path.join(ROOT, "gpurun_out") if os.path.isdir(os.path.join(ROOT, "gpurun_out"))
-                        else "/tmp")
+    logdir = logdir or os.environ.get("INFERA_LOG_DIR", "/tmp")   # worker / router logs
     procs = []
     th = None
     stop = threading.Event()

@@ -73,7 +73,7 @@ def main(argv=None) -> None:
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--max-tokens", type=int, default=32)
     a = ap.parse_args(argv)
-    logdir = os.path.join(ROOT, "gpurun_out") if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "/tmp"
+    logdir = os.environ.get("INFERA_LOG_DIR", "/tmp")   # worker / router logs
     etcd, router = free_tcp_port(), free_tcp_port()
     pport, dport = free_tcp_port(), free_tcp_port()
     kv_ep = f"ipc:///tmp/infera-b200-pd-{os.getpid()}"

@@ -117,7 +117,7 @@ def run_reference(args) -> dict:
         if world > 1:
             dist.barrier()
 
-    logdir = os.path.join(ROOT, "gpurun_out") if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "/tmp"
+    logdir = os.environ.get("INFERA_LOG_DIR", "/tmp")   # worker / router logs
     procs = []
     t_setup = time.time()
     try:
