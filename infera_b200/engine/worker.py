@@ -208,7 +208,7 @@ async def run_worker(args) -> None:
     while not server.started:
         await asyncio.sleep(0.05)
     payload = build_payload(args, tok)
-    bus_srv = bus = None
+    bus_srv = bus = relay = None
     if args.nats_url:
         from infera_b200.common.nats_wire import NatsBus
         from infera_b200.common.request_transport import BusRequestClient, BusRequestServer, local_http_handler
@@ -220,6 +220,11 @@ async def run_worker(args) -> None:
 
         bus_srv = BusRequestServer(bus, BusRequestClient.token(_W), local_http_handler(f"http://127.0.0.1:{args.port}"))
         await bus_srv.start()
+        if args.kv_events_endpoint:   # KV events onto the bus as well
+            from infera_b200.kv.nats_relay import KvEventNatsRelay
+
+            relay = KvEventNatsRelay(bus, payload["worker_id"], args.kv_events_endpoint)
+            relay.start()
     reg = None
     hb = None
     if args.etcd_endpoint:
@@ -256,6 +261,8 @@ async def run_worker(args) -> None:
     await serve_task
     if reg is not None:
         await reg.close()
+    if relay is not None:
+        await relay.stop()
     if bus is not None:
         await bus.close()
 

@@ -10,7 +10,9 @@ indexed (``kv_cache_spec_kind`` absent, ``full_attention``,
 ``mla_attention`` or ``sink_full_attention``). Behaviour of
 ``infera/router/kv_event/client.py:104-350``.
 
-Transports: ZMQ SUB per worker endpoint (per DP rank: port + rank), or
+Transports: ZMQ SUB per worker endpoint (per DP rank: port + rank), one
+NATS subscription to ``infera.kv.events.>`` (:meth:`attach_nats`; workers'
+relays republish their batches on ``infera.kv.events.<worker token>``), or
 :meth:`feed` for in-process publishers.
 """
 
@@ -26,6 +28,12 @@ from infera_b200.utils.hashing import ROUTER_SEED, chain_hashes
 logger = logging.getLogger(__name__)
 
 TOPIC = b"kv-events"
+NATS_SUBJECT = "infera.kv.events."
+
+
+def worker_token(worker_id: str) -> str:
+    """A worker id as one NATS subject token (the bus transport's form)."""
+    return str(worker_id).replace(".", "_").replace(":", "_")
 INDEXABLE = frozenset({"full_attention", "mla_attention", "sink_full_attention"})
 MAX_BACKOFF = 5.0
 
@@ -177,6 +185,29 @@ class KvEventClient:
             finally:
                 sock.close(linger=0)
 
+    # ------------------------------------------------------------------ NATS
+    async def attach_nats(self, bus) -> None:
+        """Receive every worker's KV-event batches from the bus (core NATS,
+        subject ``infera.kv.events.<worker token>``)."""
+
+        async def on_batch(m) -> None:
+            token = m.subject[len(NATS_SUBJECT):]
+            wv = next((w for w in self.workers.values() if worker_token(w.worker_id) == token), None)
+            if wv is None:
+                return
+            try:
+                batch = decoder_for_engine(wv.engine).decode(m.data)
+            except Exception as e:
+                self.stats["decode_errors"] += 1
+                logger.warning("kv decode failed for %s: %s", wv.worker_id, e)
+                return
+            for ev in batch.events:
+                self._handle(wv, ev, batch.attn_dp_rank)
+
+        self._nats_unsub = await bus.subscribe(NATS_SUBJECT + ">", on_batch)
+
     async def aclose(self) -> None:
         for wv in self.workers.values():
             self._cancel(wv)
+        if getattr(self, "_nats_unsub", None) is not None:
+            self._nats_unsub()

@@ -36,7 +36,7 @@ def build_router_stack(args, registry=None, transport=None):
     policy = build_policy(args.router_policy, tokenizer=tok, overlap_weight=args.kv_overlap_weight,
                           prefill_overlap_weight=args.kv_prefill_overlap_weight,
                           decode_overlap_weight=args.kv_decode_overlap_weight, metrics=metrics,
-                          use_zmq=transport is None)
+                          use_zmq=transport is None and getattr(args, "kv_event_transport", "zmq") == "zmq")
     breaker = CircuitBreaker(args.breaker_failure_threshold, args.breaker_cooldown_s, args.breaker_max_cooldown_s,
                              on_change=metrics.breaker_changed)
     if registry is None:
@@ -93,6 +93,13 @@ async def serve(args) -> None:
     bus = getattr(getattr(state.router.transport, "bus", None), "bus", None)
     if bus is not None:
         await bus.connect()
+    kv = getattr(state.policy, "kv_client", None)
+    if args.kv_event_transport == "nats" and kv is not None:
+        if bus is None:
+            from infera_b200.common.nats_wire import NatsBus
+
+            bus = await NatsBus(args.nats_url).connect()
+        await kv.attach_nats(bus)
     await state.registry.start()
     app = build_app(state)
     cfg = uvicorn.Config(app, host=args.host, port=args.port, log_level=args.log_level, access_log=False)

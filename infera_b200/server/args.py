@@ -36,7 +36,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--router-backend", choices=("python", "native"), default=_env("INFERA_ROUTER_BACKEND", "python"))
     p.add_argument("--router-mode", choices=("auto", "direct"), default=_env("INFERA_ROUTER_MODE", "auto"))
     p.add_argument("--router-policy", choices=POLICY_NAMES, default="kv-aware")
-    p.add_argument("--kv-event-transport", choices=("zmq",), default="zmq")
+    p.add_argument("--kv-event-transport", choices=("zmq", "nats"), default=_env("INFERA_KV_EVENT_TRANSPORT", "zmq"),
+                   help="nats: KV-event batches arrive on infera.kv.events.> (workers run the NATS relay)")
     p.add_argument("--router-tokenizer-path", default=_env("INFERA_ROUTER_TOKENIZER_PATH"))
     p.add_argument("--kv-overlap-weight", type=float, default=1.0)
     p.add_argument("--kv-prefill-overlap-weight", type=float, default=None)

@@ -309,3 +309,51 @@ def test_router_reaches_a_bus_worker_over_nats():
         await br.stop()
 
     asyncio.run(go())
+
+
+def test_kv_events_relayed_over_nats():
+    """Engine KV events: ZMQ publisher -> worker relay -> NATS
+    infera.kv.events.<worker token> -> the router's KV client, which then
+    holds the worker's prefix blocks."""
+    from infera_b200.common.nats_wire import NatsBus
+    from infera_b200.engine.kv_events import KvEventPublisher
+    from infera_b200.kv.nats_relay import KvEventNatsRelay
+    from infera_b200.router.kv_event.client import KvEventClient
+    from tests.nats_stub import Broker
+
+    async def go():
+        br = await Broker().start()
+        url = f"nats://127.0.0.1:{br.port}"
+        wbus, rbus = await NatsBus(url).connect(), await NatsBus(url).connect()
+        port = free_tcp_port()
+        pub = KvEventPublisher(f"tcp://127.0.0.1:{port}")
+        w = WorkerInfo(worker_id="10.0.0.5:9000", url="http://10.0.0.5:9000", model_name="m", kv_block_size=4)
+        kv = KvEventClient(use_zmq=False)
+        kv.on_worker_added(w)
+        await kv.attach_nats(rbus)
+        relay = KvEventNatsRelay(wbus, w.worker_id, f"tcp://127.0.0.1:{port}")
+        relay.start()
+        await asyncio.sleep(0.3)   # ZMQ slow joiner
+        pub("BlockStored", {"block_hashes": [11, 12], "parent_block_hash": None,
+                            "token_ids": list(range(8)), "block_size": 4})
+        pub.flush()
+        for _ in range(200):
+            if len(kv.cache_view(w.worker_id)) >= 2:
+                break
+            await asyncio.sleep(0.01)
+        assert len(kv.cache_view(w.worker_id)) == 2 and relay.relayed >= 1
+        pub("BlockRemoved", {"block_hashes": [12]})
+        pub.flush()
+        for _ in range(200):
+            if len(kv.cache_view(w.worker_id)) == 1:
+                break
+            await asyncio.sleep(0.01)
+        assert len(kv.cache_view(w.worker_id)) == 1
+        await relay.stop()
+        pub.close()
+        await kv.aclose()
+        await wbus.close()
+        await rbus.close()
+        await br.stop()
+
+    asyncio.run(go())
