@@ -1,0 +1,91 @@
+"""More engine behaviour on CPU: stop tokens, min_tokens, abort, seeded
+sampling, duplicate ids, the per-sequence prefill chunk cap, the sequence
+limit, shared prefix pages and cache clearing."""
+
+import pytest
+import torch
+
+from infera_b200.engine.block_manager import BlockManager
+from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
+from infera_b200.engine.request import SamplingParams
+
+
+def _engine(**kw):
+    kw.setdefault("num_pages", 64)
+    return LLMEngine(EngineConfig(model="tiny-dense", use_cuda_graphs=False, **kw), device="cpu")
+
+
+def _prompt(seed, n=20):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, 1024, (n,), generator=g).tolist()
+
+
+def test_stop_token_and_min_tokens():
+    eng = _engine()
+    p = _prompt(1)
+    free = eng.generate([p], SamplingParams(max_tokens=8, ignore_eos=True))[0]
+    stop = free[2]
+    first = free.index(stop)
+    out = eng.generate([p], SamplingParams(max_tokens=8, ignore_eos=True, stop_token_ids=[stop]))[0]
+    assert out == free[:first + 1]
+    # min_tokens defers the stop check
+    out = eng.generate([p], SamplingParams(max_tokens=8, ignore_eos=True, stop_token_ids=[stop],
+                                           min_tokens=first + 2))[0]
+    assert len(out) > first + 1 and out == free[:len(out)]
+
+
+def test_abort_frees_pages_and_finishes():
+    eng = _engine()
+    free0 = eng.bm.num_free()
+    eng.add_request("a", _prompt(2, 40), SamplingParams(max_tokens=50, ignore_eos=True))
+    eng.step()
+    assert eng.bm.num_free() < free0
+    assert eng.abort_request("a")
+    assert not eng.has_unfinished()
+    assert not eng.abort_request("a")          # already gone
+    with pytest.raises(ValueError):
+        eng.add_request("b", [1, 2, 3])
+        eng.add_request("b", [1, 2, 3])        # duplicate id
+
+
+def test_seeded_sampling_is_reproducible():
+    eng = _engine()
+    p = _prompt(3)
+    sp = SamplingParams(max_tokens=6, ignore_eos=True, temperature=1.0, seed=1234)
+    a = eng.generate([p], sp)[0]
+    b = eng.generate([p], sp)[0]
+    c = eng.generate([p], SamplingParams(max_tokens=6, ignore_eos=True, temperature=1.0, seed=99))[0]
+    assert a == b and len(a) == 6
+    assert a != c   # 6 tokens from a 1024-token vocabulary at temperature 1
+
+
+def test_long_prefill_cap_and_sequence_limit():
+    eng = _engine(max_batched_tokens=256, max_num_seqs=2, long_prefill_threshold=32)
+    for i in range(3):
+        eng.add_request(f"r{i}", _prompt(10 + i, 100), SamplingParams(max_tokens=2, ignore_eos=True))
+    sched = eng.scheduler.schedule()
+    assert len(sched.prefills) == 2                      # max_num_seqs
+    assert all(c.num_tokens <= 32 for c in sched.prefills)
+    for c in sched.prefills:                             # leave the scheduler consistent
+        eng.scheduler.abort(c.req.request_id)
+
+
+def test_shared_prefix_pages_are_refcounted():
+    bm = BlockManager(num_pages=8, page_size=4)
+    toks = list(range(12))
+    a = bm.allocate_prompt(toks + [100], 13)
+    bm.commit_full_pages(a, toks + [100], 12)
+    b = bm.allocate_prompt(toks + [200], 13)
+    assert b.num_cached_tokens == 12 and b.pages[:3] == a.pages[:3]
+    bm.free(a)
+    # b still holds the shared pages: a new prompt cannot take them
+    c = bm.allocate_prompt(list(range(500, 520)), 20)
+    assert c is None or not set(c.pages) & set(b.pages)
+    bm.free(b)
+    if c is not None:
+        bm.free(c)
+    events = []
+    bm.event_sink = lambda k, p: events.append(k)
+    bm.clear_cache()
+    # every page but the reserved padding page 0 is free again
+    assert bm.cached_hashes() == [] and bm.num_free() == 8 - bm.reserved and events == ["AllBlocksCleared"]
