@@ -34,6 +34,8 @@
 //
 // Reference parity: the reference delegates all GEMMs to its engines
 // (vLLM/hipBLASLt); there is no GEMM source in it to mirror.
+#include <cstdlib>
+
 #include "sm100.cuh"
 #include "tma_host.h"
 
@@ -58,6 +60,16 @@ constexpr int MAX_BN_FP8 = 192;
 constexpr int BK_FP8 = 128;           // one 128-byte swizzle atom of e4m3
 constexpr int SF_COL0 = 2 * MAX_BN_FP8;  // scale slots after the accumulators
 constexpr int SF_SLOT = 16;              // per stage: A scales at +0 (4), B at +8 (8)
+// Small token tiles (bn <= 64, decode-size GEMMs that stream the weights):
+// Q slots of 64 rows let the same shared memory hold an 8-deep ring, which
+// keeps more weight bytes in flight per SM. fp8 scale slots then end at
+// TMEM column SF_COL0 + 8 * SF_SLOT = 512.
+constexpr int DEEP_BN = 64;
+constexpr int STAGES_DEEP = 8;
+constexpr int Q_STAGE_DEEP = DEEP_BN * 128;   // 64 rows x 128 bytes (bf16 or e4m3 K atom)
+static_assert(STAGES_DEEP * (P_STAGE + Q_STAGE_DEEP) <= (SMEM_BF16 > SMEM_FP8 ? SMEM_BF16 : SMEM_FP8),
+              "the deep ring fits the shared memory the kernel is launched with");
+static_assert(SF_COL0 + STAGES_DEEP * SF_SLOT <= TMEM_COLS, "fp8 scale slots of the deep ring fit in TMEM");
 
 enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_ATOMIC_F32 = 2 };
 constexpr int kMaxPeers = 8;
@@ -309,14 +321,15 @@ __device__ __forceinline__ int tile_qrow(const Params& p, int t, int qt) {
   return p.grouped ? p.gtab[t].z : qt * p.bn;
 }
 
-template <bool FP8>
+// DEEP: the 8-deep ring with 64-row Q slots (launched only when p.bn <= DEEP_BN)
+template <bool FP8, bool DEEP>
 __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                 const Params p) {
   constexpr int kBK = FP8 ? BK_FP8 : BK;          // K elements per stage (128 bytes per row)
   constexpr int kAccCols = FP8 ? MAX_BN_FP8 : MAX_BN;
-  constexpr int kStages = FP8 ? STAGES_FP8 : STAGES;
-  constexpr int kQStage = FP8 ? Q_STAGE_FP8 : Q_STAGE;
+  constexpr int kStages = DEEP ? STAGES_DEEP : (FP8 ? STAGES_FP8 : STAGES);
+  constexpr int kQStage = DEEP ? Q_STAGE_DEEP : (FP8 ? Q_STAGE_FP8 : Q_STAGE);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sP = smem;
@@ -684,21 +697,33 @@ struct Plan {
 
 static long long* g_gemm_trace = nullptr;
 
+template <bool FP8, bool DEEP>
+inline int launch_gemm_variant(const CUtensorMap& tmP, const CUtensorMap& tmQ, const Params& p, int grid,
+                               cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaFuncSetAttribute(gemm_kernel<FP8, DEEP>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_set[dev] = true;
+  }
+  gemm_kernel<FP8, DEEP><<<grid, FP8 ? NUM_THREADS_FP8 : NUM_THREADS, SMEM_BYTES, stream>>>(tmP, tmQ, p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
 template <bool FP8>
 inline int launch_gemm(const CUtensorMap& tmP, const CUtensorMap& tmQ, const Params& p_in, int grid,
                        cudaStream_t stream) {
   Params p = p_in;
   p.trace = g_gemm_trace;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(gemm_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    attr_set[dev] = true;
-  }
-  gemm_kernel<FP8><<<grid, FP8 ? NUM_THREADS_FP8 : NUM_THREADS, SMEM_BYTES, stream>>>(tmP, tmQ, p);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 0 : static_cast<int>(e);
+  // INFERA_GEMM_DEEP=0 keeps small tiles on the shallow ring (for comparison)
+  static const bool deep = [] {
+    const char* v = getenv("INFERA_GEMM_DEEP");
+    return v == nullptr || v[0] != '0';
+  }();
+  if (deep && p.bn <= DEEP_BN) return launch_gemm_variant<FP8, true>(tmP, tmQ, p, grid, stream);
+  return launch_gemm_variant<FP8, false>(tmP, tmQ, p, grid, stream);
 }
 
 // Split-K factor for a plan whose tiles are set: minimise waves/split (time
