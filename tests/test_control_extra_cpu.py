@@ -123,3 +123,17 @@ def test_arch_gate():
 
     assert is_supported("sm_100a") or is_supported("sm_100")
     assert not is_supported(None) and not is_supported("sm_80")
+
+
+def test_worker_record_advertises_its_request_transport():
+    from infera_b200.engine.worker import build_payload, parse_args
+    from infera_b200.utils.tokenizer import load_tokenizer
+
+    tok = load_tokenizer(None, vocab_size=1024)
+    a = parse_args(["--model", "tiny-dense", "--port", "9100", "--host", "127.0.0.1"])
+    assert build_payload(a, tok)["request_transport"] == "http"
+    a = parse_args(["--model", "tiny-dense", "--port", "9100", "--host", "127.0.0.1", "--nats-url",
+                    "nats://127.0.0.1:4222", "--disagg-mode", "decode", "--kv-push-endpoint", "tcp://127.0.0.1:7000"])
+    d = build_payload(a, tok)
+    assert d["request_transport"] == "bus" and d["worker_id"] == "127.0.0.1:9100"
+    assert d["disagg_mode"] == "decode" and d["disagg_meta"]["params"]["kv_endpoint"] == "tcp://127.0.0.1:7000"
