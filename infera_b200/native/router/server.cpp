@@ -29,6 +29,7 @@
 
 #include "discovery.h"
 #include "net.h"
+#include "nats.h"
 #include "router.h"
 
 namespace ib {
@@ -50,6 +51,9 @@ struct Config {
   double breaker_cooldown = 5.0, breaker_max_cooldown = 60.0;
   int block_size = 16;
   bool verbose = false;
+  std::string request_transport = "http";   // "nats": workers registered with request_transport=bus over NATS
+  std::string nats_url = "nats://127.0.0.1:4222";
+  double nats_idle_timeout = 900.0;
 };
 
 static double now_s() {
@@ -164,6 +168,8 @@ class App {
   Breaker breaker;
   std::unique_ptr<Tokenizer> tok;
   std::unique_ptr<EtcdDiscovery> disc;
+  std::unique_ptr<NatsConn> nats;   // set with --request-transport nats
+  double nats_idle = 900.0;
   UpstreamPool ups;
 
   // metrics
@@ -267,9 +273,145 @@ class App {
   // Attempt one mixed-role worker. Returns 1 (response fully handled and
   // sent to the client), 0 (failed before any byte reached the client:
   // *fail holds the error response, *fail_status the breaker status).
+  static std::string bus_token(const std::string& worker_id) {
+    std::string t = worker_id;
+    for (char& c : t)
+      if (c == '.' || c == ':') c = '_';
+    return t;
+  }
+
+  static bool wants_bus(const Worker& w) {
+    const Value* v = w.record.get("request_transport");
+    return v != nullptr && v->is_str() && v->str() == "bus";
+  }
+
+  // The bus request transport (workers registered with request_transport=bus):
+  // admission on infera.admit.<token>, the request on infera.req.<token> with a
+  // private reply subject, frames whose rs-type header is data / done / error;
+  // after nats_idle seconds without a frame the request is cancelled on
+  // infera.cancel.<token> (three times) and answered 504.
+  int attempt_bus(int cfd, const Target& t, const std::vector<uint64_t>& blocks, const Value& body,
+                  const CacheHints& hints, const std::string& path, bool stream, const std::string& rid, bool keep,
+                  Reply* fail, int* fail_status) {
+    const Worker& w = *t.w;
+    const std::string token = bus_token(w.worker_id);
+    policy->started(t.route_key(), blocks);
+    struct Done {
+      App* a; const Target& t; const std::vector<uint64_t>& b;
+      ~Done() { a->policy->finished(t.route_key(), b); }
+    } done{this, t, blocks};
+    NatsMsg m;
+    {
+      const std::string inbox = "_INBOX." + rand_hex(12);
+      int sid = nats->subscribe(inbox);
+      nats->publish("infera.admit." + token, inbox, "", {});
+      bool ok = false;
+      if (nats->next(sid, 2.0, &m)) {
+        Value v;
+        std::string perr;
+        const Value* okv = parse_json(m.data, &v, &perr) ? v.get("ok") : nullptr;
+        ok = okv != nullptr && okv->truthy();
+      }
+      nats->unsubscribe(sid);
+      if (!ok) {
+        *fail = {429, err_json("worker at its admission limit")};
+        *fail_status = 429;
+        return 0;
+      }
+    }
+    std::string hdrs = "{}";
+    if (t.dp_rank >= 0 && t.w->dp_size > 1) hdrs = "{\"X-Data-Parallel-Rank\":\"" + std::to_string(t.dp_rank) + "\"}";
+    const std::string req = "{\"path\":\"" + path + "\",\"body\":" + forward_body(body, hints, w, false) +
+                            ",\"headers\":" + hdrs + "}";
+    const std::string inbox = "_INBOX." + rand_hex(12);
+    int sid = nats->subscribe(inbox);
+    nats->publish("infera.req." + token, inbox, req, {{"rid", rid}});
+    auto frame = [&](std::string* kind, int* status) -> bool {
+      if (!nats->next(sid, nats_idle, &m)) return false;
+      auto k = m.headers.find("rs-type");
+      auto st = m.headers.find("rs-status");
+      *kind = k == m.headers.end() ? "data" : k->second;
+      *status = st == m.headers.end() ? 200 : std::atoi(st->second.c_str());
+      return true;
+    };
+    auto cancel = [&]() {
+      for (int i = 0; i < 3; ++i) nats->publish("infera.cancel." + token, "", rid, {});
+    };
+    std::string kind;
+    int status = 0;
+    if (!frame(&kind, &status)) {
+      cancel();
+      nats->unsubscribe(sid);
+      *fail = {504, err_json("worker " + w.worker_id + " sent nothing for " + std::to_string(nats_idle) + " s")};
+      *fail_status = 0;
+      return 0;
+    }
+    if (kind == "error") {
+      nats->unsubscribe(sid);
+      *fail = {status ? status : 502, m.data.empty() ? err_json("worker " + w.worker_id + " failed") : m.data};
+      *fail_status = status;
+      return 0;
+    }
+    if (!stream) {
+      std::string raw;
+      while (kind == "data") {
+        raw += m.data;
+        if (!frame(&kind, &status)) {
+          kind = "timeout";
+          break;
+        }
+      }
+      nats->unsubscribe(sid);
+      if (kind != "done") {
+        if (kind == "timeout") cancel();
+        *fail = {kind == "timeout" ? 504 : (status ? status : 502), err_json("worker " + w.worker_id + " failed")};
+        *fail_status = kind == "timeout" ? 0 : status;
+        return 0;
+      }
+      send_simple(cfd, 200, "application/json", raw, {{"X-Infera-Request-Id", rid}}, keep);
+      breaker.success(w.worker_id);
+      return 1;
+    }
+    write_all(cfd, response_head(200, "text/event-stream", -1,
+                                 {{"X-Infera-Request-Id", rid}, {"Cache-Control", "no-cache"}}, keep));
+    breaker.success(w.worker_id);
+    bool broken = false, ended = false;
+    while (true) {
+      if (kind == "data") {
+        if (!m.data.empty() && !send_chunk(cfd, m.data.data(), m.data.size())) {
+          broken = true;
+          break;
+        }
+      } else if (kind == "done") {
+        ended = true;
+        break;
+      } else {   // error frame mid-stream (503: the worker is draining)
+        std::string what = status == 503 ? "is shutting down" : "failed";
+        std::string msg = "data: " + err_json("worker " + w.worker_id + " " + what + " mid-stream") + "\n\n";
+        send_chunk(cfd, msg.data(), msg.size());
+        if (status != 503) breaker.failure(w.worker_id, 0);
+        ended = true;
+        break;
+      }
+      if (!frame(&kind, &status)) {
+        cancel();
+        std::string msg = "data: " + err_json("worker " + w.worker_id + " timed out mid-stream") + "\n\n";
+        send_chunk(cfd, msg.data(), msg.size());
+        ended = true;
+        break;
+      }
+    }
+    if (broken) cancel();
+    nats->unsubscribe(sid);
+    if (ended && !broken) send_last_chunk(cfd);
+    return 1;
+  }
+
   int attempt(int cfd, const Target& t, const std::vector<uint64_t>& blocks, const Value& body,
               const CacheHints& hints, const std::string& path, bool stream, const std::string& rid, bool keep,
               Reply* fail, int* fail_status) {
+    if (nats && wants_bus(*t.w)) return attempt_bus(cfd, t, blocks, body, hints, path, stream, rid, keep, fail,
+                                                    fail_status);
     const Worker& w = *t.w;
     std::string fwd = forward_body(body, hints, w, false);
     Upstream u;
@@ -911,7 +1053,10 @@ int main(int argc, char** argv) {
     else if (a == "--block-size") cfg.block_size = std::atoi(v.c_str());
     else if (a == "--log-level") cfg.verbose = v == "debug" || v == "info";
     else if (a == "--help" || a == "-h") { usage(); return 0; }
-    else if (a == "--router-backend" || a == "--request-transport" || a == "--kv-event-transport" ||
+    else if (a == "--request-transport") cfg.request_transport = v;
+    else if (a == "--nats-url") cfg.nats_url = v;
+    else if (a == "--nats-idle-timeout") cfg.nats_idle_timeout = std::atof(v.c_str());
+    else if (a == "--router-backend" || a == "--kv-event-transport" ||
              a == "--enable-profiling" || a == "--enable-scaling-api") {
       // accepted for flag compatibility with the Python router; no effect here
     } else {
@@ -925,6 +1070,15 @@ int main(int argc, char** argv) {
     return 2;
   }
   App app(cfg);
+  if (cfg.request_transport == "nats") {
+    app.nats = std::make_unique<NatsConn>();
+    app.nats_idle = cfg.nats_idle_timeout;
+    std::string nerr;
+    if (!app.nats->connect(cfg.nats_url, &nerr)) {
+      std::fprintf(stderr, "[ib200_router] %s\n", nerr.c_str());
+      return 2;
+    }
+  }
   if (cfg.discovery == "etcd") {
     if (cfg.etcd_endpoint.empty()) {
       std::fprintf(stderr, "[ib200_router] --discovery-backend=etcd requires --etcd-endpoint\n");

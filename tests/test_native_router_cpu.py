@@ -194,3 +194,71 @@ def test_launcher_strips_python_only_flags():
     argv = ["--router-backend", "native", "--enable-profiling", "--kvd-socket-path", "/tmp/x", "--port", "9"]
     assert native_argv(argv) == ["--router-backend", "native", "--port", "9"]
     assert os.path.exists(router_binary())
+
+
+def test_native_router_bus_transport_over_nats(binary, tmp_path):
+    """--request-transport nats: a worker registered with
+    request_transport=bus is reached over NATS (admission, streamed frames,
+    unary reply, refusal at the admission limit)."""
+    import asyncio
+    import threading
+
+    from infera_b200.common.nats_wire import NatsBus
+    from infera_b200.common.request_transport import BusRequestClient, BusRequestServer
+    from infera_b200.common.worker_pool import WorkerInfo
+    from infera_b200.router.transport import DATA, DONE
+    from tests.nats_stub import Broker
+
+    seen = []
+
+    async def handler(path, body, headers):
+        seen.append((path, body))
+        if body.get("stream"):
+            for i in range(3):
+                yield DATA, 200, f'data: {{"choices":[{{"text":"t{i}"}}]}}\n\n'.encode()
+            yield DATA, 200, b"data: [DONE]\n\n"
+        else:
+            yield DATA, 200, b'{"choices":[{"text":"whole"}]}'
+        yield DONE, 200, b""
+
+    loop = asyncio.new_event_loop()
+    state = {}
+    ready = threading.Event()
+
+    async def serve():
+        br = await Broker().start()
+        bus = await NatsBus(f"nats://127.0.0.1:{br.port}").connect()
+        w = WorkerInfo(worker_id="10.1.2.3:9000", url="bus://", model_name="m")
+        srv = BusRequestServer(bus, BusRequestClient.token(w), handler, max_pending=4)
+        await srv.start()
+        state.update(br=br, bus=bus, srv=srv)
+        ready.set()
+
+    th = threading.Thread(target=lambda: (loop.run_until_complete(serve()), loop.run_forever()), daemon=True)
+    th.start()
+    assert ready.wait(10)
+    recs = [{"worker_id": "10.1.2.3:9000", "url": "http://127.0.0.1:1", "model_name": "m", "kv_block_size": 16,
+             "request_transport": "bus"}]
+    p, url = _start_router(binary, "--discovery-backend", "static", "--static-workers", _records_file(tmp_path, recs),
+                           "--request-transport", "nats", "--nats-url", f"nats://127.0.0.1:{state['br'].port}")
+    try:
+        r = httpx.post(url + "/v1/completions", json={"model": "m", "prompt": [1, 2, 3], "max_tokens": 3,
+                                                      "stream": True}, timeout=20)
+        assert r.status_code == 200 and r.content.count(b'"text":"t') == 3 and b"[DONE]" in r.content
+        r = httpx.post(url + "/v1/completions", json={"model": "m", "prompt": [1], "max_tokens": 2}, timeout=20)
+        assert r.status_code == 200 and r.json()["choices"][0]["text"] == "whole"
+        state["srv"].max_pending = 0                      # at its limit: refused without queueing
+        r = httpx.post(url + "/v1/completions", json={"model": "m", "prompt": [1], "max_tokens": 2}, timeout=20)
+        assert r.status_code == 429
+    finally:
+        _stop(p)
+
+        async def down():
+            await state["srv"].stop()
+            await state["bus"].close()
+            await state["br"].stop()
+
+        asyncio.run_coroutine_threadsafe(down(), loop).result(10)
+        loop.call_soon_threadsafe(loop.stop)
+    assert [s[0] for s in seen] == ["/v1/completions", "/v1/completions"]
+    assert seen[0][1]["max_tokens"] == 3 and seen[0][1]["stream"] is True
