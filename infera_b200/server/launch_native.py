@@ -16,7 +16,8 @@ import sys
 from infera_b200.build import ROUTER_BIN, build_router
 
 PY_ONLY = {"--enable-profiling", "--enable-scaling-api"}
-PY_ONLY_WITH_VALUE = {"--scaling-deployment", "--kvd-socket-path", "--k8s-label-selector", "--k8s-namespace"}
+PY_ONLY_WITH_VALUE = {"--scaling-deployment", "--kvd-socket-path", "--k8s-label-selector", "--k8s-namespace",
+                      "--nats-max-duration"}
 
 
 def native_argv(argv: list[str]) -> list[str]:
