@@ -13,11 +13,17 @@ One step is a one-second slice of the open-loop trace (the engine iterates
 continuously across slices). W warm-up slices run untimed, then K slices
 are timed between barrier + synchronize fences. Token timestamps are CUDA
 events recorded at the end of each engine iteration, relative to the
-window's origin; the value is the sum over ranks of SLO-meeting requests
-completed in the window divided by the longest rank's window.
+window's origin. The goodput cohort is every request that ARRIVED in the
+timed window; the trace keeps arriving for ``--tail`` seconds after it
+(untimed) so that those requests finish under the same load, and a request
+counts once it has finished within the SLO. The value is the sum over ranks
+of SLO-meeting requests of the cohort divided by the longest rank's window.
+(Counting by arrival keeps the figure independent of where the window's
+edges fall relative to a server's latency; both arms use it.)
 
 The end-to-end figure ("e2e") is the reference arm's setup with this
-framework's parts: every rank's engine (prefix cache cleared) serves the
+framework's parts: every rank's engine (prefix cache cleared, then the same
+untimed prewarm through the router as the reference arm gets) serves the
 OpenAI-compatible HTTP API from a separate worker process, all workers sit
 behind one KV-aware router (etcd discovery, ZMQ KV events), and each rank's
 load generator replays the same sessions and seed as the reference arm
@@ -66,6 +72,11 @@ def parse_args(argv=None):
     ap.add_argument("--rate", type=float, default=8.0,
                     help="Poisson arrivals per second per GPU (8 = 64 req/s over 8 instances, the top of the sweep)")
     ap.add_argument("--slice", type=float, default=1.0, help="seconds of trace per step")
+    ap.add_argument("--tail", type=float, default=8.0,
+                    help="seconds the trace keeps arriving after the timed window, for the window's arrivals "
+                         "to finish (the goodput cohort is the requests that arrived in the window)")
+    ap.add_argument("--mixed-prefill-tokens", type=int, default=512,
+                    help="prompt tokens per engine step while sequences are decoding")
     ap.add_argument("--model", default=MODEL)
     ap.add_argument("--max-num-seqs", type=int, default=128)
     ap.add_argument("--max-batched-tokens", type=int, default=2048)
@@ -129,7 +140,7 @@ def run_ours(args) -> dict:
 
     from infera_b200.bench.clocks import ClockSampler
     from infera_b200.bench.replay import EngineReplay
-    from infera_b200.bench.slo import SLO, percentile, summarize
+    from infera_b200.bench.slo import SLO, cohort, percentile, summarize
     from infera_b200.bench.trace import PRESETS
     from infera_b200.engine.llm_engine import EngineConfig, LLMEngine
     from infera_b200.ops import kernels as K
@@ -140,7 +151,7 @@ def run_ours(args) -> dict:
     spec = PRESETS["agentic-8b"]
     ecfg = EngineConfig(model=args.model, max_num_seqs=args.max_num_seqs,
                         max_batched_tokens=args.max_batched_tokens, use_cuda_graphs=not args.no_graphs,
-                        seed=args.seed)
+                        seed=args.seed, mixed_prefill_tokens=args.mixed_prefill_tokens)
     eng = LLMEngine(ecfg, device=dev)
     log(f"engine ready: {eng.bm.num_pages} KV pages, graphs={ecfg.use_cuda_graphs}")
     sessions = list(range(rank * SESSIONS_PER_GPU, (rank + 1) * SESSIONS_PER_GPU))
@@ -172,21 +183,25 @@ def run_ours(args) -> dict:
     ev_end.record()
     torch.cuda.synchronize()
     clocks = sampler.stop()
+    launches1 = K.LAUNCHES[0]
+    h2d1, d2h1 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
     log(f"timed window done: {eng.num_steps - steps0} iterations, running={eng.num_running()} "
         f"waiting={eng.num_waiting()}")
+    # the trace keeps arriving while the window's arrivals finish (untimed)
+    rp.run_until(rp.now() + args.tail)
     records = rp.resolve()
     w0 = rp.ev0.elapsed_time(ev_start) / 1000.0
     w1 = rp.ev0.elapsed_time(ev_end) / 1000.0
     st = summarize(records, (w0, w1), SLO())
-    done = [r for r in records if r.finish is not None and w0 <= r.finish <= w1]
+    done = cohort(records, (w0, w1))
     local_res = {
         "window_s": w1 - w0, "slo_met": st["slo_met"], "completed": st["completed"],
         "ttfts": [r.ttft for r in done],
         "itls": [x for r in done for x in r.itls()],
         "out_tokens": st["output_tok_s"] * st["window_s"],
-        "launches": K.LAUNCHES[0] - launches0,
+        "launches": launches1 - launches0, "cohort": st["cohort"],
         "engine_steps": eng.num_steps - steps0,
-        "h2d": eng.runner.h2d_bytes - h2d0, "d2h": eng.runner.d2h_bytes - d2h0,
+        "h2d": h2d1 - h2d0, "d2h": d2h1 - d2h0,
         "prefix_hit_rate": st["prefix_hit_rate"], "clocks": clocks,
         "kernel_status": K.scratch(dev).read_status(),
     }
@@ -199,7 +214,7 @@ def run_ours(args) -> dict:
                                   sessions=range(rank * SESSIONS_PER_GPU, (rank + 1) * SESSIONS_PER_GPU),
                                   rate=args.rate, warmup_s=args.warmup * args.slice,
                                   timed_s=(args.e2e_steps or args.steps) * args.slice, seed=args.seed + rank,
-                                  router_backend=args.router_backend)
+                                  router_backend=args.router_backend, tail_s=args.tail)
         log(f"e2e done: {e2e_local['completed']} completed, {e2e_local['errors']} errors")
     allr = _gather(local_res, world)
     e2e_all = _gather(e2e_local, world) if e2e_local is not None else None
@@ -216,6 +231,7 @@ def run_ours(args) -> dict:
     res = {
         "value": good / win,
         "window_s": win,
+        "arrived": sum(r["cohort"] for r in allr),
         "completed": sum(r["completed"] for r in allr),
         "slo_met": good,
         "ttft_p50_s": percentile(ttfts, 50),
@@ -282,11 +298,18 @@ def main(argv=None) -> int:
             "l2": "inputs larger than L2 (16 GB of weights + KV read every iteration)",
             "prefixes_primed": True,
             "max_batched_tokens": res["engine_cfg"]["max_batched_tokens"],
+            "mixed_prefill_tokens": args.mixed_prefill_tokens,
+            "goodput_cohort": f"requests arriving in the timed window; arrivals continue {args.tail:g} s after "
+                              f"it (untimed) for them to finish",
+            "prewarm": "device-timed: every prefix group's system prefix computed before the clock; e2e: each "
+                       "prefix group's system prefix + 8 random 1024-token prompts through the router, untimed "
+                       "(the reference arm gets the same)",
         },
         "ttft_p50_s": round(res["ttft_p50_s"], 4),
         "ttft_p99_s": round(res["ttft_p99_s"], 4),
         "itl_p50_ms": round(res["itl_p50_ms"], 3),
         "itl_p99_ms": round(res["itl_p99_ms"], 3),
+        "arrived": res["arrived"],
         "completed": res["completed"],
         "slo_met": res["slo_met"],
         "output_tok_s": round(res["output_tok_s"], 1),

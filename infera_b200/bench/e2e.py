@@ -32,7 +32,7 @@ import sys
 import threading
 import time
 
-from infera_b200.bench.slo import SLO, ReqRecord, percentile, summarize
+from infera_b200.bench.slo import SLO, ReqRecord, cohort, percentile, summarize
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 ETCD_PORT = 23890
@@ -86,9 +86,13 @@ def router_cmd(backend: str, etcd_port: int = ETCD_PORT, router_port: int = ROUT
 def run_e2e_fleet(engine, *, model: str, rank: int, world: int, barrier, sessions: range, rate: float,
                   warmup_s: float, timed_s: float, seed: int, router_backend: str = "python",
                   logdir: str | None = None, trace: str = "agentic-8b", drain_s: float = 0.0,
-                  ports: dict | None = None, appear_timeout: float = 300.0) -> dict:
+                  ports: dict | None = None, appear_timeout: float = 300.0, tail_s: float = 0.0,
+                  prewarm: bool = True) -> dict:
     """``barrier()`` synchronises the ranks (host-side). ``ports`` overrides
-    the fixed ports (keys etcd, router, worker0, events0)."""
+    the fixed ports (keys etcd, router, worker0, events0). Arrivals continue
+    for ``tail_s`` after the timed window so that the window's arrivals can
+    finish under the same load; ``prewarm``: the untimed warm-up of
+    :func:`infera_b200.bench.http_loadgen.prewarm` before the trace clock."""
     P = {"etcd": ETCD_PORT, "router": ROUTER_PORT, "worker0": WORKER_PORT0, "events0": EVENTS_PORT0}
     P.update(ports or {})
     from infera_b200.engine.core_ipc import EngineCoreServer, ipc_pair
@@ -134,12 +138,12 @@ def run_e2e_fleet(engine, *, model: str, rank: int, world: int, barrier, session
         it0 = engine.num_steps
         cmd = [sys.executable, "-m", "infera_b200.bench.http_loadgen", "--url", f"http://127.0.0.1:{P['router']}",
                "--model", model, "--sessions", f"{sessions.start}:{sessions.stop}", "--rate", str(rate),
-               "--duration", str(warmup_s + timed_s), "--seed", str(seed), "--drain-s", str(drain_s),
-               "--trace", trace]
+               "--duration", str(warmup_s + timed_s + tail_s), "--seed", str(seed), "--drain-s", str(drain_s),
+               "--trace", trace] + (["--prewarm"] if prewarm else [])
         env = dict(os.environ)
         env["PYTHONPATH"] = os.pathsep.join([ROOT, env.get("PYTHONPATH", "")])
         out = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, env=env,
-                             timeout=warmup_s + timed_s + 300)
+                             timeout=warmup_s + timed_s + tail_s + 900)
         h2d, d2h = engine.runner.h2d_bytes - h2d0, engine.runner.d2h_bytes - d2h0
         iters = engine.num_steps - it0
         if out.returncode != 0:
@@ -166,10 +170,11 @@ def run_e2e_fleet(engine, *, model: str, rank: int, world: int, barrier, session
         recs.append(rec)
     win = (warmup_s, warmup_s + timed_s)
     st = summarize(recs, win, SLO())
-    done = [r for r in recs if r.finish is not None and win[0] <= r.finish <= win[1]]
-    total = warmup_s + timed_s
+    done = cohort(recs, win)
+    total = warmup_s + timed_s + tail_s
     return {
-        "window_s": timed_s, "slo_met": st["slo_met"], "completed": st["completed"],
+        "window_s": timed_s, "slo_met": st["slo_met"], "completed": st["completed"], "cohort": st["cohort"],
+        "prewarm": res.get("prewarm"),
         "ttfts": [r.ttft for r in done if r.ttft is not None], "itls": [x for r in done for x in r.itls()],
         "errors": res["errors"], "prefix_hit_rate": st["prefix_hit_rate"],
         # copies happen every engine iteration; report them per benchmark step (1 s slice)
@@ -185,6 +190,7 @@ def aggregate(allr: list[dict], path: str) -> dict:
         "value": round(sum(r["slo_met"] for r in allr) / win, 4),
         "unit": "req/s",
         "path": path,
+        "arrived": sum(r.get("cohort", r["completed"]) for r in allr),
         "completed": sum(r["completed"] for r in allr),
         "slo_met": sum(r["slo_met"] for r in allr),
         "ttft_p50_s": round(percentile(ttfts, 50), 4),

@@ -7,8 +7,10 @@ length, and ``return_token_ids`` so the next turn can append exactly what
 was generated. Time is the client's wall clock (``time.monotonic``).
 
 Run as ``python -m infera_b200.bench.http_loadgen --url ... --sessions
-A:B --rate R --duration S``; prints one JSON object with the per-request
-records on stdout. Running it as a separate process keeps the client's
+A:B --rate R --duration S [--prewarm]``; prints one JSON object with the
+per-request records on stdout. Arrivals are issued until ``duration``;
+requests still in flight then are cancelled (``--drain-s``: wait that long
+for them first). Running it as a separate process keeps the client's
 parsing off the server's interpreter.
 """
 
@@ -136,6 +138,47 @@ async def run(url: str, model: str, spec_name: str, sids: list[int], rate: float
     return {"records": records, "errors": errors[0], "duration": duration}
 
 
+async def prewarm(url: str, model: str, spec_name: str, sids: list[int], seed: int, text_prompts: bool = False,
+                  extra: int = 8, extra_len: int = 1024, timeout: float = 600.0) -> dict:
+    """Untimed warm-up given to every arm before its trace clock starts.
+
+    Sends, concurrently, the system prefix of every prefix group among
+    ``sids`` (16 output tokens each: the server caches the prefix and the
+    router learns where it lives), and ``extra`` requests with fresh random
+    prompts of ``extra_len`` tokens and 32 output tokens (first-use costs
+    of batched prefill + decode shapes are paid here, not in the window).
+    Returns counts of requests sent and failed."""
+    from infera_b200.bench.hf_model_dir import ids_to_text
+
+    spec = PRESETS[spec_name]
+    sessions = build_sessions(spec, seed, sids)
+    prompts, seen = [], set()
+    for s in sessions:
+        key = tuple(s.prefix[:8])
+        if s.prefix and key not in seen:
+            seen.add(key)
+            prompts.append((s.prefix, 16))
+    rng = random.Random(seed * 31 + 7)
+    for _ in range(extra):
+        prompts.append(([rng.randrange(spec.vocab) for _ in range(extra_len)], 32))
+    failed = [0]
+    t0 = time.monotonic()
+    async with httpx.AsyncClient(base_url=url, timeout=httpx.Timeout(timeout, connect=30.0)) as client:
+
+        async def one(p, n):
+            body = {"model": model, "prompt": ids_to_text(p) if text_prompts else p, "max_tokens": n,
+                    "ignore_eos": True, "temperature": 0.0}
+            try:
+                r = await client.post("/v1/completions", json=body)
+                if r.status_code >= 400:
+                    failed[0] += 1
+            except httpx.HTTPError:
+                failed[0] += 1
+
+        await asyncio.gather(*(one(p, n) for p, n in prompts))
+    return {"sent": len(prompts), "failed": failed[0], "wall_s": round(time.monotonic() - t0, 3)}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--url", required=True)
@@ -147,10 +190,15 @@ def main(argv=None) -> None:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--drain-s", type=float, default=0.0)
     ap.add_argument("--text-prompts", action="store_true")
+    ap.add_argument("--prewarm", action="store_true", help="run prewarm() before the trace clock starts")
     a = ap.parse_args(argv)
     lo, hi = (int(x) for x in a.sessions.split(":"))
+    warm = None
+    if a.prewarm:
+        warm = asyncio.run(prewarm(a.url, a.model, a.trace, list(range(lo, hi)), a.seed, text_prompts=a.text_prompts))
     res = asyncio.run(run(a.url, a.model, a.trace, list(range(lo, hi)), a.rate, a.duration, a.seed, a.drain_s,
                           text_prompts=a.text_prompts))
+    res["prewarm"] = warm
     json.dump(res, sys.stdout)
     sys.stdout.flush()
 

@@ -2,8 +2,8 @@
 
 A request meets its SLO when its time to first token is within the TTFT
 bound and the 99th percentile of its inter-token latencies is within the
-ITL bound. Goodput = SLO-meeting requests completed in the window per
-second. The fleet-level p99 TTFT / p99 ITL over all requests and tokens and
+ITL bound. Goodput = SLO-meeting requests of the window's cohort (by
+default: the requests that arrived in it) per second of window. The fleet-level p99 TTFT / p99 ITL over all requests and tokens and
 the p50 TTFT are reported beside it.
 """
 
@@ -50,10 +50,27 @@ class SLO:
     itl_s: float = 0.050
 
 
-def summarize(records: list[ReqRecord], window: tuple[float, float], slo: SLO) -> dict:
+def summarize(records: list[ReqRecord], window: tuple[float, float], slo: SLO, by: str = "arrival") -> dict:
+    """``by="arrival"``: the cohort is every request that ARRIVED in the
+    window; it counts toward goodput once it has finished within the SLO
+    (a request still unfinished when the run stops has missed it). The run
+    must continue past the window (same arrival process) long enough for
+    the cohort to finish. Counting by arrival makes the figure independent
+    of where the window's edges fall relative to each server's latency: two
+    servers that both meet the SLO on the same trace get the same goodput.
+
+    ``by="finish"``: the cohort is every request that FINISHED in the window
+    (a server whose backlog drains into the window is credited with it)."""
     t0, t1 = window
     dur = max(1e-9, t1 - t0)
-    done = [r for r in records if r.finish is not None and t0 <= r.finish <= t1]
+    if by == "arrival":
+        cohort = [r for r in records if t0 <= r.arrival < t1]
+        done = [r for r in cohort if r.finish is not None]
+    elif by == "finish":
+        done = [r for r in records if r.finish is not None and t0 <= r.finish <= t1]
+        cohort = done
+    else:
+        raise ValueError(f"unknown cohort {by!r}")
     good = 0
     ttfts, itls = [], []
     for r in done:
@@ -69,6 +86,7 @@ def summarize(records: list[ReqRecord], window: tuple[float, float], slo: SLO) -
     cached_tokens = sum(r.cached_len for r in done)
     return {
         "window_s": dur,
+        "cohort": len(cohort),
         "completed": len(done),
         "slo_met": good,
         "goodput_rps": good / dur,
@@ -78,6 +96,14 @@ def summarize(records: list[ReqRecord], window: tuple[float, float], slo: SLO) -
         "ttft_p99_s": percentile(ttfts, 99),
         "itl_p50_s": percentile(itls, 50),
         "itl_p99_s": percentile(itls, 99),
-        "slo_attainment": good / max(1, len(done)),
+        "slo_attainment": good / max(1, len(cohort)),
         "prefix_hit_rate": cached_tokens / max(1, prompt_tokens),
     }
+
+
+def cohort(records: list[ReqRecord], window: tuple[float, float], by: str = "arrival") -> list[ReqRecord]:
+    """The finished requests that :func:`summarize` counts for ``window``."""
+    t0, t1 = window
+    if by == "arrival":
+        return [r for r in records if t0 <= r.arrival < t1 and r.finish is not None]
+    return [r for r in records if r.finish is not None and t0 <= r.finish <= t1]

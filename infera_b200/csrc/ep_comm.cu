@@ -192,11 +192,11 @@ __global__ void row_map_kernel(int rows, const int* __restrict__ C, int W, int E
   }
 }
 
-__global__ void wait_kernel(const unsigned int* flag, unsigned int target, int* status) {
+__global__ void wait_kernel(const unsigned int* flag, unsigned int target, int* status, unsigned long long limit_ns) {
   if (threadIdx.x != 0) return;
   const unsigned long long t0 = gtimer();
   while (ld_acquire_sys(flag) < target) {
-    if (gtimer() - t0 > kWaitNs) {
+    if (gtimer() - t0 > limit_ns) {
       atomicCAS(status, 0, kStatusTimeoutEp);
       return;
     }
@@ -270,7 +270,16 @@ extern "C" int ib_ep_return(const void* y, int rows, int H, const int* C, int wo
 }
 
 extern "C" int ib_ep_wait(const unsigned int* flag, unsigned int target, int* status, cudaStream_t stream) {
-  wait_kernel<<<1, 32, 0, stream>>>(flag, target, status);
+  wait_kernel<<<1, 32, 0, stream>>>(flag, target, status, kWaitNs);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+// As ib_ep_wait with the wait bounded by limit_ns; on expiry *status gets
+// 0x4201 (if it was 0) and the kernel returns.
+extern "C" int ib_ep_wait_for(const unsigned int* flag, unsigned int target, int* status, unsigned long long limit_ns,
+                              cudaStream_t stream) {
+  wait_kernel<<<1, 32, 0, stream>>>(flag, target, status, limit_ns);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }

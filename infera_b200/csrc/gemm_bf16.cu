@@ -114,6 +114,7 @@ struct Params {
   // bounded, until *wait_flag >= wait_target before the first read
   const unsigned int* wait_flag;
   unsigned int wait_target;
+  uint64_t wait_limit_ns;   // bound of that wait (0: kWaitLimitNs)
 };
 
 // Bounded wait for the dispatch's arrival counter (release-incremented by
@@ -131,7 +132,7 @@ __device__ __forceinline__ bool wait_arrivals(const Params& p, volatile int* abo
     if (v >= p.wait_target) break;
     if (((++spins) & 63u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > (p.wait_limit_ns ? p.wait_limit_ns : kWaitLimitNs)) {
         record_status(p.status, kStatusTimeoutPeer);
         *abort_flag = 1;
         return false;
@@ -926,7 +927,7 @@ inline int run_grouped(const Operands& o, const void* A, const void* W, void* ou
                        int* status, cudaStream_t stream, const int* row_map = nullptr, int world = 1,
                        void* const* peer_out = nullptr, unsigned int* const* peer_flag = nullptr,
                        unsigned int* done_ctr = nullptr, const unsigned int* wait_flag = nullptr,
-                       unsigned int wait_target = 0) {
+                       unsigned int wait_target = 0, uint64_t wait_limit_ns = 0) {
   if (R <= 0 || N <= 0 || K <= 0 || E <= 0) return 0;
   if (!operands_ok(o, K, lda, ldw) || (N % BM) != 0) return -1;
   if (o.fp8 ? (bn < 32 || bn > MAX_BN_FP8 || (bn % 32) != 0) : (bn < 16 || bn > MAX_BN || (bn % 16) != 0))
@@ -954,6 +955,7 @@ inline int run_grouped(const Operands& o, const void* A, const void* W, void* ou
   p.row_map = row_map;
   p.wait_flag = wait_flag;
   p.wait_target = wait_target;
+  p.wait_limit_ns = wait_limit_ns;
   if (row_map != nullptr) {
     if (epi != EPI_BF16 || world < 1 || world > kMaxPeers || done_ctr == nullptr) return -1;
     p.push = 1;
@@ -1061,6 +1063,20 @@ extern "C" int ib_gemm_grouped_wait(const void* A, const uint8_t* sf_a, int sf_a
   const gemm::Operands o{sf_w != nullptr, sf_a, sf_a_ld, sf_w};
   return gemm::run_grouped(o, A, W, out, R, N, K, E, lda, ldw, ldc, epi, gtab, gnum, bn, grid_tiles, status, stream,
                            nullptr, 1, nullptr, nullptr, nullptr, wait_flag, wait_target);
+}
+
+// As ib_gemm_grouped_wait with the arrival wait bounded by wait_limit_ns
+// instead of the default 2 s. On expiry the status word gets
+// kStatusTimeoutPeer (5), every role of the CTA stops, drains what it
+// issued, frees its TMEM and returns, so the context stays usable.
+extern "C" int ib_gemm_grouped_wait_for(const void* A, const uint8_t* sf_a, int sf_a_ld, const void* W,
+                                        const uint8_t* sf_w, void* out, int R, int N, int K, int E, int lda, int ldw,
+                                        int ldc, int epi, const int* gtab, const int* gnum, int bn, int grid_tiles,
+                                        const unsigned int* wait_flag, unsigned int wait_target,
+                                        unsigned long long wait_limit_ns, int* status, cudaStream_t stream) {
+  const gemm::Operands o{sf_w != nullptr, sf_a, sf_a_ld, sf_w};
+  return gemm::run_grouped(o, A, W, out, R, N, K, E, lda, ldw, ldc, epi, gtab, gnum, bn, grid_tiles, status, stream,
+                           nullptr, 1, nullptr, nullptr, nullptr, wait_flag, wait_target, wait_limit_ns);
 }
 
 // fp8 grouped GEMM: as above with e4m3 operands; sf_a [K/128, sf_a_ld] over

@@ -185,11 +185,12 @@ __global__ void __launch_bounds__(256) ar_add_rmsnorm_kernel(const ArParams p) {
 }
 
 // Bounded wait until *flag >= target (the x rows of every owner arrived).
-__global__ void tp_wait_kernel(const unsigned int* flag, unsigned int target, int* status) {
+__global__ void tp_wait_kernel(const unsigned int* flag, unsigned int target, int* status,
+                               unsigned long long limit_ns) {
   if (threadIdx.x != 0) return;
   const unsigned long long t0 = globaltimer();
   while (ld_acquire_sys(flag) < target) {
-    if (globaltimer() - t0 > kWaitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       atomicCAS(status, 0, kStatusTimeoutArrive);
       return;
     }
@@ -322,7 +323,16 @@ extern "C" int ib_ar_add_rmsnorm_rs(const void* recv, long long src_stride, int 
 }
 
 extern "C" int ib_tp_wait(const unsigned int* flag, unsigned int target, int* status, cudaStream_t stream) {
-  tp_wait_kernel<<<1, 32, 0, stream>>>(flag, target, status);
+  tp_wait_kernel<<<1, 32, 0, stream>>>(flag, target, status, ib200::tp::kWaitNs);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+// As ib_tp_wait with the wait bounded by limit_ns; on expiry *status gets
+// 0x4101 (if it was 0) and the kernel returns.
+extern "C" int ib_tp_wait_for(const unsigned int* flag, unsigned int target, int* status,
+                              unsigned long long limit_ns, cudaStream_t stream) {
+  tp_wait_kernel<<<1, 32, 0, stream>>>(flag, target, status, limit_ns);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }

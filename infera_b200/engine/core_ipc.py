@@ -412,6 +412,8 @@ def main(argv=None) -> None:
     p.add_argument("--page-size", type=int, default=16)
     p.add_argument("--max-num-seqs", type=int, default=128)
     p.add_argument("--max-batched-tokens", type=int, default=2048)
+    p.add_argument("--mixed-prefill-tokens", type=int, default=512,
+                   help="prompt tokens per step while sequences are decoding (0: no cap)")
     p.add_argument("--gpu-memory-utilization", type=float, default=0.90)
     p.add_argument("--num-pages", type=int, default=None)
     p.add_argument("--no-cuda-graphs", action="store_true")
@@ -441,6 +443,7 @@ def main(argv=None) -> None:
     pub = KvEventPublisher(a.kv_events_endpoint) if a.kv_events_endpoint and rank == 0 else None
     cfg = EngineConfig(model=a.model, page_size=a.page_size, max_num_seqs=a.max_num_seqs,
                        max_batched_tokens=a.max_batched_tokens, gpu_memory_utilization=a.gpu_memory_utilization,
+                       mixed_prefill_tokens=a.mixed_prefill_tokens,
                        num_pages=a.num_pages, use_cuda_graphs=not a.no_cuda_graphs, seed=a.seed, kv_tier=a.kv_tier,
                        disagg_mode=a.disagg_mode, kv_push_endpoint=a.kv_push_endpoint)
     eng = LLMEngine(cfg, device=device, event_sink=pub, tp=tp)
@@ -501,6 +504,7 @@ def _main_dp(a) -> None:
     pub = KvEventPublisher(events) if events else None
     cfg = EngineConfig(model=a.model, page_size=a.page_size, max_num_seqs=a.max_num_seqs,
                        max_batched_tokens=a.max_batched_tokens, gpu_memory_utilization=a.gpu_memory_utilization,
+                       mixed_prefill_tokens=a.mixed_prefill_tokens,
                        num_pages=a.num_pages, use_cuda_graphs=False, seed=a.seed)
     dp = DPAttentionEngine(cfg, EPSpec(rank, world, group=None, gloo=gloo, fused=a.ep_fused and on_gpu),
                            device=device)

@@ -53,6 +53,10 @@ class EngineConfig:
     enable_prefix_cache: bool = True
     seed: int = 0
     long_prefill_threshold: int = 0
+    # prompt tokens per step while sequences are decoding: bounds the step
+    # time that decoding sequences see as their inter-token latency (0: the
+    # whole max_batched_tokens budget)
+    mixed_prefill_tokens: int = 512
     max_model_len: int | None = None
     model_overrides: dict = field(default_factory=dict)
     # KV tiering: None (off), "host:<GiB>[:<nvme dir>]" (in-process host store,
@@ -120,7 +124,8 @@ class LLMEngine:
         self.bm = BlockManager(num_pages, cfg.page_size, cfg.enable_prefix_cache, event_sink=self._on_kv_event)
         self.scheduler = Scheduler(self.bm, cfg.max_num_seqs, cfg.max_batched_tokens, mcfg.max_model_len,
                                    watermark_pages=max(1, num_pages // 100),
-                                   long_prefill_threshold=cfg.long_prefill_threshold)
+                                   long_prefill_threshold=cfg.long_prefill_threshold,
+                                   mixed_prefill_tokens=cfg.mixed_prefill_tokens)
         self.runner = ModelRunner(self.model, num_pages, cfg.page_size, cfg.max_num_seqs, cfg.max_batched_tokens,
                                   use_graphs=cfg.use_cuda_graphs, exportable=cfg.disagg_mode == "decode")
         self.tier = None

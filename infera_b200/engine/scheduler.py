@@ -51,7 +51,8 @@ class SchedulerOutput:
 
 class Scheduler:
     def __init__(self, block_manager: BlockManager, max_num_seqs: int = 256, max_batched_tokens: int = 4096,
-                 max_model_len: int = 32768, watermark_pages: int = 0, long_prefill_threshold: int = 0):
+                 max_model_len: int = 32768, watermark_pages: int = 0, long_prefill_threshold: int = 0,
+                 mixed_prefill_tokens: int = 0):
         self.bm = block_manager
         self.max_num_seqs = max_num_seqs
         self.max_batched_tokens = max_batched_tokens
@@ -60,6 +61,8 @@ class Scheduler:
         # a single sequence's chunk is capped so that one long prompt cannot
         # occupy the whole budget while decode latency suffers (0: no cap)
         self.long_prefill_threshold = long_prefill_threshold
+        # prompt tokens per step while sequences are decoding (0: no cap)
+        self.mixed_prefill_tokens = mixed_prefill_tokens
         self.waiting: deque[Request] = deque()
         self.running: list[Request] = []
         # PD decode side: admitted requests waiting for their pushed KV
@@ -143,6 +146,15 @@ class Scheduler:
         out = SchedulerOutput()
         budget = self.max_batched_tokens
         ps = self.bm.page_size
+        # While sequences are decoding, every step is one of their inter-token
+        # gaps: prefill chunks joining it are capped so that the step stays
+        # near the decode-step time (the cap does not apply to steps with no
+        # decodes, which run prompts at the full budget).
+        n_dec = sum(1 for r in self.running
+                    if r.num_tokens - r.num_computed == 1 and len(r.output_token_ids) > 0)
+        pbudget = budget
+        if n_dec and self.mixed_prefill_tokens:
+            pbudget = min(budget, n_dec + self.mixed_prefill_tokens)
 
         # 1 + 2: running sequences (oldest first)
         i = 0
@@ -153,7 +165,11 @@ class Scheduler:
                 i += 1
                 continue
             is_decode = pending == 1 and len(r.output_token_ids) > 0
-            n = 1 if is_decode else min(pending, budget)
+            if is_decode:
+                n = 1
+            else:
+                # decodes still to come in this pass keep their token
+                n = min(pending, pbudget - n_dec)
             if self.long_prefill_threshold and not is_decode:
                 n = min(n, self.long_prefill_threshold)
             if n <= 0:
@@ -166,15 +182,23 @@ class Scheduler:
                     self._preempt(r, out)
                     r = None
                     break
+                if victim.num_tokens - victim.num_computed == 1 and len(victim.output_token_ids) > 0:
+                    n_dec -= 1
                 self._preempt(victim, out)
             if r is None:
+                if is_decode:
+                    n_dec -= 1
                 continue
             chunk = ScheduledChunk(r, r.num_computed, n, is_decode, r.num_computed + n == r.num_tokens)
             (out.decodes if is_decode else out.prefills).append(chunk)
             budget -= n
+            pbudget -= n
+            if is_decode:
+                n_dec -= 1
             i += 1
             if budget <= 0:
                 break
+        budget = min(budget, pbudget)
 
         # 3: admit waiting sequences
         while self.waiting and budget > 0 and self.free_rows and len(self.running) < self.max_num_seqs:

@@ -62,6 +62,8 @@ def parse_args(argv=None):
     p.add_argument("--page-size", type=int, default=16)
     p.add_argument("--max-num-seqs", type=int, default=128)
     p.add_argument("--max-batched-tokens", type=int, default=2048)
+    p.add_argument("--mixed-prefill-tokens", type=int, default=512,
+                   help="prompt tokens per step while sequences are decoding (0: no cap)")
     p.add_argument("--gpu-memory-utilization", type=float, default=0.90)
     p.add_argument("--num-pages", type=int, default=None)
     p.add_argument("--no-cuda-graphs", action="store_true")
@@ -93,6 +95,7 @@ def _core_cmd(args, in_addr: str, out_addr: str) -> list[str]:
     cmd = [sys.executable, "-m", "infera_b200.engine.core_ipc", "--in", in_addr, "--out", out_addr,
            "--model", args.model, "--device", args.device, "--page-size", str(args.page_size),
            "--max-num-seqs", str(args.max_num_seqs), "--max-batched-tokens", str(args.max_batched_tokens),
+           "--mixed-prefill-tokens", str(args.mixed_prefill_tokens),
            "--gpu-memory-utilization", str(args.gpu_memory_utilization), "--seed", str(args.seed)]
     if args.num_pages:
         cmd += ["--num-pages", str(args.num_pages)]
@@ -118,6 +121,7 @@ async def start_engine(args):
         pub = KvEventPublisher(args.kv_events_endpoint) if args.kv_events_endpoint else None
         ecfg = EngineConfig(model=args.model, page_size=args.page_size, max_num_seqs=args.max_num_seqs,
                             max_batched_tokens=args.max_batched_tokens,
+                            mixed_prefill_tokens=args.mixed_prefill_tokens,
                             gpu_memory_utilization=args.gpu_memory_utilization, num_pages=args.num_pages,
                             use_cuda_graphs=not args.no_cuda_graphs, seed=args.seed, kv_tier=args.kv_tier,
                             disagg_mode=args.disagg_mode, kv_push_endpoint=args.kv_push_endpoint)

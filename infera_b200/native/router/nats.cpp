@@ -1,6 +1,8 @@
 // Core NATS client (see nats.h).
 #include "nats.h"
 
+#include <cstdio>
+
 #include <sys/socket.h>
 #include <unistd.h>
 
@@ -61,6 +63,17 @@ bool NatsConn::connect(const std::string& url, std::string* err) {
   if (!conn.read_line(&line) || line.compare(0, 5, "INFO ") != 0) {
     *err = "not a NATS server at " + url;
     return false;
+  }
+  {
+    // "max_payload":<n> in the INFO object bounds what the reader accepts
+    const size_t at = line.find("\"max_payload\"");
+    if (at != std::string::npos) {
+      const size_t colon = line.find(':', at);
+      if (colon != std::string::npos) {
+        const unsigned long long mp = std::strtoull(line.c_str() + colon + 1, nullptr, 10);
+        if (mp > 0 && mp < max_payload_) max_payload_ = static_cast<size_t>(mp);
+      }
+    }
   }
   if (!write("CONNECT {\"verbose\":false,\"pedantic\":false,\"headers\":true,\"no_responders\":true,"
              "\"protocol\":1,\"lang\":\"cpp\",\"version\":\"infera-b200\",\"name\":\"infera-b200-router\"}\r\n"
@@ -160,6 +173,11 @@ void NatsConn::reader() {
       if (parts.size() == need + 1) m.reply = parts[2];
       size_t total = std::strtoull(parts.back().c_str(), nullptr, 10);
       size_t hl = hmsg ? std::strtoull(parts[parts.size() - 2].c_str(), nullptr, 10) : 0;
+      if (total > max_payload_) {
+        std::fprintf(stderr, "[ib200_router] NATS message of %zu bytes exceeds max_payload %zu; closing\n", total,
+                     max_payload_);
+        break;
+      }
       std::string block;
       if (!conn.read_exact(total + 2, &block) || hl > total) break;
       block.resize(total);
@@ -174,6 +192,7 @@ void NatsConn::reader() {
     }
     // PONG, +OK, INFO and -ERR need no action here
   }
+  if (alive_) std::fprintf(stderr, "[ib200_router] NATS connection lost\n");
   std::lock_guard<std::mutex> g(qmu_);
   alive_ = false;
   cv_.notify_all();

@@ -37,6 +37,9 @@ class NatsConn {
   // next message of a subscription; false after timeout_s without one (or on a lost connection)
   bool next(int sid, double timeout_s, NatsMsg* out);
   bool alive() const { return alive_; }
+  // largest message the reader accepts (the server's INFO max_payload when it
+  // states one, else 64 MiB); a larger one closes the connection
+  size_t max_payload() const { return max_payload_; }
 
  private:
   void reader();
@@ -49,6 +52,7 @@ class NatsConn {
   std::condition_variable cv_;
   std::map<int, std::deque<NatsMsg>> q_;
   int next_sid_ = 1;
+  size_t max_payload_ = size_t(64) << 20;
 };
 
 std::map<std::string, std::string> nats_parse_headers(const std::string& block);

@@ -54,6 +54,7 @@ struct Config {
   std::string request_transport = "http";   // "nats": workers registered with request_transport=bus over NATS
   std::string nats_url = "nats://127.0.0.1:4222";
   double nats_idle_timeout = 900.0;
+  double nats_max_duration = 0.0;
 };
 
 static double now_s() {
@@ -170,6 +171,8 @@ class App {
   std::unique_ptr<EtcdDiscovery> disc;
   std::unique_ptr<NatsConn> nats;   // set with --request-transport nats
   double nats_idle = 900.0;
+  double nats_max_duration = 0.0;   // 0: no overall limit
+  static constexpr size_t kMaxUnaryBody = size_t(64) << 20;
   UpstreamPool ups;
 
   // metrics
@@ -288,13 +291,25 @@ class App {
   // The bus request transport (workers registered with request_transport=bus):
   // admission on infera.admit.<token>, the request on infera.req.<token> with a
   // private reply subject, frames whose rs-type header is data / done / error;
-  // after nats_idle seconds without a frame the request is cancelled on
-  // infera.cancel.<token> (three times) and answered 504.
+  // after nats_idle seconds without a frame, or nats_max_duration seconds in
+  // total, the request is cancelled on infera.cancel.<token> (three times)
+  // and answered 504. Each attempt carries its own bus id (the rid header and
+  // the cancel payload): the client's X-Infera-Request-Id is only echoed
+  // back, so two client requests with one id never collide on a worker.
+  // A lost NATS connection answers 503.
   int attempt_bus(int cfd, const Target& t, const std::vector<uint64_t>& blocks, const Value& body,
                   const CacheHints& hints, const std::string& path, bool stream, const std::string& rid, bool keep,
                   Reply* fail, int* fail_status) {
     const Worker& w = *t.w;
     const std::string token = bus_token(w.worker_id);
+    if (!nats->alive()) {
+      std::fprintf(stderr, "[ib200_router] bus request to %s refused: NATS connection lost\n", w.worker_id.c_str());
+      *fail = {503, err_json("NATS connection lost")};
+      *fail_status = -1;   // the router's own failure: not counted against the worker by the breaker
+      return 0;
+    }
+    const std::string bus_rid = rand_hex(16);
+    const auto t_start = std::chrono::steady_clock::now();
     policy->started(t.route_key(), blocks);
     struct Done {
       App* a; const Target& t; const std::vector<uint64_t>& b;
@@ -325,9 +340,14 @@ class App {
                             ",\"headers\":" + hdrs + "}";
     const std::string inbox = "_INBOX." + rand_hex(12);
     int sid = nats->subscribe(inbox);
-    nats->publish("infera.req." + token, inbox, req, {{"rid", rid}});
+    nats->publish("infera.req." + token, inbox, req, {{"rid", bus_rid}});
     auto frame = [&](std::string* kind, int* status) -> bool {
-      if (!nats->next(sid, nats_idle, &m)) return false;
+      double wait = nats_idle;
+      if (nats_max_duration > 0) {
+        const double used = std::chrono::duration<double>(std::chrono::steady_clock::now() - t_start).count();
+        wait = std::min(wait, std::max(0.0, nats_max_duration - used));
+      }
+      if (!nats->next(sid, wait, &m)) return false;
       auto k = m.headers.find("rs-type");
       auto st = m.headers.find("rs-status");
       *kind = k == m.headers.end() ? "data" : k->second;
@@ -335,7 +355,7 @@ class App {
       return true;
     };
     auto cancel = [&]() {
-      for (int i = 0; i < 3; ++i) nats->publish("infera.cancel." + token, "", rid, {});
+      for (int i = 0; i < 3; ++i) nats->publish("infera.cancel." + token, "", bus_rid, {});
     };
     std::string kind;
     int status = 0;
@@ -356,6 +376,10 @@ class App {
       std::string raw;
       while (kind == "data") {
         raw += m.data;
+        if (raw.size() > kMaxUnaryBody) {
+          kind = "too_big";
+          break;
+        }
         if (!frame(&kind, &status)) {
           kind = "timeout";
           break;
@@ -363,7 +387,13 @@ class App {
       }
       nats->unsubscribe(sid);
       if (kind != "done") {
-        if (kind == "timeout") cancel();
+        if (kind == "timeout" || kind == "too_big") cancel();
+        if (kind == "too_big") {
+          *fail = {502, err_json("worker " + w.worker_id + " response exceeds " + std::to_string(kMaxUnaryBody) +
+                                 " bytes")};
+          *fail_status = 0;
+          return 0;
+        }
         *fail = {kind == "timeout" ? 504 : (status ? status : 502), err_json("worker " + w.worker_id + " failed")};
         *fail_status = kind == "timeout" ? 0 : status;
         return 0;
@@ -1056,6 +1086,7 @@ int main(int argc, char** argv) {
     else if (a == "--request-transport") cfg.request_transport = v;
     else if (a == "--nats-url") cfg.nats_url = v;
     else if (a == "--nats-idle-timeout") cfg.nats_idle_timeout = std::atof(v.c_str());
+    else if (a == "--nats-max-duration") cfg.nats_max_duration = std::atof(v.c_str());
     else if (a == "--router-backend" || a == "--kv-event-transport" ||
              a == "--enable-profiling" || a == "--enable-scaling-api") {
       // accepted for flag compatibility with the Python router; no effect here
@@ -1073,6 +1104,7 @@ int main(int argc, char** argv) {
   if (cfg.request_transport == "nats") {
     app.nats = std::make_unique<NatsConn>();
     app.nats_idle = cfg.nats_idle_timeout;
+    app.nats_max_duration = cfg.nats_max_duration;
     std::string nerr;
     if (!app.nats->connect(cfg.nats_url, &nerr)) {
       std::fprintf(stderr, "[ib200_router] %s\n", nerr.c_str());

@@ -70,6 +70,7 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_ep_dispatch": [c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp],
         "ib_ep_return": [c_vp, c_int, c_int, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
         "ib_ep_wait": [c_vp, ctypes.c_uint, c_vp, c_vp],
+        "ib_ep_wait_for": [c_vp, ctypes.c_uint, c_vp, ctypes.c_ulonglong, c_vp],
         "ib_gemm_grouped": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp,
                             c_int, c_int, c_vp, c_vp],
         "ib_kv_push_pages": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_int, c_int, c_int,
@@ -89,6 +90,7 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_ar_add_rmsnorm_rs": [c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_float,
                                  c_vp, c_vp, c_vp, c_vp],
         "ib_tp_wait": [c_vp, ctypes.c_uint, c_vp, c_vp],
+        "ib_tp_wait_for": [c_vp, ctypes.c_uint, c_vp, ctypes.c_ulonglong, c_vp],
         "ib_mla_decode": [c_vp, c_int, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_float, c_vp, c_vp, c_vp,
                           c_vp, c_vp],
         "ib_mla_set_trace": [c_vp],
@@ -97,6 +99,9 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
                                  c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp],
         "ib_gemm_grouped_wait": [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int,
                                  c_int, c_int, c_vp, c_vp, c_int, c_int, c_vp, c_uint, c_vp, c_vp],
+        "ib_gemm_grouped_wait_for": [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int,
+                                     c_int, c_int, c_vp, c_vp, c_int, c_int, c_vp, c_uint, ctypes.c_ulonglong, c_vp,
+                                     c_vp],
         "ib_ep_dispatch_q": [c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int,
                              c_vp, c_vp, c_vp],
         "ib_gemm_set_trace": [c_vp],

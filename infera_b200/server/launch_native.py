@@ -16,8 +16,7 @@ import sys
 from infera_b200.build import ROUTER_BIN, build_router
 
 PY_ONLY = {"--enable-profiling", "--enable-scaling-api"}
-PY_ONLY_WITH_VALUE = {"--scaling-deployment", "--kvd-socket-path", "--k8s-label-selector", "--k8s-namespace",
-                      "--nats-max-duration"}
+PY_ONLY_WITH_VALUE = {"--scaling-deployment", "--kvd-socket-path", "--k8s-label-selector", "--k8s-namespace"}
 
 
 def native_argv(argv: list[str]) -> list[str]:

@@ -24,17 +24,24 @@ class Broker:
         self.server = None
         self.port = 0
         self.published = 0
+        self.writers: set = set()
 
     async def start(self) -> "Broker":
         self.server = await asyncio.start_server(self._conn, "127.0.0.1", 0)
         self.port = self.server.sockets[0].getsockname()[1]
         return self
 
+    def kick(self) -> None:
+        """Close every client connection (a broker that went away)."""
+        for w in list(self.writers):
+            w.close()
+
     async def stop(self) -> None:
         self.server.close()
         await self.server.wait_closed()
 
     async def _conn(self, r: asyncio.StreamReader, w: asyncio.StreamWriter) -> None:
+        self.writers.add(w)
         w.write(b'INFO {"server_id":"stub","version":"2.10.0","headers":true,"max_payload":1048576}\r\n')
         opts = {}
         try:
@@ -83,4 +90,5 @@ class Broker:
             pass
         finally:
             self.subs = [x for x in self.subs if x[0] is not w]
+            self.writers.discard(w)
             w.close()

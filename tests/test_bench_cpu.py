@@ -48,3 +48,24 @@ def test_replay_runs_multiturn_on_cpu():
     for r in done:
         assert r.first_token >= r.arrival
         assert len(r.token_times) == r.out_len
+
+
+def test_goodput_cohort_by_arrival():
+    """The cohort is the requests that arrived in the window; one that has
+    not finished counts as a miss, one that arrived before the window is not
+    counted even if it finishes inside it."""
+    def rec(arr, times):
+        r = ReqRecord("", arrival=arr)
+        r.token_times = times
+        r.first_token = times[0] if times else None
+        r.finish = times[-1] if times else None
+        return r
+
+    recs = [rec(1.0, [1.1, 1.12]), rec(5.0, [5.2, 5.22]), rec(9.5, [10.5, 10.52]),   # in window, met
+            rec(6.0, []),                                                           # never finished
+            rec(0.5, [2.0, 2.01]),                                                  # arrived before
+            rec(7.0, [9.5, 9.51])]                                                  # TTFT 2.5 s > 2 s
+    s = summarize(recs, (1.0, 10.0), SLO(2.0, 0.05))
+    assert s["cohort"] == 5 and s["completed"] == 4 and s["slo_met"] == 3
+    f = summarize(recs, (1.0, 10.0), SLO(2.0, 0.05), by="finish")
+    assert f["completed"] == 4   # the 0.5 s arrival is counted, the 10.52 s finish is not

@@ -89,3 +89,30 @@ def test_shared_prefix_pages_are_refcounted():
     bm.clear_cache()
     # every page but the reserved padding page 0 is free again
     assert bm.cached_hashes() == [] and bm.num_free() == 8 - bm.reserved and events == ["AllBlocksCleared"]
+
+
+def test_mixed_step_prefill_cap_while_decoding():
+    """While sequences decode, prompt chunks joining a step are capped (the
+    step is their inter-token gap); with nothing decoding, prompts get the
+    whole budget. Outputs are unchanged by the chunking."""
+    eng = _engine(num_pages=256, max_batched_tokens=256, mixed_prefill_tokens=24)
+    eng.add_request("d", _prompt(20, 30), SamplingParams(max_tokens=40, ignore_eos=True))
+    eng.step()                                            # "d" prefills, then decodes
+    eng.add_request("p", _prompt(21, 200), SamplingParams(max_tokens=3, ignore_eos=True))
+    sched = eng.scheduler.schedule()
+    assert len(sched.decodes) == 1
+    assert sum(c.num_tokens for c in sched.prefills) <= 24
+    for c in sched.prefills + sched.decodes:
+        eng.scheduler.abort(c.req.request_id)
+    eng.requests.clear()
+    # nothing decoding: the full budget
+    eng.add_request("q", _prompt(22, 200), SamplingParams(max_tokens=3, ignore_eos=True))
+    sched = eng.scheduler.schedule()
+    assert not sched.decodes and sum(c.num_tokens for c in sched.prefills) == 200
+    eng.scheduler.abort("q")
+    eng.requests.clear()
+    # same tokens as an uncapped engine
+    ref = _engine(num_pages=256, max_batched_tokens=256, mixed_prefill_tokens=0)
+    ps = [_prompt(30 + i, 90 + 20 * i) for i in range(3)]
+    sp = SamplingParams(max_tokens=5, ignore_eos=True)
+    assert eng.generate(ps, sp) == ref.generate(ps, sp)

@@ -193,13 +193,17 @@ def test_pd_nvlink_push_shaping(binary, tmp_path):
 def test_launcher_strips_python_only_flags():
     argv = ["--router-backend", "native", "--enable-profiling", "--kvd-socket-path", "/tmp/x", "--port", "9"]
     assert native_argv(argv) == ["--router-backend", "native", "--port", "9"]
+    # the native router enforces the bus requests' overall limit itself
+    assert native_argv(["--nats-max-duration", "30"]) == ["--nats-max-duration", "30"]
     assert os.path.exists(router_binary())
 
 
 def test_native_router_bus_transport_over_nats(binary, tmp_path):
     """--request-transport nats: a worker registered with
     request_transport=bus is reached over NATS (admission, streamed frames,
-    unary reply, refusal at the admission limit)."""
+    unary reply, refusal at the admission limit); two client requests that
+    share one X-Infera-Request-Id are both served (each bus attempt has its
+    own id); a lost NATS connection answers 503."""
     import asyncio
     import threading
 
@@ -215,6 +219,8 @@ def test_native_router_bus_transport_over_nats(binary, tmp_path):
         seen.append((path, body))
         if body.get("stream"):
             for i in range(3):
+                if body.get("max_tokens") == 7:           # slow: overlaps a twin request
+                    await asyncio.sleep(0.3)
                 yield DATA, 200, f'data: {{"choices":[{{"text":"t{i}"}}]}}\n\n'.encode()
             yield DATA, 200, b"data: [DONE]\n\n"
         else:
@@ -250,6 +256,23 @@ def test_native_router_bus_transport_over_nats(binary, tmp_path):
         state["srv"].max_pending = 0                      # at its limit: refused without queueing
         r = httpx.post(url + "/v1/completions", json={"model": "m", "prompt": [1], "max_tokens": 2}, timeout=20)
         assert r.status_code == 429
+        state["srv"].max_pending = 4
+        import concurrent.futures
+
+        def twin():
+            return httpx.post(url + "/v1/completions", json={"model": "m", "prompt": [1], "max_tokens": 7,
+                                                             "stream": True},
+                              headers={"X-Infera-Request-Id": "same-id"}, timeout=20)
+
+        with concurrent.futures.ThreadPoolExecutor(2) as ex:
+            rs = list(ex.map(lambda _: twin(), range(2)))
+        for r in rs:
+            assert r.status_code == 200 and r.content.count(b'"text":"t') == 3, r.content
+            assert r.headers.get("x-infera-request-id") == "same-id"
+        loop.call_soon_threadsafe(state["br"].kick)       # the broker goes away
+        time.sleep(0.5)
+        r = httpx.post(url + "/v1/completions", json={"model": "m", "prompt": [1], "max_tokens": 2}, timeout=20)
+        assert r.status_code == 503 and "NATS connection lost" in r.text
     finally:
         _stop(p)
 
@@ -260,5 +283,5 @@ def test_native_router_bus_transport_over_nats(binary, tmp_path):
 
         asyncio.run_coroutine_threadsafe(down(), loop).result(10)
         loop.call_soon_threadsafe(loop.stop)
-    assert [s[0] for s in seen] == ["/v1/completions", "/v1/completions"]
+    assert [s[0] for s in seen] == ["/v1/completions"] * 4
     assert seen[0][1]["max_tokens"] == 3 and seen[0][1]["stream"] is True
