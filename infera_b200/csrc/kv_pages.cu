@@ -10,6 +10,9 @@
 //
 //   dir 0 (gather / save):  chunk[c, l, p*16 + i, :] = cache_c[l, pages[p]*16 + i, :]
 //   dir 1 (scatter / load): cache_c[l, pages[p]*16 + i, :] = chunk[c, l, p*16 + i, :]
+//   dir 2 / 3: the same with a page-major chunk [n_pages, C, L, 16, H], i.e.
+//   one v2 payload per page back to back (the tier staging rings: each slot
+//   is one page's blob payload).
 //
 // Reference parity: the reference implements this transfer as a Triton
 // kernel (infera/engine/vllm/triton_kv_gather.py:82-220, with a Python loop
@@ -29,9 +32,11 @@ __global__ void page_copy_kernel(uint4* __restrict__ k_cache, uint4* __restrict_
   const long long tokens = static_cast<long long>(n_pages) * 16;
   const long long n = 16ll * vec_per_token;
   uint4* cbase = cache + (static_cast<long long>(l) * slots_per_layer + page * 16) * vec_per_token;
-  uint4* xbase = chunk + ((static_cast<long long>(c) * L + l) * tokens + static_cast<long long>(p) * 16) *
-                             vec_per_token;
-  if (dir == 0) {
+  const int C = gridDim.z;
+  uint4* xbase = (dir & 2) ? chunk + (((static_cast<long long>(p) * C + c) * L + l) * 16) * vec_per_token
+                           : chunk + ((static_cast<long long>(c) * L + l) * tokens + static_cast<long long>(p) * 16) *
+                                         vec_per_token;
+  if ((dir & 1) == 0) {
     for (long long i = threadIdx.x; i < n; i += blockDim.x) xbase[i] = cbase[i];
   } else {
     for (long long i = threadIdx.x; i < n; i += blockDim.x) cbase[i] = xbase[i];
@@ -42,13 +47,14 @@ __global__ void page_copy_kernel(uint4* __restrict__ k_cache, uint4* __restrict_
 }  // namespace ib200
 
 // k_cache / v_cache: [L, slots, H] of elem_bytes elements (v_cache unused when
-// channels == 1); chunk: [channels, L, n_pages*16, H].
+// channels == 1); chunk: [channels, L, n_pages*16, H] (dir 0 / 1) or
+// [n_pages, channels, L, 16, H] (dir 2 / 3).
 // H * elem_bytes must be a multiple of 16.
 extern "C" int ib_kv_page_copy(void* k_cache, void* v_cache, void* chunk, const int* pages, int n_pages, int L,
                                long long slots_per_layer, int H, int elem_bytes, int channels, int dir,
                                cudaStream_t stream) {
   if (n_pages <= 0) return 0;
-  if ((H * elem_bytes) % 16 != 0 || (dir != 0 && dir != 1) || (channels != 1 && channels != 2)) return -1;
+  if ((H * elem_bytes) % 16 != 0 || dir < 0 || dir > 3 || (channels != 1 && channels != 2)) return -1;
   dim3 grid(n_pages, L, channels);
   ib200::kvp::page_copy_kernel<<<grid, 256, 0, stream>>>(
       static_cast<uint4*>(k_cache), static_cast<uint4*>(v_cache), static_cast<uint4*>(chunk), pages, n_pages, L,

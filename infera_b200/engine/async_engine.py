@@ -170,6 +170,12 @@ class AsyncEngine:
         bm = self.engine.bm
         return {"block_size": bm.page_size, "block_hashes": [str(h) for h in bm.cached_hashes()], "ts": time.time()}
 
+    async def kv_index_snapshot(self) -> dict:
+        feed = getattr(self.engine, "kv_index", None)
+        if feed is None:
+            return {"error": "no KV index feed"}
+        return feed.snapshot()
+
     async def start_profile(self) -> dict:
         import torch
 

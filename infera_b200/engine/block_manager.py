@@ -35,6 +35,9 @@ class SeqBlocks:
     pages: list[int] = field(default_factory=list)
     hashes: list[int] = field(default_factory=list)   # hashes of the full pages registered so far
     num_cached_tokens: int = 0                          # tokens with K/V present (computed or hit)
+    # (first page, page count) that a KV tier holds and an asynchronous
+    # promote will fill; the scheduler parks the sequence until it lands
+    tier_load: tuple[int, int] | None = None
 
 
 class BlockManager:
@@ -148,11 +151,14 @@ class BlockManager:
             sb.pages.append(p)
         if n_tier > 0:
             start = len(hit_pages)
-            got = self.tier.load(sb.pages[start:start + n_tier], hashes[start:start + n_tier])
-            if got > 0:
-                self.commit_full_pages(sb, token_ids, (start + got) * self.page_size)
-                sb.num_cached_tokens = (start + got) * self.page_size
-                self.stats["tier_hit_tokens"] += got * self.page_size
+            if getattr(self.tier, "async_load", False):
+                sb.tier_load = (start, n_tier)
+            else:
+                got = self.tier.load(sb.pages[start:start + n_tier], hashes[start:start + n_tier])
+                if got > 0:
+                    self.commit_full_pages(sb, token_ids, (start + got) * self.page_size)
+                    sb.num_cached_tokens = (start + got) * self.page_size
+                    self.stats["tier_hit_tokens"] += got * self.page_size
         self.stats["hit_tokens"] += sb.num_cached_tokens
         self.stats["query_tokens"] += len(token_ids)
         return sb

@@ -64,11 +64,13 @@ def _unpack(b: bytes):
 class EngineCoreServer:
     """Drives an :class:`LLMEngine` from ZMQ commands. ``run()`` blocks."""
 
-    def __init__(self, engine, in_addr: str, out_addr: str, publisher=None, info: dict | None = None):
+    def __init__(self, engine, in_addr: str, out_addr: str, publisher=None, info: dict | None = None,
+                 index_feed=None):
         import zmq
 
         self.engine = engine
         self.publisher = publisher
+        self.index_feed = index_feed
         self.info = dict(info or {})
         self._ctx = zmq.Context.instance()
         self._pull = self._ctx.socket(zmq.PULL)
@@ -140,6 +142,10 @@ class EngineCoreServer:
         if name == "kv_snapshot":
             return {"block_size": eng.bm.page_size, "block_hashes": [str(h) for h in eng.bm.cached_hashes()],
                     "ts": time.time()}
+        if name == "kv_index_snapshot":
+            if self.index_feed is None:
+                return {"error": "no KV index feed"}
+            return self.index_feed.snapshot()
         if name == "profile_start":
             import torch
 
@@ -208,6 +214,8 @@ class EngineCoreServer:
             self._send_outputs(outs)
         if self.publisher is not None:
             self.publisher.flush()
+        if self.index_feed is not None:
+            self.index_feed.flush()
         return not self._stop
 
     def run(self, should_stop=None) -> None:
@@ -376,6 +384,9 @@ class EngineCoreClient:
     async def kv_snapshot(self) -> dict:
         return await self.call("kv_snapshot")
 
+    async def kv_index_snapshot(self) -> dict:
+        return await self.call("kv_index_snapshot")
+
     async def start_profile(self) -> dict:
         return await self.call("profile_start")
 
@@ -399,6 +410,17 @@ class EngineCoreClient:
 # ---------------------------------------------------------------------------
 
 
+def make_index_feed(a, page_size: int):
+    """The tier-aware KV index feed of ``--kv-index-endpoint`` (or None)."""
+    if not getattr(a, "kv_index_endpoint", None):
+        return None
+    from infera_b200.engine.kv_index_feed import KvIndexFeed
+    from infera_b200.kv.publisher import KvIndexPublisher
+
+    return KvIndexFeed(a.kv_index_publisher, a.kv_index_model or a.model, a.kv_index_compat, page_size,
+                       sink=KvIndexPublisher(a.kv_index_endpoint))
+
+
 def main(argv=None) -> None:
     """``python -m infera_b200.engine.core_ipc --in ADDR --out ADDR [engine flags]``"""
     import argparse
@@ -419,6 +441,11 @@ def main(argv=None) -> None:
     p.add_argument("--no-cuda-graphs", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-events-endpoint", default=None)
+    p.add_argument("--kv-index-endpoint", default=None,
+                   help="ZMQ PUB bind address of the tier-aware KV index events (topic kv-index)")
+    p.add_argument("--kv-index-publisher", default="", help="publisher id in those events (the worker id)")
+    p.add_argument("--kv-index-model", default="", help="served model name in those events")
+    p.add_argument("--kv-index-compat", default="", help="compat key (tokenizer digest) in those events")
     p.add_argument("--kv-tier", default=None)
     p.add_argument("--tp-size", type=int, default=1, help="tensor-parallel ranks (RANK / LOCAL_RANK / MASTER_* from env)")
     p.add_argument("--disagg-mode", choices=("mixed", "prefill", "decode"), default="mixed")
@@ -447,6 +474,9 @@ def main(argv=None) -> None:
                        num_pages=a.num_pages, use_cuda_graphs=not a.no_cuda_graphs, seed=a.seed, kv_tier=a.kv_tier,
                        disagg_mode=a.disagg_mode, kv_push_endpoint=a.kv_push_endpoint)
     eng = LLMEngine(cfg, device=device, event_sink=pub, tp=tp)
+    feed = make_index_feed(a, cfg.page_size) if rank == 0 else None
+    if feed is not None:
+        eng.attach_kv_index(feed)
     if rank > 0:
         from infera_b200.engine.tp_engine import follower_loop
 
@@ -461,7 +491,8 @@ def main(argv=None) -> None:
         served = TPLeader(eng, tp.gloo)
     srv = EngineCoreServer(served, a.in_addr, a.out_addr, publisher=pub,
                            info={"vocab": eng.model_cfg.vocab, "page_size": cfg.page_size,
-                                 "num_pages": eng.bm.num_pages, "pid": os.getpid(), "tp_size": a.tp_size})
+                                 "num_pages": eng.bm.num_pages, "pid": os.getpid(), "tp_size": a.tp_size},
+                           index_feed=feed)
     stop = [False]
     signal.signal(signal.SIGTERM, lambda *_: stop.__setitem__(0, True))
     srv.announce_ready()

@@ -62,6 +62,9 @@ class EngineConfig:
     # KV tiering: None (off), "host:<GiB>[:<nvme dir>]" (in-process host store,
     # optional NVMe tablespace) or "kvd:<socket path>" (shared daemon)
     kv_tier: str | None = None
+    # promote tier hits on a loader thread while the engine keeps stepping
+    # (tensor-parallel ranks always promote inline)
+    kv_tier_async: bool = True
     # prefill/decode disaggregation: "mixed", "prefill" or "decode"; a decode
     # instance serves its KV rendezvous on kv_push_endpoint
     disagg_mode: str = "mixed"
@@ -121,6 +124,7 @@ class LLMEngine:
             dist.all_reduce(t, op=dist.ReduceOp.MIN, group=tp.gloo)
             num_pages = int(t.item())
         self._event_sink = event_sink
+        self.kv_index = None
         self.bm = BlockManager(num_pages, cfg.page_size, cfg.enable_prefix_cache, event_sink=self._on_kv_event)
         self.scheduler = Scheduler(self.bm, cfg.max_num_seqs, cfg.max_batched_tokens, mcfg.max_model_len,
                                    watermark_pages=max(1, num_pages // 100),
@@ -132,9 +136,15 @@ class LLMEngine:
         if cfg.kv_tier:
             from infera_b200.engine.tiering import TierManager
 
+            tp_world = tp.world if tp is not None else 1
+            # tensor-parallel ranks hold different KV-head shards under the same
+            # block hashes (their keys carry the rank), and promote inline so
+            # that every rank makes the same scheduling decisions
             self.tier = TierManager(self.runner.k_cache, self.runner.v_cache, _tier_store(cfg.kv_tier),
-                                    cfg.page_size)
+                                    cfg.page_size, async_load=cfg.kv_tier_async and tp_world == 1,
+                                    key_tag=f"/tp{tp.rank}of{tp_world}".encode() if tp_world > 1 else b"")
             self.bm.tier = self.tier
+            self.scheduler.on_tier_load = self._begin_tier_load
         self.pd_rendezvous = None
         self.pd_agent = None
         if cfg.disagg_mode == "decode":
@@ -175,6 +185,16 @@ class LLMEngine:
     def _on_kv_event(self, kind: str, payload: dict) -> None:
         if self._event_sink is not None:
             self._event_sink(kind, payload)
+        if self.kv_index is not None:
+            self.kv_index.on_engine_event(kind, payload)
+
+    def attach_kv_index(self, feed) -> None:
+        """Announce this engine's device / host / disk blocks to the router's
+        tier-aware KV index through ``feed`` (a
+        :class:`~infera_b200.engine.kv_index_feed.KvIndexFeed`)."""
+        self.kv_index = feed
+        if self.tier is not None:
+            self.tier.index_sink = feed.on_tier_event
 
     def set_event_sink(self, sink: Callable[[str, dict], None] | None) -> None:
         self._event_sink = sink
@@ -264,6 +284,25 @@ class LLMEngine:
                 if st != "pending":
                     self.scheduler.resume_parked(r, st == "ok")
 
+    # ------------------------------------------------------------------ KV tiers
+    def _begin_tier_load(self, r: Request, pages: list[int], hashes: list[int]) -> None:
+        self.tier.begin_load(r, pages, hashes)
+
+    def _tier_progress(self) -> None:
+        """Requests whose tier promote landed: register the promoted pages in
+        the prefix cache and let them run."""
+        ps = self.bm.page_size
+        for r, got in self.tier.poll_loads():
+            if r.request_id in self.scheduler.loading and r.status != Status.FINISHED_ABORTED and got > 0:
+                done = (r.tier_start + got) * ps
+                self.bm.commit_full_pages(r.blocks, r.all_token_ids(), done)
+                r.num_computed = max(r.num_computed, done)
+                if r.num_preemptions == 0:
+                    r.num_cached_prompt_tokens = r.num_computed
+                self.bm.stats["tier_hit_tokens"] += got * ps
+                self.bm.stats["hit_tokens"] += got * ps
+            self.scheduler.resume_loaded(r)
+
     def _release_pushed(self, job) -> None:
         if job.blocks is not None:
             self.bm.free(job.blocks)
@@ -303,8 +342,15 @@ class LLMEngine:
         if self.pd_agent is not None or self.pd_rendezvous is not None:
             with self._phase("kv_push"):
                 self._pd_progress()
+        if self.tier is not None and self.scheduler.loading:
+            self._tier_progress()
         with self._phase("schedule"):
             sched = self.scheduler.schedule()
+        if self.tier is not None:
+            # evicted prefix pages are copied out before this step's forward
+            # can overwrite them; promotes start after that
+            self.tier.flush_saves()
+            self.tier.submit_loads()
         outputs: list[RequestOutput] = []
         for r in sched.preempted:
             if r.status == Status.FINISHED_LENGTH:  # prompt longer than the model allows
@@ -312,8 +358,9 @@ class LLMEngine:
             else:
                 self.counters["preemptions"] += 1
         if sched.empty:
-            if self.scheduler.parked or (self.pd_agent is not None and self.pd_agent.pending()):
-                time.sleep(0.0005)  # only waiting on a KV push
+            if (self.scheduler.parked or self.scheduler.loading
+                    or (self.pd_agent is not None and self.pd_agent.pending())):
+                time.sleep(0.0005)  # only waiting on a KV push or a tier promote
             return outputs
         upd = self._block_table_updates(sched.prefills + sched.decodes)
         layer_push = None

@@ -75,11 +75,16 @@ def pack_header(h: ChunkHeader, align: int = 4096) -> tuple[bytes, ChunkHeader]:
     return raw + b"\0" * (off - len(raw)), h
 
 
-def pack_chunk(h: ChunkHeader, payload, align: int = 4096) -> bytes:
+def pack_chunk(h: ChunkHeader, payload, align: int = 4096) -> bytearray:
+    """Header + payload in one buffer (the payload is copied once)."""
     hdr, h = pack_header(h, align)
-    if len(payload) != h.payload_bytes:
-        raise PackedFormatError(f"payload is {len(payload)} bytes, header says {h.payload_bytes}")
-    return hdr + bytes(payload)
+    n = memoryview(payload).nbytes
+    if n != h.payload_bytes:
+        raise PackedFormatError(f"payload is {n} bytes, header says {h.payload_bytes}")
+    out = bytearray(len(hdr) + n)
+    out[:len(hdr)] = hdr
+    out[len(hdr):] = memoryview(payload).cast("B")
+    return out
 
 
 def unpack_header(blob) -> ChunkHeader:

@@ -61,6 +61,8 @@ class Request:
     # pushes to (room, decode endpoint) once its prompt is computed
     remote_room: int | None = None
     remote_decode: tuple | None = None
+    # KV tiers: first page of the prefix an asynchronous promote fills
+    tier_start: int = 0
 
     @property
     def num_tokens(self) -> int:

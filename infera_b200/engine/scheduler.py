@@ -68,6 +68,11 @@ class Scheduler:
         # PD decode side: admitted requests waiting for their pushed KV
         self.parked: dict[str, Request] = {}
         self.on_park = None  # fn(request, pages to receive, skip_tokens, n_tokens)
+        # KV-tier promotes in flight: admitted requests whose prefix pages a
+        # tier is copying in (asynchronously); on_tier_load(request, pages,
+        # chained hashes) starts one
+        self.loading: dict[str, Request] = {}
+        self.on_tier_load = None
         self.free_rows: list[int] = list(range(max_num_seqs - 1, -1, -1))
 
     # ------------------------------------------------------------------
@@ -75,7 +80,19 @@ class Scheduler:
         self.waiting.append(req)
 
     def num_unfinished(self) -> int:
-        return len(self.waiting) + len(self.running) + len(self.parked)
+        return len(self.waiting) + len(self.running) + len(self.parked) + len(self.loading)
+
+    def resume_loaded(self, r: Request) -> None:
+        """A tier promote for ``r`` completed (the caller registered what
+        landed): the request runs, or - aborted meanwhile - its pages, which
+        the copies were writing, are released only now."""
+        if self.loading.pop(r.request_id, None) is None:
+            return
+        if r.status == Status.FINISHED_ABORTED:
+            self._release(r)
+            return
+        r.status = Status.RUNNING
+        self.running.append(r)
 
     def resume_parked(self, r: Request, pushed_ok: bool) -> None:
         """The pushed KV arrived (prompt minus its last token now cached) or
@@ -88,6 +105,11 @@ class Scheduler:
         self.running.append(r)
 
     def abort(self, request_id: str) -> Request | None:
+        r = self.loading.get(request_id)
+        if r is not None:
+            # the promote is still writing its pages: released when it lands
+            r.status = Status.FINISHED_ABORTED
+            return r
         r = self.parked.pop(request_id, None)
         if r is not None:
             self._release(r)
@@ -227,6 +249,15 @@ class Scheduler:
                 r.num_cached_prompt_tokens = sb.num_cached_tokens
             r.table_row = self.free_rows.pop()
             r.pages_synced = 0
+            tl, sb.tier_load = sb.tier_load, None
+            if tl is not None and self.on_tier_load is not None and r.remote_room is None:
+                # a tier holds the next blocks of the prompt: park the request
+                # until the asynchronous promote has copied them in
+                r.status = Status.WAITING
+                r.tier_start = tl[0]
+                self.loading[r.request_id] = r
+                self.on_tier_load(r, sb.pages[tl[0]:tl[0] + tl[1]], r.prompt_hashes[tl[0]:tl[0] + tl[1]])
+                continue
             if r.remote_room is not None and self.on_park is not None and r.num_preemptions == 0:
                 # PD decode: the prefill instance pushes the prompt's KV
                 # (all but the last token) into the pages beyond the prefix

@@ -186,8 +186,20 @@ def build_worker_app(aeng, tokenizer, model_name: str, extra_metrics=None) -> Fa
         return Response("\n".join(lines) + "\n", media_type="text/plain; version=0.0.4")
 
     @app.get("/v1/kv-snapshot")
-    async def kv_snapshot():
-        return await aeng.kv_snapshot()
+    async def kv_snapshot(model: str | None = None, compat_key: str | None = None):
+        """Without parameters: the device prefix cache's block hashes (the
+        router's seed-0 chain). With ``model`` and ``compat_key``: this
+        instance's chains in the tier-aware KV index (device / host / disk),
+        what the router's reconciler pulls."""
+        if model is None and compat_key is None:
+            return await aeng.kv_snapshot()
+        snap = await aeng.kv_index_snapshot()
+        if "error" in snap:
+            return JSONResponse(snap, status_code=404)
+        if (model is not None and snap.get("model") != model) or (
+                compat_key is not None and snap.get("compat") != compat_key):
+            return JSONResponse({"error": "no snapshot for that model / compat key"}, status_code=404)
+        return snap
 
     @app.post("/start_profile")
     async def start_profile(request: Request):

@@ -28,6 +28,22 @@ import socket
 logger = logging.getLogger(__name__)
 
 
+def _connect_addr(bind: str, host: str) -> str:
+    """A ZMQ bind address as peers connect to it (a wildcard host becomes
+    the advertised one)."""
+    for wild in ("tcp://*:", "tcp://0.0.0.0:"):
+        if bind.startswith(wild):
+            return f"tcp://{host}:" + bind[len(wild):]
+    return bind
+
+
+def worker_id(args) -> str:
+    host = args.advertise_host or args.host
+    if host in ("0.0.0.0", ""):
+        host = socket.gethostname()
+    return f"{host}:{args.port}"
+
+
 def build_payload(args, tokenizer) -> dict:
     from infera_b200.common.worker_pool import (DisaggMode, EngineType, KvRegistrationMetadata, WorkerInfo)
     from infera_b200.utils.tokenizer import canary
@@ -39,10 +55,13 @@ def build_payload(args, tokenizer) -> dict:
     meta = {}
     if args.disagg_mode != "mixed":
         meta = {"protocol": "b200-nvlink-push", "params": {"kv_endpoint": args.kv_push_endpoint or ""}}
+    idx_ep = getattr(args, "kv_index_endpoint", None)
+    tiers = ["device"] + (["host", "disk"] if args.kv_tier else [])
     kv = KvRegistrationMetadata(engine_block_size=args.page_size, index_block_size=args.page_size,
                                 tokenizer=tokenizer.name, tokenizer_digest=tokenizer.digest(),
-                                tokenizer_canary=canary(tokenizer), events_endpoint=args.kv_events_endpoint,
-                                snapshot_endpoint=f"http://{host}:{args.port}", tiers=["device"])
+                                tokenizer_canary=canary(tokenizer), supports_events=bool(idx_ep),
+                                events_endpoint=_connect_addr(idx_ep, host) if idx_ep else None,
+                                snapshot_endpoint=f"http://{host}:{args.port}", tiers=tiers)
     w = WorkerInfo(worker_id=wid, url=f"http://{host}:{args.port}", model_name=args.served_model_name or args.model,
                    engine=EngineType.INFERA_B200, disagg_mode=DisaggMode(args.disagg_mode), disagg_meta=meta,
                    kv_events_endpoint=args.kv_events_endpoint, kv_block_size=args.page_size, kv=kv,
@@ -72,6 +91,8 @@ def parse_args(argv=None):
     p.add_argument("--k8s-register", action="store_true",
                    help="register through this Pod's worker-info annotation (in-cluster service account)")
     p.add_argument("--kv-events-endpoint", default=None, help="ZMQ PUB bind address, e.g. tcp://127.0.0.1:5557")
+    p.add_argument("--kv-index-endpoint", default=None,
+                   help="ZMQ PUB bind address of the tier-aware KV index events (registered as kv.events_endpoint)")
     p.add_argument("--disagg-mode", choices=("mixed", "prefill", "decode"), default="mixed")
     p.add_argument("--kv-push-endpoint", default=None)
     p.add_argument("--drain-timeout", type=float, default=30.0)
@@ -103,6 +124,10 @@ def _core_cmd(args, in_addr: str, out_addr: str) -> list[str]:
         cmd.append("--no-cuda-graphs")
     if args.kv_events_endpoint:
         cmd += ["--kv-events-endpoint", args.kv_events_endpoint]
+    if getattr(args, "kv_index_endpoint", None):
+        cmd += ["--kv-index-endpoint", args.kv_index_endpoint, "--kv-index-publisher", worker_id(args),
+                "--kv-index-model", args.served_model_name or args.model,
+                "--kv-index-compat", getattr(args, "_compat", "")]
     if args.kv_tier:
         cmd += ["--kv-tier", args.kv_tier]
     cmd += ["--disagg-mode", args.disagg_mode]
@@ -126,9 +151,18 @@ async def start_engine(args):
                             use_cuda_graphs=not args.no_cuda_graphs, seed=args.seed, kv_tier=args.kv_tier,
                             disagg_mode=args.disagg_mode, kv_push_endpoint=args.kv_push_endpoint)
         eng = LLMEngine(ecfg, device=args.device, event_sink=pub)
+        feed = None
+        if getattr(args, "kv_index_endpoint", None):
+            from infera_b200.engine.kv_index_feed import KvIndexFeed
+            from infera_b200.kv.publisher import KvIndexPublisher
+
+            feed = KvIndexFeed(worker_id(args), args.served_model_name or args.model, getattr(args, "_compat", ""),
+                               args.page_size, sink=KvIndexPublisher(args.kv_index_endpoint))
+            eng.attach_kv_index(feed)
         aeng = AsyncEngine(eng)
         aeng.start()
-        flusher = asyncio.create_task(_flush_loop(pub)) if pub else None
+        flushers = [p for p in (pub, feed) if p is not None]
+        flusher = asyncio.create_task(_flush_loop(*flushers)) if flushers else None
 
         async def shutdown():
             aeng.stop()
@@ -203,8 +237,13 @@ async def run_worker(args) -> None:
         preflight(mode=args.disagg_mode, advertise_host=args.advertise_host or args.host,
                   kv_endpoint=args.kv_push_endpoint, single_node=(args.advertise_host or args.host) in
                   ("127.0.0.1", "localhost", "0.0.0.0"))
+    from infera_b200.models.config import get_config
+
+    # the tokenizer's digest is the KV index's compat key, which the engine
+    # core stamps on its index events: load it before the core starts
+    tok = load_tokenizer(args.tokenizer, vocab_size=get_config(args.model).vocab)
+    args._compat = tok.digest()
     aeng, vocab, shutdown_engine = await start_engine(args)
-    tok = load_tokenizer(args.tokenizer, vocab_size=vocab)
     app = build_worker_app(aeng, tok, args.served_model_name or args.model)
     server = uvicorn.Server(uvicorn.Config(app, host=args.host, port=args.port, log_level="warning",
                                            access_log=False))
@@ -271,10 +310,11 @@ async def run_worker(args) -> None:
         await bus.close()
 
 
-async def _flush_loop(pub) -> None:
+async def _flush_loop(*pubs) -> None:
     while True:
         await asyncio.sleep(0.01)
-        pub.flush()
+        for p in pubs:
+            p.flush()
 
 
 def main(argv=None) -> None:

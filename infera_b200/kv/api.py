@@ -40,6 +40,19 @@ def index_router(index) -> APIRouter:
     return r
 
 
+def stats_router(plane) -> APIRouter:
+    """``GET /v1/kv-stats``: counters of the router's index data plane
+    (index, writer, subscribers, reconciler), as ``infera/kv/api.py:78-133``
+    serves them."""
+    r = APIRouter()
+
+    @r.get("/v1/kv-stats")
+    async def kv_stats():
+        return plane.stats()
+
+    return r
+
+
 def publisher_router(probe) -> APIRouter:
     r = APIRouter()
 

@@ -80,6 +80,24 @@ class KVIndex:
             t = self._trees[key] = _Tree()
         return t
 
+    def drop_publisher(self, publisher: str) -> int:
+        """Forget every tree of ``publisher`` (it left the fleet)."""
+        keys = [k for k in self._trees if k[2] == publisher]
+        for k in keys:
+            del self._trees[k]
+        return len(keys)
+
+    def tier_counts(self, publisher: str) -> dict[str, int]:
+        """Blocks ``publisher`` holds per tier (over all its trees)."""
+        out: dict[str, int] = {}
+        for k, t in self._trees.items():
+            if k[2] != publisher:
+                continue
+            for node in t.by_seq.values():
+                for tier in node.tiers:
+                    out[tier.value] = out.get(tier.value, 0) + 1
+        return out
+
     def publishers(self, model: str, compat: str) -> list[str]:
         return [k[2] for k in self._trees if k[0] == model and k[1] == compat]
 
@@ -223,18 +241,20 @@ class KVIndex:
         return s
 
     def chains(self, key: IndexKey) -> list[tuple[list[BlockKey], Tier]]:
-        """Root-to-leaf chains with the fastest tier common to each chain
-        (what a snapshot carries)."""
+        """What a snapshot carries: for every tier, the root-to-leaf chains
+        of blocks that all hold that tier (a block in two tiers appears in a
+        chain of each; replaying the chains restores every node's tiers)."""
         t = self._trees.get(key)
         if t is None:
             return []
         out = []
-        stack = [(c, [c]) for c in t.root.children.values()]
-        while stack:
-            node, path = stack.pop()
-            if not node.children:
-                tier = max((min(x.tiers, key=lambda z: z.rank) for x in path), key=lambda z: z.rank)
-                out.append(([BlockKey(x.block_hash, x.sequence_hash) for x in path], tier))
-            for c in node.children.values():
-                stack.append((c, path + [c]))
+        for tier in Tier:
+            stack = [(c, [c]) for c in t.root.children.values() if tier in c.tiers]
+            while stack:
+                node, path = stack.pop()
+                kids = [c for c in node.children.values() if tier in c.tiers]
+                if not kids:
+                    out.append(([BlockKey(x.block_hash, x.sequence_hash) for x in path], tier))
+                for c in kids:
+                    stack.append((c, path + [c]))
         return out

@@ -118,7 +118,8 @@ class KvIndexSubscriber:
 
 
 class SnapshotReconciler:
-    """``fetch(publisher_url) -> snapshot dict``; ``publishers() -> [url]``."""
+    """``fetch(target) -> snapshot dict``; ``publishers() -> [target]`` (a
+    target is whatever ``fetch`` understands: a URL, or a tuple)."""
 
     def __init__(self, index: KVIndex, publishers, fetch, period_s: float = 30.0):
         self.index = index

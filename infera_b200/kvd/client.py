@@ -144,6 +144,10 @@ class SyncKvdStore:
     def exists(self, key: bytes) -> bool:
         return self._run(self.client.exists([key]))[0]
 
+    def exists_many(self, keys: list[bytes]) -> list[bool]:
+        """One round trip for a run of keys (the tier manager's hit count)."""
+        return self._run(self.client.exists(list(keys)))
+
     def close(self) -> None:
         self._run(self.client.close())
         self.loop.call_soon_threadsafe(self.loop.stop)

@@ -43,6 +43,12 @@ class HostStore:
         self.file_entries: dict[bytes, tuple] = {}
         self.stats = {"gets": 0, "sets": 0, "hits": 0, "misses": 0, "evictions": 0, "spills": 0, "promotions": 0,
                       "rejected": 0}
+        # fn(key, spilled: bool): an entry left host memory (to the NVMe tier
+        # when spilled); the engine's tier manager reports it to the KV index
+        self.listeners: list = []
+
+    def add_listener(self, fn) -> None:
+        self.listeners.append(fn)
 
     @staticmethod
     def _prio(retention: str) -> int:
@@ -57,12 +63,19 @@ class HostStore:
         e = self.entries.pop(key)
         self.lru[self._prio(e.retention)].pop(key, None)
         self.used -= e.size
+        spilled = False
         if spill and self.l3 is not None:
             data = self._read(e)
             if data is not None and self.l3.put(key, data, e.retention):
                 self.stats["spills"] += 1
+                spilled = True
         if e.slot is not None:
             self.arena.free(e.slot)
+        for fn in self.listeners:
+            try:
+                fn(key, spilled)
+            except Exception:
+                pass
 
     def _read(self, e: Entry) -> bytes | None:
         if e.slot is None:
@@ -101,7 +114,8 @@ class HostStore:
                 e.slot = self.arena.alloc()
                 e.version = self.arena.write(e.slot, value)
             else:
-                e.value = bytes(value)
+                # a buffer built for this call (a packed chunk) is kept as is
+                e.value = value if isinstance(value, (bytes, bytearray)) else bytes(value)
             self.entries[key] = e
             self.used += size
             self._touch(key, e)
@@ -165,6 +179,9 @@ class HostStore:
     def get(self, key: bytes) -> bytes | None:
         e = self.get_entry(key)
         return None if e is None else self._read(e)
+
+    def exists_many(self, keys: list[bytes]) -> list[bool]:
+        return [self.exists(k) for k in keys]
 
     def exists(self, key: bytes) -> bool:
         with self.lock:

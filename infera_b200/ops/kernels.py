@@ -494,10 +494,12 @@ def kv_channels(k_cache: torch.Tensor, v_cache: torch.Tensor) -> int:
 
 
 def kv_page_copy(k_cache: torch.Tensor, v_cache: torch.Tensor, chunk: torch.Tensor, pages: torch.Tensor,
-                 page_size: int = 16, gather: bool = True) -> None:
+                 page_size: int = 16, gather: bool = True, page_major: bool = False) -> None:
     """Move whole KV pages between the cache ([L, slots, H] per channel) and a
-    contiguous chunk [C, L, n_pages*page_size, H] (C = :func:`kv_channels`):
-    ``gather=True`` copies cache -> chunk (save), ``False`` chunk -> cache (load)."""
+    contiguous chunk [C, L, n_pages*page_size, H] (C = :func:`kv_channels`),
+    or with ``page_major`` [n_pages, C, L, page_size, H] (one chunk payload
+    per page): ``gather=True`` copies cache -> chunk (save), ``False`` chunk
+    -> cache (load)."""
     n = pages.shape[0]
     if n == 0:
         return
@@ -505,17 +507,24 @@ def kv_page_copy(k_cache: torch.Tensor, v_cache: torch.Tensor, chunk: torch.Tens
     C = kv_channels(k_cache, v_cache)
     if not k_cache.is_cuda:
         idx = (pages.long()[:, None] * page_size + torch.arange(page_size)[None, :]).reshape(-1)
-        view = chunk.view(C, L, n * page_size, H)
         for c, cache in enumerate((k_cache, v_cache)[:C]):
-            if gather:
-                view[c] = cache[:, idx]
+            if page_major:
+                view = chunk.view(n, C, L, page_size, H)
+                if gather:
+                    view[:, c] = cache[:, idx].view(L, n, page_size, H).permute(1, 0, 2, 3)
+                else:
+                    cache[:, idx] = view[:, c].permute(1, 0, 2, 3).reshape(L, n * page_size, H)
             else:
-                cache[:, idx] = view[c]
+                view = chunk.view(C, L, n * page_size, H)
+                if gather:
+                    view[c] = cache[:, idx]
+                else:
+                    cache[:, idx] = view[c]
         return
     assert page_size == 16 and chunk.is_contiguous()
     rc = _native.kernels().ib_kv_page_copy(k_cache.data_ptr(), v_cache.data_ptr(), chunk.data_ptr(),
                                            pages.data_ptr(), n, L, slots, H, k_cache.element_size(), C,
-                                           0 if gather else 1, _stream())
+                                           (0 if gather else 1) | (2 if page_major else 0), _stream())
     _native.check(rc, "ib_kv_page_copy")
     _count()
 

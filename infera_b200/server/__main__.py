@@ -1,7 +1,8 @@
 """``python -m infera_b200.server``: the router process.
 
 Builds the policy (KV-aware: tokenizer + KV-event client), the breaker and
-metrics, the registry (etcd gateway, Kubernetes, or in-process) whose
+metrics, the tier-aware KV index plane (index, writer, per-worker
+subscribers, snapshot reconciler), the registry (etcd gateway, Kubernetes, or in-process) whose
 add/remove callbacks feed the policy, then the Auto or Direct router and the
 FastAPI app, and serves it with uvicorn. ``--router-backend native`` execs
 the C++ router binary instead (same flags where supported). Structure of
@@ -53,6 +54,14 @@ def build_router_stack(args, registry=None, transport=None):
             registry = InProcessRegistry()
     registry.on_worker_added(policy.on_worker_added)
     registry.on_worker_removed(lambda w: (policy.on_worker_removed(w.worker_id), breaker.forget(w.worker_id)))
+    # the tier-aware KV index: workers that register a kv block with an
+    # events endpoint publish which prefixes they hold in GPU memory, host
+    # memory and on disk
+    from infera_b200.kv.plane import KvIndexPlane
+
+    kv_plane = KvIndexPlane()
+    registry.on_worker_added(kv_plane.on_worker_added)
+    registry.on_worker_removed(kv_plane.on_worker_removed)
     kw = dict(breaker=breaker, request_max_retries=args.request_max_retries, migration_limit=args.migration_limit,
               metrics=metrics)
     if transport is None and getattr(args, "request_transport", "http") == "nats":
@@ -81,7 +90,7 @@ def build_router_stack(args, registry=None, transport=None):
 
         kvd = KvdPrefetchClient(args.kvd_socket_path)
     return AppState(router=router, registry=registry, policy=policy, metrics=metrics, profiler=profiler,
-                    scaler=scaler, kvd_client=kvd, block_size=args.block_size)
+                    scaler=scaler, kvd_client=kvd, block_size=args.block_size, kv_plane=kv_plane)
 
 
 async def serve(args) -> None:
@@ -100,6 +109,7 @@ async def serve(args) -> None:
 
             bus = await NatsBus(args.nats_url).connect()
         await kv.attach_nats(bus)
+    await state.kv_plane.start()
     await state.registry.start()
     app = build_app(state)
     cfg = uvicorn.Config(app, host=args.host, port=args.port, log_level=args.log_level, access_log=False)
@@ -108,6 +118,7 @@ async def serve(args) -> None:
         await server.serve()
     finally:
         await state.registry.stop()
+        await state.kv_plane.stop()
         await state.router.aclose()
         await state.policy.aclose()
 

@@ -10,6 +10,8 @@ Routes (paths and status codes of ``infera/server/app.py:110-619``):
     GET|POST /v1/admin/scale                     404 unless the scaling API is on
     POST /v1/cache/prewarm                       202 / 400 / 503
     GET  /health, /metrics
+    GET  /v1/kv-stats, /v1/kv-index/stats        tier-aware KV index counters
+    POST /v1/kv-index/match                      per-publisher, per-tier prefix overlap
 
 Every inference request is stamped with an ``X-Infera-Request-Id`` (body
 field ``_infera_request_id`` while inside the router; response header on
@@ -48,6 +50,7 @@ class AppState:
     scaler: object = None            # DeploymentScaler or None (disabled)
     kvd_client: object = None        # prefetch-hint sink or None
     block_size: int = 16
+    kv_plane: object = None          # tier-aware KV index plane (infera_b200.kv.plane) or None
     extra: dict = field(default_factory=dict)
 
 
@@ -63,6 +66,11 @@ def _stash_gateway_headers(body: dict, request: Request) -> None:
 def build_app(state: AppState) -> FastAPI:
     app = FastAPI(title="infera-b200")
     app.state.s = state
+    if state.kv_plane is not None:
+        from infera_b200.kv.api import index_router, stats_router
+
+        app.include_router(stats_router(state.kv_plane))
+        app.include_router(index_router(state.kv_plane.index))
 
     async def dispatch_inference(request: Request, path: str) -> Response:
         try:
@@ -152,8 +160,11 @@ def build_app(state: AppState) -> FastAPI:
         if state.registry.pool.get(worker_id) is None:
             return JSONResponse({"error": f"unknown worker {worker_id!r}"}, status_code=404)
         view = client.cache_view(worker_id, dp_rank)
-        return {"worker_id": worker_id, "dp_rank": dp_rank, "num_blocks": len(view),
-                "block_hashes": [str(h) for h in list(view)[:10000]]}
+        out = {"worker_id": worker_id, "dp_rank": dp_rank, "num_blocks": len(view),
+               "block_hashes": [str(h) for h in list(view)[:10000]]}
+        if state.kv_plane is not None:   # blocks per tier (device / host / disk) in the tier-aware index
+            out["index_tiers"] = state.kv_plane.index.tier_counts(worker_id)
+        return out
 
     @app.post("/v1/admin/profile/{action}")
     async def profile(action: str, request: Request):

@@ -39,9 +39,13 @@ def test_kv_page_copy_roundtrip():
     assert torch.equal(k2[:, 48:64], k[:, 48:64]) and torch.equal(v2[:, 16:32], v[:, 16:32])
 
 
-def test_engine_tier_save_and_promote():
+@pytest.mark.parametrize("async_load", [True, False])
+def test_engine_tier_save_and_promote(async_load):
+    """Asynchronous promote: the request waits (parked) while the loader
+    copies its prefix in, the engine keeps stepping; inline promote: the
+    copies are issued at admission."""
     eng = LLMEngine(EngineConfig(model="tiny-dense", use_cuda_graphs=False, num_pages=12, max_batched_tokens=256,
-                                 kv_tier="host:0.05"), device="cpu")
+                                 kv_tier="host:0.05", kv_tier_async=async_load), device="cpu")
     g = torch.Generator().manual_seed(4)
     a = torch.randint(0, 1000, (64,), generator=g).tolist()
     sp = SamplingParams(max_tokens=2, ignore_eos=True)
@@ -58,3 +62,28 @@ def test_engine_tier_save_and_promote():
         if x != y:
             assert margins[i] < 0.05
             break
+
+
+def test_tier_promote_abort_releases_pages_after_landing():
+    """A request aborted while its promote is in flight keeps its pages until
+    the copies land (they are being written), then frees them."""
+    eng = LLMEngine(EngineConfig(model="tiny-dense", use_cuda_graphs=False, num_pages=12, max_batched_tokens=256,
+                                 kv_tier="host:0.05"), device="cpu")
+    g = torch.Generator().manual_seed(9)
+    a = torch.randint(0, 1000, (64,), generator=g).tolist()
+    sp = SamplingParams(max_tokens=2, ignore_eos=True)
+    eng.generate([a], sp)
+    for _ in range(3):
+        eng.generate([torch.randint(0, 1000, (64,), generator=g).tolist()], sp)
+    eng.tier.flush()
+    free0 = eng.bm.num_free()
+    eng.add_request("x", a + [1, 2], SamplingParams(max_tokens=4, ignore_eos=True))
+    eng.step()                                    # admitted and parked while the promote runs
+    assert "x" in eng.scheduler.loading
+    assert eng.abort_request("x")
+    assert "x" in eng.scheduler.loading           # pages held until the copies land
+    for _ in range(200):
+        if not eng.has_unfinished():
+            break
+        eng.step()
+    assert not eng.scheduler.loading and eng.bm.num_free() == free0
