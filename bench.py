@@ -204,6 +204,7 @@ def run_ours(args) -> dict:
         "h2d": h2d1 - h2d0, "d2h": d2h1 - d2h0,
         "prefix_hit_rate": st["prefix_hit_rate"], "clocks": clocks,
         "kernel_status": K.scratch(dev).read_status(),
+        "step_profile": rp.step_profile((w0, w1)),
     }
     e2e_local = None
     if not args.no_e2e:
@@ -245,6 +246,7 @@ def run_ours(args) -> dict:
         "prefix_hit_rate": sum(r["prefix_hit_rate"] for r in allr) / len(allr),
         "clocks": allr[0]["clocks"],
         "kernel_status": max(r["kernel_status"] for r in allr),
+        "step_profile": allr[0]["step_profile"],
         "engine_cfg": {"max_num_seqs": eng_cfg.max_num_seqs, "max_batched_tokens": eng_cfg.max_batched_tokens},
     }
     if e2e_all is not None:
@@ -316,6 +318,7 @@ def main(argv=None) -> int:
         "prefix_hit_rate": round(res["prefix_hit_rate"], 4),
         "engine_iterations": res["engine_steps"],
         "kernel_status": res["kernel_status"],
+        "step_profile_rank0": res["step_profile"],
         "clocks": res["clocks"],
         "gpu_launches": res["launches"],
         "impl": "ours",

@@ -43,6 +43,7 @@ class EngineReplay:
         self.t0_host = None
         self.ev0 = None
         self.step_events: list = []         # (event, host_time)
+        self.step_shapes: list = []         # (prompt tokens, decoding sequences) per step
         self.token_steps: dict[str, list[int]] = {}
         self.collected: dict[str, list[int]] = {}
         self.next_arrival = None
@@ -120,6 +121,7 @@ class EngineReplay:
             if self.eng.has_unfinished():
                 outs = self.eng.step()
                 step_idx = len(self.step_events)
+                self.step_shapes.append(getattr(self.eng, "last_step_shape", (0, 0)))
                 if self.device_timing:
                     ev = torch.cuda.Event(enable_timing=True)
                     ev.record()
@@ -149,6 +151,31 @@ class EngineReplay:
                     time.sleep(min(wait, t_end - now, 0.002))
 
     # ------------------------------------------------------------------ results
+    def step_profile(self, window: tuple[float, float]) -> dict:
+        """Durations of the engine steps that ended inside ``window`` (device
+        time between consecutive step-end events), by kind: decode-only,
+        mixed (prompt chunks joining decodes, by prompt tokens) and
+        prompt-only. Call after :meth:`resolve`."""
+        from infera_b200.bench.slo import percentile
+
+        times = self._times
+        kinds: dict[str, list[float]] = {}
+        toks: dict[str, list[int]] = {}
+        for i in range(1, len(times)):
+            if not (window[0] <= times[i] <= window[1]):
+                continue
+            pt, nd = self.step_shapes[i]
+            if nd and not pt:
+                k = "decode"
+            elif nd:
+                k = "mixed<=256" if pt <= 256 else ("mixed<=512" if pt <= 512 else "mixed>512")
+            else:
+                k = "prefill"
+            kinds.setdefault(k, []).append(1000 * (times[i] - times[i - 1]))
+            toks.setdefault(k, []).append(pt)
+        return {k: {"n": len(v), "p50_ms": round(percentile(v, 50), 3), "p99_ms": round(percentile(v, 99), 3),
+                    "mean_prompt_tokens": round(sum(toks[k]) / len(v), 1)} for k, v in sorted(kinds.items())}
+
     def resolve(self) -> list[ReqRecord]:
         """Convert step indices into timestamps (device when available)."""
         if self.device_timing:
@@ -156,6 +183,7 @@ class EngineReplay:
             times = [self.ev0.elapsed_time(ev) / 1000.0 for ev, _ in self.step_events]
         else:
             times = [t for _, t in self.step_events]
+        self._times = times
         out = []
         for rid, rec in self.records.items():
             steps = self.token_steps.get(rid, [])

@@ -159,6 +159,7 @@ class LLMEngine:
         # replays them on its followers (None: not recorded)
         self.cmd_log: list | None = None
         self.num_steps = 0
+        self.last_step_shape = (0, 0)
         self.clock: Callable[[], float] = time.monotonic
         self.counters = {"prompt_tokens": 0, "generation_tokens": 0, "finished": 0, "preemptions": 0}
         # named phase ranges (torch.profiler record_function + NVTX) while a
@@ -382,6 +383,8 @@ class LLMEngine:
             layer_push.finish()
         now = self.clock()
         self.num_steps += 1
+        # (prompt tokens, decoding sequences) of this step, for step-time profiles
+        self.last_step_shape = (sum(c.num_tokens for c in sched.prefills), len(sched.decodes))
         for c in sched.prefills:
             c.req.num_computed = c.start + c.num_tokens
             self.counters["prompt_tokens"] += c.num_tokens
