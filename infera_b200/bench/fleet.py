@@ -64,7 +64,8 @@ class ServerThread:
 
 class MockWorker:
     def __init__(self, idx: int, etcd_url: str, model: str, *, capacity_blocks=4096, prefill_ms=0.05,
-                 decode_ms=10.0, vocab=32000, port: int | None = None, engine: str = "infera-b200"):
+                 decode_ms=10.0, vocab=32000, port: int | None = None, engine: str = "infera-b200",
+                 word_ids: bool = False):
         from infera_b200.bench.mock_engine import MockEngine, build_mock_app
         from infera_b200.common.worker_pool import EngineType, KvRegistrationMetadata, WorkerInfo
         from infera_b200.engine.kv_events import KvEventPublisher
@@ -76,7 +77,7 @@ class MockWorker:
         self.pub = KvEventPublisher(self.ev_endpoint, flush_ms=0.0)
         self.eng = MockEngine(capacity_blocks=capacity_blocks, prefill_ms_per_token=prefill_ms,
                               decode_ms_per_token=decode_ms, vocab=vocab, publisher=self.pub, seed=idx)
-        self.server = ServerThread(build_mock_app(self.eng, model), self.port)
+        self.server = ServerThread(build_mock_app(self.eng, model, word_ids=word_ids), self.port)
         tok = ByteTokenizer(vocab_size=vocab)
         kv = KvRegistrationMetadata(engine_block_size=16, index_block_size=16, tokenizer=tok.name,
                                     tokenizer_digest=tok.digest(), tokenizer_canary=canary(tok),
@@ -125,11 +126,11 @@ class WorkerProcess:
     real SIGTERM."""
 
     def __init__(self, idx: int, etcd_url: str, model: str, *, decode_ms: float = 10.0, prefill_ms: float = 0.05,
-                 engine: str = "infera-b200"):
+                 engine: str = "infera-b200", word_ids: bool = False):
         self.port = free_port()
         self.cmd = [sys.executable, "-m", "infera_b200.bench.fleet", "--serve-worker", "--etcd", etcd_url,
                     "--index", str(idx), "--model", model, "--port", str(self.port), "--decode-ms", str(decode_ms),
-                    "--prefill-ms", str(prefill_ms), "--engine", engine]
+                    "--prefill-ms", str(prefill_ms), "--engine", engine] + (["--word-ids"] if word_ids else [])
         self.proc = None
         self.worker_id = f"127.0.0.1:{self.port}"
         self.final: dict = {}
@@ -181,7 +182,7 @@ def serve_worker(a) -> None:
 
     async def go():
         w = MockWorker(a.index, a.etcd, a.model, decode_ms=a.decode_ms, prefill_ms=a.prefill_ms, port=a.port,
-                       engine=a.engine)
+                       engine=a.engine, word_ids=a.word_ids)
         await w.start()
         print(json.dumps({"worker_id": w.info.worker_id}), flush=True)
         stop = asyncio.Event()
@@ -196,8 +197,12 @@ def serve_worker(a) -> None:
 
 async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 60.0, drain_at: float | None = 30.0,
                     sessions: int = 64, policy: str = "kv-aware", seed: int = 0, trace: str = "router-plumbing",
-                    decode_ms: float = 10.0, prefill_ms: float = 0.05, router_backend: str = "python") -> dict:
-    """``router_backend``: "python" (the router stack in this process),
+                    decode_ms: float = 10.0, prefill_ms: float = 0.05, router_backend: str = "python",
+                    text_prompts: bool = False) -> dict:
+    """``text_prompts``: prompts go as ``t<id>`` word text that the router
+    tokenizes with a word-level ``tokenizer.json`` (always on for the
+    reference router, which accepts text only); else as token ids.
+    ``router_backend``: "python" (the router stack in this process),
     "native" (the C++ router binary as a child process) or "reference" (the
     reference's router, ``python -m infera.server``, as a child process)."""
     from types import SimpleNamespace
@@ -207,6 +212,12 @@ async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 6
     from infera_b200.server.app import build_app
 
     model = "mock-model"
+    text_prompts = text_prompts or router_backend == "reference"
+    tok_dir = None
+    if text_prompts:
+        from infera_b200.bench.hf_model_dir import write_model_dir
+
+        tok_dir = write_model_dir("/tmp/infera_fleet_tokenizer", "llama-3.1-8b")   # word-level t<id> tokenizer
     etcd = ServerThread(etcd_app(), free_port()).start()
     etcd_url = f"http://127.0.0.1:{etcd.port}"
     # the worker that is shut down mid-run is a separate process (SIGTERM)
@@ -214,13 +225,13 @@ async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 6
     # the mocks speak vLLM's API and KV events; the reference's registry only
     # accepts the engine types it knows
     eng_t = "vllm" if router_backend == "reference" else "infera-b200"
-    ws = [MockWorker(i, etcd_url, model, decode_ms=decode_ms, prefill_ms=prefill_ms, engine=eng_t)
-          for i in range(workers - n_proc)]
+    ws = [MockWorker(i, etcd_url, model, decode_ms=decode_ms, prefill_ms=prefill_ms, engine=eng_t,
+                     word_ids=text_prompts) for i in range(workers - n_proc)]
     for w in ws:
         await w.start()
     if n_proc:
         ws.append(WorkerProcess(workers - 1, etcd_url, model, decode_ms=decode_ms, prefill_ms=prefill_ms,
-                                engine=eng_t).start())
+                                engine=eng_t, word_ids=text_prompts).start())
     native = None
     state = None
     if router_backend in ("native", "reference"):
@@ -233,15 +244,14 @@ async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 6
 
             cmd = [router_binary(), "--port", str(rport), "--host", "127.0.0.1", "--discovery-backend", "etcd",
                    "--etcd-endpoint", etcd_url, "--router-policy", policy, "--log-level", "warning"]
+            if tok_dir:
+                cmd += ["--router-tokenizer-path", os.path.join(tok_dir, "tokenizer.json")]
             env = None
         else:
             # the reference's own router, unmodified (installed under baseline/_ref)
             ref = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
                                "baseline", "_ref")
             env = dict(os.environ, PYTHONPATH=ref, HF_HUB_OFFLINE="1", TRANSFORMERS_OFFLINE="1")
-            from infera_b200.bench.hf_model_dir import write_model_dir
-
-            tok_dir = write_model_dir("/tmp/infera_fleet_tokenizer", "llama-3.1-8b")   # word-level t<id> tokenizer
             cmd = [sys.executable, "-m", "infera.server", "--discovery-backend", "etcd", "--etcd-endpoint",
                    etcd_url.replace("http://", ""), "--router-policy", policy, "--host", "127.0.0.1",
                    "--port", str(rport), "--router-tokenizer-path", tok_dir, "--request-transport", "http",
@@ -250,7 +260,7 @@ async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 6
         native = subprocess.Popen(cmd, stdout=log, stderr=subprocess.STDOUT, start_new_session=True, env=env)
         router_url = f"http://127.0.0.1:{rport}"
     else:
-        args = SimpleNamespace(router_policy=policy, router_tokenizer_path=None, kv_overlap_weight=1.0,
+        args = SimpleNamespace(router_policy=policy, router_tokenizer_path=tok_dir, kv_overlap_weight=1.0,
                                kv_prefill_overlap_weight=None, kv_decode_overlap_weight=None,
                                breaker_failure_threshold=3, breaker_cooldown_s=5.0, breaker_max_cooldown_s=60.0,
                                discovery_backend="etcd", etcd_endpoint=etcd_url, etcd_prefix="/infera/workers/",
@@ -284,7 +294,7 @@ async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 6
 
     try:
         return await _drive(ws, listed, view_size, router_url, workers, drain_at, trace, sessions, rate, duration, seed,
-                            model, policy)
+                            model, policy, text_prompts=router_backend == "reference")
     finally:
         if native is not None:
             native.terminate()
@@ -305,7 +315,7 @@ async def run_fleet(*, workers: int = 4, rate: float = 20.0, duration: float = 6
 
 
 async def _drive(ws, listed, view_size, router_url, workers, drain_at, trace, sessions, rate, duration, seed, model,
-                 policy) -> dict:
+                 policy, text_prompts: bool = False) -> dict:
     from infera_b200.bench.http_loadgen import run as loadgen
 
     t_wait = time.time()
@@ -328,7 +338,8 @@ async def _drive(ws, listed, view_size, router_url, workers, drain_at, trace, se
         drain_info.update(info)
 
     dtask = asyncio.create_task(drainer()) if drain_at is not None and workers > 1 else None
-    res = await loadgen(router_url, model, trace, list(range(sessions)), rate, duration, seed, stop_after_s=30.0)
+    res = await loadgen(router_url, model, trace, list(range(sessions)), rate, duration, seed, stop_after_s=30.0,
+                        text_prompts=text_prompts)
     if dtask is not None:
         await dtask
     recs = [r for r in res["records"] if r["token_times"]]
@@ -356,6 +367,8 @@ def main(argv=None) -> None:
     ap.add_argument("--policy", default="kv-aware")
     ap.add_argument("--router-backend", choices=("python", "native", "reference"), default="python",
                     help="reference: the reference's own router (baseline/_ref) in front of the same mock fleet")
+    ap.add_argument("--text-prompts", action="store_true",
+                    help="send prompts as t<id> word text tokenized by the router (word-level tokenizer.json)")
     ap.add_argument("--serve-worker", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--etcd", default=None, help=argparse.SUPPRESS)
     ap.add_argument("--index", type=int, default=0, help=argparse.SUPPRESS)
@@ -364,12 +377,14 @@ def main(argv=None) -> None:
     ap.add_argument("--decode-ms", type=float, default=10.0)
     ap.add_argument("--prefill-ms", type=float, default=0.05)
     ap.add_argument("--engine", default="infera-b200", help=argparse.SUPPRESS)
+    ap.add_argument("--word-ids", action="store_true", help=argparse.SUPPRESS)
     a = ap.parse_args(argv)
     if a.serve_worker:
         serve_worker(a)
         return
     res = asyncio.run(run_fleet(workers=a.workers, rate=a.rate, duration=a.duration, drain_at=a.drain_at,
-                                sessions=a.sessions, policy=a.policy, router_backend=a.router_backend))
+                                sessions=a.sessions, policy=a.policy, router_backend=a.router_backend,
+                                text_prompts=a.text_prompts))
     print(json.dumps(res, indent=1))
 
 

@@ -103,9 +103,27 @@ class MockEngine:
             yield self.rng.randrange(self.vocab), hit
 
 
-def build_mock_app(eng: MockEngine, model: str) -> FastAPI:
+class WordIdTokenizer:
+    """Text prompts written as ``t<id>`` words (one word per token id), the
+    form in which the benchmark sends token-id traces through routers that
+    accept text only (see ``infera_b200.bench.hf_model_dir``)."""
+
+    name = "word-ids"
+
+    def encode(self, text: str, add_bos: bool = False) -> list[int]:
+        from infera_b200.bench.hf_model_dir import text_to_ids
+
+        return text_to_ids(text)
+
+    def apply_chat_template(self, messages: list[dict], add_generation_prompt: bool = True) -> list[int]:
+        return self.encode(" ".join(str(m.get("content") or "") for m in messages))
+
+
+def build_mock_app(eng: MockEngine, model: str, word_ids: bool = False) -> FastAPI:
+    """``word_ids``: string prompts are ``t<id>`` words and generated text
+    is written the same way (for text-only routers)."""
     app = FastAPI()
-    tok = ByteTokenizer(vocab_size=eng.vocab)
+    tok = WordIdTokenizer() if word_ids else ByteTokenizer(vocab_size=eng.vocab)
 
     async def run(body: dict, chat: bool):
         if eng.draining:
@@ -122,8 +140,9 @@ def build_mock_app(eng: MockEngine, model: str) -> FastAPI:
         eng.inflight += 1
 
         def chunk(tok_id, finish):
-            c = ({"index": 0, "delta": {"content": "x"}, "finish_reason": finish} if chat
-                 else {"index": 0, "text": "x", "finish_reason": finish})
+            txt = f" t{tok_id}" if word_ids else "x"
+            c = ({"index": 0, "delta": {"content": txt}, "finish_reason": finish} if chat
+                 else {"index": 0, "text": txt, "finish_reason": finish})
             if want_ids:
                 c["token_ids"] = [tok_id]
             return {"id": rid, "object": kind, "created": created, "model": model, "choices": [c]}
