@@ -239,8 +239,9 @@ class TierManager:
         """Read blobs into pinned buffer ``buf``; returns how many consecutive
         pages were filled (a blob that vanished or fails to parse ends it)."""
         m = 0
+        read = getattr(self.store, "read", self.store.get)
         for i, (page, h) in enumerate(zip(pages, hashes)):
-            blob = self.store.get(self._key(h))
+            blob = read(self._key(h))
             if blob is None:
                 break
             try:

@@ -180,6 +180,21 @@ class HostStore:
         e = self.get_entry(key)
         return None if e is None else self._read(e)
 
+    def read(self, key: bytes) -> bytes | None:
+        """The value from host memory, or straight from the NVMe tier
+        without promoting it into host memory (a reader that copies it
+        onward - the engine promoting into HBM - needs no host copy kept)."""
+        with self.lock:
+            self.stats["gets"] += 1
+            e = self._live(key)
+            if e is not None:
+                self.stats["hits"] += 1
+                self._touch(key, e)
+                return self._read(e)
+            data = self.l3.get(key) if self.l3 is not None and key in self.l3 else None
+            self.stats["hits" if data is not None else "misses"] += 1
+            return data
+
     def exists_many(self, keys: list[bytes]) -> list[bool]:
         return [self.exists(k) for k in keys]
 

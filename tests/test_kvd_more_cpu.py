@@ -93,3 +93,12 @@ def test_tablespace_evicts_lowest_priority_first(tmp_path):
 def test_tablespace_rejects_bad_geometry(tmp_path):
     with pytest.raises(ValueError):
         Tablespace(str(tmp_path / "bad"), container_bytes=10000, slot_bytes=4096)
+
+
+def test_l3_bench_round_trip_through_the_tier_path(tmp_path):
+    """The L3 bench drives the engine's tier manager: pages saved through the
+    host store land on the tablespace and come back byte for byte."""
+    from infera_b200.kvd.bench import run
+
+    res = run(str(tmp_path / "l3"), total_gb=0.01, device="cpu", layers=2, batch_pages=8, chunk_pages=4)
+    assert res["round_trip_ok"] and res["saved"] == res["pages"] and res["reload_gbs"] > 0
