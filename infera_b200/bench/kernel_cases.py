@@ -5,7 +5,9 @@ footprint, inputs larger than L2 where the case is memory-bound).
 
 Cases: gemm_prefill (2048x6144x4096 bf16), gemm_decode (64 tokens x
 28672x4096, SwiGLU epilogue), gemm_lmhead (64x128256x4096), decode_attn
-(32 seqs x 8192 keys, GQA 32/8), fp8_decode (64 x 28672 x 8192 e4m3,
+(32 seqs x 8192 keys, GQA 32/8), decode_attn_shared / decode_attn_private
+(24 seqs, 4096-token prefix shared by groups of 12 or all pages private, +1k-12k
+tail each), fp8_decode (64 x 28672 x 8192 e4m3,
 block scales, SwiGLU), fp8_prefill (4096 x 8192 x 8192 e4m3), mla_decode (64
 queries x 128 heads over 4096 latent keys each), prefill_attn (2048 queries over 2048 keys,
 causal), prefill_attn_prefix (1024 queries over 8192 keys). Prints one JSON
@@ -92,6 +94,41 @@ def run_case(case: str, iters: int) -> dict:
         ms = _time(lambda: K.attn_decode(q, kc, vc, bt, sl, hq, hkv, 1 / math.sqrt(D), splits=sp), iters)
         by = 2 * B * L * hkv * D * 2
         return {"case": case, "ms": ms, "gbs": by / ms / 1e6, "splits": sp}
+    if case in ("decode_attn_shared", "decode_attn_private"):
+        # the serving trace's decode batch: 24 sequences in 2 groups of 12 that
+        # share a 4096-token system prefix (the same physical pages, as the
+        # prefix cache hands them out), then private tails of 1k-12k tokens;
+        # "private": the same lengths with every page distinct
+        B, P = 24, 4096
+        gg = torch.Generator().manual_seed(1)
+        tails = torch.randint(1000, 12000, (B,), generator=gg).tolist()
+        lens = [P + t for t in tails]
+        shared = case == "decode_attn_shared"
+        n_pages = (2 * P // 16 if shared else 0) + sum(((n if not shared else n - P) + 15) // 16 for n in lens)
+        kc = torch.randn(n_pages * 16, hkv * D, device=dev, generator=g).to(bf)
+        vc = torch.randn(n_pages * 16, hkv * D, device=dev, generator=g).to(bf)
+        perm = torch.randperm(n_pages, generator=gg).tolist()
+        width = max((n + 15) // 16 for n in lens)
+        bt = torch.zeros(B, width, dtype=torch.int32)
+        nxt = 2 * P // 16 if shared else 0
+        for b, n in enumerate(lens):
+            row = []
+            if shared:
+                grp = b % 2
+                row += perm[grp * (P // 16):(grp + 1) * (P // 16)]
+            need = (n + 15) // 16 - len(row)
+            row += perm[nxt:nxt + need]
+            nxt += need
+            bt[b, :len(row)] = torch.tensor(row, dtype=torch.int32)
+        bt = bt.to(dev)
+        sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+        q = torch.randn(B, hq * D, device=dev, generator=g).to(bf)
+        sp = K.decode_splits(B, hkv, max(lens))
+        ms = _time(lambda: K.attn_decode(q, kc, vc, bt, sl, hq, hkv, 1 / math.sqrt(D), splits=sp), iters)
+        by_all = sum(lens) * hkv * D * 2 * 2
+        by_unique = n_pages * 16 * hkv * D * 2 * 2
+        return {"case": case, "ms": ms, "gbs_all_keys": by_all / ms / 1e6, "gbs_unique_pages": by_unique / ms / 1e6,
+                "bytes_all": by_all, "bytes_unique": by_unique, "splits": sp}
     if case in ("prefill_attn", "prefill_attn_prefix"):
         ql, ctx = (2048, 2048) if case == "prefill_attn" else (1024, 8192)
         pages = ctx // 16

@@ -36,6 +36,9 @@ def main(argv=None) -> None:
     ap.add_argument("--k-total", type=int, default=8192)
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--check-only", action="store_true")
+    ap.add_argument("--lm-head", type=int, default=0, metavar="VOCAB",
+                    help="instead: the vocab-parallel LM head (each rank owns VOCAB / N rows of the weight) with "
+                         "the all-gather of the logits fused into its GEMM, against GEMM + NCCL all-gather")
     ap.add_argument("--one-shot-rows", type=int, default=0,
                     help="largest row count for the one-shot path; larger rows take the two-shot "
                          "(reduce-scatter + all-gather) path (0: one-shot for every row count)")
@@ -53,6 +56,8 @@ def main(argv=None) -> None:
     H, KT = a.hidden, a.k_total
     Ks = KT // world
     rows = [int(r) for r in a.rows.split(",")]
+    if a.lm_head:
+        return _lm_head(a, rank, world, dev, nccl, gloo, rows)
     if a.one_shot_rows:
         comm = TPComm(rank, world, dev, H, max_rows=a.one_shot_rows, nccl_group=nccl, gloo_group=gloo,
                       max_rows_rs=max(rows), two_shot=True)
@@ -158,6 +163,88 @@ def main(argv=None) -> None:
         dist.destroy_process_group()
     if worst > 2e-2:
         raise SystemExit(f"tensor-parallel all-reduce mismatch: worst relative error {worst}")
+
+
+def _graph_time(fn, iters: int, world: int, gloo, nccl, dev) -> float:
+    """Device microseconds per call of ``fn`` replayed from a CUDA graph, max
+    over ranks."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(gr, stream=st):
+            for _ in range(iters):
+                fn()
+    torch.cuda.current_stream().wait_stream(st)
+    gr.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(group=gloo)
+    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+    s.record()
+    gr.replay()
+    e.record()
+    torch.cuda.synchronize()
+    del gr
+    t = torch.tensor([s.elapsed_time(e) * 1000 / iters], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=nccl)
+    return float(t.item())
+
+
+def _lm_head(a, rank, world, dev, nccl, gloo, rows) -> None:
+    """Vocab-parallel LM head: logits = x @ W.T with W split by rows over the
+    ranks; every rank needs every column of the logits."""
+    H, V = a.hidden, a.lm_head
+    n = V // world
+    comm = TPComm(rank, world, dev, H, max_rows=8, nccl_group=nccl, gloo_group=gloo)
+    comm.ensure_gather(max(rows), V)
+    base = TPComm(rank, world, dev, H, max_rows=8, nccl_group=nccl, gloo_group=gloo, fused=False)
+    g = torch.Generator(device=dev).manual_seed(99)
+    w_full = (torch.randn(V, H, device=dev, generator=g) / H ** 0.5).to(torch.bfloat16)
+    w_loc = w_full[rank * n:(rank + 1) * n].contiguous()
+    worst = 0.0
+    for M in rows:
+        x = (torch.randn(M, H, device=dev, generator=g)).to(torch.bfloat16)
+        ref = x.float() @ w_full.float().t()
+        got = comm.gemm_allgather_cols(x, w_loc).clone()
+        torch.cuda.synchronize()
+        err = float((got.float() - ref).norm() / ref.norm())
+        errb = float((base.all_gather_cols(K.linear(x, w_loc)).float() - ref).norm() / ref.norm())
+        worst = max(worst, err, errb)
+        res = {"case": "lm_head", "rows": M, "hidden": H, "vocab": V, "world": world, "rel_err_fused": err,
+               "rel_err_nccl": errb, "status": K.scratch(dev).read_status(),
+               "fused": comm.uses_fused_gather(M, n, w_loc)}
+        if not a.check_only:
+            nrep = max(1, -(-(256 << 20) // (n * H * 2)))
+            wl = [w_loc] + [w_loc.clone() for _ in range(nrep - 1)]
+            it = [0]
+
+            def fused():
+                it[0] += 1
+                comm.gemm_allgather_cols(x, wl[it[0] % nrep])
+
+            def nccl_path():
+                it[0] += 1
+                base.all_gather_cols(K.linear(x, wl[it[0] % nrep]))
+
+            res["us_fused"] = round(_graph_time(fused, a.iters, world, gloo, nccl, dev), 2)
+            res["us_nccl"] = round(_graph_time(nccl_path, a.iters, world, gloo, nccl, dev), 2)
+            w_bytes = n * H * 2
+            push = (world - 1) * M * n * 2
+            res["roofline_us"] = round(max(2.0 * M * n * H / 1672.1e12, w_bytes / 6534.5e9, push / 770e9) * 1e6, 2)
+            res["frac_fused"] = round(res["roofline_us"] / res["us_fused"], 3)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    comm.close()
+    if world > 1:
+        dist.barrier(group=gloo)
+        dist.destroy_process_group()
+    if worst > 2e-2:
+        raise SystemExit(f"LM-head gather mismatch: worst relative error {worst}")
 
 
 if __name__ == "__main__":

@@ -197,6 +197,24 @@ __global__ void tp_wait_kernel(const unsigned int* flag, unsigned int target, in
   }
 }
 
+// Bounded wait until *flag >= *consumed + inc, then *consumed advances by
+// inc. The target lives in device memory, so a CUDA graph that replays this
+// launch waits for each replay's own arrivals (a host-side target would be
+// frozen into the graph).
+__global__ void tp_wait_next_kernel(const unsigned int* flag, unsigned int* consumed, unsigned int inc, int* status,
+                                    unsigned long long limit_ns) {
+  if (threadIdx.x != 0) return;
+  const unsigned int target = *reinterpret_cast<volatile unsigned int*>(consumed) + inc;
+  const unsigned long long t0 = globaltimer();
+  while (ld_acquire_sys(flag) < target) {
+    if (globaltimer() - t0 > limit_ns) {
+      atomicCAS(status, 0, kStatusTimeoutArrive);
+      break;
+    }
+  }
+  *reinterpret_cast<volatile unsigned int*>(consumed) = target;
+}
+
 }  // namespace tp
 }  // namespace ib200
 
@@ -324,6 +342,15 @@ extern "C" int ib_ar_add_rmsnorm_rs(const void* recv, long long src_stride, int 
 
 extern "C" int ib_tp_wait(const unsigned int* flag, unsigned int target, int* status, cudaStream_t stream) {
   tp_wait_kernel<<<1, 32, 0, stream>>>(flag, target, status, ib200::tp::kWaitNs);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+// Graph-safe form (see tp_wait_next_kernel): waits for `inc` more arrivals
+// than the previous call on the same `consumed` counter had.
+extern "C" int ib_tp_wait_next(const unsigned int* flag, unsigned int* consumed, unsigned int inc, int* status,
+                               cudaStream_t stream) {
+  ib200::tp::tp_wait_next_kernel<<<1, 32, 0, stream>>>(flag, consumed, inc, status, ib200::tp::kWaitNs);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }

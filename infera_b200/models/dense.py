@@ -22,7 +22,10 @@ QKV and gate/up are column-parallel (each rank owns 1/world of the heads
 and of the MLP width), the attention output and MLP down projections are
 row-parallel and each is followed by an all-reduce fused with the residual
 add and the next RMSNorm (NVLink one-shot push for small batches, NCCL
-otherwise); the LM head is vocab-parallel and its logits are all-gathered.
+otherwise); the LM head is vocab-parallel and its logits are all-gathered
+(fused into the LM-head GEMM's epilogue, which stores each rank's column
+block into every rank's logits over NVLink, up to the batch the symmetric
+buffer holds; NCCL otherwise).
 ``model.cfg`` is this rank's local shape; ``model.full_cfg`` the model's.
 Weights are generated full-size from the seed and sliced, so any TP size
 computes the same model.
@@ -232,6 +235,10 @@ class DenseModel:
         logits = bufs["logits"][:S] if "logits" in bufs else None
         if self.tp is None or self.tp.world == 1:
             return K.linear(xs, self.w.lm_head, out=logits)
+        fused = getattr(self.tp, "uses_fused_gather", None)
+        if fused is not None and fused(S, self.w.lm_head.shape[0], self.w.lm_head):
+            # vocab-parallel LM head with the all-gather fused into its epilogue
+            return self.tp.gemm_allgather_cols(xs, self.w.lm_head)
         local = K.linear(xs, self.w.lm_head, out=bufs["logits_local"][:S] if "logits_local" in bufs else None)
         return self.tp.all_gather_cols(local, out=logits)
 
@@ -239,6 +246,8 @@ class DenseModel:
         cfg = self.cfg
         bf = torch.bfloat16
         dev = self.device
+        if self.tp is not None and self.tp.world > 1 and hasattr(self.tp, "ensure_gather"):
+            self.tp.ensure_gather(max_seqs, self.full_cfg.vocab)
         return {
             "h": torch.empty(max_tokens, cfg.hidden, dtype=bf, device=dev),
             "x": torch.empty(max_tokens, cfg.hidden, dtype=bf, device=dev),

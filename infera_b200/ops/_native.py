@@ -91,6 +91,7 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
                                  c_vp, c_vp, c_vp, c_vp],
         "ib_tp_wait": [c_vp, ctypes.c_uint, c_vp, c_vp],
         "ib_tp_wait_for": [c_vp, ctypes.c_uint, c_vp, ctypes.c_ulonglong, c_vp],
+        "ib_tp_wait_next": [c_vp, c_vp, ctypes.c_uint, c_vp, c_vp],
         "ib_mla_decode": [c_vp, c_int, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_float, c_vp, c_vp, c_vp,
                           c_vp, c_vp],
         "ib_mla_set_trace": [c_vp],

@@ -71,10 +71,54 @@ class TPComm:
         self.fused = fused and self.device.type == "cuda" and os.environ.get("INFERA_TP_FUSED", "1") != "0"
         self.base = None
         self.peers: list[int] = []
+        # vocab-parallel LM head: GEMM whose epilogue stores each rank's column
+        # block into every rank's full logits buffer (ensure_gather)
+        self.g_base = None
+        self.g_peers: list[int] = []
+        self.g_opened: list[int] = []
+        self.g_rows = self.g_cols = 0
         if self.fused:
             self._setup_symmetric()
 
     # ------------------------------------------------------------------ setup
+    def _exchange(self, base: int) -> tuple[list[int], list[int]]:
+        """CUDA-IPC handles of ``base`` all round: (every rank's mapping of
+        its region, the mappings this rank opened)."""
+        lib = _native.kernels()
+        handle = (ctypes.c_char * 64)()
+        _native.check(lib.ib_ipc_handle(ctypes.c_void_p(base), handle), "ib_ipc_handle")
+        allh = [bytes(handle)]
+        if self.world > 1:
+            allh = [None] * self.world
+            dist.all_gather_object(allh, bytes(handle), group=self.gloo)
+        peers, opened = [], []
+        for r, h in enumerate(allh):
+            if r == self.rank:
+                peers.append(base)
+                continue
+            p = ctypes.c_void_p()
+            buf = (ctypes.c_char * 64).from_buffer_copy(h)
+            _native.check(lib.ib_ipc_open(buf, ctypes.byref(p)), f"ib_ipc_open(rank {r})")
+            peers.append(p.value)
+            opened.append(p.value)
+        return peers, opened
+
+    def ensure_gather(self, rows: int, cols: int) -> None:
+        """Allocate (once, on every rank at the same point: it exchanges IPC
+        handles) the symmetric [rows, cols] bf16 buffer of the fused GEMM ->
+        all-gather, plus its arrival counter."""
+        if not self.fused or self.world == 1 or self.g_base is not None:
+            return
+        lib = _native.kernels()
+        ptr = ctypes.c_void_p()
+        _native.check(lib.ib_sym_alloc(rows * cols * 2 + FLAG_BYTES, ctypes.byref(ptr)), "ib_sym_alloc")
+        self.g_base = ptr.value
+        self.g_rows, self.g_cols = rows, cols
+        self.g_peers, self.g_opened = self._exchange(self.g_base)
+        self.g_ctr = torch.zeros(4, dtype=torch.int32, device=self.device)   # done_ctr, consumed
+        if self.world > 1:
+            dist.barrier(group=self.gloo)
+
     def _setup_symmetric(self) -> None:
         lib = _native.kernels()
         self.slot_elems = self.cap * self.hidden
@@ -114,10 +158,13 @@ class TPComm:
         torch.cuda.synchronize(self.device)
         if self.world > 1:
             dist.barrier(group=self.gloo)
-        for p in self._opened:
+        for p in self._opened + self.g_opened:
             lib.ib_ipc_close(ctypes.c_void_p(p))
         lib.ib_sym_free(ctypes.c_void_p(self.base))
         self.base = None
+        if self.g_base is not None:
+            lib.ib_sym_free(ctypes.c_void_p(self.g_base))
+            self.g_base = None
 
     # ------------------------------------------------------------------ ops
     def _slot(self, rank_base: int, parity: int, src: int) -> int:
@@ -243,6 +290,54 @@ class TPComm:
         b.ptr = self._xbuf(self.base, parity)
         t = torch.as_tensor(_View(b, (rows, self.hidden), "<i2"), device=self.device).view(torch.bfloat16)
         return t
+
+    def uses_fused_gather(self, rows: int, cols_local: int, w) -> bool:
+        return (self.g_base is not None and rows <= self.g_rows and cols_local * self.world == self.g_cols
+                and isinstance(w, torch.Tensor))
+
+    def gemm_allgather_cols(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """[M, K] @ w_local[n, K].T on every rank -> [M, world * n] on every
+        rank (rank r's columns at r * n): one tcgen05 GEMM whose epilogue
+        stores each output tile straight into every rank's symmetric buffer
+        at this rank's column block over NVLink, then a bounded wait for the
+        other ranks' blocks (target kept on the device: graph-safe). Falls
+        back to GEMM + NCCL all-gather when the buffer does not fit."""
+        M, Kd = x.shape
+        n = w.shape[0]
+        if not self.uses_fused_gather(M, n, w):
+            return self.all_gather_cols(K.linear(x, w), out=out)
+        lib = _native.kernels()
+        sc = K.scratch(x.device)
+        flag_off = self.g_rows * self.g_cols * 2
+        peer_out = (ctypes.c_void_p * MAX_PEERS)(*[self.g_peers[d] + self.rank * n * 2 for d in range(self.world)])
+        peer_flag = (ctypes.c_void_p * MAX_PEERS)(*[self.g_peers[d] + flag_off for d in range(self.world)])
+        splits = K._gemm_splits(M, n, Kd, 0)
+        ws = sc.ensure_gemm(M * n if splits > 1 else 1)
+        stream = K._stream()
+        ctr = self.g_ctr.data_ptr()
+        rc = lib.ib_gemm_bf16_push(x.data_ptr(), w.data_ptr(), M, n, Kd, x.stride(0), w.stride(0), self.g_cols,
+                                   self.world, peer_out, peer_flag, ctypes.c_void_p(ctr), ws.data_ptr(),
+                                   sc.status.data_ptr(), stream)
+        _native.check(rc, "ib_gemm_bf16_push")
+        rc = lib.ib_tp_wait_next(ctypes.c_void_p(self.g_base + flag_off), ctypes.c_void_p(ctr + 4), self.world,
+                                 sc.status.data_ptr(), stream)
+        _native.check(rc, "ib_tp_wait_next")
+        K._count(3 if splits > 1 else 2)
+        full = self._raw_view(self.g_base, (self.g_rows, self.g_cols))[:M]
+        if out is not None:
+            out.copy_(full)
+            return out
+        return full
+
+    def _raw_view(self, ptr: int, shape) -> torch.Tensor:
+        from infera_b200.parallel.symmem import _View
+
+        class _B:
+            pass
+
+        b = _B()
+        b.ptr = ptr
+        return torch.as_tensor(_View(b, shape, "<i2"), device=self.device).view(torch.bfloat16)
 
     def all_gather_cols(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """[M, n] per rank -> [M, world * n] (rank r's columns at r*n), NCCL."""

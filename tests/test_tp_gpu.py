@@ -65,3 +65,17 @@ def test_tp_engine_matches_single_gpu():
     assert res["status"] == 0
     # every divergence from the single-GPU model is at a rounding tie
     assert res["greedy_agreement"] >= 0.9 or res["max_rel_gap_at_divergence"] < 0.01, res
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_lm_head_fused_gather_two_ranks():
+    """The vocab-parallel LM head whose epilogue stores every rank's column
+    block into every rank's logits, against the fp32 product of the whole
+    weight and against GEMM + NCCL all-gather."""
+    env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29614", "-m",
+           "infera_b200.bench.tp_comm_bench", "--lm-head", "128256", "--hidden", "4096", "--rows", "1,37,128",
+           "--check-only"]
+    r = subprocess.run(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, timeout=300)
+    assert r.returncode == 0, r.stdout.decode()[-3000:]
