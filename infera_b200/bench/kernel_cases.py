@@ -123,12 +123,21 @@ def run_case(case: str, iters: int) -> dict:
         bt = bt.to(dev)
         sl = torch.tensor(lens, dtype=torch.int32, device=dev)
         q = torch.randn(B, hq * D, device=dev, generator=g).to(bf)
-        sp = K.decode_splits(B, hkv, max(lens))
-        ms = _time(lambda: K.attn_decode(q, kc, vc, bt, sl, hq, hkv, 1 / math.sqrt(D), splits=sp), iters)
+        import os
+
+        tps = int(os.environ.get("INFERA_DECODE_TPS", "0"))       # tiles per split (0: even split)
+        l2 = int(os.environ.get("INFERA_DECODE_L2", "0"))
+        sp = K.decode_splits(B, hkv, max(lens)) if tps == 0 else -(-max(lens) // (tps * 128))
+        ms = _time(lambda: K.attn_decode(q, kc, vc, bt, sl, hq, hkv, 1 / math.sqrt(D), splits=sp,
+                                         tiles_per_split=tps, l2_policy=l2), iters)
+        ref = K.attn_decode(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), sl.cpu(), hq, hkv, 1 / math.sqrt(D)).float()
+        got = K.attn_decode(q, kc, vc, bt, sl, hq, hkv, 1 / math.sqrt(D), splits=sp, tiles_per_split=tps,
+                            l2_policy=l2).float().cpu()
         by_all = sum(lens) * hkv * D * 2 * 2
         by_unique = n_pages * 16 * hkv * D * 2 * 2
         return {"case": case, "ms": ms, "gbs_all_keys": by_all / ms / 1e6, "gbs_unique_pages": by_unique / ms / 1e6,
-                "bytes_all": by_all, "bytes_unique": by_unique, "splits": sp}
+                "bytes_all": by_all, "bytes_unique": by_unique, "splits": sp, "tiles_per_split": tps,
+                "l2_policy": l2, "rel_err": float((got - ref).norm() / ref.norm())}
     if case in ("prefill_attn", "prefill_attn_prefix"):
         ql, ctx = (2048, 2048) if case == "prefill_attn" else (1024, 8192)
         pages = ctx // 16

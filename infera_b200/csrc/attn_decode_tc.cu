@@ -56,6 +56,13 @@ struct Params {
   __nv_bfloat16* out;
   int ldo;
   int* status;
+  // > 0: every split covers this many 128-key tiles starting at split *
+  // tiles_per_split (the same absolute key range in every sequence, so the
+  // CTAs that read a prefix shared by several sequences run together and
+  // its pages are served from L2); 0: each sequence's tiles are divided
+  // evenly over the splits
+  int tiles_per_split;
+  int l2_policy;   // K/V loads: 0 evict_first, 1 evict_normal, 2 evict_last
 };
 
 __device__ __forceinline__ uint32_t s_col(int j) { return (j & 1) ? 16u : 0u; }
@@ -75,7 +82,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int G = p.G;
   const int len = p.seq_lens[b];
   const int n_tiles = (len + BKV - 1) / BKV;
-  const int tps = (n_tiles + p.splits - 1) / p.splits;
+  const int tps = p.tiles_per_split > 0 ? p.tiles_per_split : (n_tiles + p.splits - 1) / p.splits;
   const int t0 = split * tps;
   const int t1 = min(n_tiles, t0 + tps);
   if (t0 >= t1) {  // nothing in this split: mark it empty for the combine
@@ -144,7 +151,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
+      const uint64_t pol = p.l2_policy == 1 ? policy_evict_normal()
+                                            : (p.l2_policy == 2 ? policy_evict_last() : policy_evict_first());
       const int bt_row = p.bt_rows != nullptr ? p.bt_rows[b] : b;
       const int* bt = p.block_table + static_cast<size_t>(bt_row) * p.max_pages;
       const int n_pages = (len + PAGE - 1) / PAGE;
@@ -399,10 +407,14 @@ using namespace ib200;
 // block_table [rows, max_pages] with bt_rows[b] (null: row b);
 // o_part / lse_part: fp32 scratch of B*hq*splits*128 / B*hq*splits (only
 // touched when splits > 1).
-extern "C" int ib_attn_decode_tc(const void* q, int ldq, const void* k_cache, const void* v_cache, long long num_slots,
-                                 const int* block_table, const int* bt_rows, const int* seq_lens, int max_pages, int B,
-                                 int hq, int hkv, int splits, float scale, float* o_part, float* lse_part, void* out,
-                                 int ldo, int* status, cudaStream_t stream) {
+// tiles_per_split > 0: split s covers tiles [s * tiles_per_split, +tiles_per_split)
+// of every sequence (splits * tiles_per_split * 128 must cover the longest
+// sequence); l2_policy: 0 evict_first, 1 evict_normal, 2 evict_last for K/V.
+extern "C" int ib_attn_decode_tc_ex(const void* q, int ldq, const void* k_cache, const void* v_cache,
+                                    long long num_slots, const int* block_table, const int* bt_rows,
+                                    const int* seq_lens, int max_pages, int B, int hq, int hkv, int splits,
+                                    float scale, float* o_part, float* lse_part, void* out, int ldo, int* status,
+                                    int tiles_per_split, int l2_policy, cudaStream_t stream) {
   using namespace ib200::dtc;
   if (B <= 0) return 0;
   if (hkv <= 0 || hq % hkv != 0 || hq / hkv > MAXG || splits < 1 || (ldq % 2) != 0) return -1;
@@ -428,6 +440,8 @@ extern "C" int ib_attn_decode_tc(const void* q, int ldq, const void* k_cache, co
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = ldo;
   p.status = status;
+  p.tiles_per_split = tiles_per_split;
+  p.l2_policy = l2_policy;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -445,4 +459,12 @@ extern "C" int ib_attn_decode_tc(const void* q, int ldq, const void* k_cache, co
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   return 0;
+}
+
+extern "C" int ib_attn_decode_tc(const void* q, int ldq, const void* k_cache, const void* v_cache, long long num_slots,
+                                 const int* block_table, const int* bt_rows, const int* seq_lens, int max_pages, int B,
+                                 int hq, int hkv, int splits, float scale, float* o_part, float* lse_part, void* out,
+                                 int ldo, int* status, cudaStream_t stream) {
+  return ib_attn_decode_tc_ex(q, ldq, k_cache, v_cache, num_slots, block_table, bt_rows, seq_lens, max_pages, B, hq,
+                              hkv, splits, scale, o_part, lse_part, out, ldo, status, 0, 0, stream);
 }

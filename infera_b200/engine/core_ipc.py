@@ -448,6 +448,7 @@ def main(argv=None) -> None:
     p.add_argument("--kv-index-compat", default="", help="compat key (tokenizer digest) in those events")
     p.add_argument("--kv-tier", default=None)
     p.add_argument("--tp-size", type=int, default=1, help="tensor-parallel ranks (RANK / LOCAL_RANK / MASTER_* from env)")
+    p.add_argument("--first-device", type=int, default=0, help="tensor-parallel rank r runs on cuda:(first + r)")
     p.add_argument("--disagg-mode", choices=("mixed", "prefill", "decode"), default="mixed")
     p.add_argument("--kv-push-endpoint", default=None)
     p.add_argument("--dp-attention-size", type=int, default=1,
@@ -466,7 +467,7 @@ def main(argv=None) -> None:
     if a.tp_size > 1:
         from infera_b200.parallel.launch import init_tp
 
-        tp, rank, device = init_tp(a.tp_size, model=a.model)
+        tp, rank, device = init_tp(a.tp_size, model=a.model, first_device=a.first_device)
     pub = KvEventPublisher(a.kv_events_endpoint) if a.kv_events_endpoint and rank == 0 else None
     cfg = EngineConfig(model=a.model, page_size=a.page_size, max_num_seqs=a.max_num_seqs,
                        max_batched_tokens=a.max_batched_tokens, gpu_memory_utilization=a.gpu_memory_utilization,

@@ -78,6 +78,10 @@ def parse_args(argv=None):
     p.add_argument("--advertise-host", default=None)
     p.add_argument("--port", type=int, default=9000)
     p.add_argument("--device", default="cuda:0")
+    p.add_argument("--tp-size", type=int, default=1,
+                   help="tensor-parallel ranks of the engine core (launched with torch.distributed.run)")
+    p.add_argument("--first-device", type=int, default=0,
+                   help="with --tp-size: rank r runs on cuda:(first + r)")
     p.add_argument("--page-size", type=int, default=16)
     p.add_argument("--max-num-seqs", type=int, default=128)
     p.add_argument("--max-batched-tokens", type=int, default=2048)
@@ -113,7 +117,17 @@ def parse_args(argv=None):
 def _core_cmd(args, in_addr: str, out_addr: str) -> list[str]:
     import sys
 
-    cmd = [sys.executable, "-m", "infera_b200.engine.core_ipc", "--in", in_addr, "--out", out_addr,
+    launch = [sys.executable, "-m", "infera_b200.engine.core_ipc"]
+    tp = getattr(args, "tp_size", 1)
+    if tp > 1:
+        # one process per GPU: rank 0 serves the core's IPC sockets, the
+        # others follow its step commands
+        from infera_b200.common.net import free_tcp_port
+
+        launch = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={tp}",
+                  "--master-addr", "127.0.0.1", "--master-port", str(free_tcp_port()), "-m",
+                  "infera_b200.engine.core_ipc", "--tp-size", str(tp), "--first-device", str(args.first_device)]
+    cmd = launch + ["--in", in_addr, "--out", out_addr,
            "--model", args.model, "--device", args.device, "--page-size", str(args.page_size),
            "--max-num-seqs", str(args.max_num_seqs), "--max-batched-tokens", str(args.max_batched_tokens),
            "--mixed-prefill-tokens", str(args.mixed_prefill_tokens),

@@ -50,6 +50,8 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_kv_page_copy": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_ll, c_int, c_int, c_int, c_int, c_vp],
         "ib_attn_decode_tc": [c_vp, c_int, c_vp, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
                               c_float, c_vp, c_vp, c_vp, c_int, c_vp, c_vp],
+        "ib_attn_decode_tc_ex": [c_vp, c_int, c_vp, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
+                                 c_float, c_vp, c_vp, c_vp, c_int, c_vp, c_int, c_int, c_vp],
         "ib_gemm_bf16_push": [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp,
                               c_vp, c_vp],
         "ib_ar_add_rmsnorm": [c_vp, c_ll, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_float, c_vp,

@@ -386,12 +386,16 @@ def decode_splits(batch: int, hkv: int, max_len: int, num_sms: int = 148) -> int
 def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
                 seq_lens: torch.Tensor, hq: int, hkv: int, scale: float, splits: int = 1,
                 out: torch.Tensor | None = None, bt_rows: torch.Tensor | None = None,
-                impl: str = "tc") -> torch.Tensor:
+                impl: str = "tc", tiles_per_split: int = 0, l2_policy: int = 0) -> torch.Tensor:
     """Single-token attention per sequence. q: [B, >=hq*D] (row stride
     free), seq_lens: int32 [B] (keys including the current token).
 
     ``impl="tc"`` is the tcgen05/TMA kernel the engine uses; ``"simt"`` is
-    the FP32-pipe kernel behind the allocation-free C entry point."""
+    the FP32-pipe kernel behind the allocation-free C entry point.
+    ``tiles_per_split`` > 0: split s covers 128-key tiles [s*T, (s+1)*T) of
+    every sequence (``splits * T * 128`` must cover the longest), so CTAs
+    reading a shared prefix run together; ``l2_policy`` 0/1/2: K/V loads
+    evict_first / evict_normal / evict_last."""
     B = seq_lens.shape[0]
     D = k_cache.shape[1] // hkv
     if not q.is_cuda:
@@ -411,11 +415,11 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, b
         o, lse = sc.ensure_decode(B * hq * splits * D, B * hq * splits)
         o_ptr, lse_ptr = o.data_ptr(), lse.data_ptr()
     if impl == "tc":
-        rc = _native.kernels().ib_attn_decode_tc(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
-                                                 k_cache.shape[0], block_table.data_ptr(), _ptr(bt_rows),
-                                                 seq_lens.data_ptr(), block_table.stride(0), B, hq, hkv, splits,
-                                                 scale, o_ptr, lse_ptr, out.data_ptr(), out.stride(0),
-                                                 sc.status.data_ptr(), _stream())
+        rc = _native.kernels().ib_attn_decode_tc_ex(q.data_ptr(), q.stride(0), k_cache.data_ptr(),
+                                                    v_cache.data_ptr(), k_cache.shape[0], block_table.data_ptr(),
+                                                    _ptr(bt_rows), seq_lens.data_ptr(), block_table.stride(0), B, hq,
+                                                    hkv, splits, scale, o_ptr, lse_ptr, out.data_ptr(), out.stride(0),
+                                                    sc.status.data_ptr(), tiles_per_split, l2_policy, _stream())
         _native.check(rc, "ib_attn_decode_tc")
     else:
         rc = _native.kernels().ib_attn_decode(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),

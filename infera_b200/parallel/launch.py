@@ -19,16 +19,19 @@ from infera_b200.parallel.comm import TPComm
 
 
 def init_tp(tp_size: int, hidden: int | None = None, model: str | None = None, max_rows: int = 256,
-            timeout_s: float = 600.0, max_rows_rs: int = 2048 + 256):
+            timeout_s: float = 600.0, max_rows_rs: int = 2048 + 256, first_device: int = 0):
     """Returns (TPComm, rank, device). ``hidden`` defaults from ``model``;
     steps of up to ``max_rows`` tokens use the one-shot fused all-reduce, up
-    to ``max_rows_rs`` the two-shot one (at 4 or more ranks)."""
+    to ``max_rows_rs`` the two-shot one (at 4 or more ranks). Rank r runs on
+    ``cuda:(first_device + LOCAL_RANK)``: two instances on one box (a PD
+    pair on GPUs 0-3 and 4-7) both see every GPU, so that CUDA-IPC mappings
+    of the other instance's caches work."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(tp_size)))
     local = int(os.environ.get("LOCAL_RANK", str(rank)))
     if world != tp_size:
         raise ValueError(f"WORLD_SIZE={world} but tensor-parallel size {tp_size}")
-    dev = torch.device("cuda", local)
+    dev = torch.device("cuda", first_device + local)
     torch.cuda.set_device(dev)
     if not dist.is_initialized():
         dist.init_process_group("nccl", timeout=timedelta(seconds=timeout_s), device_id=dev)

@@ -62,3 +62,19 @@ def test_loadgen_multiturn(worker):
     for r in recs:
         assert r["out_len"] == len(r["token_times"]) and r["out_len"] > 0
         assert r["token_times"][0] >= r["arrival"]
+
+
+def test_worker_tp_core_command_launches_ranks():
+    """--tp-size N: the worker launches its engine core ranks with
+    torch.distributed.run (rank r on cuda:(first + r))."""
+    from infera_b200.engine.worker import _core_cmd, parse_args
+
+    a = parse_args(["--model", "llama-3.1-70b", "--tp-size", "4", "--first-device", "4", "--disagg-mode", "decode",
+                    "--kv-push-endpoint", "ipc:///tmp/x"])
+    cmd = _core_cmd(a, "ipc:///tmp/in", "ipc:///tmp/out")
+    assert cmd[1:3] == ["-m", "torch.distributed.run"] and "--nproc-per-node=4" in cmd
+    i = cmd.index("infera_b200.engine.core_ipc")
+    assert cmd[i + 1:i + 5] == ["--tp-size", "4", "--first-device", "4"]
+    assert "--kv-push-endpoint" in cmd and cmd[cmd.index("--disagg-mode") + 1] == "decode"
+    single = _core_cmd(parse_args([]), "a", "b")
+    assert single[1:3] == ["-m", "infera_b200.engine.core_ipc"]
