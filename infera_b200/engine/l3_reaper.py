@@ -112,3 +112,80 @@ class L3FileReaper:
                 self.stats["enospc_retries"] += 1
                 self.reap(2 * len(data))
         return path
+
+
+class _Ext:
+    def __init__(self, retention: str):
+        self.retention = retention
+
+
+class FileChunkStore:
+    """File-per-chunk NVMe tier (``<key hex>.<retention>.kvcache`` in one
+    directory) with the reaper keeping it under its byte budget and above the
+    free-space floor. It offers the L3 surface the host store spills to and
+    promotes from (``put`` / ``get`` / ``in`` / ``index``), so the engine's
+    tier can use it in place of the tablespace: ``kv_tier="host:<GiB>:files:
+    <dir>"``. A file removed by the reaper simply misses on the next lookup.
+    Role of the reference's file-per-chunk L3 of its vLLM connector with
+    ``infera/engine/vllm/_l3_reaper.py``."""
+
+    def __init__(self, directory: str, budget_bytes: int | None = None, free_floor_bytes: int = 0):
+        os.makedirs(directory, exist_ok=True)
+        self.dir = directory
+        self.reaper = L3FileReaper(directory, budget_bytes, free_floor_bytes)
+        self.reaper.startup_budget_clamp()
+        self.index: dict[bytes, _Ext] = {}
+        for f in self.reaper.scan():      # chunks left by an earlier run stay usable
+            name = os.path.basename(f.path)
+            try:
+                key = bytes.fromhex(name.split(".", 1)[0])
+            except ValueError:
+                continue
+            self.index[key] = _Ext(f.retention)
+
+    def _name(self, key: bytes, retention: str) -> str:
+        return f"{key.hex()}.{retention if retention in PRIORITY else 'short'}{SUFFIX}"
+
+    def put(self, key: bytes, value, retention: str = "short") -> bool:
+        try:
+            self.reaper.write_with_reap(self._name(key, retention), bytes(value))
+        except OSError:
+            return False
+        self.index[key] = _Ext(retention)
+        return True
+
+    def get(self, key: bytes) -> bytes | None:
+        ext = self.index.get(key)
+        if ext is None:
+            return None
+        path = os.path.join(self.dir, self._name(key, ext.retention))
+        try:
+            with open(path, "rb") as f:
+                data = f.read()
+            os.utime(path)            # recency for the reaper's LRU
+            return data
+        except FileNotFoundError:     # reaped
+            self.index.pop(key, None)
+            return None
+
+    def __contains__(self, key: bytes) -> bool:
+        ext = self.index.get(key)
+        if ext is None:
+            return False
+        if not os.path.exists(os.path.join(self.dir, self._name(key, ext.retention))):
+            self.index.pop(key, None)
+            return False
+        return True
+
+    def delete(self, key: bytes) -> bool:
+        ext = self.index.pop(key, None)
+        if ext is None:
+            return False
+        try:
+            os.unlink(os.path.join(self.dir, self._name(key, ext.retention)))
+        except FileNotFoundError:
+            pass
+        return True
+
+    def __len__(self) -> int:
+        return len(self.index)

@@ -36,7 +36,13 @@ def _tier_store(spec: str):
         from infera_b200.kvd.tablespace import Tablespace
 
         gib, _, nvme = rest.partition(":")
-        l3 = Tablespace(nvme, fsync=False) if nvme else None
+        if nvme.startswith("files:"):
+            # one file per chunk, kept under INFERA_KVD_L3_BUDGET_BYTES by the reaper
+            from infera_b200.engine.l3_reaper import FileChunkStore
+
+            l3 = FileChunkStore(nvme[len("files:"):])
+        else:
+            l3 = Tablespace(nvme, fsync=False) if nvme else None
         return HostStore(int(float(gib or 4) * (1 << 30)), l3=l3)
     raise ValueError(f"unknown kv_tier spec {spec!r}")
 
@@ -60,7 +66,9 @@ class EngineConfig:
     max_model_len: int | None = None
     model_overrides: dict = field(default_factory=dict)
     # KV tiering: None (off), "host:<GiB>[:<nvme dir>]" (in-process host store,
-    # optional NVMe tablespace) or "kvd:<socket path>" (shared daemon)
+    # optional NVMe tablespace), "host:<GiB>:files:<dir>" (NVMe tier of one
+    # file per chunk under the reaper's budget) or "kvd:<socket path>"
+    # (shared daemon)
     kv_tier: str | None = None
     # promote tier hits on a loader thread while the engine keeps stepping
     # (tensor-parallel ranks always promote inline)

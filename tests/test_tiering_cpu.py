@@ -87,3 +87,23 @@ def test_tier_promote_abort_releases_pages_after_landing():
             break
         eng.step()
     assert not eng.scheduler.loading and eng.bm.num_free() == free0
+
+
+def test_engine_tier_file_per_chunk_l3_under_reaper_budget(tmp_path, monkeypatch):
+    """kv_tier host:<tiny>:files:<dir>: evicted pages spill from the host
+    store to one file per chunk; the reaper keeps the directory under its
+    budget; a promote of a reaped chunk misses instead of failing."""
+    d = tmp_path / "l3"
+    page_bytes = 2 * 2 * 16 * 2 * 64 * 2 + 8192          # tiny-dense page payload + header, rounded up
+    monkeypatch.setenv("INFERA_KVD_L3_BUDGET_BYTES", str(6 * page_bytes))
+    eng = LLMEngine(EngineConfig(model="tiny-dense", use_cuda_graphs=False, num_pages=12, max_batched_tokens=256,
+                                 kv_tier=f"host:0.0001:files:{d}"), device="cpu")
+    g = torch.Generator().manual_seed(6)
+    sp = SamplingParams(max_tokens=2, ignore_eos=True)
+    for _ in range(6):
+        eng.generate([torch.randint(0, 1000, (64,), generator=g).tolist()], sp)
+    eng.tier.flush()
+    files = [p for p in d.iterdir() if p.name.endswith(".kvcache")]
+    assert files and sum(p.stat().st_size for p in files) <= 6 * page_bytes
+    l3 = eng.tier.store.l3
+    assert l3.reaper.stats["reaped_files"] > 0 and len(files) <= len(l3.index) + 1
