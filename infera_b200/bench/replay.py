@@ -44,6 +44,7 @@ class EngineReplay:
         self.ev0 = None
         self.step_events: list = []         # (event, host_time)
         self.step_shapes: list = []         # (prompt tokens, decoding sequences) per step
+        self.step_host: list = []           # (host issue s, host wait-for-device s) per step
         self.token_steps: dict[str, list[int]] = {}
         self.collected: dict[str, list[int]] = {}
         self.next_arrival = None
@@ -122,6 +123,8 @@ class EngineReplay:
                 outs = self.eng.step()
                 step_idx = len(self.step_events)
                 self.step_shapes.append(getattr(self.eng, "last_step_shape", (0, 0)))
+                runner = getattr(self.eng, "runner", None)
+                self.step_host.append(getattr(runner, "last_timing", (0.0, 0.0)))
                 if self.device_timing:
                     ev = torch.cuda.Event(enable_timing=True)
                     ev.record()
@@ -161,6 +164,8 @@ class EngineReplay:
         times = self._times
         kinds: dict[str, list[float]] = {}
         toks: dict[str, list[int]] = {}
+        issue: dict[str, list[float]] = {}
+        wait: dict[str, list[float]] = {}
         for i in range(1, len(times)):
             if not (window[0] <= times[i] <= window[1]):
                 continue
@@ -173,8 +178,16 @@ class EngineReplay:
                 k = "prefill"
             kinds.setdefault(k, []).append(1000 * (times[i] - times[i - 1]))
             toks.setdefault(k, []).append(pt)
+            hi, hw = self.step_host[i] if i < len(self.step_host) else (0.0, 0.0)
+            issue.setdefault(k, []).append(1000 * hi)
+            wait.setdefault(k, []).append(1000 * hw)
+        # host_issue: host time from the start of the forward to its last
+        # launch; host_wait: time the host then waited for the device (near
+        # zero means the step was bound by the host's launch rate)
         return {k: {"n": len(v), "p50_ms": round(percentile(v, 50), 3), "p99_ms": round(percentile(v, 99), 3),
-                    "mean_prompt_tokens": round(sum(toks[k]) / len(v), 1)} for k, v in sorted(kinds.items())}
+                    "mean_prompt_tokens": round(sum(toks[k]) / len(v), 1),
+                    "host_issue_p50_ms": round(percentile(issue[k], 50), 3),
+                    "host_wait_p50_ms": round(percentile(wait[k], 50), 3)} for k, v in sorted(kinds.items())}
 
     def resolve(self) -> list[ReqRecord]:
         """Convert step indices into timestamps (device when available)."""

@@ -93,22 +93,58 @@ def _frame_headers(kind: str, status: int) -> dict:
     return {"rs-type": kind, "rs-status": str(status)}
 
 
+REQUEST_STREAM = "INFERA_REQUESTS"
+HDR_INBOX = "infera-inbox"
+
+
+def request_durable(token: str) -> str:
+    """Durable JetStream consumer of one worker's request subject."""
+    return f"infera-req-{token}"
+
+
 class BusRequestClient:
-    """Router side; ``stream`` has the router transports' interface."""
+    """Router side; ``stream`` has the router transports' interface.
+
+    ``jetstream=True``: requests go through the ``INFERA_REQUESTS``
+    work-queue stream (one durable consumer per worker; the reply inbox rides
+    in a header because a stream-delivered message's reply subject is its
+    ack subject), and admission is the worker consumer's pending count
+    against ``max_pending`` instead of an admit request."""
 
     def __init__(self, bus, idle_timeout: float = 900.0, max_duration: float | None = None,
-                 admit_timeout: float = 2.0):
+                 admit_timeout: float = 2.0, jetstream: bool = False, max_pending: int = 64):
         self.bus = bus
         self.idle_timeout = idle_timeout
         self.max_duration = max_duration
         self.admit_timeout = admit_timeout
+        self.jetstream = jetstream
+        self.max_pending = max_pending
+        self._js = None
         self.stats = {"requests": 0, "rejected": 0, "timeouts": 0, "cancels_sent": 0}
+
+    async def _jetstream(self):
+        if self._js is None:
+            from infera_b200.common.jetstream import JetStream
+
+            js = JetStream(self.bus)
+            await js.add_stream(REQUEST_STREAM, [REQ + ">"], retention="workqueue")
+            self._js = js
+        return self._js
 
     @staticmethod
     def token(worker) -> str:
         return str(worker.worker_id).replace(".", "_").replace(":", "_")
 
     async def admit(self, worker) -> bool:
+        if self.jetstream:
+            from infera_b200.common.jetstream import JetStreamError
+
+            js = await self._jetstream()
+            try:
+                info = await js.consumer_info(REQUEST_STREAM, request_durable(self.token(worker)))
+            except (JetStreamError, asyncio.TimeoutError):
+                return False      # the worker has not attached its consumer: not serving
+            return int(info.get("num_pending", 0)) < self.max_pending
         try:
             m = await self.bus.request(ADMIT + self.token(worker), b"", timeout=self.admit_timeout)
         except asyncio.TimeoutError:
@@ -138,7 +174,11 @@ class BusRequestClient:
         t0 = time.monotonic()
         try:
             payload = json.dumps({"path": path, "body": body, "headers": headers or {}}).encode()
-            await self.bus.publish(REQ + self.token(worker), payload, headers={"rid": rid}, reply=inbox)
+            if self.jetstream:
+                js = await self._jetstream()
+                await js.publish(REQ + self.token(worker), payload, headers={"rid": rid, HDR_INBOX: inbox})
+            else:
+                await self.bus.publish(REQ + self.token(worker), payload, headers={"rid": rid}, reply=inbox)
             while True:
                 wait = self.idle_timeout
                 if self.max_duration is not None:
@@ -166,8 +206,14 @@ class BusRequestServer:
     """Worker side: admission, bounded concurrency, cancel, drain, hand-back."""
 
     def __init__(self, bus, worker_token: str, handler: Handler, max_concurrency: int = 256,
-                 max_pending: int = 1024, migratable: Callable[[dict], bool] | None = None):
+                 max_pending: int = 1024, migratable: Callable[[dict], bool] | None = None,
+                 jetstream: bool = False, fetch_batch: int = 8):
         self.bus = bus
+        # jetstream: pull this worker's requests from its durable consumer on
+        # the INFERA_REQUESTS work queue (each is acked when taken)
+        self.jetstream = jetstream
+        self.fetch_batch = fetch_batch
+        self._pull: asyncio.Task | None = None
         self.token = worker_token
         self.handler = handler
         self.max_concurrency = max_concurrency
@@ -185,11 +231,43 @@ class BusRequestServer:
         return len(self._tasks)
 
     async def start(self) -> None:
-        self._unsubs.append(await self.bus.subscribe(REQ + self.token, self._on_request))
+        if self.jetstream:
+            from infera_b200.common.jetstream import JetStream
+
+            js = JetStream(self.bus)
+            await js.add_stream(REQUEST_STREAM, [REQ + ">"], retention="workqueue")
+            await js.add_consumer(REQUEST_STREAM, durable=request_durable(self.token), filter_subject=REQ + self.token)
+            self._pull = asyncio.get_running_loop().create_task(self._pull_loop(js))
+        else:
+            self._unsubs.append(await self.bus.subscribe(REQ + self.token, self._on_request))
         self._unsubs.append(await self.bus.subscribe(CANCEL + self.token, self._on_cancel))
         self._unsubs.append(await self.bus.subscribe(ADMIT + self.token, self._on_admit))
 
+    async def _pull_loop(self, js) -> None:
+        durable = request_durable(self.token)
+        while True:
+            if self.draining:
+                await asyncio.sleep(0.05)   # leave queued requests to the stream (and other workers' retries)
+                continue
+            try:
+                msgs = await js.fetch(REQUEST_STREAM, durable, batch=self.fetch_batch, expires_s=1.0)
+            except asyncio.CancelledError:
+                raise
+            except Exception:
+                await asyncio.sleep(0.2)
+                continue
+            for jm in msgs:
+                await js.ack(jm)
+                await self._on_request(Msg(jm.subject, jm.data, jm.headers, jm.headers.get(HDR_INBOX)))
+
     async def stop(self) -> None:
+        if self._pull is not None:
+            self._pull.cancel()
+            try:
+                await self._pull
+            except (asyncio.CancelledError, Exception):
+                pass
+            self._pull = None
         for u in self._unsubs:
             u()
         self._unsubs.clear()

@@ -10,10 +10,13 @@
 //               the 16 columns are query-head slots (G <= 8 real heads of
 //               the KV group, the rest zero)
 //   warps 2..5  thread <-> key row for the softmax (max over keys through a
-//               bounded mbarrier-based group barrier, one exp2 per head per key)
-//               and thread <-> dim
-//               row when folding each tile's O^T into fp32 registers with
-//               the online-softmax rescale; they also stage Q.
+//               bounded mbarrier-based group barrier, one exp2 per head per key),
+//               P into one of two shared-memory buffers; they also stage Q.
+// O^T accumulates in TMEM across the tiles. The softmax keeps a running max
+// per head and rescales O only when a tile's max exceeds it by more than
+// 2^8 (lazy rescale: the thread <-> dim row multiplies its O^T row in
+// TMEM), so a tile's softmax never waits for the previous tile's PV; the
+// double-buffered P is only reused after the PV two tiles back.
 // Split partials (output normalised by its own sum, LSE in log2 units) are
 // merged by a combine kernel when a sequence is split.
 //
@@ -38,8 +41,10 @@ constexpr int NQ = 16;              // UMMA N (query-head slots)
 constexpr int QBLK = NQ * 128;      // 16 rows x 128 B
 constexpr int MAXG = 8;
 constexpr int NUM_THREADS = 192;
-constexpr int SMEM_BYTES = 1024 + STAGES * 4 * BLK + 4 * QBLK + 1024;
-constexpr uint32_t TMEM_COLS = 64;  // S0 [0,16) S1 [16,32) O0 [32,48) O1 [48,64)
+constexpr int SMEM_BYTES = 1024 + STAGES * 4 * BLK + 6 * QBLK + 1024;
+constexpr uint32_t TMEM_COLS = 64;  // S0 [0,16) S1 [16,32) O [32,48)
+constexpr uint32_t O_COL = 32;
+constexpr float kRescaleLog2 = 8.0f;  // lazy rescale threshold (log2 units)
 
 struct Params {
   const __nv_bfloat16* q;
@@ -66,7 +71,6 @@ struct Params {
 };
 
 __device__ __forceinline__ uint32_t s_col(int j) { return (j & 1) ? 16u : 0u; }
-__device__ __forceinline__ uint32_t o_col(int j) { return (j & 1) ? 48u : 32u; }
 
 // byte offset of element (row, k) of a 16-row K-major block pair
 // [lo: k < 64 | hi: k >= 64] in the 128-byte-swizzled layout
@@ -101,15 +105,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sKV = smem;                        // stage s: K lo, K hi, V lo, V hi
   uint8_t* sQ = smem + STAGES * 4 * BLK;      // Q lo, Q hi
-  uint8_t* sP = sQ + 2 * QBLK;                // P lo, P hi (rows = head slots, cols = keys)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * QBLK);
+  uint8_t* sP = sQ + 2 * QBLK;                // [2 buffers] P lo, P hi (rows = head slots, cols = keys)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 4 * QBLK);
   uint64_t* k_full = bars;
   uint64_t* v_full = k_full + STAGES;
   uint64_t* kv_empty = v_full + STAGES;
   uint64_t* s_full = kv_empty + STAGES;       // [2]
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = p_full + 1;
-  uint64_t* q_ready = pv_done + 1;
+  uint64_t* p_full = s_full + 2;              // [2] one per P buffer
+  uint64_t* pv_done = p_full + 2;             // [2] PV of tile j commits to pv_done[j & 1]
+  uint64_t* q_ready = pv_done + 2;
   uint64_t* grp = q_ready + 1;                // bounded barrier of the 128 softmax threads
   uint64_t* drain = grp + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -128,8 +132,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
+    mbar_init(&p_full[0], 128);
+    mbar_init(&p_full[1], 128);
+    mbar_init(&pv_done[0], 1);
+    mbar_init(&pv_done[1], 1);
     mbar_init(q_ready, 128);
     mbar_init(grp, 128);
     mbar_init(drain, 1);
@@ -203,21 +209,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
         const int st = jj % STAGES;
-        if (!mbar_wait(p_full, static_cast<uint32_t>(jj & 1), abort_flag, p.status, kStatusTimeoutTmemEmpty))
+        if (!mbar_wait(&p_full[jj & 1], static_cast<uint32_t>((jj >> 1) & 1), abort_flag, p.status,
+                       kStatusTimeoutTmemEmpty))
           return false;
         if (!mbar_wait(&v_full[st], static_cast<uint32_t>((jj / STAGES) & 1), abort_flag, p.status,
                        kStatusTimeoutFull))
           return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sKV + st * 4 * BLK + 2 * BLK);
+        const uint32_t pb = p_addr + static_cast<uint32_t>((jj & 1) * 2 * QBLK);
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
           // A = V^T, MN-major: LBO = distance to the dims 64..127 block, SBO = 8 keys
           const uint64_t ad = make_sw128_desc(v_addr + s * 2048, BLK, 1024);
-          const uint64_t bd = make_sw128_desc(p_addr + (s < 4 ? s * 32 : QBLK + (s - 4) * 32), 16, 1024);
-          umma_bf16(tmem + o_col(jj), ad, bd, idesc_o, s > 0 ? 1u : 0u);
+          const uint64_t bd = make_sw128_desc(pb + (s < 4 ? s * 32 : QBLK + (s - 4) * 32), 16, 1024);
+          umma_bf16(tmem + O_COL, ad, bd, idesc_o, (jj > 0 || s > 0) ? 1u : 0u);
         }
-        umma_commit(pv_done);
+        umma_commit(&pv_done[jj & 1]);
         umma_commit(&kv_empty[st]);
         return true;
       };
@@ -260,8 +268,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ok = mbar_wait_warp(grp, gph & 1u, abort_flag, p.status, kStatusTimeoutTmemFull) && ok;
       ++gph;
     };
-    // stage Q (head slots >= G and the P block start at zero)
-    for (int i = t; i < 4 * QBLK / 16; i += 128) reinterpret_cast<uint4*>(sQ)[i] = make_uint4(0, 0, 0, 0);
+    // stage Q (head slots >= G and both P buffers start at zero)
+    for (int i = t; i < 6 * QBLK / 16; i += 128) reinterpret_cast<uint4*>(sQ)[i] = make_uint4(0, 0, 0, 0);
     group_sync();
     for (int idx = t; idx < G * 64; idx += 128) {
       const int h = idx >> 6, d = (idx & 63) * 2;
@@ -272,14 +280,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     fence_proxy_async_smem();
     mbar_arrive(q_ready);
 
-    float m_run[MAXG], l_part[MAXG], acc[MAXG], alpha_prev[MAXG];
+    float m_run[MAXG], l_part[MAXG], acc[MAXG];
 #pragma unroll
     for (int h = 0; h < MAXG; ++h) {
       m_run[h] = -INFINITY;
       l_part[h] = 0.f;
       acc[h] = 0.f;
-      alpha_prev[h] = 1.f;
     }
+    // wait until the PV of tile jj has completed (its commit is the
+    // ((jj >> 1) + 1)-th completion of pv_done[jj & 1]; no later PV on that
+    // barrier can have been issued yet when this is called)
+    auto wait_pv = [&](int jj) -> bool {
+      if (!mbar_wait_warp(&pv_done[jj & 1], static_cast<uint32_t>((jj >> 1) & 1), abort_flag, p.status,
+                          kStatusTimeoutTmemFull))
+        return false;
+      tc_fence_after();
+      return true;
+    };
     for (int j = 0; j < nt && ok; ++j) {
       if (!mbar_wait_warp(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status,
                           kStatusTimeoutTmemFull)) {
@@ -302,48 +319,64 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       group_sync();
       if (!ok) break;
-      float alpha[MAXG], pj[MAXG];
+      // new running maxima; every thread derives the same values from red,
+      // so the rescale decision below is uniform over the CTA
+      float alpha[MAXG];
+      bool any_rescale = false;
 #pragma unroll
       for (int h = 0; h < MAXG; ++h) {
         const float* rr = red + (j & 1) * 4 * MAXG;
         const float tmax = fmaxf(fmaxf(rr[h], rr[MAXG + h]), fmaxf(rr[2 * MAXG + h], rr[3 * MAXG + h]));
-        const float m_new = fmaxf(m_run[h], tmax);
-        alpha[h] = (m_run[h] == -INFINITY) ? 0.f : exp2f(m_run[h] - m_new);
-        pj[h] = (s[h] == -INFINITY) ? 0.f : exp2f(s[h] - m_new);
-        l_part[h] = l_part[h] * alpha[h] + pj[h];
-        m_run[h] = (m_new == -INFINITY) ? m_run[h] : m_new;
+        alpha[h] = 1.f;
+        if (m_run[h] == -INFINITY) {
+          m_run[h] = tmax;                       // first keys of this head: nothing accumulated yet
+        } else if (tmax > m_run[h] + kRescaleLog2) {
+          alpha[h] = exp2f(m_run[h] - tmax);
+          m_run[h] = tmax;
+          any_rescale = true;
+        }
       }
-      if (j > 0) {
-        if (!mbar_wait_warp(pv_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status,
-                            kStatusTimeoutTmemFull)) {
+      if (any_rescale) {
+        // O^T holds every earlier tile: once the last PV landed, scale each
+        // rescaled head's column (this thread owns dim row r)
+        if (!wait_pv(j - 1)) {
           ok = false;
           break;
         }
-        tc_fence_after();
         uint32_t ov[16];
-        tmem_ld16(lane_addr + o_col(j - 1), ov);
+        tmem_ld16(lane_addr + O_COL, ov);
         tmem_ld_wait();
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h) acc[h] = acc[h] * alpha_prev[h] + __uint_as_float(ov[h]);
+        for (int h = 0; h < MAXG; ++h) ov[h] = __float_as_uint(__uint_as_float(ov[h]) * alpha[h]);
+        tmem_st16(lane_addr + O_COL, ov);
+        tmem_st_wait();
       }
+      float pj[MAXG];
 #pragma unroll
       for (int h = 0; h < MAXG; ++h) {
-        if (h < G) *reinterpret_cast<__nv_bfloat16*>(sP + qp_offset(h, r)) = __float2bfloat16(pj[h]);
-        alpha_prev[h] = alpha[h];
+        pj[h] = (s[h] == -INFINITY || m_run[h] == -INFINITY) ? 0.f : exp2f(s[h] - m_run[h]);
+        l_part[h] = l_part[h] * alpha[h] + pj[h];
       }
+      // P buffer j & 1 was last read by the PV of tile j - 2
+      if (j >= 2 && !wait_pv(j - 2)) {
+        ok = false;
+        break;
+      }
+      uint8_t* pbuf = sP + (j & 1) * 2 * QBLK;
+#pragma unroll
+      for (int h = 0; h < MAXG; ++h)
+        if (h < G) *reinterpret_cast<__nv_bfloat16*>(pbuf + qp_offset(h, r)) = __float2bfloat16(pj[h]);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1]);
     }
     ok = __all_sync(0xffffffffu, ok);
-    if (ok && mbar_wait_warp(pv_done, static_cast<uint32_t>((nt - 1) & 1), abort_flag, p.status,
-                             kStatusTimeoutTmemFull)) {
-      tc_fence_after();
+    if (ok && wait_pv(nt - 1)) {
       uint32_t ov[16];
-      tmem_ld16(lane_addr + o_col(nt - 1), ov);
+      tmem_ld16(lane_addr + O_COL, ov);
       tmem_ld_wait();
 #pragma unroll
-      for (int h = 0; h < MAXG; ++h) acc[h] = acc[h] * alpha_prev[h] + __uint_as_float(ov[h]);
+      for (int h = 0; h < MAXG; ++h) acc[h] = __uint_as_float(ov[h]);
     }
     // softmax denominators: sum of the per-key partials over the 128 rows
 #pragma unroll

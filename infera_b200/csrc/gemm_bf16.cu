@@ -729,18 +729,16 @@ inline int launch_gemm(const CUtensorMap& tmP, const CUtensorMap& tmQ, const Par
 
 // Split-K factor for a plan whose tiles are set: minimise waves/split (time
 // in units of one full tile), with a 3% penalty per extra split for the
-// atomics and the finalize pass. Also applied above one wave of tiles when
-// the fp32 workspace is small (weight-streaming decode GEMMs: 224 tiles on
-// 148 SMs leave half the SMs idle for the second tile; three K splits
-// balance them, and the workspace stays in L2).
+// atomics and the finalize pass. (Splitting above one wave of tiles - 224
+// decode tiles on 148 SMs - measured slower: 58.8 vs 54.5 us for
+// 64 x 28672 x 4096.)
 inline void choose_splits(Plan& pl, int num_sms, int force_split) {
   Params& p = pl.p;
   const int tiles = p.p_tiles * p.q_tiles;
   int best = 1;
-  const bool small_ws = static_cast<long long>(p.M) * p.N * 4 <= (32ll << 20);
   if (force_split > 0) {
     best = force_split;
-  } else if (tiles < num_sms || (small_ws && tiles < 4 * num_sms)) {
+  } else if (tiles < num_sms) {
     double best_cost = 1e30;
     for (int s = 1; s <= 16; ++s) {
       if (p.nkb / s < 4 && s > 1) break;

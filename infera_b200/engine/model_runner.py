@@ -8,12 +8,15 @@ on the device ([max_num_seqs + 1, max_pages], one row per running sequence,
 plus a dummy row for graph padding) and only new page ids are scattered in.
 
 Decode-only steps replay a CUDA graph captured for the next larger batch
-bucket; steps with prefill chunks run eagerly.
+bucket and the length class of the step's longest sequence (the decode
+attention's split count is fixed inside a graph); steps with prefill chunks
+run eagerly.
 """
 
 from __future__ import annotations
 
 import bisect
+import time
 import zlib
 from dataclasses import dataclass
 
@@ -76,12 +79,20 @@ class ModelRunner:
         self.d2h_bytes = 0
         self.forwards = 0
         self.last_logits = None
+        self.last_timing = (0.0, 0.0)
+        self._t_exec = 0.0
         if self.on_gpu:
             sc = K.scratch(self.dev)
             sc.ensure_gemm(8 * 1024 * 1024)
-            sc.ensure_decode(max_num_seqs * cfg.num_heads * 4 * 128 + 64 * cfg.num_heads * 64 * 128,
-                             max_num_seqs * cfg.num_heads * 4 + 64 * cfg.num_heads * 64)
+            max_splits = max(4, K.decode_plan(max_num_seqs, cfg.num_kv_heads, cfg.max_model_len)[0])
+            sc.ensure_decode(max_num_seqs * cfg.num_heads * max_splits * 128 + 64 * cfg.num_heads * 64 * 128,
+                             max_num_seqs * cfg.num_heads * max_splits + 64 * cfg.num_heads * 64)
         self.graph_sizes = [g for g in (graph_sizes or DEFAULT_GRAPH_SIZES) if g <= max_num_seqs]
+        # decode graphs are captured per length class (the longest sequence
+        # of the step): the split count of the decode attention is fixed in a
+        # graph, and short batches should not launch the empty splits of
+        # long ones
+        self.len_classes = sorted({c for c in (8192, 16384) if c < cfg.max_model_len} | {cfg.max_model_len})
         self.graphs: dict[int, tuple] = {}
         self.graph_launches: dict[int, int] = {}
         self.use_graphs = use_graphs and self.on_gpu
@@ -159,6 +170,7 @@ class ModelRunner:
         """``layer_hook(layer)``: called by the model right after each
         layer's KV write (forces the eager path)."""
         self.forwards += 1
+        self._t_exec = time.perf_counter()
         self._layer_hook = layer_hook
         ids, pos, slots, logits_rows, sampled, Tp, pmeta, dmeta = self._pack(sched, bt_updates)
         T = len(ids)
@@ -182,7 +194,10 @@ class ModelRunner:
             return []
         if self.on_gpu:
             self.h_out[:n].copy_(src[:n], non_blocking=True)
+            t0 = time.perf_counter()
             torch.cuda.current_stream().synchronize()
+            # host time spent issuing this step, and waiting for the device
+            self.last_timing = (t0 - self._t_exec, time.perf_counter() - t0)
             self.d2h_bytes += 4 * n
             return self.h_out[:n].tolist()
         return src[:n].tolist()
@@ -234,7 +249,8 @@ class ModelRunner:
             fb.d_seq_lens = v("dl")
             fb.d_bt_rows = v("drow")
             fb.num_decode = B
-            fb.d_splits = K.decode_splits(B, self.cfg.num_kv_heads, max(d_lens)) if self.on_gpu else 1
+            if self.on_gpu:
+                fb.d_splits, fb.d_tps = K.decode_plan(B, self.cfg.num_kv_heads, max(d_lens))
         logits = self.model.forward(fb, self.k_cache, self.v_cache, self.bufs)
         self.last_logits = logits
         temp = v("temp").view(torch.float32)
@@ -288,35 +304,39 @@ class ModelRunner:
         stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(stream):
             for B in reversed(self.graph_sizes):
-                lay, v = self._graph_inputs(B)
-                # benign placeholder values: every row reads the dummy table row
-                self.g_in.zero_()
-                v("dl").fill_(1)
-                v("drow").fill_(self.dummy_row)
-                v("slots").fill_(-1)
-                v("lidx").copy_(torch.arange(B, dtype=torch.int32, device=self.dev))
-                splits = K.decode_splits(B, self.cfg.num_kv_heads, 8192)
-                fb = ForwardBatch(token_ids=v("ids"), positions=v("pos"), slots=v("slots"), logits_idx=v("lidx"),
-                                  num_prefill_tokens=0, d_block_table=self.block_table, d_seq_lens=v("dl"),
-                                  d_splits=splits, num_decode=B)
-                fb.d_bt_rows = v("drow")
-                so, sn = lay["seed"]
-
-                def run():
-                    logits = self.model.forward(fb, self.k_cache, self.v_cache, self.bufs)
-                    K.sample(logits, v("temp").view(torch.float32), self.g_in[so:so + sn].view(torch.int64),
-                             out=self.g_out[:B])
-
-                run()  # warm-up outside capture (tensor-map cache, lazy init)
-                torch.cuda.synchronize()
-                g = torch.cuda.CUDAGraph()
-                n0 = K.LAUNCHES[0]
-                with torch.cuda.graph(g, pool=pool, stream=stream):
-                    run()
-                self.graph_launches[B] = K.LAUNCHES[0] - n0
-                self.graphs[B] = (g, lay)
+                for cls in self.len_classes:
+                    self._capture_one(B, cls, pool, stream)
         torch.cuda.current_stream().wait_stream(stream)
         torch.cuda.synchronize()
+
+    def _capture_one(self, B: int, cls: int, pool, stream) -> None:
+        lay, v = self._graph_inputs(B)
+        # benign placeholder values: every row reads the dummy table row
+        self.g_in.zero_()
+        v("dl").fill_(1)
+        v("drow").fill_(self.dummy_row)
+        v("slots").fill_(-1)
+        v("lidx").copy_(torch.arange(B, dtype=torch.int32, device=self.dev))
+        splits, tps = K.decode_plan(B, self.cfg.num_kv_heads, cls)
+        fb = ForwardBatch(token_ids=v("ids"), positions=v("pos"), slots=v("slots"), logits_idx=v("lidx"),
+                          num_prefill_tokens=0, d_block_table=self.block_table, d_seq_lens=v("dl"),
+                          d_splits=splits, d_tps=tps, num_decode=B)
+        fb.d_bt_rows = v("drow")
+        so, sn = lay["seed"]
+
+        def run():
+            logits = self.model.forward(fb, self.k_cache, self.v_cache, self.bufs)
+            K.sample(logits, v("temp").view(torch.float32), self.g_in[so:so + sn].view(torch.int64),
+                     out=self.g_out[:B])
+
+        run()  # warm-up outside capture (tensor-map cache, lazy init)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        n0 = K.LAUNCHES[0]
+        with torch.cuda.graph(g, pool=pool, stream=stream):
+            run()
+        self.graph_launches[(B, cls)] = K.LAUNCHES[0] - n0
+        self.graphs[(B, cls)] = (g, lay)
 
     def release_graphs(self) -> None:
         """Drop the captured graphs (a graph holding NCCL calls must be
@@ -328,8 +348,9 @@ class ModelRunner:
     def _run_graph(self, ids, pos, slots, dmeta, temps, seeds, bt_updates) -> list[int]:
         B = len(ids)
         Bg = self.graph_sizes[bisect.bisect_left(self.graph_sizes, B)]
-        g, lay = self.graphs[Bg]
         d_lens, d_rows = dmeta
+        cls = self.len_classes[min(bisect.bisect_left(self.len_classes, max(d_lens)), len(self.len_classes) - 1)]
+        g, lay = self.graphs[(Bg, cls)]
         pad = Bg - B
         h = self.h_in.numpy()
         h[: lay["_end"]] = 0
@@ -359,6 +380,6 @@ class ModelRunner:
         if nu:
             K.scatter_i32(self.block_table, self.d_in[end:end + nu], self.d_in[end + nu:end + 2 * nu])
         g.replay()
-        K.LAUNCHES[0] += self.graph_launches[Bg]
+        K.LAUNCHES[0] += self.graph_launches[(Bg, cls)]
         del pad
         return self._d2h(self.g_out, B)

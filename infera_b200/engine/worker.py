@@ -108,6 +108,9 @@ def parse_args(argv=None):
     p.add_argument("--dp-rank", type=int, default=None,
                    help="data-parallel attention rank this worker serves (registered for DP-rank routing)")
     p.add_argument("--dp-size", type=int, default=1)
+    p.add_argument("--nats-jetstream", action="store_true",
+                   help="with --nats-url: KV events into the INFERA_KV_EVENTS stream and this worker's view into "
+                        "the INFERA_KV_VIEWS bucket; requests from the INFERA_REQUESTS work queue")
     p.add_argument("--nats-url", default=None,
                    help="also serve requests over NATS (infera.req.<worker token>); registers request_transport=bus")
     p.add_argument("--log-level", default="info")
@@ -275,12 +278,14 @@ async def run_worker(args) -> None:
         class _W:
             worker_id = payload["worker_id"]
 
-        bus_srv = BusRequestServer(bus, BusRequestClient.token(_W), local_http_handler(f"http://127.0.0.1:{args.port}"))
+        bus_srv = BusRequestServer(bus, BusRequestClient.token(_W), local_http_handler(f"http://127.0.0.1:{args.port}"),
+                                   jetstream=args.nats_jetstream)
         await bus_srv.start()
         if args.kv_events_endpoint:   # KV events onto the bus as well
             from infera_b200.kv.nats_relay import KvEventNatsRelay
 
-            relay = KvEventNatsRelay(bus, payload["worker_id"], args.kv_events_endpoint)
+            relay = KvEventNatsRelay(bus, payload["worker_id"], args.kv_events_endpoint,
+                                     jetstream=args.nats_jetstream, block_size=args.page_size)
             relay.start()
     reg = None
     hb = None

@@ -64,6 +64,7 @@ class ForwardBatch:
     d_seq_lens: torch.Tensor | None = None
     d_bt_rows: torch.Tensor | None = None
     d_splits: int = 1
+    d_tps: int = 0                 # decode attention tiles per split (0: even split)
     num_decode: int = 0
     layer_hook: object = None  # called with the layer index after its KV write
 
@@ -212,7 +213,8 @@ class DenseModel:
                                host_meta=fb.p_host_meta, bt_rows=fb.p_bt_rows)
             if fb.num_decode > 0:
                 K.attn_decode(qkv[Tp:T], kc, vc, fb.d_block_table, fb.d_seq_lens, cfg.num_heads, cfg.num_kv_heads,
-                              self.scale, splits=fb.d_splits, out=attn[Tp:T], bt_rows=fb.d_bt_rows)
+                              self.scale, splits=fb.d_splits, out=attn[Tp:T], bt_rows=fb.d_bt_rows,
+                              tiles_per_split=fb.d_tps)
             nxt = self.w.layers[li + 1]["ln1"] if li + 1 < cfg.num_layers else self.w.final_norm
             if "moe" in lw:
                 K.linear(attn, lw["o"], out=o)

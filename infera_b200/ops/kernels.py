@@ -375,6 +375,24 @@ def _ref_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor
     return outs
 
 
+# Decode attention splits every sequence into chunks of this many 128-key
+# tiles at the same absolute positions (INFERA_DECODE_TPS=0: divide each
+# sequence evenly over decode_splits() splits instead).
+import os as _os
+
+DECODE_TILES_PER_SPLIT = int(_os.environ.get("INFERA_DECODE_TPS", "16"))
+
+
+def decode_plan(batch: int, hkv: int, max_len: int) -> tuple[int, int]:
+    """(splits, tiles per split) of the decode attention for a batch whose
+    longest sequence has ``max_len`` keys."""
+    tps = DECODE_TILES_PER_SPLIT
+    if tps <= 0:
+        return decode_splits(batch, hkv, max_len), 0
+    tiles = max(1, (max_len + 127) // 128)
+    return max(1, -(-tiles // tps)), tps
+
+
 def decode_splits(batch: int, hkv: int, max_len: int, num_sms: int = 148) -> int:
     """Split-KV factor: enough CTAs for ~2 waves, at least 4 tiles per split."""
     ctas = max(1, batch * hkv)

@@ -186,9 +186,15 @@ class KvEventClient:
                 sock.close(linger=0)
 
     # ------------------------------------------------------------------ NATS
-    async def attach_nats(self, bus) -> None:
-        """Receive every worker's KV-event batches from the bus (core NATS,
-        subject ``infera.kv.events.<worker token>``)."""
+    async def attach_nats(self, bus, jetstream: bool = False) -> None:
+        """Receive every worker's KV-event batches from the bus (subject
+        ``infera.kv.events.<worker token>``). With ``jetstream``: first the
+        workers' views from the ``INFERA_KV_VIEWS`` bucket (the latest value
+        per worker, and every refresh after it: bootstrap and self-heal),
+        then new batches from the ``INFERA_KV_EVENTS`` stream."""
+
+        def by_token(token: str):
+            return next((w for w in self.workers.values() if worker_token(w.worker_id) == token), None)
 
         async def on_batch(m) -> None:
             token = m.subject[len(NATS_SUBJECT):]
@@ -204,10 +210,38 @@ class KvEventClient:
             for ev in batch.events:
                 self._handle(wv, ev, batch.attn_dp_rank)
 
-        self._nats_unsub = await bus.subscribe(NATS_SUBJECT + ">", on_batch)
+        if not jetstream:
+            self._nats_unsub = await bus.subscribe(NATS_SUBJECT + ">", on_batch)
+            return
+        from infera_b200.common.jetstream import JetStream
+        from infera_b200.kv.nats_relay import KV_STREAM, VIEW_BUCKET, decode_view
+
+        js = JetStream(bus)
+        await js.add_stream(KV_STREAM, [NATS_SUBJECT + ">"], max_age_s=600.0)
+        kv = await js.key_value(VIEW_BUCKET)
+
+        async def on_view(token: str, value: bytes | None) -> None:
+            wv = by_token(token)
+            if wv is None or value is None:
+                return
+            try:
+                ranks = decode_view(value)
+            except Exception:
+                self.stats["decode_errors"] += 1
+                return
+            for r, (view, hmap) in ranks.items():
+                wv.views[r] = view
+                wv.maps[r] = hmap
+            self.stats["bootstraps"] = self.stats.get("bootstraps", 0) + 1
+
+        self._view_unsub = await kv.watch(on_view)
+        self._nats_unsub = await js.subscribe_push(KV_STREAM, on_batch, filter_subject=NATS_SUBJECT + ">",
+                                                   deliver_policy="new")
 
     async def aclose(self) -> None:
         for wv in self.workers.values():
             self._cancel(wv)
         if getattr(self, "_nats_unsub", None) is not None:
             self._nats_unsub()
+        if getattr(self, "_view_unsub", None) is not None:
+            self._view_unsub()

@@ -72,7 +72,8 @@ def build_router_stack(args, registry=None, transport=None):
         # connected by ``serve`` inside the event loop
         transport = RoutingTransport(bus_client=BusRequestClient(NatsBus(args.nats_url),
                                                                  idle_timeout=args.nats_idle_timeout,
-                                                                 max_duration=args.nats_max_duration))
+                                                                 max_duration=args.nats_max_duration,
+                                                                 jetstream=getattr(args, "nats_jetstream", False)))
     if transport is not None:
         kw["transport"] = transport
     router_cls = DirectRouter if args.router_mode == "direct" else AutoRouter
@@ -108,7 +109,7 @@ async def serve(args) -> None:
             from infera_b200.common.nats_wire import NatsBus
 
             bus = await NatsBus(args.nats_url).connect()
-        await kv.attach_nats(bus)
+        await kv.attach_nats(bus, jetstream=getattr(args, "nats_jetstream", False))
     await state.kv_plane.start()
     await state.registry.start()
     app = build_app(state)

@@ -38,6 +38,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--router-policy", choices=POLICY_NAMES, default="kv-aware")
     p.add_argument("--kv-event-transport", choices=("zmq", "nats"), default=_env("INFERA_KV_EVENT_TRANSPORT", "zmq"),
                    help="nats: KV-event batches arrive on infera.kv.events.> (workers run the NATS relay)")
+    p.add_argument("--nats-jetstream", action="store_true", default=_env("INFERA_NATS_JETSTREAM", "") == "1",
+                   help="with NATS: KV events from the INFERA_KV_EVENTS stream with views bootstrapped from the "
+                        "INFERA_KV_VIEWS bucket; bus requests through the INFERA_REQUESTS work queue")
     p.add_argument("--router-tokenizer-path", default=_env("INFERA_ROUTER_TOKENIZER_PATH"))
     p.add_argument("--kv-overlap-weight", type=float, default=1.0)
     p.add_argument("--kv-prefill-overlap-weight", type=float, default=None)
