@@ -109,6 +109,10 @@ class TierManager:
         self._new_loads: list = []
         if hasattr(store, "add_listener"):
             store.add_listener(self._on_store_drop)
+        # the kvd daemon's shared arena, page-locked: promotes copy pages from
+        # it straight into device memory
+        self.arena_t = store.register_arena() if self.on_gpu and hasattr(store, "register_arena") else None
+        self.stats["direct_pages"] = 0
         self._loader_t = None
         if self.async_load:
             self._loader_t = threading.Thread(target=self._loader, daemon=True, name="kv-tier-loader")
@@ -256,11 +260,40 @@ class TierManager:
             m += 1
         return m
 
-    def _scatter(self, buf: int, m: int, stream) -> None:
+    def _fill_direct(self, buf: int, pages: list[int], hashes: list[int], stream) -> tuple[int, list]:
+        """Arena-resident blobs: one DMA per page from the registered arena
+        into the device staging slot. Returns (pages issued, [(arena, blob
+        offset, version)]) for the version check after the copies land."""
+        from infera_b200.engine.packed_format import unpack_header
+
+        m, checks = 0, []
+        for i, (page, h) in enumerate(zip(pages, hashes)):
+            r = self.store.read_shared(self._key(h))
+            if r is None:
+                break
+            arena, off, size, ver = r
+            try:
+                hdr = unpack_header(memoryview(arena.mm)[off:off + min(size, 1 << 16)])
+            except PackedFormatError:
+                break
+            if (hdr.num_layers != self.L or hdr.hidden_dim != self.H or hdr.chunk_tokens != self.ps
+                    or hdr.num_kv_channels != self.C or hdr.payload_byte_offset + self.page_bytes > size):
+                break
+            po = off + hdr.payload_byte_offset
+            with torch.cuda.stream(stream):
+                self.load_dev[buf, i].view(torch.uint8).copy_(self.arena_t[po:po + self.page_bytes],
+                                                             non_blocking=True)
+            self.load_idx_np[buf, i] = page
+            checks.append((arena, off, ver))
+            m += 1
+        return m, checks
+
+    def _scatter(self, buf: int, m: int, stream, staged: bool = True) -> None:
         if self.on_gpu:
             with torch.cuda.stream(stream):
                 self.load_idx_dev[buf, :m].copy_(self.load_idx_host[buf, :m], non_blocking=True)
-                self.load_dev[buf, :m].copy_(self.load_host[buf, :m], non_blocking=True)
+                if staged:
+                    self.load_dev[buf, :m].copy_(self.load_host[buf, :m], non_blocking=True)
                 K.kv_page_copy(self.k, self.v, self.load_dev[buf, :m], self.load_idx_dev[buf, :m], self.ps,
                                gather=False, page_major=True)
                 e = torch.cuda.Event()
@@ -279,10 +312,25 @@ class TierManager:
                 self.load_ev[buf].synchronize()      # that buffer's previous copies have landed
                 self.load_ev[buf] = None
             want = pages[c0:c0 + self.load_chunk]
-            m = self._fill(buf, want, hashes[c0:c0 + self.load_chunk])
-            if m:
-                self._scatter(buf, m, stream)
-                self.load_buf ^= 1
+            if self.arena_t is not None and hasattr(self.store, "read_shared"):
+                m, checks = self._fill_direct(buf, want, hashes[c0:c0 + self.load_chunk], stream)
+                if m:
+                    self._scatter(buf, m, stream, staged=False)
+                    self.load_buf ^= 1
+                    # a slot rewritten while it was being copied is not used
+                    self.load_ev[buf].synchronize()
+                    ok = 0
+                    for arena, off, ver in checks:
+                        if arena.version_at(off) != ver:
+                            break
+                        ok += 1
+                    self.stats["direct_pages"] += ok
+                    m = ok
+            else:
+                m = self._fill(buf, want, hashes[c0:c0 + self.load_chunk])
+                if m:
+                    self._scatter(buf, m, stream)
+                    self.load_buf ^= 1
             got += m
             if m < len(want):
                 break

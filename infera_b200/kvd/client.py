@@ -64,6 +64,14 @@ class KvdClient:
             await W.write_frame(self.writer, msg)
             return await W.read_frame(self.reader)
 
+    async def get_shared(self, key: bytes):
+        """(payload offset in the arena, size, version) of a value held in the
+        shared arena; None when it is not (missing, or served inline)."""
+        r = await self._call(W.Get(key))
+        if isinstance(r, W.GetSharedResponse):
+            return r.slot_offset, r.size, r.version
+        return None
+
     async def get(self, key: bytes) -> bytes | None:
         r = await self._call(W.Get(key))
         if isinstance(r, W.GetSharedResponse):
@@ -143,6 +151,23 @@ class SyncKvdStore:
 
     def exists(self, key: bytes) -> bool:
         return self._run(self.client.exists([key]))[0]
+
+    def register_arena(self):
+        """Page-lock the shared arena for device copies; a uint8 tensor over
+        it, or None (no arena / no GPU)."""
+        if self.client.arena is None:
+            return None
+        if getattr(self, "_arena_t", None) is None:
+            self._arena_t = self.client.arena.register_cuda()
+        return self._arena_t
+
+    def read_shared(self, key: bytes):
+        """(arena view, payload offset, size, version) of an arena-held value,
+        or None (then use :meth:`get`)."""
+        if self.client.arena is None:
+            return None
+        r = self._run(self.client.get_shared(key))
+        return None if r is None else (self.client.arena, *r)
 
     def exists_many(self, keys: list[bytes]) -> list[bool]:
         """One round trip for a run of keys (the tier manager's hit count)."""

@@ -8,9 +8,11 @@ bump it to even. Readers copy the payload between two version reads and
 retry when the version was odd or changed, so a reader never returns a torn
 value (``infera/kvd/shared_arena.py:193-1201`` uses the same slot protocol).
 
-The fd is handed to clients over the daemon's Unix socket (SCM_RIGHTS);
-engines register the mapping with ``cudaHostRegister`` so device copies
-from it are DMA transfers.
+The fd is handed to clients over the daemon's Unix socket (SCM_RIGHTS); an
+engine on a GPU registers its mapping with ``cudaHostRegister``
+(:meth:`ArenaView.register_cuda`), so the tier's promotes copy a page
+straight from the arena into device memory (a DMA transfer, no host-side
+copy) and validate the slot's version after the copy landed.
 """
 
 from __future__ import annotations
@@ -125,10 +127,42 @@ class ArenaView:
                 return data
         return None
 
+    def version_at(self, payload_offset: int) -> int:
+        return _HDR.unpack_from(self.mm, payload_offset - HEADER)[0]
+
+    def register_cuda(self):
+        """Page-lock the mapping for the CUDA device copies (cudaHostRegister)
+        and return a uint8 CPU tensor over it (torch reports it pinned, so
+        ``copy_(..., non_blocking=True)`` from its slices is a DMA transfer).
+        Returns None when no GPU is usable."""
+        try:
+            import ctypes
+
+            import torch
+
+            if not torch.cuda.is_available():
+                return None
+            addr = ctypes.addressof(ctypes.c_char.from_buffer(self.mm))
+            rc = torch.cuda.cudart().cudaHostRegister(addr, self.size, 0)
+            if int(rc) != 0:
+                return None
+            self._registered = addr
+            return torch.frombuffer(self.mm, dtype=torch.uint8)
+        except Exception:
+            return None
+
     def write_payload(self, payload_offset: int, data) -> None:
         """Fill a slot leased by SET_RESERVE (the daemon owns the seqlock)."""
         self.mm[payload_offset: payload_offset + len(data)] = data
 
     def close(self) -> None:
+        if getattr(self, "_registered", None) is not None:
+            try:
+                import torch
+
+                torch.cuda.cudart().cudaHostUnregister(self._registered)
+            except Exception:
+                pass
+            self._registered = None
         self.mm.close()
         os.close(self.fd)

@@ -66,3 +66,49 @@ def test_tier_evict_save_and_async_promote_match_recompute():
     err = float((got - ref).norm() / ref.norm())
     assert err < 2e-2, err
     eng.tier.close()
+
+
+def test_tier_promote_from_kvd_shared_arena_by_dma(tmp_path):
+    """With the kvd daemon's shared arena (handed over SCM_RIGHTS) page-locked
+    by cudaHostRegister, promotes copy each page straight from the arena
+    into device memory; the pages come back byte-identical."""
+    import asyncio
+    import threading
+
+    from infera_b200.kvd.server import KvdServer
+    from infera_b200.kvd.shared_arena import SharedArena
+    from infera_b200.kvd.store import HostStore
+
+    path = str(tmp_path / "kvd.sock")
+    store = HostStore(0, arena=SharedArena(256, 1 << 16))
+    loop = asyncio.new_event_loop()
+    ready = threading.Event()
+
+    async def serve():
+        srv = KvdServer(path, store)
+        await srv.start()
+        ready.set()
+
+    th = threading.Thread(target=lambda: (loop.run_until_complete(serve()), loop.run_forever()), daemon=True)
+    th.start()
+    assert ready.wait(10)
+    try:
+        g = torch.Generator().manual_seed(12)
+        a = torch.randint(0, 4000, (320,), generator=g).tolist()
+        eng = _engine(kv_tier=f"kvd:{path}")
+        assert eng.tier.arena_t is not None                  # the arena is page-locked for DMA
+        sp = SamplingParams(max_tokens=2, ignore_eos=True)
+        eng.generate([a], sp)
+        hashes = chain_hashes(a, 16)[:19]
+        before = _gather(eng, _pages_of(eng, hashes))
+        for _ in range(3):
+            eng.generate([torch.randint(0, 4000, (300,), generator=g).tolist()], sp)
+        eng.tier.flush()
+        _first_logits(eng, "a2", a + [1, 2])
+        assert eng.tier.stats["direct_pages"] >= 16, eng.tier.stats
+        after = _gather(eng, _pages_of(eng, hashes))
+        assert torch.equal(after, before)
+        assert K.scratch(torch.device("cuda", 0)).read_status() == 0
+        eng.tier.close()
+    finally:
+        loop.call_soon_threadsafe(loop.stop)
