@@ -79,3 +79,49 @@ def test_lm_head_fused_gather_two_ranks():
            "--check-only"]
     r = subprocess.run(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, timeout=300)
     assert r.returncode == 0, r.stdout.decode()[-3000:]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_worker_serves_over_http():
+    """``python -m infera_b200.engine.worker --tp-size 2``: the worker launches
+    its two engine-core ranks with torch.distributed.run and serves the
+    OpenAI API; greedy completions come back."""
+    import json
+    import time
+
+    import httpx
+
+    from infera_b200.common.net import free_tcp_port
+
+    port = free_tcp_port()
+    env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
+    p = subprocess.Popen([sys.executable, "-m", "infera_b200.engine.worker", "--model", "llama-3.1-8b",
+                          "--tp-size", "2", "--port", str(port), "--max-num-seqs", "16", "--log-level", "warning"],
+                         env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, start_new_session=True)
+    url = f"http://127.0.0.1:{port}"
+    try:
+        t0 = time.time()
+        while time.time() - t0 < 400:
+            try:
+                if httpx.get(url + "/health", timeout=2).status_code == 200:
+                    break
+            except httpx.HTTPError:
+                pass
+            if p.poll() is not None:
+                raise AssertionError(p.stdout.read().decode()[-3000:])
+            time.sleep(1)
+        outs = []
+        for prompt in ([1, 2, 3, 4, 5, 6, 7, 8], list(range(100, 400))):
+            r = httpx.post(url + "/v1/completions", json={"model": "llama-3.1-8b", "prompt": prompt, "max_tokens": 8,
+                                                          "ignore_eos": True, "return_token_ids": True}, timeout=120)
+            assert r.status_code == 200, r.text
+            outs.append(r.json()["choices"][0])
+        assert all(len(o.get("token_ids") or []) == 8 for o in outs), json.dumps(outs)[:500]
+    finally:
+        import signal as _signal
+
+        os.killpg(p.pid, _signal.SIGTERM)
+        try:
+            p.wait(timeout=60)
+        except subprocess.TimeoutExpired:
+            os.killpg(p.pid, _signal.SIGKILL)
