@@ -10,7 +10,10 @@ Cases: gemm_prefill (2048x6144x4096 bf16), gemm_decode (64 tokens x
 tail each), fp8_decode (64 x 28672 x 8192 e4m3,
 block scales, SwiGLU), fp8_prefill (4096 x 8192 x 8192 e4m3), mla_decode (64
 queries x 128 heads over 4096 latent keys each), prefill_attn (2048 queries over 2048 keys,
-causal), prefill_attn_prefix (1024 queries over 8192 keys). Prints one JSON
+causal), prefill_attn_prefix (1024 queries over 8192 keys), mla_prefill /
+mla_prefill_prefix (DeepSeek-V3 MLA prompt chunk, 128 heads: 2048 queries
+over 2048 keys causal, or 1024 over 8192; the non-absorbed path against the
+absorbed latent kernel on the same queries). Prints one JSON
 line per case: mean CUDA-event time per launch after 3 warm-up launches, and the
 achieved TFLOP/s or GB/s.
 """
@@ -150,6 +153,34 @@ def run_case(case: str, iters: int) -> dict:
         ms = _time(lambda: K.attn_prefill(q, kc, vc, bt, *meta, tiles, hq, hkv, 1 / math.sqrt(D)), iters)
         keys = sum(ctx - ql + i + 1 for i in range(ql))
         return {"case": case, "ms": ms, "tflops": 4 * keys * D * hq / ms / 1e9}
+    if case in ("mla_prefill", "mla_prefill_prefix"):
+        from infera_b200.ops import mla as M
+
+        ql, ctx = (2048, 2048) if case == "mla_prefill" else (1024, 8192)
+        hq = 128
+        pages = ctx // 16
+        cache = (torch.randn(pages * 16, 576, device=dev, generator=g) * 0.5).to(bf)
+        bt = torch.arange(pages, device=dev, dtype=torch.int32).view(1, -1)
+        qb = (torch.randn(ql, hq * 192, device=dev, generator=g) * 0.5).to(bf)
+        q_full = (torch.randn(ql, hq, 576, device=dev, generator=g) * 0.5).to(bf)
+        w_uk = (torch.randn(hq, 512, 128, device=dev, generator=g) / math.sqrt(512)).to(bf)
+        w_uv = (torch.randn(hq, 128, 512, device=dev, generator=g) / math.sqrt(512)).to(bf)
+        w_up = M.kv_up_weight(w_uk, w_uv)
+        tiles = torch.tensor(K.prefill_tiles([ql]), dtype=torch.int32, device=dev)
+        meta = [torch.tensor([v], dtype=torch.int32, device=dev) for v in (0, ql, ctx)]
+        scale = M.default_scale(128, 64)
+        run = lambda: M.mla_prefill(qb, q_full, cache, bt, None, ([ql], [ctx]), *meta, tiles, w_up, hq, 128,  # noqa
+                                    128, scale)
+        ms = _time(run, iters)
+        keys = sum(ctx - ql + i + 1 for i in range(ql))
+        attn_fl = 2 * keys * hq * (192 + 128)
+        up_fl = 2 * ctx * 512 * hq * 256
+        # the absorbed latent kernel on the same queries (one per token)
+        rows = torch.zeros(ql, dtype=torch.int32, device=dev)
+        kvl = torch.arange(ctx - ql + 1, ctx + 1, dtype=torch.int32, device=dev)
+        ms_abs = _time(lambda: M.mla_attention(q_full, cache, bt, rows, kvl, scale, max_kvlen=ctx), max(2, iters // 4))
+        return {"case": case, "ms": ms, "tflops_attn_plus_up": (attn_fl + up_fl) / ms / 1e9,
+                "ms_absorbed_attention_only": ms_abs, "speedup_vs_absorbed": ms_abs / ms}
     if case in ("moe_decode", "moe_prefill"):
         # one expert-parallel shard of a DeepSeek-V3 layer: 32 local experts,
         # hidden 7168, expert width 2048; tokens x 8 slots spread over them

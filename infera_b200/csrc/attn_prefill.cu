@@ -9,15 +9,25 @@
 //               share a TMEM lane quadrant (the same 32 rows) and each
 //               handles half of the 128 keys of S / P and half of the 128
 //               dims of O, exchanging only per-row maxima (bounded mbarrier
-//               pair barrier); the exponentials run while the previous
-//               tile's PV is on the tensor core; P goes to shared memory (K-major, 128-byte
-//               swizzle); O is rescaled in TMEM only when the running max
-//               grows by more than 2^8 (lazy rescale); final O / l epilogue.
+//               pair barrier); P (bf16 pairs) is written back into the
+//               tile's own S columns of TMEM and the PV MMA reads its A
+//               operand from there, so P never touches shared memory and
+//               the softmax of tile j does not wait for PV(j-1) unless O
+//               must be rescaled; O is rescaled in TMEM only when the
+//               running max grows by more than 2^8 (lazy rescale); final
+//               O / l epilogue.
 //               Half of the exponentials run on the FMA pipe (polynomial).
 //
 // KV cache layout (per layer): [num_slots, Hkv * 128] bf16 with slot =
 // page * 16 + offset, i.e. a page is 16 tokens x Hkv heads x 128 dims.
 // V tiles are consumed MN-major (dims contiguous) as the B operand.
+//
+// The EXT variant scores over 192 query / key dims (MLA prefill: 128
+// "nope" dims per head plus 64 rope dims that come from separate tensors,
+// the rope key shared by every head) and still accumulates 128-dim values;
+// every operand has its own row stride and per-head column stride, so the
+// up-projected [k_nope | v] rows and the latent cache's rope columns are
+// read in place.
 //
 // Reference parity: the reference runs prefill attention inside vLLM /
 // SGLang / AITER (not in its tree); this is this framework's own kernel.
@@ -31,12 +41,15 @@ constexpr int D = 128;
 constexpr int BQ = 128;
 constexpr int BKV = 128;
 constexpr int PAGE = 16;
-constexpr int HALF = 64 * 128 * 2;    // not used directly
 constexpr int BLK = 128 * 128;        // bytes of one 128-row x 64-col bf16 block (16 KiB)
 constexpr int KV_STAGES = 2;
 constexpr int NUM_THREADS = 320;  // producer, MMA, 8 softmax warps
-// smem: Q (2 blocks) + P (2 blocks) + KV_STAGES x (K 2 blocks + V 2 blocks)
-constexpr int SMEM_BYTES = 1024 + (4 + KV_STAGES * 4) * BLK + 4096;
+// 64-dim blocks of Q / K: 2, or 3 with the extra rope dims
+__host__ __device__ constexpr int qk_blocks(bool ext) { return ext ? 3 : 2; }
+// smem: Q blocks + KV_STAGES x (K blocks + V 2 blocks)
+__host__ __device__ constexpr int smem_bytes(bool ext) {
+  return 1024 + (qk_blocks(ext) + KV_STAGES * (qk_blocks(ext) + 2)) * BLK + 4096;
+}
 constexpr uint32_t S_COL0 = 0, S_COL1 = 128, O_COL = 256;
 
 struct Params {
@@ -48,6 +61,8 @@ struct Params {
   const int* bt_rows;      // [num_seqs] table row of each sequence (null: row = seq)
   int max_pages;
   int num_heads, num_kv_heads;
+  int q_hs, k_hs, v_hs;    // column stride between heads of Q / K / V (elements)
+  int qe_hs, ke_hs;        // EXT: the same for the rope Q / K columns (0: shared)
   float scale_log2;        // softmax scale * log2(e)
   __nv_bfloat16* out;      // [T, num_heads * 128]
   int ldo;
@@ -77,19 +92,18 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return x == -INFINITY ? 0.0f : r;
 }
 
-__device__ __forceinline__ uint32_t sw128_offset(int row, int chunk16) {
-  return static_cast<uint32_t>(row * 128 + ((chunk16 ^ (row & 7)) << 4));
-}
-
+template <bool EXT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                      const __grid_constant__ CUtensorMap tmV, const Params p) {
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQe,
+                      const __grid_constant__ CUtensorMap tmKe, const Params p) {
+  constexpr int QKB = qk_blocks(EXT);
+  constexpr int STB = QKB + 2;     // blocks per KV stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;              // 2 blocks: dims 0-63, 64-127
-  uint8_t* sP = smem + 2 * BLK;    // 2 blocks: keys 0-63, 64-127
-  uint8_t* sKV = smem + 4 * BLK;   // stage s: K lo, K hi, V lo, V hi
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + KV_STAGES * 4 * BLK);
+  uint8_t* sQ = smem;                // QKB blocks of 64 dims
+  uint8_t* sKV = smem + QKB * BLK;   // stage s: K blocks, V lo, V hi
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + KV_STAGES * STB * BLK);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;                 // [KV_STAGES]
   uint64_t* v_full = k_full + KV_STAGES;       // [KV_STAGES]
@@ -138,6 +152,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    if (EXT) {
+      tma_prefetch_desc(&tmQe);
+      tma_prefetch_desc(&tmKe);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -151,9 +169,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol = policy_evict_last();
-      mbar_expect_tx(q_full, 2 * BLK);
-      tma_load_2d(sQ, &tmQ, q_full, h * D, row0, pol);
-      tma_load_2d(sQ + BLK, &tmQ, q_full, h * D + 64, row0, pol);
+      mbar_expect_tx(q_full, QKB * BLK);
+      tma_load_2d(sQ, &tmQ, q_full, h * p.q_hs, row0, pol);
+      tma_load_2d(sQ + BLK, &tmQ, q_full, h * p.q_hs + 64, row0, pol);
+      if (EXT) tma_load_2d(sQ + 2 * BLK, &tmQe, q_full, h * p.qe_hs, row0, pol);
       const int bt_row = p.bt_rows != nullptr ? p.bt_rows[seq] : seq;
       const int* bt = p.block_table + static_cast<size_t>(bt_row) * p.max_pages;
       const int n_pages = (ctx + PAGE - 1) / PAGE;
@@ -168,21 +187,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
         if (j + 1 < n_kv) load_tile_pages(bt, j + 1, n_pages, nxt);  // in flight while we wait
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
-        uint8_t* base = sKV + st * 4 * BLK;
+        uint8_t* base = sKV + st * STB * BLK;
         fstamp(p, FTR_TMA, j);
-        mbar_expect_tx(&k_full[st], 2 * BLK);
+        mbar_expect_tx(&k_full[st], QKB * BLK);
 #pragma unroll
         for (int pg = 0; pg < BKV / PAGE; ++pg) {
           const int r = cur[pg] * PAGE;
-          tma_load_2d(base + pg * PAGE * 128, &tmK, &k_full[st], kvh * D, r, pol);
-          tma_load_2d(base + BLK + pg * PAGE * 128, &tmK, &k_full[st], kvh * D + 64, r, pol);
+          tma_load_2d(base + pg * PAGE * 128, &tmK, &k_full[st], kvh * p.k_hs, r, pol);
+          tma_load_2d(base + BLK + pg * PAGE * 128, &tmK, &k_full[st], kvh * p.k_hs + 64, r, pol);
+          if (EXT) tma_load_2d(base + 2 * BLK + pg * PAGE * 128, &tmKe, &k_full[st], kvh * p.ke_hs, r, pol);
         }
         mbar_expect_tx(&v_full[st], 2 * BLK);
 #pragma unroll
         for (int pg = 0; pg < BKV / PAGE; ++pg) {
           const int r = cur[pg] * PAGE;
-          tma_load_2d(base + 2 * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * D, r, pol);
-          tma_load_2d(base + 3 * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * D + 64, r, pol);
+          tma_load_2d(base + QKB * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * p.v_hs, r, pol);
+          tma_load_2d(base + (QKB + 1) * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * p.v_hs + 64, r, pol);
         }
         ++issued;
       }
@@ -201,7 +221,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t idesc_qk = make_idesc_bf16(128, 128, false);
       const uint32_t idesc_pv = make_idesc_bf16(128, 128, true);
       const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t p_addr = smem_u32(sP);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kStatusTimeoutFull);
       auto issue_pv = [&](int jj) -> bool {
         // O += P V_jj once softmax has written P for tile jj
@@ -212,14 +231,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                        kStatusTimeoutFull))
           return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sKV + st * 4 * BLK + 2 * BLK);
+        const uint32_t v_addr = smem_u32(sKV + st * STB * BLK + QKB * BLK);
+        // P of tile jj sits in the first 32 columns of each 64-column half
+        // of S(jj): keys 16s..16s+15 are 8 packed columns
+        const uint32_t p_col = (jj & 1) ? S_COL1 : S_COL0;
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
-          const uint32_t a = p_addr + (s < 4 ? s * 32 : BLK + (s - 4) * 32);
-          const uint64_t ad = make_sw128_desc(a, 16, 1024);
+          const uint32_t a_tmem = tmem + p_col + (s >> 2) * 64 + (s & 3) * 8;
           // MN-major V: LBO = distance between the two 64-dim halves, SBO = 8 keys
           const uint64_t bd = make_sw128_desc(v_addr + s * 2048, BLK, 1024);
-          umma_bf16(tmem + O_COL, ad, bd, idesc_pv, (jj > 0 || s > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + O_COL, a_tmem, bd, idesc_pv, (jj > 0 || s > 0) ? 1u : 0u);
         }
         umma_commit(o_done);
         fstamp(p, FTR_PVISSUE, jj);
@@ -235,11 +256,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         fstamp(p, FTR_KFULL, j);
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sKV + st * 4 * BLK);
+        const uint32_t k_addr = smem_u32(sKV + st * STB * BLK);
         const uint32_t s_col = (j & 1) ? S_COL1 : S_COL0;
 #pragma unroll
-        for (int s = 0; s < 8; ++s) {
-          const uint32_t off = s < 4 ? s * 32 : BLK + (s - 4) * 32;
+        for (int s = 0; s < 4 * QKB; ++s) {
+          const uint32_t off = (s >> 2) * BLK + (s & 3) * 32;
           const uint64_t ad = make_sw128_desc(q_addr + off, 16, 1024);
           const uint64_t bd = make_sw128_desc(k_addr + off, 16, 1024);
           umma_bf16(tmem + s_col, ad, bd, idesc_qk, s > 0 ? 1u : 0u);
@@ -319,10 +340,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float m_use = rescale ? m_new : m_run;
       const float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
       const bool warp_rescale = __any_sync(0xffffffffu, rescale && j > 0);
-      // P / O of the previous tile must be consumed before they are touched:
-      // a rescale of O waits here; otherwise the exponentials below run
-      // while the previous tile's PV is still on the tensor core, and the
-      // wait comes just before P is stored
+      // O must not be rescaled while the previous tile's PV accumulates into
+      // it: only a rescale waits for PV(j-1). P(j) goes to S(j)'s own
+      // columns, which no MMA in flight reads or writes (S(j+2) reuses them
+      // and is issued after PV(j); tcgen05.mma runs in issue order).
       if (j > 0 && warp_rescale) {
         if (!mbar_wait_warp(o_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status,
                             kStatusTimeoutTmemFull)) {
@@ -355,24 +376,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         sum += __low2float(bb) + __high2float(bb);
         v[i / 2] = *reinterpret_cast<uint32_t*>(&bb);   // packed pairs reuse the low half of v
       }
-      if (j > 0 && !warp_rescale) {
-        if (!mbar_wait_warp(o_done, static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status,
-                            kStatusTimeoutTmemFull)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
-      uint8_t* blk = sP + half * BLK;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const uint4 w = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        *reinterpret_cast<uint4*>(blk + sw128_offset(r, q)) = w;
-      }
+      // this half's S columns are already in registers: its packed P
+      // overwrites the first 32 of them
+      tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
       if (tr0) fstamp(p, FTR_SOFTMAX, j);
       l_run = l_run * alpha + sum;
       m_run = m_use;
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full);
       if (tr0) fstamp(p, FTR_PARRIVE, j);
@@ -430,23 +440,41 @@ static long long* g_fa_trace = nullptr;
 // trace[8 * 64] (clock64), or stop when trace is null.
 extern "C" void ib_attn_prefill_set_trace(long long* trace) { g_fa_trace = trace; }
 
-// q: [T, ldq] bf16 with head h at columns [h*128, h*128+128).
-// k_cache / v_cache: [num_slots, num_kv_heads*128] bf16.
-// tiles: device int32 [num_tiles, 2] (seq, q_block), longest first.
-extern "C" int ib_attn_prefill(const void* q, int T, int ldq, const void* k_cache, const void* v_cache,
-                               long long num_slots, const int* tiles, int num_tiles, const int* q_start,
-                               const int* q_len, const int* ctx_len, const int* block_table, const int* bt_rows,
-                               int max_pages,
-                               int num_heads, int num_kv_heads, float scale, void* out, int ldo, int* status,
-                               cudaStream_t stream) {
+namespace {
+
+struct FaOperand {
+  const void* ptr;
+  long long rows;  // rows addressable through the tensor map
+  int ld;          // row stride (elements)
+  int hs;          // column stride between heads (elements)
+  int width;       // columns read per head (64 or 128)
+  int heads;       // heads addressed (1 with hs == 0: shared)
+};
+
+bool fa_tmap(CUtensorMap* m, const FaOperand& o, int box_rows) {
+  if (o.ptr == nullptr || (reinterpret_cast<uintptr_t>(o.ptr) & 15) != 0 || (o.ld % 8) != 0 || (o.hs % 8) != 0)
+    return false;
+  const long long cols = static_cast<long long>(o.heads - 1) * o.hs + o.width;
+  if (cols > o.ld) return false;
+  return cached_tmap_2d(m, o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, o.rows, cols, o.ld, box_rows, 64);
+}
+
+template <bool EXT>
+int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const FaOperand* qe, const FaOperand* ke,
+              const int* tiles, int num_tiles, const int* q_start, const int* q_len, const int* ctx_len,
+              const int* block_table, const int* bt_rows, int max_pages, int num_heads, int num_kv_heads,
+              float scale, void* out, int ldo, int* status, cudaStream_t stream) {
   using namespace ib200::fa;
-  if (num_tiles <= 0 || T <= 0) return 0;
-  if ((ldq % 8) != 0 || (ldo % 8) != 0 || num_heads % num_kv_heads != 0) return -1;
-  CUtensorMap tq, tk, tv;
-  const int kvw = num_kv_heads * D;
-  if (!cached_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, num_heads * D, ldq, 128, 64)) return -2;
-  if (!cached_tmap_2d(&tk, k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, kvw, kvw, 16, 64)) return -2;
-  if (!cached_tmap_2d(&tv, v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, kvw, kvw, 16, 64)) return -2;
+  if (num_tiles <= 0 || q.rows <= 0) return 0;
+  if ((ldo % 8) != 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return -1;
+  CUtensorMap tq, tk, tv, tqe, tke;
+  if (!fa_tmap(&tq, q, 128) || !fa_tmap(&tk, k, 16) || !fa_tmap(&tv, v, 16)) return -2;
+  if (EXT) {
+    if (!fa_tmap(&tqe, *qe, 128) || !fa_tmap(&tke, *ke, 16)) return -2;
+  } else {
+    tqe = tq;
+    tke = tk;
+  }
   Params p;
   p.tiles = tiles;
   p.q_start = q_start;
@@ -457,6 +485,11 @@ extern "C" int ib_attn_prefill(const void* q, int T, int ldq, const void* k_cach
   p.max_pages = max_pages;
   p.num_heads = num_heads;
   p.num_kv_heads = num_kv_heads;
+  p.q_hs = q.hs;
+  p.k_hs = k.hs;
+  p.v_hs = v.hs;
+  p.qe_hs = EXT ? qe->hs : 0;
+  p.ke_hs = EXT ? ke->hs : 0;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = ldo;
@@ -466,11 +499,58 @@ extern "C" int ib_attn_prefill(const void* q, int T, int ldq, const void* k_cach
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(fa_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(fa_prefill_kernel<EXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(EXT));
     attr_set[dev] = true;
   }
   dim3 grid(num_heads, num_tiles);
-  fa_prefill_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  fa_prefill_kernel<EXT><<<grid, NUM_THREADS, smem_bytes(EXT), stream>>>(tq, tk, tv, tqe, tke, p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+}  // namespace
+
+// q: [T, ldq] bf16 with head h at columns [h*128, h*128+128).
+// k_cache / v_cache: [num_slots, num_kv_heads*128] bf16.
+// tiles: device int32 [num_tiles, 2] (seq, q_block), longest first.
+extern "C" int ib_attn_prefill(const void* q, int T, int ldq, const void* k_cache, const void* v_cache,
+                               long long num_slots, const int* tiles, int num_tiles, const int* q_start,
+                               const int* q_len, const int* ctx_len, const int* block_table, const int* bt_rows,
+                               int max_pages,
+                               int num_heads, int num_kv_heads, float scale, void* out, int ldo, int* status,
+                               cudaStream_t stream) {
+  using namespace ib200::fa;
+  if (T <= 0) return 0;
+  const int kvw = num_kv_heads * D;
+  const FaOperand fq{q, T, ldq, D, D, num_heads};
+  const FaOperand fk{k_cache, num_slots, kvw, D, D, num_kv_heads};
+  const FaOperand fv{v_cache, num_slots, kvw, D, D, num_kv_heads};
+  return fa_launch<false>(fq, fk, fv, nullptr, nullptr, tiles, num_tiles, q_start, q_len, ctx_len, block_table,
+                          bt_rows, max_pages, num_heads, num_kv_heads, scale, out, ldo, status, stream);
+}
+
+// Attention over 128 + 64 score dims (MLA prefill, not absorbed):
+//   q  [T, ldq]:   head h's 128 nope dims at column h*q_hs
+//   qe [T, ldqe]:  head h's 64 rope dims at column h*qe_hs
+//   k  [rows, ldk]: key head g's 128 nope dims at column g*k_hs
+//   ke [rows, ldke]: key head g's 64 rope dims at column g*ke_hs (0: shared)
+//   v  [rows, ldv]: value head g's 128 dims at column g*v_hs
+// k / ke / v rows are addressed through the block table like cache slots
+// (page of 16 rows); out [T, ldo] gets head h at columns h*128.
+extern "C" int ib_attn_prefill_ext(const void* q, int T, int ldq, int q_hs, const void* qe, int ldqe, int qe_hs,
+                                   const void* k, int ldk, int k_hs, const void* ke, int ldke, int ke_hs,
+                                   const void* v, int ldv, int v_hs, long long num_rows, const int* tiles,
+                                   int num_tiles, const int* q_start, const int* q_len, const int* ctx_len,
+                                   const int* block_table, const int* bt_rows, int max_pages, int num_heads,
+                                   int num_kv_heads, float scale, void* out, int ldo, int* status,
+                                   cudaStream_t stream) {
+  using namespace ib200::fa;
+  if (T <= 0) return 0;
+  const FaOperand fq{q, T, ldq, q_hs, D, num_heads};
+  const FaOperand fqe{qe, T, ldqe, qe_hs, 64, qe_hs == 0 ? 1 : num_heads};
+  const FaOperand fk{k, num_rows, ldk, k_hs, D, num_kv_heads};
+  const FaOperand fke{ke, num_rows, ldke, ke_hs, 64, ke_hs == 0 ? 1 : num_kv_heads};
+  const FaOperand fv{v, num_rows, ldv, v_hs, D, num_kv_heads};
+  return fa_launch<true>(fq, fk, fv, &fqe, &fke, tiles, num_tiles, q_start, q_len, ctx_len, block_table, bt_rows,
+                         max_pages, num_heads, num_kv_heads, scale, out, ldo, status, stream);
 }

@@ -15,10 +15,14 @@ Per layer (q_lora_rank > 0):
                        (+ shared expert) after
 
 The per-head absorptions run as grouped GEMMs with the heads as groups
-(``ib_gemm_grouped``), the attention as ``ib_mla_decode`` for prompt and
-decode tokens alike (each token is a query with its own causal key count),
-the big projections as fp8 block-scaled GEMMs when ``weight_dtype`` is
-"fp8". RoPE rotates pairs (i, i + 32) of the 64 rope dims (a fixed
+(``ib_gemm_grouped``), decode tokens' attention as ``ib_mla_decode`` (each
+token a query with its own causal key count). Prompt chunks take the
+non-absorbed path: every sequence's latent context is up-projected once to
+per-head [k_nope | v] (one GEMM against ``w_kv_up``) and attended by the
+flash-attention kernel over 128 + 64 score dims with 128-dim values, which
+needs no W_UV absorption afterwards (``M.mla_prefill``; the absorbed decode
+kernel for prompt tokens too when ``INFERA_MLA_PREFILL=absorbed``). The big
+projections run as fp8 block-scaled GEMMs when ``weight_dtype`` is "fp8". RoPE rotates pairs (i, i + 32) of the 64 rope dims (a fixed
 permutation of the interleaved pairing of the published checkpoints; the
 weights here are random).
 
@@ -74,6 +78,7 @@ class MLAWeights:
             # W_UV [Hq, dv, L] (out = W_UV o_lat), both K-major for the GEMMs
             lw["w_uk"] = rnd(Hq, L, dn, scale=1.0 / math.sqrt(dn))
             lw["w_uv"] = rnd(Hq, dv, L, scale=1.0 / math.sqrt(L))
+            lw["w_kv_up"] = M.kv_up_weight(lw["w_uk"], lw["w_uv"])
             lw["o"] = lin(H, Hq * dv, scale=out_scale)
             if cfg.is_moe_layer(li):
                 from infera_b200.models.moe import MoELayer
@@ -129,6 +134,13 @@ class MLAModel:
                                       fused=ep.fused, max_tokens=ep.max_tokens, gloo_group=ep.gloo)
         self.cos_sin = K.rope_cos_sin(cfg.max_model_len, cfg.qk_rope_dim, cfg.rope_theta, None, device=self.device)
         self.scale = M.default_scale(cfg.qk_nope_dim, cfg.qk_rope_dim)
+        import os
+
+        # the kernel takes 128 nope + 64 rope score dims and 128 value dims;
+        # the CPU restatement takes any
+        self.prefill_unabsorbed = (os.environ.get("INFERA_MLA_PREFILL", "flash") != "absorbed"
+                                   and (self.device.type == "cpu" or (cfg.qk_nope_dim == 128 and cfg.v_head_dim == 128
+                                                                      and cfg.qk_rope_dim == 64)))
 
     def _query_meta(self, fb: ForwardBatch, T: int) -> tuple[torch.Tensor, torch.Tensor, int]:
         """Per-token block-table row, visible key count and the largest one."""
@@ -166,6 +178,10 @@ class MLAModel:
         x = K.rmsnorm(h, self.w.layers[0]["ln1"], cfg.rms_eps)
         q_row, q_kvlen, max_len = self._query_meta(fb, T)
         bt = fb.p_block_table if fb.num_prefill_tokens > 0 else fb.d_block_table
+        Tp = fb.num_prefill_tokens
+        pf = self.prefill_unabsorbed and Tp > 0      # prompt rows take the non-absorbed path
+        T0 = Tp if pf else 0                          # first row that is absorbed
+        Ta = T - T0
         for li, lw in enumerate(self.w.layers):
             if "q_a" in lw:
                 qa = K.rmsnorm(K.linear(x, lw["q_a"]), lw["q_a_norm"], cfg.rms_eps)
@@ -174,20 +190,27 @@ class MLAModel:
                 qb = K.linear(x, lw["q"])
             kva = K.linear(x, lw["kv_a"])
             qb3 = qb.view(T, Hq, dn + dr)
-            q_nope_hm = qb3[:, :, :dn].transpose(0, 1).contiguous().view(Hq * T, dn)
-            q_lat = self._absorb(q_nope_hm, lw["w_uk"], T).view(Hq, T, L)
             q_full = torch.empty(T, Hq, L + dr, dtype=torch.bfloat16, device=self.device)
-            q_full[:, :, :L] = q_lat.transpose(0, 1)
+            if Ta > 0:
+                q_nope_hm = qb3[T0:, :, :dn].transpose(0, 1).contiguous().view(Hq * Ta, dn)
+                q_lat = self._absorb(q_nope_hm, lw["w_uk"], Ta).view(Hq, Ta, L)
+                q_full[T0:, :, :L] = q_lat.transpose(0, 1)
             q_full[:, :, L:] = qb3[:, :, dn:]
             cache = k_caches[li]
             M.mla_rope_kvwrite(q_full, kva, fb.positions, fb.slots, self.cos_sin, lw["kv_a_norm"], cfg.rms_eps,
                                cache)
             if fb.layer_hook is not None:
                 fb.layer_hook(li)   # this layer's latent rows are written (layer-by-layer KV push)
-            o_lat = M.mla_attention(q_full, cache, bt, q_row, q_kvlen, self.scale, max_kvlen=max_len,
-                                    rope_dim=dr)
-            o_hm = o_lat.transpose(0, 1).contiguous().view(Hq * T, L)
-            attn = self._absorb(o_hm, lw["w_uv"], T).view(Hq, T, dv).transpose(0, 1).reshape(T, Hq * dv)
+            attn = torch.empty(T, Hq * dv, dtype=torch.bfloat16, device=self.device)
+            if pf:
+                M.mla_prefill(qb[:Tp], q_full[:Tp], cache, fb.p_block_table, fb.p_bt_rows, fb.p_host_meta,
+                              fb.p_q_start, fb.p_q_len, fb.p_ctx_len, fb.p_tiles, lw["w_kv_up"], Hq, dn, dv,
+                              self.scale, out=attn[:Tp], dr=dr)
+            if Ta > 0:
+                o_lat = M.mla_attention(q_full[T0:], cache, bt, q_row[T0:], q_kvlen[T0:], self.scale,
+                                        max_kvlen=max_len, rope_dim=dr)
+                o_hm = o_lat.transpose(0, 1).contiguous().view(Hq * Ta, L)
+                attn[T0:] = self._absorb(o_hm, lw["w_uv"], Ta).view(Hq, Ta, dv).transpose(0, 1).reshape(Ta, Hq * dv)
             o = K.linear(attn, lw["o"])
             x = K.add_rmsnorm(o, h, lw["ln2"], cfg.rms_eps, out=torch.empty_like(x))
             if "moe" in lw:

@@ -125,3 +125,32 @@ def test_pd_refuses_a_mismatched_decode_cache():
     agent = PDPushAgent(pre)
     with pytest.raises(RuntimeError, match="channels"):
         agent._peer(dec.pd_rendezvous.endpoint)
+
+
+def test_mla_prefill_unabsorbed_cpu_matches_absorbed_attention():
+    """The non-absorbed prompt path (gathered latent -> per-head [k_nope | v]
+    -> 128 + rope score dims) equals the absorbed latent attention followed
+    by the W_UV projection, with prior context and permuted pages."""
+    g = torch.Generator().manual_seed(5)
+    hq, L, dn, dv, dr = 4, 64, 32, 32, 32
+    q_lens, ctx_lens = [5, 19], [40, 19]
+    bt = torch.tensor([[0, 0, 0], [4, 2, 7], [1, 5, 3]], dtype=torch.int32)
+    rows = torch.tensor([2, 1], dtype=torch.int32)
+    cache = torch.randn(8 * 16, L + dr, generator=g).to(torch.bfloat16)
+    w_uk = (torch.randn(hq, L, dn, generator=g) / L ** 0.5).to(torch.bfloat16)
+    w_uv = (torch.randn(hq, dv, L, generator=g) / L ** 0.5).to(torch.bfloat16)
+    Tp = sum(q_lens)
+    qb = torch.randn(Tp, hq * (dn + dr), generator=g).to(torch.bfloat16)
+    q_rope = torch.randn(Tp, hq, L + dr, generator=g).to(torch.bfloat16)
+    t = lambda v: torch.tensor(v, dtype=torch.int32)  # noqa: E731
+    out = M.mla_prefill(qb, q_rope, cache, bt, rows, (q_lens, ctx_lens), t([0, 5]), t(q_lens), t(ctx_lens),
+                        t([[0, 0], [1, 0]]), M.kv_up_weight(w_uk, w_uv), hq, dn, dv, 0.1, dr=dr)
+    # absorbed: q_lat = W_UK q_nope, attention over the latent rows, then W_UV
+    qn = qb.float().view(Tp, hq, dn + dr)[:, :, :dn]
+    q_abs = torch.cat([torch.einsum("thd,hld->thl", qn, w_uk.float()), q_rope.float()[:, :, L:]], -1)
+    row_of = torch.cat([rows[i].repeat(n) for i, n in enumerate(q_lens)])
+    kvlen = torch.cat([torch.arange(c - n, c) + 1 for n, c in zip(q_lens, ctx_lens)])
+    o_lat = M.mla_attention(q_abs.to(torch.bfloat16), cache, bt, row_of, kvlen, 0.1, rope_dim=dr)
+    ref = torch.einsum("thl,hvl->thv", o_lat.float(), w_uv.float()).reshape(Tp, hq * dv)
+    err = float((out.float() - ref).norm() / ref.norm())
+    assert err < 3e-2, err

@@ -80,3 +80,38 @@ def test_mla_engine_matches_oracle():
     ref = reference_logits_mla(eng.model, p)[-1]
     cc = torch.corrcoef(torch.stack([lg, ref]))[0, 1]
     assert cc > 0.995, float(cc)
+
+
+@pytest.mark.parametrize("hq,q_lens,ctx_lens", [(128, [300, 128], [300, 1000]), (16, [1, 257, 64], [4097, 257, 64]),
+                                                (32, [513], [2000])])
+def test_mla_prefill_unabsorbed_matches_fp32(hq, q_lens, ctx_lens):
+    """Prompt chunks through the gathered latent -> [k_nope | v] GEMM -> flash
+    attention over 128 + 64 score dims, against the CPU restatement of the
+    same math (fp32), with permuted pages, table rows and prior context."""
+    g = torch.Generator(device="cuda").manual_seed(hq + sum(q_lens))
+    B = len(q_lens)
+    pages_per = max(-(-c // 16) for c in ctx_lens)
+    n_pages = B * pages_per + 5
+    cache = (torch.randn(n_pages * 16, 576, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    perm = torch.randperm(n_pages, device="cuda", generator=g).to(torch.int32)
+    bt = torch.zeros(B + 2, pages_per, dtype=torch.int32, device="cuda")
+    rows = torch.arange(B, dtype=torch.int32, device="cuda").flip(0) + 1          # table rows 1..B, reversed
+    bt[rows.long()] = perm[: B * pages_per].view(B, pages_per)
+    Tp = sum(q_lens)
+    qb = (torch.randn(Tp, hq * 192, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    q_full = (torch.randn(Tp, hq, 576, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    w_uk = (torch.randn(hq, 512, 128, device="cuda", generator=g) / 512 ** 0.5).to(torch.bfloat16)
+    w_uv = (torch.randn(hq, 128, 512, device="cuda", generator=g) / 512 ** 0.5).to(torch.bfloat16)
+    w_up = M.kv_up_weight(w_uk, w_uv)
+    starts = [0]
+    for n in q_lens[:-1]:
+        starts.append(starts[-1] + n)
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")  # noqa: E731
+    tiles = i32(K.prefill_tiles(q_lens)).view(-1, 2)
+    args = (cache, bt, rows, (q_lens, ctx_lens), i32(starts), i32(q_lens), i32(ctx_lens), tiles)
+    out = M.mla_prefill(qb, q_full, *args, w_up, hq, 128, 128, 0.07)
+    torch.cuda.synchronize()
+    assert K.scratch().read_status() == 0
+    cpu = lambda t: t.cpu() if isinstance(t, torch.Tensor) else t  # noqa: E731
+    ref = M.mla_prefill(qb.cpu(), q_full.cpu(), *[cpu(a) for a in args], w_up.cpu(), hq, 128, 128, 0.07)
+    assert _rel(out.cpu(), ref) < 2e-2
