@@ -120,38 +120,43 @@ class EngineReplay:
                 return
             self._admit_arrivals()
             if self.eng.has_unfinished():
-                outs = self.eng.step()
-                step_idx = len(self.step_events)
-                self.step_shapes.append(getattr(self.eng, "last_step_shape", (0, 0)))
-                runner = getattr(self.eng, "runner", None)
-                self.step_host.append(getattr(runner, "last_timing", (0.0, 0.0)))
-                if self.device_timing:
-                    ev = torch.cuda.Event(enable_timing=True)
-                    ev.record()
-                    self.step_events.append((ev, self.now()))
-                else:
-                    self.step_events.append((None, self.now()))
-                for o in outs:
-                    rid = o.request_id
-                    rec = self.records.get(rid)
-                    if rec is None:
-                        continue
-                    self.token_steps[rid].extend([step_idx] * len(o.new_token_ids))
-                    self.collected[rid].extend(o.new_token_ids)
-                    if o.finished:
-                        s, prompt = self.inflight.pop(rid)
-                        rec.cached_len = o.num_cached_tokens
-                        rec.out_len = o.num_output_tokens
-                        rec.finish = step_idx  # resolved to a time later
-                        s.history = prompt + self.collected.pop(rid)
-                        s.turn += 1
-                        s.busy = False
-                        s.idle_since = self.now()
-                        self.idle.append(s)
+                self.step_once()
             else:
                 wait = (self.next_arrival or now) - now
                 if wait > 0:
                     time.sleep(min(wait, t_end - now, 0.002))
+
+    def step_once(self) -> None:
+        """One engine step and its bookkeeping (token steps, finished turns
+        returning their session to the idle pool)."""
+        outs = self.eng.step()
+        step_idx = len(self.step_events)
+        self.step_shapes.append(getattr(self.eng, "last_step_shape", (0, 0)))
+        runner = getattr(self.eng, "runner", None)
+        self.step_host.append(getattr(runner, "last_timing", (0.0, 0.0)))
+        if self.device_timing:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.step_events.append((ev, self.now()))
+        else:
+            self.step_events.append((None, self.now()))
+        for o in outs:
+            rid = o.request_id
+            rec = self.records.get(rid)
+            if rec is None:
+                continue
+            self.token_steps[rid].extend([step_idx] * len(o.new_token_ids))
+            self.collected[rid].extend(o.new_token_ids)
+            if o.finished:
+                s, prompt = self.inflight.pop(rid)
+                rec.cached_len = o.num_cached_tokens
+                rec.out_len = o.num_output_tokens
+                rec.finish = step_idx  # resolved to a time later
+                s.history = prompt + self.collected.pop(rid)
+                s.turn += 1
+                s.busy = False
+                s.idle_since = self.now()
+                self.idle.append(s)
 
     # ------------------------------------------------------------------ results
     def step_profile(self, window: tuple[float, float]) -> dict:
