@@ -149,7 +149,7 @@ PRESETS: dict[str, DenseConfig | MoEConfig] = {
                                  ffn=28672, weight_dtype="fp8"),
     "qwen3-32b": DenseConfig(name="qwen3-32b", num_layers=64, hidden=5120, num_heads=64, num_kv_heads=8, ffn=25600,
                              vocab=151936, rope_theta=1000000.0, rope_scaling=None, rms_eps=1e-6, qk_norm=True,
-                             max_model_len=65536 + 2048, eos_token_id=151645),
+                             max_model_len=65536 + 4096, eos_token_id=151645),
     "deepseek-v3": MoEConfig(),
     # GQA attention + routed experts (Qwen3-30B-A3B shape)
     "qwen3-30b-a3b": DenseConfig(name="qwen3-30b-a3b", num_layers=48, hidden=2048, num_heads=32, num_kv_heads=4,

@@ -107,3 +107,17 @@ def test_engine_tier_file_per_chunk_l3_under_reaper_budget(tmp_path, monkeypatch
     assert files and sum(p.stat().st_size for p in files) <= 6 * page_bytes
     l3 = eng.tier.store.l3
     assert l3.reaper.stats["reaped_files"] > 0 and len(files) <= len(l3.index) + 1
+
+
+def test_tier_ttft_bench_cpu(capsys):
+    """The tier-hit vs recompute TTFT bench: with the HBM pool capped below
+    three prefixes, session 0 comes back from the host tier."""
+    import json
+
+    from infera_b200.bench.tier_ttft import main
+
+    main(["--model", "tiny-dense", "--prefix", "400", "--increment", "16", "--sessions", "3", "--hbm-kv-gb",
+          "0.002", "--host-gb", "1", "--max-batched-tokens", "256", "--device", "cpu"])
+    d = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert d["tier_loads"] >= 1 and d["tier_hit_cached_tokens"] >= 384
+    assert d["hbm_hit_cached_tokens"] >= 384 and len(d["ttft_cold_s"]) == 3
