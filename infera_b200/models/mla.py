@@ -44,7 +44,10 @@ from infera_b200.ops import mla as M
 
 
 class MLAWeights:
-    def __init__(self, cfg: MoEConfig, device: torch.device, seed: int = 0, std: float = 0.02):
+    def __init__(self, cfg: MoEConfig, device: torch.device, seed: int = 0, std: float = 0.02,
+                 expert_range: tuple[int, int] | None = None):
+        """``expert_range``: routed experts built per MoE layer (an expert-
+        parallel rank's shard; None: all)."""
         self.cfg = cfg
         g = torch.Generator(device=device).manual_seed(seed)
         bf = torch.bfloat16
@@ -85,7 +88,7 @@ class MLAWeights:
 
                 lw["moe"] = MoELayer(H, cfg.moe_ffn, cfg.num_experts, cfg.top_k, cfg.n_groups, cfg.topk_groups,
                                      cfg.routed_scaling, cfg.num_shared_experts, device, seed=seed * 1000 + li,
-                                     std=std, weight_dtype=cfg.weight_dtype)
+                                     std=std, weight_dtype=cfg.weight_dtype, expert_range=expert_range)
             else:
                 lw["gate_up"] = lin(2 * cfg.dense_ffn, H)
                 lw["down"] = lin(H, cfg.dense_ffn, scale=out_scale)
@@ -123,7 +126,11 @@ class MLAModel:
         self.cfg = cfg
         self.tp = None
         self.device = torch.device(device)
-        self.w = MLAWeights(cfg, self.device, seed=seed)
+        shard = None
+        if ep is not None and ep.world > 1:
+            el = cfg.num_experts // ep.world
+            shard = (ep.rank * el, (ep.rank + 1) * el)
+        self.w = MLAWeights(cfg, self.device, seed=seed, expert_range=shard)
         self.ep = ep
         if ep is not None and ep.world > 1:
             from infera_b200.parallel.ep import EPMoE

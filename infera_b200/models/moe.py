@@ -25,30 +25,41 @@ from infera_b200.ops import kernels as K
 class MoELayer:
     def __init__(self, hidden: int, moe_ffn: int, num_experts: int, top_k: int, n_groups: int = 1,
                  topk_groups: int = 1, routed_scaling: float = 1.0, num_shared: int = 0,
-                 device: str | torch.device = "cuda", seed: int = 0, std: float = 0.02, weight_dtype: str = "bf16"):
+                 device: str | torch.device = "cuda", seed: int = 0, std: float = 0.02, weight_dtype: str = "bf16",
+                 expert_range: tuple[int, int] | None = None):
+        """``expert_range=(lo, hi)``: build only experts lo..hi-1 (an expert-
+        parallel shard; the router still scores all ``num_experts``). Each
+        expert's weights come from its own seed, so a shard holds exactly
+        the rows the full layer would."""
         self.H, self.F, self.E, self.k = hidden, moe_ffn, num_experts, top_k
         self.n_groups, self.topk_groups, self.scaling = n_groups, topk_groups, routed_scaling
+        self.lo, self.hi = expert_range if expert_range is not None else (0, num_experts)
         dev = torch.device(device)
         g = torch.Generator(device=dev).manual_seed(seed)
         bf = torch.bfloat16
 
-        def rnd(*shape, scale=std):
-            return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * scale).to(bf)
+        def rnd(*shape, scale=std, gen=g):
+            return (torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32) * scale).to(bf)
 
         self.gate = rnd(num_experts, hidden, scale=1.0 / math.sqrt(hidden))
         self.bias = torch.zeros(num_experts, dtype=torch.float32, device=dev)
-        self.w13 = rnd(num_experts, 2 * moe_ffn, hidden)          # interleaved gate / up rows
-        self.w2 = rnd(num_experts, hidden, moe_ffn, scale=std / math.sqrt(2))
+        n = self.hi - self.lo
+        self.w13 = torch.empty(n, 2 * moe_ffn, hidden, dtype=bf, device=dev)   # interleaved gate / up rows
+        self.w2 = torch.empty(n, hidden, moe_ffn, dtype=bf, device=dev)
+        for e in range(self.lo, self.hi):
+            ge = torch.Generator(device=dev).manual_seed(seed * 1_000_003 + 7 * e + 1)
+            self.w13[e - self.lo] = rnd(2 * moe_ffn, hidden, gen=ge)
+            self.w2[e - self.lo] = rnd(hidden, moe_ffn, scale=std / math.sqrt(2), gen=ge)
         self.shared = None
         if num_shared:
             self.shared = (rnd(2 * moe_ffn * num_shared, hidden), rnd(hidden, moe_ffn * num_shared))
-        # fp8: experts stacked to [E*2F, H] / [E*H, F] e4m3 with 128x128 block scales
+        # fp8: experts stacked to [n*2F, H] / [n*H, F] e4m3 with 128x128 block scales
         self.fp8 = weight_dtype == "fp8"
         if self.fp8:
             from infera_b200.ops import fp8
 
-            self.w13 = fp8.quantize_weight(self.w13.reshape(num_experts * 2 * moe_ffn, hidden))
-            self.w2 = fp8.quantize_weight(self.w2.reshape(num_experts * hidden, moe_ffn))
+            self.w13 = fp8.quantize_weight(self.w13.reshape(n * 2 * moe_ffn, hidden))
+            self.w2 = fp8.quantize_weight(self.w2.reshape(n * hidden, moe_ffn))
             if self.shared is not None:
                 self.shared = tuple(fp8.quantize_weight(t) for t in self.shared)
 

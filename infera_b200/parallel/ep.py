@@ -57,14 +57,20 @@ class EPMoE:
         # routing parameters only: the other ranks' experts are not kept
         self.n_groups, self.topk_groups, self.scaling = full.n_groups, full.topk_groups, full.scaling
         dev = torch.device(device)
-        lo, hi = rank * self.El, (rank + 1) * self.El
+        # this rank's experts, relative to the ones the given layer holds
+        # (the full layer, or already just this shard)
+        lo, hi = rank * self.El - full.lo, (rank + 1) * self.El - full.lo
+        if lo < 0 or hi > full.hi - full.lo:
+            raise ValueError(f"layer holds experts [{full.lo}, {full.hi}), rank {rank} needs "
+                             f"[{rank * self.El}, {(rank + 1) * self.El})")
         self.gate = full.gate.to(dev)
         self.bias = full.bias.to(dev)
         self.fp8 = getattr(full, "fp8", False)
+        whole = (lo, hi) == (0, full.hi - full.lo)
         if self.fp8:  # stacked e4m3 experts: rows of experts lo..hi-1
             self.F = full.F
-            self.w13 = full.w13.rows(lo * 2 * full.F, hi * 2 * full.F).to(dev)
-            self.w2 = full.w2.rows(lo * full.H, hi * full.H).to(dev)
+            self.w13 = (full.w13 if whole else full.w13.rows(lo * 2 * full.F, hi * 2 * full.F)).to(dev)
+            self.w2 = (full.w2 if whole else full.w2.rows(lo * full.H, hi * full.H)).to(dev)
         else:
             self.w13 = full.w13[lo:hi].to(dev).contiguous()
             self.w2 = full.w2[lo:hi].to(dev).contiguous()
