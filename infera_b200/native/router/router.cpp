@@ -328,26 +328,6 @@ std::vector<uint64_t> image_keys(const Value& body) {
 
 namespace {
 
-std::string content_text(const Value* c) {
-  if (!c || c->is_null()) return "";
-  if (c->is_str()) return c->s;
-  if (c->is_arr()) {
-    std::string out;
-    for (const auto& b : c->arr()) {
-      if (b.is_str()) out += b.s;
-      else if (b.is_obj()) {
-        const Value* t = b.get("type");
-        if (t && t->is_str() && (t->s == "text" || t->s == "input_text")) {
-          const Value* x = b.get("text");
-          if (x && x->is_str()) out += x->s;
-        }
-      }
-    }
-    return out;
-  }
-  return dump_json(*c);
-}
-
 class ByteTok : public Tokenizer {
  public:
   explicit ByteTok(int vocab) {
@@ -372,7 +352,7 @@ class ByteTok : public Tokenizer {
       out.push_back(static_cast<uint32_t>(start_));
       const Value* role = m.get("role");
       app((role && role->is_str() ? role->s : std::string(role ? dump_json(*role) : "user")) + "\n");
-      app(content_text(m.get("content")));
+      app(chat_content_text(m.get("content")));
       out.push_back(static_cast<uint32_t>(end_));
     }
     out.push_back(static_cast<uint32_t>(start_));
@@ -405,7 +385,7 @@ class WordLevelTok : public Tokenizer {
   }
   std::vector<uint32_t> chat(const Value& messages) const override {
     std::string text;
-    for (const auto& m : messages.arr()) text += content_text(m.get("content")) + " ";
+    for (const auto& m : messages.arr()) text += chat_content_text(m.get("content")) + " ";
     return encode(text);
   }
 };
@@ -414,13 +394,9 @@ class WordLevelTok : public Tokenizer {
 
 std::unique_ptr<Tokenizer> make_byte_tokenizer(int vocab_size) { return std::make_unique<ByteTok>(vocab_size); }
 
-std::unique_ptr<Tokenizer> load_wordlevel_tokenizer(const std::string& path, std::string* err) {
-  std::ifstream f(path);
-  if (!f) { *err = "cannot open " + path; return nullptr; }
-  std::stringstream ss;
-  ss << f.rdbuf();
-  Value v;
-  if (!parse_json(ss.str(), &v, err)) return nullptr;
+namespace {
+
+std::unique_ptr<Tokenizer> wordlevel_from(const Value& v, std::string* err) {
   const Value* model = v.get("model");
   const Value* type = model ? model->get("type") : nullptr;
   if (!type || !type->is_str() || type->s != "WordLevel") {
@@ -435,6 +411,34 @@ std::unique_ptr<Tokenizer> load_wordlevel_tokenizer(const std::string& path, std
     if (it != tok->vocab.end()) tok->unk = it->second;
   }
   return tok;
+}
+
+bool read_json_file(const std::string& path, Value* v, std::string* err) {
+  std::ifstream f(path);
+  if (!f) {
+    *err = "cannot open " + path;
+    return false;
+  }
+  std::stringstream ss;
+  ss << f.rdbuf();
+  return parse_json(ss.str(), v, err);
+}
+
+}  // namespace
+
+std::unique_ptr<Tokenizer> load_wordlevel_tokenizer(const std::string& path, std::string* err) {
+  Value v;
+  if (!read_json_file(path, &v, err)) return nullptr;
+  return wordlevel_from(v, err);
+}
+
+std::unique_ptr<Tokenizer> load_tokenizer_json(const std::string& path, std::string* err) {
+  Value v;
+  if (!read_json_file(path, &v, err)) return nullptr;
+  const Value* model = v.get("model");
+  const Value* type = model ? model->get("type") : nullptr;
+  if (type && type->is_str() && type->s == "BPE") return load_bpe_tokenizer(v, err);
+  return wordlevel_from(v, err);
 }
 
 bool request_token_ids(const Value& body, const Tokenizer* tok, std::vector<uint32_t>* out) {
@@ -453,17 +457,14 @@ bool request_token_ids(const Value& body, const Tokenizer* tok, std::vector<uint
         return true;
       }
       if (!tok) return false;
-      *out = tok->encode(a[0].is_str() ? a[0].s : dump_json(a[0]));
-      return true;
+      return tok->try_encode(a[0].is_str() ? a[0].s : dump_json(a[0]), out);
     }
     if (!tok) return false;
-    *out = tok->encode(prompt->is_str() ? prompt->s : dump_json(*prompt));
-    return true;
+    return tok->try_encode(prompt->is_str() ? prompt->s : dump_json(*prompt), out);
   }
   if (!tok) return false;
   const Value* msgs = body.get("messages");
-  *out = tok->chat(msgs ? *msgs : Value::array());
-  return true;
+  return tok->try_chat(msgs ? *msgs : Value::array(), out);
 }
 
 // ---------------------------------------------------------------------------

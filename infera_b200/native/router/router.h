@@ -97,12 +97,28 @@ class Tokenizer {
   virtual ~Tokenizer() = default;
   virtual std::vector<uint32_t> encode(const std::string& text) const = 0;
   virtual std::vector<uint32_t> chat(const Value& messages) const = 0;
+  // false: this text's ids cannot be known exactly (route without locality)
+  virtual bool try_encode(const std::string& text, std::vector<uint32_t>* out) const {
+    *out = encode(text);
+    return true;
+  }
+  virtual bool try_chat(const Value& messages, std::vector<uint32_t>* out) const {
+    *out = chat(messages);
+    return true;
+  }
 };
 // UTF-8 bytes at [base, base + 256); base 1000 for vocabularies >= 2048
 std::unique_ptr<Tokenizer> make_byte_tokenizer(int vocab_size);
 // HF tokenizer.json with a WordLevel model and whitespace pre-tokenization;
 // nullptr if the file is another kind
 std::unique_ptr<Tokenizer> load_wordlevel_tokenizer(const std::string& path, std::string* err);
+// HF tokenizer.json with a byte-level BPE model (GPT-2 / Llama-3 / Qwen2
+// families; bpe.cpp lists what is supported); nullptr + err otherwise
+std::unique_ptr<Tokenizer> load_bpe_tokenizer(const Value& tokenizer_json, std::string* err);
+// WordLevel or byte-level BPE, by the file's model type
+std::unique_ptr<Tokenizer> load_tokenizer_json(const std::string& path, std::string* err);
+// text of an OpenAI message content: a string, or its text blocks joined
+std::string chat_content_text(const Value* content);
 // token ids of a completions / chat body; false if they cannot be known
 bool request_token_ids(const Value& body, const Tokenizer* tok, std::vector<uint32_t>* out);
 

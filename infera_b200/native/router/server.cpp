@@ -143,7 +143,7 @@ class App {
     if (!cfg.tokenizer_path.empty() && cfg.tokenizer_path.size() > 5 &&
         cfg.tokenizer_path.compare(cfg.tokenizer_path.size() - 5, 5, ".json") == 0) {
       std::string err;
-      tok = load_wordlevel_tokenizer(cfg.tokenizer_path, &err);
+      tok = load_tokenizer_json(cfg.tokenizer_path, &err);
       if (!tok) std::fprintf(stderr, "[ib200_router] tokenizer %s: %s; text prompts route without locality\n",
                              cfg.tokenizer_path.c_str(), err.c_str());
     } else {
@@ -1037,6 +1037,34 @@ int main(int argc, char** argv) {
     unsigned long long x;
     while (std::scanf("%llu", &x) == 1) ids.push_back(static_cast<uint32_t>(x));
     for (uint64_t h : chain_hashes(ids, std::atoi(argv[2]))) std::printf("%llu\n", static_cast<unsigned long long>(h));
+    return 0;
+  }
+  if (argc == 3 && std::strcmp(argv[1], "--tokenize") == 0) {
+    // self-check: one JSON value per stdin line (a string: encode it; an
+    // array: chat messages) -> a JSON array of ids, or null if refused
+    std::string err;
+    auto tk = load_tokenizer_json(argv[2], &err);
+    if (!tk) {
+      std::fprintf(stderr, "tokenizer: %s\n", err.c_str());
+      return 2;
+    }
+    std::string line;
+    char buf[1 << 16];
+    while (std::fgets(buf, sizeof buf, stdin)) {
+      line += buf;
+      if (line.empty() || line.back() != '\n') continue;
+      Value v;
+      std::vector<uint32_t> ids;
+      bool ok = parse_json(line, &v, &err) &&
+                (v.is_str() ? tk->try_encode(v.s, &ids) : (v.is_arr() && tk->try_chat(v, &ids)));
+      std::string out = ok ? "[" : "null";
+      if (ok) {
+        for (size_t i = 0; i < ids.size(); ++i) out += (i ? "," : "") + std::to_string(ids[i]);
+        out += "]";
+      }
+      std::printf("%s\n", out.c_str());
+      line.clear();
+    }
     return 0;
   }
   Config cfg;

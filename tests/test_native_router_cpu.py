@@ -285,3 +285,64 @@ def test_native_router_bus_transport_over_nats(binary, tmp_path):
         loop.call_soon_threadsafe(loop.stop)
     assert [s[0] for s in seen] == ["/v1/completions"] * 4
     assert seen[0][1]["max_tokens"] == 3 and seen[0][1]["stream"] is True
+
+
+def _train_bpe(path, family: str):
+    """A small byte-level BPE tokenizer.json of the given family, trained
+    with the `tokenizers` library on a multilingual random corpus."""
+    import random
+
+    from tokenizers import Regex, Tokenizer, models, normalizers, pre_tokenizers, trainers
+
+    split = (r"(?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}{1,3}| ?[^\s\p{L}\p{N}]+[\r\n]*"
+             r"|\s*[\r\n]+|\s+(?!\S)|\s+")
+    rng = random.Random(0)
+    words = ["hello", "world", "don't", "I'm", "THEY'RE", "naïve", "café", "日本語", "한국어", "Привет", "αβγ", "123456",
+             "3.14", "x=y+1;", "<tag>", "  ", "\t", "\n\n", "foo_bar", "!!!", "—", "😀", "٣٤٥"]
+    corpus = [" ".join(rng.choice(words) for _ in range(30)) for _ in range(1500)]
+    if family == "gpt2":
+        t = Tokenizer(models.BPE())
+        t.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=True, use_regex=True)
+    else:
+        t = Tokenizer(models.BPE(ignore_merges=family == "llama3"))
+        if family == "qwen2":
+            split = split.replace(r"\p{N}{1,3}", r"\p{N}")
+            t.normalizer = normalizers.NFC()
+        t.pre_tokenizer = pre_tokenizers.Sequence([pre_tokenizers.Split(Regex(split), "isolated"),
+                                                   pre_tokenizers.ByteLevel(add_prefix_space=False, use_regex=False)])
+    t.train_from_iterator(corpus, trainers.BpeTrainer(vocab_size=1200, initial_alphabet=pre_tokenizers.ByteLevel.alphabet(),
+                                                      special_tokens=["<|begin_of_text|>", "<|user|>"]))
+    t.save(str(path))
+    return t
+
+
+@pytest.mark.parametrize("family", ["llama3", "qwen2", "gpt2"])
+def test_bpe_tokenizer_matches_tokenizers_library(binary, tmp_path, family):
+    """The router's byte-level BPE (split pattern scanned by hand, merges,
+    added tokens, NFC refusal) gives the same ids as the `tokenizers`
+    library with add_special_tokens=False, the engine's encoding."""
+    import random
+
+    path = tmp_path / f"{family}.json"
+    tok = _train_bpe(path, family)
+    rng = random.Random(1)
+    pieces = ["hello", "World", "don't", "I'M", "we'LL", "'S", "naïve", "café", "über", "日本語", "中文", "Привет",
+              "1", "12", "1234567", "3.14159", "x=y+1;", " ", "  ", "\t", "\n", "\n\n", " \n ", "\r\n", "é", "!!!",
+              "...", "😀", "٣٤٥", "<|begin_of_text|>", "<|user|>", " ", "　", "Ⅻ", "½", "'", "'x"]
+    texts = ["".join(rng.choice(pieces) + rng.choice(["", " "]) for _ in range(rng.randint(1, 10)))
+             for _ in range(600)] + ["", " ", "  a", "a  ", "'s'S'Re", "   \n\n  x", "x\n  \ny"]
+    r = subprocess.run([binary, "--tokenize", str(path)], input=("\n".join(json.dumps(t) for t in texts) + "\n").encode(),
+                       capture_output=True, timeout=120, env=dict(os.environ, **_SAN_ENV))
+    assert r.returncode == 0, r.stderr.decode()[-2000:]
+    assert not [m for m in _SAN_MARKS if m in r.stderr.decode(errors="replace")], r.stderr.decode()[-4000:]
+    outs = r.stdout.decode().splitlines()
+    assert len(outs) == len(texts)
+    refused = 0
+    for t, o in zip(texts, outs):
+        got = json.loads(o)
+        if got is None:
+            refused += 1
+            assert family == "qwen2" and "́" in t        # only texts NFC would change are refused
+            continue
+        assert got == tok.encode(t, add_special_tokens=False).ids, repr(t)
+    assert refused < len(texts) // 2
