@@ -10,7 +10,8 @@ Cases: gemm_prefill (2048x6144x4096 bf16), gemm_decode (64 tokens x
 tail each), fp8_decode (64 x 28672 x 8192 e4m3,
 block scales, SwiGLU), fp8_prefill (4096 x 8192 x 8192 e4m3), mla_decode (64
 queries x 128 heads over 4096 latent keys each), prefill_attn (2048 queries over 2048 keys,
-causal), prefill_attn_prefix (1024 queries over 8192 keys), mla_prefill /
+causal), prefill_attn_prefix (1024 queries over 8192 keys), prefill_attn_chunk
+(a 224-token chunk over 8192 cached keys: key shares), mla_prefill /
 mla_prefill_prefix (DeepSeek-V3 MLA prompt chunk, 128 heads: 2048 queries
 over 2048 keys causal, or 1024 over 8192; the non-absorbed path against the
 absorbed latent kernel on the same queries). Prints one JSON
@@ -141,8 +142,9 @@ def run_case(case: str, iters: int) -> dict:
         return {"case": case, "ms": ms, "gbs_all_keys": by_all / ms / 1e6, "gbs_unique_pages": by_unique / ms / 1e6,
                 "bytes_all": by_all, "bytes_unique": by_unique, "splits": sp, "tiles_per_split": tps,
                 "l2_policy": l2, "rel_err": float((got - ref).norm() / ref.norm())}
-    if case in ("prefill_attn", "prefill_attn_prefix"):
-        ql, ctx = (2048, 2048) if case == "prefill_attn" else (1024, 8192)
+    if case in ("prefill_attn", "prefill_attn_prefix", "prefill_attn_chunk"):
+        ql, ctx = {"prefill_attn": (2048, 2048), "prefill_attn_prefix": (1024, 8192),
+                   "prefill_attn_chunk": (224, 8192)}[case]
         pages = ctx // 16
         kc = torch.randn(pages * 16, hkv * D, device=dev, generator=g).to(bf)
         vc = torch.randn(pages * 16, hkv * D, device=dev, generator=g).to(bf)
@@ -150,9 +152,16 @@ def run_case(case: str, iters: int) -> dict:
         q = torch.randn(ql, hq * D, device=dev, generator=g).to(bf)
         tiles = torch.tensor(K.prefill_tiles([ql]), dtype=torch.int32, device=dev)
         meta = [torch.tensor([v], dtype=torch.int32, device=dev) for v in (0, ql, ctx)]
-        ms = _time(lambda: K.attn_prefill(q, kc, vc, bt, *meta, tiles, hq, hkv, 1 / math.sqrt(D)), iters)
+        splits = K.prefill_kv_splits(hq, tiles.shape[0], ctx)
+        ms = _time(lambda: K.attn_prefill(q, kc, vc, bt, *meta, tiles, hq, hkv, 1 / math.sqrt(D),
+                                          kv_splits=splits), iters)
         keys = sum(ctx - ql + i + 1 for i in range(ql))
-        return {"case": case, "ms": ms, "tflops": 4 * keys * D * hq / ms / 1e9}
+        res = {"case": case, "ms": ms, "tflops": 4 * keys * D * hq / ms / 1e9, "kv_splits": splits}
+        if splits > 1:
+            ms1 = _time(lambda: K.attn_prefill(q, kc, vc, bt, *meta, tiles, hq, hkv, 1 / math.sqrt(D),
+                                               kv_splits=1), iters)
+            res.update(ms_unsplit=ms1, speedup_vs_unsplit=ms1 / ms)
+        return res
     if case in ("mla_prefill", "mla_prefill_prefix"):
         from infera_b200.ops import mla as M
 

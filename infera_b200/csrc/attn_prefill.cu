@@ -68,6 +68,9 @@ struct Params {
   int ldo;
   int* status;
   long long* trace;        // optional: clock64 stamps of CTA (0,0)'s pipeline events (FTR_*)
+  int kv_splits;           // > 1: blockIdx.z takes one contiguous share of the key tiles
+  float* o_part;           // kv_splits > 1: [T][num_heads][kv_splits][128] O / l of each share
+  float* lse_part;         // kv_splits > 1: [T][num_heads][kv_splits] m + log2(l) (scaled log2 units)
 };
 
 // pipeline event stamps (trace[event * kFTraceTiles + tile]) for diagnosis
@@ -131,6 +134,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int pos0 = ctx - qlen + qb * BQ;           // position of row 0
   const int last_pos = pos0 + valid_rows - 1;
   const int n_kv = (last_pos + 1 + BKV - 1) / BKV;
+  // this CTA's share of the key tiles: [j_lo, j_lo + nk)
+  const int S = p.kv_splits > 1 ? p.kv_splits : 1;
+  const int z = S > 1 ? blockIdx.z : 0;
+  const int chunk = (n_kv + S - 1) / S;
+  const int j_lo = z * chunk;
+  const int nk = min(n_kv - j_lo, chunk);
+  if (nk <= 0) {  // nothing in this share: mark it empty for the combine
+    for (int r = threadIdx.x; r < valid_rows; r += blockDim.x)
+      p.lse_part[(static_cast<size_t>(row0 + r) * p.num_heads + h) * S + z] = -INFINITY;
+    return;
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -178,14 +192,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int n_pages = (ctx + PAGE - 1) / PAGE;
       long long issued = 0;
       int nxt[8];
-      load_tile_pages(bt, 0, n_pages, nxt);
-      for (int j = 0; j < n_kv; ++j) {
+      load_tile_pages(bt, j_lo, n_pages, nxt);
+      for (int j = 0; j < nk; ++j) {
         const int st = j % KV_STAGES;
         const uint32_t ph = (j / KV_STAGES) & 1;
         int cur[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
-        if (j + 1 < n_kv) load_tile_pages(bt, j + 1, n_pages, nxt);  // in flight while we wait
+        if (j + 1 < nk) load_tile_pages(bt, j_lo + j + 1, n_pages, nxt);  // in flight while we wait
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
         uint8_t* base = sKV + st * STB * BLK;
         fstamp(p, FTR_TMA, j);
@@ -247,7 +261,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         umma_commit(&kv_empty[st]);
         return true;
       };
-      for (int j = 0; j < n_kv && ok; ++j) {
+      for (int j = 0; j < nk && ok; ++j) {
         const int st = j % KV_STAGES;
         if (!mbar_wait(&k_full[st], static_cast<uint32_t>((j / KV_STAGES) & 1), abort_flag, p.status,
                        kStatusTimeoutFull)) {
@@ -272,7 +286,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
       }
-      if (ok && n_kv > 0) issue_pv(n_kv - 1);
+      if (ok && nk > 0) issue_pv(nk - 1);
       umma_commit(drain);
       mbar_wait(drain, 0, nullptr, p.status, kStatusTimeoutFull);
     }
@@ -296,7 +310,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ++pph;
     };
     const bool tr0 = half == 0 && r == 0;  // one softmax thread stamps
-    for (int j = 0; j < n_kv && ok; ++j) {
+    for (int j = 0; j < nk && ok; ++j) {
       if (!mbar_wait_warp(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status,
                           kStatusTimeoutTmemFull)) {
         ok = false;
@@ -305,7 +319,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (tr0) fstamp(p, FTR_SFULL, j);
       tc_fence_after();
       const uint32_t s_addr = lane_addr + ((j & 1) ? S_COL1 : S_COL0) + cb;
-      const int kbase = j * BKV;
+      const int kbase = (j_lo + j) * BKV;
       const int lim = pos - kbase - cb;  // local key c visible iff c <= lim
       // every row of the CTA sees the whole tile when it ends at or before the
       // position of row 0 (CTA-uniform): no per-element mask needed
@@ -338,7 +352,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // rows needs it, with factor 1.0 for the others.
       const bool rescale = (j == 0) || (m_new > m_run + 8.0f);
       const float m_use = rescale ? m_new : m_run;
-      const float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
+      // a row whose keys in this share are all masked so far keeps m = -inf
+      // (only possible in a later share of a split row): no rescale, and
+      // the exponentials below use 0 as reference so they give exact zeros
+      const float alpha = (j == 0 || m_run == -INFINITY) ? 0.f : exp2f(m_run - m_use);
+      const float m_ref = m_use == -INFINITY ? 0.f : m_use;
       const bool warp_rescale = __any_sync(0xffffffffu, rescale && j > 0);
       // O must not be rescaled while the previous tile's PV accumulates into
       // it: only a rescale waits for PV(j-1). P(j) goes to S(j)'s own
@@ -370,8 +388,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float sl = p.scale_log2;
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
-        const float e0 = exp2f(fmaf(__uint_as_float(v[i]), sl, -m_use));
-        const float e1 = exp2_fma(fmaf(__uint_as_float(v[i + 1]), sl, -m_use));
+        const float e0 = exp2f(fmaf(__uint_as_float(v[i]), sl, -m_ref));
+        const float e1 = exp2_fma(fmaf(__uint_as_float(v[i + 1]), sl, -m_ref));
         __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
         sum += __low2float(bb) + __high2float(bb);
         v[i / 2] = *reinterpret_cast<uint32_t*>(&bb);   // packed pairs reuse the low half of v
@@ -391,28 +409,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // row sums: add the two halves' shares
     lsum[half * BQ + r] = l_run;
     pair_sync();
-    if (ok && n_kv > 0) {
-      if (mbar_wait_warp(o_done, static_cast<uint32_t>((n_kv - 1) & 1), abort_flag, p.status,
+    if (ok && nk > 0) {
+      if (mbar_wait_warp(o_done, static_cast<uint32_t>((nk - 1) & 1), abort_flag, p.status,
                          kStatusTimeoutTmemFull)) {
         tc_fence_after();
         const float l = lsum[r] + lsum[BQ + r];
         const float inv = l > 0.f ? 1.0f / l : 0.f;
         const bool write = r < valid_rows;
-        __nv_bfloat16* orow = p.out + static_cast<size_t>(row0 + r) * p.ldo + h * D + cb;
+        if (S > 1) {
+          // this share's O / l and m + log2(l), merged by the combine kernel
+          const size_t base = (static_cast<size_t>(row0 + r) * p.num_heads + h) * S + z;
+          if (write && half == 0) p.lse_part[base] = l > 0.f ? m_run + __log2f(l) : -INFINITY;
+          float* orow = p.o_part + base * D + cb;
 #pragma unroll 1
-        for (int c0 = 0; c0 < 64; c0 += 32) {
-          uint32_t o[32];
-          tmem_ld32(lane_addr + O_COL + cb + c0, o);
-          tmem_ld_wait();
-          if (write) {
+          for (int c0 = 0; c0 < 64; c0 += 32) {
+            uint32_t o[32];
+            tmem_ld32(lane_addr + O_COL + cb + c0, o);
+            tmem_ld_wait();
+            if (write) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 w;
-              w.x = pack_bf16(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
-              w.y = pack_bf16(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
-              w.z = pack_bf16(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
-              w.w = pack_bf16(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
-              *reinterpret_cast<uint4*>(orow + c0 + i) = w;
+              for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(orow + c0 + i) =
+                    make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                                __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+            }
+          }
+        } else {
+          __nv_bfloat16* orow = p.out + static_cast<size_t>(row0 + r) * p.ldo + h * D + cb;
+#pragma unroll 1
+          for (int c0 = 0; c0 < 64; c0 += 32) {
+            uint32_t o[32];
+            tmem_ld32(lane_addr + O_COL + cb + c0, o);
+            tmem_ld_wait();
+            if (write) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 8) {
+                uint4 w;
+                w.x = pack_bf16(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
+                w.y = pack_bf16(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+                w.z = pack_bf16(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+                w.w = pack_bf16(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+                *reinterpret_cast<uint4*>(orow + c0 + i) = w;
+              }
             }
           }
         }
@@ -427,6 +465,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
     tmem_dealloc(tmem, 512);
   }
+}
+
+// Merge the key shares of split rows: out = sum_s 2^(lse_s - max) O_s / sum_s 2^(lse_s - max).
+__global__ void fa_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ lse_part, int S,
+                                  int H, __nv_bfloat16* __restrict__ out, int ldo) {
+  const int row = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const size_t base = (static_cast<size_t>(row) * H + h) * S;
+  float mx = -INFINITY;
+  for (int s = 0; s < S; ++s) mx = fmaxf(mx, lse_part[base + s]);
+  float num = 0.f, den = 0.f;
+  if (mx != -INFINITY) {
+    for (int s = 0; s < S; ++s) {
+      const float lse = lse_part[base + s];
+      if (lse == -INFINITY) continue;
+      const float w = exp2f(lse - mx);
+      den += w;
+      num += o_part[(base + s) * D + d] * w;
+    }
+  }
+  out[static_cast<size_t>(row) * ldo + h * D + d] = __float2bfloat16(den > 0.f ? num / den : 0.f);
 }
 
 }  // namespace fa
@@ -463,10 +521,13 @@ template <bool EXT>
 int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const FaOperand* qe, const FaOperand* ke,
               const int* tiles, int num_tiles, const int* q_start, const int* q_len, const int* ctx_len,
               const int* block_table, const int* bt_rows, int max_pages, int num_heads, int num_kv_heads,
-              float scale, void* out, int ldo, int* status, cudaStream_t stream) {
+              float scale, void* out, int ldo, int* status, int kv_splits, float* o_part, float* lse_part,
+              cudaStream_t stream) {
   using namespace ib200::fa;
   if (num_tiles <= 0 || q.rows <= 0) return 0;
   if ((ldo % 8) != 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return -1;
+  if (kv_splits > 1 && (o_part == nullptr || lse_part == nullptr || (reinterpret_cast<uintptr_t>(o_part) & 15)))
+    return -1;
   CUtensorMap tq, tk, tv, tqe, tke;
   if (!fa_tmap(&tq, q, 128) || !fa_tmap(&tk, k, 16) || !fa_tmap(&tv, v, 16)) return -2;
   if (EXT) {
@@ -495,6 +556,9 @@ int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const 
   p.ldo = ldo;
   p.status = status;
   p.trace = g_fa_trace;
+  p.kv_splits = kv_splits > 1 ? kv_splits : 1;
+  p.o_part = o_part;
+  p.lse_part = lse_part;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -502,8 +566,11 @@ int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const 
     cudaFuncSetAttribute(fa_prefill_kernel<EXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(EXT));
     attr_set[dev] = true;
   }
-  dim3 grid(num_heads, num_tiles);
+  dim3 grid(num_heads, num_tiles, p.kv_splits);
   fa_prefill_kernel<EXT><<<grid, NUM_THREADS, smem_bytes(EXT), stream>>>(tq, tk, tv, tqe, tke, p);
+  if (p.kv_splits > 1)
+    fa_combine_kernel<<<dim3(static_cast<unsigned>(q.rows), num_heads), D, 0, stream>>>(
+        o_part, lse_part, p.kv_splits, num_heads, static_cast<__nv_bfloat16*>(out), ldo);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
@@ -513,12 +580,15 @@ int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const 
 // q: [T, ldq] bf16 with head h at columns [h*128, h*128+128).
 // k_cache / v_cache: [num_slots, num_kv_heads*128] bf16.
 // tiles: device int32 [num_tiles, 2] (seq, q_block), longest first.
+// kv_splits > 1: each tile's key tiles are shared out over that many CTAs
+// whose partials (o_part fp32 [T*num_heads*kv_splits*128], lse_part
+// [T*num_heads*kv_splits]) a combine kernel merges into out.
 extern "C" int ib_attn_prefill(const void* q, int T, int ldq, const void* k_cache, const void* v_cache,
                                long long num_slots, const int* tiles, int num_tiles, const int* q_start,
                                const int* q_len, const int* ctx_len, const int* block_table, const int* bt_rows,
                                int max_pages,
                                int num_heads, int num_kv_heads, float scale, void* out, int ldo, int* status,
-                               cudaStream_t stream) {
+                               int kv_splits, float* o_part, float* lse_part, cudaStream_t stream) {
   using namespace ib200::fa;
   if (T <= 0) return 0;
   const int kvw = num_kv_heads * D;
@@ -526,7 +596,8 @@ extern "C" int ib_attn_prefill(const void* q, int T, int ldq, const void* k_cach
   const FaOperand fk{k_cache, num_slots, kvw, D, D, num_kv_heads};
   const FaOperand fv{v_cache, num_slots, kvw, D, D, num_kv_heads};
   return fa_launch<false>(fq, fk, fv, nullptr, nullptr, tiles, num_tiles, q_start, q_len, ctx_len, block_table,
-                          bt_rows, max_pages, num_heads, num_kv_heads, scale, out, ldo, status, stream);
+                          bt_rows, max_pages, num_heads, num_kv_heads, scale, out, ldo, status, kv_splits, o_part,
+                          lse_part, stream);
 }
 
 // Attention over 128 + 64 score dims (MLA prefill, not absorbed):
@@ -543,7 +614,7 @@ extern "C" int ib_attn_prefill_ext(const void* q, int T, int ldq, int q_hs, cons
                                    int num_tiles, const int* q_start, const int* q_len, const int* ctx_len,
                                    const int* block_table, const int* bt_rows, int max_pages, int num_heads,
                                    int num_kv_heads, float scale, void* out, int ldo, int* status,
-                                   cudaStream_t stream) {
+                                   int kv_splits, float* o_part, float* lse_part, cudaStream_t stream) {
   using namespace ib200::fa;
   if (T <= 0) return 0;
   const FaOperand fq{q, T, ldq, q_hs, D, num_heads};
@@ -552,5 +623,6 @@ extern "C" int ib_attn_prefill_ext(const void* q, int T, int ldq, int q_hs, cons
   const FaOperand fke{ke, num_rows, ldke, ke_hs, 64, ke_hs == 0 ? 1 : num_kv_heads};
   const FaOperand fv{v, num_rows, ldv, v_hs, D, num_kv_heads};
   return fa_launch<true>(fq, fk, fv, &fqe, &fke, tiles, num_tiles, q_start, q_len, ctx_len, block_table, bt_rows,
-                         max_pages, num_heads, num_kv_heads, scale, out, ldo, status, stream);
+                         max_pages, num_heads, num_kv_heads, scale, out, ldo, status, kv_splits, o_part, lse_part,
+                         stream);
 }

@@ -45,10 +45,10 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_attn_decode": [c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float,
                            c_vp, c_vp, c_vp, c_int, c_vp],
         "ib_attn_prefill": [c_vp, c_int, c_int, c_vp, c_vp, c_ll, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int,
-                            c_int, c_int, c_float, c_vp, c_int, c_vp, c_vp],
+                            c_int, c_int, c_float, c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp],
         "ib_attn_prefill_ext": [c_vp, c_int, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int,
                                 c_int, c_vp, c_int, c_int, c_ll, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int,
-                                c_int, c_int, c_float, c_vp, c_int, c_vp, c_vp],
+                                c_int, c_int, c_float, c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp],
         "ib_scatter_i32": [c_vp, c_vp, c_vp, c_int, c_vp],
         "ib_kv_page_copy": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_ll, c_int, c_int, c_int, c_int, c_vp],
         "ib_attn_decode_tc": [c_vp, c_int, c_vp, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,

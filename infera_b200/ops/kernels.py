@@ -29,6 +29,8 @@ class DeviceScratch:
     gemm_ws: torch.Tensor = field(default_factory=lambda: torch.empty(0))
     dec_o: torch.Tensor = field(default_factory=lambda: torch.empty(0))
     dec_lse: torch.Tensor = field(default_factory=lambda: torch.empty(0))
+    pf_o: torch.Tensor = field(default_factory=lambda: torch.empty(0))
+    pf_lse: torch.Tensor = field(default_factory=lambda: torch.empty(0))
 
     # Growth is refused while a CUDA graph is being captured (a captured
     # kernel must keep pointing at live memory); engines size the scratch
@@ -48,6 +50,14 @@ class DeviceScratch:
             self.dec_lse = torch.empty(max(lse_numel, self.dec_lse.numel()), dtype=torch.float32,
                                        device=self.device)
         return self.dec_o, self.dec_lse
+
+    def ensure_prefill(self, o_numel: int, lse_numel: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Partials of key-split prefill attention (prefill runs eagerly, never
+        inside a captured graph, so this may grow at any time)."""
+        if self.pf_o.numel() < o_numel or self.pf_lse.numel() < lse_numel:
+            self.pf_o = torch.empty(max(o_numel, self.pf_o.numel()), dtype=torch.float32, device=self.device)
+            self.pf_lse = torch.empty(max(lse_numel, self.pf_lse.numel()), dtype=torch.float32, device=self.device)
+        return self.pf_o, self.pf_lse
 
     def read_status(self) -> int:
         return int(self.status.item())
@@ -460,14 +470,27 @@ def prefill_tiles(q_lens: list[int]) -> list[tuple[int, int]]:
     return items
 
 
+def prefill_kv_splits(num_heads: int, num_tiles: int, max_ctx: int, num_sms: int = 148) -> int:
+    """Key shares per (head, query tile) CTA: when the CTAs do not cover the
+    SMs twice (a short chunk over a long cached context), split each tile's
+    keys so they do, keeping at least 8 key tiles of 128 per share."""
+    ctas = num_heads * num_tiles
+    kv_tiles = -(-max_ctx // 128)
+    if ctas >= 2 * num_sms or kv_tiles < 16:
+        return 1
+    return max(1, min(-(-2 * num_sms // ctas), kv_tiles // 8, 16))
+
+
 def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
                  q_start: torch.Tensor, q_len: torch.Tensor, ctx_len: torch.Tensor, tiles: torch.Tensor, hq: int,
                  hkv: int, scale: float, out: torch.Tensor | None = None,
                  host_meta: tuple[list[int], list[int]] | None = None,
-                 bt_rows: torch.Tensor | None = None) -> torch.Tensor:
+                 bt_rows: torch.Tensor | None = None, kv_splits: int | None = None) -> torch.Tensor:
     """Causal attention for chunks of new tokens whose K/V already sit in the
     paged cache. q: [T, >=hq*D]; q_start/q_len/ctx_len: int32 [num_seqs];
-    tiles: int32 [num_tiles, 2] from :func:`prefill_tiles`."""
+    tiles: int32 [num_tiles, 2] from :func:`prefill_tiles`. ``kv_splits``:
+    key shares per tile (None: :func:`prefill_kv_splits` from ``host_meta``,
+    1 without it)."""
     T = q.shape[0]
     D = k_cache.shape[1] // hkv
     if not q.is_cuda:
@@ -485,14 +508,20 @@ def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
     if out is None:
         out = torch.empty(T, hq * D, dtype=q.dtype, device=q.device)
     sc = scratch(q.device)
+    if kv_splits is None:
+        kv_splits = prefill_kv_splits(hq, tiles.shape[0], max(host_meta[1]), _num_sms()) if host_meta else 1
+    o_ptr = lse_ptr = None
+    if kv_splits > 1:
+        o, lse = sc.ensure_prefill(T * hq * kv_splits * D, T * hq * kv_splits)
+        o_ptr, lse_ptr = o.data_ptr(), lse.data_ptr()
     rc = _native.kernels().ib_attn_prefill(q.data_ptr(), T, q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
                                            k_cache.shape[0], tiles.data_ptr(), tiles.shape[0], q_start.data_ptr(),
                                            q_len.data_ptr(), ctx_len.data_ptr(), block_table.data_ptr(),
                                            _ptr(bt_rows), block_table.stride(0), hq, hkv, scale, out.data_ptr(),
-                                           out.stride(0),
-                                           sc.status.data_ptr(), _stream())
+                                           out.stride(0), sc.status.data_ptr(), kv_splits, o_ptr, lse_ptr,
+                                           _stream())
     _native.check(rc, "ib_attn_prefill")
-    _count()
+    _count(2 if kv_splits > 1 else 1)
     return out
 
 

@@ -196,6 +196,11 @@ def mla_prefill(qb: torch.Tensor, q_rope: torch.Tensor, cache: torch.Tensor, blo
         out = torch.empty(Tp, hq * dv, dtype=torch.bfloat16, device=qb.device)
     qe = q_rope[..., -DR:]
     sc_ = K.scratch(qb.device)
+    splits = K.prefill_kv_splits(hq, tiles.shape[0], max(ctxs), K._num_sms())
+    o_ptr = lse_ptr = None
+    if splits > 1:
+        o_p, lse_p = sc_.ensure_prefill(Tp * hq * splits * 128, Tp * hq * splits)
+        o_ptr, lse_ptr = o_p.data_ptr(), lse_p.data_ptr()
     rc = _native.kernels().ib_attn_prefill_ext(
         qb.data_ptr(), Tp, qb.stride(0), qb.shape[1] // hq,
         qe.data_ptr(), qe.stride(0), qe.stride(1),
@@ -204,9 +209,9 @@ def mla_prefill(qb: torch.Tensor, q_rope: torch.Tensor, cache: torch.Tensor, blo
         kv_up[:, dn:].data_ptr(), kv_up.stride(0), w,
         P * PAGE, tiles.data_ptr(), tiles.shape[0], q_start.data_ptr(), q_len.data_ptr(), ctx_len.data_ptr(),
         bt_c.data_ptr(), None, bt_c.shape[1], hq, hq, scale, out.data_ptr(), out.stride(0),
-        sc_.status.data_ptr(), K._stream())
+        sc_.status.data_ptr(), splits, o_ptr, lse_ptr, K._stream())
     _native.check(rc, "ib_attn_prefill_ext")
-    K._count(1)
+    K._count(2 if splits > 1 else 1)
     return out
 
 

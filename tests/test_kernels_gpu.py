@@ -173,6 +173,32 @@ def test_attn_prefill(q_lens, ctx_lens):
     assert _rel_err(out.cpu(), ref) < 2e-2
 
 
+@pytest.mark.parametrize("q_lens,ctx_lens,splits", [
+    ([200], [8192], 4), ([1, 77, 300], [3000, 77, 2600], 3), ([256, 128], [6000, 6000], 16), ([130], [130], 2),
+])
+def test_attn_prefill_key_split(q_lens, ctx_lens, splits):
+    """Key shares of each query tile over several CTAs, merged by the
+    combine kernel: later shares hold rows whose keys are all masked (the
+    chunk's first rows see only the early keys) and shares past a short
+    sequence's keys are empty."""
+    hq, hkv, D = 32, 8, 128
+    kc, vc, bt = _paged_setup(ctx_lens, hkv, D, seed=9)
+    T = sum(q_lens)
+    q = torch.randn(T, (hq + 2 * hkv) * D).to(torch.bfloat16)
+    q_start = torch.tensor([sum(q_lens[:i]) for i in range(len(q_lens))], dtype=torch.int32)
+    ql = torch.tensor(q_lens, dtype=torch.int32)
+    cl = torch.tensor(ctx_lens, dtype=torch.int32)
+    tiles = torch.tensor(K.prefill_tiles(q_lens), dtype=torch.int32).view(-1, 2)
+    scale = 1 / math.sqrt(D)
+    ref = K.attn_prefill(q, kc, vc, bt, q_start, ql, cl, tiles, hq, hkv, scale)
+    out = K.attn_prefill(q.cuda(), kc.cuda(), vc.cuda(), bt.cuda(), q_start.cuda(), ql.cuda(), cl.cuda(),
+                         tiles.cuda(), hq, hkv, scale, kv_splits=splits)
+    torch.cuda.synchronize()
+    _check_status()
+    assert _rel_err(out.cpu(), ref) < 2e-2
+    assert K.prefill_kv_splits(hq, tiles.shape[0], max(ctx_lens)) >= 1
+
+
 def test_attn_prefill_divergent_rescale():
     """Rows whose running max grows by different amounts across KV tiles, so
     the lazy O rescale is needed by some rows of a warp and not others."""
