@@ -42,13 +42,23 @@ def free_port() -> int:
 class ServerThread:
     """A uvicorn server on a background thread."""
 
-    def __init__(self, app, port: int):
+    def __init__(self, app, port: int, ssl_certfile: str | None = None, ssl_keyfile: str | None = None):
         import uvicorn
 
         self.port = port
         self.server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning",
-                                                   access_log=False))
-        self.thread = threading.Thread(target=self.server.run, daemon=True)
+                                                   access_log=False, ssl_certfile=ssl_certfile,
+                                                   ssl_keyfile=ssl_keyfile))
+        self.server_loop = None
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        import asyncio
+
+        loop = asyncio.new_event_loop()
+        asyncio.set_event_loop(loop)
+        self.server_loop = loop
+        loop.run_until_complete(self.server.serve())
 
     def start(self) -> "ServerThread":
         self.thread.start()

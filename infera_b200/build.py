@@ -130,7 +130,7 @@ def build_router(sanitize: str | None = None) -> Path | None:
             with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
                 list(ex.map(_run, todo))
         link = [] if sanitize is None else [f for f in flags if f.startswith("-fsanitize")]
-        _run(["g++", *link, "-o", str(out_bin), *map(str, objs), "-lpthread"])
+        _run(["g++", *link, "-o", str(out_bin), *map(str, objs), "-lpthread", "-lssl", "-lcrypto"])
     return out_bin
 
 

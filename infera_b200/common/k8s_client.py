@@ -126,6 +126,7 @@ class FakeK8sClient:
         self.crs: dict[tuple, dict] = {}
         self._watchers: list[tuple[str, str, asyncio.Queue]] = []
         self.patches = 0
+        self.log: list[tuple[int, str, dict]] = []     # (resource version, type, pod) for watch resumes
 
     def _bump(self, obj: dict) -> None:
         self.rv += 1
@@ -133,6 +134,7 @@ class FakeK8sClient:
 
     def _emit(self, kind: str, pod: dict) -> None:
         ns = pod["metadata"].get("namespace", "default")
+        self.log.append((int(pod["metadata"]["resourceVersion"]), kind, copy.deepcopy(pod)))
         for wns, sel, q in list(self._watchers):
             if wns == ns and _selector_matches(pod["metadata"].get("labels") or {}, sel):
                 q.put_nowait({"type": kind, "object": copy.deepcopy(pod)})
@@ -158,6 +160,17 @@ class FakeK8sClient:
         self._bump(pod)
         if not silent:  # silent: the watch misses the delete (a re-list must catch it)
             self._emit("DELETED", pod)
+
+    def events_since(self, namespace: str, label_selector: str, resource_version: str) -> list[dict]:
+        """Logged events after ``resource_version`` (a watch resuming there
+        replays them before following new ones)."""
+        try:
+            rv = int(resource_version or 0)
+        except ValueError:
+            rv = 0
+        return [{"type": k, "object": copy.deepcopy(p)} for r, k, p in self.log
+                if r > rv and p["metadata"].get("namespace", "default") == namespace
+                and _selector_matches(p["metadata"].get("labels") or {}, label_selector)]
 
     def break_watches(self) -> None:
         for _, _, q in self._watchers:

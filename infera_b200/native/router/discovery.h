@@ -51,6 +51,48 @@ class EtcdDiscovery {
   int64_t rev_ = 0;
 };
 
+// Kubernetes: Pods matching a label selector that carry the annotation
+// infera.amd.com/worker-info (the registration record) are workers; a Pod
+// with a deletionTimestamp stays in the pool as draining (in-flight
+// streams finish, nothing new is routed); DELETED or a missing annotation
+// removes it. List, then watch from the list's resourceVersion; any break
+// re-lists, which also reconciles deletes the watch missed. The API is
+// reached over https (service-account token + CA) or plain http (e.g. a
+// `kubectl proxy` sidecar).
+struct K8sConfig {
+  std::string api_url;       // https://host:port or http://host:port
+  std::string namespace_;
+  std::string selector;
+  std::string token_file;    // bearer token (read at every connect; empty: none)
+  std::string ca_file;       // CA bundle for https (empty: system store)
+};
+
+class K8sDiscovery {
+ public:
+  K8sDiscovery(K8sConfig cfg, Pool* pool, CanaryGate* gate) : cfg_(std::move(cfg)), pool_(pool), gate_(gate) {}
+  ~K8sDiscovery() { stop(); }
+  void start();
+  void stop();
+  bool wait_ready(double timeout_s);
+  std::atomic<uint64_t> events{0}, relists{0}, rejected{0};
+
+ private:
+  void run();
+  bool relist();
+  void watch();
+  void handle(const std::string& kind, const Value& pod);
+  // GET path on the API server; opens a connection the caller reads from
+  struct Stream;
+  bool open_get(const std::string& path_query, Stream* st, int* status);
+  K8sConfig cfg_;
+  Pool* pool_;
+  CanaryGate* gate_;
+  std::thread th_;
+  std::atomic<bool> stop_{false}, ready_{false};
+  std::string rv_ = "0";
+  std::map<std::string, std::string> pod_worker_;  // pod name -> worker id
+};
+
 // records from a JSON file: a list of registration payloads
 bool load_static_workers(const std::string& path, Pool* pool, std::string* err);
 

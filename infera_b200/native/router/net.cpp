@@ -190,8 +190,7 @@ bool Conn::fill() {
   }
   char tmp[65536];
   while (true) {
-    ssize_t r = ::recv(fd_, tmp, sizeof(tmp), 0);
-    if (r < 0 && errno == EINTR) continue;
+    const long r = raw_read(tmp, sizeof(tmp));
     if (r <= 0) return false;
     buf_.append(tmp, static_cast<size_t>(r));
     return true;
@@ -237,15 +236,20 @@ bool Conn::read_exact(size_t n, std::string* out) {
   return true;
 }
 
+long Conn::raw_read(char* dst, size_t cap) {
+  if (tls_ != nullptr) return tls_read(tls_, dst, cap);
+  ssize_t r;
+  do {
+    r = ::recv(fd_, dst, cap, 0);
+  } while (r < 0 && errno == EINTR);
+  return r < 0 ? -1 : static_cast<long>(r);
+}
+
 long Conn::read_some(char* dst, size_t cap) {
   if (buffered() == 0) {
     buf_.clear();
     off_ = 0;
-    ssize_t r;
-    do {
-      r = ::recv(fd_, dst, cap, 0);
-    } while (r < 0 && errno == EINTR);
-    return r < 0 ? -1 : static_cast<long>(r);
+    return raw_read(dst, cap);
   }
   size_t n = std::min(cap, buffered());
   std::memcpy(dst, buf_.data() + off_, n);

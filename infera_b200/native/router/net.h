@@ -24,6 +24,15 @@ void set_timeouts(int fd, int recv_ms, int send_ms);
 bool write_all(int fd, const char* p, size_t n);
 inline bool write_all(int fd, const std::string& s) { return write_all(fd, s.data(), s.size()); }
 
+// TLS client sessions (OpenSSL) for the Kubernetes API server; the data
+// plane itself stays plain HTTP. ca_file empty: the system trust store.
+struct TlsSession;
+TlsSession* tls_connect(int fd, const std::string& host, const std::string& ca_file, std::string* err);
+void tls_free(TlsSession* s);
+long tls_read(TlsSession* s, char* dst, size_t cap);  // 0 = closed, -1 = error
+size_t tls_pending(TlsSession* s);                     // decrypted bytes ready to read
+bool tls_write_all(TlsSession* s, const std::string& data);
+
 std::string base64_encode(const std::string& in);
 std::string base64_decode(const std::string& in);
 std::string lower(std::string s);
@@ -33,6 +42,8 @@ class Conn {
  public:
   explicit Conn(int fd = -1) : fd_(fd) {}
   int fd() const { return fd_; }
+  // read through a TLS session on fd (not owned)
+  void set_tls(TlsSession* t) { tls_ = t; }
   void reset(int fd) { fd_ = fd; buf_.clear(); off_ = 0; }
   // read until "\r\n\r\n"; returns the header block (without the blank line)
   bool read_head(std::string* head, size_t max_bytes = 1 << 20);
@@ -44,7 +55,9 @@ class Conn {
 
  private:
   bool fill();
+  long raw_read(char* dst, size_t cap);
   int fd_;
+  TlsSession* tls_ = nullptr;
   std::string buf_;
   size_t off_ = 0;
 };

@@ -18,6 +18,8 @@
 #include <sys/socket.h>
 #include <unistd.h>
 
+#include <fstream>
+
 #include <atomic>
 #include <chrono>
 #include <cstdio>
@@ -55,6 +57,7 @@ struct Config {
   std::string nats_url = "nats://127.0.0.1:4222";
   double nats_idle_timeout = 900.0;
   double nats_max_duration = 0.0;
+  K8sConfig k8s;
 };
 
 static double now_s() {
@@ -169,6 +172,7 @@ class App {
   Breaker breaker;
   std::unique_ptr<Tokenizer> tok;
   std::unique_ptr<EtcdDiscovery> disc;
+  std::unique_ptr<K8sDiscovery> k8s;
   std::unique_ptr<NatsConn> nats;   // set with --request-transport nats
   double nats_idle = 900.0;
   double nats_max_duration = 0.0;   // 0: no overall limit
@@ -1076,6 +1080,24 @@ int main(int argc, char** argv) {
   cfg.etcd_endpoint = env("INFERA_ETCD_ENDPOINT", "");
   cfg.router_mode = env("INFERA_ROUTER_MODE", "auto");
   cfg.tokenizer_path = env("INFERA_ROUTER_TOKENIZER_PATH", "");
+  {
+    // in-cluster defaults: the API service from the environment, the Pod's
+    // service account for token, CA and namespace
+    const std::string sa = "/var/run/secrets/kubernetes.io/serviceaccount/";
+    auto exists = [](const std::string& f) { return ::access(f.c_str(), R_OK) == 0; };
+    const std::string kh = env("KUBERNETES_SERVICE_HOST", "kubernetes.default.svc");
+    cfg.k8s.api_url = env("INFERA_K8S_API_URL", ("https://" + kh + ":" + env("KUBERNETES_SERVICE_PORT", "443")).c_str());
+    cfg.k8s.selector = env("INFERA_K8S_LABEL_SELECTOR", "");
+    cfg.k8s.token_file = exists(sa + "token") ? sa + "token" : "";
+    cfg.k8s.ca_file = exists(sa + "ca.crt") ? sa + "ca.crt" : "";
+    std::string ns = env("POD_NAMESPACE", "default");
+    if (exists(sa + "namespace")) {
+      std::ifstream f(sa + "namespace");
+      std::string v;
+      if (std::getline(f, v) && !v.empty()) ns = v;
+    }
+    cfg.k8s.namespace_ = ns;
+  }
   cfg.max_retries = std::atoi(env("INFERA_REQUEST_MAX_RETRIES", "1").c_str());
   cfg.migration_limit = std::atoi(env("INFERA_MIGRATION_LIMIT", "0").c_str());
   cfg.breaker_threshold = std::atoi(env("INFERA_BREAKER_FAILURE_THRESHOLD", "3").c_str());
@@ -1112,6 +1134,11 @@ int main(int argc, char** argv) {
     else if (a == "--log-level") cfg.verbose = v == "debug" || v == "info";
     else if (a == "--help" || a == "-h") { usage(); return 0; }
     else if (a == "--request-transport") cfg.request_transport = v;
+    else if (a == "--k8s-label-selector") cfg.k8s.selector = v;
+    else if (a == "--k8s-namespace") cfg.k8s.namespace_ = v;
+    else if (a == "--k8s-api-url") cfg.k8s.api_url = v;
+    else if (a == "--k8s-token-file") cfg.k8s.token_file = v;
+    else if (a == "--k8s-ca-file") cfg.k8s.ca_file = v;
     else if (a == "--nats-url") cfg.nats_url = v;
     else if (a == "--nats-idle-timeout") cfg.nats_idle_timeout = std::atof(v.c_str());
     else if (a == "--nats-max-duration") cfg.nats_max_duration = std::atof(v.c_str());
@@ -1147,6 +1174,15 @@ int main(int argc, char** argv) {
     app.disc = std::make_unique<EtcdDiscovery>(cfg.etcd_endpoint, cfg.etcd_prefix, &app.pool, &app.gate);
     app.disc->start();
     if (!app.disc->wait_ready(10.0)) std::fprintf(stderr, "[ib200_router] etcd not ready after 10 s; continuing\n");
+  } else if (cfg.discovery == "kubernetes" || cfg.discovery == "k8s") {
+    if (cfg.k8s.selector.empty()) {
+      std::fprintf(stderr, "[ib200_router] --discovery-backend=kubernetes requires --k8s-label-selector\n");
+      return 2;
+    }
+    app.k8s = std::make_unique<K8sDiscovery>(cfg.k8s, &app.pool, &app.gate);
+    app.k8s->start();
+    if (!app.k8s->wait_ready(10.0))
+      std::fprintf(stderr, "[ib200_router] kubernetes API not ready after 10 s; continuing\n");
   } else if (cfg.discovery == "static") {
     std::string err;
     if (!cfg.static_workers.empty() && !load_static_workers(cfg.static_workers, &app.pool, &err)) {

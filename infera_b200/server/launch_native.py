@@ -2,7 +2,8 @@
 
 The native binary (``infera_b200/lib/ib200_router``, built from
 ``infera_b200/native/router``) takes the same flags as the Python router
-for the features it implements (etcd or static discovery, KV-aware and
+for the features it implements (etcd, Kubernetes or static discovery,
+byte, word-level and byte-level BPE tokenizers, KV-aware and
 round-robin policies, auto / direct modes, failover, breaker, PD pairs);
 Python-only flags are accepted and ignored. Role of the reference's Rust
 launcher (``infera/server/__main__.py:323-327`` execs ``rust/router``).
@@ -16,7 +17,7 @@ import sys
 from infera_b200.build import ROUTER_BIN, build_router
 
 PY_ONLY = {"--enable-profiling", "--enable-scaling-api"}
-PY_ONLY_WITH_VALUE = {"--scaling-deployment", "--kvd-socket-path", "--k8s-label-selector", "--k8s-namespace"}
+PY_ONLY_WITH_VALUE = {"--scaling-deployment", "--kvd-socket-path"}
 
 
 def native_argv(argv: list[str]) -> list[str]:
@@ -43,8 +44,9 @@ def router_binary() -> str:
 
 
 def exec_native(args, argv: list[str]) -> None:
-    if args.discovery_backend not in ("etcd",):
-        raise SystemExit(f"--router-backend native supports etcd discovery; got {args.discovery_backend!r}")
+    if args.discovery_backend not in ("etcd", "kubernetes"):
+        raise SystemExit(f"--router-backend native supports etcd and kubernetes discovery; "
+                         f"got {args.discovery_backend!r}")
     binary = router_binary()
     sys.stdout.flush()
     sys.stderr.flush()

@@ -346,3 +346,102 @@ def test_bpe_tokenizer_matches_tokenizers_library(binary, tmp_path, family):
             continue
         assert got == tok.encode(t, add_special_tokens=False).ids, repr(t)
     assert refused < len(texts) // 2
+
+
+def _self_signed(tmp_path):
+    """A CA-less self-signed certificate for 127.0.0.1 (it is its own CA bundle)."""
+    import datetime
+    import ipaddress
+
+    from cryptography import x509
+    from cryptography.hazmat.primitives import hashes, serialization
+    from cryptography.hazmat.primitives.asymmetric import ec
+    from cryptography.x509.oid import NameOID
+
+    key = ec.generate_private_key(ec.SECP256R1())
+    name = x509.Name([x509.NameAttribute(NameOID.COMMON_NAME, "fake-apiserver")])
+    now = datetime.datetime.now(datetime.timezone.utc)
+    cert = (x509.CertificateBuilder().subject_name(name).issuer_name(name).public_key(key.public_key())
+            .serial_number(x509.random_serial_number()).not_valid_before(now - datetime.timedelta(minutes=5))
+            .not_valid_after(now + datetime.timedelta(days=1))
+            .add_extension(x509.SubjectAlternativeName([x509.IPAddress(ipaddress.ip_address("127.0.0.1"))]),
+                           critical=False)
+            .add_extension(x509.BasicConstraints(ca=True, path_length=None), critical=True)
+            .sign(key, hashes.SHA256()))
+    cf, kf = tmp_path / "apiserver.crt", tmp_path / "apiserver.key"
+    cf.write_bytes(cert.public_bytes(serialization.Encoding.PEM))
+    kf.write_bytes(key.private_bytes(serialization.Encoding.PEM, serialization.PrivateFormat.TraditionalOpenSSL,
+                                     serialization.NoEncryption()))
+    return str(cf), str(kf)
+
+
+@pytest.mark.parametrize("tls", [False, True])
+def test_kubernetes_discovery(binary, tmp_path, tls):
+    """Pods with the worker-info annotation become workers (list, then the
+    watch), a deletionTimestamp makes one draining (listed, not routed), a
+    DELETED event removes it, and a delete the watch missed is reconciled by
+    the re-list after the watch breaks. TLS: the API server's certificate is
+    verified against the given CA bundle and the bearer token is sent."""
+    from infera_b200.common.k8s_client import FakeK8sClient
+    from infera_b200.common.k8s_fake_server import build_app as k8s_app
+
+    fake = FakeK8sClient()
+    token = tmp_path / "token"
+    token.write_text("s3cret\n")
+    cert = _self_signed(tmp_path) if tls else (None, None)
+    srv = ServerThread(k8s_app(fake, require_token="s3cret"), free_port(), ssl_certfile=cert[0],
+                       ssl_keyfile=cert[1]).start()
+    labels = {"app": "infera-worker"}
+
+    def rec(i):
+        return json.dumps({"worker_id": f"w{i}", "url": f"http://127.0.0.1:{40000 + i}", "model_name": "m"})
+
+    def on_loop(fn, *a):
+        # mutate the fake on the server's event loop (its watch queues live there)
+        import threading
+
+        done = threading.Event()
+
+        def run():
+            fn(*a)
+            done.set()
+
+        srv.server_loop.call_soon_threadsafe(run)
+        assert done.wait(5)
+
+    for i in range(2):
+        fake.create_pod("infera", f"pod{i}", labels, {"infera.amd.com/worker-info": rec(i)})
+    fake.create_pod("infera", "other", {"app": "else"}, {"infera.amd.com/worker-info": rec(9)})
+    scheme = "https" if tls else "http"
+    args = ["--discovery-backend", "kubernetes", "--k8s-label-selector", "app=infera-worker", "--k8s-namespace",
+            "infera", "--k8s-api-url", f"{scheme}://127.0.0.1:{srv.port}", "--k8s-token-file", str(token)]
+    if tls:
+        args += ["--k8s-ca-file", cert[0]]
+    p, url = _start_router(binary, *args)
+
+    def workers():
+        return {w["worker_id"]: w.get("status") for w in httpx.get(url + "/v1/workers").json()["workers"]}
+
+    def wait_for(pred, what):
+        t0 = time.time()
+        while time.time() - t0 < 10:
+            if pred(workers()):
+                return
+            time.sleep(0.05)
+        raise AssertionError(f"{what}: {workers()}")
+
+    try:
+        wait_for(lambda w: set(w) == {"w0", "w1"}, "listed pods")
+        on_loop(fake.create_pod, "infera", "pod2", labels, {"infera.amd.com/worker-info": rec(2)})
+        wait_for(lambda w: "w2" in w, "watched ADDED")
+        on_loop(fake.mark_terminating, "infera", "pod1")
+        wait_for(lambda w: w.get("w1") == "draining", "terminating pod draining")
+        assert httpx.get(url + "/health").json()["workers"] == 2
+        on_loop(fake.delete_pod, "infera", "pod1")
+        wait_for(lambda w: "w1" not in w, "DELETED")
+        on_loop(fake.delete_pod, "infera", "pod0", True)       # the watch misses it
+        on_loop(fake.break_watches)
+        wait_for(lambda w: set(w) == {"w2"}, "re-list reconciles the missed delete")
+    finally:
+        _stop(p)
+        srv.stop()
