@@ -112,8 +112,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* v_full = k_full + KV_STAGES;       // [KV_STAGES]
   uint64_t* kv_empty = v_full + KV_STAGES;     // [KV_STAGES]
   uint64_t* s_full = kv_empty + KV_STAGES;     // [2]
-  uint64_t* p_full = s_full + 2;               // [1]
-  uint64_t* o_done = p_full + 1;               // [1]
+  uint64_t* p_full = s_full + 2;               // [2] by tile parity: the softmax may run a tile ahead of PV
+  uint64_t* o_done = p_full + 2;               // [1]
   uint64_t* drain = o_done + 1;
   uint64_t* pair = drain + 1;                  // [4] per TMEM quadrant: the two softmax warps on it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair + 4);
@@ -155,7 +155,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 256);
+    mbar_init(&p_full[0], 256);
+    mbar_init(&p_full[1], 256);
     for (int i = 0; i < 4; ++i) mbar_init(&pair[i], 64);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
@@ -238,7 +239,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kStatusTimeoutFull);
       auto issue_pv = [&](int jj) -> bool {
         // O += P V_jj once softmax has written P for tile jj
-        if (!mbar_wait(p_full, static_cast<uint32_t>(jj & 1), abort_flag, p.status, kStatusTimeoutTmemEmpty))
+        if (!mbar_wait(&p_full[jj & 1], static_cast<uint32_t>((jj >> 1) & 1), abort_flag, p.status,
+                       kStatusTimeoutTmemEmpty))
           return false;
         const int st = jj % KV_STAGES;
         if (!mbar_wait(&v_full[st], static_cast<uint32_t>((jj / KV_STAGES) & 1), abort_flag, p.status,
@@ -402,7 +404,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       m_run = m_use;
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1]);
       if (tr0) fstamp(p, FTR_PARRIVE, j);
     }
     ok = __all_sync(0xffffffffu, ok);

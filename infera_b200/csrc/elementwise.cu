@@ -97,13 +97,19 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
 // Rotate q and k in place (rotate-half pairs (i, i + D/2)), then copy k, v
 // into the cache slot of each token (slot < 0: skip the cache write).
 // cos_sin: [max_pos, D/2, 2] fp32.
+// Out-of-range positions or slots (bad host metadata) are recorded in the
+// status word and skipped instead of touching memory outside the tables.
 __global__ void rope_kvwrite_kernel(__nv_bfloat16* __restrict__ qkv, int ldqkv, const int* __restrict__ pos,
                                     const int* __restrict__ slots, const float2* __restrict__ cos_sin, int hq,
                                     int hkv, int D, __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
-                                    int ldkv) {
+                                    int ldkv, long long num_slots, int max_pos, int* status) {
   const int t = blockIdx.x;
   const int p = pos[t];
-  const long long slot = slots[t];
+  long long slot = slots[t];
+  if (p < 0 || p >= max_pos || slot >= num_slots) {
+    if (threadIdx.x == 0) record_status(status, kStatusBadIndex);
+    return;
+  }
   __nv_bfloat16* row = qkv + static_cast<size_t>(t) * ldqkv;
   const int half = D / 2;
   const float2* cs = cos_sin + static_cast<size_t>(p) * half;
@@ -136,11 +142,18 @@ __global__ void rope_kvwrite_kernel(__nv_bfloat16* __restrict__ qkv, int ldqkv, 
   }
 }
 
+// An id outside [0, vocab) is recorded in the status word and its row zeroed.
 __global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
-                             __nv_bfloat16* __restrict__ out, int H) {
+                             __nv_bfloat16* __restrict__ out, int H, int vocab, int* status) {
   const int t = blockIdx.x;
-  const uint4* src = reinterpret_cast<const uint4*>(table + static_cast<size_t>(ids[t]) * H);
+  const int id = ids[t];
   uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H);
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) record_status(status, kStatusBadIndex);
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + static_cast<size_t>(id) * H);
   for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = src[c];
 }
 
@@ -258,22 +271,26 @@ extern "C" int ib_add_rmsnorm(const void* delta, void* residual, const void* w, 
   return ret_launch();
 }
 
+// num_slots: rows of each cache; max_pos: rows of the cos / sin table.
 extern "C" int ib_rope_kvwrite(void* qkv, int T, int ldqkv, const int* pos, const int* slots, const void* cos_sin,
-                               int hq, int hkv, int D, void* k_cache, void* v_cache, int ldkv, cudaStream_t stream) {
+                               int hq, int hkv, int D, void* k_cache, void* v_cache, int ldkv, long long num_slots,
+                               int max_pos, int* status, cudaStream_t stream) {
   if (T <= 0) return 0;
   if (D % 4 != 0) return -1;
   ew::rope_kvwrite_kernel<<<T, 256, 0, stream>>>(static_cast<__nv_bfloat16*>(qkv), ldqkv, pos, slots,
                                                   static_cast<const float2*>(cos_sin), hq, hkv, D,
                                                   static_cast<__nv_bfloat16*>(k_cache),
-                                                  static_cast<__nv_bfloat16*>(v_cache), ldkv);
+                                                  static_cast<__nv_bfloat16*>(v_cache), ldkv, num_slots, max_pos,
+                                                  status);
   return ret_launch();
 }
 
-extern "C" int ib_embed(const int* ids, const void* table, void* out, int T, int H, cudaStream_t stream) {
+extern "C" int ib_embed(const int* ids, const void* table, void* out, int T, int H, int vocab, int* status,
+                        cudaStream_t stream) {
   if (T <= 0) return 0;
   if (H % 8 != 0) return -1;
   ew::embed_kernel<<<T, 256, 0, stream>>>(ids, static_cast<const __nv_bfloat16*>(table),
-                                           static_cast<__nv_bfloat16*>(out), H);
+                                           static_cast<__nv_bfloat16*>(out), H, vocab, status);
   return ret_launch();
 }
 

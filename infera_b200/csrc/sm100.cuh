@@ -25,6 +25,7 @@ enum : int {
   kStatusTimeoutTmemEmpty = 4, // epilogue never released an accumulator
   kStatusTimeoutPeer = 5,      // a peer GPU flag never arrived
   kStatusBadArgs = 6,
+  kStatusBadIndex = 7,         // an index from device data was out of range (the access was skipped)
 };
 
 // Default bound for a single wait: 2 s of wall time.

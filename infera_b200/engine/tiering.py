@@ -53,7 +53,7 @@ def hash_key(h: int) -> bytes:
 
 class TierManager:
     def __init__(self, k_cache: torch.Tensor, v_cache: torch.Tensor, store, page_size: int = 16,
-                 retention: str = "long", staging_pages: int = 64, load_chunk: int = 32,
+                 retention: str = "long", staging_pages: int = 0, load_chunk: int = 32,
                  async_load: bool = True, key_tag: bytes = b""):
         self.k = k_cache
         self.v = v_cache
@@ -71,8 +71,9 @@ class TierManager:
                                   hidden_dim=self.H, dtype="bf16", num_kv_channels=self.C)
         dt = k_cache.dtype
         pin = self.on_gpu
-        # save ring: slots [head, head + inflight) are in use, released in order
-        n = staging_pages
+        # save ring: slots [head, head + inflight) are in use, released in order;
+        # 0 = as many pages as fit in 1 GiB (at least 16)
+        n = staging_pages if staging_pages > 0 else max(16, (1 << 30) // self.page_bytes)
         self.n_save = n
         self.save_dev = torch.empty(n, self.elems, dtype=dt, device=self.dev)
         self.save_host = torch.empty(n, self.elems, dtype=dt, pin_memory=pin)
@@ -135,22 +136,36 @@ class TierManager:
         """The block manager is reusing ``page`` (it held ``block_hash``)."""
         self.pending_saves.append((page, block_hash))
 
-    def flush_saves(self) -> int:
+    def flush_saves(self, wait_s: float = 60.0) -> int:
         """Issue the gather + copy-out of every page evicted since the last
-        call (call after scheduling, before the forward pass). Returns the
-        number of pages queued."""
+        call (call after scheduling, before the forward pass: the pages are
+        about to be overwritten). A burst larger than the free staging slots
+        goes out in rounds, waiting for the writer to release slots between
+        them (backpressure instead of dropping pages); only a writer stuck
+        for ``wait_s`` makes the rest count as dropped. Returns the number of
+        pages queued."""
         items, self.pending_saves = self.pending_saves, []
-        if not items:
-            return 0
+        queued = 0
+        t0 = time.time()
+        while items:
+            with self._lock:
+                free = self.n_save - self.save_inflight
+            if free <= 0:
+                if time.time() - t0 > wait_s:
+                    break
+                time.sleep(0.0005)
+                continue
+            take, items = items[:free], items[free:]
+            self._issue_saves(take)
+            queued += len(take)
+        self.stats["save_dropped"] += len(items)
+        return queued
+
+    def _issue_saves(self, take: list[tuple[int, int]]) -> None:
         with self._lock:
-            free = self.n_save - self.save_inflight
-            take = items[:free]
             start = self.save_head
             self.save_inflight += len(take)
             self.save_head = (start + len(take)) % self.n_save
-        self.stats["save_dropped"] += len(items) - len(take)
-        if not take:
-            return 0
         m = len(take)
         slots = [(start + i) % self.n_save for i in range(m)]
         self.save_idx_np[slots] = [p for p, _ in take]
@@ -177,7 +192,6 @@ class TierManager:
                                self.ps, gather=True, page_major=True)
         self.stats["save_batches"] += 1
         self._save_q.put((slots, [h for _, h in take], ev))
-        return m
 
     def _writer(self) -> None:
         while True:

@@ -38,8 +38,9 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_gemm_bf16_plan": [c_int, c_int, c_int, c_int, c_int, c_vp],
         "ib_rmsnorm": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_vp],
         "ib_add_rmsnorm": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float, c_vp],
-        "ib_rope_kvwrite": [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp],
-        "ib_embed": [c_vp, c_vp, c_vp, c_int, c_int, c_vp],
+        "ib_rope_kvwrite": [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_int, c_ll,
+                            c_int, c_vp, c_vp],
+        "ib_embed": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp],
         "ib_sample": [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp],
         "ib_gather_rows": [c_vp, c_vp, c_vp, c_int, c_int, c_vp],
         "ib_attn_decode": [c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float,
@@ -140,6 +141,19 @@ def kernels() -> ctypes.CDLL:
     return _kernels
 
 
+# INFERA_SYNC_CHECK=1: synchronise after every launch, so a device fault is
+# reported against the kernel that caused it (slow; for diagnosis)
+_SYNC_CHECK = os.environ.get("INFERA_SYNC_CHECK", "") == "1"
+
+
 def check(rc: int, what: str) -> None:
     if rc != 0:
         raise RuntimeError(f"{what} failed with code {rc}")
+    if _SYNC_CHECK:
+        import torch
+
+        if torch.cuda.is_available():
+            try:
+                torch.cuda.synchronize()
+            except RuntimeError as e:
+                raise RuntimeError(f"{what}: device error after this launch: {e}") from e
