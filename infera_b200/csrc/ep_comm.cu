@@ -16,6 +16,13 @@
 //                   counter on every rank;
 //   ib_ep_dispatch_q the same for e4m3 rows plus their UE8M0 scale columns
 //                   (the sender quantised them; half the bytes of bf16);
+//   ib_ep_dispatch_ex / ib_ep_dispatch_q_ex: the same, plus per-expert
+//                   arrival counters: when the last row of (this source,
+//                   expert e) has been stored, its destination's counter of
+//                   local expert e grows by 1 (experts this source sends no
+//                   rows to are signalled at once), so the destination's up
+//                   projection starts an expert's tiles as soon as that
+//                   expert's rows from every source are in;
 //   ib_ep_wait      waits (bounded, 2 s) until all W arrivals of a round are in
 //                   (the up projection can instead wait inside its own
 //                   producer: ib_gemm_grouped_wait);
@@ -39,7 +46,38 @@ constexpr unsigned long long kWaitNs = 2000000000ull;
 struct Peers {
   void* buf[kMaxRanks];            // recv (dispatch) or ret (return) base on each rank
   unsigned int* flag[kMaxRanks];   // arrival counter on each rank for this phase
+  unsigned int* eflag[kMaxRanks];  // per-local-expert arrival counters on each rank (null: not used)
 };
+
+// Per-expert arrival signalling of one dispatched row (every thread of the
+// CTA calls it after its stores of the row): the row's stores are made
+// visible system-wide, counted in local_done[e], and the CTA that stores
+// the last row of expert e bumps the destination's counter of e.
+__device__ __forceinline__ void row_landed(const Peers& pr, unsigned int* local_done, const int* offsets, int e,
+                                           int El) {
+  if (pr.eflag[0] == nullptr) return;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned int n_e = static_cast<unsigned int>(offsets[e + 1] - offsets[e]);
+    if (atomicAdd(&local_done[e], 1u) == n_e - 1) {
+      local_done[e] = 0;  // no other increment of e this round
+      __threadfence_system();
+      const int d = e / El;
+      atomicAdd_system(pr.eflag[d] + (e - d * El), 1u);
+    }
+  }
+}
+
+// experts this source sends nothing to are complete from the start
+__device__ __forceinline__ void signal_empty_experts(const Peers& pr, const int* offsets, int E, int El) {
+  if (pr.eflag[0] == nullptr || blockIdx.x != 0) return;
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    if (offsets[e + 1] == offsets[e]) {
+      const int d = e / El;
+      atomicAdd_system(pr.eflag[d] + (e - d * El), 1u);
+    }
+}
 
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
@@ -113,7 +151,8 @@ __device__ __forceinline__ void signal_all(unsigned int* done_ctr, const Peers& 
 __global__ void __launch_bounds__(256) dispatch_kernel(const uint4* __restrict__ x, int rows, int vec_per_row,
                                                        const int* __restrict__ offsets, int E, int El,
                                                        const int* __restrict__ dst_off, Peers pr, int world,
-                                                       unsigned int* done_ctr) {
+                                                       unsigned int* done_ctr, unsigned int* local_done) {
+  signal_empty_experts(pr, offsets, E, El);
   for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     const int e = find_bin(offsets, E, r);
     const int d = e / El;
@@ -121,6 +160,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(const uint4* __restrict__
     uint4* dst = static_cast<uint4*>(pr.buf[d]) + pos * vec_per_row;
     const uint4* src = x + static_cast<long long>(r) * vec_per_row;
     for (int i = threadIdx.x; i < vec_per_row; i += blockDim.x) dst[i] = __ldg(src + i);
+    row_landed(pr, local_done, offsets, e, El);
   }
   signal_all(done_ctr, pr, world);
 }
@@ -134,7 +174,9 @@ __global__ void __launch_bounds__(256) dispatch_q_kernel(const uint4* __restrict
                                                          const uint8_t* __restrict__ sf, int sf_ld, int n_groups,
                                                          const int* __restrict__ offsets, int E, int El,
                                                          const int* __restrict__ dst_off, Peers pr, Peers psf,
-                                                         int recv_sf_ld, int world, unsigned int* done_ctr) {
+                                                         int recv_sf_ld, int world, unsigned int* done_ctr,
+                                                         unsigned int* local_done) {
+  signal_empty_experts(pr, offsets, E, El);
   for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     const int e = find_bin(offsets, E, r);
     const int d = e / El;
@@ -145,6 +187,7 @@ __global__ void __launch_bounds__(256) dispatch_q_kernel(const uint4* __restrict
     uint8_t* dsf = static_cast<uint8_t*>(psf.buf[d]);
     for (int g = threadIdx.x; g < n_groups; g += blockDim.x)
       dsf[static_cast<long long>(g) * recv_sf_ld + pos] = __ldg(sf + static_cast<long long>(g) * sf_ld + r);
+    row_landed(pr, local_done, offsets, e, El);
   }
   signal_all(done_ctr, pr, world);
 }
@@ -217,40 +260,64 @@ extern "C" int ib_ep_offsets(const int* C, int W, int E, int rank, int* dst_off,
 }
 
 // peer_buf / peer_flag: host arrays of `world` device pointers
-extern "C" int ib_ep_dispatch(const void* x, int rows, int H, const int* offsets, int E, int world,
-                              const int* dst_off, void* const* peer_buf, unsigned int* const* peer_flag,
-                              unsigned int* done_ctr, cudaStream_t stream) {
+// peer_eflag (null: no per-expert counters): each rank's per-local-expert
+// counters; local_done: E zeroed counters of this rank (reset by the kernel)
+extern "C" int ib_ep_dispatch_ex(const void* x, int rows, int H, const int* offsets, int E, int world,
+                                 const int* dst_off, void* const* peer_buf, unsigned int* const* peer_flag,
+                                 unsigned int* const* peer_eflag, unsigned int* local_done, unsigned int* done_ctr,
+                                 cudaStream_t stream) {
   if (world < 1 || world > kMaxRanks || (H * 2) % 16) return -1;
+  if (peer_eflag != nullptr && local_done == nullptr) return -1;
   Peers pr{};
   for (int d = 0; d < world; ++d) {
     pr.buf[d] = peer_buf[d];
     pr.flag[d] = peer_flag[d];
+    pr.eflag[d] = peer_eflag != nullptr ? peer_eflag[d] : nullptr;
   }
   const int grid = rows < 1 ? 1 : (rows < 2048 ? rows : 2048);
   dispatch_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(x), rows, H * 2 / 16, offsets, E, E / world,
-                                            dst_off, pr, world, done_ctr);
+                                            dst_off, pr, world, done_ctr, local_done);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
 
+extern "C" int ib_ep_dispatch(const void* x, int rows, int H, const int* offsets, int E, int world,
+                              const int* dst_off, void* const* peer_buf, unsigned int* const* peer_flag,
+                              unsigned int* done_ctr, cudaStream_t stream) {
+  return ib_ep_dispatch_ex(x, rows, H, offsets, E, world, dst_off, peer_buf, peer_flag, nullptr, nullptr, done_ctr,
+                           stream);
+}
+
 // fp8 rows (row_bytes % 16 == 0) with their scale columns; peer_sf: each
 // rank's recv_sf base ([n_groups, recv_sf_ld] bytes)
-extern "C" int ib_ep_dispatch_q(const void* x, int rows, int row_bytes, const uint8_t* sf, int sf_ld, int n_groups,
-                                const int* offsets, int E, int world, const int* dst_off, void* const* peer_buf,
-                                void* const* peer_sf, int recv_sf_ld, unsigned int* const* peer_flag,
-                                unsigned int* done_ctr, cudaStream_t stream) {
+extern "C" int ib_ep_dispatch_q_ex(const void* x, int rows, int row_bytes, const uint8_t* sf, int sf_ld,
+                                   int n_groups, const int* offsets, int E, int world, const int* dst_off,
+                                   void* const* peer_buf, void* const* peer_sf, int recv_sf_ld,
+                                   unsigned int* const* peer_flag, unsigned int* const* peer_eflag,
+                                   unsigned int* local_done, unsigned int* done_ctr, cudaStream_t stream) {
   if (world < 1 || world > kMaxRanks || row_bytes % 16 || n_groups < 0) return -1;
+  if (peer_eflag != nullptr && local_done == nullptr) return -1;
   Peers pr{}, psf{};
   for (int d = 0; d < world; ++d) {
     pr.buf[d] = peer_buf[d];
     pr.flag[d] = peer_flag[d];
+    pr.eflag[d] = peer_eflag != nullptr ? peer_eflag[d] : nullptr;
     psf.buf[d] = peer_sf[d];
   }
   const int grid = rows < 1 ? 1 : (rows < 2048 ? rows : 2048);
   dispatch_q_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4*>(x), rows, row_bytes / 16, sf, sf_ld, n_groups,
-                                              offsets, E, E / world, dst_off, pr, psf, recv_sf_ld, world, done_ctr);
+                                              offsets, E, E / world, dst_off, pr, psf, recv_sf_ld, world, done_ctr,
+                                              local_done);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+extern "C" int ib_ep_dispatch_q(const void* x, int rows, int row_bytes, const uint8_t* sf, int sf_ld, int n_groups,
+                                const int* offsets, int E, int world, const int* dst_off, void* const* peer_buf,
+                                void* const* peer_sf, int recv_sf_ld, unsigned int* const* peer_flag,
+                                unsigned int* done_ctr, cudaStream_t stream) {
+  return ib_ep_dispatch_q_ex(x, rows, row_bytes, sf, sf_ld, n_groups, offsets, E, world, dst_off, peer_buf, peer_sf,
+                             recv_sf_ld, peer_flag, nullptr, nullptr, done_ctr, stream);
 }
 
 extern "C" int ib_ep_return(const void* y, int rows, int H, const int* C, int world, int E, int rank,

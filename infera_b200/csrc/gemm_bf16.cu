@@ -115,6 +115,7 @@ struct Params {
   const unsigned int* wait_flag;
   unsigned int wait_target;
   uint64_t wait_limit_ns;   // bound of that wait (0: kWaitLimitNs)
+  int wait_per_expert;      // grouped: wait_flag[e] per local expert, waited before each of e's tiles
 };
 
 // Bounded wait for the dispatch's arrival counter (release-incremented by
@@ -122,13 +123,14 @@ struct Params {
 // ordered before this thread's later TMA (async-proxy) reads; on timeout the
 // status is recorded and the CTA's other roles are released through
 // abort_flag.
-__device__ __forceinline__ bool wait_arrivals(const Params& p, volatile int* abort_flag) {
+__device__ __forceinline__ bool wait_arrivals(const Params& p, volatile int* abort_flag, int expert = 0) {
   if (p.wait_flag == nullptr) return true;
+  const unsigned int* flag = p.wait_flag + (p.wait_per_expert ? expert : 0);
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
     uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.wait_flag) : "memory");
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
     if (v >= p.wait_target) break;
     if (((++spins) & 63u) == 0) {
       if (*abort_flag) return false;
@@ -386,10 +388,15 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       const uint32_t tx = static_cast<uint32_t>((BM + p.bn) * 128);
       uint32_t stage = 0, phase = 0;
       long long issued = 0;
-      bool ok = wait_arrivals(p, abort_flag);
+      // one wait for the whole round, or per tile on the tile's expert
+      bool ok = p.wait_per_expert ? true : wait_arrivals(p, abort_flag);
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         int pt, qt, sp;
         tile_coords(p, t, pt, qt, sp);
+        if (p.wait_per_expert && !wait_arrivals(p, abort_flag, p.gtab[t].x)) {
+          ok = false;
+          break;
+        }
         const int kb0 = sp * p.kbps;
         const int kb1 = min(kb0 + p.kbps, p.nkb);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -490,6 +497,11 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
         if (fresh) {
           int pt, qt, sp;
           tile_coords(p, ft, pt, qt, sp);
+          if (p.wait_per_expert) {  // this tile's scales arrive with its expert's rows
+            int ok = 1;
+            if (lane == 0) ok = wait_arrivals(p, abort_flag, p.gtab[ft].x) ? 1 : 0;
+            if (__shfl_sync(0xffffffffu, ok, 0) == 0) return false;
+          }
           fkb = sp * p.kbps;
           fkb1 = min(fkb + p.kbps, p.nkb);
           fwrow = tile_prow(p, ft, pt) / BM;
@@ -539,7 +551,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     uint32_t wv[kAhead], rv[kAhead][8];
     bool has[kAhead];
     bool arrived = true;
-    if (p.wait_flag != nullptr) {   // the activation scales arrive with the dispatched rows
+    if (p.wait_flag != nullptr && !p.wait_per_expert) {   // the activation scales arrive with the dispatched rows
       if (lane == 0) arrived = wait_arrivals(p, abort_flag);
       arrived = __shfl_sync(0xffffffffu, arrived ? 1 : 0, 0) != 0;
     }
@@ -929,7 +941,7 @@ inline int run_grouped(const Operands& o, const void* A, const void* W, void* ou
                        int* status, cudaStream_t stream, const int* row_map = nullptr, int world = 1,
                        void* const* peer_out = nullptr, unsigned int* const* peer_flag = nullptr,
                        unsigned int* done_ctr = nullptr, const unsigned int* wait_flag = nullptr,
-                       unsigned int wait_target = 0, uint64_t wait_limit_ns = 0) {
+                       unsigned int wait_target = 0, uint64_t wait_limit_ns = 0, int wait_per_expert = 0) {
   if (R <= 0 || N <= 0 || K <= 0 || E <= 0) return 0;
   if (!operands_ok(o, K, lda, ldw) || (N % BM) != 0) return -1;
   if (o.fp8 ? (bn < 32 || bn > MAX_BN_FP8 || (bn % 32) != 0) : (bn < 16 || bn > MAX_BN || (bn % 16) != 0))
@@ -958,6 +970,7 @@ inline int run_grouped(const Operands& o, const void* A, const void* W, void* ou
   p.wait_flag = wait_flag;
   p.wait_target = wait_target;
   p.wait_limit_ns = wait_limit_ns;
+  p.wait_per_expert = wait_flag != nullptr && wait_per_expert ? 1 : 0;
   if (row_map != nullptr) {
     if (epi != EPI_BF16 || world < 1 || world > kMaxPeers || done_ctr == nullptr) return -1;
     p.push = 1;
@@ -1065,6 +1078,20 @@ extern "C" int ib_gemm_grouped_wait(const void* A, const uint8_t* sf_a, int sf_a
   const gemm::Operands o{sf_w != nullptr, sf_a, sf_a_ld, sf_w};
   return gemm::run_grouped(o, A, W, out, R, N, K, E, lda, ldw, ldc, epi, gtab, gnum, bn, grid_tiles, status, stream,
                            nullptr, 1, nullptr, nullptr, nullptr, wait_flag, wait_target);
+}
+
+// As ib_gemm_grouped_wait with one arrival counter per local expert:
+// wait_flag[e] >= wait_target is waited (bounded) before each tile of
+// expert e, by the TMA producer and (fp8) the scale stagers, so an
+// expert's tiles start as soon as its rows from every source are in.
+extern "C" int ib_gemm_grouped_wait_ex(const void* A, const uint8_t* sf_a, int sf_a_ld, const void* W,
+                                       const uint8_t* sf_w, void* out, int R, int N, int K, int E, int lda, int ldw,
+                                       int ldc, int epi, const int* gtab, const int* gnum, int bn, int grid_tiles,
+                                       const unsigned int* wait_flag, unsigned int wait_target, int per_expert,
+                                       unsigned long long wait_limit_ns, int* status, cudaStream_t stream) {
+  const gemm::Operands o{sf_w != nullptr, sf_a, sf_a_ld, sf_w};
+  return gemm::run_grouped(o, A, W, out, R, N, K, E, lda, ldw, ldc, epi, gtab, gnum, bn, grid_tiles, status, stream,
+                           nullptr, 1, nullptr, nullptr, nullptr, wait_flag, wait_target, wait_limit_ns, per_expert);
 }
 
 // As ib_gemm_grouped_wait with the arrival wait bounded by wait_limit_ns

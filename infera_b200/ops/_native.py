@@ -111,6 +111,12 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
                                      c_vp],
         "ib_ep_dispatch_q": [c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int,
                              c_vp, c_vp, c_vp],
+        "ib_ep_dispatch_ex": [c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+        "ib_ep_dispatch_q_ex": [c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int,
+                                c_vp, c_vp, c_vp, c_vp, c_vp],
+        "ib_gemm_grouped_wait_ex": [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int,
+                                    c_int, c_int, c_vp, c_vp, c_int, c_int, c_vp, c_uint, c_int, ctypes.c_ulonglong,
+                                    c_vp, c_vp],
         "ib_gemm_set_trace": [c_vp],
         "ib_attn_prefill_set_trace": [c_vp],
         "ib_mla_rope_kvwrite": [c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_float, c_vp, c_vp],

@@ -23,8 +23,13 @@ Two data paths:
   destination's receive buffer at its [local expert][source] place (no
   regroup on the receiver; fp8 experts: the sender quantises and
   ``ib_ep_dispatch_q`` moves e4m3 rows with their scale columns), the up
-  projection (``ib_gemm_grouped_wait``) waits for the arrivals inside its
-  own TMA producer, and the down projection's epilogue
+  projection waits for the arrivals inside its own TMA producer - per
+  local expert: the dispatch bumps a counter of expert e on its
+  destination once its last row of e has landed, and the up projection
+  (``ib_gemm_grouped_wait_ex``) waits on that counter before each of e's
+  tiles, so a lightly loaded expert's tiles start before a heavy one's
+  rows are in (one round counter with ``INFERA_EP_PER_EXPERT=0``) - and
+  the down projection's epilogue
   (``ib_gemm_grouped_push``) stores each expert-output row straight back
   at its source's sorted row; arrival counters with bounded waits
   separate the phases, and nothing is read back to the host.
@@ -44,7 +49,10 @@ from infera_b200.models.moe import MoELayer
 from infera_b200.ops import _native
 from infera_b200.ops import kernels as K
 
-FLAGS = 256  # two u32 arrival counters, padded
+# two u32 round counters at 0 / 4, then one u32 arrival counter per local
+# expert from byte 64 (up to 240 local experts), padded
+FLAGS = 1024
+EFLAG_OFF = 64
 
 
 class EPMoE:
@@ -76,6 +84,9 @@ class EPMoE:
             self.w2 = full.w2[lo:hi].to(dev).contiguous()
         self.shared = None if full.shared is None else tuple(t.to(dev) for t in full.shared)
         self.stats = {"sent_rows": 0, "recv_rows": 0}
+        import os
+
+        self.per_expert = os.environ.get("INFERA_EP_PER_EXPERT", "1") != "0"
         self.device = dev
         self.fused = fused and dev.type == "cuda"
         if self.fused:
@@ -110,11 +121,18 @@ class EPMoE:
             self.peers.append(q.value)
         self.round = 0
         self.ctr = torch.zeros(4, dtype=torch.int32, device=self.device)  # done counters of the two phases
+        if self.El * 4 > FLAGS - EFLAG_OFF:
+            self.per_expert = False
+        # per-expert rows stored so far this round (zeroed by the dispatch)
+        self.local_done = torch.zeros(self.E, dtype=torch.int32, device=self.device)
         W, E = self.world, self.E
         self.counts_all = torch.zeros(W * E, dtype=torch.int32, device=self.device)
         self.offs = torch.zeros(E + self.El + 1 + W * E, dtype=torch.int32, device=self.device)
         self.row_map = torch.zeros(max_rows, dtype=torch.int32, device=self.device)
         dist.barrier(group=gloo_group)
+
+    def _local_done(self):
+        return ctypes.c_void_p(self.local_done.data_ptr()) if self.per_expert else None
 
     def _recv_view(self, base: int) -> int:
         return base + FLAGS
@@ -155,6 +173,7 @@ class EPMoE:
         target = self.round * W
         recv_peers = (ctypes.c_void_p * 8)(*[self._recv_view(b) for b in self.peers])
         flagA = (ctypes.c_void_p * 8)(*[b for b in self.peers])
+        eflags = (ctypes.c_void_p * 8)(*[b + EFLAG_OFF for b in self.peers]) if self.per_expert else None
         ctr = self.ctr.data_ptr()
         bn = K.grouped_bn(R, El)
         if self.fp8:
@@ -165,16 +184,17 @@ class EPMoE:
             # rows land with their scales where the up projection reads them
             q, qsf = fp8.quant_act(xs)
             sf_peers = (ctypes.c_void_p * 8)(*[self._sf_view(b) for b in self.peers])
-            _native.check(lib.ib_ep_dispatch_q(q.data_ptr(), R, H, qsf.data_ptr(), qsf.stride(0), H // 128,
-                                               offsets.data_ptr(), E, W, dst_off.data_ptr(), recv_peers, sf_peers,
-                                               self.max_rows, flagA, ctypes.c_void_p(ctr), stream),
-                          "ib_ep_dispatch_q")
+            _native.check(lib.ib_ep_dispatch_q_ex(q.data_ptr(), R, H, qsf.data_ptr(), qsf.stride(0), H // 128,
+                                                  offsets.data_ptr(), E, W, dst_off.data_ptr(), recv_peers, sf_peers,
+                                                  self.max_rows, flagA, eflags, self._local_done(),
+                                                  ctypes.c_void_p(ctr), stream), "ib_ep_dispatch_q_ex")
             w13, w13sf, ldw13 = self.w13.q.data_ptr(), self.w13.sf.data_ptr(), self.w13.q.stride(0)
             a13, sf13 = self._recv_view(self.base), self._sf_view(self.base)
             n13 = self.w13.q.shape[0] // El
         else:
-            _native.check(lib.ib_ep_dispatch(xs.data_ptr(), R, H, offsets.data_ptr(), E, W, dst_off.data_ptr(),
-                                             recv_peers, flagA, ctypes.c_void_p(ctr), stream), "ib_ep_dispatch")
+            _native.check(lib.ib_ep_dispatch_ex(xs.data_ptr(), R, H, offsets.data_ptr(), E, W, dst_off.data_ptr(),
+                                                recv_peers, flagA, eflags, self._local_done(), ctypes.c_void_p(ctr),
+                                                stream), "ib_ep_dispatch_ex")
             w13, w13sf, ldw13 = self.w13.data_ptr(), None, self.w13.stride(1)
             a13, sf13 = self._recv_view(self.base), None
             n13 = self.w13.shape[1]
@@ -182,10 +202,12 @@ class EPMoE:
         # scale stagers wait for the dispatch's arrivals themselves
         tab, num, cap = K.grouped_tiles(loc_off, El, n13, bn, self.max_rows)
         act = torch.empty(self.max_rows, n13 // 2, dtype=torch.bfloat16, device=x.device)
-        _native.check(lib.ib_gemm_grouped_wait(a13, sf13, self.max_rows, w13, w13sf, act.data_ptr(), self.max_rows,
-                                               n13, H, El, H, ldw13, act.stride(0), 1,
-                                               tab.data_ptr(), num.data_ptr(), bn, cap, ctypes.c_void_p(self.base),
-                                               target, sc.status.data_ptr(), stream), "ib_gemm_grouped_wait")
+        wflag = self.base + (EFLAG_OFF if self.per_expert else 0)
+        _native.check(lib.ib_gemm_grouped_wait_ex(a13, sf13, self.max_rows, w13, w13sf, act.data_ptr(), self.max_rows,
+                                                  n13, H, El, H, ldw13, act.stride(0), 1,
+                                                  tab.data_ptr(), num.data_ptr(), bn, cap, ctypes.c_void_p(wflag),
+                                                  target, 1 if self.per_expert else 0, 0, sc.status.data_ptr(),
+                                                  stream), "ib_gemm_grouped_wait_ex")
         # down projection whose epilogue stores each expert-output row straight
         # into its source's return buffer (the return all-to-all fused in)
         _native.check(lib.ib_ep_row_map(self.counts_all.data_ptr(), W, E, self.rank, loc_off.data_ptr(),
