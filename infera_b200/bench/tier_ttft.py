@@ -28,6 +28,8 @@ import time
 
 import torch
 
+from infera_b200.ops import kernels as K
+
 
 def _mem_available_gib() -> float:
     try:
@@ -106,6 +108,7 @@ def main(argv=None) -> None:
         "ttft_tier_hit_s": round(tier_t, 3), "tier_hit_cached_tokens": tier_cached,
         "speedup_tier_hit_vs_cold": round(sum(cold) / len(cold) / tier_t, 2) if tier_t else None,
         "tier_loads": st.get("loads", 0) - loads0, "tier_stats": st, "init_s": round(init_s, 1),
+        "kernel_status": K.scratch(eng.device).read_status() if eng.device.type == "cuda" else 0,
         "timing": "host clock, each step synchronises on its sampled tokens", "data": "synthetic random tokens",
     }
     eng.tier.close()
