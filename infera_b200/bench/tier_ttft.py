@@ -68,6 +68,8 @@ def main(argv=None) -> None:
     ap.add_argument("--sessions", type=int, default=3)
     ap.add_argument("--hbm-kv-gb", type=float, default=40.0, help="HBM KV pool cap (GB)")
     ap.add_argument("--host-gb", type=float, default=64.0, help="host tier capacity (GiB), clamped to RAM / 2")
+    ap.add_argument("--tier", choices=("pinned", "host"), default="pinned",
+                    help="pinned: page-locked arena of page slots (DMA both ways); host: store of packed blobs")
     ap.add_argument("--max-batched-tokens", type=int, default=8192)
     ap.add_argument("--device", default="cuda:0")
     ap.add_argument("--seed", type=int, default=0)
@@ -81,7 +83,7 @@ def main(argv=None) -> None:
     num_pages = int(a.hbm_kv_gb * 1e9 // page_bytes)
     host_gib = min(a.host_gb, 0.5 * _mem_available_gib())
     cfg = EngineConfig(model=a.model, num_pages=num_pages, max_num_seqs=4, max_batched_tokens=a.max_batched_tokens,
-                       use_cuda_graphs=False, kv_tier=f"host:{host_gib:.2f}", seed=a.seed)
+                       use_cuda_graphs=False, kv_tier=f"{a.tier}:{host_gib:.2f}", seed=a.seed)
     t_init = time.time()
     eng = LLMEngine(cfg, device=a.device)
     init_s = time.time() - t_init
@@ -102,12 +104,15 @@ def main(argv=None) -> None:
     out = {
         "metric": "TTFT on a KV-tier hit vs full recompute (one engine, HBM KV pool capped)",
         "model": a.model, "prefix_tokens": a.prefix, "increment": a.increment, "hbm_kv_gb": a.hbm_kv_gb,
-        "num_pages": num_pages, "host_tier_gib": round(host_gib, 1), "kv_bytes_per_token": page_bytes // 16,
+        "num_pages": num_pages, "host_tier": a.tier, "host_tier_gib": round(host_gib, 1),
+        "kv_bytes_per_token": page_bytes // 16,
         "ttft_cold_s": [round(x, 3) for x in cold],
         "ttft_hbm_hit_s": round(hbm_t, 3), "hbm_hit_cached_tokens": hbm_cached,
         "ttft_tier_hit_s": round(tier_t, 3), "tier_hit_cached_tokens": tier_cached,
         "speedup_tier_hit_vs_cold": round(sum(cold) / len(cold) / tier_t, 2) if tier_t else None,
         "tier_loads": st.get("loads", 0) - loads0, "tier_stats": st, "init_s": round(init_s, 1),
+        "promote_gbs": round(st.get("promoted", 0) * page_bytes * 16 / 16 / st["load_s"] / 1e9, 1)
+        if st.get("load_s") else None,
         "kernel_status": K.scratch(eng.device).read_status() if eng.device.type == "cuda" else 0,
         "timing": "host clock, each step synchronises on its sampled tokens", "data": "synthetic random tokens",
     }

@@ -31,6 +31,11 @@ def _tier_store(spec: str):
         from infera_b200.kvd.client import SyncKvdStore
 
         return SyncKvdStore(rest)
+    if kind == "pinned":
+        # one page-locked arena of page slots, copied to and from by DMA
+        from infera_b200.engine.pinned_store import PinnedPageStore
+
+        return PinnedPageStore(int(float(rest or 4) * (1 << 30)))
     if kind == "host":
         from infera_b200.kvd.store import HostStore
         from infera_b200.kvd.tablespace import Tablespace
@@ -65,7 +70,8 @@ class EngineConfig:
     mixed_prefill_tokens: int = 512
     max_model_len: int | None = None
     model_overrides: dict = field(default_factory=dict)
-    # KV tiering: None (off), "host:<GiB>[:<nvme dir>]" (in-process host store,
+    # KV tiering: None (off), "pinned:<GiB>" (in-process page-locked arena of
+    # page slots, DMA both ways), "host:<GiB>[:<nvme dir>]" (in-process host store,
     # optional NVMe tablespace), "host:<GiB>:files:<dir>" (NVMe tier of one
     # file per chunk under the reaper's budget) or "kvd:<socket path>"
     # (shared daemon)

@@ -23,6 +23,11 @@
   the step loop never blocks on a promote. With ``async_load=False``
   (tensor-parallel ranks, which must make the same scheduling decisions in
   lockstep) the same chunked copies run inline on the compute stream.
+* With a :class:`~infera_b200.engine.pinned_store.PinnedPageStore` (spec
+  ``pinned:<GiB>``) the host tier is one page-locked arena of page slots:
+  a save copies each staging slot straight into the slot reserved for its
+  block (committed once the copy landed) and a promote copies the slot
+  straight into device staging, so no page passes through Python.
 * Every block the tiers gain or lose is reported through ``index_sink``
   (the engine's tier-aware KV index feed).
 
@@ -43,6 +48,7 @@ import numpy as np
 import torch
 
 from infera_b200.engine.packed_format import ChunkHeader, PackedFormatError, pack_chunk, unpack_chunk
+from infera_b200.engine.pinned_store import PinnedPageStore
 from infera_b200.kv.types import Tier
 from infera_b200.ops import kernels as K
 
@@ -102,6 +108,9 @@ class TierManager:
         self.stats = {"saved": 0, "save_dropped": 0, "save_batches": 0, "promoted": 0, "lookups": 0,
                       "loads": 0, "load_s": 0.0}
         self._save_q: queue.Queue = queue.Queue()
+        self.pinned = store if isinstance(store, PinnedPageStore) else None
+        if self.pinned is not None:
+            self.pinned.bind(self.elems, dt, pin=pin)
         self._writer_t = threading.Thread(target=self._writer, daemon=True, name="kv-tier-writer")
         self._writer_t.start()
         self._load_q: queue.Queue = queue.Queue()
@@ -162,6 +171,15 @@ class TierManager:
         return queued
 
     def _issue_saves(self, take: list[tuple[int, int]]) -> None:
+        arena_slots = None
+        if self.pinned is not None:
+            res = self.pinned.reserve([self._key(h) for _, h in take])
+            kept = [(t, a) for t, a in zip(take, res) if a is not None and a >= 0]
+            self.stats["save_dropped"] += sum(1 for a in res if a is not None and a < 0)
+            if not kept:
+                return
+            take = [t for t, _ in kept]
+            arena_slots = [a for _, a in kept]
         with self._lock:
             start = self.save_head
             self.save_inflight += len(take)
@@ -182,26 +200,39 @@ class TierManager:
             gathered.record()
             with torch.cuda.stream(self.side):
                 self.side.wait_event(gathered)
-                for s0, cnt in segs:
-                    self.save_host[s0:s0 + cnt].copy_(self.save_dev[s0:s0 + cnt], non_blocking=True)
+                if arena_slots is None:
+                    for s0, cnt in segs:
+                        self.save_host[s0:s0 + cnt].copy_(self.save_dev[s0:s0 + cnt], non_blocking=True)
+                else:   # straight into the arena slots reserved for the blocks
+                    arena = self.pinned.arena
+                    for ring, a in zip(slots, arena_slots):
+                        arena[a].copy_(self.save_dev[ring], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(self.side)
         else:
             for s0, cnt in segs:
                 K.kv_page_copy(self.k, self.v, self.save_host[s0:s0 + cnt], self.save_idx_host[s0:s0 + cnt],
                                self.ps, gather=True, page_major=True)
+            if arena_slots is not None:
+                for ring, a in zip(slots, arena_slots):
+                    self.pinned.arena[a].copy_(self.save_host[ring])
         self.stats["save_batches"] += 1
-        self._save_q.put((slots, [h for _, h in take], ev))
+        self._save_q.put((slots, [h for _, h in take], ev, arena_slots is not None))
 
     def _writer(self) -> None:
         while True:
             job = self._save_q.get()
             if job is None:
                 return
-            slots, hashes, ev = job
+            slots, hashes, ev, in_arena = job
             if ev is not None:
                 ev.synchronize()
             stored = []
+            if in_arena:        # the pages already sit in their arena slots
+                done = set(self.pinned.commit([self._key(h) for h in hashes]))
+                stored = [h for h in hashes if self._key(h) in done]
+                self.stats["saved"] += len(stored)
+                hashes = []
             for slot, h in zip(slots, hashes):
                 try:
                     blob = pack_chunk(self.header, memoryview(self.save_host_u8[slot]))
@@ -302,6 +333,32 @@ class TierManager:
             m += 1
         return m, checks
 
+    def _fill_pinned(self, buf: int, pages: list[int], hashes: list[int], stream) -> int:
+        """Arena slots of the leading run of held blocks, copied straight to
+        the device staging buffer (one DMA per page) and scattered into the
+        pages; the slots stay pinned until the copies have landed."""
+        slots = self.pinned.acquire([self._key(h) for h in hashes])
+        m = len(slots)
+        if not m:
+            return 0
+        arena = self.pinned.arena
+        try:
+            if self.on_gpu:
+                with torch.cuda.stream(stream):
+                    for i, a in enumerate(slots):
+                        self.load_dev[buf, i].copy_(arena[a], non_blocking=True)
+            else:
+                for i, a in enumerate(slots):
+                    self.load_host[buf, i].copy_(arena[a])
+            self.load_idx_np[buf, :m] = pages[:m]
+            self._scatter(buf, m, stream, staged=False)
+            self.load_buf ^= 1
+            if self.on_gpu:
+                self.load_ev[buf].synchronize()
+        finally:
+            self.pinned.release(slots)
+        return m
+
     def _scatter(self, buf: int, m: int, stream, staged: bool = True) -> None:
         if self.on_gpu:
             with torch.cuda.stream(stream):
@@ -326,7 +383,9 @@ class TierManager:
                 self.load_ev[buf].synchronize()      # that buffer's previous copies have landed
                 self.load_ev[buf] = None
             want = pages[c0:c0 + self.load_chunk]
-            if self.arena_t is not None and hasattr(self.store, "read_shared"):
+            if self.pinned is not None:
+                m = self._fill_pinned(buf, want, hashes[c0:c0 + self.load_chunk], stream)
+            elif self.arena_t is not None and hasattr(self.store, "read_shared"):
                 m, checks = self._fill_direct(buf, want, hashes[c0:c0 + self.load_chunk], stream)
                 if m:
                     self._scatter(buf, m, stream, staged=False)

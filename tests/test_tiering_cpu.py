@@ -39,13 +39,15 @@ def test_kv_page_copy_roundtrip():
     assert torch.equal(k2[:, 48:64], k[:, 48:64]) and torch.equal(v2[:, 16:32], v[:, 16:32])
 
 
-@pytest.mark.parametrize("async_load", [True, False])
-def test_engine_tier_save_and_promote(async_load):
+@pytest.mark.parametrize("async_load,spec", [(True, "host:0.05"), (False, "host:0.05"), (True, "pinned:0.05"),
+                                              (False, "pinned:0.05")])
+def test_engine_tier_save_and_promote(async_load, spec):
     """Asynchronous promote: the request waits (parked) while the loader
     copies its prefix in, the engine keeps stepping; inline promote: the
-    copies are issued at admission."""
+    copies are issued at admission. Both host tiers: packed blobs, and the
+    arena of page slots written and read by copy."""
     eng = LLMEngine(EngineConfig(model="tiny-dense", use_cuda_graphs=False, num_pages=12, max_batched_tokens=256,
-                                 kv_tier="host:0.05", kv_tier_async=async_load), device="cpu")
+                                 kv_tier=spec, kv_tier_async=async_load), device="cpu")
     g = torch.Generator().manual_seed(4)
     a = torch.randint(0, 1000, (64,), generator=g).tolist()
     sp = SamplingParams(max_tokens=2, ignore_eos=True)
@@ -121,3 +123,25 @@ def test_tier_ttft_bench_cpu(capsys):
     d = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert d["tier_loads"] >= 1 and d["tier_hit_cached_tokens"] >= 384
     assert d["hbm_hit_cached_tokens"] >= 384 and len(d["ttft_cold_s"]) == 3
+
+
+def test_pinned_store_lru_pins_and_listeners():
+    from infera_b200.engine.pinned_store import PinnedPageStore
+
+    st = PinnedPageStore(capacity_bytes=3 * 64)
+    st.bind(32, torch.bfloat16, pin=False)                 # 64-byte pages: 3 slots
+    dropped = []
+    st.add_listener(lambda k, spilled: dropped.append(k))
+    a = st.reserve([b"a", b"b", b"c"])
+    assert sorted(a) == [0, 1, 2] and not st.exists(b"a")  # reserved: invisible
+    assert st.commit([b"a", b"b", b"c"]) == [b"a", b"b", b"c"]
+    assert st.reserve([b"a"]) == [None]                    # already held
+    pinned = st.acquire([b"a"])                            # a is read: refreshed and pinned
+    assert st.reserve([b"d"]) != [-1] and dropped == [b"b"]
+    st.commit([b"d"])
+    st.reserve([b"e"])                                     # c goes (a is pinned)
+    assert dropped == [b"b", b"c"]
+    st.commit([b"e"])
+    assert st.reserve([b"f"]) != [-1] and dropped[-1] == b"d"  # a is the oldest but pinned: d goes
+    st.release(pinned)
+    assert st.exists_many([b"a", b"d", b"e"]) == [True, False, True]

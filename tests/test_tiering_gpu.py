@@ -43,10 +43,13 @@ def _first_logits(eng, rid, prompt):
     raise AssertionError("no token")
 
 
-def test_tier_evict_save_and_async_promote_match_recompute():
+@pytest.mark.parametrize("spec", ["host:1", "pinned:1"])
+def test_tier_evict_save_and_async_promote_match_recompute(spec):
+    """Both host tiers: packed blobs, and the page-locked arena of page slots
+    written and read by DMA."""
     g = torch.Generator().manual_seed(11)
     a = torch.randint(0, 4000, (320,), generator=g).tolist()          # 20 full pages
-    eng = _engine(kv_tier="host:1")
+    eng = _engine(kv_tier=spec)
     sp = SamplingParams(max_tokens=2, ignore_eos=True)
     eng.generate([a], sp)
     hashes = chain_hashes(a, 16)[:19]
