@@ -81,6 +81,7 @@ __device__ __forceinline__ uint32_t qp_offset(int row, int k) {
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                     const __grid_constant__ CUtensorMap tmK8, const __grid_constant__ CUtensorMap tmV8,
                      const Params p) {
   const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int G = p.G;
@@ -145,6 +146,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmK8);
+    tma_prefetch_desc(&tmV8);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -175,19 +178,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                        kStatusTimeoutEmpty))
           break;
         uint8_t* base = sKV + st * 4 * BLK;
-        mbar_expect_tx(&k_full[st], 2 * BLK);
+        // eight consecutive pages are one 128-row box per half (the 128-byte
+        // swizzle repeats every 8 rows, so the shared-memory image is the
+        // same as eight page boxes)
+        bool run = true;
 #pragma unroll
-        for (int pg = 0; pg < BKV / PAGE; ++pg) {
-          const int row = cur[pg] * PAGE;
-          tma_load_2d(base + pg * PAGE * 128, &tmK, &k_full[st], kvh * D, row, pol);
-          tma_load_2d(base + BLK + pg * PAGE * 128, &tmK, &k_full[st], kvh * D + 64, row, pol);
+        for (int pg = 1; pg < BKV / PAGE; ++pg) run = run && cur[pg] == cur[0] + pg;
+        mbar_expect_tx(&k_full[st], 2 * BLK);
+        if (run) {
+          tma_load_2d(base, &tmK8, &k_full[st], kvh * D, cur[0] * PAGE, pol);
+          tma_load_2d(base + BLK, &tmK8, &k_full[st], kvh * D + 64, cur[0] * PAGE, pol);
+        } else {
+#pragma unroll
+          for (int pg = 0; pg < BKV / PAGE; ++pg) {
+            const int row = cur[pg] * PAGE;
+            tma_load_2d(base + pg * PAGE * 128, &tmK, &k_full[st], kvh * D, row, pol);
+            tma_load_2d(base + BLK + pg * PAGE * 128, &tmK, &k_full[st], kvh * D + 64, row, pol);
+          }
         }
         mbar_expect_tx(&v_full[st], 2 * BLK);
+        if (run) {
+          tma_load_2d(base + 2 * BLK, &tmV8, &v_full[st], kvh * D, cur[0] * PAGE, pol);
+          tma_load_2d(base + 3 * BLK, &tmV8, &v_full[st], kvh * D + 64, cur[0] * PAGE, pol);
+        } else {
 #pragma unroll
-        for (int pg = 0; pg < BKV / PAGE; ++pg) {
-          const int row = cur[pg] * PAGE;
-          tma_load_2d(base + 2 * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * D, row, pol);
-          tma_load_2d(base + 3 * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * D + 64, row, pol);
+          for (int pg = 0; pg < BKV / PAGE; ++pg) {
+            const int row = cur[pg] * PAGE;
+            tma_load_2d(base + 2 * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * D, row, pol);
+            tma_load_2d(base + 3 * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * D + 64, row, pol);
+          }
         }
         ++issued;
       }
@@ -453,9 +472,11 @@ extern "C" int ib_attn_decode_tc_ex(const void* q, int ldq, const void* k_cache,
   if (hkv <= 0 || hq % hkv != 0 || hq / hkv > MAXG || splits < 1 || (ldq % 2) != 0) return -1;
   if (splits > 1 && (o_part == nullptr || lse_part == nullptr)) return -1;
   const int kvw = hkv * D;
-  CUtensorMap tk, tv;
+  CUtensorMap tk, tv, tk8, tv8;
   if (!cached_tmap_2d(&tk, k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, kvw, kvw, 16, 64)) return -2;
   if (!cached_tmap_2d(&tv, v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, kvw, kvw, 16, 64)) return -2;
+  if (!cached_tmap_2d(&tk8, k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, kvw, kvw, 128, 64)) return -2;
+  if (!cached_tmap_2d(&tv8, v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, kvw, kvw, 128, 64)) return -2;
   Params p;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.ldq = ldq;
@@ -483,7 +504,7 @@ extern "C" int ib_attn_decode_tc_ex(const void* q, int ldq, const void* k_cache,
     attr_set[dev] = true;
   }
   dim3 grid(B, hkv, splits);
-  decode_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tk, tv, p);
+  decode_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tk, tv, tk8, tv8, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return static_cast<int>(e);
   if (splits > 1) {

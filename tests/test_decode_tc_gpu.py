@@ -48,3 +48,32 @@ def test_decode_tc(hq, hkv, lens, splits):
     torch.cuda.synchronize()
     assert K.scratch().read_status() == 0
     assert _rel(out.cpu(), ref) < 2e-2
+
+
+@pytest.mark.parametrize("lens,splits", [([1000, 129, 2048], 1), ([5000, 77], 4)])
+def test_decode_tc_consecutive_pages(lens, splits):
+    """Eight consecutive pages load as one 128-row box per half; runs that
+    start mid-tile, partial last tiles and a break inside a tile take the
+    page-by-page path."""
+    hq, hkv = 32, 8
+    g = torch.Generator().manual_seed(21)
+    width = max((n + 15) // 16 for n in lens) + 2
+    pages = len(lens) * width + 8
+    bt = torch.zeros(len(lens), width, dtype=torch.int32)
+    start = 3
+    for i, n in enumerate(lens):
+        np_ = (n + 15) // 16
+        bt[i, :np_] = torch.arange(start, start + np_, dtype=torch.int32)
+        start += np_ + 1
+    bt[0, 10] = pages - 1          # one page out of line inside the first sequence's second tile
+    kc = torch.randn(pages * 16, hkv * 128, generator=g).to(torch.bfloat16)
+    vc = torch.randn(pages * 16, hkv * 128, generator=g).to(torch.bfloat16)
+    q = torch.randn(len(lens), (hq + 2 * hkv) * 128, generator=g).to(torch.bfloat16)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    scale = 1 / math.sqrt(128)
+    ref = K.attn_decode(q, kc, vc, bt, sl, hq, hkv, scale)
+    out = K.attn_decode(q.cuda(), kc.cuda(), vc.cuda(), bt.cuda(), sl.cuda(), hq, hkv, scale, splits=splits,
+                        impl="tc")
+    torch.cuda.synchronize()
+    assert K.scratch().read_status() == 0
+    assert _rel(out.cpu(), ref) < 2e-2
