@@ -116,6 +116,7 @@ struct Params {
   unsigned int wait_target;
   uint64_t wait_limit_ns;   // bound of that wait (0: kWaitLimitNs)
   int wait_per_expert;      // grouped: wait_flag[e] per local expert, waited before each of e's tiles
+  int streamk;              // each CTA takes an equal share of all (tile, k-block) steps (fp32 atomic epilogue)
 };
 
 // Bounded wait for the dispatch's arrival counter (release-incremented by
@@ -166,6 +167,44 @@ __device__ __forceinline__ void tile_coords(const Params& p, int t, int& pt, int
   int rest = t / p.splits;
   pt = rest % p.p_tiles;
   qt = rest / p.p_tiles;
+}
+
+// The (tile, k-block range) segments one CTA works through, in order: tiles
+// blockIdx.x, +gridDim.x with their split-K share, or (stream-K) one equal
+// contiguous share of all tiles x k-blocks, cut at tile boundaries. Every
+// role walks the same sequence.
+struct SegIter {
+  long long k, hi;
+  int t;
+};
+
+__device__ __forceinline__ void seg_begin(const Params& p, int total, SegIter& it) {
+  if (p.streamk) {
+    const long long all = static_cast<long long>(total) * p.nkb;
+    it.k = all * blockIdx.x / gridDim.x;
+    it.hi = all * (blockIdx.x + 1) / gridDim.x;
+  } else {
+    it.t = blockIdx.x;
+  }
+}
+
+__device__ __forceinline__ bool seg_next(const Params& p, int total, SegIter& it, int& t, int& kb0, int& kb1) {
+  if (p.streamk) {
+    if (it.k >= it.hi) return false;
+    t = static_cast<int>(it.k / p.nkb);
+    kb0 = static_cast<int>(it.k % p.nkb);
+    kb1 = static_cast<int>(min(static_cast<long long>(p.nkb), kb0 + (it.hi - it.k)));
+    it.k += kb1 - kb0;
+    return true;
+  }
+  if (it.t >= total) return false;
+  t = it.t;
+  it.t += gridDim.x;
+  int pt, qt, sp;
+  tile_coords(p, t, pt, qt, sp);
+  kb0 = sp * p.kbps;
+  kb1 = min(kb0 + p.kbps, p.nkb);
+  return true;
 }
 
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
@@ -390,15 +429,16 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       long long issued = 0;
       // one wait for the whole round, or per tile on the tile's expert
       bool ok = p.wait_per_expert ? true : wait_arrivals(p, abort_flag);
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      SegIter it;
+      seg_begin(p, total, it);
+      int t, kb0, kb1;
+      while (ok && seg_next(p, total, it, t, kb0, kb1)) {
         int pt, qt, sp;
         tile_coords(p, t, pt, qt, sp);
         if (p.wait_per_expert && !wait_arrivals(p, abort_flag, p.gtab[t].x)) {
           ok = false;
           break;
         }
-        const int kb0 = sp * p.kbps;
-        const int kb1 = min(kb0 + p.kbps, p.nkb);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) {
             ok = false;
@@ -430,11 +470,10 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       int local = 0;
       bool ok = true;
       long long steps = 0;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
-        int pt, qt, sp;
-        tile_coords(p, t, pt, qt, sp);
-        const int kb0 = sp * p.kbps;
-        const int kb1 = min(kb0 + p.kbps, p.nkb);
+      SegIter it;
+      seg_begin(p, total, it);
+      int t, kb0, kb1;
+      for (; ok && seg_next(p, total, it, t, kb0, kb1); ++local) {
         const uint32_t acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status, kStatusTimeoutTmemEmpty)) break;
@@ -576,7 +615,10 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = q * 32 + lane;
     int local = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
+    SegIter it;
+    seg_begin(p, total, it);
+    int t, kb0, kb1;
+    for (; seg_next(p, total, it, t, kb0, kb1); ++local) {
       int pt, qt, sp;
       tile_coords(p, t, pt, qt, sp);
       const uint32_t acc = local & 1;
@@ -807,6 +849,19 @@ inline Plan make_plan(int M, int N, int K, int num_sms, int force_split) {
     p.q_tiles = (N + MAX_BN - 1) / MAX_BN;
   }
   choose_splits(pl, num_sms, force_split);
+  // Stream-K when whole tiles would leave most of the last wave idle (e.g.
+  // 224 weight tiles of a 64-token decode GEMM on 148 SMs: 2 waves for 1.51
+  // waves of work): every CTA takes 1/num_sms of all k-steps, partial tiles
+  // meet in the fp32 workspace.
+  const int tiles = p.p_tiles * p.q_tiles;
+  if (force_split == 0 && p.splits == 1 && tiles >= num_sms && tiles < 4 * num_sms && p.nkb >= 8 &&
+      (p.N % 4) == 0) {
+    const int waves = (tiles + num_sms - 1) / num_sms;
+    if (static_cast<double>(tiles) / (waves * num_sms) < 0.85) {
+      p.streamk = 1;
+      pl.grid = num_sms;
+    }
+  }
   return pl;
 }
 
@@ -874,7 +929,8 @@ inline int run_dense(const Operands& o, const void* A, const void* W, void* out,
   p.done_ctr = nullptr;
   p.grouped = 0;
   set_scales(p, o);
-  const bool split = p.splits > 1;
+  if (ws == nullptr) p.streamk = 0;
+  const bool split = p.splits > 1 || p.streamk;
   p.epi = split ? EPI_ATOMIC_F32 : epi;
   p.out = split ? static_cast<void*>(ws) : out;
   CUtensorMap tmP, tmQ;
@@ -903,6 +959,7 @@ inline int run_push(const Operands& o, const void* A, const void* W, int M, int 
   const int fs = ws == nullptr ? 1 : 0;
   Plan pl = o.fp8 ? make_plan_fp8(M, N, K, num_sms, fs) : make_plan(M, N, K, num_sms, fs);
   Params& p = pl.p;
+  p.streamk = 0;  // peer-store epilogues write whole tiles
   const bool split = p.splits > 1;
   p.status = status;
   p.ldc = split ? N : ldc;
@@ -1143,7 +1200,9 @@ extern "C" void ib_gemm_bf16_plan(int M, int N, int K, int num_sms, int force_sp
   out7[1] = pl.p.bn;
   out7[2] = pl.p.p_tiles;
   out7[3] = pl.p.q_tiles;
-  out7[4] = pl.p.splits;
+  // a stream-K plan needs the split-K workspace and finalize pass too: it
+  // reports splits = -1
+  out7[4] = pl.p.streamk ? -1 : pl.p.splits;
   out7[5] = pl.p.kbps;
   out7[6] = pl.grid;
 }

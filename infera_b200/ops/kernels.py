@@ -98,7 +98,8 @@ def _count(n: int = 1) -> None:
     LAUNCHES[0] += n
 
 
-def _gemm_splits(M: int, N: int, K: int, force_split: int = 0) -> int:
+def _gemm_plan_splits(M: int, N: int, K: int, force_split: int = 0) -> int:
+    """The plan's split-K factor, or -1 for a stream-K plan."""
     key = (M, N, K, force_split)
     v = _plan_cache.get(key)
     if v is None:
@@ -107,8 +108,20 @@ def _gemm_splits(M: int, N: int, K: int, force_split: int = 0) -> int:
     return v
 
 
+def _gemm_splits(M: int, N: int, K: int, force_split: int = 0) -> int:
+    """K splits of the plan (1 for stream-K, whose shares are uneven)."""
+    return max(1, _gemm_plan_splits(M, N, K, force_split))
+
+
+def _gemm_ws(M: int, N: int, K: int, force_split: int = 0) -> bool:
+    """Whether the plain GEMM accumulates in the fp32 workspace (split-K or
+    stream-K) and runs the finalize pass."""
+    v = _gemm_plan_splits(M, N, K, force_split)
+    return v > 1 or v < 0
+
+
 def _gemm_launches(M: int, N: int, K: int, force_split: int = 0) -> int:
-    return 1 + (1 if _gemm_splits(M, N, K, force_split) > 1 else 0)
+    return 1 + (1 if _gemm_ws(M, N, K, force_split) else 0)
 
 
 _NUM_SMS: list[int] = []
@@ -168,8 +181,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, sw
     if out is None:
         out = torch.empty(M, n_out, dtype=torch.bfloat16, device=x.device)
     sc = scratch(x.device)
-    splits = _gemm_splits(M, N, K, force_split)
-    ws = sc.ensure_gemm(M * N if splits > 1 else 1)
+    ws = sc.ensure_gemm(M * N if _gemm_ws(M, N, K, force_split) else 1)
     rc = _native.kernels().ib_gemm_bf16(x.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, K, x.stride(0),
                                         w.stride(0), out.stride(0), 1 if swiglu else 0, ws.data_ptr(),
                                         force_split, sc.status.data_ptr(), _stream())

@@ -55,6 +55,23 @@ def test_gemm_swiglu(M, force_split):
     assert float(K.scratch().gemm_ws.abs().sum()) == 0.0
 
 
+@pytest.mark.parametrize("M,swiglu", [(1, True), (64, True), (64, False), (128, False)])
+def test_gemm_stream_k(M, swiglu):
+    """224 weight tiles on 148 SMs: every CTA takes an equal share of the
+    k-steps, partial tiles meet in the fp32 workspace (left zeroed)."""
+    torch.manual_seed(4)
+    N, K_ = 28672, 4096
+    assert K.gemm_plan(M, N, K_)["splits"] == -1
+    x = (torch.randn(M, K_, device=DEV) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K_, device=DEV) / math.sqrt(K_)).to(torch.bfloat16)
+    y = K.linear(x, w, swiglu=swiglu)
+    torch.cuda.synchronize()
+    _check_status()
+    ref = K.linear(x.cpu(), w.cpu(), swiglu=swiglu)
+    assert _rel_err(y.cpu(), ref) < 1e-2
+    assert float(K.scratch().gemm_ws.abs().sum()) == 0.0
+
+
 def test_gemm_repeated_split_consistent():
     torch.manual_seed(2)
     x = torch.randn(8, 4096, device=DEV).to(torch.bfloat16)
