@@ -75,7 +75,7 @@ def parse_args(argv=None):
     ap.add_argument("--tail", type=float, default=8.0,
                     help="seconds the trace keeps arriving after the timed window, for the window's arrivals "
                          "to finish (the goodput cohort is the requests that arrived in the window)")
-    ap.add_argument("--mixed-prefill-tokens", type=int, default=512,
+    ap.add_argument("--mixed-prefill-tokens", type=int, default=256,
                     help="prompt tokens per engine step while sequences are decoding")
     ap.add_argument("--model", default=MODEL)
     ap.add_argument("--max-num-seqs", type=int, default=128)

@@ -66,8 +66,10 @@ class EngineConfig:
     long_prefill_threshold: int = 0
     # prompt tokens per step while sequences are decoding: bounds the step
     # time that decoding sequences see as their inter-token latency (0: the
-    # whole max_batched_tokens budget)
-    mixed_prefill_tokens: int = 512
+    # whole max_batched_tokens budget). On the 8B agentic trace at 8 req/s,
+    # 256 gave ITL p99 19.1 ms / TTFT p50 48 ms against 22.0 ms / 37 ms for
+    # 512, both far inside the SLO
+    mixed_prefill_tokens: int = 256
     max_model_len: int | None = None
     model_overrides: dict = field(default_factory=dict)
     # KV tiering: None (off), "pinned:<GiB>" (in-process page-locked arena of

@@ -85,7 +85,7 @@ def parse_args(argv=None):
     p.add_argument("--page-size", type=int, default=16)
     p.add_argument("--max-num-seqs", type=int, default=128)
     p.add_argument("--max-batched-tokens", type=int, default=2048)
-    p.add_argument("--mixed-prefill-tokens", type=int, default=512,
+    p.add_argument("--mixed-prefill-tokens", type=int, default=256,
                    help="prompt tokens per step while sequences are decoding (0: no cap)")
     p.add_argument("--gpu-memory-utilization", type=float, default=0.90)
     p.add_argument("--num-pages", type=int, default=None)
