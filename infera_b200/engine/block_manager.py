@@ -51,7 +51,13 @@ class BlockManager:
         self.reserved = reserved_pages
         self.refcount = [0] * num_pages
         self.page_hash: list[int | None] = [None] * num_pages
+        # free never-hashed pages: a stack (lazily cleaned) plus the set that
+        # says which entries are still free; a sequence's next page is its
+        # last page + 1 when that one is free, so sequences hold runs of
+        # consecutive pages (the decode attention loads an 8-page run as one
+        # TMA box per half)
         self.free_plain: list[int] = list(range(num_pages - 1, reserved_pages - 1, -1))
+        self.free_set: set[int] = set(self.free_plain)
         self.evictable: OrderedDict[int, None] = OrderedDict()   # cached pages with refcount 0 (LRU order)
         self.hash_to_page: dict[int, int] = {}
         self.stats = {"hit_tokens": 0, "query_tokens": 0, "evictions": 0, "tier_hit_tokens": 0}
@@ -59,7 +65,7 @@ class BlockManager:
 
     # ------------------------------------------------------------------ capacity
     def num_free(self) -> int:
-        return len(self.free_plain) + len(self.evictable)
+        return len(self.free_set) + len(self.evictable)
 
     def usage(self) -> float:
         usable = self.num_pages - self.reserved
@@ -69,9 +75,30 @@ class BlockManager:
         return self.num_free() - watermark >= n
 
     # ------------------------------------------------------------------ allocation
-    def _take_page(self) -> int:
-        if self.free_plain:
-            return self.free_plain.pop()
+    def _push_free(self, page: int) -> None:
+        if page not in self.free_set:
+            self.free_set.add(page)
+            self.free_plain.append(page)
+            if len(self.free_plain) > 2 * len(self.free_set) + 1024:
+                # drop stale entries (pages taken as a run's next page),
+                # keeping each free page's latest position in the stack
+                seen: set[int] = set()
+                keep = []
+                for q in reversed(self.free_plain):
+                    if q in self.free_set and q not in seen:
+                        seen.add(q)
+                        keep.append(q)
+                self.free_plain = keep[::-1]
+
+    def _take_page(self, prev: int | None = None) -> int:
+        if prev is not None and prev + 1 in self.free_set:
+            self.free_set.discard(prev + 1)      # its stack entry is skipped when reached
+            return prev + 1
+        while self.free_plain:
+            page = self.free_plain.pop()
+            if page in self.free_set:
+                self.free_set.discard(page)
+                return page
         if not self.evictable:
             raise MemoryError("KV cache exhausted")
         page, _ = self.evictable.popitem(last=False)
@@ -93,7 +120,7 @@ class BlockManager:
                 self.evictable[page] = None
             else:
                 self.page_hash[page] = None
-                self.free_plain.append(page)
+                self._push_free(page)
 
     def _emit(self, kind: str, payload: dict) -> None:
         if self.event_sink is not None:
@@ -146,7 +173,7 @@ class BlockManager:
         sb = SeqBlocks(pages=list(hit_pages), hashes=list(hit_hashes),
                        num_cached_tokens=len(hit_pages) * self.page_size)
         for _ in range(max(0, need)):
-            p = self._take_page()
+            p = self._take_page(sb.pages[-1] if sb.pages else None)
             self.refcount[p] = 1
             sb.pages.append(p)
         if n_tier > 0:
@@ -171,7 +198,7 @@ class BlockManager:
         if self.num_free() < need:
             return False
         for _ in range(need):
-            p = self._take_page()
+            p = self._take_page(sb.pages[-1] if sb.pages else None)
             self.refcount[p] = 1
             sb.pages.append(p)
         return True
@@ -230,7 +257,7 @@ class BlockManager:
             if h is not None and self.hash_to_page.get(h) == page:
                 del self.hash_to_page[h]
             self.page_hash[page] = None
-            self.free_plain.append(page)
+            self._push_free(page)
         self.evictable.clear()
         self._emit("AllBlocksCleared", {})
 

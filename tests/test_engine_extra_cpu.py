@@ -116,3 +116,28 @@ def test_mixed_step_prefill_cap_while_decoding():
     ps = [_prompt(30 + i, 90 + 20 * i) for i in range(3)]
     sp = SamplingParams(max_tokens=5, ignore_eos=True)
     assert eng.generate(ps, sp) == ref.generate(ps, sp)
+
+
+def test_block_manager_keeps_sequences_in_page_runs():
+    """A sequence's next page is its last page + 1 when that one is free, so
+    pages come in consecutive runs even after other sequences freed theirs."""
+    from infera_b200.engine.block_manager import BlockManager
+
+    bm = BlockManager(num_pages=200, page_size=16, enable_prefix_cache=False)
+    a = bm.allocate_prompt(list(range(40 * 16)), 40 * 16)
+    b = bm.allocate_prompt(list(range(20 * 16)), 20 * 16)
+    assert a.pages == list(range(a.pages[0], a.pages[0] + 40))
+    bm.free(a)
+    c = bm.allocate_prompt(list(range(30 * 16)), 30 * 16)
+    assert c.pages == list(range(c.pages[0], c.pages[0] + 30))
+    assert bm.ensure_capacity(b, 28 * 16)            # b grows past its run end into free pages
+    runs = sum(1 for i in range(1, len(b.pages)) if b.pages[i] != b.pages[i - 1] + 1)
+    assert runs <= 1
+    free_before = bm.num_free()
+    bm.free(b)
+    bm.free(c)
+    assert bm.num_free() == free_before + 28 + 30 and bm.num_free() == 199
+    for _ in range(3000):                            # stale stack entries stay bounded
+        s = bm.allocate_prompt(list(range(33)), 33)
+        bm.free(s)
+    assert len(bm.free_plain) <= 2 * len(bm.free_set) + 1024
