@@ -28,6 +28,12 @@ import torch.distributed as dist
 from infera_b200.ops import kernels as K
 from infera_b200.parallel.comm import TPComm
 
+# roofline denominators measured on B200: copy bandwidth (read + write bytes),
+# bf16 GEMM burst rate, NVLink peer-copy rate per direction
+PEAK_HBM = 6418.2e9
+PEAK_BF16 = 1675.3e12
+PEAK_PEER = 770e9
+
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
@@ -151,8 +157,9 @@ def main(argv=None) -> None:
             flops = 2.0 * M * H * Ks
             w_bytes = H * Ks * 2
             push_bytes = (2 * (world - 1) / world if two else (world - 1)) * M * H * 2
-            res["roofline_us"] = round(max(flops / 1672.1e12, w_bytes / 6534.5e9, push_bytes / 770e9) * 1e6, 2)
-            res["roofline_note"] = "max(FLOPs / 1672.1 TF, weight bytes / 6534.5 GB/s, pushed bytes / 770 GB/s)"
+            res["roofline_us"] = round(max(flops / PEAK_BF16, w_bytes / PEAK_HBM, push_bytes / PEAK_PEER) * 1e6, 2)
+            res["roofline_note"] = (f"max(FLOPs / {PEAK_BF16 / 1e12:.1f} TF, weight bytes / {PEAK_HBM / 1e9:.1f} GB/s, "
+                                    f"pushed bytes / {PEAK_PEER / 1e9:.0f} GB/s)")
             res["frac_fused"] = round(res["roofline_us"] / res["us_fused"], 3)
         results.append(res)
         if rank == 0:
@@ -235,7 +242,7 @@ def _lm_head(a, rank, world, dev, nccl, gloo, rows) -> None:
             res["us_nccl"] = round(_graph_time(nccl_path, a.iters, world, gloo, nccl, dev), 2)
             w_bytes = n * H * 2
             push = (world - 1) * M * n * 2
-            res["roofline_us"] = round(max(2.0 * M * n * H / 1672.1e12, w_bytes / 6534.5e9, push / 770e9) * 1e6, 2)
+            res["roofline_us"] = round(max(2.0 * M * n * H / PEAK_BF16, w_bytes / PEAK_HBM, push / PEAK_PEER) * 1e6, 2)
             res["frac_fused"] = round(res["roofline_us"] / res["us_fused"], 3)
         if rank == 0:
             print(json.dumps(res), flush=True)
