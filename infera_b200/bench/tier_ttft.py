@@ -113,7 +113,7 @@ def main(argv=None) -> None:
         "tier_loads": st.get("loads", 0) - loads0, "tier_stats": st, "init_s": round(init_s, 1),
         "promote_gbs": round(st.get("promoted", 0) * page_bytes * 16 / 16 / st["load_s"] / 1e9, 1)
         if st.get("load_s") else None,
-        "kernel_status": K.scratch(eng.device).read_status() if eng.device.type == "cuda" else 0,
+        "kernel_status": K.scratch(eng.device).read_status_detail() if eng.device.type == "cuda" else 0,
         "timing": "host clock, each step synchronises on its sampled tokens", "data": "synthetic random tokens",
     }
     eng.tier.close()

@@ -107,7 +107,9 @@ __global__ void rope_kvwrite_kernel(__nv_bfloat16* __restrict__ qkv, int ldqkv, 
   const int p = pos[t];
   long long slot = slots[t];
   if (p < 0 || p >= max_pos || slot >= num_slots) {
-    if (threadIdx.x == 0) record_status(status, kStatusBadIndex);
+    if (threadIdx.x == 0)
+      record_status_detail(status, kStatusBadIndex, p < 0 || p >= max_pos ? 1 : 2, t,
+                           p < 0 || p >= max_pos ? p : static_cast<int>(slot));
     return;
   }
   __nv_bfloat16* row = qkv + static_cast<size_t>(t) * ldqkv;
@@ -149,7 +151,7 @@ __global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* _
   const int id = ids[t];
   uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H);
   if (id < 0 || id >= vocab) {
-    if (threadIdx.x == 0) record_status(status, kStatusBadIndex);
+    if (threadIdx.x == 0) record_status_detail(status, kStatusBadIndex, 3, t, id);
     for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = make_uint4(0, 0, 0, 0);
     return;
   }

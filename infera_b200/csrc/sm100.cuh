@@ -45,6 +45,17 @@ __device__ __forceinline__ void record_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
 
+// As record_status, and the first error's details go to status[1..3]
+// (the status word is the first of four ints): what was checked, where, the
+// offending value.
+__device__ __forceinline__ void record_status_detail(int* status, int code, int what, int where, int value) {
+  if (status != nullptr && atomicCAS(status, 0, code) == 0) {
+    status[1] = what;
+    status[2] = where;
+    status[3] = value;
+  }
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

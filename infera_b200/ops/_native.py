@@ -163,3 +163,12 @@ def check(rc: int, what: str) -> None:
                 torch.cuda.synchronize()
             except RuntimeError as e:
                 raise RuntimeError(f"{what}: device error after this launch: {e}") from e
+            if status_probe is not None:
+                st = status_probe()
+                if st and st.get("code"):
+                    raise RuntimeError(f"{what}: kernel status after this launch: {st}")
+
+
+# set by the kernel wrappers: reads the current device's status word and
+# details (used by INFERA_SYNC_CHECK)
+status_probe = None

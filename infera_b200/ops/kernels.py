@@ -60,13 +60,28 @@ class DeviceScratch:
         return self.pf_o, self.pf_lse
 
     def read_status(self) -> int:
-        return int(self.status.item())
+        return int(self.status[0].item())
+
+    def read_status_detail(self) -> dict:
+        """The first error's details (index checks): what (1 position, 2 KV
+        slot, 3 token id), the token row, the offending value."""
+        code, what, where, value = (int(v) for v in self.status.tolist())
+        return {"code": code, "what": what, "where": where, "value": value}
 
     def clear_status(self) -> None:
         self.status.zero_()
 
 
 _scratch: dict[int, DeviceScratch] = {}
+
+
+def _probe_status() -> dict | None:
+    idx = torch.cuda.current_device()
+    s = _scratch.get(idx)
+    return s.read_status_detail() if s is not None else None
+
+
+_native.status_probe = _probe_status
 
 
 def scratch(device: torch.device | int | None = None) -> DeviceScratch:
@@ -83,7 +98,8 @@ def scratch(device: torch.device | int | None = None) -> DeviceScratch:
     s = _scratch.get(idx)
     if s is None:
         dev = torch.device("cuda", idx)
-        s = DeviceScratch(device=dev, status=torch.zeros(1, dtype=torch.int32, device=dev))
+        # the status word, then three ints of details of the first error
+        s = DeviceScratch(device=dev, status=torch.zeros(4, dtype=torch.int32, device=dev))
         _scratch[idx] = s
     return s
 
