@@ -185,9 +185,23 @@ class ModelRunner:
     def _h2d(self, n: int) -> None:
         if self.on_gpu:
             self.d_in[:n].copy_(self.h_in[:n], non_blocking=True)
+            # the copy reads the pinned buffer when the stream reaches it: the
+            # next step may refill the buffer only after that (a step that
+            # samples nothing - an inner prompt chunk - does not wait for its
+            # kernels, so the host can be a step ahead)
+            self._h2d_ev = torch.cuda.Event()
+            self._h2d_ev.record()
             self.h2d_bytes += 4 * n
         else:
             self.d_in[:n].copy_(self.h_in[:n])
+
+    def _host_in(self) -> np.ndarray:
+        """The pinned input buffer, once the previous step's copy of it is done."""
+        ev = getattr(self, "_h2d_ev", None)
+        if ev is not None:
+            ev.synchronize()
+            self._h2d_ev = None
+        return self.h_in.numpy()
 
     def _d2h(self, src: torch.Tensor, n: int) -> list[int]:
         if n == 0:
@@ -212,7 +226,7 @@ class ModelRunner:
                  ("ql", q_len), ("cl", ctx_len), ("prow", p_rows), ("tiles", [x for t in tiles for x in t]),
                  ("dl", d_lens), ("drow", d_rows), ("ui", upd_idx), ("uv", upd_val),
                  ("temp", temps.view(np.int32).tolist()), ("seed", seeds.view(np.int32).tolist())]
-        h = self.h_in.numpy()
+        h = self._host_in()
         off = 0
         views = {}
         for name, arr in parts:
@@ -352,7 +366,7 @@ class ModelRunner:
         cls = self.len_classes[min(bisect.bisect_left(self.len_classes, max(d_lens)), len(self.len_classes) - 1)]
         g, lay = self.graphs[(Bg, cls)]
         pad = Bg - B
-        h = self.h_in.numpy()
+        h = self._host_in()
         h[: lay["_end"]] = 0
 
         def put(name, arr, fill):
