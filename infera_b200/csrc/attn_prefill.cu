@@ -99,7 +99,9 @@ template <bool EXT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQe,
-                      const __grid_constant__ CUtensorMap tmKe, const Params p) {
+                      const __grid_constant__ CUtensorMap tmKe, const __grid_constant__ CUtensorMap tmK8,
+                      const __grid_constant__ CUtensorMap tmV8, const __grid_constant__ CUtensorMap tmKe8,
+                      const Params p) {
   constexpr int QKB = qk_blocks(EXT);
   constexpr int STB = QKB + 2;     // blocks per KV stage
   extern __shared__ uint8_t smem_raw[];
@@ -204,20 +206,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
         uint8_t* base = sKV + st * STB * BLK;
         fstamp(p, FTR_TMA, j);
-        mbar_expect_tx(&k_full[st], QKB * BLK);
+        // eight consecutive pages are one 128-row box per 64-dim block (the
+        // same shared-memory image as eight page boxes: the 128-byte swizzle
+        // repeats every 8 rows)
+        bool run = true;
 #pragma unroll
-        for (int pg = 0; pg < BKV / PAGE; ++pg) {
-          const int r = cur[pg] * PAGE;
-          tma_load_2d(base + pg * PAGE * 128, &tmK, &k_full[st], kvh * p.k_hs, r, pol);
-          tma_load_2d(base + BLK + pg * PAGE * 128, &tmK, &k_full[st], kvh * p.k_hs + 64, r, pol);
-          if (EXT) tma_load_2d(base + 2 * BLK + pg * PAGE * 128, &tmKe, &k_full[st], kvh * p.ke_hs, r, pol);
+        for (int pg = 1; pg < BKV / PAGE; ++pg) run = run && cur[pg] == cur[0] + pg;
+        mbar_expect_tx(&k_full[st], QKB * BLK);
+        if (run) {
+          const int r = cur[0] * PAGE;
+          tma_load_2d(base, &tmK8, &k_full[st], kvh * p.k_hs, r, pol);
+          tma_load_2d(base + BLK, &tmK8, &k_full[st], kvh * p.k_hs + 64, r, pol);
+          if (EXT) tma_load_2d(base + 2 * BLK, &tmKe8, &k_full[st], kvh * p.ke_hs, r, pol);
+        } else {
+#pragma unroll
+          for (int pg = 0; pg < BKV / PAGE; ++pg) {
+            const int r = cur[pg] * PAGE;
+            tma_load_2d(base + pg * PAGE * 128, &tmK, &k_full[st], kvh * p.k_hs, r, pol);
+            tma_load_2d(base + BLK + pg * PAGE * 128, &tmK, &k_full[st], kvh * p.k_hs + 64, r, pol);
+            if (EXT) tma_load_2d(base + 2 * BLK + pg * PAGE * 128, &tmKe, &k_full[st], kvh * p.ke_hs, r, pol);
+          }
         }
         mbar_expect_tx(&v_full[st], 2 * BLK);
+        if (run) {
+          const int r = cur[0] * PAGE;
+          tma_load_2d(base + QKB * BLK, &tmV8, &v_full[st], kvh * p.v_hs, r, pol);
+          tma_load_2d(base + (QKB + 1) * BLK, &tmV8, &v_full[st], kvh * p.v_hs + 64, r, pol);
+        } else {
 #pragma unroll
-        for (int pg = 0; pg < BKV / PAGE; ++pg) {
-          const int r = cur[pg] * PAGE;
-          tma_load_2d(base + QKB * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * p.v_hs, r, pol);
-          tma_load_2d(base + (QKB + 1) * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * p.v_hs + 64, r, pol);
+          for (int pg = 0; pg < BKV / PAGE; ++pg) {
+            const int r = cur[pg] * PAGE;
+            tma_load_2d(base + QKB * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * p.v_hs, r, pol);
+            tma_load_2d(base + (QKB + 1) * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * p.v_hs + 64, r, pol);
+          }
         }
         ++issued;
       }
@@ -530,13 +551,15 @@ int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const 
   if ((ldo % 8) != 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return -1;
   if (kv_splits > 1 && (o_part == nullptr || lse_part == nullptr || (reinterpret_cast<uintptr_t>(o_part) & 15)))
     return -1;
-  CUtensorMap tq, tk, tv, tqe, tke;
+  CUtensorMap tq, tk, tv, tqe, tke, tk8, tv8, tke8;
   if (!fa_tmap(&tq, q, 128) || !fa_tmap(&tk, k, 16) || !fa_tmap(&tv, v, 16)) return -2;
+  if (!fa_tmap(&tk8, k, 128) || !fa_tmap(&tv8, v, 128)) return -2;
   if (EXT) {
-    if (!fa_tmap(&tqe, *qe, 128) || !fa_tmap(&tke, *ke, 16)) return -2;
+    if (!fa_tmap(&tqe, *qe, 128) || !fa_tmap(&tke, *ke, 16) || !fa_tmap(&tke8, *ke, 128)) return -2;
   } else {
     tqe = tq;
     tke = tk;
+    tke8 = tk8;
   }
   Params p;
   p.tiles = tiles;
@@ -569,7 +592,7 @@ int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const 
     attr_set[dev] = true;
   }
   dim3 grid(num_heads, num_tiles, p.kv_splits);
-  fa_prefill_kernel<EXT><<<grid, NUM_THREADS, smem_bytes(EXT), stream>>>(tq, tk, tv, tqe, tke, p);
+  fa_prefill_kernel<EXT><<<grid, NUM_THREADS, smem_bytes(EXT), stream>>>(tq, tk, tv, tqe, tke, tk8, tv8, tke8, p);
   if (p.kv_splits > 1)
     fa_combine_kernel<<<dim3(static_cast<unsigned>(q.rows), num_heads), D, 0, stream>>>(
         o_part, lse_part, p.kv_splits, num_heads, static_cast<__nv_bfloat16*>(out), ldo);

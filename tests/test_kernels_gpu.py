@@ -216,6 +216,38 @@ def test_attn_prefill_key_split(q_lens, ctx_lens, splits):
     assert K.prefill_kv_splits(hq, tiles.shape[0], max(ctx_lens)) >= 1
 
 
+@pytest.mark.parametrize("q_lens,ctx_lens", [([300, 1000], [2300, 1000]), ([129], [129])])
+def test_attn_prefill_consecutive_pages(q_lens, ctx_lens):
+    """Eight consecutive pages load as one 128-row box per 64-dim block; a
+    page out of line and partial last tiles take the page-by-page path."""
+    hq, hkv, D = 32, 8, 128
+    g = torch.Generator().manual_seed(13)
+    width = max((n + 15) // 16 for n in ctx_lens)
+    n_pages = len(ctx_lens) * (width + 1) + 4
+    bt = torch.zeros(len(ctx_lens), width, dtype=torch.int32)
+    start = 2
+    for i, n in enumerate(ctx_lens):
+        npg = (n + 15) // 16
+        bt[i, :npg] = torch.arange(start, start + npg, dtype=torch.int32)
+        start += npg + 1
+    bt[0, 9] = n_pages - 1             # one page out of line in the first sequence's second tile
+    kc = torch.randn(n_pages * 16, hkv * D, generator=g).to(torch.bfloat16)
+    vc = torch.randn(n_pages * 16, hkv * D, generator=g).to(torch.bfloat16)
+    T = sum(q_lens)
+    q = torch.randn(T, (hq + 2 * hkv) * D, generator=g).to(torch.bfloat16)
+    q_start = torch.tensor([sum(q_lens[:i]) for i in range(len(q_lens))], dtype=torch.int32)
+    ql = torch.tensor(q_lens, dtype=torch.int32)
+    cl = torch.tensor(ctx_lens, dtype=torch.int32)
+    tiles = torch.tensor(K.prefill_tiles(q_lens), dtype=torch.int32).view(-1, 2)
+    scale = 1 / math.sqrt(D)
+    ref = K.attn_prefill(q, kc, vc, bt, q_start, ql, cl, tiles, hq, hkv, scale)
+    out = K.attn_prefill(q.cuda(), kc.cuda(), vc.cuda(), bt.cuda(), q_start.cuda(), ql.cuda(), cl.cuda(),
+                         tiles.cuda(), hq, hkv, scale)
+    torch.cuda.synchronize()
+    _check_status()
+    assert _rel_err(out.cpu(), ref) < 2e-2
+
+
 def test_attn_prefill_divergent_rescale():
     """Rows whose running max grows by different amounts across KV tiles, so
     the lazy O rescale is needed by some rows of a warp and not others."""
