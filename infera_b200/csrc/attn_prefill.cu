@@ -112,8 +112,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;                 // [KV_STAGES]
   uint64_t* v_full = k_full + KV_STAGES;       // [KV_STAGES]
-  uint64_t* kv_empty = v_full + KV_STAGES;     // [KV_STAGES]
-  uint64_t* s_full = kv_empty + KV_STAGES;     // [2]
+  // K stages are released once S of the tile is computed, V stages once its
+  // PV is: the next K tiles load while the softmax still works on this one
+  uint64_t* k_empty = v_full + KV_STAGES;      // [KV_STAGES]
+  uint64_t* v_empty = k_empty + KV_STAGES;     // [KV_STAGES]
+  uint64_t* s_full = v_empty + KV_STAGES;      // [2]
   uint64_t* p_full = s_full + 2;               // [2] by tile parity: the softmax may run a tile ahead of PV
   uint64_t* o_done = p_full + 2;               // [1]
   uint64_t* drain = o_done + 1;
@@ -153,7 +156,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int s = 0; s < KV_STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
@@ -184,12 +188,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
+    // lane 0 loads Q and the K tiles, lane 1 the V tiles, each at its own
+    // pace (K stages free up after S, V stages after PV)
+    if (lane < 2) {
+      const bool is_k = lane == 0;
       const uint64_t pol = policy_evict_last();
-      mbar_expect_tx(q_full, QKB * BLK);
-      tma_load_2d(sQ, &tmQ, q_full, h * p.q_hs, row0, pol);
-      tma_load_2d(sQ + BLK, &tmQ, q_full, h * p.q_hs + 64, row0, pol);
-      if (EXT) tma_load_2d(sQ + 2 * BLK, &tmQe, q_full, h * p.qe_hs, row0, pol);
+      if (is_k) {
+        mbar_expect_tx(q_full, QKB * BLK);
+        tma_load_2d(sQ, &tmQ, q_full, h * p.q_hs, row0, pol);
+        tma_load_2d(sQ + BLK, &tmQ, q_full, h * p.q_hs + 64, row0, pol);
+        if (EXT) tma_load_2d(sQ + 2 * BLK, &tmQe, q_full, h * p.qe_hs, row0, pol);
+      }
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
       const int bt_row = p.bt_rows != nullptr ? p.bt_rows[seq] : seq;
       const int* bt = p.block_table + static_cast<size_t>(bt_row) * p.max_pages;
       const int n_pages = (ctx + PAGE - 1) / PAGE;
@@ -203,54 +214,55 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
         if (j + 1 < nk) load_tile_pages(bt, j_lo + j + 1, n_pages, nxt);  // in flight while we wait
-        if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
+        if (!mbar_wait(&empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
         uint8_t* base = sKV + st * STB * BLK;
-        fstamp(p, FTR_TMA, j);
+        if (is_k) fstamp(p, FTR_TMA, j);
         // eight consecutive pages are one 128-row box per 64-dim block (the
         // same shared-memory image as eight page boxes: the 128-byte swizzle
         // repeats every 8 rows)
         bool run = true;
 #pragma unroll
         for (int pg = 1; pg < BKV / PAGE; ++pg) run = run && cur[pg] == cur[0] + pg;
-        mbar_expect_tx(&k_full[st], QKB * BLK);
-        if (run) {
-          const int r = cur[0] * PAGE;
-          tma_load_2d(base, &tmK8, &k_full[st], kvh * p.k_hs, r, pol);
-          tma_load_2d(base + BLK, &tmK8, &k_full[st], kvh * p.k_hs + 64, r, pol);
-          if (EXT) tma_load_2d(base + 2 * BLK, &tmKe8, &k_full[st], kvh * p.ke_hs, r, pol);
-        } else {
+        if (is_k) {
+          mbar_expect_tx(&full[st], QKB * BLK);
+          if (run) {
+            const int r = cur[0] * PAGE;
+            tma_load_2d(base, &tmK8, &full[st], kvh * p.k_hs, r, pol);
+            tma_load_2d(base + BLK, &tmK8, &full[st], kvh * p.k_hs + 64, r, pol);
+            if (EXT) tma_load_2d(base + 2 * BLK, &tmKe8, &full[st], kvh * p.ke_hs, r, pol);
+          } else {
 #pragma unroll
-          for (int pg = 0; pg < BKV / PAGE; ++pg) {
-            const int r = cur[pg] * PAGE;
-            tma_load_2d(base + pg * PAGE * 128, &tmK, &k_full[st], kvh * p.k_hs, r, pol);
-            tma_load_2d(base + BLK + pg * PAGE * 128, &tmK, &k_full[st], kvh * p.k_hs + 64, r, pol);
-            if (EXT) tma_load_2d(base + 2 * BLK + pg * PAGE * 128, &tmKe, &k_full[st], kvh * p.ke_hs, r, pol);
+            for (int pg = 0; pg < BKV / PAGE; ++pg) {
+              const int r = cur[pg] * PAGE;
+              tma_load_2d(base + pg * PAGE * 128, &tmK, &full[st], kvh * p.k_hs, r, pol);
+              tma_load_2d(base + BLK + pg * PAGE * 128, &tmK, &full[st], kvh * p.k_hs + 64, r, pol);
+              if (EXT) tma_load_2d(base + 2 * BLK + pg * PAGE * 128, &tmKe, &full[st], kvh * p.ke_hs, r, pol);
+            }
           }
-        }
-        mbar_expect_tx(&v_full[st], 2 * BLK);
-        if (run) {
-          const int r = cur[0] * PAGE;
-          tma_load_2d(base + QKB * BLK, &tmV8, &v_full[st], kvh * p.v_hs, r, pol);
-          tma_load_2d(base + (QKB + 1) * BLK, &tmV8, &v_full[st], kvh * p.v_hs + 64, r, pol);
         } else {
+          mbar_expect_tx(&full[st], 2 * BLK);
+          if (run) {
+            const int r = cur[0] * PAGE;
+            tma_load_2d(base + QKB * BLK, &tmV8, &full[st], kvh * p.v_hs, r, pol);
+            tma_load_2d(base + (QKB + 1) * BLK, &tmV8, &full[st], kvh * p.v_hs + 64, r, pol);
+          } else {
 #pragma unroll
-          for (int pg = 0; pg < BKV / PAGE; ++pg) {
-            const int r = cur[pg] * PAGE;
-            tma_load_2d(base + QKB * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * p.v_hs, r, pol);
-            tma_load_2d(base + (QKB + 1) * BLK + pg * PAGE * 128, &tmV, &v_full[st], kvh * p.v_hs + 64, r, pol);
+            for (int pg = 0; pg < BKV / PAGE; ++pg) {
+              const int r = cur[pg] * PAGE;
+              tma_load_2d(base + QKB * BLK + pg * PAGE * 128, &tmV, &full[st], kvh * p.v_hs, r, pol);
+              tma_load_2d(base + (QKB + 1) * BLK + pg * PAGE * 128, &tmV, &full[st], kvh * p.v_hs + 64, r,
+                          pol);
+            }
           }
         }
         ++issued;
       }
       // drain: every issued tile's bytes must have landed before exit
-      mbar_wait(q_full, 0, nullptr, nullptr, 0, kWaitLimitNs / 4);
+      if (is_k) mbar_wait(q_full, 0, nullptr, nullptr, 0, kWaitLimitNs / 4);
       long long first = issued > KV_STAGES ? issued - KV_STAGES : 0;
-      for (long long i = first; i < issued; ++i) {
-        mbar_wait(&k_full[i % KV_STAGES], static_cast<uint32_t>((i / KV_STAGES) & 1), nullptr, nullptr, 0,
+      for (long long i = first; i < issued; ++i)
+        mbar_wait(&full[i % KV_STAGES], static_cast<uint32_t>((i / KV_STAGES) & 1), nullptr, nullptr, 0,
                   kWaitLimitNs / 4);
-        mbar_wait(&v_full[i % KV_STAGES], static_cast<uint32_t>((i / KV_STAGES) & 1), nullptr, nullptr, 0,
-                  kWaitLimitNs / 4);
-      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -281,7 +293,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         umma_commit(o_done);
         fstamp(p, FTR_PVISSUE, jj);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&v_empty[st]);
         return true;
       };
       for (int j = 0; j < nk && ok; ++j) {
@@ -303,6 +315,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           umma_bf16(tmem + s_col, ad, bd, idesc_qk, s > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[j & 1]);
+        umma_commit(&k_empty[st]);   // K(j) is read once S(j) is done
         fstamp(p, FTR_SISSUE, j);
         if (j > 0 && !issue_pv(j - 1)) {
           ok = false;
