@@ -49,7 +49,10 @@ def run_case(case: str, iters: int) -> dict:
     g = torch.Generator(device=dev).manual_seed(0)
     if case.startswith("gemm"):
         M, N, Kd, swiglu = {"gemm_prefill": (2048, 6144, 4096, False), "gemm_decode": (64, 28672, 4096, True),
-                            "gemm_lmhead": (64, 128256, 4096, False)}[case]
+                            "gemm_lmhead": (64, 128256, 4096, False),
+                            # a mixed step: ~60 decodes + a 224-token prompt chunk
+                            "gemm_mixed": (288, 28672, 4096, True),
+                            "gemm_mixed_down": (288, 4096, 14336, False)}[case]
         x = torch.randn(M, Kd, device=dev, generator=g).to(bf)
         w = (torch.randn(N, Kd, device=dev, generator=g) / math.sqrt(Kd)).to(bf)
         ms = _time(lambda: K.linear(x, w, swiglu=swiglu), iters)
