@@ -12,21 +12,21 @@
 // the tile unused), one 256-dim half of the value dims and one split of the
 // keys:
 //   warp 0      TMA producer: the query's 9 x [128 x 64] blocks once, then
-//               key tiles of one page (16 tokens x 9 blocks of 64 dims) into
-//               a 4-stage ring
-//   warp 1      MMA issuer: S = Q K^T (M 128, N 16, K 576) into TMEM (double
-//               buffered); O += P V (M 128, N 256, K 16) with V = the tile's
-//               latent dims of this CTA's half, read MN-major from the same
-//               ring stage
+//               key tiles of two pages (32 tokens x 9 blocks of 64 dims) into
+//               a 2-stage ring
+//   warp 1      MMA issuer: S = Q K^T (M 128, N 32, K 576) into TMEM (double
+//               buffered); O += P V (M 128, N 256, K 32) with P read from
+//               TMEM and V = the tile's latent dims of this CTA's half, read
+//               MN-major from the same ring stage
 //   warps 2..5  softmax, thread = head row: running max with lazy O rescale
-//               (only when the max grows by more than 2^8), P to shared
-//               memory (K-major, 64-byte swizzle; even tiles in the first 16
-//               columns, odd tiles in the last 16, so P of tile j is written
-//               while tile j-1's P is still being read), final O / l
-//               epilogue or split partials with their log-sum-exp
-// Small page-sized tiles in a 4-deep ring keep more key bytes in flight
-// than a 2-deep ring of larger tiles in the same 72 KiB.
-// TMEM: S 2 x 16 columns, O 256 columns. The 128 x 512 fp32 output of all
+//               (only when the max grows by more than 2^8), P (bf16 pairs)
+//               written back over the first 16 columns of the tile's own S,
+//               final O / l epilogue or split partials with their
+//               log-sum-exp
+// The S MMAs cost about the same per instruction at N 16 and N 32 (issue-
+// bound), so 32-key tiles halve their cost per key; 2 stages of 36 KiB keep
+// the same key bytes in flight as 4 stages of one page did.
+// TMEM: S 2 x 32 columns, O 256 columns. The 128 x 512 fp32 output of all
 // heads would fill TMEM on its own, hence the value split over two CTAs (the
 // two recompute S; they read the same key tiles, which L2 serves once).
 // Prefill reuses the kernel with one "query" per prompt token (its own
@@ -44,17 +44,18 @@ constexpr int DL = 512;
 constexpr int DR = 64;
 constexpr int DQK = DL + DR;
 constexpr int NCH = DQK / 64;              // 9 blocks of 64 dims
-constexpr int BT = 16;                     // keys per tile (one page)
+constexpr int BT = 32;                     // keys per tile (two pages)
 constexpr int PAGE = 16;
-constexpr int STAGES = 4;
+constexpr int STAGES = 2;
 constexpr int QCH = 128 * 128;             // one [128 rows x 64 dims] bf16 block
-constexpr int KCH = BT * 128;              // one [16 keys x 64 dims] block
-constexpr int KV_STAGE = NCH * KCH;        // 18 KiB
-constexpr int P_BYTES = 128 * 32 * 2;      // 8 KiB: two 16-key halves
+constexpr int KCH = BT * 128;              // one [32 keys x 64 dims] block
+constexpr int KV_STAGE = NCH * KCH;        // 36 KiB
 constexpr int DV = 256;                    // value dims per CTA
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t S_COL0 = 0, S_COL1 = 16, O_COL = 64;
-constexpr int SMEM_BYTES = 1024 + NCH * QCH + STAGES * KV_STAGE + P_BYTES + 256;
+// S of even / odd tiles (32 fp32 columns each; P of the tile, bf16 pairs,
+// is written back over the first 16 of them), O 256 columns
+constexpr uint32_t S_COL0 = 0, S_COL1 = 32, O_COL = 64;
+constexpr int SMEM_BYTES = 1024 + NCH * QCH + STAGES * KV_STAGE + 256;
 
 struct Params {
   const int* q_row;        // [nq] block-table row of each query
@@ -79,23 +80,6 @@ __device__ __forceinline__ void stamp(const Params& p, bool cta0, int ev, int j)
   if (p.trace != nullptr && cta0 && j < kTraceTiles) p.trace[ev * kTraceTiles + j] = clock64();
 }
 
-// K-major operand with 64-byte swizzle (layout type 4): 8-row atoms of
-// 64-byte rows, atoms SBO bytes apart.
-__device__ __forceinline__ uint64_t make_sw64_desc(uint32_t smem_addr, uint32_t sbo_bytes) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>(1u) << 16;
-  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
-  d |= 1ull << 46;
-  d |= 4ull << 61;
-  return d;
-}
-
-// byte offset of 16-byte chunk c (0..3) of row r in a 64-byte-swizzled tile
-__device__ __forceinline__ uint32_t sw64_offset(int r, int c) {
-  return static_cast<uint32_t>((r >> 3) * 512 + (r & 7) * 64 + ((c ^ ((r & 7) >> 1)) << 4));
-}
-
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     mla_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                       const Params p) {
@@ -103,16 +87,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + NCH * QCH;
-  uint8_t* sP = sKV + STAGES * KV_STAGE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + STAGES * KV_STAGE);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;          // [STAGES]
   uint64_t* kv_empty = kv_full + STAGES; // [STAGES]
   uint64_t* s_full = kv_empty + STAGES;  // [2]
-  // [2] each: P half written (128 arrivals) / PV done, for even and odd
-  // tiles. One barrier per half: a warp may run a tile ahead of the others
-  // (writing the other half), and its arrival must not count toward the
-  // tile the slower warps are still writing.
+  // [2] each: P written (128 arrivals) / PV done, for even and odd tiles: a
+  // warp may run a tile ahead of the others, and its arrival must not count
+  // toward the tile the slower warps are still writing.
   uint64_t* p_full = s_full + 2;
   uint64_t* o_done = p_full + 2;
   uint64_t* drain = o_done + 2;
@@ -167,17 +149,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_expect_tx(q_full, NCH * QCH);
       for (int c = 0; c < NCH; ++c) tma_load_2d(sQ + c * QCH, &tmQ, q_full, c * 64, qi * p.hq, pol_q);
       const int* bt = p.block_table + static_cast<size_t>(p.q_row[qi]) * p.max_pages;
+      const int n_pages = (kvlen + PAGE - 1) / PAGE;
+      // pages of tile t: 2t and 2t + 1 (past the sequence's last page: the
+      // first again, its keys masked)
+      auto pages_of = [&](int t, int& a, int& b) {
+        a = __ldg(bt + 2 * t);
+        b = 2 * t + 1 < n_pages ? __ldg(bt + 2 * t + 1) : a;
+      };
       long long issued = 0;
-      int pg_next = __ldg(bt + tile0);
+      int na, nb;
+      pages_of(tile0, na, nb);
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % STAGES;
         const uint32_t ph = (j / STAGES) & 1;
-        const int pg = pg_next;
-        if (j + 1 < n_tiles) pg_next = __ldg(bt + tile0 + j + 1);  // in flight while we wait
+        const int pa = na, pb = nb;
+        if (j + 1 < n_tiles) pages_of(tile0 + j + 1, na, nb);  // in flight while we wait
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
         uint8_t* base = sKV + st * KV_STAGE;
         mbar_expect_tx(&kv_full[st], KV_STAGE);
-        for (int c = 0; c < NCH; ++c) tma_load_2d(base + c * KCH, &tmKV, &kv_full[st], c * 64, pg * PAGE, pol_kv);
+        for (int c = 0; c < NCH; ++c) {
+          tma_load_2d(base + c * KCH, &tmKV, &kv_full[st], c * 64, pa * PAGE, pol_kv);
+          tma_load_2d(base + c * KCH + PAGE * 128, &tmKV, &kv_full[st], c * 64, pb * PAGE, pol_kv);
+        }
         stamp(p, cta0, TR_TMA, j);
         ++issued;
       }
@@ -193,7 +186,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t idesc_qk = make_idesc_bf16(128, BT);
       const uint32_t idesc_pv = make_idesc_bf16(128, DV, true);
       const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t p_addr = smem_u32(sP);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kStatusTimeoutFull);
       auto issue_pv = [&](int jj) -> bool {
         if (!mbar_wait(&p_full[jj & 1], static_cast<uint32_t>((jj >> 1) & 1), abort_flag, p.status,
@@ -203,12 +195,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const int st = jj % STAGES;
         // V = latent dims [256*half, +256) of the tile: blocks 4*half .. 4*half+3;
-        // P of this tile = columns [16*(jj&1), +16) of the P buffer
+        // P of this tile = the first 16 columns of its S (keys 16s.. are 8 columns)
         const uint32_t v_addr = smem_u32(sKV + st * KV_STAGE + half * 4 * KCH);
-        const uint64_t ad = make_sw64_desc(p_addr + (jj & 1) * 32, 512);
-        // MN-major V: LBO = distance between 64-dim blocks, SBO = 8 keys
-        const uint64_t bd = make_sw128_desc(v_addr, KCH, 1024);
-        umma_bf16(tmem + O_COL, ad, bd, idesc_pv, jj > 0 ? 1u : 0u);
+        const uint32_t p_col = (jj & 1) ? S_COL1 : S_COL0;
+#pragma unroll
+        for (int s = 0; s < BT / 16; ++s) {
+          // MN-major V: LBO = distance between 64-dim blocks, SBO = 8 keys
+          const uint64_t bd = make_sw128_desc(v_addr + s * 16 * 128, KCH, 1024);
+          umma_bf16_ts(tmem + O_COL, tmem + p_col + s * 8, bd, idesc_pv, (jj > 0 || s > 0) ? 1u : 0u);
+        }
         umma_commit(&o_done[jj & 1]);
         umma_commit(&kv_empty[st]);
         return true;
@@ -258,13 +253,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (r == 0) stamp(p, cta0, TR_SFULL, j);
       tc_fence_after();
-      uint32_t v[16];
-      tmem_ld16(lane_addr + ((j & 1) ? S_COL1 : S_COL0), v);
+      uint32_t v[32];
+      const uint32_t s_addr = lane_addr + ((j & 1) ? S_COL1 : S_COL0);
+      tmem_ld32(s_addr, v);
       tmem_ld_wait();
       const int lim = kvlen - (tile0 + j) * BT;  // keys c < lim are valid
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < 32; ++i) {
         if (i >= lim) v[i] = __float_as_uint(-INFINITY);
         mx = fmaxf(mx, __uint_as_float(v[i]));
       }
@@ -274,9 +270,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float m_use = rescale ? m_new : m_run;
       const float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
       const bool warp_rescale = __any_sync(0xffffffffu, rescale && j > 0);
-      // this P half was last read by tile j-2's PV; a rescale of O needs
-      // every PV so far (tile j-1's, which completes after j-2's) done
-      const int wait_tile = warp_rescale ? j - 1 : j - 2;
+      // P goes over S(j)'s own columns, which no MMA in flight touches (S(j+2)
+      // reuses them and is issued after PV(j)); only a rescale of O waits for
+      // every PV so far (tile j-1's)
+      const int wait_tile = warp_rescale ? j - 1 : -1;
       if (wait_tile >= 0) {
         if (!mbar_wait_warp(&o_done[wait_tile & 1], static_cast<uint32_t>((wait_tile >> 1) & 1), abort_flag,
                             p.status, kStatusTimeoutTmemFull)) {
@@ -299,22 +296,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_st_wait();
       }
       float sum = 0.f;
-      uint32_t pk[8];
+      uint32_t pk[16];
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
+      for (int i = 0; i < 32; i += 2) {
         const float e0 = exp2f(fmaf(__uint_as_float(v[i]), p.scale_log2, -m_use));
         const float e1 = exp2f(fmaf(__uint_as_float(v[i + 1]), p.scale_log2, -m_use));
         __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
         sum += __low2float(bb) + __high2float(bb);
         pk[i / 2] = *reinterpret_cast<uint32_t*>(&bb);
       }
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
-        *reinterpret_cast<uint4*>(sP + sw64_offset(r, 2 * (j & 1) + c)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      tmem_st16(s_addr, pk);
       l_run = l_run * alpha + sum;
       m_run = m_use;
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
       if (r == 0) stamp(p, cta0, TR_PARRIVE, j);
