@@ -165,8 +165,13 @@ __device__ __forceinline__ void tile_coords(const Params& p, int t, int& pt, int
   }
   sp = t % p.splits;
   int rest = t / p.splits;
-  pt = rest % p.p_tiles;
-  qt = rest / p.p_tiles;
+  if (p.swap) {  // the token tiles of one weight tile run back to back (the weight tile read once)
+    qt = rest % p.q_tiles;
+    pt = rest / p.q_tiles;
+  } else {       // the row blocks of one weight block run back to back
+    pt = rest % p.p_tiles;
+    qt = rest / p.p_tiles;
+  }
 }
 
 // The (tile, k-block range) segments one CTA works through, in order: tiles
@@ -831,18 +836,33 @@ inline Plan make_plan_fp8(int M, int N, int K, int num_sms, int force_split) {
 }
 
 // Choose operand order, tile width and split-K factor for one problem.
-inline Plan make_plan(int M, int N, int K, int num_sms, int force_split) {
+// Largest token count that runs swap-AB (weights on the 128-row MMA side,
+// tokens as N in up to two tiles of <= 256): every weight tile is read by
+// the CTAs of its token tiles back to back, instead of once per 128-token
+// row block. INFERA_GEMM_SWAP_MAX overrides (128: swap only for one token tile
+// of <= 128).
+inline int swap_max_tokens() {
+  static const int v = [] {
+    const char* e = std::getenv("INFERA_GEMM_SWAP_MAX");
+    return e != nullptr && *e ? std::atoi(e) : 512;
+  }();
+  return v;
+}
+
+inline Plan make_plan(int M, int N, int K, int num_sms, int force_split, int swap_max = -1) {
   Plan pl{};
   Params& p = pl.p;
   p.M = M;
   p.N = N;
   p.K = K;
   p.nkb = (K + BK - 1) / BK;
-  p.swap = M <= 128 ? 1 : 0;
+  if (swap_max < 0) swap_max = swap_max_tokens();
+  p.swap = (M <= 128 || M <= swap_max) ? 1 : 0;
   if (p.swap) {
-    p.bn = ((M + 15) / 16) * 16;
+    p.q_tiles = (M + MAX_BN - 1) / MAX_BN;
+    const int per = (M + p.q_tiles - 1) / p.q_tiles;
+    p.bn = ((per + 15) / 16) * 16;
     p.p_tiles = (N + BM - 1) / BM;
-    p.q_tiles = 1;
   } else {
     p.bn = MAX_BN;
     p.p_tiles = (M + BM - 1) / BM;
@@ -957,7 +977,7 @@ inline int run_push(const Operands& o, const void* A, const void* W, int M, int 
   // split K like the plain GEMM does (small M leaves most SMs idle
   // otherwise); the split path pushes from its finalize kernel
   const int fs = ws == nullptr ? 1 : 0;
-  Plan pl = o.fp8 ? make_plan_fp8(M, N, K, num_sms, fs) : make_plan(M, N, K, num_sms, fs);
+  Plan pl = o.fp8 ? make_plan_fp8(M, N, K, num_sms, fs) : make_plan(M, N, K, num_sms, fs, 128);
   Params& p = pl.p;
   p.streamk = 0;  // peer-store epilogues write whole tiles
   const bool split = p.splits > 1;
