@@ -196,6 +196,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, sw
     assert x.stride(1) == 1 and w.stride(1) == 1
     if out is None:
         out = torch.empty(M, n_out, dtype=torch.bfloat16, device=x.device)
+    if M == 0:
+        return out
     sc = scratch(x.device)
     ws = sc.ensure_gemm(M * N if _gemm_ws(M, N, K, force_split) else 1)
     rc = _native.kernels().ib_gemm_bf16(x.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, K, x.stride(0),

@@ -230,7 +230,8 @@ def test_attn_prefill_consecutive_pages(q_lens, ctx_lens):
         npg = (n + 15) // 16
         bt[i, :npg] = torch.arange(start, start + npg, dtype=torch.int32)
         start += npg + 1
-    bt[0, 9] = n_pages - 1             # one page out of line in the first sequence's second tile
+    if (ctx_lens[0] + 15) // 16 > 9:
+        bt[0, 9] = n_pages - 1         # one page out of line in the first sequence's second tile
     kc = torch.randn(n_pages * 16, hkv * D, generator=g).to(torch.bfloat16)
     vc = torch.randn(n_pages * 16, hkv * D, generator=g).to(torch.bfloat16)
     T = sum(q_lens)
