@@ -169,6 +169,15 @@ def run_case(case: str, iters: int) -> dict:
             ms1 = _time(lambda: K.attn_prefill(q, kc, vc, bt, *meta, tiles, hq, hkv, 1 / math.sqrt(D),
                                                kv_splits=1), iters)
             res.update(ms_unsplit=ms1, speedup_vs_unsplit=ms1 / ms)
+        # one 128-row query tile per CTA, for comparison
+        t1 = torch.tensor(K.prefill_tiles([ql], 128), dtype=torch.int32, device=dev)
+        s1 = K.prefill_kv_splits(hq, t1.shape[0], ctx)
+        ref = K.attn_prefill(q, kc, vc, bt, *meta, t1, hq, hkv, 1 / math.sqrt(D), kv_splits=s1, tile_rows=128)
+        got = K.attn_prefill(q, kc, vc, bt, *meta, tiles, hq, hkv, 1 / math.sqrt(D), kv_splits=splits)
+        ms128 = _time(lambda: K.attn_prefill(q, kc, vc, bt, *meta, t1, hq, hkv, 1 / math.sqrt(D), kv_splits=s1,
+                                             tile_rows=128), iters)
+        res.update(tile_rows=K.PREFILL_TILE_ROWS, ms_tile128=ms128, tflops_tile128=4 * keys * D * hq / ms128 / 1e9,
+                   max_abs_diff_vs_tile128=float((got.float() - ref.float()).abs().max()))
         return res
     if case in ("mla_prefill", "mla_prefill_prefix"):
         from infera_b200.ops import mla as M
@@ -183,7 +192,7 @@ def run_case(case: str, iters: int) -> dict:
         w_uk = (torch.randn(hq, 512, 128, device=dev, generator=g) / math.sqrt(512)).to(bf)
         w_uv = (torch.randn(hq, 128, 512, device=dev, generator=g) / math.sqrt(512)).to(bf)
         w_up = M.kv_up_weight(w_uk, w_uv)
-        tiles = torch.tensor(K.prefill_tiles([ql]), dtype=torch.int32, device=dev)
+        tiles = torch.tensor(K.prefill_tiles([ql], 128), dtype=torch.int32, device=dev)
         meta = [torch.tensor([v], dtype=torch.int32, device=dev) for v in (0, ql, ctx)]
         scale = M.default_scale(128, 64)
         run = lambda: M.mla_prefill(qb, q_full, cache, bt, None, ([ql], [ctx]), *meta, tiles, w_up, hq, 128,  # noqa

@@ -503,6 +503,403 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------------
+// Two query tiles per CTA (128-dim heads): 256 query rows of one head share
+// every K / V tile, so each tile is read from shared memory by twice the
+// math, and the tensor core alternates between the tiles while the other
+// tile's softmax runs:
+//   warp 0      TMA producer: Q0 / Q1 once, then K (lane 0) and V (lane 1)
+//   warp 1      MMA issuer, per key tile j:
+//                 PV0(j-1), S0(j), PV1(j-1), S1(j)
+//               S_t(j) overwrites the columns that held P_t(j-1), so it is
+//               issued after PV_t(j-1); tcgen05 MMAs run in issue order,
+//               hence S_t(j) complete implies O_t holds every PV up to j-1.
+//   warps 2..5  softmax of tile 0, one query row per thread (all 128 keys)
+//   warps 6..9  softmax of tile 1
+// TMEM: S_t / P_t at columns [128 t, 128 t + 128), O_t at [256 + 128 t, +128).
+// A tile whose rows need fewer key tiles (the first tile of a causal pair)
+// stops early; a pair whose second tile lies past the sequence runs tile 0
+// alone.
+constexpr int SMEM2 = 1024 + (4 + KV_STAGES * 4) * BLK + 1024;
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fa_prefill2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmK8,
+                       const __grid_constant__ CUtensorMap tmV8, const Params p) {
+  constexpr int STB = 4;  // blocks per KV stage: K lo, K hi, V lo, V hi
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                // tile t: blocks 2t, 2t+1
+  uint8_t* sKV = smem + 4 * BLK;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + KV_STAGES * STB * BLK);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;                 // [KV_STAGES]
+  uint64_t* v_full = k_full + KV_STAGES;       // [KV_STAGES]
+  uint64_t* k_empty = v_full + KV_STAGES;      // [KV_STAGES]
+  uint64_t* v_empty = k_empty + KV_STAGES;     // [KV_STAGES]
+  uint64_t* s_full = v_empty + KV_STAGES;      // [2] per query tile
+  uint64_t* p_full = s_full + 2;               // [2] per query tile
+  uint64_t* o_done = p_full + 2;               // [2] per query tile
+  uint64_t* drain = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.x;
+  const int seq = p.tiles[blockIdx.y * 2 + 0];
+  const int qb = p.tiles[blockIdx.y * 2 + 1];   // first of the pair's two 128-row blocks
+  const int kvh = h / (p.num_heads / p.num_kv_heads);
+  const int qlen = p.q_len[seq];
+  const int ctx = p.ctx_len[seq];
+  int rows_t[2], pos0_t[2], nkv_t[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    rows_t[t] = min(BQ, qlen - (qb + t) * BQ);
+    pos0_t[t] = ctx - qlen + (qb + t) * BQ;
+    nkv_t[t] = rows_t[t] > 0 ? (pos0_t[t] + rows_t[t] + BKV - 1) / BKV : 0;
+  }
+  const int n_kv = max(nkv_t[0], nkv_t[1]);
+  const int S = p.kv_splits > 1 ? p.kv_splits : 1;
+  const int z = S > 1 ? blockIdx.z : 0;
+  const int chunk = (n_kv + S - 1) / S;
+  const int j_lo = z * chunk;
+  const int nk = min(n_kv - j_lo, chunk);
+  int nk_t[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) nk_t[t] = max(0, min(nkv_t[t] - j_lo, chunk));
+  const int row_base = p.q_start[seq] + qb * BQ;
+  if (nk <= 0) {
+    for (int r = threadIdx.x; r < 2 * BQ; r += blockDim.x)
+      if (r < BQ ? r < rows_t[0] : r - BQ < rows_t[1])
+        p.lse_part[(static_cast<size_t>(row_base + r) * p.num_heads + h) * S + z] = -INFINITY;
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&o_done[t], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK8);
+    tma_prefetch_desc(&tmV8);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane < 2) {
+      const bool is_k = lane == 0;
+      const uint64_t pol = policy_evict_last();
+      if (is_k) {
+        const int nq = rows_t[1] > 0 ? 2 : 1;
+        mbar_expect_tx(q_full, nq * 2 * BLK);
+        for (int t = 0; t < nq; ++t) {
+          tma_load_2d(sQ + 2 * t * BLK, &tmQ, q_full, h * p.q_hs, row_base + t * BQ, pol);
+          tma_load_2d(sQ + (2 * t + 1) * BLK, &tmQ, q_full, h * p.q_hs + 64, row_base + t * BQ, pol);
+        }
+      }
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      const int bt_row = p.bt_rows != nullptr ? p.bt_rows[seq] : seq;
+      const int* bt = p.block_table + static_cast<size_t>(bt_row) * p.max_pages;
+      const int n_pages = (ctx + PAGE - 1) / PAGE;
+      const int hs = is_k ? p.k_hs : p.v_hs;
+      const CUtensorMap* tm1 = is_k ? &tmK : &tmV;
+      const CUtensorMap* tm8 = is_k ? &tmK8 : &tmV8;
+      const int boff = is_k ? 0 : 2 * BLK;
+      long long issued = 0;
+      int nxt[8];
+      load_tile_pages(bt, j_lo, n_pages, nxt);
+      for (int j = 0; j < nk; ++j) {
+        const int st = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1;
+        int cur[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
+        if (j + 1 < nk) load_tile_pages(bt, j_lo + j + 1, n_pages, nxt);
+        if (!mbar_wait(&empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) break;
+        uint8_t* base = sKV + st * STB * BLK + boff;
+        if (is_k) fstamp(p, FTR_TMA, j);
+        bool run = true;
+#pragma unroll
+        for (int pg = 1; pg < BKV / PAGE; ++pg) run = run && cur[pg] == cur[0] + pg;
+        mbar_expect_tx(&full[st], 2 * BLK);
+        if (run) {
+          const int r = cur[0] * PAGE;
+          tma_load_2d(base, tm8, &full[st], kvh * hs, r, pol);
+          tma_load_2d(base + BLK, tm8, &full[st], kvh * hs + 64, r, pol);
+        } else {
+#pragma unroll
+          for (int pg = 0; pg < BKV / PAGE; ++pg) {
+            const int r = cur[pg] * PAGE;
+            tma_load_2d(base + pg * PAGE * 128, tm1, &full[st], kvh * hs, r, pol);
+            tma_load_2d(base + BLK + pg * PAGE * 128, tm1, &full[st], kvh * hs + 64, r, pol);
+          }
+        }
+        ++issued;
+      }
+      if (is_k) mbar_wait(q_full, 0, nullptr, nullptr, 0, kWaitLimitNs / 4);
+      long long first = issued > KV_STAGES ? issued - KV_STAGES : 0;
+      for (long long i = first; i < issued; ++i)
+        mbar_wait(&full[i % KV_STAGES], static_cast<uint32_t>((i / KV_STAGES) & 1), nullptr, nullptr, 0,
+                  kWaitLimitNs / 4);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_qk = make_idesc_bf16(128, 128, false);
+      const uint32_t idesc_pv = make_idesc_bf16(128, 128, true);
+      const uint32_t q_addr = smem_u32(sQ);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kStatusTimeoutFull);
+      for (int j = 0; j <= nk && ok; ++j) {
+        const int st = j % KV_STAGES;
+        if (j < nk) {
+          if (!mbar_wait(&k_full[st], static_cast<uint32_t>((j / KV_STAGES) & 1), abort_flag, p.status,
+                         kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          fstamp(p, FTR_KFULL, j);
+        }
+        const int pst = (j + KV_STAGES - 1) % KV_STAGES;   // stage of key tile j-1
+        bool v_ready = false;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int nkt = t ? nk_t[1] : nk_t[0];
+          if (j >= 1 && j - 1 < nkt) {
+            // O_t += P_t(j-1) V(j-1)
+            if (!mbar_wait(&p_full[t], static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status,
+                           kStatusTimeoutTmemEmpty)) {
+              ok = false;
+              break;
+            }
+            if (!v_ready) {
+              if (!mbar_wait(&v_full[pst], static_cast<uint32_t>(((j - 1) / KV_STAGES) & 1), abort_flag, p.status,
+                             kStatusTimeoutFull)) {
+                ok = false;
+                break;
+              }
+              v_ready = true;
+            }
+            tc_fence_after();
+            const uint32_t v_addr = smem_u32(sKV + pst * STB * BLK + 2 * BLK);
+#pragma unroll
+            for (int s = 0; s < 8; ++s) {
+              // P_t packs keys 16s..16s+15 into columns 8s..8s+7 of S_t
+              const uint64_t bd = make_sw128_desc(v_addr + s * 2048, BLK, 1024);
+              umma_bf16_ts(tmem + O_COL + t * 128, tmem + t * 128 + s * 8, bd, idesc_pv,
+                           (j > 1 || s > 0) ? 1u : 0u);
+            }
+            umma_commit(&o_done[t]);
+            if (t == 0) fstamp(p, FTR_PVISSUE, j - 1);
+          }
+          if (j < nkt) {
+            tc_fence_after();
+            const uint32_t k_addr = smem_u32(sKV + st * STB * BLK);
+            const uint32_t qa = q_addr + t * 2 * BLK;
+#pragma unroll
+            for (int s = 0; s < 8; ++s) {
+              const uint32_t off = (s >> 2) * BLK + (s & 3) * 32;
+              umma_bf16(tmem + t * 128, make_sw128_desc(qa + off, 16, 1024), make_sw128_desc(k_addr + off, 16, 1024),
+                        idesc_qk, s > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[t]);
+            if (t == 0) fstamp(p, FTR_SISSUE, j);
+          }
+        }
+        if (!ok) break;
+        if (j < nk) umma_commit(&k_empty[st]);
+        if (j >= 1) umma_commit(&v_empty[pst]);
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, p.status, kStatusTimeoutFull);
+    }
+  } else {
+    const int t = (warp - 2) >> 2;
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const int rows = t ? rows_t[1] : rows_t[0];   // selects: no dynamically indexed local arrays
+    const int pos0 = t ? pos0_t[1] : pos0_t[0];
+    const int nkt = t ? nk_t[1] : nk_t[0];
+    const int pos = pos0 + min(r, max(rows, 1) - 1);
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    const uint32_t s_addr = lane_addr + t * 128;
+    const uint32_t o_addr = lane_addr + O_COL + t * 128;
+    const float sl = p.scale_log2;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    const bool tr0 = t == 0 && r == 0;
+    for (int j = 0; j < nkt && ok; ++j) {
+      if (!mbar_wait_warp(&s_full[t], static_cast<uint32_t>(j & 1), abort_flag, p.status, kStatusTimeoutTmemFull)) {
+        ok = false;
+        break;
+      }
+      if (tr0) fstamp(p, FTR_SFULL, j);
+      tc_fence_after();
+      const int kbase = (j_lo + j) * BKV;
+      const int lim = pos - kbase;  // key c of the tile is visible iff c <= lim
+      const bool full_tile = kbase + BKV - 1 <= pos0;
+      // pass 1: the row maximum over all 128 keys
+      float mx;
+      {
+        uint32_t v[128];
+        tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&v[64]));
+        tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&v[96]));
+        tmem_ld_wait();
+        if (!full_tile) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i > lim) v[i] = __float_as_uint(-INFINITY);
+        }
+        float mx0 = __uint_as_float(v[0]), mx1 = __uint_as_float(v[1]);
+#pragma unroll
+        for (int i = 2; i < 128; i += 4) {
+          mx0 = max3f(mx0, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+          mx1 = max3f(mx1, __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+        }
+        mx = fmaxf(mx0, mx1) * sl;
+      }
+      const float m_new = fmaxf(m_run, mx);
+      // lazy rescale: keep a stale max unless the new one exceeds it by 2^8
+      const bool rescale = (j == 0) || (m_new > m_run + 8.0f);
+      const float m_use = rescale ? m_new : m_run;
+      const float alpha = (j == 0 || m_run == -INFINITY) ? 0.f : exp2f(m_run - m_use);
+      const float m_ref = m_use == -INFINITY ? 0.f : m_use;
+      // pass 2, per 64 keys: P = 2^(s*scale - m), even keys on the MUFU unit,
+      // odd keys with the FMA-pipe polynomial (masked keys give exactly 0),
+      // packed bf16 pairs written over the S columns already read
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t v[64];
+        tmem_ld32(s_addr + hh * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(s_addr + hh * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_ld_wait();
+        if (!full_tile) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (hh * 64 + i > lim) v[i] = __float_as_uint(-INFINITY);
+        }
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {
+          const float e0 = exp2f(fmaf(__uint_as_float(v[i]), sl, -m_ref));
+          const float e1 = exp2_fma(fmaf(__uint_as_float(v[i + 1]), sl, -m_ref));
+          __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
+          sum0 += __low2float(bb);
+          sum1 += __high2float(bb);
+          v[i / 2] = *reinterpret_cast<uint32_t*>(&bb);
+        }
+        tmem_st32(s_addr + hh * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      }
+      // S_t(j) was issued after PV_t(j-1): O_t is complete up to j-1 and no
+      // MMA touches it until P_t(j) is published (rescaled here, once the
+      // scores are out of registers)
+      if (__any_sync(0xffffffffu, rescale && j > 0)) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c0, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(o_addr + c0, o);
+        }
+      }
+      if (tr0) fstamp(p, FTR_SOFTMAX, j);
+      l_run = l_run * alpha + (sum0 + sum1);
+      m_run = m_use;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+      if (tr0) fstamp(p, FTR_PARRIVE, j);
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    const bool write = r < rows;
+    const size_t prow = static_cast<size_t>(row_base + t * BQ + r);
+    if (nkt <= 0) {
+      if (S > 1 && write) p.lse_part[(prow * p.num_heads + h) * S + z] = -INFINITY;
+    } else if (ok && mbar_wait_warp(&o_done[t], static_cast<uint32_t>((nkt - 1) & 1), abort_flag, p.status,
+                                    kStatusTimeoutTmemFull)) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+      if (S > 1) {
+        const size_t base = (prow * p.num_heads + h) * S + z;
+        if (write) p.lse_part[base] = l_run > 0.f ? m_run + __log2f(l_run) : -INFINITY;
+        float* orow = p.o_part + base * D;
+#pragma unroll 1
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c0, o);
+          tmem_ld_wait();
+          if (write) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(orow + c0 + i) =
+                  make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                              __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+          }
+        }
+      } else {
+        __nv_bfloat16* orow = p.out + prow * p.ldo + h * D;
+#pragma unroll 1
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c0, o);
+          tmem_ld_wait();
+          if (write) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 w;
+              w.x = pack_bf16(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
+              w.y = pack_bf16(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+              w.z = pack_bf16(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+              w.w = pack_bf16(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + c0 + i) = w;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // Merge the key shares of split rows: out = sum_s 2^(lse_s - max) O_s / sum_s 2^(lse_s - max).
 __global__ void fa_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ lse_part, int S,
                                   int H, __nv_bfloat16* __restrict__ out, int ldo) {
@@ -558,9 +955,10 @@ int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const 
               const int* tiles, int num_tiles, const int* q_start, const int* q_len, const int* ctx_len,
               const int* block_table, const int* bt_rows, int max_pages, int num_heads, int num_kv_heads,
               float scale, void* out, int ldo, int* status, int kv_splits, float* o_part, float* lse_part,
-              cudaStream_t stream) {
+              int tile_rows, cudaStream_t stream) {
   using namespace ib200::fa;
   if (num_tiles <= 0 || q.rows <= 0) return 0;
+  if (tile_rows != 128 && (EXT || tile_rows != 256)) return -1;
   if ((ldo % 8) != 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return -1;
   if (kv_splits > 1 && (o_part == nullptr || lse_part == nullptr || (reinterpret_cast<uintptr_t>(o_part) & 15)))
     return -1;
@@ -602,10 +1000,14 @@ int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const 
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     cudaFuncSetAttribute(fa_prefill_kernel<EXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(EXT));
+    if (!EXT) cudaFuncSetAttribute(fa_prefill2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
     attr_set[dev] = true;
   }
   dim3 grid(num_heads, num_tiles, p.kv_splits);
-  fa_prefill_kernel<EXT><<<grid, NUM_THREADS, smem_bytes(EXT), stream>>>(tq, tk, tv, tqe, tke, tk8, tv8, tke8, p);
+  if (tile_rows == 256)
+    fa_prefill2_kernel<<<grid, NUM_THREADS, SMEM2, stream>>>(tq, tk, tv, tk8, tv8, p);
+  else
+    fa_prefill_kernel<EXT><<<grid, NUM_THREADS, smem_bytes(EXT), stream>>>(tq, tk, tv, tqe, tke, tk8, tv8, tke8, p);
   if (p.kv_splits > 1)
     fa_combine_kernel<<<dim3(static_cast<unsigned>(q.rows), num_heads), D, 0, stream>>>(
         o_part, lse_part, p.kv_splits, num_heads, static_cast<__nv_bfloat16*>(out), ldo);
@@ -617,7 +1019,9 @@ int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const 
 
 // q: [T, ldq] bf16 with head h at columns [h*128, h*128+128).
 // k_cache / v_cache: [num_slots, num_kv_heads*128] bf16.
-// tiles: device int32 [num_tiles, 2] (seq, q_block), longest first.
+// tiles: device int32 [num_tiles, 2] (seq, q_block of 128 rows), longest
+// first; tile_rows 256: each entry covers blocks q_block and q_block + 1
+// (two query tiles per CTA), 128: one block.
 // kv_splits > 1: each tile's key tiles are shared out over that many CTAs
 // whose partials (o_part fp32 [T*num_heads*kv_splits*128], lse_part
 // [T*num_heads*kv_splits]) a combine kernel merges into out.
@@ -626,7 +1030,7 @@ extern "C" int ib_attn_prefill(const void* q, int T, int ldq, const void* k_cach
                                const int* q_len, const int* ctx_len, const int* block_table, const int* bt_rows,
                                int max_pages,
                                int num_heads, int num_kv_heads, float scale, void* out, int ldo, int* status,
-                               int kv_splits, float* o_part, float* lse_part, cudaStream_t stream) {
+                               int kv_splits, float* o_part, float* lse_part, int tile_rows, cudaStream_t stream) {
   using namespace ib200::fa;
   if (T <= 0) return 0;
   const int kvw = num_kv_heads * D;
@@ -635,7 +1039,7 @@ extern "C" int ib_attn_prefill(const void* q, int T, int ldq, const void* k_cach
   const FaOperand fv{v_cache, num_slots, kvw, D, D, num_kv_heads};
   return fa_launch<false>(fq, fk, fv, nullptr, nullptr, tiles, num_tiles, q_start, q_len, ctx_len, block_table,
                           bt_rows, max_pages, num_heads, num_kv_heads, scale, out, ldo, status, kv_splits, o_part,
-                          lse_part, stream);
+                          lse_part, tile_rows, stream);
 }
 
 // Attention over 128 + 64 score dims (MLA prefill, not absorbed):
@@ -662,5 +1066,5 @@ extern "C" int ib_attn_prefill_ext(const void* q, int T, int ldq, int q_hs, cons
   const FaOperand fv{v, num_rows, ldv, v_hs, D, num_kv_heads};
   return fa_launch<true>(fq, fk, fv, &fqe, &fke, tiles, num_tiles, q_start, q_len, ctx_len, block_table, bt_rows,
                          max_pages, num_heads, num_kv_heads, scale, out, ldo, status, kv_splits, o_part, lse_part,
-                         stream);
+                         128, stream);
 }

@@ -220,7 +220,7 @@ class ModelRunner:
         T, S = len(ids), len(logits_rows)
         q_start, q_len, ctx_len, p_rows = pmeta
         d_lens, d_rows = dmeta
-        tiles = K.prefill_tiles(q_len) if Tp > 0 else []
+        tiles = K.prefill_tiles(q_len, getattr(self.model, "prefill_tile_rows", None)) if Tp > 0 else []
         upd_idx, upd_val = bt_updates
         parts = [("ids", ids), ("pos", pos), ("slots", slots), ("lidx", logits_rows), ("qs", q_start),
                  ("ql", q_len), ("cl", ctx_len), ("prow", p_rows), ("tiles", [x for t in tiles for x in t]),

@@ -115,6 +115,8 @@ class MLAModel:
     """Stateless forward over the paged latent cache owned by the engine
     (``k_caches`` [num_layers, slots, 576]; ``v_caches`` is unused)."""
 
+    prefill_tile_rows = 128   # the 192-dim prefill attention runs one query tile per CTA
+
     def __init__(self, cfg: MoEConfig, device: torch.device | str, seed: int = 0, tp=None, ep=None):
         """``ep``: expert parallelism under data-parallel attention - an
         object with ``rank``, ``world``, ``group`` (the all-to-all group),

@@ -46,7 +46,7 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_attn_decode": [c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float,
                            c_vp, c_vp, c_vp, c_int, c_vp],
         "ib_attn_prefill": [c_vp, c_int, c_int, c_vp, c_vp, c_ll, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int,
-                            c_int, c_int, c_float, c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp],
+                            c_int, c_int, c_float, c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_int, c_vp],
         "ib_attn_prefill_ext": [c_vp, c_int, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int, c_int, c_vp, c_int,
                                 c_int, c_vp, c_int, c_int, c_ll, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int,
                                 c_int, c_int, c_float, c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp],

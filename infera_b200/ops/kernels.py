@@ -491,11 +491,20 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, b
     return out
 
 
-def prefill_tiles(q_lens: list[int]) -> list[tuple[int, int]]:
-    """(seq, q_block) work items of 128 query rows, longest-work first."""
+# Query rows per prefill attention CTA: 256 runs two 128-row tiles per CTA
+# that share every K / V tile and alternate on the tensor core (128-dim
+# heads); 128 runs one tile (INFERA_PREFILL_TILE_ROWS=128).
+PREFILL_TILE_ROWS = int(_os.environ.get("INFERA_PREFILL_TILE_ROWS", "256"))
+
+
+def prefill_tiles(q_lens: list[int], rows: int | None = None) -> list[tuple[int, int]]:
+    """(seq, q_block) work items of ``rows`` query rows (q_block counts
+    128-row blocks; a 256-row item covers q_block and q_block + 1),
+    longest-work first."""
+    step = (rows or PREFILL_TILE_ROWS) // 128
     items = []
     for s, n in enumerate(q_lens):
-        for b in range((n + 127) // 128):
+        for b in range(0, (n + 127) // 128, step):
             items.append((s, b))
     # later blocks of long sequences see more keys; schedule them first
     items.sort(key=lambda it: -(it[1]))
@@ -519,12 +528,14 @@ def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
                  q_start: torch.Tensor, q_len: torch.Tensor, ctx_len: torch.Tensor, tiles: torch.Tensor, hq: int,
                  hkv: int, scale: float, out: torch.Tensor | None = None,
                  host_meta: tuple[list[int], list[int]] | None = None,
-                 bt_rows: torch.Tensor | None = None, kv_splits: int | None = None) -> torch.Tensor:
+                 bt_rows: torch.Tensor | None = None, kv_splits: int | None = None,
+                 tile_rows: int | None = None) -> torch.Tensor:
     """Causal attention for chunks of new tokens whose K/V already sit in the
     paged cache. q: [T, >=hq*D]; q_start/q_len/ctx_len: int32 [num_seqs];
-    tiles: int32 [num_tiles, 2] from :func:`prefill_tiles`. ``kv_splits``:
-    key shares per tile (None: :func:`prefill_kv_splits` from ``host_meta``,
-    1 without it)."""
+    tiles: int32 [num_tiles, 2] from :func:`prefill_tiles` with the same
+    ``tile_rows`` (None: ``PREFILL_TILE_ROWS``). ``kv_splits``: key shares
+    per tile (None: :func:`prefill_kv_splits` from ``host_meta``, 1 without
+    it)."""
     T = q.shape[0]
     D = k_cache.shape[1] // hkv
     if not q.is_cuda:
@@ -553,7 +564,7 @@ def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
                                            q_len.data_ptr(), ctx_len.data_ptr(), block_table.data_ptr(),
                                            _ptr(bt_rows), block_table.stride(0), hq, hkv, scale, out.data_ptr(),
                                            out.stride(0), sc.status.data_ptr(), kv_splits, o_ptr, lse_ptr,
-                                           _stream())
+                                           tile_rows or PREFILL_TILE_ROWS, _stream())
     _native.check(rc, "ib_attn_prefill")
     _count(2 if kv_splits > 1 else 1)
     return out

@@ -107,7 +107,7 @@ def test_mla_prefill_unabsorbed_matches_fp32(hq, q_lens, ctx_lens):
     for n in q_lens[:-1]:
         starts.append(starts[-1] + n)
     i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")  # noqa: E731
-    tiles = i32(K.prefill_tiles(q_lens)).view(-1, 2)
+    tiles = i32(K.prefill_tiles(q_lens, 128)).view(-1, 2)
     args = (cache, bt, rows, (q_lens, ctx_lens), i32(starts), i32(q_lens), i32(ctx_lens), tiles)
     out = M.mla_prefill(qb, q_full, *args, w_up, hq, 128, 128, 0.07)
     torch.cuda.synchronize()
