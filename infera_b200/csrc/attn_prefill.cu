@@ -31,6 +31,8 @@
 //
 // Reference parity: the reference runs prefill attention inside vLLM /
 // SGLang / AITER (not in its tree); this is this framework's own kernel.
+#include <cstdlib>
+
 #include "sm100.cuh"
 #include "tma_host.h"
 
@@ -522,12 +524,54 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // alone.
 constexpr int SMEM2 = 1024 + (4 + KV_STAGES * 4) * BLK + 1024;
 
+// Packed fp32 pairs (Blackwell f32x2 FMA / add): two lanes of work per issue.
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x for two values on the FMA pipe, packed: x = n + f with n = round(x)
+// (adding 1.5 * 2^23 leaves n in the low mantissa bits) and f in
+// [-0.5, 0.5]; 2^f from a cubic fitted here to minimise the relative error
+// on that interval (7.5e-5 at fp32, far below bf16's 3.9e-3); n joins the
+// exponent by an integer add of n << 23 (the constant's own bits shift out).
+// Inputs below -125 are clamped (the result stays a normal number).
+__device__ __forceinline__ void exp2_poly2(float xa, float xb, float& ea, float& eb) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  const float a = fmaxf(xa, -125.0f), b = fmaxf(xb, -125.0f);
+  const float ta = a + kRound, tb = b + kRound;
+  const uint64_t n2 = fadd2(f2pack(ta, tb), f2pack(-kRound, -kRound));
+  const uint64_t f2 = ffma2(n2, f2pack(-1.0f, -1.0f), f2pack(a, b));
+  uint64_t p2 = ffma2(f2pack(0.05517098f, 0.05517098f), f2, f2pack(0.24260972f, 0.24260972f));
+  p2 = ffma2(p2, f2, f2pack(0.69326097f, 0.69326097f));
+  p2 = ffma2(p2, f2, f2pack(0.99992818f, 0.99992818f));
+  float pa, pb;
+  f2unpack(p2, pa, pb);
+  ea = __uint_as_float((__float_as_uint(ta) << 23) + __float_as_uint(pa));
+  eb = __uint_as_float((__float_as_uint(tb) << 23) + __float_as_uint(pb));
+}
+
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
 
+template <bool PACKED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fa_prefill2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmK8,
@@ -794,11 +838,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float m_use = rescale ? m_new : m_run;
       const float alpha = (j == 0 || m_run == -INFINITY) ? 0.f : exp2f(m_run - m_use);
       const float m_ref = m_use == -INFINITY ? 0.f : m_use;
-      // pass 2, per 64 keys: P = 2^(s*scale - m), even keys on the MUFU unit,
-      // odd keys with the FMA-pipe polynomial (masked keys give exactly 0),
-      // packed bf16 pairs written over the S columns already read
+      // pass 2, per 64 keys: P = 2^(s*scale - m), half of the keys on the
+      // MUFU unit and half with an FMA-pipe polynomial (masked keys give
+      // exactly 0), packed bf16 pairs written over the S columns already read
       float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
+#pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t v[64];
         tmem_ld32(s_addr + hh * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
@@ -809,14 +853,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int i = 0; i < 64; ++i)
             if (hh * 64 + i > lim) v[i] = __float_as_uint(-INFINITY);
         }
+        if constexpr (PACKED) {
+          // scale and shift pairs with one f32x2 FMA; keys 4c and 4c+2 on
+          // MUFU, 4c+1 and 4c+3 through the packed polynomial; row sums as
+          // f32x2 adds of the unrounded values
+          const uint64_t sl2 = f2pack(sl, sl), nm2 = f2pack(-m_ref, -m_ref);
+          uint64_t s2 = f2pack(0.f, 0.f);
 #pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          const float e0 = exp2f(fmaf(__uint_as_float(v[i]), sl, -m_ref));
-          const float e1 = exp2_fma(fmaf(__uint_as_float(v[i + 1]), sl, -m_ref));
-          __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
-          sum0 += __low2float(bb);
-          sum1 += __high2float(bb);
-          v[i / 2] = *reinterpret_cast<uint32_t*>(&bb);
+          for (int i = 0; i < 64; i += 4) {
+            float x0, x1, x2, x3;
+            f2unpack(ffma2(f2pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), sl2, nm2), x0, x1);
+            f2unpack(ffma2(f2pack(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3])), sl2, nm2), x2, x3);
+            const float e0 = exp2f(x0), e2 = exp2f(x2);
+            float e1, e3;
+            exp2_poly2(x1, x3, e1, e3);
+            if (!full_tile) {
+              if (hh * 64 + i + 1 > lim) e1 = 0.f;
+              if (hh * 64 + i + 3 > lim) e3 = 0.f;
+            }
+            s2 = fadd2(s2, f2pack(e0, e1));
+            s2 = fadd2(s2, f2pack(e2, e3));
+            v[i / 2] = pack_bf16(e0, e1);
+            v[i / 2 + 1] = pack_bf16(e2, e3);
+          }
+          float a, b;
+          f2unpack(s2, a, b);
+          sum0 += a;
+          sum1 += b;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) {
+            const float e0 = exp2f(fmaf(__uint_as_float(v[i]), sl, -m_ref));
+            const float e1 = exp2_fma(fmaf(__uint_as_float(v[i + 1]), sl, -m_ref));
+            __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
+            sum0 += __low2float(bb);
+            sum1 += __high2float(bb);
+            v[i / 2] = *reinterpret_cast<uint32_t*>(&bb);
+          }
         }
         tmem_st32(s_addr + hh * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
       }
@@ -950,6 +1023,16 @@ bool fa_tmap(CUtensorMap* m, const FaOperand& o, int box_rows) {
   return cached_tmap_2d(m, o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, o.rows, cols, o.ld, box_rows, 64);
 }
 
+// Packed f32x2 softmax arithmetic in the two-tile kernel (INFERA_FA_PACKED=0:
+// scalar, for comparison).
+bool fa_packed_softmax() {
+  static const bool v = [] {
+    const char* e = std::getenv("INFERA_FA_PACKED");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return v;
+}
+
 template <bool EXT>
 int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const FaOperand* qe, const FaOperand* ke,
               const int* tiles, int num_tiles, const int* q_start, const int* q_len, const int* ctx_len,
@@ -1000,12 +1083,16 @@ int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const 
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     cudaFuncSetAttribute(fa_prefill_kernel<EXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(EXT));
-    if (!EXT) cudaFuncSetAttribute(fa_prefill2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
+    if (!EXT) {
+      cudaFuncSetAttribute(fa_prefill2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
+      cudaFuncSetAttribute(fa_prefill2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
+    }
     attr_set[dev] = true;
   }
   dim3 grid(num_heads, num_tiles, p.kv_splits);
   if (tile_rows == 256)
-    fa_prefill2_kernel<<<grid, NUM_THREADS, SMEM2, stream>>>(tq, tk, tv, tk8, tv8, p);
+    (fa_packed_softmax() ? fa_prefill2_kernel<true> : fa_prefill2_kernel<false>)<<<grid, NUM_THREADS, SMEM2,
+                                                                                   stream>>>(tq, tk, tv, tk8, tv8, p);
   else
     fa_prefill_kernel<EXT><<<grid, NUM_THREADS, smem_bytes(EXT), stream>>>(tq, tk, tv, tqe, tke, tk8, tv8, tke8, p);
   if (p.kv_splits > 1)
