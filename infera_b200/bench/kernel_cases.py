@@ -150,9 +150,11 @@ def run_case(case: str, iters: int) -> dict:
         return {"case": case, "ms": ms, "gbs_all_keys": by_all / ms / 1e6, "gbs_unique_pages": by_unique / ms / 1e6,
                 "bytes_all": by_all, "bytes_unique": by_unique, "splits": sp, "tiles_per_split": tps,
                 "l2_policy": l2, "rel_err": float((got - ref).norm() / ref.norm())}
-    if case in ("prefill_attn", "prefill_attn_prefix", "prefill_attn_chunk"):
+    if case in ("prefill_attn", "prefill_attn_prefix", "prefill_attn_chunk", "prefill_attn_8k",
+                "prefill_attn_32k"):
         ql, ctx = {"prefill_attn": (2048, 2048), "prefill_attn_prefix": (1024, 8192),
-                   "prefill_attn_chunk": (224, 8192)}[case]
+                   "prefill_attn_chunk": (224, 8192), "prefill_attn_8k": (8192, 8192),
+                   "prefill_attn_32k": (8192, 32768)}[case]
         pages = ctx // 16
         kc = torch.randn(pages * 16, hkv * D, device=dev, generator=g).to(bf)
         vc = torch.randn(pages * 16, hkv * D, device=dev, generator=g).to(bf)
