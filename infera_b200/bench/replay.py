@@ -44,6 +44,7 @@ class EngineReplay:
         self.ev0 = None
         self.step_events: list = []         # (event, host_time)
         self.step_shapes: list = []         # (prompt tokens, decoding sequences) per step
+        self.step_kv: list = []             # cached tokens read by decode attention per step
         self.step_host: list = []           # (host issue s, host wait-for-device s) per step
         self.token_steps: dict[str, list[int]] = {}
         self.collected: dict[str, list[int]] = {}
@@ -132,6 +133,7 @@ class EngineReplay:
         outs = self.eng.step()
         step_idx = len(self.step_events)
         self.step_shapes.append(getattr(self.eng, "last_step_shape", (0, 0)))
+        self.step_kv.append(getattr(self.eng, "last_step_kv", 0))
         runner = getattr(self.eng, "runner", None)
         self.step_host.append(getattr(runner, "last_timing", (0.0, 0.0)))
         if self.device_timing:
@@ -189,10 +191,41 @@ class EngineReplay:
         # host_issue: host time from the start of the forward to its last
         # launch; host_wait: time the host then waited for the device (near
         # zero means the step was bound by the host's launch rate)
-        return {k: {"n": len(v), "p50_ms": round(percentile(v, 50), 3), "p99_ms": round(percentile(v, 99), 3),
-                    "mean_prompt_tokens": round(sum(toks[k]) / len(v), 1),
-                    "host_issue_p50_ms": round(percentile(issue[k], 50), 3),
-                    "host_wait_p50_ms": round(percentile(wait[k], 50), 3)} for k, v in sorted(kinds.items())}
+        out = {k: {"n": len(v), "p50_ms": round(percentile(v, 50), 3), "p99_ms": round(percentile(v, 99), 3),
+                   "mean_prompt_tokens": round(sum(toks[k]) / len(v), 1),
+                   "host_issue_p50_ms": round(percentile(issue[k], 50), 3),
+                   "host_wait_p50_ms": round(percentile(wait[k], 50), 3)} for k, v in sorted(kinds.items())}
+        # decode steps against their byte roofline: every weight byte plus
+        # the K/V bytes of the cached tokens read, at the measured copy rate
+        wb, kvb = self.roofline_bytes()
+        if "decode" in out and wb:
+            kv = [self.step_kv[i] for i in range(1, len(times)) if window[0] <= times[i] <= window[1]
+                  and i < len(self.step_kv) and self.step_shapes[i][1] and not self.step_shapes[i][0]]
+            if kv:
+                roof = [(wb + kvb * n) / self.PEAK_HBM * 1e3 for n in kv]
+                r50 = percentile(roof, 50)
+                out["decode"].update(mean_kv_tokens=round(sum(kv) / len(kv)), weight_gb=round(wb / 1e9, 2),
+                                     roofline_p50_ms=round(r50, 3),
+                                     frac_of_roofline_p50=round(r50 / out["decode"]["p50_ms"], 3)
+                                     if out["decode"]["p50_ms"] else None)
+        return out
+
+    PEAK_HBM = 6418.2e9   # measured B200 copy rate (bytes/s)
+
+    def roofline_bytes(self) -> tuple[int, int]:
+        """(weight bytes, K/V bytes per cached token) of this GPU's model."""
+        m = getattr(self.eng, "model", None)
+        w = getattr(m, "w", None)
+        cfg = getattr(m, "cfg", None)
+        if w is None or cfg is None or not hasattr(w, "nbytes"):
+            return 0, 0
+        hd = getattr(cfg, "head_dim", 0)
+        kvh = getattr(cfg, "num_kv_heads", 0)
+        if hd and kvh:
+            per_tok = cfg.num_layers * kvh * hd * 2 * 2
+        else:  # latent cache: one 576-element row per token and layer
+            per_tok = cfg.num_layers * 576 * 2
+        return w.nbytes(), per_tok
 
     def resolve(self) -> list[ReqRecord]:
         """Convert step indices into timestamps (device when available)."""

@@ -176,6 +176,7 @@ class LLMEngine:
         self.cmd_log: list | None = None
         self.num_steps = 0
         self.last_step_shape = (0, 0)
+        self.last_step_kv = 0
         self.clock: Callable[[], float] = time.monotonic
         self.counters = {"prompt_tokens": 0, "generation_tokens": 0, "finished": 0, "preemptions": 0}
         # named phase ranges (torch.profiler record_function + NVTX) while a
@@ -401,6 +402,8 @@ class LLMEngine:
         self.num_steps += 1
         # (prompt tokens, decoding sequences) of this step, for step-time profiles
         self.last_step_shape = (sum(c.num_tokens for c in sched.prefills), len(sched.decodes))
+        # cached tokens the step's decode attention read (the step's KV bytes)
+        self.last_step_kv = sum(c.req.num_computed for c in sched.decodes)
         for c in sched.prefills:
             c.req.num_computed = c.start + c.num_tokens
             self.counters["prompt_tokens"] += c.num_tokens

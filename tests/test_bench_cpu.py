@@ -48,6 +48,13 @@ def test_replay_runs_multiturn_on_cpu():
     for r in done:
         assert r.first_token >= r.arrival
         assert len(r.token_times) == r.out_len
+    # decode steps carry their byte roofline (weights + cached K/V read)
+    prof = rp.step_profile((0.0, 1e9))
+    wb, per_tok = rp.roofline_bytes()
+    assert wb > 0 and per_tok > 0
+    if "decode" in prof:
+        d = prof["decode"]
+        assert d["roofline_p50_ms"] > 0 and d["mean_kv_tokens"] > 0
 
 
 def test_goodput_cohort_by_arrival():
