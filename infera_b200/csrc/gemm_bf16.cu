@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     }
   } else if (FP8 && warp >= 6) {
     // scale-factor stagers: one warp per TMEM lane quadrant writes the same
-    // values into its own quadrant. The scale bytes of stage i+4 are loaded
+    // values into its own quadrant. The scale bytes of stage i+8 are loaded
     // while stage i is stored, so a global-load latency is not paid once
     // per stage.
     const int q = warp & 3;
@@ -535,7 +535,9 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     // fetch cursor over the (tile, k-block) sequence this CTA walks
     int ft = blockIdx.x, fkb = 0, fkb1 = 0, fwrow = 0, ftok0 = 0;
     bool fresh = true;
-    auto fetch = [&](uint32_t& wb, uint32_t (&r)[8]) -> bool {
+    // r packs the 8 token-scale bytes of a lane (tokens c * 32 + lane,
+    // c = 0..7) four to a register
+    auto fetch = [&](uint32_t& wb, uint32_t (&r)[2]) -> bool {
       while (true) {
         if (ft >= total) return false;
         if (fresh) {
@@ -557,22 +559,25 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
         fresh = true;
       }
       wb = __ldg(p.sf_w + static_cast<size_t>(fwrow) * p.sf_w_ld + fkb);
+      r[0] = r[1] = 0;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const int tok = ftok0 + c * 32 + lane;
-        r[c] = (c * 32 < p.bn && tok < p.M) ? __ldg(p.sf_a + static_cast<size_t>(fkb) * p.sf_a_ld + tok) : 127u;
+        const uint32_t b =
+            (c * 32 < p.bn && tok < p.M) ? __ldg(p.sf_a + static_cast<size_t>(fkb) * p.sf_a_ld + tok) : 127u;
+        r[c >> 2] |= b << (8 * (c & 3));
       }
       ++fkb;
       return true;
     };
     uint32_t stage = 0, phase = 0;
     long long sf_steps = 0;
-    auto store = [&](uint32_t wb, const uint32_t (&r)[8]) -> bool {
+    auto store = [&](uint32_t wb, const uint32_t (&r)[2]) -> bool {
       if (!mbar_wait_warp(&empty[stage], phase ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) return false;
       tc_fence_after();  // the MMAs that read this slot before have completed
       uint32_t rr[8];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) rr[c] = r[c] * 0x01010101u;
+      for (int c = 0; c < 8; ++c) rr[c] = ((r[c >> 2] >> (8 * (c & 3))) & 0xFFu) * 0x01010101u;
       const uint32_t w4 = wb * 0x01010101u;
       const uint32_t slot = tmem_base + lane_base + SF_COL0 + stage * SF_SLOT;
       tmem_st4(slot, w4, w4, w4, w4);
@@ -589,10 +594,11 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       }
       return true;
     };
-    // four register sets in flight: the loads of stage i+4 are issued when
-    // stage i is stored (compile-time indices keep them in registers)
-    constexpr int kAhead = 4;
-    uint32_t wv[kAhead], rv[kAhead][8];
+    // eight register sets in flight: the loads of stage i+8 are issued when
+    // stage i is stored (compile-time indices keep them in registers), so a
+    // DRAM round trip under full load is covered by 8 weight stages
+    constexpr int kAhead = 8;
+    uint32_t wv[kAhead], rv[kAhead][2];
     bool has[kAhead];
     bool arrived = true;
     if (p.wait_flag != nullptr && !p.wait_per_expert) {   // the activation scales arrive with the dispatched rows
