@@ -1,7 +1,7 @@
 """Kernel-time breakdown of one decode step and one mixed step (a prompt
 chunk joining running decodes) of the serving engine.
 
-    python -m infera_b200.bench.step_breakdown [--model qwen3-8b] [--decodes 48] [--context 2048]
+    python -m infera_b200.bench.step_breakdown [--model llama-3.1-8b] [--decodes 48] [--context 2048]
         [--chunk 224] [--top 15]
 
 Builds the engine, fills it with ``--decodes`` running sequences of
@@ -41,7 +41,7 @@ def _top(prof, top: int) -> tuple[float, list[dict]]:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--model", default="qwen3-8b")
+    ap.add_argument("--model", default="llama-3.1-8b")
     ap.add_argument("--decodes", type=int, default=48)
     ap.add_argument("--context", type=int, default=2048)
     ap.add_argument("--chunk", type=int, default=224)
