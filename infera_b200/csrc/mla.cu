@@ -34,11 +34,21 @@
 //
 // Reference parity: the reference serves DeepSeek-V3 MLA through its
 // engines (AITER MLA in vLLM / SGLang); none of that code is in its tree.
+#include <cstdlib>
+
 #include "sm100.cuh"
 #include "tma_host.h"
 
 namespace ib200 {
 namespace mla {
+
+inline int mla_key_tile() {
+  static const int v = [] {
+    const char* e = std::getenv("INFERA_MLA_TILE");
+    return e != nullptr && std::atoi(e) == 32 ? 32 : 128;
+  }();
+  return v;
+}
 
 constexpr int DL = 512;
 constexpr int DR = 64;
@@ -372,6 +382,367 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------------
+// 128-key tiles (eight pages): the S MMAs run at N = 128 (128 heads x 128
+// keys x 16 dims each), where an MMA's math outlasts its fixed issue cost,
+// instead of N = 32. A tile's 576 key dims no longer fit next to the
+// resident Q, so keys stream through a 5-slot ring of [128 keys x 64 dims]
+// chunks (16 KiB) in the order the MMA warp consumes them:
+//   S chunks 0..8 of tile j, then V chunks 0..3 of tile j-1
+// (V = this CTA's 256 latent dims, read again from L2: the S chunks of the
+// same dims were released right after their MMAs).
+//   warp 0      TMA producer (one lane)
+//   warp 1      MMA issuer: S(j) = Q K^T into S buffer j&1 (9 x 4 MMAs,
+//               M 128, N 128), then O[:, 64v:+64] += P(j-1) V_v
+//               (4 x 8 MMAs, N 64, P from TMEM); S(j+1) overwrites P(j-1)
+//               only after PV(j-1) was issued (tcgen05 MMAs run in order)
+//   warps 2..5  softmax, thread = head row, 128 keys per tile; P as bf16
+//               pairs over the first 64 columns of the tile's S
+// TMEM: S 2 x 128 columns, O 256 columns.
+constexpr int BT2 = 128;
+constexpr int RING = 5;
+constexpr int CH2 = BT2 * 128;                              // 16 KiB
+constexpr int SMEM2 = 1024 + NCH * QCH + RING * CH2 + 256;
+constexpr uint32_t S2_COL1 = 128, O2_COL = 256;
+
+__device__ __forceinline__ uint64_t m2pack(float a, float b) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ void m2unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t m2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    mla_decode128_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+                         const __grid_constant__ CUtensorMap tmKV8, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sR = sQ + NCH * QCH;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sR + RING * CH2);
+  uint64_t* q_full = bars;
+  uint64_t* r_full = bars + 1;           // [RING]
+  uint64_t* r_empty = r_full + RING;     // [RING]
+  uint64_t* s_full = r_empty + RING;     // [2] by tile parity
+  uint64_t* p_full = s_full + 2;         // [2]
+  uint64_t* o_done = p_full + 2;         // [2]
+  uint64_t* drain = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qi = blockIdx.x;
+  const int half = blockIdx.y;
+  const int sp = blockIdx.z;
+  const int kvlen = p.q_kvlen[qi];
+  const int n_tiles_all = (kvlen + BT2 - 1) / BT2;
+  const int tps = (n_tiles_all + p.splits - 1) / p.splits;
+  const int tile0 = sp * tps;
+  const int n_tiles = max(0, min(n_tiles_all - tile0, tps));
+  const bool cta0 = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < RING; ++s) {
+      mbar_init(&r_full[s], 1);
+      mbar_init(&r_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 128);
+      mbar_init(&o_done[b], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmKV);
+    tma_prefetch_desc(&tmKV8);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && n_tiles > 0) {
+      const uint64_t pol_q = policy_evict_first();
+      const uint64_t pol_kv = policy_evict_last();  // V chunks and the other value half read the same rows
+      mbar_expect_tx(q_full, NCH * QCH);
+      for (int c = 0; c < NCH; ++c) tma_load_2d(sQ + c * QCH, &tmQ, q_full, c * 64, qi * p.hq, pol_q);
+      const int* bt = p.block_table + static_cast<size_t>(p.q_row[qi]) * p.max_pages;
+      const int n_pages = (kvlen + PAGE - 1) / PAGE;
+      long long seq = 0;  // chunks issued so far (ring position)
+      bool ok = true;
+      int pg[8];
+      auto load_chunk = [&](int col) -> bool {
+        const int st = static_cast<int>(seq % RING);
+        const uint32_t ph = static_cast<uint32_t>((seq / RING) & 1);
+        if (!mbar_wait(&r_empty[st], ph ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) return false;
+        uint8_t* dst = sR + st * CH2;
+        mbar_expect_tx(&r_full[st], CH2);
+        bool run = true;
+#pragma unroll
+        for (int i = 1; i < 8; ++i) run = run && pg[i] == pg[0] + i;
+        if (run) {
+          tma_load_2d(dst, &tmKV8, &r_full[st], col, pg[0] * PAGE, pol_kv);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) tma_load_2d(dst + i * PAGE * 128, &tmKV, &r_full[st], col, pg[i] * PAGE, pol_kv);
+        }
+        ++seq;
+        return true;
+      };
+      // pages of tile t (past the sequence's last page: its first page again,
+      // those keys are masked)
+      auto pages_of = [&](int t) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int lp = t * 8 + i;
+          pg[i] = __ldg(bt + (lp < n_pages ? lp : t * 8));
+        }
+      };
+      for (int j = 0; j <= n_tiles && ok; ++j) {
+        if (j < n_tiles) {
+          pages_of(tile0 + j);
+          for (int c = 0; c < NCH && ok; ++c) ok = load_chunk(c * 64);
+          stamp(p, cta0, TR_TMA, j);
+        }
+        if (j >= 1 && ok) {
+          pages_of(tile0 + j - 1);
+          for (int v = 0; v < 4 && ok; ++v) ok = load_chunk(half * DV + v * 64);
+        }
+      }
+      // drain: every issued copy must land before the CTA exits
+      mbar_wait(q_full, 0, nullptr, nullptr, 0, kWaitLimitNs / 4);
+      const long long first = seq > RING ? seq - RING : 0;
+      for (long long i = first; i < seq; ++i)
+        mbar_wait(&r_full[i % RING], static_cast<uint32_t>((i / RING) & 1), nullptr, nullptr, 0, kWaitLimitNs / 4);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t idesc_qk = make_idesc_bf16(128, BT2);
+      const uint32_t idesc_pv = make_idesc_bf16(128, 64, true);
+      const uint32_t q_addr = smem_u32(sQ);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kStatusTimeoutFull);
+      long long seq = 0;
+      auto take = [&](uint32_t& addr) -> bool {
+        const int st = static_cast<int>(seq % RING);
+        if (!mbar_wait(&r_full[st], static_cast<uint32_t>((seq / RING) & 1), abort_flag, p.status,
+                       kStatusTimeoutFull))
+          return false;
+        tc_fence_after();
+        addr = smem_u32(sR + st * CH2);
+        return true;
+      };
+      auto release = [&]() {
+        umma_commit(&r_empty[seq % RING]);
+        ++seq;
+      };
+      for (int j = 0; j <= n_tiles && ok; ++j) {
+        if (j < n_tiles) {
+          const uint32_t s_col = (j & 1) ? S2_COL1 : 0u;
+          for (int c = 0; c < NCH && ok; ++c) {
+            uint32_t k_addr;
+            if (!(ok = take(k_addr))) break;
+            if (c == 0) stamp(p, cta0, TR_KVFULL, j);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = make_sw128_desc(q_addr + c * QCH + kk * 32, 16, 1024);
+              const uint64_t bd = make_sw128_desc(k_addr + kk * 32, 16, 1024);
+              umma_bf16(tmem + s_col, ad, bd, idesc_qk, (c > 0 || kk > 0) ? 1u : 0u);
+            }
+            release();
+          }
+          if (!ok) break;
+          umma_commit(&s_full[j & 1]);
+          stamp(p, cta0, TR_SISSUE, j);
+        }
+        if (j >= 1) {
+          const int jj = j - 1;
+          if (!mbar_wait(&p_full[jj & 1], static_cast<uint32_t>((jj >> 1) & 1), abort_flag, p.status,
+                         kStatusTimeoutTmemEmpty)) {
+            ok = false;
+            break;
+          }
+          stamp(p, cta0, TR_PFULL, jj);
+          tc_fence_after();
+          const uint32_t p_col = (jj & 1) ? S2_COL1 : 0u;
+          for (int v = 0; v < 4 && ok; ++v) {
+            uint32_t v_addr;
+            if (!(ok = take(v_addr))) break;
+#pragma unroll
+            for (int s = 0; s < BT2 / 16; ++s) {
+              // MN-major V chunk: keys 16s.. start 16 rows (2 KiB) further; SBO = 8 keys
+              const uint64_t bd = make_sw128_desc(v_addr + s * 16 * 128, CH2, 1024);
+              umma_bf16_ts(tmem + O2_COL + v * 64, tmem + p_col + s * 8, bd, idesc_pv,
+                           (jj > 0 || s > 0) ? 1u : 0u);
+            }
+            release();
+          }
+          if (!ok) break;
+          umma_commit(&o_done[jj & 1]);
+        }
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, p.status, kStatusTimeoutFull);
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;  // head row
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    const float sl = p.scale_log2;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      if (!mbar_wait_warp(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status,
+                          kStatusTimeoutTmemFull)) {
+        ok = false;
+        break;
+      }
+      if (r == 0) stamp(p, cta0, TR_SFULL, j);
+      tc_fence_after();
+      const uint32_t s_addr = lane_addr + ((j & 1) ? S2_COL1 : 0u);
+      const int lim = kvlen - (tile0 + j) * BT2;  // keys c < lim are valid
+      uint32_t v[128];
+      tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&v[64]));
+      tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&v[96]));
+      tmem_ld_wait();
+      if (lim < BT2) {
+#pragma unroll
+        for (int i = 0; i < BT2; ++i)
+          if (i >= lim) v[i] = __float_as_uint(-INFINITY);
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BT2; i += 2) {
+        mx0 = fmaxf(mx0, __uint_as_float(v[i]));
+        mx1 = fmaxf(mx1, __uint_as_float(v[i + 1]));
+      }
+      const float mx = fmaxf(mx0, mx1) * sl;
+      const float m_new = fmaxf(m_run, mx);
+      const bool rescale = (j == 0) || (m_new > m_run + 8.0f);
+      const float m_use = rescale ? m_new : m_run;
+      const float alpha = (j == 0) ? 0.f : exp2f(m_run - m_use);
+      const bool warp_rescale = __any_sync(0xffffffffu, rescale && j > 0);
+      // P goes over S(j)'s own columns, which no MMA in flight touches; only
+      // a rescale of O waits for every PV so far (tile j-1's)
+      if (warp_rescale) {
+        if (!mbar_wait_warp(&o_done[(j - 1) & 1], static_cast<uint32_t>(((j - 1) >> 1) & 1), abort_flag, p.status,
+                            kStatusTimeoutTmemFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (r == 0) stamp(p, cta0, TR_ODONE, j);
+      // P = 2^(s*scale - m): pairs scaled with one f32x2 FMA, exponentials on MUFU
+      const uint64_t sl2 = m2pack(sl, sl), nm2 = m2pack(-m_use, -m_use);
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < BT2; i += 2) {
+        float x0, x1;
+        m2unpack(m2fma(m2pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), sl2, nm2), x0, x1);
+        const float e0 = exp2f(x0), e1 = exp2f(x1);
+        sum0 += e0;
+        sum1 += e1;
+        v[i / 2] = pack_bf16(e0, e1);
+      }
+      tmem_st32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tmem_st32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      if (warp_rescale) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < DV; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(lane_addr + O2_COL + c0, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(lane_addr + O2_COL + c0, o);
+        }
+      }
+      l_run = l_run * alpha + (sum0 + sum1);
+      m_run = m_use;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[j & 1]);
+      if (r == 0) stamp(p, cta0, TR_PARRIVE, j);
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    const bool write = r < p.hq;
+    const size_t row = static_cast<size_t>(qi) * p.hq + r;
+    const int dv0 = half * DV;
+    if (n_tiles == 0) {
+      if (write) {
+        if (p.splits == 1) {
+          for (int c = 0; c < DV; ++c) p.out[row * DL + dv0 + c] = __float2bfloat16(0.f);
+        } else {
+          const size_t prow = (static_cast<size_t>(qi) * p.splits + sp) * p.hq + r;
+          for (int c = 0; c < DV; ++c) p.o_part[prow * DL + dv0 + c] = 0.f;
+          if (half == 0) p.lse_part[prow] = -INFINITY;
+        }
+      }
+    } else if (ok && mbar_wait_warp(&o_done[(n_tiles - 1) & 1], static_cast<uint32_t>(((n_tiles - 1) >> 1) & 1),
+                                    abort_flag, p.status, kStatusTimeoutTmemFull)) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+      const size_t prow = (static_cast<size_t>(qi) * p.splits + sp) * p.hq + r;
+#pragma unroll 1
+      for (int c0 = 0; c0 < DV; c0 += 32) {
+        uint32_t o[32];
+        tmem_ld32(lane_addr + O2_COL + c0, o);
+        tmem_ld_wait();
+        if (!write) continue;
+        if (p.splits == 1) {
+          __nv_bfloat16* dst = p.out + row * DL + dv0 + c0;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
+            w.y = pack_bf16(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+            w.z = pack_bf16(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+            w.w = pack_bf16(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + i) = w;
+          }
+        } else {
+          float* dst = p.o_part + prow * DL + dv0 + c0;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(dst + i) =
+                make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                            __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+        }
+      }
+      if (write && p.splits > 1 && half == 0) p.lse_part[prow] = m_run + log2f(l_run);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // out[row] = sum_s 2^(lse_s - m) o_s / sum_s 2^(lse_s - m); one CTA per
 // (query, head) row, 128 threads x 4 dims.
 __global__ void __launch_bounds__(128) mla_combine_kernel(const float* __restrict__ o_part,
@@ -469,6 +840,9 @@ using namespace ib200;
 // lse_part [nq, splits, hq] fp32 scratch.
 static long long* g_mla_trace = nullptr;
 
+// Keys per tile of the decode kernel: 128 (default) or 32 (INFERA_MLA_TILE=32).
+extern "C" int ib_mla_key_tile() { return mla::mla_key_tile(); }
+
 // Diagnostics: the next launches stamp CTA (0,0,0)'s pipeline events into
 // trace[7 * 64] (clock64), or stop when trace is null.
 extern "C" void ib_mla_set_trace(long long* trace) { g_mla_trace = trace; }
@@ -480,11 +854,14 @@ extern "C" int ib_mla_decode(const void* q, int nq, int hq, const void* cache, l
   using namespace ib200::mla;
   if (nq <= 0) return 0;
   if (hq < 1 || hq > 128 || splits < 1 || (splits > 1 && (o_part == nullptr || lse_part == nullptr))) return -1;
-  CUtensorMap tq, tkv;
+  CUtensorMap tq, tkv, tkv8;
   if (!cached_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<long long>(nq) * hq, DQK, DQK, 128,
                       64))
     return -2;
   if (!cached_tmap_2d(&tkv, cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, DQK, DQK, PAGE, 64)) return -2;
+  const bool wide = mla_key_tile() == BT2;
+  if (wide && !cached_tmap_2d(&tkv8, cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, DQK, DQK, BT2, 64))
+    return -2;
   Params p;
   p.q_row = q_row;
   p.q_kvlen = q_kvlen;
@@ -503,10 +880,14 @@ extern "C" int ib_mla_decode(const void* q, int nq, int hq, const void* cache, l
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(mla_decode128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
     attr_set[dev] = true;
   }
   dim3 grid(nq, 2, splits);
-  mla_decode_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tq, tkv, p);
+  if (wide)
+    mla_decode128_kernel<<<grid, NUM_THREADS, SMEM2, stream>>>(tq, tkv, tkv8, p);
+  else
+    mla_decode_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tq, tkv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return static_cast<int>(e);
   if (splits > 1) {

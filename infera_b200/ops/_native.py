@@ -100,6 +100,7 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_tp_wait_next": [c_vp, c_vp, ctypes.c_uint, c_vp, c_vp],
         "ib_mla_decode": [c_vp, c_int, c_int, c_vp, c_ll, c_vp, c_vp, c_vp, c_int, c_int, c_float, c_vp, c_vp, c_vp,
                           c_vp, c_vp],
+        "ib_mla_key_tile": [],
         "ib_mla_set_trace": [c_vp],
         "ib_ep_row_map": [c_vp, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp, c_vp],
         "ib_gemm_grouped_push": [c_vp, c_vp, c_int, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int,

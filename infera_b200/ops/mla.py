@@ -33,12 +33,33 @@ DQK = DL + DR
 PAGE = 16
 
 
+def mla_key_tile() -> int:
+    """Keys per tile of the decode kernel (128, or 32 with INFERA_MLA_TILE=32)."""
+    try:
+        return int(_native.kernels().ib_mla_key_tile())
+    except Exception:
+        return 128
+
+
 def mla_splits(nq: int, max_kvlen: int, num_sms: int = 148) -> int:
-    """Key splits per query: enough CTAs (nq x 2 value halves x splits) to
-    cover the SMs, each split keeping at least 4 tiles of 32 keys."""
-    tiles = max(1, -(-max_kvlen // 32))
-    want = max(1, -(-num_sms // (2 * max(nq, 1))))
-    return max(1, min(want, tiles // 4 if tiles >= 8 else 1, 64))
+    """Key splits per query. 32-key tiles: enough CTAs (nq x 2 value halves
+    x splits) to cover the SMs, each split keeping at least 4 tiles.
+    128-key tiles (one CTA per SM): the split count that minimises the
+    work on the busiest SM, waves x (tiles per split + one tile's worth of
+    per-CTA start-up: the resident query load and the pipeline fill),
+    fewest splits on a tie."""
+    bt = mla_key_tile()
+    tiles = max(1, -(-max_kvlen // bt))
+    if bt == 32:
+        want = max(1, -(-num_sms // (2 * max(nq, 1))))
+        return max(1, min(want, tiles // 4 if tiles >= 8 else 1, 64))
+    ctas = 2 * max(nq, 1)
+    best, best_cost = 1, None
+    for sp in range(1, min(64, tiles) + 1):
+        cost = -(-ctas * sp // num_sms) * (-(-tiles // sp) + 1)
+        if best_cost is None or cost < best_cost:
+            best, best_cost = sp, cost
+    return best
 
 
 def mla_rope_kvwrite(q: torch.Tensor, kva: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor,

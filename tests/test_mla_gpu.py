@@ -17,15 +17,21 @@ def _rel(a, b):
     return float((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12))
 
 
-@pytest.mark.parametrize("hq,lens,splits", [(128, [1, 33, 500], 1), (16, [7, 64, 2049], 1),
-                                            (128, [3000, 17], 4), (64, [0, 100, 4096], 8)])
-def test_mla_attention_matches_fp32(hq, lens, splits):
+@pytest.mark.parametrize("hq,lens,splits,contig", [(128, [1, 33, 500], 1, False), (16, [7, 64, 2049], 1, False),
+                                                   (128, [3000, 17], 4, False), (64, [0, 100, 4096], 8, False),
+                                                   (128, [1000, 4096, 129], 2, True),
+                                                   (128, [2048, 300], None, True)])
+def test_mla_attention_matches_fp32(hq, lens, splits, contig):
+    """contig: each sequence's pages consecutive (eight-page runs load as one box)."""
     g = torch.Generator(device="cuda").manual_seed(hq + len(lens))
     B = len(lens)
     pages_per = max(1, max(-(-L // 16) for L in lens))
     n_pages = B * pages_per + 3
     cache = torch.randn(n_pages * 16, 576, device="cuda", generator=g).to(torch.bfloat16)
-    perm = torch.randperm(n_pages, device="cuda", generator=g).to(torch.int32)
+    if contig:
+        perm = torch.arange(1, n_pages, device="cuda", dtype=torch.int32)
+    else:
+        perm = torch.randperm(n_pages, device="cuda", generator=g).to(torch.int32)
     bt = perm[: B * pages_per].view(B, pages_per).contiguous()
     q = (torch.randn(B, hq, 576, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
     rows = torch.arange(B, dtype=torch.int32, device="cuda")
