@@ -171,6 +171,10 @@ def run_case(case: str, iters: int) -> dict:
             ms1 = _time(lambda: K.attn_prefill(q, kc, vc, bt, *meta, tiles, hq, hkv, 1 / math.sqrt(D),
                                                kv_splits=1), iters)
             res.update(ms_unsplit=ms1, speedup_vs_unsplit=ms1 / ms)
+        if case == "prefill_attn_chunk":
+            res["ms_by_splits"] = {sp: _time(lambda: K.attn_prefill(q, kc, vc, bt, *meta, tiles, hq, hkv,
+                                                                    1 / math.sqrt(D), kv_splits=sp), iters)
+                                   for sp in (1, 2, 4, 8)}
         # one 128-row query tile per CTA, for comparison
         t1 = torch.tensor(K.prefill_tiles([ql], 128), dtype=torch.int32, device=dev)
         s1 = K.prefill_kv_splits(hq, t1.shape[0], ctx)

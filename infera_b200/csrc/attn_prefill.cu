@@ -571,7 +571,7 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 
-template <bool PACKED>
+template <bool PACKED, int POLY>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fa_prefill2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmK8,
@@ -854,32 +854,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (hh * 64 + i > lim) v[i] = __float_as_uint(-INFINITY);
         }
         if constexpr (PACKED) {
-          // scale and shift pairs with one f32x2 FMA; keys 4c and 4c+2 on
-          // MUFU, 4c+1 and 4c+3 through the packed polynomial; row sums as
-          // f32x2 adds of the unrounded values
+          // scale and shift pairs with one f32x2 FMA; POLY of every 8 keys
+          // through the packed polynomial on the FMA pipe, the rest on MUFU;
+          // row sums as f32x2 adds of the unrounded values
           const uint64_t sl2 = f2pack(sl, sl), nm2 = f2pack(-m_ref, -m_ref);
-          uint64_t s2 = f2pack(0.f, 0.f);
+          uint64_t s2a = f2pack(0.f, 0.f), s2b = s2a;
 #pragma unroll
-          for (int i = 0; i < 64; i += 4) {
-            float x0, x1, x2, x3;
-            f2unpack(ffma2(f2pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), sl2, nm2), x0, x1);
-            f2unpack(ffma2(f2pack(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3])), sl2, nm2), x2, x3);
-            const float e0 = exp2f(x0), e2 = exp2f(x2);
-            float e1, e3;
-            exp2_poly2(x1, x3, e1, e3);
-            if (!full_tile) {
-              if (hh * 64 + i + 1 > lim) e1 = 0.f;
-              if (hh * 64 + i + 3 > lim) e3 = 0.f;
+          for (int i = 0; i < 64; i += 8) {
+            float x[8], e[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              f2unpack(ffma2(f2pack(__uint_as_float(v[i + 2 * k]), __uint_as_float(v[i + 2 * k + 1])), sl2, nm2),
+                       x[2 * k], x[2 * k + 1]);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const bool poly = (POLY == 4 && (k & 1)) || (POLY == 2 && (k & 3) == 3);
+              if (!poly) e[k] = exp2f(x[k]);
             }
-            s2 = fadd2(s2, f2pack(e0, e1));
-            s2 = fadd2(s2, f2pack(e2, e3));
-            v[i / 2] = pack_bf16(e0, e1);
-            v[i / 2 + 1] = pack_bf16(e2, e3);
+            if constexpr (POLY == 4) {
+              exp2_poly2(x[1], x[3], e[1], e[3]);
+              exp2_poly2(x[5], x[7], e[5], e[7]);
+            } else if constexpr (POLY == 2) {
+              exp2_poly2(x[3], x[7], e[3], e[7]);
+            }
+            if (POLY > 0 && !full_tile) {
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                const bool poly = (POLY == 4 && (k & 1)) || (POLY == 2 && (k & 3) == 3);
+                if (poly && hh * 64 + i + k > lim) e[k] = 0.f;
+              }
+            }
+            s2a = fadd2(s2a, f2pack(e[0], e[1]));
+            s2b = fadd2(s2b, f2pack(e[2], e[3]));
+            s2a = fadd2(s2a, f2pack(e[4], e[5]));
+            s2b = fadd2(s2b, f2pack(e[6], e[7]));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[i / 2 + k] = pack_bf16(e[2 * k], e[2 * k + 1]);
           }
-          float a, b;
-          f2unpack(s2, a, b);
-          sum0 += a;
-          sum1 += b;
+          float a, b, c, d;
+          f2unpack(s2a, a, b);
+          f2unpack(s2b, c, d);
+          sum0 += a + c;
+          sum1 += b + d;
         } else {
 #pragma unroll
           for (int i = 0; i < 64; i += 2) {
@@ -1023,14 +1039,23 @@ bool fa_tmap(CUtensorMap* m, const FaOperand& o, int box_rows) {
   return cached_tmap_2d(m, o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, o.rows, cols, o.ld, box_rows, 64);
 }
 
-// Packed f32x2 softmax arithmetic in the two-tile kernel (INFERA_FA_PACKED=0:
-// scalar, for comparison).
-bool fa_packed_softmax() {
-  static const bool v = [] {
+// Softmax variant of the two-tile kernel: packed f32x2 arithmetic with 4
+// (default), 2 or 0 of every 8 exponentials on the FMA-pipe polynomial
+// (INFERA_FA_POLY), or scalar arithmetic (INFERA_FA_PACKED=0, for comparison).
+using Fa2Kernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                           const CUtensorMap, const ib200::fa::Params);
+Fa2Kernel fa2_variant() {
+  using namespace ib200::fa;
+  static const Fa2Kernel k = [] {
     const char* e = std::getenv("INFERA_FA_PACKED");
-    return !(e != nullptr && e[0] == '0');
+    if (e != nullptr && e[0] == '0') return static_cast<Fa2Kernel>(fa_prefill2_kernel<false, 4>);
+    const char* pe = std::getenv("INFERA_FA_POLY");
+    const int poly = pe != nullptr && *pe ? std::atoi(pe) : 4;
+    if (poly == 0) return static_cast<Fa2Kernel>(fa_prefill2_kernel<true, 0>);
+    if (poly == 2) return static_cast<Fa2Kernel>(fa_prefill2_kernel<true, 2>);
+    return static_cast<Fa2Kernel>(fa_prefill2_kernel<true, 4>);
   }();
-  return v;
+  return k;
 }
 
 template <bool EXT>
@@ -1084,15 +1109,16 @@ int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const 
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     cudaFuncSetAttribute(fa_prefill_kernel<EXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(EXT));
     if (!EXT) {
-      cudaFuncSetAttribute(fa_prefill2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
-      cudaFuncSetAttribute(fa_prefill2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
+      cudaFuncSetAttribute(fa_prefill2_kernel<true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
+      cudaFuncSetAttribute(fa_prefill2_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
+      cudaFuncSetAttribute(fa_prefill2_kernel<true, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
+      cudaFuncSetAttribute(fa_prefill2_kernel<false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
     }
     attr_set[dev] = true;
   }
   dim3 grid(num_heads, num_tiles, p.kv_splits);
   if (tile_rows == 256)
-    (fa_packed_softmax() ? fa_prefill2_kernel<true> : fa_prefill2_kernel<false>)<<<grid, NUM_THREADS, SMEM2,
-                                                                                   stream>>>(tq, tk, tv, tk8, tv8, p);
+    fa2_variant()<<<grid, NUM_THREADS, SMEM2, stream>>>(tq, tk, tv, tk8, tv8, p);
   else
     fa_prefill_kernel<EXT><<<grid, NUM_THREADS, smem_bytes(EXT), stream>>>(tq, tk, tv, tqe, tke, tk8, tv8, tke8, p);
   if (p.kv_splits > 1)
