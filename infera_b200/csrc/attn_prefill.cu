@@ -1039,9 +1039,13 @@ bool fa_tmap(CUtensorMap* m, const FaOperand& o, int box_rows) {
   return cached_tmap_2d(m, o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, o.rows, cols, o.ld, box_rows, 64);
 }
 
-// Softmax variant of the two-tile kernel: packed f32x2 arithmetic with 4
-// (default), 2 or 0 of every 8 exponentials on the FMA-pipe polynomial
+// Softmax variant of the two-tile kernel: packed f32x2 arithmetic with 0
+// (default), 2 or 4 of every 8 exponentials on the FMA-pipe polynomial
 // (INFERA_FA_POLY), or scalar arithmetic (INFERA_FA_PACKED=0, for comparison).
+// All on MUFU measured fastest: the softmax is bound by issue slots, and an
+// exponential costs one MUFU issue against about six FMA-pipe issues (8192 x
+// 8192 causal: 0.516 ms all on MUFU, 0.536 ms with 2 of 8 and 0.594 ms with
+// 4 of 8 on the polynomial).
 using Fa2Kernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
                            const CUtensorMap, const ib200::fa::Params);
 Fa2Kernel fa2_variant() {
@@ -1050,7 +1054,7 @@ Fa2Kernel fa2_variant() {
     const char* e = std::getenv("INFERA_FA_PACKED");
     if (e != nullptr && e[0] == '0') return static_cast<Fa2Kernel>(fa_prefill2_kernel<false, 4>);
     const char* pe = std::getenv("INFERA_FA_POLY");
-    const int poly = pe != nullptr && *pe ? std::atoi(pe) : 4;
+    const int poly = pe != nullptr && *pe ? std::atoi(pe) : 0;
     if (poly == 0) return static_cast<Fa2Kernel>(fa_prefill2_kernel<true, 0>);
     if (poly == 2) return static_cast<Fa2Kernel>(fa_prefill2_kernel<true, 2>);
     return static_cast<Fa2Kernel>(fa_prefill2_kernel<true, 4>);

@@ -116,7 +116,17 @@ struct Params {
   unsigned int wait_target;
   uint64_t wait_limit_ns;   // bound of that wait (0: kWaitLimitNs)
   int wait_per_expert;      // grouped: wait_flag[e] per local expert, waited before each of e's tiles
-  int streamk;              // each CTA takes an equal share of all (tile, k-block) steps (fp32 atomic epilogue)
+  int streamk;              // each CTA takes an equal share of the (tile, k-block) steps of tiles
+                            // [dp_tiles, total) (fp32 atomic epilogue), after whole tiles blockIdx.x,
+                            // +gridDim.x below dp_tiles written directly (epi_dp into out_dp)
+  int dp_tiles;
+  int epi_dp;
+  void* out_dp;
+  // optional: per-tile counters of k-blocks accumulated into the workspace
+  // (zero between launches); the CTA whose share completes a tile reads the
+  // tile back, stores it (epi_dp into out_dp) and re-zeroes it, so no
+  // finalize kernel runs
+  unsigned int* tile_ctr;
 };
 
 // Bounded wait for the dispatch's arrival counter (release-incremented by
@@ -184,19 +194,25 @@ struct SegIter {
 };
 
 __device__ __forceinline__ void seg_begin(const Params& p, int total, SegIter& it) {
+  it.t = blockIdx.x;
   if (p.streamk) {
-    const long long all = static_cast<long long>(total) * p.nkb;
+    const long long all = static_cast<long long>(total - p.dp_tiles) * p.nkb;
     it.k = all * blockIdx.x / gridDim.x;
     it.hi = all * (blockIdx.x + 1) / gridDim.x;
-  } else {
-    it.t = blockIdx.x;
   }
 }
 
 __device__ __forceinline__ bool seg_next(const Params& p, int total, SegIter& it, int& t, int& kb0, int& kb1) {
   if (p.streamk) {
+    if (it.t < p.dp_tiles) {  // whole tiles first (full waves), written directly
+      t = it.t;
+      it.t += gridDim.x;
+      kb0 = 0;
+      kb1 = p.nkb;
+      return true;
+    }
     if (it.k >= it.hi) return false;
-    t = static_cast<int>(it.k / p.nkb);
+    t = p.dp_tiles + static_cast<int>(it.k / p.nkb);
     kb0 = static_cast<int>(it.k % p.nkb);
     kb1 = static_cast<int>(min(static_cast<long long>(p.nkb), kb0 + (it.hi - it.k)));
     it.k += kb1 - kb0;
@@ -221,16 +237,19 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
 // `r` holds this thread's row of the chunk (row = TMEM lane).
 template <int NC>
 __device__ __forceinline__ void store_chunk(const Params& p, int pt, int qt, int row, int c0,
-                                            const uint32_t (&r)[NC]) {
+                                            const uint32_t (&r)[NC], bool dp) {
+  // dp: a whole tile of a stream-K run, stored directly
+  const int epi = dp ? p.epi_dp : p.epi;
+  void* const out = dp ? p.out_dp : p.out;
   if (!p.swap) {
     const int m = pt * BM + row;
     const int n0 = qt * p.bn + c0;
-    if (p.epi == EPI_BF16) {
+    if (epi == EPI_BF16) {
       if (m >= p.M) return;
       const int nout = p.push ? p.world : 1;
       for (int d = 0; d < nout; ++d) {
         if (p.push && p.push_owner && d != pt % p.world) continue;
-        void* base = p.push ? p.peer_out[d] : p.out;
+        void* base = p.push ? p.peer_out[d] : out;
         __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(base) + static_cast<size_t>(m) * p.ldc + n0;
         if (n0 + NC <= p.N && (p.ldc & 7) == 0) {
 #pragma unroll
@@ -248,9 +267,9 @@ __device__ __forceinline__ void store_chunk(const Params& p, int pt, int qt, int
             if (n0 + j < p.N) C[j] = __float2bfloat16(__uint_as_float(r[j]));
         }
       }
-    } else if (p.epi == EPI_SWIGLU) {
+    } else if (epi == EPI_SWIGLU) {
       if (m >= p.M) return;
-      __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldc + n0 / 2;
+      __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(out) + static_cast<size_t>(m) * p.ldc + n0 / 2;
       if (n0 + NC <= p.N && (p.ldc & 7) == 0) {
 #pragma unroll
         for (int j = 0; j < NC; j += 16) {
@@ -273,7 +292,7 @@ __device__ __forceinline__ void store_chunk(const Params& p, int pt, int qt, int
       }
     } else {
       if (m >= p.M) return;
-      float* W = reinterpret_cast<float*>(p.out) + static_cast<size_t>(m) * p.N + n0;
+      float* W = reinterpret_cast<float*>(out) + static_cast<size_t>(m) * p.N + n0;
       if (n0 + NC <= p.N && (p.N & 3) == 0) {
 #pragma unroll
         for (int j = 0; j < NC; j += 4)
@@ -289,20 +308,20 @@ __device__ __forceinline__ void store_chunk(const Params& p, int pt, int qt, int
     // swap-AB: row = output feature, columns = tokens
     const int n = pt * BM + row;
     const int m0 = qt * p.bn + c0;
-    if (p.epi == EPI_BF16) {
+    if (epi == EPI_BF16) {
       if (n >= p.N) return;
       const int nout = p.push ? p.world : 1;
       for (int d = 0; d < nout; ++d) {
-        __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.push ? p.peer_out[d] : p.out) + n;
+        __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.push ? p.peer_out[d] : out) + n;
 #pragma unroll
         for (int j = 0; j < NC; ++j)
           if (m0 + j < p.M && !(p.push && p.push_owner && d != ((m0 + j) >> 7) % p.world))
             C[static_cast<size_t>(m0 + j) * p.ldc] = __float2bfloat16(__uint_as_float(r[j]));
       }
-    } else if (p.epi == EPI_SWIGLU) {
+    } else if (epi == EPI_SWIGLU) {
       // lanes 2j / 2j+1 hold gate_j / up_j for the same tokens
       const bool even = (threadIdx.x & 1) == 0;
-      __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.out) + n / 2;
+      __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(out) + n / 2;
 #pragma unroll
       for (int j = 0; j < NC; ++j) {
         float mine = __uint_as_float(r[j]);
@@ -312,12 +331,48 @@ __device__ __forceinline__ void store_chunk(const Params& p, int pt, int qt, int
       }
     } else {
       if (n >= p.N) return;
-      float* W = reinterpret_cast<float*>(p.out) + n;
+      float* W = reinterpret_cast<float*>(out) + n;
 #pragma unroll
       for (int j = 0; j < NC; ++j)
         if (m0 + j < p.M) atomicAdd(W + static_cast<size_t>(m0 + j) * p.N, __uint_as_float(r[j]));
     }
   }
+}
+
+// The tile's reduced fp32 sums, read back from the workspace by the CTA
+// that completed it (and zeroed there), stored like a whole tile.
+template <int NC>
+__device__ __forceinline__ void finish_chunk(const Params& p, int pt, int qt, int row, int c0) {
+  float* ws = reinterpret_cast<float*>(p.out);
+  uint32_t r[NC];
+  if (p.swap) {
+    const int n = pt * BM + row;
+    const int m0 = qt * p.bn + c0;
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+      float v = 0.f;
+      if (n < p.N && m0 + j < p.M) {
+        float* a = ws + static_cast<size_t>(m0 + j) * p.N + n;
+        v = __ldcg(a);
+        __stcg(a, 0.f);
+      }
+      r[j] = __float_as_uint(v);
+    }
+  } else {
+    const int m = pt * BM + row;
+    const int n0 = qt * p.bn + c0;
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+      float v = 0.f;
+      if (m < p.M && n0 + j < p.N) {
+        float* a = ws + static_cast<size_t>(m) * p.N + n0 + j;
+        v = __ldcg(a);
+        __stcg(a, 0.f);
+      }
+      r[j] = __float_as_uint(v);
+    }
+  }
+  store_chunk<NC>(p, pt, qt, row, c0, r, true);
 }
 
 // Grouped-mode epilogue (swap-AB): TMEM lane = feature of the expert,
@@ -388,8 +443,10 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* sf_full = drain + 1;  // fp8: scale factors of a stage are in TMEM
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_full + kStages);
+  uint64_t* ebar = sf_full + kStages;    // the 4 epilogue warps (in-kernel split reduction)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* s_last = abort_flag + 1;  // epilogue: this CTA completed the tile
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -405,6 +462,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       mbar_init(&tempty[a], 128);
     }
     mbar_init(drain, 1);
+    mbar_init(ebar, 128);
     if (FP8)
       for (int s = 0; s < kStages; ++s) mbar_init(&sf_full[s], 4);
     *abort_flag = 0;
@@ -527,7 +585,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     }
   } else if (FP8 && warp >= 6) {
     // scale-factor stagers: one warp per TMEM lane quadrant writes the same
-    // values into its own quadrant. The scale bytes of stage i+8 are loaded
+    // values into its own quadrant. The scale bytes of stage i+4 are loaded
     // while stage i is stored, so a global-load latency is not paid once
     // per stage.
     const int q = warp & 3;
@@ -535,9 +593,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     // fetch cursor over the (tile, k-block) sequence this CTA walks
     int ft = blockIdx.x, fkb = 0, fkb1 = 0, fwrow = 0, ftok0 = 0;
     bool fresh = true;
-    // r packs the 8 token-scale bytes of a lane (tokens c * 32 + lane,
-    // c = 0..7) four to a register
-    auto fetch = [&](uint32_t& wb, uint32_t (&r)[2]) -> bool {
+    auto fetch = [&](uint32_t& wb, uint32_t (&r)[8]) -> bool {
       while (true) {
         if (ft >= total) return false;
         if (fresh) {
@@ -559,25 +615,22 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
         fresh = true;
       }
       wb = __ldg(p.sf_w + static_cast<size_t>(fwrow) * p.sf_w_ld + fkb);
-      r[0] = r[1] = 0;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const int tok = ftok0 + c * 32 + lane;
-        const uint32_t b =
-            (c * 32 < p.bn && tok < p.M) ? __ldg(p.sf_a + static_cast<size_t>(fkb) * p.sf_a_ld + tok) : 127u;
-        r[c >> 2] |= b << (8 * (c & 3));
+        r[c] = (c * 32 < p.bn && tok < p.M) ? __ldg(p.sf_a + static_cast<size_t>(fkb) * p.sf_a_ld + tok) : 127u;
       }
       ++fkb;
       return true;
     };
     uint32_t stage = 0, phase = 0;
     long long sf_steps = 0;
-    auto store = [&](uint32_t wb, const uint32_t (&r)[2]) -> bool {
+    auto store = [&](uint32_t wb, const uint32_t (&r)[8]) -> bool {
       if (!mbar_wait_warp(&empty[stage], phase ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) return false;
       tc_fence_after();  // the MMAs that read this slot before have completed
       uint32_t rr[8];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) rr[c] = ((r[c >> 2] >> (8 * (c & 3))) & 0xFFu) * 0x01010101u;
+      for (int c = 0; c < 8; ++c) rr[c] = r[c] * 0x01010101u;
       const uint32_t w4 = wb * 0x01010101u;
       const uint32_t slot = tmem_base + lane_base + SF_COL0 + stage * SF_SLOT;
       tmem_st4(slot, w4, w4, w4, w4);
@@ -594,11 +647,10 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       }
       return true;
     };
-    // eight register sets in flight: the loads of stage i+8 are issued when
-    // stage i is stored (compile-time indices keep them in registers), so a
-    // DRAM round trip under full load is covered by 8 weight stages
-    constexpr int kAhead = 8;
-    uint32_t wv[kAhead], rv[kAhead][2];
+    // four register sets in flight: the loads of stage i+4 are issued when
+    // stage i is stored (compile-time indices keep them in registers)
+    constexpr int kAhead = 4;
+    uint32_t wv[kAhead], rv[kAhead][8];
     bool has[kAhead];
     bool arrived = true;
     if (p.wait_flag != nullptr && !p.wait_per_expert) {   // the activation scales arrive with the dispatched rows
@@ -626,6 +678,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = q * 32 + lane;
     int local = 0;
+    uint32_t eph = 0;        // phase of the epilogue warps' mbarrier
     SegIter it;
     seg_begin(p, total, it);
     int t, kb0, kb1;
@@ -637,23 +690,49 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutTmemFull)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kAccCols;
+      const bool dp = p.streamk && t < p.dp_tiles;
       int c0 = 0;
       for (; c0 + 32 <= p.bn; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(t_row + c0, r);
         tmem_ld_wait();
         if (p.grouped) store_chunk_grouped<32>(p, t, row, c0, r);
-        else store_chunk<32>(p, pt, qt, row, c0, r);
+        else store_chunk<32>(p, pt, qt, row, c0, r, dp);
       }
       if (c0 < p.bn) {
         uint32_t r[16];
         tmem_ld16(t_row + c0, r);
         tmem_ld_wait();
         if (p.grouped) store_chunk_grouped<16>(p, t, row, c0, r);
-        else store_chunk<16>(p, pt, qt, row, c0, r);
+        else store_chunk<16>(p, pt, qt, row, c0, r, dp);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
+      if (p.tile_ctr != nullptr && !p.grouped && !dp && p.epi == EPI_ATOMIC_F32) {
+        // this share's partial sums are in the workspace: count its
+        // k-blocks; the share that completes the tile stores it. The
+        // epilogue warps meet on a bounded mbarrier (never an unbounded
+        // bar.sync: a warp that gave up on a wait must not strand the rest).
+        __threadfence();
+        mbar_arrive(ebar);
+        if (!mbar_wait_warp(ebar, eph & 1u, abort_flag, p.status, kStatusTimeoutTmemFull)) break;
+        ++eph;
+        if (threadIdx.x == 64) {
+          const unsigned add = static_cast<unsigned>(kb1 - kb0);
+          const unsigned old = atomicAdd(&p.tile_ctr[t / p.splits], add);
+          *s_last = (old + add == static_cast<unsigned>(p.nkb)) ? 1 : 0;
+        }
+        mbar_arrive(ebar);
+        if (!mbar_wait_warp(ebar, eph & 1u, abort_flag, p.status, kStatusTimeoutTmemFull)) break;
+        ++eph;
+        if (*s_last) {
+          __threadfence();
+          int c1 = 0;
+          for (; c1 + 32 <= p.bn; c1 += 32) finish_chunk<32>(p, pt, qt, row, c1);
+          if (c1 < p.bn) finish_chunk<16>(p, pt, qt, row, c1);
+          if (threadIdx.x == 64) p.tile_ctr[t / p.splits] = 0;
+        }
+      }
     }
   }
 
@@ -725,13 +804,13 @@ __global__ void splitk_finalize_push_kernel(float* __restrict__ ws, int M, int N
 }
 
 __global__ void splitk_finalize_kernel(float* __restrict__ ws, __nv_bfloat16* __restrict__ out, int M, int N,
-                                       int ldc, int swiglu) {
+                                       int ldc, int swiglu, int n_begin) {
   const int m = blockIdx.y;
   if (m >= M) return;
   float* row = ws + static_cast<size_t>(m) * N;
   __nv_bfloat16* orow = out + static_cast<size_t>(m) * ldc;
   if (!swiglu) {
-    for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < N; n += gridDim.x * blockDim.x * 4) {
+    for (int n = n_begin + (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < N; n += gridDim.x * blockDim.x * 4) {
       if (n + 4 <= N) {
         float4 v = *reinterpret_cast<float4*>(row + n);
         *reinterpret_cast<float4*>(row + n) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -747,7 +826,7 @@ __global__ void splitk_finalize_kernel(float* __restrict__ ws, __nv_bfloat16* __
       }
     }
   } else {
-    for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < N; n += gridDim.x * blockDim.x * 4) {
+    for (int n = n_begin + (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < N; n += gridDim.x * blockDim.x * 4) {
       float4 v = *reinterpret_cast<float4*>(row + n);
       *reinterpret_cast<float4*>(row + n) = make_float4(0.f, 0.f, 0.f, 0.f);
       uint32_t o = pack_bf16(silu(v.x) * v.y, silu(v.z) * v.w);
@@ -888,6 +967,16 @@ inline Plan make_plan(int M, int N, int K, int num_sms, int force_split, int swa
     if (static_cast<double>(tiles) / (waves * num_sms) < 0.85) {
       p.streamk = 1;
       pl.grid = num_sms;
+      // whole tiles for the full waves, stream-K only over the partial wave
+      // (plus one full wave when the partial one is under half the SMs, so
+      // no share is a sliver): most tiles skip the workspace. The whole
+      // tiles end on a weight-row block (swap-AB) / token-column tile
+      // boundary, so the workspace columns are one contiguous range.
+      const int rem = tiles % num_sms;
+      int sk = rem >= num_sms / 2 ? rem : rem + num_sms;
+      if (sk > tiles) sk = tiles;
+      const int unit = p.swap ? p.q_tiles : p.p_tiles;
+      p.dp_tiles = ((tiles - sk) / unit) * unit;
     }
   }
   return pl;
@@ -941,6 +1030,19 @@ inline int launch(const Operands& o, const CUtensorMap& tmP, const CUtensorMap& 
   return o.fp8 ? launch_gemm<true>(tmP, tmQ, p, grid, stream) : launch_gemm<false>(tmP, tmQ, p, grid, stream);
 }
 
+// Per-device tile counters for the in-kernel split reduction (registered by
+// the host scratch owner; absent: the finalize kernel reduces).
+struct TileCounters {
+  unsigned int* ptr = nullptr;
+  int n = 0;
+};
+inline TileCounters& tile_counters() {
+  static TileCounters t[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return t[dev >= 0 && dev < 64 ? dev : 0];
+}
+
 inline int run_dense(const Operands& o, const void* A, const void* W, void* out, int M, int N, int K, int lda,
                      int ldw, int ldc, int epi, float* ws, int force_split, int* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
@@ -961,14 +1063,22 @@ inline int run_dense(const Operands& o, const void* A, const void* W, void* out,
   const bool split = p.splits > 1 || p.streamk;
   p.epi = split ? EPI_ATOMIC_F32 : epi;
   p.out = split ? static_cast<void*>(ws) : out;
+  p.epi_dp = epi;
+  p.out_dp = out;
+  if (!p.streamk) p.dp_tiles = 0;
+  const TileCounters& tc = tile_counters();
+  p.tile_ctr = split && tc.ptr != nullptr && p.p_tiles * p.q_tiles <= tc.n ? tc.ptr : nullptr;
   CUtensorMap tmP, tmQ;
   if (!encode_pq(o, p, A, W, N, lda, ldw, &tmP, &tmQ)) return -2;
   int rc = launch(o, tmP, tmQ, p, pl.grid, stream);
   if (rc != 0) return rc;
-  if (split) {
-    dim3 g((N + 1023) / 1024, M);
+  if (split && p.tile_ctr == nullptr) {
+    // stream-K: only the columns of the tiles past dp_tiles went through
+    // the workspace (swap-AB: weight-row blocks, else token-column tiles)
+    const int n_begin = p.streamk ? (p.swap ? (p.dp_tiles / p.q_tiles) * BM : (p.dp_tiles / p.p_tiles) * p.bn) : 0;
+    dim3 g((N - n_begin + 1023) / 1024, M);
     splitk_finalize_kernel<<<g, 256, 0, stream>>>(ws, static_cast<__nv_bfloat16*>(out), M, N, ldc,
-                                                  epi == EPI_SWIGLU ? 1 : 0);
+                                                  epi == EPI_SWIGLU ? 1 : 0, n_begin);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return static_cast<int>(e);
   }
@@ -1249,4 +1359,15 @@ extern "C" void ib_gemm_fp8_plan(int M, int N, int K, int num_sms, int force_spl
 
 // Diagnostics: the next GEMM launches stamp CTA 0's pipeline events into
 // trace[5 * 128] (clock64), or stop when trace is null.
+// Register n zero-initialised uint32 tile counters on the current device
+// (null: none): split-K and stream-K GEMMs then reduce inside the kernel.
+extern "C" void ib_gemm_set_tile_counters(void* ptr, int n) {
+  auto& t = ib200::gemm::tile_counters();
+  t.ptr = static_cast<unsigned int*>(ptr);
+  t.n = ptr != nullptr ? n : 0;
+}
+
+// Whether dense GEMMs on the current device reduce split partials in-kernel.
+extern "C" int ib_gemm_fused_reduce() { return ib200::gemm::tile_counters().ptr != nullptr ? 1 : 0; }
+
 extern "C" void ib_gemm_set_trace(long long* trace) { ib200::gemm::g_gemm_trace = trace; }

@@ -119,6 +119,8 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
                                     c_int, c_int, c_vp, c_vp, c_int, c_int, c_vp, c_uint, c_int, ctypes.c_ulonglong,
                                     c_vp, c_vp],
         "ib_gemm_set_trace": [c_vp],
+        "ib_gemm_set_tile_counters": [c_vp, c_int],
+        "ib_gemm_fused_reduce": [],
         "ib_attn_prefill_set_trace": [c_vp],
         "ib_mla_rope_kvwrite": [c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_float, c_vp, c_vp],
     }
@@ -128,7 +130,8 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
             continue
         fn.argtypes = args
         fn.restype = None if name in ("ib_gemm_bf16_plan", "ib_gemm_fp8_plan", "ib_mla_set_trace",
-                                        "ib_gemm_set_trace", "ib_attn_prefill_set_trace") else c_int
+                                        "ib_gemm_set_trace", "ib_attn_prefill_set_trace",
+                                        "ib_gemm_set_tile_counters") else c_int
 
 
 def kernels() -> ctypes.CDLL:

@@ -162,7 +162,7 @@ def gemm_fp8(q: torch.Tensor, sf: torch.Tensor, w: FP8Weight, out: torch.Tensor 
                                        out.data_ptr(), M, N, Kd, q.stride(0), w.q.stride(0), out.stride(0),
                                        1 if swiglu else 0, ws.data_ptr(), 0, sc.status.data_ptr(), K._stream())
     _native.check(rc, "ib_gemm_fp8")
-    K._count(2 if splits > 1 else 1)
+    K._count(2 if splits > 1 and not K._FUSED_REDUCE else 1)
     return out
 
 

@@ -13,6 +13,7 @@ engine sizes it once at start-up so that CUDA-graph capture never allocates.
 from __future__ import annotations
 
 import math
+import os as _os
 from dataclasses import dataclass, field
 
 import torch
@@ -31,6 +32,9 @@ class DeviceScratch:
     dec_lse: torch.Tensor = field(default_factory=lambda: torch.empty(0))
     pf_o: torch.Tensor = field(default_factory=lambda: torch.empty(0))
     pf_lse: torch.Tensor = field(default_factory=lambda: torch.empty(0))
+    # per-tile k-block counters of the in-kernel split reduction (uint32,
+    # zero between GEMMs; the GEMM that completes a tile resets its counter)
+    gemm_ctr: torch.Tensor = field(default_factory=lambda: torch.empty(0))
 
     # Growth is refused while a CUDA graph is being captured (a captured
     # kernel must keep pointing at live memory); engines size the scratch
@@ -100,6 +104,9 @@ def scratch(device: torch.device | int | None = None) -> DeviceScratch:
         dev = torch.device("cuda", idx)
         # the status word, then three ints of details of the first error
         s = DeviceScratch(device=dev, status=torch.zeros(4, dtype=torch.int32, device=dev))
+        if _FUSED_REDUCE:
+            s.gemm_ctr = torch.zeros(_GEMM_CTRS, dtype=torch.int32, device=dev)
+            _native.kernels().ib_gemm_set_tile_counters(s.gemm_ctr.data_ptr(), _GEMM_CTRS)
         _scratch[idx] = s
     return s
 
@@ -136,8 +143,15 @@ def _gemm_ws(M: int, N: int, K: int, force_split: int = 0) -> bool:
     return v > 1 or v < 0
 
 
+# Split-K / stream-K partial sums are reduced inside the GEMM (the CTA that
+# completes a tile stores it) instead of by a finalize kernel
+# (INFERA_GEMM_FUSED_REDUCE=0: finalize kernel).
+_FUSED_REDUCE = _os.environ.get("INFERA_GEMM_FUSED_REDUCE", "1") != "0"
+_GEMM_CTRS = 1 << 16
+
+
 def _gemm_launches(M: int, N: int, K: int, force_split: int = 0) -> int:
-    return 1 + (1 if _gemm_ws(M, N, K, force_split) else 0)
+    return 1 + (1 if _gemm_ws(M, N, K, force_split) and not _FUSED_REDUCE else 0)
 
 
 _NUM_SMS: list[int] = []
@@ -420,7 +434,6 @@ def _ref_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor
 # Decode attention splits every sequence into chunks of this many 128-key
 # tiles at the same absolute positions (INFERA_DECODE_TPS=0: divide each
 # sequence evenly over decode_splits() splits instead).
-import os as _os
 
 DECODE_TILES_PER_SPLIT = int(_os.environ.get("INFERA_DECODE_TPS", "16"))
 

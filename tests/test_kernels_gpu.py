@@ -55,12 +55,16 @@ def test_gemm_swiglu(M, force_split):
     assert float(K.scratch().gemm_ws.abs().sum()) == 0.0
 
 
-@pytest.mark.parametrize("M,swiglu", [(1, True), (64, True), (64, False), (128, False)])
-def test_gemm_stream_k(M, swiglu):
-    """224 weight tiles on 148 SMs: every CTA takes an equal share of the
-    k-steps, partial tiles meet in the fp32 workspace (left zeroed)."""
+@pytest.mark.parametrize("M,N,K_,swiglu", [(1, 28672, 4096, True), (64, 28672, 4096, True),
+                                            (64, 28672, 4096, False), (128, 28672, 4096, False),
+                                            (288, 28672, 4096, True), (3840, 2560, 1024, False)])
+def test_gemm_stream_k(M, N, K_, swiglu):
+    """More tiles than SMs but a poor last wave: whole tiles for the full
+    waves, the rest shared out k-step by k-step; partial tiles meet in the
+    fp32 workspace, which is left zeroed, as are the per-tile counters of the
+    in-kernel reduction (288 x 28672: swap-AB with 296 whole tiles; 3840 x
+    2560: token-row tiles with 120 whole tiles)."""
     torch.manual_seed(4)
-    N, K_ = 28672, 4096
     assert K.gemm_plan(M, N, K_)["splits"] == -1
     x = (torch.randn(M, K_, device=DEV) * 0.5).to(torch.bfloat16)
     w = (torch.randn(N, K_, device=DEV) / math.sqrt(K_)).to(torch.bfloat16)
@@ -70,6 +74,9 @@ def test_gemm_stream_k(M, swiglu):
     ref = K.linear(x.cpu(), w.cpu(), swiglu=swiglu)
     assert _rel_err(y.cpu(), ref) < 1e-2
     assert float(K.scratch().gemm_ws.abs().sum()) == 0.0
+    sc = K.scratch()
+    if sc.gemm_ctr.numel():
+        assert int(sc.gemm_ctr.abs().sum()) == 0
 
 
 def test_gemm_repeated_split_consistent():
