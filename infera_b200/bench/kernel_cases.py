@@ -89,14 +89,15 @@ def run_case(case: str, iters: int) -> dict:
         return {"case": case, "ms": ms, "tflops": fl / ms / 1e9, "gbs": by / ms / 1e6,
                 "splits": M.mla_splits(B, L, K._num_sms())}
     hq, hkv, D = 32, 8, 128
-    if case in ("decode_attn", "decode_attn_contig"):
+    if case in ("decode_attn", "decode_attn_contig", "decode_attn_48x2048", "decode_attn_48x2048_contig"):
         # decode_attn: every page placed at random; _contig: each sequence's
-        # pages consecutive (eight-page runs load as one box per half)
-        B, L = 32, 8192
+        # pages consecutive (eight-page runs load as one box per half);
+        # 48x2048: the serving bench's decode batch shape
+        B, L = (48, 2048) if "48x2048" in case else (32, 8192)
         pages = B * L // 16
         kc = torch.randn(pages * 16, hkv * D, device=dev, generator=g).to(bf)
         vc = torch.randn(pages * 16, hkv * D, device=dev, generator=g).to(bf)
-        if case == "decode_attn":
+        if not case.endswith("contig"):
             bt = torch.randperm(pages, device=dev, dtype=torch.int32).view(B, -1)
         else:
             bt = torch.arange(pages, device=dev, dtype=torch.int32).view(B, -1)

@@ -80,6 +80,8 @@ struct Params {
   float* lse_part;         // [nq, splits, hq] (log2 units)
   int* status;
   long long* trace;        // optional: clock64 stamps of CTA (0,0,0)'s pipeline events (see TR_*)
+  const __nv_bfloat16* cache;  // [num_slots, 576] (L2 prefetch of coming pages)
+  int prefetch;            // tiles ahead whose pages are prefetched into L2 (0: none)
 };
 
 // pipeline event stamps (trace[event * kTraceTiles + tile]) for diagnosis
@@ -516,8 +518,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           pg[i] = __ldg(bt + (lp < n_pages ? lp : t * 8));
         }
       };
+      // pages of the tile kPrefetch ahead go to L2 while this one streams:
+      // each chunk load then waits an L2 hit, not a DRAM round trip (a page
+      // is 16 rows x 576 dims, 18 KiB contiguous)
+      const int kPrefetch = p.prefetch;
+      auto prefetch_tile = [&](int t) {
+        if (kPrefetch <= 0 || t >= tile0 + n_tiles) return;
+        for (int i = 0; i < 8; ++i) {
+          const int lp = t * 8 + i;
+          if (lp >= n_pages) break;
+          l2_prefetch_bulk(p.cache + static_cast<size_t>(__ldg(bt + lp)) * PAGE * DQK, PAGE * DQK * 2);
+        }
+      };
+      for (int t = 0; t < kPrefetch; ++t) prefetch_tile(tile0 + t);
       for (int j = 0; j <= n_tiles && ok; ++j) {
         if (j < n_tiles) {
+          prefetch_tile(tile0 + j + kPrefetch);
           pages_of(tile0 + j);
           for (int c = 0; c < NCH && ok; ++c) ok = load_chunk(c * 64);
           stamp(p, cta0, TR_TMA, j);
@@ -875,6 +891,12 @@ extern "C" int ib_mla_decode(const void* q, int nq, int hq, const void* cache, l
   p.lse_part = lse_part;
   p.status = status;
   p.trace = g_mla_trace;
+  p.cache = static_cast<const __nv_bfloat16*>(cache);
+  static const int prefetch = [] {
+    const char* e = std::getenv("INFERA_MLA_PREFETCH");
+    return e != nullptr && *e ? std::atoi(e) : 2;
+  }();
+  p.prefetch = prefetch;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);

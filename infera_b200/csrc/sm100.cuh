@@ -141,6 +141,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, ui
       : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) from global memory into L2 (no
+// shared memory, no completion): src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void l2_prefetch_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
 // L2 cache-policy constants (createpolicy.fractional, fraction 1.0).
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
