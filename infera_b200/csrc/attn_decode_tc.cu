@@ -83,6 +83,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                      const __grid_constant__ CUtensorMap tmK8, const __grid_constant__ CUtensorMap tmV8,
                      const Params p) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int G = p.G;
   const int len = p.seq_lens[b];
@@ -433,6 +435,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // o = sum_s 2^(lse_s - M) o_s / sum_s 2^(lse_s - M)
 __global__ void combine_kernel(const Params p) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const size_t base = (static_cast<size_t>(b) * p.hq + h) * p.splits;
   float mx = -INFINITY;
@@ -504,11 +508,11 @@ extern "C" int ib_attn_decode_tc_ex(const void* q, int ldq, const void* k_cache,
     attr_set[dev] = true;
   }
   dim3 grid(B, hkv, splits);
-  decode_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tk, tv, tk8, tv8, p);
+  launch_pdl(decode_tc_kernel, grid, NUM_THREADS, SMEM_BYTES, stream, tk, tv, tk8, tv8, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return static_cast<int>(e);
   if (splits > 1) {
-    combine_kernel<<<dim3(B, hq), D, 0, stream>>>(p);
+    launch_pdl(combine_kernel, dim3(B, hq), D, 0, stream, p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return static_cast<int>(e);
   }

@@ -104,6 +104,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                       const __grid_constant__ CUtensorMap tmKe, const __grid_constant__ CUtensorMap tmK8,
                       const __grid_constant__ CUtensorMap tmV8, const __grid_constant__ CUtensorMap tmKe8,
                       const Params p) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int QKB = qk_blocks(EXT);
   constexpr int STB = QKB + 2;     // blocks per KV stage
   extern __shared__ uint8_t smem_raw[];
@@ -576,6 +578,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     fa_prefill2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmK8,
                        const __grid_constant__ CUtensorMap tmV8, const Params p) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int STB = 4;  // blocks per KV stage: K lo, K hi, V lo, V hi
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -992,6 +996,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // Merge the key shares of split rows: out = sum_s 2^(lse_s - max) O_s / sum_s 2^(lse_s - max).
 __global__ void fa_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ lse_part, int S,
                                   int H, __nv_bfloat16* __restrict__ out, int ldo) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const size_t base = (static_cast<size_t>(row) * H + h) * S;
   float mx = -INFINITY;
@@ -1122,9 +1128,9 @@ int fa_launch(const FaOperand& q, const FaOperand& k, const FaOperand& v, const 
   }
   dim3 grid(num_heads, num_tiles, p.kv_splits);
   if (tile_rows == 256)
-    fa2_variant()<<<grid, NUM_THREADS, SMEM2, stream>>>(tq, tk, tv, tk8, tv8, p);
+    launch_pdl(fa2_variant(), grid, NUM_THREADS, SMEM2, stream, tq, tk, tv, tk8, tv8, p);
   else
-    fa_prefill_kernel<EXT><<<grid, NUM_THREADS, smem_bytes(EXT), stream>>>(tq, tk, tv, tqe, tke, tk8, tv8, tke8, p);
+    launch_pdl(fa_prefill_kernel<EXT>, grid, NUM_THREADS, smem_bytes(EXT), stream, tq, tk, tv, tqe, tke, tk8, tv8, tke8, p);
   if (p.kv_splits > 1)
     fa_combine_kernel<<<dim3(static_cast<unsigned>(q.rows), num_heads), D, 0, stream>>>(
         o_part, lse_part, p.kv_splits, num_heads, static_cast<__nv_bfloat16*>(out), ldo);

@@ -40,6 +40,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
                                                       __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                                       __nv_bfloat16* __restrict__ out, int H, int ldx, int ldd,
                                                       int ldo, float eps) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int t = blockIdx.x;
   __nv_bfloat16* xr = x + static_cast<size_t>(t) * ldx;
@@ -103,6 +105,8 @@ __global__ void rope_kvwrite_kernel(__nv_bfloat16* __restrict__ qkv, int ldqkv, 
                                     const int* __restrict__ slots, const float2* __restrict__ cos_sin, int hq,
                                     int hkv, int D, __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
                                     int ldkv, long long num_slots, int max_pos, int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const int p = pos[t];
   long long slot = slots[t];
@@ -147,6 +151,8 @@ __global__ void rope_kvwrite_kernel(__nv_bfloat16* __restrict__ qkv, int ldqkv, 
 // An id outside [0, vocab) is recorded in the status word and its row zeroed.
 __global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                              __nv_bfloat16* __restrict__ out, int H, int vocab, int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const int id = ids[t];
   uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H);
@@ -172,6 +178,8 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 __global__ void __launch_bounds__(1024) sample_kernel(const __nv_bfloat16* __restrict__ logits, int ld, int V,
                                                       const float* __restrict__ temperature,
                                                       const long long* __restrict__ seeds, int* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int b = blockIdx.x;
@@ -228,6 +236,8 @@ __global__ void __launch_bounds__(1024) sample_kernel(const __nv_bfloat16* __res
 // Gather the rows `idx[i]` of src [*, ld] into dst [n, ld] (bf16, ld % 8 == 0).
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, const int* __restrict__ idx,
                                    __nv_bfloat16* __restrict__ dst, int ld) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x;
   const uint4* s = reinterpret_cast<const uint4*>(src + static_cast<size_t>(idx[i]) * ld);
   uint4* d = reinterpret_cast<uint4*>(dst + static_cast<size_t>(i) * ld);
@@ -237,6 +247,8 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, const 
 // dst[idx[i]] = val[i] for i < n (incremental block-table updates).
 __global__ void scatter_i32_kernel(int* __restrict__ dst, const int* __restrict__ idx, const int* __restrict__ val,
                                    int n) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) dst[idx[i]] = val[i];
 }
@@ -255,7 +267,7 @@ extern "C" int ib_rmsnorm(const void* x, const void* w, void* out, int T, int H,
                           cudaStream_t stream) {
   if (T <= 0) return 0;
   if (H % 8 != 0 || H / 8 > 4 * 256) return -1;
-  ew::rmsnorm_kernel<false><<<T, 256, 0, stream>>>(nullptr, static_cast<__nv_bfloat16*>(const_cast<void*>(x)),
+  launch_pdl(ew::rmsnorm_kernel<false>, T, 256, 0, stream, nullptr, static_cast<__nv_bfloat16*>(const_cast<void*>(x)),
                                                     static_cast<const __nv_bfloat16*>(w),
                                                     static_cast<__nv_bfloat16*>(out), H, ldx, 0, ldo, eps);
   return ret_launch();
@@ -266,7 +278,7 @@ extern "C" int ib_add_rmsnorm(const void* delta, void* residual, const void* w, 
                               int ldr, int ldo, float eps, cudaStream_t stream) {
   if (T <= 0) return 0;
   if (H % 8 != 0 || H / 8 > 4 * 256) return -1;
-  ew::rmsnorm_kernel<true><<<T, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(delta),
+  launch_pdl(ew::rmsnorm_kernel<true>, T, 256, 0, stream, static_cast<const __nv_bfloat16*>(delta),
                                                    static_cast<__nv_bfloat16*>(residual),
                                                    static_cast<const __nv_bfloat16*>(w),
                                                    static_cast<__nv_bfloat16*>(out), H, ldr, ldd, ldo, eps);
@@ -279,7 +291,7 @@ extern "C" int ib_rope_kvwrite(void* qkv, int T, int ldqkv, const int* pos, cons
                                int max_pos, int* status, cudaStream_t stream) {
   if (T <= 0) return 0;
   if (D % 4 != 0) return -1;
-  ew::rope_kvwrite_kernel<<<T, 256, 0, stream>>>(static_cast<__nv_bfloat16*>(qkv), ldqkv, pos, slots,
+  launch_pdl(ew::rope_kvwrite_kernel, T, 256, 0, stream, static_cast<__nv_bfloat16*>(qkv), ldqkv, pos, slots,
                                                   static_cast<const float2*>(cos_sin), hq, hkv, D,
                                                   static_cast<__nv_bfloat16*>(k_cache),
                                                   static_cast<__nv_bfloat16*>(v_cache), ldkv, num_slots, max_pos,
@@ -291,7 +303,7 @@ extern "C" int ib_embed(const int* ids, const void* table, void* out, int T, int
                         cudaStream_t stream) {
   if (T <= 0) return 0;
   if (H % 8 != 0) return -1;
-  ew::embed_kernel<<<T, 256, 0, stream>>>(ids, static_cast<const __nv_bfloat16*>(table),
+  launch_pdl(ew::embed_kernel, T, 256, 0, stream, ids, static_cast<const __nv_bfloat16*>(table),
                                            static_cast<__nv_bfloat16*>(out), H, vocab, status);
   return ret_launch();
 }
@@ -299,7 +311,7 @@ extern "C" int ib_embed(const int* ids, const void* table, void* out, int T, int
 extern "C" int ib_sample(const void* logits, int B, int ld, int V, const float* temperature, const long long* seeds,
                          int* out, cudaStream_t stream) {
   if (B <= 0) return 0;
-  ew::sample_kernel<<<B, 1024, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), ld, V, temperature, seeds,
+  launch_pdl(ew::sample_kernel, B, 1024, 0, stream, static_cast<const __nv_bfloat16*>(logits), ld, V, temperature, seeds,
                                              out);
   return ret_launch();
 }
@@ -307,13 +319,13 @@ extern "C" int ib_sample(const void* logits, int B, int ld, int V, const float* 
 extern "C" int ib_gather_rows(const void* src, const int* idx, void* dst, int n, int ld, cudaStream_t stream) {
   if (n <= 0) return 0;
   if (ld % 8 != 0) return -1;
-  ew::gather_rows_kernel<<<n, 128, 0, stream>>>(static_cast<const __nv_bfloat16*>(src), idx,
+  launch_pdl(ew::gather_rows_kernel, n, 128, 0, stream, static_cast<const __nv_bfloat16*>(src), idx,
                                                  static_cast<__nv_bfloat16*>(dst), ld);
   return ret_launch();
 }
 
 extern "C" int ib_scatter_i32(int* dst, const int* idx, const int* val, int n, cudaStream_t stream) {
   if (n <= 0) return 0;
-  ew::scatter_i32_kernel<<<(n + 255) / 256, 256, 0, stream>>>(dst, idx, val, n);
+  launch_pdl(ew::scatter_i32_kernel, (n + 255) / 256, 256, 0, stream, dst, idx, val, n);
   return ret_launch();
 }

@@ -450,6 +450,14 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // PDL: let the next kernel be scheduled once every CTA got here. A
+  // grouped run reads device data of earlier kernels from the start (tile
+  // table, tile count) and waits for them at once; a dense run lets its
+  // producer put the first stages' weight tiles (static data) in flight
+  // before it waits (every other thread waits right after the setup).
+  pdl_trigger();
+  const bool early_weights = !p.grouped;
+  if (!early_weights) pdl_wait();
   const int total = p.grouped ? *p.gnum : p.p_tiles * p.q_tiles * p.splits;
 
   if (threadIdx.x == 0) {
@@ -480,6 +488,7 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (early_weights && !(warp == 0 && lane == 0)) pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -490,6 +499,27 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
       const uint32_t tx = static_cast<uint32_t>((BM + p.bn) * 128);
       uint32_t stage = 0, phase = 0;
       long long issued = 0;
+      // weight tiles of this CTA's first stages, issued before the previous
+      // kernel has finished (their stages are fresh: no empty wait); each
+      // stage's activation tile follows after pdl_wait()
+      int pre = 0;
+      if (early_weights) {
+        SegIter it0;
+        seg_begin(p, total, it0);
+        int t0, a0, a1;
+        while (pre < kStages && seg_next(p, total, it0, t0, a0, a1)) {
+          int pt0, qt0, sp0;
+          tile_coords(p, t0, pt0, qt0, sp0);
+          for (int kb = a0; kb < a1 && pre < kStages; ++kb, ++pre) {
+            mbar_expect_tx(&full[pre], tx);
+            if (p.swap)
+              tma_load_2d(sP + pre * P_STAGE, &tmP, &full[pre], kb * kBK, tile_prow(p, t0, pt0), polP);
+            else
+              tma_load_2d(sQ + pre * kQStage, &tmQ, &full[pre], kb * kBK, tile_qrow(p, t0, qt0), polQ);
+          }
+        }
+        pdl_wait();
+      }
       // one wait for the whole round, or per tile on the tile's expert
       bool ok = p.wait_per_expert ? true : wait_arrivals(p, abort_flag);
       SegIter it;
@@ -503,6 +533,19 @@ __global__ void __launch_bounds__(FP8 ? NUM_THREADS_FP8 : NUM_THREADS, 1)
           break;
         }
         for (int kb = kb0; kb < kb1; ++kb) {
+          if (issued < pre) {  // its weight tile is already in flight
+            if (p.swap)
+              tma_load_2d(sQ + stage * kQStage, &tmQ, &full[stage], kb * kBK, tile_qrow(p, t, qt), polQ);
+            else
+              tma_load_2d(sP + stage * P_STAGE, &tmP, &full[stage], kb * kBK, tile_prow(p, t, pt), polP);
+            gstamp(p, TRG_TMA, issued);
+            ++issued;
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, kStatusTimeoutEmpty)) {
             ok = false;
             break;
@@ -805,6 +848,8 @@ __global__ void splitk_finalize_push_kernel(float* __restrict__ ws, int M, int N
 
 __global__ void splitk_finalize_kernel(float* __restrict__ ws, __nv_bfloat16* __restrict__ out, int M, int N,
                                        int ldc, int swiglu, int n_begin) {
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.y;
   if (m >= M) return;
   float* row = ws + static_cast<size_t>(m) * N;
@@ -852,7 +897,7 @@ inline int launch_gemm_variant(const CUtensorMap& tmP, const CUtensorMap& tmQ, c
     cudaFuncSetAttribute(gemm_kernel<FP8, DEEP>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     attr_set[dev] = true;
   }
-  gemm_kernel<FP8, DEEP><<<grid, FP8 ? NUM_THREADS_FP8 : NUM_THREADS, SMEM_BYTES, stream>>>(tmP, tmQ, p);
+  launch_pdl(gemm_kernel<FP8, DEEP>, grid, FP8 ? NUM_THREADS_FP8 : NUM_THREADS, SMEM_BYTES, stream, tmP, tmQ, p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
@@ -1077,7 +1122,7 @@ inline int run_dense(const Operands& o, const void* A, const void* W, void* out,
     // the workspace (swap-AB: weight-row blocks, else token-column tiles)
     const int n_begin = p.streamk ? (p.swap ? (p.dp_tiles / p.q_tiles) * BM : (p.dp_tiles / p.p_tiles) * p.bn) : 0;
     dim3 g((N - n_begin + 1023) / 1024, M);
-    splitk_finalize_kernel<<<g, 256, 0, stream>>>(ws, static_cast<__nv_bfloat16*>(out), M, N, ldc,
+    launch_pdl(splitk_finalize_kernel, g, 256, 0, stream, ws, static_cast<__nv_bfloat16*>(out), M, N, ldc,
                                                   epi == EPI_SWIGLU ? 1 : 0, n_begin);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return static_cast<int>(e);

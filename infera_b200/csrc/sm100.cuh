@@ -9,6 +9,8 @@
 // traps.
 #pragma once
 
+#include <cstdlib>
+
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -30,6 +32,42 @@ enum : int {
 
 // Default bound for a single wait: 2 s of wall time.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch. A kernel started with launch_pdl() may be
+// scheduled while the previous kernel on its stream still runs; it calls
+// pdl_wait() before it reads anything earlier kernels wrote or writes
+// anything they may still read (the wait returns once those grids have
+// completed and their writes are visible). pdl_trigger() lets the next
+// kernel be scheduled as soon as every CTA of this one has reached it; the
+// next kernel's own pdl_wait() still waits for this one to complete.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// INFERA_PDL=0 launches without the attribute (plain stream order).
+inline bool pdl_on() {
+  static const bool v = [] {
+    const char* e = std::getenv("INFERA_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return v;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_on() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
