@@ -48,6 +48,8 @@ def main(argv=None) -> None:
     ap.add_argument("--top", type=int, default=15)
     ap.add_argument("--graphs", type=int, default=1)
     ap.add_argument("--device", default="cuda:0")
+    ap.add_argument("--time-steps", type=int, default=0,
+                    help="also time this many decode-only steps without the profiler (host clock per step)")
     a = ap.parse_args(argv)
 
     from torch.profiler import ProfilerActivity, profile
@@ -93,6 +95,17 @@ def main(argv=None) -> None:
                     SamplingParams(max_tokens=1, ignore_eos=True))
     eng.step()
     eng.step()
+    if a.time_steps > 0:
+        ts = []
+        for _ in range(a.time_steps):
+            sync()
+            t0 = time.perf_counter()
+            eng.step()
+            sync()
+            ts.append((time.perf_counter() - t0) * 1e3)
+        ts.sort()
+        print(json.dumps({"step": "decode_timed", "n": len(ts), "p50_ms": round(ts[len(ts) // 2], 3),
+                          "min_ms": round(ts[0], 3), "p90_ms": round(ts[int(0.9 * len(ts))], 3)}), flush=True)
     record("decode")
     record("mixed", lambda: eng.add_request("chunk", torch.randint(0, V, (a.chunk,), generator=g).tolist(),
                                             SamplingParams(max_tokens=1, ignore_eos=True)))
