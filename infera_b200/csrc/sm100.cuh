@@ -65,7 +65,13 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_on() ? 1 : 0;
+  // eager launches only: inside a captured CUDA graph the kernels already
+  // run back to back, and a graphed decode step measured 0.9 % slower with
+  // programmatic edges (7.45 vs 7.38 ms) while eager mixed steps gained
+  // 6.5 % (11.63 vs 12.44 ms)
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(stream, &cs);
+  cfg.numAttrs = pdl_on() && cs == cudaStreamCaptureStatusNone ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
