@@ -73,13 +73,18 @@ def run_case(case: str, iters: int) -> dict:
         fl = 2 * M * N * Kd
         by = M * Kd + N * Kd + N * Kd // 16384 + M * (N // 2 if swiglu else N) * 2
         return {"case": case, "ms": ms, "ms_with_act_quant": ms_q, "tflops": fl / ms / 1e9, "gbs": by / ms / 1e6}
-    if case in ("mla_decode", "mla_decode_small"):
+    if case in ("mla_decode", "mla_decode_small", "mla_decode_contig"):
+        # _contig: each sequence's pages consecutive (as the page allocator
+        # hands out prompt pages), the others placed at random
         from infera_b200.ops import mla as M
 
-        B, L, hq = (64, 4096, 128) if case == "mla_decode" else (16, 4096, 128)
+        B, L, hq = (16, 4096, 128) if case == "mla_decode_small" else (64, 4096, 128)
         pages = B * L // 16
         cache = torch.randn(pages * 16, 576, device=dev, generator=g).to(bf)
-        bt = torch.randperm(pages, device=dev, dtype=torch.int32).view(B, -1)
+        if case == "mla_decode_contig":
+            bt = torch.arange(pages, device=dev, dtype=torch.int32).view(B, -1)
+        else:
+            bt = torch.randperm(pages, device=dev, dtype=torch.int32).view(B, -1)
         q = (torch.randn(B, hq, 576, device=dev, generator=g) * 0.05).to(bf)
         rows = torch.arange(B, dtype=torch.int32, device=dev)
         kvl = torch.full((B,), L, dtype=torch.int32, device=dev)
