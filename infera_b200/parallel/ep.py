@@ -55,6 +55,26 @@ FLAGS = 1024
 EFLAG_OFF = 64
 
 
+class _SharedComm:
+    """The symmetric buffers of one process's EP layers: every MoE layer of
+    a model uses the same receive / return buffers, arrival counters and
+    scratch (a DeepSeek-V3 shard has 58 MoE layers; 7.5 GB of buffers each
+    would not fit). Sharing is safe because layers run one after another in
+    the same order on every rank: a rank starts layer i+1's dispatch only
+    after its layer-i wait saw every rank's returns, i.e. after every rank's
+    layer-i up projection has read its receive buffer, and a rank's layer
+    i+1 return stores into a peer need that peer's layer-i+1 dispatch, which
+    its stream issues after its layer-i combine read the return buffer.
+    The arrival counters are cumulative, so the round counter is shared."""
+
+    def __init__(self):
+        self.users = 0
+        self.round = 0
+
+
+_SHARED: dict[tuple, _SharedComm] = {}
+
+
 class EPMoE:
     def __init__(self, full: MoELayer, rank: int, world: int, group=None, device: str | torch.device = "cuda",
                  fused: bool = False, max_tokens: int = 256, gloo_group=None):
@@ -100,6 +120,16 @@ class EPMoE:
         # fp8 experts: the dispatched rows are e4m3 (first half of the
         # receive buffer) with their scale columns [H/128, max_rows] here
         self.sf_bytes = ((H // 128) * max_rows + 15) // 16 * 16 if self.fp8 else 0
+        key = (self.device.index, self.world, self.E, max_rows, H, self.fp8, id(gloo_group))
+        sh = _SHARED.get(key)
+        if sh is not None:
+            self._shared = sh
+            sh.users += 1
+            for name in ("base", "peers", "ctr", "local_done", "counts_all", "offs", "row_map"):
+                setattr(self, name, getattr(sh, name))
+            if self.El * 4 > FLAGS - EFLAG_OFF:
+                self.per_expert = False
+            return
         total = FLAGS + 2 * self.buf_bytes + self.sf_bytes
         p = ctypes.c_void_p()
         with torch.cuda.device(self.device):
@@ -119,7 +149,6 @@ class EPMoE:
             with torch.cuda.device(self.device):
                 _native.check(lib.ib_ipc_open(buf, ctypes.byref(q)), f"ib_ipc_open(rank {r})")
             self.peers.append(q.value)
-        self.round = 0
         self.ctr = torch.zeros(4, dtype=torch.int32, device=self.device)  # done counters of the two phases
         if self.El * 4 > FLAGS - EFLAG_OFF:
             self.per_expert = False
@@ -129,6 +158,12 @@ class EPMoE:
         self.counts_all = torch.zeros(W * E, dtype=torch.int32, device=self.device)
         self.offs = torch.zeros(E + self.El + 1 + W * E, dtype=torch.int32, device=self.device)
         self.row_map = torch.zeros(max_rows, dtype=torch.int32, device=self.device)
+        sh = _SharedComm()
+        sh.users = 1
+        for name in ("base", "peers", "ctr", "local_done", "counts_all", "offs", "row_map"):
+            setattr(sh, name, getattr(self, name))
+        _SHARED[key] = sh
+        self._shared = sh
         dist.barrier(group=gloo_group)
 
     def _local_done(self):
@@ -169,8 +204,8 @@ class EPMoE:
         src_off = self.offs[E + El + 1:]
         _native.check(lib.ib_ep_offsets(self.counts_all.data_ptr(), W, E, self.rank, dst_off.data_ptr(),
                                         loc_off.data_ptr(), src_off.data_ptr(), stream), "ib_ep_offsets")
-        self.round += 1
-        target = self.round * W
+        self._shared.round += 1
+        target = self._shared.round * W
         recv_peers = (ctypes.c_void_p * 8)(*[self._recv_view(b) for b in self.peers])
         flagA = (ctypes.c_void_p * 8)(*[b for b in self.peers])
         eflags = (ctypes.c_void_p * 8)(*[b + EFLAG_OFF for b in self.peers]) if self.per_expert else None
@@ -250,13 +285,20 @@ class EPMoE:
 
     def close(self) -> None:
         if getattr(self, "base", None):
+            sh = self._shared
+            self.base = None
+            sh.users -= 1
+            if sh.users > 0:
+                return
+            for k, v in list(_SHARED.items()):
+                if v is sh:
+                    del _SHARED[k]
             lib = _native.kernels()
             torch.cuda.synchronize(self.device)
-            for r, p in enumerate(self.peers):
+            for r, p in enumerate(sh.peers):
                 if r != self.rank:
                     lib.ib_ipc_close(ctypes.c_void_p(p))
-            lib.ib_sym_free(ctypes.c_void_p(self.base))
-            self.base = None
+            lib.ib_sym_free(ctypes.c_void_p(sh.base))
 
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits=None, in_splits=None) -> None:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)

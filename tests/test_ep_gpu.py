@@ -73,3 +73,18 @@ def test_dp_attention_ep_two_gpus(fused):
     assert r.returncode == 0, out[-3000:]
     res = json.loads([x for x in out.splitlines() if x.startswith("{")][-1])
     assert res["agreement"] >= 0.9, res
+
+
+def test_dp_attention_ep_one_gpu_fused_layers_share_buffers():
+    """World 1, fused path, two MoE layers: every EP layer of the process
+    uses one set of symmetric buffers and one round counter (full-size
+    DeepSeek-V3 shards cannot afford a set per layer)."""
+    env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "10", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "1", "--master-addr", "127.0.0.1", "--master-port", "29779", "-m",
+           "infera_b200.bench.dp_check", "--model", "tiny-mla-gpu", "--prompts", "4", "--fused"]
+    r = subprocess.run(cmd, env=env, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, timeout=330)
+    out = r.stdout.decode()
+    assert r.returncode == 0, out[-3000:]
+    res = json.loads([x for x in out.splitlines() if x.startswith("{")][-1])
+    assert res["agreement"] >= 0.9, res
