@@ -95,6 +95,130 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
   }
 }
 
+// residual += delta; out = rmsnorm(residual) * w, with delta read from a
+// split GEMM's fp32 workspace row [t, 0:H) (stride ldws) instead of a
+// finalized bf16 output; the workspace row is zeroed for the next GEMM.
+__global__ void __launch_bounds__(256) add_rmsnorm_ws_kernel(float* __restrict__ ws, int ldws,
+                                                             __nv_bfloat16* __restrict__ x,
+                                                             const __nv_bfloat16* __restrict__ w,
+                                                             __nv_bfloat16* __restrict__ out, int H, int ldx, int ldo,
+                                                             float eps) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  __nv_bfloat16* xr = x + static_cast<size_t>(t) * ldx;
+  float* wr = ws + static_cast<size_t>(t) * ldws;
+  const int nchunk = H / 8;
+  constexpr int MAXC = 4;
+  float vals[MAXC][8];
+  float ss = 0.f;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < nchunk) {
+      uint4 a = reinterpret_cast<const uint4*>(xr)[c];
+      float4* d4 = reinterpret_cast<float4*>(wr + c * 8);
+      const float4 d0 = __ldcg(d4), d1 = __ldcg(d4 + 1);
+      __stcg(d4, zero);
+      __stcg(d4 + 1, zero);
+      // the delta rounded to bf16 first, as a finalized GEMM output would be
+      auto rb = [](float v) { return __bfloat162float(__float2bfloat16(v)); };
+      uint4 r;
+      r.x = pack_bf16(bf16_lo(a.x) + rb(d0.x), bf16_hi(a.x) + rb(d0.y));
+      r.y = pack_bf16(bf16_lo(a.y) + rb(d0.z), bf16_hi(a.y) + rb(d0.w));
+      r.z = pack_bf16(bf16_lo(a.z) + rb(d1.x), bf16_hi(a.z) + rb(d1.y));
+      r.w = pack_bf16(bf16_lo(a.w) + rb(d1.z), bf16_hi(a.w) + rb(d1.w));
+      reinterpret_cast<uint4*>(xr)[c] = r;
+      const float f[8] = {bf16_lo(r.x), bf16_hi(r.x), bf16_lo(r.y), bf16_hi(r.y),
+                          bf16_lo(r.z), bf16_hi(r.z), bf16_lo(r.w), bf16_hi(r.w)};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        vals[i][j] = f[j];
+        ss += f[j] * f[j];
+      }
+    }
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / H + eps);
+  __nv_bfloat16* orow = out + static_cast<size_t>(t) * ldo;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < nchunk) {
+      uint4 wv = reinterpret_cast<const uint4*>(w)[c];
+      uint4 o;
+      o.x = pack_bf16(vals[i][0] * inv * bf16_lo(wv.x), vals[i][1] * inv * bf16_hi(wv.x));
+      o.y = pack_bf16(vals[i][2] * inv * bf16_lo(wv.y), vals[i][3] * inv * bf16_hi(wv.y));
+      o.z = pack_bf16(vals[i][4] * inv * bf16_lo(wv.z), vals[i][5] * inv * bf16_hi(wv.z));
+      o.w = pack_bf16(vals[i][6] * inv * bf16_lo(wv.w), vals[i][7] * inv * bf16_hi(wv.w));
+      reinterpret_cast<uint4*>(orow)[c] = o;
+    }
+  }
+}
+
+// rope_kvwrite over a split GEMM's fp32 workspace row [t, 0:(hq+2hkv)*D)
+// (stride ldws) instead of a finalized bf16 qkv row: the rotated q heads go
+// to qkv (what attention reads), rotated k and v to the cache slot; the
+// workspace row is zeroed (also when the token's indices are rejected).
+__global__ void rope_kvwrite_ws_kernel(float* __restrict__ ws, int ldws, __nv_bfloat16* __restrict__ qkv,
+                                       int ldqkv, const int* __restrict__ pos, const int* __restrict__ slots,
+                                       const float2* __restrict__ cos_sin, int hq, int hkv, int D,
+                                       __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, int ldkv,
+                                       long long num_slots, int max_pos, int* status) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int p = pos[t];
+  long long slot = slots[t];
+  float* wr = ws + static_cast<size_t>(t) * ldws;
+  const int width = (hq + 2 * hkv) * D;
+  const bool bad = p < 0 || p >= max_pos || slot >= num_slots;
+  if (bad) {
+    if (threadIdx.x == 0)
+      record_status_detail(status, kStatusBadIndex, p < 0 || p >= max_pos ? 1 : 2, t,
+                           p < 0 || p >= max_pos ? p : static_cast<int>(slot));
+    for (int c = threadIdx.x; c < width; c += blockDim.x) wr[c] = 0.f;
+    return;
+  }
+  __nv_bfloat16* row = qkv + static_cast<size_t>(t) * ldqkv;
+  const int half = D / 2;
+  const float2* cs = cos_sin + static_cast<size_t>(p) * half;
+  const int pairs_per_head = half / 2;
+  const int nheads = hq + hkv;
+  for (int idx = threadIdx.x; idx < nheads * pairs_per_head; idx += blockDim.x) {
+    const int hh = idx / pairs_per_head;
+    const int i = (idx % pairs_per_head) * 2;
+    float* hp = wr + hh * D;
+    const float2 a = __ldcg(reinterpret_cast<const float2*>(hp + i));
+    const float2 b = __ldcg(reinterpret_cast<const float2*>(hp + i + half));
+    __stcg(reinterpret_cast<float2*>(hp + i), make_float2(0.f, 0.f));
+    __stcg(reinterpret_cast<float2*>(hp + i + half), make_float2(0.f, 0.f));
+    // round the projections to bf16 first, as the finalized path does
+    const float a0 = __bfloat162float(__float2bfloat16(a.x)), a1 = __bfloat162float(__float2bfloat16(a.y));
+    const float b0 = __bfloat162float(__float2bfloat16(b.x)), b1 = __bfloat162float(__float2bfloat16(b.y));
+    const float2 c0 = cs[i], c1 = cs[i + 1];
+    const __nv_bfloat162 na = __floats2bfloat162_rn(a0 * c0.x - b0 * c0.y, a1 * c1.x - b1 * c1.y);
+    const __nv_bfloat162 nb = __floats2bfloat162_rn(b0 * c0.x + a0 * c0.y, b1 * c1.x + a1 * c1.y);
+    if (hh < hq) {
+      *reinterpret_cast<__nv_bfloat162*>(row + hh * D + i) = na;
+      *reinterpret_cast<__nv_bfloat162*>(row + hh * D + i + half) = nb;
+    } else if (slot >= 0) {
+      __nv_bfloat16* kd = kc + slot * ldkv + (hh - hq) * D;
+      *reinterpret_cast<__nv_bfloat162*>(kd + i) = na;
+      *reinterpret_cast<__nv_bfloat162*>(kd + i + half) = nb;
+    }
+  }
+  const int v0 = nheads * D;
+  for (int c = threadIdx.x * 2; c < hkv * D; c += blockDim.x * 2) {
+    float2* src = reinterpret_cast<float2*>(wr + v0 + c);
+    const float2 v = __ldcg(src);
+    __stcg(src, make_float2(0.f, 0.f));
+    if (slot >= 0) *reinterpret_cast<__nv_bfloat162*>(vc + slot * ldkv + c) = __floats2bfloat162_rn(v.x, v.y);
+  }
+}
+
 // qkv: [T, ldqkv] with q heads at [0, hq*D), k at [hq*D, (hq+hkv)*D), v after.
 // Rotate q and k in place (rotate-half pairs (i, i + D/2)), then copy k, v
 // into the cache slot of each token (slot < 0: skip the cache write).
@@ -282,6 +406,31 @@ extern "C" int ib_add_rmsnorm(const void* delta, void* residual, const void* w, 
                                                    static_cast<__nv_bfloat16*>(residual),
                                                    static_cast<const __nv_bfloat16*>(w),
                                                    static_cast<__nv_bfloat16*>(out), H, ldr, ldd, ldo, eps);
+  return ret_launch();
+}
+
+// residual += ws[t, 0:H] (fp32 split-GEMM workspace, zeroed); out = rmsnorm(residual) * w
+extern "C" int ib_add_rmsnorm_ws(void* ws, int ldws, void* residual, const void* w, void* out, int T, int H, int ldr,
+                                 int ldo, float eps, cudaStream_t stream) {
+  if (T <= 0) return 0;
+  if (H % 8 != 0 || H / 8 > 4 * 256 || (ldws % 4) != 0) return -1;
+  launch_pdl(ew::add_rmsnorm_ws_kernel, T, 256, 0, stream, static_cast<float*>(ws), ldws,
+             static_cast<__nv_bfloat16*>(residual), static_cast<const __nv_bfloat16*>(w),
+             static_cast<__nv_bfloat16*>(out), H, ldr, ldo, eps);
+  return ret_launch();
+}
+
+// rope_kvwrite whose q / k / v come from the fp32 split-GEMM workspace
+// [T, ldws] (zeroed); rotated q heads are written to qkv.
+extern "C" int ib_rope_kvwrite_ws(void* ws, int ldws, void* qkv, int T, int ldqkv, const int* pos, const int* slots,
+                                  const void* cos_sin, int hq, int hkv, int D, void* k_cache, void* v_cache,
+                                  int ldkv, long long num_slots, int max_pos, int* status, cudaStream_t stream) {
+  if (T <= 0) return 0;
+  if (D % 4 != 0 || (ldws % 2) != 0) return -1;
+  launch_pdl(ew::rope_kvwrite_ws_kernel, T, 256, 0, stream, static_cast<float*>(ws), ldws,
+             static_cast<__nv_bfloat16*>(qkv), ldqkv, pos, slots, static_cast<const float2*>(cos_sin), hq, hkv, D,
+             static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), ldkv, num_slots, max_pos,
+             status);
   return ret_launch();
 }
 

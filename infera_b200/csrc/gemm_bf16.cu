@@ -1088,8 +1088,12 @@ inline TileCounters& tile_counters() {
   return t[dev >= 0 && dev < 64 ? dev : 0];
 }
 
+// defer: a split result stays in the fp32 workspace (every tile through it,
+// no finalize); *in_ws (optional) reports whether it did.
 inline int run_dense(const Operands& o, const void* A, const void* W, void* out, int M, int N, int K, int lda,
-                     int ldw, int ldc, int epi, float* ws, int force_split, int* status, cudaStream_t stream) {
+                     int ldw, int ldc, int epi, float* ws, int force_split, int* status, cudaStream_t stream,
+                     bool defer = false, int* in_ws = nullptr) {
+  if (in_ws != nullptr) *in_ws = 0;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if (!operands_ok(o, K, lda, ldw)) return -1;
   if (epi == EPI_SWIGLU && (N % 2) != 0) return -1;
@@ -1110,13 +1114,17 @@ inline int run_dense(const Operands& o, const void* A, const void* W, void* out,
   p.out = split ? static_cast<void*>(ws) : out;
   p.epi_dp = epi;
   p.out_dp = out;
-  if (!p.streamk) p.dp_tiles = 0;
+  if (!p.streamk || defer) p.dp_tiles = 0;
   const TileCounters& tc = tile_counters();
-  p.tile_ctr = split && tc.ptr != nullptr && p.p_tiles * p.q_tiles <= tc.n ? tc.ptr : nullptr;
+  p.tile_ctr = split && !defer && tc.ptr != nullptr && p.p_tiles * p.q_tiles <= tc.n ? tc.ptr : nullptr;
   CUtensorMap tmP, tmQ;
   if (!encode_pq(o, p, A, W, N, lda, ldw, &tmP, &tmQ)) return -2;
   int rc = launch(o, tmP, tmQ, p, pl.grid, stream);
   if (rc != 0) return rc;
+  if (split && defer) {
+    if (in_ws != nullptr) *in_ws = 1;
+    return 0;
+  }
   if (split && p.tile_ctr == nullptr) {
     // stream-K: only the columns of the tiles past dp_tiles went through
     // the workspace (swap-AB: weight-row blocks, else token-column tiles)
@@ -1241,6 +1249,15 @@ extern "C" int ib_gemm_bf16(const void* A, const void* W, void* out, int M, int 
                             int ldc, int epi, float* ws, int force_split, int* status, cudaStream_t stream) {
   const gemm::Operands o{false, nullptr, 0, nullptr};
   return gemm::run_dense(o, A, W, out, M, N, K, lda, ldw, ldc, epi, ws, force_split, status, stream);
+}
+
+// As ib_gemm_bf16 (plain epilogue), but a split-K / stream-K result is left
+// in ws ([M, N] fp32, row stride N) for its consumer to read and zero;
+// *in_ws = 1 then, 0 when the GEMM wrote out directly.
+extern "C" int ib_gemm_bf16_deferred(const void* A, const void* W, void* out, int M, int N, int K, int lda, int ldw,
+                                     int ldc, float* ws, int* status, int* in_ws, cudaStream_t stream) {
+  const gemm::Operands o{false, nullptr, 0, nullptr};
+  return gemm::run_dense(o, A, W, out, M, N, K, lda, ldw, ldc, gemm::EPI_BF16, ws, 0, status, stream, true, in_ws);
 }
 
 // W8A8 e4m3 GEMM with UE8M0 block scales: A [M, K] e4m3 (row pitch lda

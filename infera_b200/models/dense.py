@@ -199,12 +199,19 @@ class DenseModel:
         act = bufs["act"][:T] if "act" in bufs else torch.empty(T, cfg.ffn, dtype=bf, device=dev)
         K.rmsnorm(h, self.w.layers[0]["ln1"], cfg.rms_eps, out=x)
         for li, lw in enumerate(self.w.layers):
-            K.linear(x, lw["qkv"], out=qkv)
-            if cfg.qk_norm:
-                self._qk_norm(qkv, lw)
             kc, vc = k_caches[li], v_caches[li]
-            K.rope_kvwrite(qkv, fb.positions, fb.slots, self.cos_sin, cfg.num_heads, cfg.num_kv_heads,
-                           cfg.head_dim, kc, vc)
+            # a split qkv GEMM hands its fp32 workspace to rope_kvwrite (no
+            # finalize launch); with q / k norms the finalized rows are needed
+            ws = None if cfg.qk_norm else K.linear_deferred(x, lw["qkv"], qkv)
+            if ws is not None:
+                K.rope_kvwrite_ws(ws, qkv, fb.positions, fb.slots, self.cos_sin, cfg.num_heads, cfg.num_kv_heads,
+                                  cfg.head_dim, kc, vc)
+            else:
+                if cfg.qk_norm:
+                    K.linear(x, lw["qkv"], out=qkv)
+                    self._qk_norm(qkv, lw)
+                K.rope_kvwrite(qkv, fb.positions, fb.slots, self.cos_sin, cfg.num_heads, cfg.num_kv_heads,
+                               cfg.head_dim, kc, vc)
             if fb.layer_hook is not None:
                 fb.layer_hook(li)
             if Tp > 0:
@@ -222,11 +229,18 @@ class DenseModel:
                 y = lw["moe"].forward(x)
                 K.add_rmsnorm(y, h, nxt, cfg.rms_eps, out=x)
             elif self.tp is None:
-                K.linear(attn, lw["o"], out=o)
-                K.add_rmsnorm(o, h, lw["ln2"], cfg.rms_eps, out=x)
+                # split o / down GEMMs hand their fp32 workspace to add_rmsnorm
+                ws = K.linear_deferred(attn, lw["o"], o)
+                if ws is None:
+                    K.add_rmsnorm(o, h, lw["ln2"], cfg.rms_eps, out=x)
+                else:
+                    K.add_rmsnorm_ws(ws, h, lw["ln2"], cfg.rms_eps, out=x)
                 K.linear(x, lw["gate_up"], out=act, swiglu=True)
-                K.linear(act, lw["down"], out=o)
-                K.add_rmsnorm(o, h, nxt, cfg.rms_eps, out=x)
+                ws = K.linear_deferred(act, lw["down"], o)
+                if ws is None:
+                    K.add_rmsnorm(o, h, nxt, cfg.rms_eps, out=x)
+                else:
+                    K.add_rmsnorm_ws(ws, h, nxt, cfg.rms_eps, out=x)
             else:
                 self.tp.gemm_allreduce_add_rmsnorm(attn, lw["o"], h, lw["ln2"], cfg.rms_eps, x, 0, tmp=o)
                 K.linear(x, lw["gate_up"], out=act, swiglu=True)

@@ -38,6 +38,11 @@ def _declare_kernels(lib: ctypes.CDLL) -> None:
         "ib_gemm_bf16_plan": [c_int, c_int, c_int, c_int, c_int, c_vp],
         "ib_rmsnorm": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_vp],
         "ib_add_rmsnorm": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float, c_vp],
+        "ib_add_rmsnorm_ws": [c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_vp],
+        "ib_rope_kvwrite_ws": [c_vp, c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp,
+                               c_int, c_ll, c_int, c_vp, c_vp],
+        "ib_gemm_bf16_deferred": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp,
+                                  c_vp],
         "ib_rope_kvwrite": [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_int, c_ll,
                             c_int, c_vp, c_vp],
         "ib_embed": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp],

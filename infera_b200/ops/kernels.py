@@ -225,6 +225,60 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, sw
     return out
 
 
+# A split GEMM's consumer can read its fp32 workspace itself (and zero it)
+# instead of a finalize launch (INFERA_GEMM_DEFER=0: always finalize).
+_DEFER = _os.environ.get("INFERA_GEMM_DEFER", "1") != "0"
+
+
+def linear_deferred(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor | None:
+    """y = x @ w.T for a consumer that can take the fp32 workspace: returns
+    the workspace view [M, N] (fp32, not rounded, the consumer zeroes it)
+    when the GEMM was split, else None with y in ``out`` (bf16)."""
+    M, Kd = x.shape
+    N = w.shape[0]
+    if not x.is_cuda or not _DEFER or not isinstance(w, torch.Tensor) or M == 0 or not _gemm_ws(M, N, Kd):
+        linear(x, w, out=out)
+        return None
+    assert x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+    assert x.stride(1) == 1 and w.stride(1) == 1
+    sc = scratch(x.device)
+    ws = sc.ensure_gemm(M * N)
+    in_ws = (_native.c_int * 1)()
+    rc = _native.kernels().ib_gemm_bf16_deferred(x.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, Kd, x.stride(0),
+                                                 w.stride(0), out.stride(0), ws.data_ptr(), sc.status.data_ptr(),
+                                                 in_ws, _stream())
+    _native.check(rc, "ib_gemm_bf16_deferred")
+    _count(1)
+    return ws[: M * N].view(M, N) if in_ws[0] else None
+
+
+def add_rmsnorm_ws(ws: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                   out: torch.Tensor) -> torch.Tensor:
+    """residual += bf16(ws) (ws: a split GEMM's fp32 [T, H] workspace view,
+    zeroed here); return rmsnorm(residual) * w."""
+    T, H = residual.shape
+    rc = _native.kernels().ib_add_rmsnorm_ws(ws.data_ptr(), ws.stride(0), residual.data_ptr(), w.data_ptr(),
+                                             out.data_ptr(), T, H, residual.stride(0), out.stride(0), eps, _stream())
+    _native.check(rc, "ib_add_rmsnorm_ws")
+    _count()
+    return out
+
+
+def rope_kvwrite_ws(ws: torch.Tensor, qkv: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor,
+                    cos_sin: torch.Tensor, hq: int, hkv: int, head_dim: int, k_cache: torch.Tensor,
+                    v_cache: torch.Tensor) -> None:
+    """rope_kvwrite over a split GEMM's fp32 qkv workspace view [T, N]
+    (zeroed here): rotated q heads into ``qkv``, k and v into the caches."""
+    T = qkv.shape[0]
+    rc = _native.kernels().ib_rope_kvwrite_ws(ws.data_ptr(), ws.stride(0), qkv.data_ptr(), T, qkv.stride(0),
+                                              pos.data_ptr(), slots.data_ptr(), cos_sin.data_ptr(), hq, hkv,
+                                              head_dim, k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
+                                              k_cache.shape[0], cos_sin.shape[0],
+                                              scratch(qkv.device).status.data_ptr(), _stream())
+    _native.check(rc, "ib_rope_kvwrite_ws")
+    _count()
+
+
 # ---------------------------------------------------------------- norms / rope / embed
 
 

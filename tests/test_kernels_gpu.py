@@ -278,3 +278,51 @@ def test_attn_prefill_divergent_rescale():
     torch.cuda.synchronize()
     _check_status()
     assert _rel_err(out.cpu(), ref) < 2e-2
+
+
+@pytest.mark.parametrize("M", [8, 64, 288])
+def test_deferred_gemm_consumers_match_finalized(M):
+    """A split GEMM left in its fp32 workspace, read by add_rmsnorm_ws /
+    rope_kvwrite_ws, gives the same rows as the finalized GEMM followed by
+    add_rmsnorm / rope_kvwrite, and the workspace is left zeroed."""
+    torch.manual_seed(7)
+    H, hq, hkv, D = 4096, 32, 8, 128
+    x = (torch.randn(M, H, device=DEV) * 0.5).to(torch.bfloat16)
+    wo = (torch.randn(H, H, device=DEV) / 64).to(torch.bfloat16)
+    nw = torch.randn(H, device=DEV).to(torch.bfloat16)
+    h0 = torch.randn(M, H, device=DEV).to(torch.bfloat16)
+    assert K._gemm_ws(M, H, H)            # this shape splits
+    o = torch.empty(M, H, dtype=torch.bfloat16, device=DEV)
+    h1, h2 = h0.clone(), h0.clone()
+    out1 = K.add_rmsnorm(K.linear(x, wo), h1, nw, 1e-5)
+    ws = K.linear_deferred(x, wo, o)
+    assert ws is not None
+    out2 = K.add_rmsnorm_ws(ws, h2, nw, 1e-5, out=torch.empty_like(h2))
+    torch.cuda.synchronize()
+    _check_status()
+    # same rounding on both paths; only the split partials' atomic order differs
+    assert _rel_err(h1.float(), h2.float()) < 1e-3
+    assert _rel_err(out1.float(), out2.float()) < 1e-3
+    assert float(K.scratch().gemm_ws.abs().sum()) == 0.0
+    # qkv -> rope + KV write
+    N = (hq + 2 * hkv) * D
+    wq = (torch.randn(N, H, device=DEV) / 64).to(torch.bfloat16)
+    cos_sin = K.rope_cos_sin(4096, D, 500000.0, device=DEV)
+    pos = torch.randint(0, 4000, (M,), device=DEV, dtype=torch.int32)
+    slots = torch.randperm(4 * M, device=DEV)[:M].to(torch.int32)
+    kc1 = torch.zeros(4 * M, hkv * D, dtype=torch.bfloat16, device=DEV)
+    vc1, kc2, vc2 = kc1.clone(), kc1.clone(), kc1.clone()
+    q1 = K.linear(x, wq)
+    K.rope_kvwrite(q1, pos, slots, cos_sin, hq, hkv, D, kc1, vc1)
+    q2 = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    ws = K.linear_deferred(x, wq, q2)
+    if ws is not None:
+        K.rope_kvwrite_ws(ws, q2, pos, slots, cos_sin, hq, hkv, D, kc2, vc2)
+    else:
+        K.rope_kvwrite(q2, pos, slots, cos_sin, hq, hkv, D, kc2, vc2)
+    torch.cuda.synchronize()
+    _check_status()
+    assert _rel_err(q1[:, :hq * D].float(), q2[:, :hq * D].float()) < 1e-3
+    assert _rel_err(kc1.float(), kc2.float()) < 1e-3
+    assert _rel_err(vc1.float(), vc2.float()) < 1e-3
+    assert float(K.scratch().gemm_ws.abs().sum()) == 0.0
