@@ -226,8 +226,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, sw
 
 
 # A split GEMM's consumer can read its fp32 workspace itself (and zero it)
-# instead of a finalize launch (INFERA_GEMM_DEFER=0: always finalize).
-_DEFER = _os.environ.get("INFERA_GEMM_DEFER", "1") != "0"
+# instead of a finalize launch (INFERA_GEMM_DEFER=1; default: finalize).
+_DEFER = _os.environ.get("INFERA_GEMM_DEFER", "0") == "1"
 
 
 def linear_deferred(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor | None:

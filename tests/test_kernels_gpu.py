@@ -286,6 +286,14 @@ def test_deferred_gemm_consumers_match_finalized(M):
     rope_kvwrite_ws, gives the same rows as the finalized GEMM followed by
     add_rmsnorm / rope_kvwrite, and the workspace is left zeroed."""
     torch.manual_seed(7)
+    K._DEFER, was = True, K._DEFER
+    try:
+        _deferred_case(M)
+    finally:
+        K._DEFER = was
+
+
+def _deferred_case(M):
     H, hq, hkv, D = 4096, 32, 8, 128
     x = (torch.randn(M, H, device=DEV) * 0.5).to(torch.bfloat16)
     wo = (torch.randn(H, H, device=DEV) / 64).to(torch.bfloat16)
