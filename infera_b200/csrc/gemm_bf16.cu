@@ -897,7 +897,7 @@ inline int launch_gemm_variant(const CUtensorMap& tmP, const CUtensorMap& tmQ, c
     cudaFuncSetAttribute(gemm_kernel<FP8, DEEP>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     attr_set[dev] = true;
   }
-  launch_pdl(gemm_kernel<FP8, DEEP>, grid, FP8 ? NUM_THREADS_FP8 : NUM_THREADS, SMEM_BYTES, stream, tmP, tmQ, p);
+  launch_pdl_g(gemm_kernel<FP8, DEEP>, grid, FP8 ? NUM_THREADS_FP8 : NUM_THREADS, SMEM_BYTES, stream, tmP, tmQ, p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }

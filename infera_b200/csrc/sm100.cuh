@@ -53,9 +53,35 @@ inline bool pdl_on() {
   return v;
 }
 
+// INFERA_PDL_GRAPH=1: kernels launched through launch_pdl_g() keep the
+// programmatic attribute inside CUDA-graph captures too.
+inline bool pdl_graph_on() {
+  static const bool v = [] {
+    const char* e = std::getenv("INFERA_PDL_GRAPH");
+    return e != nullptr && e[0] == '1';
+  }();
+  return v;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_impl(bool in_graph, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                   cudaStream_t stream, Args... args);
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                               Args... args) {
+  return launch_pdl_impl(false, kernel, grid, block, smem, stream, args...);
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_g(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                Args... args) {
+  return launch_pdl_impl(pdl_graph_on(), kernel, grid, block, smem, stream, args...);
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_impl(bool in_graph, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                   cudaStream_t stream, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -71,7 +97,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   // 6.5 % (11.63 vs 12.44 ms)
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   cudaStreamIsCapturing(stream, &cs);
-  cfg.numAttrs = pdl_on() && cs == cudaStreamCaptureStatusNone ? 1 : 0;
+  cfg.numAttrs = pdl_on() && (in_graph || cs == cudaStreamCaptureStatusNone) ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
