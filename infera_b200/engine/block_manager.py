@@ -38,6 +38,9 @@ class SeqBlocks:
     # (first page, page count) that a KV tier holds and an asynchronous
     # promote will fill; the scheduler parks the sequence until it lands
     tier_load: tuple[int, int] | None = None
+    # free pages set aside for this sequence's next pages: the rest of the
+    # 8-page tile its last page started, so the tile is one consecutive run
+    run_ahead: list[int] = field(default_factory=list)
 
 
 class BlockManager:
@@ -89,6 +92,31 @@ class BlockManager:
                         seen.add(q)
                         keep.append(q)
                 self.free_plain = keep[::-1]
+
+    # pages per attention key tile: a tile of consecutive pages loads as one
+    # TMA box per 64-dim half
+    RUN = 8
+
+    def _take_run_page(self, sb: SeqBlocks) -> int:
+        """The sequence's next page. At the start of an 8-page key tile the
+        seven pages after the one taken are set aside for the same sequence
+        when they are free, so sequences that grow side by side (decode
+        steps) still fill each tile with one run of consecutive pages."""
+        if sb.run_ahead:
+            return sb.run_ahead.pop(0)
+        p = self._take_page(sb.pages[-1] if sb.pages else None)
+        if len(sb.pages) % self.RUN == 0 and len(self.free_set) > 64 * self.RUN:
+            run = [p + i for i in range(1, self.RUN)]
+            if all(q in self.free_set for q in run):
+                for q in run:
+                    self.free_set.discard(q)      # their stack entries are skipped when reached
+                sb.run_ahead = run
+        return p
+
+    def _drop_run_ahead(self, sb: SeqBlocks) -> None:
+        for q in sb.run_ahead:
+            self._push_free(q)
+        sb.run_ahead = []
 
     def _take_page(self, prev: int | None = None) -> int:
         if prev is not None and prev + 1 in self.free_set:
@@ -173,7 +201,7 @@ class BlockManager:
         sb = SeqBlocks(pages=list(hit_pages), hashes=list(hit_hashes),
                        num_cached_tokens=len(hit_pages) * self.page_size)
         for _ in range(max(0, need)):
-            p = self._take_page(sb.pages[-1] if sb.pages else None)
+            p = self._take_run_page(sb)
             self.refcount[p] = 1
             sb.pages.append(p)
         if n_tier > 0:
@@ -195,10 +223,10 @@ class BlockManager:
         need = (num_tokens + self.page_size - 1) // self.page_size - len(sb.pages)
         if need <= 0:
             return True
-        if self.num_free() < need:
+        if self.num_free() + len(sb.run_ahead) < need:
             return False
         for _ in range(need):
-            p = self._take_page(sb.pages[-1] if sb.pages else None)
+            p = self._take_run_page(sb)
             self.refcount[p] = 1
             sb.pages.append(p)
         return True
@@ -244,6 +272,7 @@ class BlockManager:
             })
 
     def free(self, sb: SeqBlocks) -> None:
+        self._drop_run_ahead(sb)
         # release in reverse so the tail of a prefix is evicted before its head
         for p in reversed(sb.pages):
             self._release(p)

@@ -141,3 +141,27 @@ def test_block_manager_keeps_sequences_in_page_runs():
         s = bm.allocate_prompt(list(range(33)), 33)
         bm.free(s)
     assert len(bm.free_plain) <= 2 * len(bm.free_set) + 1024
+
+
+def test_block_manager_keeps_tiles_consecutive_under_interleaved_growth():
+    """Sequences that grow side by side (decode steps) still fill every
+    8-page key tile with one run of consecutive pages: the rest of a tile
+    is set aside for its sequence when the tile's first page is taken, and
+    returned when the sequence is freed."""
+    from infera_b200.engine.block_manager import BlockManager, SeqBlocks
+
+    bm = BlockManager(num_pages=4096, page_size=16, enable_prefix_cache=False)
+    seqs = [SeqBlocks() for _ in range(6)]
+    free0 = bm.num_free()
+    for step in range(1, 40 * 16 + 1):          # 40 pages each, one token at a time, interleaved
+        for sb in seqs:
+            assert bm.ensure_capacity(sb, step)
+    for sb in seqs:
+        pages = sb.pages
+        assert len(pages) == 40
+        for t in range(0, 40, 8):
+            assert pages[t:t + 8] == list(range(pages[t], pages[t] + 8))
+    for sb in seqs:
+        bm.free(sb)
+        assert sb.run_ahead == []
+    assert bm.num_free() == free0
