@@ -139,7 +139,10 @@ def main(argv=None) -> None:
             "itl": [x for r in done for x in r.itls()],
             "out_tokens_in_window": sum(1 for r in recs for t in r.token_times if win[0] <= t <= win[1]),
             "idle_forwards": dp.idle_forwards, "iters": iters, "init_s": init_s,
-            "status": 0 if a.cpu else K.scratch(device).read_status()}
+            "status": 0 if a.cpu else K.scratch(device).read_status(),
+            # this rank's engine steps over the whole run, by kind (decode /
+            # mixed / prefill): what an iteration costs and what it carries
+            "steps": rp.step_profile((0.0, float("inf")))}
     allr = [None] * world
     dist.all_gather_object(allr, mine, group=gloo)
     if rank == 0:
@@ -161,6 +164,7 @@ def main(argv=None) -> None:
             "itl_p99_ms": round(1000 * percentile(itl, 99), 2) if itl else None,
             "idle_forwards": [r["idle_forwards"] for r in allr], "iters": allr[0]["iters"],
             "init_s": round(max(r["init_s"] for r in allr), 1), "kernel_status": [r["status"] for r in allr],
+            "step_profile_rank0": allr[0]["steps"],
             "data": "synthetic random tokens, random-init fp8 weights", "timing": "CUDA events per rank",
         }
         print(json.dumps(out), flush=True)

@@ -24,3 +24,6 @@ def test_ep_serve_two_gloo_ranks():
     assert d["parallelism"] == "EP2 + DP-attention2"
     assert d["arrived"] > 0 and d["completed"] == d["arrived"]
     assert len(d["idle_forwards"]) == 2 and d["iters"] > 0
+    # the step profile says what an iteration cost and carried
+    prof = d["step_profile_rank0"]
+    assert prof and all(v["n"] > 0 and v["p50_ms"] >= 0 for v in prof.values())
