@@ -130,6 +130,15 @@ def main(argv=None) -> None:
             "push_frac_of_measured_770": round(pb / ps / 770e9, 3) if ps else None,
             "decode_prompt_tokens_computed": dm.get("infera_engine:prompt_tokens_total"),
             "prefill_prompt_tokens_computed": pm.get("infera_engine:prompt_tokens_total"),
+            # busy time and rate of each instance: low busy time points at
+            # admission / hand-off, a low rate inside the forwards at compute
+            "prefill_steps": pm.get("infera_engine:steps_total"),
+            "prefill_forward_s": pm.get("infera_engine:forward_seconds_total"),
+            "prefill_tokens_per_forward_s": round(pm.get("infera_engine:prompt_tokens_total", 0.0)
+                                                  / pm["infera_engine:forward_seconds_total"], 1)
+            if pm.get("infera_engine:forward_seconds_total") else None,
+            "decode_steps": dm.get("infera_engine:steps_total"),
+            "decode_forward_s": dm.get("infera_engine:forward_seconds_total"),
         }
         print(json.dumps(out), flush=True)
     finally:

@@ -178,7 +178,10 @@ class LLMEngine:
         self.last_step_shape = (0, 0)
         self.last_step_kv = 0
         self.clock: Callable[[], float] = time.monotonic
-        self.counters = {"prompt_tokens": 0, "generation_tokens": 0, "finished": 0, "preemptions": 0}
+        # forward_s: host time inside the model forward (each step ends by
+        # reading its sampled tokens back, so this is the engine's busy time)
+        self.counters = {"prompt_tokens": 0, "generation_tokens": 0, "finished": 0, "preemptions": 0,
+                         "forward_s": 0.0}
         # named phase ranges (torch.profiler record_function + NVTX) while a
         # profile is being taken: schedule / forward (prefill+decode counts) / kv push
         self.trace_phases = False
@@ -394,8 +397,10 @@ class LLMEngine:
                 from infera_b200.engine.pd import LayerPush
 
                 layer_push = LayerPush(self, items)
+        t_fwd = time.perf_counter()
         with self._phase(f"forward prefill={len(sched.prefills)} decode={len(sched.decodes)}"):
             res = self.runner.execute(sched, upd, layer_hook=layer_push)
+        self.counters["forward_s"] += time.perf_counter() - t_fwd
         if layer_push is not None:
             layer_push.finish()
         now = self.clock()

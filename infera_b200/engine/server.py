@@ -178,6 +178,9 @@ def build_worker_app(aeng, tokenizer, model_name: str, extra_metrics=None) -> Fa
         g("infera_engine:pd_parked", s.get("pd_parked", 0), "Requests waiting for pushed KV")
         g("infera_engine:generation_tokens_total", s["generation_tokens"], "Generated tokens")
         g("infera_engine:prompt_tokens_total", s["prompt_tokens"], "Computed prompt tokens")
+        g("infera_engine:steps_total", s.get("steps", 0), "Engine steps that ran a forward")
+        g("infera_engine:forward_seconds_total", round(s.get("forward_s", 0.0), 6),
+          "Host time inside model forwards (each ends on its sampled tokens)")
         # names the reference's drain reader understands
         g("vllm:num_requests_running", s["running"], "alias")
         g("vllm:num_requests_waiting", s["waiting"], "alias")

@@ -120,6 +120,11 @@ def test_worker_cli_spawns_engine_core():
         assert r.status_code == 200 and len(r.json()["choices"][0]["token_ids"]) == 4
         m = httpx.get(f"http://127.0.0.1:{port}/metrics", timeout=10).text
         assert "infera_engine:generation_tokens_total" in m
+        # busy-time counters: steps that ran a forward and the time inside them
+        vals = {ln.split()[0].split("{")[0]: float(ln.split()[-1]) for ln in m.splitlines()
+                if ln.startswith("infera_engine:")}
+        assert vals.get("infera_engine:steps_total", 0) >= 4
+        assert vals.get("infera_engine:forward_seconds_total", 0) > 0
         p.send_signal(signal.SIGTERM)
         assert p.wait(timeout=60) == 0
     finally:
